@@ -1,0 +1,211 @@
+/*
+ * zjai — B200 (sm_100a) engine for the JPEG AI synthesis / analysis networks.
+ *
+ * Plain C ABI (no C++ or torch types): opaque handles, plain pointers and sizes, an int
+ * status. It replaces the float-network path of the imazen/zenjpegai crate behind the
+ * crate's own interfaces; each entry names the reference interface it stands in for
+ * (paths are files of that crate). A Rust `extern "C"` binding of this header is mechanical
+ * (see INTEGRATION.md).
+ *
+ * Conventions
+ *  - Tensors crossing the ABI are planar f32 `[c][h][w]`, like the crate's `Tensor<f32>`
+ *    (src/tensor.rs:10-120). `mem` says whether the pointers are host (ZJAI_MEM_HOST) or
+ *    device (ZJAI_MEM_DEVICE) memory of the context's GPU. Host calls are synchronous: they
+ *    return after the output has been written. Device calls are ordered on the context's
+ *    stream and return after the work has been enqueued (zjai_ctx_sync waits).
+ *  - The caller owns inputs and outputs; the library owns weights and scratch.
+ *  - One call in flight per context at a time; separate contexts are independent and may be
+ *    used from separate host threads.
+ *  - Every function returns a zjai_status; zjai_last_error_message() describes the last
+ *    failure on the calling thread.
+ */
+#ifndef ZJAI_H
+#define ZJAI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Status codes: the variants of the crate's `Error` (src/error.rs:10-31) this path can
+ * produce, plus the device-side failures. */
+typedef enum {
+  ZJAI_OK = 0,
+  ZJAI_INVALID_ARGUMENT = 1, /* Error::InvalidArgument */
+  ZJAI_UNSUPPORTED = 2,      /* Error::Unsupported */
+  ZJAI_LIMIT_EXCEEDED = 3,   /* Error::LimitExceeded (arena / size limits) */
+  ZJAI_CANCELLED = 4,        /* Error::Cancelled (the caller's stop flag was set) */
+  ZJAI_MODEL = 5,            /* Error::Model (missing / mis-shaped parameter) */
+  ZJAI_INVALID_DATA = 6,     /* Error::InvalidData (malformed tile geometry) */
+  ZJAI_DEVICE = 7,           /* a CUDA call failed */
+  ZJAI_DEVICE_TIMEOUT = 8    /* a kernel's bounded wait gave up (status word set) */
+} zjai_status;
+
+enum { ZJAI_MEM_HOST = 0, ZJAI_MEM_DEVICE = 1 };
+
+/* Operating points (src/header.rs `OperatingPoint`). */
+enum { ZJAI_SOP = 0, ZJAI_BOP = 1, ZJAI_HOP = 2 };
+
+/* Network kinds: synthesis primary / secondary (src/model/synthesis.rs), analysis primary /
+ * secondary (src/model/analysis.rs). */
+enum { ZJAI_SYN_Y = 0, ZJAI_SYN_UV = 1, ZJAI_ANA_Y = 2, ZJAI_ANA_UV = 3 };
+
+/* Epilogue activations of the layer entry points. ZJAI_ACT_LEAKY is LeakyReLU(0.01), which
+ * the reference does not have (only relu / relu6, src/nn/fast/layers.rs:174-186); it exists
+ * for the benchmark configurations that prescribe it. */
+enum { ZJAI_ACT_NONE = 0, ZJAI_ACT_RELU = 1, ZJAI_ACT_LEAKY = 2, ZJAI_ACT_SIGMOID = 3,
+       ZJAI_ACT_RELU6 = 4 };
+
+typedef struct zjai_ctx zjai_ctx;
+typedef struct zjai_net zjai_net;
+
+/* ---------------------------------------------------------------------------------------- */
+/* Library / context                                                                          */
+/* ---------------------------------------------------------------------------------------- */
+
+const char *zjai_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char *zjai_last_error_message(void);
+
+/* Context on CUDA device `device`: a stream, a device arena of `arena_bytes` (0 = default
+ * 4 GiB) for activations and staging, and the kernels' status word. Stands in for the
+ * crate's `Engine` (src/nn/fast/mod.rs:127-169): the GPU is one more engine kind. */
+int zjai_ctx_create(int device, size_t arena_bytes, zjai_ctx **out);
+int zjai_ctx_destroy(zjai_ctx *ctx);
+
+/* Use the caller's CUDA stream (a cudaStream_t) instead of the context's own; NULL restores
+ * the context's stream. */
+int zjai_ctx_set_stream(zjai_ctx *ctx, void *cuda_stream);
+
+/* Wait for all work enqueued on the context's stream, then report a kernel status word
+ * (ZJAI_DEVICE_TIMEOUT) if a bounded wait gave up. */
+int zjai_ctx_sync(zjai_ctx *ctx);
+
+/* Number of kernels this context has launched since creation (for launch accounting). */
+int64_t zjai_ctx_launch_count(const zjai_ctx *ctx);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Networks (model load + GPU-resident packed weights)                                        */
+/* ---------------------------------------------------------------------------------------- */
+
+/* One named f32 parameter in PyTorch layout, as the crate's checkpoint readers hand them to
+ * the loaders (src/model/load.rs:11-85; src/weights/mod.rs:135). */
+typedef struct {
+  const char *name;  /* e.g. "first_stage.0.0.conv1.weight" */
+  int ndim;
+  int64_t shape[4];
+  const float *data; /* host memory */
+} zjai_param;
+
+/* Build network `kind` for operating point `op` from named parameters: validates every
+ * name and shape like the crate's loaders (ZJAI_MODEL on mismatch), packs the weights into
+ * GPU-resident f16 K-major tiles. Replaces `SynthesisPrimary::load` (synthesis.rs:241-246),
+ * `SynthesisSecondary::load` (:971-990), `AnalysisPrimary::load` (analysis.rs:229-239),
+ * `AnalysisSecondary::load` (:280-289). */
+int zjai_net_create(zjai_ctx *ctx, int kind, int op, const zjai_param *params, int nparams,
+                    zjai_net **out);
+int zjai_net_destroy(zjai_net *net);
+
+/* Output extent of a synthesis network for a tile of h x w picture samples (the maps are
+ * cropped for the tile inside the network; the caller crops the result to h x w). */
+int zjai_synth_out_size(int kind, int op, int h, int w, int *out_h, int *out_w);
+
+/* `SynthesisPrimary::forward` (synthesis.rs:253-274): y_hat [160][lh][lw] -> out
+ * [1][oh][ow] in [0, 255], (oh, ow) from zjai_synth_out_size. */
+int zjai_synthesis_primary(zjai_net *net, const float *y_hat, int lh, int lw, int h, int w,
+                           float *out, int mem);
+
+/* `SynthesisSecondary::forward` (synthesis.rs:992-1038): luma latent [160][llh][llw] and
+ * chroma latent [96][lh][lw] -> out [2][oh][ow] in [0, 255]. */
+int zjai_synthesis_secondary(zjai_net *net, const float *y_hat_luma, int llh, int llw,
+                             const float *y_hat_chroma, int lh, int lw, int h, int w,
+                             float *out, int mem);
+
+/* `AnalysisPrimary::forward` (analysis.rs:242-269): x [1][h][w] in [0, 255] ->
+ * [160][ceil(h/16)][ceil(w/16)]. */
+int zjai_analysis_primary(zjai_net *net, const float *x, int h, int w, float *out, int mem);
+
+/* `AnalysisSecondary::forward` (analysis.rs:292-311): x [12][h][w] ->
+ * [96][ceil(h/8)][ceil(w/8)]. */
+int zjai_analysis_secondary(zjai_net *net, const float *x, int h, int w, float *out, int mem);
+
+/* One synthesis tile (src/tools/tiles.rs:26-32 `SynthesisTile`). */
+typedef struct {
+  int img_x, img_y, img_w, img_h;
+  int lat_x, lat_y, lat_w, lat_h;
+  int core_x, core_y, core_w, core_h;
+  int off_x, off_y;
+} zjai_tile;
+
+/* `synthesis_tiles` (src/tools/tiles.rs:39-119) without independent regions. tile_size <= 0
+ * means one tile. Returns ZJAI_INVALID_DATA for malformed geometry; *count receives the
+ * number of tiles (at most max_tiles are written). */
+int zjai_synthesis_tiles(int height, int width, int latent_h, int latent_w, int tile_size,
+                         int overlap, zjai_tile *tiles, int max_tiles, int *count);
+
+/* `synthesize_with` (src/decoder/reconstruct.rs:274-331, 379-464): whole-picture synthesis,
+ * tile by tile, written straight into the output planes: rec_y [out_h][out_w] cropped to
+ * the displayed size, rec_u / rec_v [ceil(out_h/sv)][ceil(out_w/sh)] subsampled. Luma and
+ * chroma run on two streams. `cancel` (may be NULL) is polled between tiles; when it reads
+ * non-zero the call returns ZJAI_CANCELLED (enough::Stop, reconstruct.rs:391,432). */
+int zjai_synthesize(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, const float *y_hat_y,
+                    const float *y_hat_uv, int lh, int lw, int height, int width, int out_h,
+                    int out_w, int tile_size, int overlap, int sv, int sh, float *rec_y,
+                    float *rec_u, float *rec_v, int mem, const volatile int *cancel);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Output stage (src/decoder/output.rs)                                                       */
+/* ---------------------------------------------------------------------------------------- */
+
+/* `quantize_plane_par` (output.rs:330-342): clip to [0,255], scale to 2^depth-1, round half
+ * to even; 8-bit output as uint8 when bit_depth == 8 (out_u8), else uint16 (out_u16). */
+int zjai_quantize_plane(zjai_ctx *ctx, const float *x, int64_t n, int bit_depth, void *out,
+                        int mem);
+
+/* `to_source_format_par` bicubic 4:2:0 -> 4:4:4 (output.rs:103-151, align_corners) then
+ * `to_rgb_planes_owned_par` BT.709 (:218-262) and `quantize_par` (:407-438): planes
+ * y [h][w], u / v [ch][cw] -> interleaved RGB [h][w][3] (uint8 for 8-bit, else uint16). */
+int zjai_yuv_to_rgb(zjai_ctx *ctx, const float *y, const float *u, const float *v, int h,
+                    int w, int ch, int cw, int bit_depth, void *rgb, int mem);
+
+/* ---------------------------------------------------------------------------------------- */
+/* nn layer interface (src/nn/fast/layers.rs, src/nn/fast/math.rs)                           */
+/* ---------------------------------------------------------------------------------------- */
+
+/* `ConvLayer::{new,with_extra_pad,forward}` (layers.rs:30-123) on planar f32 tensors:
+ * weight [oc][c/groups][kh][kw], bias [oc] or NULL, extra = [top, left, bottom, right] zero
+ * border or NULL; `act` is applied after the bias. */
+int zjai_conv2d(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,
+                const float *bias, int oc, int kh, int kw, int stride, int pad_h, int pad_w,
+                int groups, const int *extra, int act, float *out, int mem);
+
+/* `ConvTransposeLayer::forward` (layers.rs:135-171): weight [c][oc][k][k], stride 2. */
+int zjai_conv_transpose2d(zjai_ctx *ctx, const float *x, int c, int h, int w,
+                          const float *weight, const float *bias, int oc, int k, int pad,
+                          int out_pad, float *out, int mem);
+
+/* `math::layer_norm_channels` (math.rs:423-448), out of place. */
+int zjai_layer_norm(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,
+                    const float *bias, float *out, int mem);
+
+/* `math::channel_attention` (math.rs:512-603): qkv [3*dim][h][w] -> [dim][h][w]. */
+int zjai_channel_attention(zjai_ctx *ctx, const float *qkv, int c3, int h, int w, int heads,
+                           const float *temperature, float *out, int mem);
+
+/* Depthwise 3x3, stride 1, pad 1, no bias (`PackedDepthwise`, depthwise.rs:118-209). */
+int zjai_depthwise3x3(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,
+                      float *out, int mem);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* ZJAI_H */

@@ -1,0 +1,369 @@
+"""ctypes front end of the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+The oracle is a plain-C restatement of the reference crate's f32 CPU path (see `oracle.h`).
+Only `tests/`, `__graft_entry__.smoke()` and the `cpu_baseline` leg of `bench.py` import this
+module; the `zenjpegai_b200` package never does. Parity is pinned against the reference's own
+golden vectors (`tests/golden/nn_vectors.npz`, converted by `tests/golden/make_golden.py`).
+"""
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "liboracle.so")
+_lib = None
+
+SOP, BOP, HOP = 0, 1, 2
+OPS = {"sop": SOP, "bop": BOP, "hop": HOP}
+
+
+def build():
+    """Compile the oracle library (gcc, no GPU needed)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        _lib = ctypes.CDLL(_LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+_f = ctypes.POINTER(ctypes.c_float)
+_i = ctypes.c_int
+_i64 = ctypes.c_int64
+
+
+class Param(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("ndim", _i), ("shape", _i * 4), ("data", _f)]
+
+
+class Ckpt(ctypes.Structure):
+    _fields_ = [("params", ctypes.POINTER(Param)), ("n", _i)]
+
+
+class Tile(ctypes.Structure):
+    _fields_ = [(k, _i) for k in (
+        "img_x", "img_y", "img_w", "img_h", "lat_x", "lat_y", "lat_w", "lat_h",
+        "core_x", "core_y", "core_w", "core_h", "off_x", "off_y")]
+
+
+DUMP_FN = ctypes.CFUNCTYPE(None, ctypes.c_char_p, _f, _i, _i, _i)
+
+
+def _declare(L):
+    L.zo_set_threads.argtypes = [_i]
+    L.zo_conv2d_out_size.argtypes = [_i] * 7 + [ctypes.POINTER(_i)] * 3
+    L.zo_conv2d.argtypes = [_f, _i, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i,
+                            ctypes.POINTER(_i), _f]
+    L.zo_conv_transpose2d_out_size.argtypes = [_i] * 6 + [ctypes.POINTER(_i)] * 2
+    L.zo_conv_transpose2d.argtypes = [_f, _i, _i, _i, _f, _f, _i, _i, _i, _i, _i, _f]
+    L.zo_pixel_shuffle.argtypes = [_f, _i, _i, _i, _i, _f]
+    for n in ("zo_relu", "zo_relu6", "zo_sigmoid", "zo_denormalize"):
+        getattr(L, n).argtypes = [_f, _i64]
+    for n in ("zo_add", "zo_gate", "zo_mul", "zo_elu_gate"):
+        getattr(L, n).argtypes = [_f, _f, _i64]
+    L.zo_exp.argtypes = [ctypes.c_float]
+    L.zo_exp.restype = ctypes.c_float
+    L.zo_layer_norm_channels.argtypes = [_f, _i, _i, _i, _f, _f]
+    L.zo_channel_attention.argtypes = [_f, _i, _i, _i, _i, _f, _f]
+    L.zo_dot8.argtypes = [_f, _f, _i64]
+    L.zo_dot8.restype = ctypes.c_double
+    L.zo_set_dump.argtypes = [DUMP_FN]
+    L.zo_synth_out_size.argtypes = [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]
+    L.zo_synthesis_primary.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _i, _i, _f]
+    L.zo_synthesis_secondary.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f, _i, _i,
+                                         _i, _i, _f]
+    L.zo_analysis_primary.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f]
+    L.zo_analysis_secondary.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f]
+    L.zo_synthesis_tiles.argtypes = [_i] * 6 + [ctypes.POINTER(Tile), _i]
+    L.zo_synthesize.argtypes = [ctypes.POINTER(Ckpt), ctypes.POINTER(Ckpt), _i, _f, _f] + \
+        [_i] * 10 + [_f, _f, _f]
+    L.zo_quantize_plane.argtypes = [_f, _i64, _i, ctypes.POINTER(ctypes.c_uint16)]
+    L.zo_resize_bicubic.argtypes = [_f, _i, _i, _i, _i, _i, _f]
+    L.zo_to_rgb_planes.argtypes = [_f, _f, _f, _i64]
+    L.zo_quantize_rgb.argtypes = [_f, _f, _f, _i64, _i, ctypes.POINTER(ctypes.c_uint16)]
+    L.zo_normalize.argtypes = [_f, _i64, _f]
+    L.zo_pad_amount.argtypes = [_i, _i]
+
+
+def _fp(a):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f)
+
+
+def _c32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def set_threads(n):
+    lib().zo_set_threads(int(n))
+
+
+def conv2d(x, w, b=None, stride=1, pad=(0, 0), groups=1, extra=(0, 0, 0, 0)):
+    """x [c,h,w], w [oc, c/groups, kh, kw] -> [oc, oh, ow] (reference.rs:92-133)."""
+    x, w = _c32(x), _c32(w)
+    c, h, wd = x.shape
+    oc, _, kh, kw = w.shape
+    ex = (_i * 4)(*extra)
+    oh, ow = _i(), _i()
+    lib().zo_conv2d_out_size(h, wd, kh, kw, stride, pad[0], pad[1], ex, oh, ow)
+    out = np.empty((oc, oh.value, ow.value), np.float32)
+    bb = _c32(b) if b is not None else None
+    r = lib().zo_conv2d(_fp(x), c, h, wd, _fp(w), _fp(bb) if bb is not None else None, oc, kh,
+                        kw, stride, pad[0], pad[1], groups, ex, _fp(out))
+    if r:
+        raise ValueError("oracle conv2d: bad geometry")
+    return out
+
+
+def conv_transpose2d(x, w, b=None, stride=2, pad=1, out_pad=0):
+    """x [c,h,w], w [c, oc, k, k] (reference.rs:204-236)."""
+    x, w = _c32(x), _c32(w)
+    c, h, wd = x.shape
+    _, oc, k, _ = w.shape
+    oh, ow = _i(), _i()
+    lib().zo_conv_transpose2d_out_size(h, wd, k, stride, pad, out_pad, oh, ow)
+    out = np.empty((oc, oh.value, ow.value), np.float32)
+    bb = _c32(b) if b is not None else None
+    r = lib().zo_conv_transpose2d(_fp(x), c, h, wd, _fp(w),
+                                  _fp(bb) if bb is not None else None, oc, k, stride, pad,
+                                  out_pad, _fp(out))
+    if r:
+        raise ValueError("oracle conv_transpose2d: bad geometry")
+    return out
+
+
+def pixel_shuffle(x, r):
+    x = _c32(x)
+    c, h, w = x.shape
+    out = np.empty((c // (r * r), h * r, w * r), np.float32)
+    if lib().zo_pixel_shuffle(_fp(x), c, h, w, r, _fp(out)):
+        raise ValueError("pixel_shuffle")
+    return out
+
+
+def _unary(name, x):
+    y = _c32(x).copy()
+    getattr(lib(), name)(_fp(y), y.size)
+    return y
+
+
+def relu(x):
+    return _unary("zo_relu", x)
+
+
+def relu6(x):
+    return _unary("zo_relu6", x)
+
+
+def sigmoid(x):
+    return _unary("zo_sigmoid", x)
+
+
+def denormalize(x):
+    return _unary("zo_denormalize", x)
+
+
+def _binary(name, a, b):
+    y = _c32(a).copy()
+    b = _c32(b)
+    assert y.size == b.size
+    getattr(lib(), name)(_fp(y), _fp(b), y.size)
+    return y
+
+
+def add(a, b):
+    return _binary("zo_add", a, b)
+
+
+def gate(x, m):
+    return _binary("zo_gate", x, m)
+
+
+def mul(a, b):
+    return _binary("zo_mul", a, b)
+
+
+def elu_gate(a, b):
+    return _binary("zo_elu_gate", a, b)
+
+
+def exp(x):
+    return np.array([lib().zo_exp(float(v)) for v in np.asarray(x, np.float32).ravel()],
+                    np.float32).reshape(np.shape(x))
+
+
+def leaky_relu(x, slope=0.01):
+    """torch.nn.functional.leaky_relu (not a reference op; used by the BASELINE configs)."""
+    x = _c32(x)
+    return np.where(x > 0, x, x * np.float32(slope)).astype(np.float32)
+
+
+def layer_norm_channels(x, w, b):
+    y = _c32(x).copy()
+    c, h, wd = y.shape
+    lib().zo_layer_norm_channels(_fp(y), c, h, wd, _fp(_c32(w)), _fp(_c32(b)))
+    return y
+
+
+def channel_attention(qkv, heads, temperature):
+    qkv = _c32(qkv)
+    c3, h, w = qkv.shape
+    out = np.empty((c3 // 3, h, w), np.float32)
+    if lib().zo_channel_attention(_fp(qkv), c3, h, w, heads, _fp(_c32(temperature)), _fp(out)):
+        raise ValueError("channel_attention")
+    return out
+
+
+def dot8(a, b):
+    a, b = _c32(a), _c32(b)
+    return lib().zo_dot8(_fp(a), _fp(b), a.size)
+
+
+class Checkpoint:
+    """Named f32 tensors handed to the C oracle (keeps the numpy buffers alive)."""
+
+    def __init__(self, params):
+        self.arrays = {k: _c32(v) for k, v in params.items()}
+        n = len(self.arrays)
+        self._p = (Param * n)()
+        self._names = []
+        for i, (k, v) in enumerate(self.arrays.items()):
+            nm = k.encode()
+            self._names.append(nm)
+            self._p[i].name = nm
+            self._p[i].ndim = v.ndim
+            for d in range(4):
+                self._p[i].shape[d] = v.shape[d] if d < v.ndim else 0
+            self._p[i].data = _fp(v)
+        self.ck = Ckpt(self._p, n)
+
+
+_dump_keep = []
+
+
+def set_dump(fn):
+    """fn(name, array) per intermediate map, or None."""
+    if fn is None:
+        cb = DUMP_FN()
+    else:
+        def _cb(name, data, c, h, w):
+            fn(name.decode(), np.ctypeslib.as_array(data, shape=(c, h, w)).copy())
+        cb = DUMP_FN(_cb)
+    _dump_keep[:] = [cb]
+    lib().zo_set_dump(cb)
+
+
+def synth_out_size(op, secondary, h, w):
+    oh, ow = _i(), _i()
+    lib().zo_synth_out_size(op, int(secondary), h, w, oh, ow)
+    return oh.value, ow.value
+
+
+def synthesis_primary(ck, op, y_hat, h, w):
+    y_hat = _c32(y_hat)
+    assert y_hat.shape[0] == 160
+    oh, ow = synth_out_size(op, 0, h, w)
+    out = np.empty((1, oh, ow), np.float32)
+    lib().zo_synthesis_primary(ctypes.byref(ck.ck), op, _fp(y_hat), y_hat.shape[1],
+                               y_hat.shape[2], h, w, _fp(out))
+    return out
+
+
+def synthesis_secondary(ck, op, y_luma, y_chroma, h, w):
+    y_luma, y_chroma = _c32(y_luma), _c32(y_chroma)
+    oh, ow = synth_out_size(op, 1, h, w)
+    out = np.empty((2, oh, ow), np.float32)
+    r = lib().zo_synthesis_secondary(ctypes.byref(ck.ck), op, _fp(y_luma), y_luma.shape[1],
+                                     y_luma.shape[2], _fp(y_chroma), y_chroma.shape[1],
+                                     y_chroma.shape[2], h, w, _fp(out))
+    if r:
+        raise ValueError("synthesis_secondary")
+    return out
+
+
+def analysis_primary(ck, op, x):
+    x = _c32(x)
+    _, h, w = x.shape
+    out = np.empty((160, -(-h // 16), -(-w // 16)), np.float32)
+    if lib().zo_analysis_primary(ctypes.byref(ck.ck), op, _fp(x), h, w, _fp(out)):
+        raise ValueError("analysis_primary")
+    return out
+
+
+def analysis_secondary(ck, op, x):
+    x = _c32(x)
+    _, h, w = x.shape
+    out = np.empty((96, -(-h // 8), -(-w // 8)), np.float32)
+    if lib().zo_analysis_secondary(ctypes.byref(ck.ck), op, _fp(x), h, w, _fp(out)):
+        raise ValueError("analysis_secondary")
+    return out
+
+
+def synthesis_tiles(height, width, lh, lw, tile_size, overlap):
+    n = lib().zo_synthesis_tiles(height, width, lh, lw, tile_size, overlap, None, 0)
+    if n <= 0:
+        raise ValueError("malformed synthesis tiling")
+    arr = (Tile * n)()
+    lib().zo_synthesis_tiles(height, width, lh, lw, tile_size, overlap, arr, n)
+    return [{k: getattr(t, k) for k, _ in Tile._fields_} for t in arr]
+
+
+def synthesize(ck_y, ck_uv, op, y_hat_y, y_hat_uv, height, width, out_h=None, out_w=None,
+               tile_size=0, overlap=0, sv=2, sh=2):
+    y_hat_y, y_hat_uv = _c32(y_hat_y), _c32(y_hat_uv)
+    _, lh, lw = y_hat_y.shape
+    out_h = height if out_h is None else out_h
+    out_w = width if out_w is None else out_w
+    ch, cw = -(-out_h // sv), -(-out_w // sh)
+    ry = np.zeros((out_h, out_w), np.float32)
+    ru = np.zeros((ch, cw), np.float32)
+    rv = np.zeros((ch, cw), np.float32)
+    r = lib().zo_synthesize(ctypes.byref(ck_y.ck), ctypes.byref(ck_uv.ck), op, _fp(y_hat_y),
+                            _fp(y_hat_uv), lh, lw, height, width, out_h, out_w, tile_size,
+                            overlap, sv, sh, _fp(ry), _fp(ru), _fp(rv))
+    if r:
+        raise ValueError("synthesize")
+    return ry, ru, rv
+
+
+def quantize_plane(x, bit_depth=8):
+    x = _c32(x)
+    out = np.empty(x.shape, np.uint16)
+    lib().zo_quantize_plane(_fp(x), x.size, bit_depth,
+                            out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)))
+    return out
+
+
+def resize_bicubic(x, out_h, out_w):
+    x = _c32(x)
+    c, h, w = x.shape
+    out = np.empty((c, out_h, out_w), np.float32)
+    if lib().zo_resize_bicubic(_fp(x), c, h, w, out_h, out_w, _fp(out)):
+        raise ValueError("resize_bicubic")
+    return out
+
+
+def to_rgb_planes(y, u, v):
+    r, g, b = _c32(y).copy(), _c32(u).copy(), _c32(v).copy()
+    lib().zo_to_rgb_planes(_fp(r), _fp(g), _fp(b), r.size)
+    return r, g, b
+
+
+def quantize_rgb(r, g, b, bit_depth=8):
+    r, g, b = _c32(r), _c32(g), _c32(b)
+    out = np.empty(r.shape + (3,), np.uint16)
+    lib().zo_quantize_rgb(_fp(r), _fp(g), _fp(b), r.size, bit_depth,
+                          out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)))
+    return out
+
+
+def pad_amount(n, d):
+    return lib().zo_pad_amount(n, d)

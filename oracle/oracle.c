@@ -1,0 +1,1057 @@
+/*
+ * CPU oracle for the JPEG AI synthesis / analysis path — TEST INFRASTRUCTURE ONLY.
+ * See oracle.h for what it restates and how it is pinned. Every function names the
+ * reference file:line (paths inside the imazen/zenjpegai crate) whose behaviour it follows.
+ *
+ * Build: `-O3 -ffp-contract=off`: the contract's multiply-adds are explicit `fmaf` calls and
+ * every other expression must round op by op, as Rust evaluates it (Rust never contracts).
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#include <stdio.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+static int g_threads = 1;
+static zo_dump_fn g_dump = NULL;
+
+void zo_set_threads(int n) { g_threads = n > 0 ? n : 1; }
+int zo_get_threads(void) { return g_threads; }
+void zo_set_dump(zo_dump_fn fn) { g_dump = fn; }
+
+static float clampf(float v, float lo, float hi) {
+    /* Rust f32::clamp: NaN passes through. */
+    if (v < lo) return lo;
+    if (v > hi) return hi;
+    return v;
+}
+
+/* ======================================================================================= */
+/* Convolution (reference.rs:16-133; layers.rs:100-115 for the extra zero border)            */
+/* ======================================================================================= */
+
+void zo_conv2d_out_size(int h, int w, int kh, int kw, int stride, int pad_h, int pad_w,
+                        const int extra[4], int *oh, int *ow) {
+    int et = extra ? extra[0] : 0, el = extra ? extra[1] : 0;
+    int eb = extra ? extra[2] : 0, er = extra ? extra[3] : 0;
+    *oh = (h + et + eb + 2 * pad_h - kh) / stride + 1;
+    *ow = (w + el + er + 2 * pad_w - kw) / stride + 1;
+}
+
+int zo_conv2d(const float *x, int c, int h, int w, const float *weight, const float *bias,
+              int oc, int kh, int kw, int stride, int pad_h, int pad_w, int groups,
+              const int extra[4], float *out) {
+    if (groups <= 0 || c % groups || oc % groups || stride <= 0 || kh <= 0 || kw <= 0)
+        return -1;
+    int et = extra ? extra[0] : 0, el = extra ? extra[1] : 0;
+    int eb = extra ? extra[2] : 0, er = extra ? extra[3] : 0;
+    int hh = h + et + eb, ww = w + el + er;
+    if (hh + 2 * pad_h < kh || ww + 2 * pad_w < kw) return -1;
+    int oh, ow;
+    zo_conv2d_out_size(h, w, kh, kw, stride, pad_h, pad_w, extra, &oh, &ow);
+    /* zero_pad (reference.rs:16-27) of the (extra-padded) input */
+    int ph = hh + 2 * pad_h, pw = ww + 2 * pad_w;
+    int top = et + pad_h, left = el + pad_w;
+    float *xp = (float *)calloc((size_t)c * ph * pw, sizeof(float));
+    if (!xp) return -2;
+    for (int ci = 0; ci < c; ci++)
+        for (int y = 0; y < h; y++)
+            memcpy(xp + ((size_t)ci * ph + y + top) * pw + left, x + ((size_t)ci * h + y) * w,
+                   sizeof(float) * w);
+    int icg = c / groups, ocg = oc / groups;
+    int wlen = icg * kh * kw;
+    /* conv_plane (reference.rs:47-89): per output row, acc = bias, then for i, ky, kx the
+     * contract's fma over the row. One output channel per task. */
+#pragma omp parallel for schedule(dynamic) num_threads(g_threads)
+    for (int o = 0; o < oc; o++) {
+        float *acc = (float *)malloc(sizeof(float) * ow);
+        int ic0 = (o / ocg) * icg;
+        const float *wt = weight + (size_t)o * wlen;
+        float b = bias ? bias[o] : 0.0f;
+        for (int oy = 0; oy < oh; oy++) {
+            for (int ox = 0; ox < ow; ox++) acc[ox] = b;
+            for (int i = 0; i < icg; i++) {
+                const float *plane = xp + (size_t)(ic0 + i) * ph * pw;
+                for (int ky = 0; ky < kh; ky++) {
+                    const float *row = plane + (size_t)(oy * stride + ky) * pw;
+                    for (int kx = 0; kx < kw; kx++) {
+                        float wv = wt[(i * kh + ky) * kw + kx];
+                        if (stride == 1) {
+                            const float *r = row + kx;
+                            for (int ox = 0; ox < ow; ox++) acc[ox] = fmaf(wv, r[ox], acc[ox]);
+                        } else {
+                            for (int ox = 0; ox < ow; ox++)
+                                acc[ox] = fmaf(wv, row[ox * stride + kx], acc[ox]);
+                        }
+                    }
+                }
+            }
+            memcpy(out + ((size_t)o * oh + oy) * ow, acc, sizeof(float) * ow);
+        }
+        free(acc);
+    }
+    free(xp);
+    return 0;
+}
+
+void zo_conv_transpose2d_out_size(int h, int w, int k, int stride, int pad, int out_pad,
+                                  int *oh, int *ow) {
+    *oh = (h - 1) * stride + k + out_pad - 2 * pad;
+    *ow = (w - 1) * stride + k + out_pad - 2 * pad;
+}
+
+/* conv_transpose2d / conv_transpose_plane (reference.rs:155-236). The reference walks, per
+ * output element, ic then ky then kx ascending over a copy zero-padded by `ext`, skipping the
+ * taps whose stride parity does not reach the element. Here the loops are interchanged so
+ * that each output plane is swept per (ic, ky, kx); every element still sees its taps in the
+ * same (ic, ky, kx) order, so the result is the same bits. */
+int zo_conv_transpose2d(const float *x, int c, int h, int w, const float *weight,
+                        const float *bias, int oc, int k, int stride, int pad, int out_pad,
+                        float *out) {
+    if (stride <= 0 || k <= 0 || pad >= k || out_pad >= stride || h <= 0 || w <= 0) return -1;
+    int oh, ow;
+    zo_conv_transpose2d_out_size(h, w, k, stride, pad, out_pad, &oh, &ow);
+    int ext = (k + stride - 1) / stride + 1;
+    int ph = h + 2 * ext, pw = w + 2 * ext;
+    float *xp = (float *)calloc((size_t)c * ph * pw, sizeof(float));
+    if (!xp) return -2;
+    for (int ci = 0; ci < c; ci++)
+        for (int y = 0; y < h; y++)
+            memcpy(xp + ((size_t)ci * ph + y + ext) * pw + ext, x + ((size_t)ci * h + y) * w,
+                   sizeof(float) * w);
+#pragma omp parallel for schedule(dynamic) num_threads(g_threads)
+    for (int o = 0; o < oc; o++) {
+        float *op = out + (size_t)o * oh * ow;
+        float b = bias ? bias[o] : 0.0f;
+        for (int64_t i = 0; i < (int64_t)oh * ow; i++) op[i] = b;
+        for (int ic = 0; ic < c; ic++) {
+            const float *plane = xp + (size_t)ic * ph * pw;
+            const float *wb = weight + ((size_t)ic * oc + o) * k * k;
+            for (int ky = 0; ky < k; ky++) {
+                for (int kx = 0; kx < k; kx++) {
+                    float wv = wb[ky * k + kx];
+                    for (int oy = 0; oy < oh; oy++) {
+                        int ty = oy + pad + ext * stride - ky;
+                        if (ty % stride) continue;
+                        const float *row = plane + (size_t)(ty / stride) * pw;
+                        float *orow = op + (size_t)oy * ow;
+                        /* first ox with matching column parity */
+                        int ox0 = 0;
+                        while (ox0 < ow && (ox0 + pad + ext * stride - kx) % stride) ox0++;
+                        for (int ox = ox0; ox < ow; ox += stride) {
+                            int tx = ox + pad + ext * stride - kx;
+                            orow[ox] = fmaf(wv, row[tx / stride], orow[ox]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    free(xp);
+    return 0;
+}
+
+/* pixel_shuffle (reference.rs:353-375) */
+int zo_pixel_shuffle(const float *x, int c4, int h, int w, int r, float *out) {
+    if (r <= 0 || c4 % (r * r)) return -1;
+    int c = c4 / (r * r);
+    for (int oc = 0; oc < c; oc++)
+        for (int dy = 0; dy < r; dy++)
+            for (int dx = 0; dx < r; dx++) {
+                const float *src = x + (size_t)(oc * r * r + dy * r + dx) * h * w;
+                for (int y = 0; y < h; y++) {
+                    float *dst = out + ((size_t)oc * h * r + (size_t)y * r + dy) * w * r;
+                    for (int xi = 0; xi < w; xi++) dst[xi * r + dx] = src[y * w + xi];
+                }
+            }
+    return 0;
+}
+
+/* ======================================================================================= */
+/* Pointwise ops (layers.rs:174-229; math.rs:28-62, 371-397)                                 */
+/* ======================================================================================= */
+
+void zo_relu(float *x, int64_t n) {
+    for (int64_t i = 0; i < n; i++) x[i] = x[i] > 0.0f ? x[i] : 0.0f;
+}
+void zo_relu6(float *x, int64_t n) {
+    for (int64_t i = 0; i < n; i++) x[i] = clampf(x[i], 0.0f, 6.0f);
+}
+void zo_add(float *dst, const float *src, int64_t n) {
+    for (int64_t i = 0; i < n; i++) dst[i] += src[i];
+}
+/* `x *= 1 + m`: two IEEE operations, not an FMA (layers.rs:195-201) */
+void zo_gate(float *x, const float *mask, int64_t n) {
+    for (int64_t i = 0; i < n; i++) x[i] *= 1.0f + mask[i];
+}
+void zo_mul(float *a, const float *b, int64_t n) {
+    for (int64_t i = 0; i < n; i++) a[i] *= b[i];
+}
+
+/* Cephes `expf` (math.rs:28-62): clamp to [-87, 88], n = floor(x log2e + 1/2), two-step
+ * Cody-Waite reduction by ln 2, degree-5 polynomial evaluated with separate multiplies and
+ * adds, then scaling by 2^n built from the exponent bits. Constants as Cephes prints them. */
+float zo_exp(float x) {
+    static const float LOG2E = 1.44269504088896340736f;
+    static const float LN2_HI = 0.693359375f;
+    static const float LN2_LO = -2.12194440e-4f;
+    static const float P0 = 1.9875691500e-4f, P1 = 1.3981999507e-3f, P2 = 8.3334519073e-3f,
+                       P3 = 4.1665795894e-2f, P4 = 1.6666665459e-1f, P5 = 5.0000001201e-1f;
+    x = clampf(x, -87.0f, 88.0f);
+    float n = floorf(x * LOG2E + 0.5f);
+    float r = x - n * LN2_HI;
+    r = r - n * LN2_LO;
+    float p = P0;
+    p = p * r + P1;
+    p = p * r + P2;
+    p = p * r + P3;
+    p = p * r + P4;
+    p = p * r + P5;
+    float y = p * (r * r) + r + 1.0f;
+    uint32_t bits = (uint32_t)((int32_t)n + 127) << 23;
+    float scale;
+    memcpy(&scale, &bits, 4);
+    return y * scale;
+}
+
+void zo_sigmoid(float *x, int64_t n) {
+    for (int64_t i = 0; i < n; i++) x[i] = 1.0f / (1.0f + zo_exp(-x[i]));
+}
+
+/* elu(a) * b (math.rs:66-72) */
+void zo_elu_gate(float *a, const float *b, int64_t n) {
+    for (int64_t i = 0; i < n; i++) {
+        float e = zo_exp(a[i]) - 1.0f;
+        float elu = a[i] > 0.0f ? a[i] : e;
+        a[i] = elu * b[i];
+    }
+}
+
+/* `x * 128 + 127.5` clamped to [0, 255] (synthesis.rs:188-192) */
+void zo_denormalize(float *x, int64_t n) {
+    for (int64_t i = 0; i < n; i++) x[i] = clampf(x[i] * 128.0f + 127.5f, 0.0f, 255.0f);
+}
+
+/* `(x - 127.5) / 128` (analysis.rs:36-39) */
+void zo_normalize(const float *x, int64_t n, float *out) {
+    for (int64_t i = 0; i < n; i++) out[i] = (x[i] - 127.5f) / 128.0f;
+}
+
+int zo_pad_amount(int len, int divider) {
+    return 2 * ((len + 2 * divider - 1) / (2 * divider)) - (len + divider - 1) / divider;
+}
+
+/* ======================================================================================= */
+/* Layer norm and channel attention (math.rs:399-603)                                        */
+/* ======================================================================================= */
+
+int zo_layer_norm_channels(float *x, int c, int h, int w, const float *weight,
+                           const float *bias) {
+    if (c <= 0) return -1;
+    int64_t n = (int64_t)h * w;
+    double *mean = (double *)calloc(n, sizeof(double));
+    double *var = (double *)calloc(n, sizeof(double));
+    float *mean32 = (float *)malloc(sizeof(float) * n);
+    float *denom = (float *)malloc(sizeof(float) * n);
+    for (int ch = 0; ch < c; ch++) {
+        const float *p = x + ch * n;
+        for (int64_t i = 0; i < n; i++) mean[i] += (double)p[i];
+    }
+    for (int64_t i = 0; i < n; i++) mean[i] /= (double)c;
+    for (int ch = 0; ch < c; ch++) {
+        const float *p = x + ch * n;
+        for (int64_t i = 0; i < n; i++) {
+            double d = (double)p[i] - mean[i];
+            var[i] += d * d;
+        }
+    }
+    for (int64_t i = 0; i < n; i++) {
+        mean32[i] = (float)mean[i];
+        denom[i] = sqrtf((float)(var[i] / (double)c) + 1e-5f);
+    }
+    for (int ch = 0; ch < c; ch++) {
+        float *p = x + ch * n;
+        float wv = weight[ch], bv = bias[ch];
+        for (int64_t i = 0; i < n; i++) p[i] = (p[i] - mean32[i]) / denom[i] * wv + bv;
+    }
+    free(mean);
+    free(var);
+    free(mean32);
+    free(denom);
+    return 0;
+}
+
+/* Eight interleaved f64 accumulators (index mod 8), combined pairwise (math.rs:452-465). */
+double zo_dot8(const float *a, const float *b, int64_t n) {
+    double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int64_t full = n / 8 * 8;
+    for (int64_t i = 0; i < full; i += 8)
+        for (int l = 0; l < 8; l++) acc[l] += (double)a[i + l] * (double)b[i + l];
+    for (int64_t i = full; i < n; i++) acc[i - full] += (double)a[i] * (double)b[i];
+    return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+}
+
+/* channel_attention_impl, exact (non-approximate) precision (math.rs:512-603):
+ * q, k rows L2-normalised over the pixels (norm from dot8 in f64, eps 1e-12), per head the
+ * c x c Gram q_i . k_j (dot8, narrowed to f32) times temperature[head], row softmax with the
+ * max subtracted and Cephes exp, f64 sum, f32 divide; out_i = sum_j a_ij v_j in f64. */
+int zo_channel_attention(const float *qkv, int c3, int h, int w, int heads,
+                         const float *temperature, float *out) {
+    if (heads <= 0 || c3 % (3 * heads)) return -1;
+    int dim = c3 / 3, c = dim / heads;
+    int64_t n = (int64_t)h * w;
+    float *qk = (float *)malloc(sizeof(float) * 2 * dim * n);
+    memcpy(qk, qkv, sizeof(float) * 2 * dim * n);
+#pragma omp parallel for schedule(dynamic) num_threads(g_threads)
+    for (int r = 0; r < 2 * dim; r++) {
+        float *row = qk + (int64_t)r * n;
+        float norm = (float)sqrt(zo_dot8(row, row, n));
+        float d = norm > 1e-12f ? norm : 1e-12f;
+        for (int64_t i = 0; i < n; i++) row[i] /= d;
+    }
+    const float *q = qk, *k = qk + (int64_t)dim * n, *v = qkv + (int64_t)2 * dim * n;
+    float *attn = (float *)malloc(sizeof(float) * dim * c);
+#pragma omp parallel for schedule(dynamic) num_threads(g_threads)
+    for (int ri = 0; ri < dim; ri++) {
+        int head = ri / c;
+        float *row = attn + (int64_t)ri * c;
+        const float *qi = q + (int64_t)ri * n;
+        float mx = -INFINITY;
+        for (int j = 0; j < c; j++) {
+            const float *kj = k + (int64_t)(head * c + j) * n;
+            row[j] = (float)zo_dot8(qi, kj, n) * temperature[head];
+            mx = row[j] > mx ? row[j] : mx;
+        }
+        for (int j = 0; j < c; j++) row[j] = zo_exp(row[j] - mx);
+        double sum = 0.0;
+        for (int j = 0; j < c; j++) sum += (double)row[j];
+        float s32 = (float)sum;
+        for (int j = 0; j < c; j++) row[j] /= s32;
+    }
+#pragma omp parallel for schedule(dynamic) num_threads(g_threads)
+    for (int ri = 0; ri < dim; ri++) {
+        int head = ri / c;
+        const float *wts = attn + (int64_t)ri * c;
+        double *acc = (double *)calloc(n, sizeof(double));
+        for (int j = 0; j < c; j++) {
+            double a = (double)wts[j];
+            const float *vj = v + (int64_t)(head * c + j) * n;
+            for (int64_t i = 0; i < n; i++) acc[i] += a * (double)vj[i];
+        }
+        float *o = out + (int64_t)ri * n;
+        for (int64_t i = 0; i < n; i++) o[i] = (float)acc[i];
+        free(acc);
+    }
+    free(attn);
+    free(qk);
+    return 0;
+}
+
+/* ======================================================================================= */
+/* Network plumbing: planar tensors and checkpoint lookups (model/load.rs:11-85)             */
+/* ======================================================================================= */
+
+typedef struct {
+    int c, h, w;
+    float *d;
+} T;
+
+static T t_new(int c, int h, int w) {
+    T t = {c, h, w, (float *)calloc((size_t)c * h * w, sizeof(float))};
+    return t;
+}
+static void t_free(T *t) {
+    free(t->d);
+    t->d = NULL;
+}
+static int64_t t_len(const T *t) { return (int64_t)t->c * t->h * t->w; }
+static T t_clone(const T *t) {
+    T o = t_new(t->c, t->h, t->w);
+    memcpy(o.d, t->d, sizeof(float) * t_len(t));
+    return o;
+}
+static void t_move(T *dst, T src) {
+    t_free(dst);
+    *dst = src;
+}
+static void dump(const char *name, const T *t) {
+    if (g_dump) g_dump(name, t->d, t->c, t->h, t->w);
+}
+
+#define ZO_FAIL(msg)                                                \
+    do {                                                            \
+        fprintf(stderr, "oracle: %s\n", msg);                       \
+        abort();                                                    \
+    } while (0)
+
+static const zo_param *find(const zo_ckpt *ck, const char *name) {
+    for (int i = 0; i < ck->n; i++)
+        if (strcmp(ck->params[i].name, name) == 0) return &ck->params[i];
+    return NULL;
+}
+
+static const float *need(const zo_ckpt *ck, const char *prefix, const char *suffix, int n0,
+                         int n1, int n2, int n3) {
+    char name[256];
+    snprintf(name, sizeof name, "%s.%s", prefix, suffix);
+    const zo_param *p = find(ck, name);
+    if (!p) {
+        fprintf(stderr, "oracle: missing parameter %s\n", name);
+        abort();
+    }
+    int want[4] = {n0, n1, n2, n3};
+    int nd = n3 >= 0 ? 4 : n2 >= 0 ? 3 : n1 >= 0 ? 2 : 1;
+    if (p->ndim != nd) {
+        fprintf(stderr, "oracle: %s has ndim %d, expected %d\n", name, p->ndim, nd);
+        abort();
+    }
+    for (int i = 0; i < nd; i++)
+        if (p->shape[i] != want[i]) {
+            fprintf(stderr, "oracle: %s dim %d is %d, expected %d\n", name, i, p->shape[i],
+                    want[i]);
+            abort();
+        }
+    return p->data;
+}
+
+/* load::conv (load.rs:11-40) + ConvLayer::forward */
+static T conv_layer(const zo_ckpt *ck, const char *prefix, const T *x, int out_ch, int kh,
+                    int kw, int stride, int pad, int groups, int bias, const int extra[4]) {
+    if (x->c % groups) ZO_FAIL("groups");
+    const float *w = need(ck, prefix, "weight", out_ch, x->c / groups, kh, kw);
+    const float *b = bias ? need(ck, prefix, "bias", out_ch, -1, -1, -1) : NULL;
+    int oh, ow;
+    zo_conv2d_out_size(x->h, x->w, kh, kw, stride, pad, pad, extra, &oh, &ow);
+    T o = t_new(out_ch, oh, ow);
+    if (zo_conv2d(x->d, x->c, x->h, x->w, w, b, out_ch, kh, kw, stride, pad, pad, groups,
+                  extra, o.d))
+        ZO_FAIL("conv2d");
+    return o;
+}
+static T conv3x3(const zo_ckpt *ck, const char *prefix, const T *x, int out_ch, int groups,
+                 int bias) {
+    return conv_layer(ck, prefix, x, out_ch, 3, 3, 1, 1, groups, bias, NULL);
+}
+static T conv1x1(const zo_ckpt *ck, const char *prefix, const T *x, int out_ch, int bias) {
+    return conv_layer(ck, prefix, x, out_ch, 1, 1, 1, 0, 1, bias, NULL);
+}
+static T conv3x3_s2(const zo_ckpt *ck, const char *prefix, const T *x, int out_ch) {
+    return conv_layer(ck, prefix, x, out_ch, 3, 3, 2, 1, 1, 1, NULL);
+}
+/* load::conv_transpose (load.rs:64-85): always with bias */
+static T convt(const zo_ckpt *ck, const char *prefix, const T *x, int out_ch, int k,
+               int stride, int pad, int out_pad) {
+    const float *w = need(ck, prefix, "weight", x->c, out_ch, k, k);
+    const float *b = need(ck, prefix, "bias", out_ch, -1, -1, -1);
+    int oh, ow;
+    zo_conv_transpose2d_out_size(x->h, x->w, k, stride, pad, out_pad, &oh, &ow);
+    T o = t_new(out_ch, oh, ow);
+    if (zo_conv_transpose2d(x->d, x->c, x->h, x->w, w, b, out_ch, k, stride, pad, out_pad,
+                            o.d))
+        ZO_FAIL("conv_transpose2d");
+    return o;
+}
+/* conv3x3_t (attention.rs:80-91): k3 s2 p1 op1 */
+static T convt3(const zo_ckpt *ck, const char *prefix, const T *x, int out_ch) {
+    return convt(ck, prefix, x, out_ch, 3, 2, 1, 1);
+}
+
+static T crop(const T *x, int h, int w) {
+    if (h > x->h || w > x->w) ZO_FAIL("crop larger than tensor");
+    T o = t_new(x->c, h, w);
+    for (int c = 0; c < x->c; c++)
+        for (int y = 0; y < h; y++)
+            memcpy(o.d + ((size_t)c * h + y) * w, x->d + ((size_t)c * x->h + y) * x->w,
+                   sizeof(float) * w);
+    return o;
+}
+
+static T pixel_shuffle_t(const T *x, int r) {
+    T o = t_new(x->c / (r * r), x->h * r, x->w * r);
+    if (zo_pixel_shuffle(x->d, x->c, x->h, x->w, r, o.d)) ZO_FAIL("pixel_shuffle");
+    return o;
+}
+
+static int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+/* ResAu::load / forward (synthesis.rs:24-74): y = x * (1 + conv1x1(gconv3x3(relu6 x))) */
+static void resau(const zo_ckpt *ck, const char *prefix, T *x) {
+    char name[256];
+    snprintf(name, sizeof name, "%s.conv.weight", prefix);
+    const zo_param *p = find(ck, name);
+    if (!p || p->ndim != 4 || p->shape[1] <= 0 || x->c % p->shape[1]) ZO_FAIL(name);
+    int groups = x->c / p->shape[1];
+    T act = t_clone(x);
+    zo_relu6(act.d, t_len(&act));
+    char pc[256], pc2[256];
+    snprintf(pc, sizeof pc, "%s.conv", prefix);
+    snprintf(pc2, sizeof pc2, "%s.conv2", prefix);
+    T t = conv3x3(ck, pc, &act, x->c, groups, 0);
+    t_free(&act);
+    T mask = conv1x1(ck, pc2, &t, x->c, 0);
+    t_free(&t);
+    zo_gate(x->d, mask.d, t_len(x));
+    t_free(&mask);
+}
+
+/* ResidualBlock::forward (attention.rs:36-43): conv2(relu(conv1 x)) + x */
+static T residual_block(const zo_ckpt *ck, const char *prefix, const T *x) {
+    char p1[256], p2[256];
+    snprintf(p1, sizeof p1, "%s.conv1", prefix);
+    snprintf(p2, sizeof p2, "%s.conv2", prefix);
+    T t = conv3x3(ck, p1, x, x->c, 1, 1);
+    zo_relu(t.d, t_len(&t));
+    T out = conv3x3(ck, p2, &t, x->c, 1, 1);
+    t_free(&t);
+    zo_add(out.d, x->d, t_len(&out));
+    return out;
+}
+
+/* Cab::forward (attention.rs:122-139): x + RB(RB(x)) * sigmoid(convT(RB(RB(conv_s2 x)))) */
+static T cab(const zo_ckpt *ck, const char *prefix, const T *x) {
+    char p[256];
+    snprintf(p, sizeof p, "%s.residual_trunk.0", prefix);
+    T trunk = residual_block(ck, p, x);
+    snprintf(p, sizeof p, "%s.residual_trunk.1", prefix);
+    t_move(&trunk, residual_block(ck, p, &trunk));
+    snprintf(p, sizeof p, "%s.subscale", prefix);
+    T m = conv3x3_s2(ck, p, x, x->c);
+    snprintf(p, sizeof p, "%s.residual_mask2.0", prefix);
+    t_move(&m, residual_block(ck, p, &m));
+    snprintf(p, sizeof p, "%s.residual_mask3.0", prefix);
+    t_move(&m, residual_block(ck, p, &m));
+    snprintf(p, sizeof p, "%s.upscale", prefix);
+    t_move(&m, convt3(ck, p, &m, x->c));
+    if (m.h != trunk.h || m.w != trunk.w) ZO_FAIL("CAB: odd feature map size");
+    zo_sigmoid(m.d, t_len(&m));
+    zo_mul(trunk.d, m.d, t_len(&trunk));
+    zo_add(trunk.d, x->d, t_len(&trunk));
+    t_free(&m);
+    return trunk;
+}
+
+/* TransformerBlock::forward (attention.rs:328-372); heads 4, FFN gamma 4 */
+static void transformer_block(const zo_ckpt *ck, const char *prefix, T *x) {
+    int dim = x->c, hidden = dim * 4;
+    char p[256];
+    /* x = x + project_out(attn(dw(conv1(LN(x))))) */
+    snprintf(p, sizeof p, "%s.prep_data.norm1", prefix);
+    T t = t_clone(x);
+    zo_layer_norm_channels(t.d, t.c, t.h, t.w, need(ck, p, "weight", dim, -1, -1, -1),
+                           need(ck, p, "bias", dim, -1, -1, -1));
+    snprintf(p, sizeof p, "%s.prep_data.conv1", prefix);
+    t_move(&t, conv1x1(ck, p, &t, 3 * dim, 0));
+    snprintf(p, sizeof p, "%s.prep_data.conv2", prefix);
+    t_move(&t, conv3x3(ck, p, &t, 3 * dim, 3 * dim, 0));
+    snprintf(p, sizeof p, "%s.attn", prefix);
+    const float *temp = need(ck, p, "temperature", 4, 1, 1, -1);
+    T a = t_new(dim, x->h, x->w);
+    zo_channel_attention(t.d, t.c, t.h, t.w, 4, temp, a.d);
+    t_free(&t);
+    snprintf(p, sizeof p, "%s.attn.project_out", prefix);
+    t_move(&a, conv1x1(ck, p, &a, dim, 0));
+    zo_add(x->d, a.d, t_len(x));
+    t_free(&a);
+    /* x = x + project_out(elu(first half) * second half of dw(project_in(LN(x)))) */
+    snprintf(p, sizeof p, "%s.ffn.norm1", prefix);
+    t = t_clone(x);
+    zo_layer_norm_channels(t.d, t.c, t.h, t.w, need(ck, p, "weight", dim, -1, -1, -1),
+                           need(ck, p, "bias", dim, -1, -1, -1));
+    snprintf(p, sizeof p, "%s.ffn.project_in", prefix);
+    t_move(&t, conv1x1(ck, p, &t, 2 * hidden, 0));
+    snprintf(p, sizeof p, "%s.ffn.dwconv", prefix);
+    t_move(&t, conv3x3(ck, p, &t, 2 * hidden, 2 * hidden, 0));
+    int64_t n = (int64_t)hidden * t.h * t.w;
+    zo_elu_gate(t.d, t.d + n, n);
+    t.c = hidden;
+    snprintf(p, sizeof p, "%s.ffn.project_out", prefix);
+    T f = conv1x1(ck, p, &t, dim, 0);
+    t_free(&t);
+    zo_add(x->d, f.d, t_len(x));
+    t_free(&f);
+}
+
+/* Tam::forward (attention.rs:530-545) */
+static void tam(const zo_ckpt *ck, const char *prefix, T *x, int downsample) {
+    char p[256];
+    if (downsample) {
+        snprintf(p, sizeof p, "%s.ds_conv", prefix);
+        t_move(x, conv3x3_s2(ck, p, x, x->c));
+    }
+    snprintf(p, sizeof p, "%s.TABs.0", prefix);
+    transformer_block(ck, p, x);
+    snprintf(p, sizeof p, "%s.TABs.1", prefix);
+    transformer_block(ck, p, x);
+    if (downsample) {
+        snprintf(p, sizeof p, "%s.us_conv", prefix);
+        t_move(x, convt3(ck, p, x, x->c));
+    }
+}
+
+/* Upsample (synthesis.rs:117-171): BOP convT 4x4 s2 p1; SOP pad(0,1,0,1) + conv2x2 + PS2 */
+static T upsample(const zo_ckpt *ck, int op, const char *prefix, const T *x, int out_ch) {
+    if (op == ZO_BOP) return convt(ck, prefix, x, out_ch, 4, 2, 1, 0);
+    char p[256];
+    snprintf(p, sizeof p, "%s.conv", prefix);
+    static const int extra[4] = {0, 0, 1, 1};
+    T t = conv_layer(ck, p, x, out_ch * 4, 2, 2, 1, 0, 1, 0, extra);
+    T o = pixel_shuffle_t(&t, 2);
+    t_free(&t);
+    return o;
+}
+
+void zo_synth_out_size(int op, int secondary, int h, int w, int *oh, int *ow) {
+    if (op == ZO_HOP && !secondary) {
+        *oh = 2 * cdiv(h, 2);
+        *ow = 2 * cdiv(w, 2);
+    } else if (op == ZO_HOP) {
+        *oh = 4 * cdiv(h, 4);
+        *ow = 4 * cdiv(w, 4);
+    } else if (!secondary) {
+        *oh = 4 * cdiv(h, 4);
+        *ow = 4 * cdiv(w, 4);
+    } else {
+        *oh = 8 * cdiv(h, 8);
+        *ow = 8 * cdiv(w, 8);
+    }
+}
+
+/* LightPrimary::forward (synthesis.rs:514-580); (c1, c2, c3) = SOP (64,32,32), BOP (64,64,96) */
+static T light_primary(const zo_ckpt *ck, int op, const T *y, int h, int w) {
+    int c1 = 64, c2 = op == ZO_SOP ? 32 : 64, c3 = op == ZO_SOP ? 32 : 96;
+    T x = conv3x3(ck, "first_stage.0.0.conv1", y, 160, 1, 1);
+    zo_relu(x.d, t_len(&x));
+    zo_add(x.d, y->d, t_len(&x));
+    dump("res", &x);
+    t_move(&x, upsample(ck, op, "first_stage.1", &x, c1));
+    dump("up1", &x);
+    resau(ck, "first_stage.2", &x);
+    t_move(&x, crop(&x, cdiv(h, 8), cdiv(w, 8)));
+    dump("act1", &x);
+    t_move(&x, upsample(ck, op, "conv2_t", &x, c2));
+    t_move(&x, crop(&x, cdiv(h, 4), cdiv(w, 4)));
+    dump("up2", &x);
+    resau(ck, "iact2", &x);
+    dump("act2", &x);
+    t_move(&x, conv3x3(ck, "conv3", &x, c3, 1, 1));
+    dump("conv3", &x);
+    resau(ck, "iact3", &x);
+    dump("act3", &x);
+    t_move(&x, conv1x1(ck, "conv4", &x, 16, 0));
+    t_move(&x, pixel_shuffle_t(&x, 4));
+    zo_denormalize(x.d, t_len(&x));
+    dump("out", &x);
+    return x;
+}
+
+/* HopPrimary::forward (synthesis.rs:324-390) */
+static T hop_primary(const zo_ckpt *ck, const T *y, int h, int w) {
+    const int c = 128;
+    T x = residual_block(ck, "first_stage.0.0", y);
+    dump("res", &x);
+    t_move(&x, convt3(ck, "first_stage.1", &x, c));
+    dump("up1", &x);
+    resau(ck, "first_stage.2", &x);
+    t_move(&x, crop(&x, cdiv(h, 8), cdiv(w, 8)));
+    dump("act1", &x);
+    t_move(&x, convt3(ck, "conv2_t", &x, c));
+    dump("up2", &x);
+    t_move(&x, cab(ck, "CAB", &x));
+    t_move(&x, crop(&x, cdiv(h, 4), cdiv(w, 4)));
+    dump("cab", &x);
+    resau(ck, "iact2", &x);
+    dump("act2", &x);
+    t_move(&x, conv1x1(ck, "conv3_t", &x, 4 * c, 1));
+    t_move(&x, pixel_shuffle_t(&x, 2));
+    dump("conv3", &x);
+    tam(ck, "TAM", &x, 1);
+    t_move(&x, crop(&x, cdiv(h, 2), cdiv(w, 2)));
+    dump("tam", &x);
+    resau(ck, "iact3", &x);
+    dump("act3", &x);
+    t_move(&x, convt3(ck, "conv4_t", &x, 1));
+    zo_denormalize(x.d, t_len(&x));
+    dump("out", &x);
+    return x;
+}
+
+int zo_synthesis_primary(const zo_ckpt *ck, int op, const float *y_hat, int lh, int lw, int h,
+                         int w, float *out) {
+    T y = {160, lh, lw, (float *)y_hat};
+    T x = op == ZO_HOP ? hop_primary(ck, &y, h, w) : light_primary(ck, op, &y, h, w);
+    memcpy(out, x.d, sizeof(float) * t_len(&x));
+    t_free(&x);
+    return 0;
+}
+
+/* LightSecondary::forward (synthesis.rs:862-909); (c2, c3) = SOP (32,32), BOP (64,128) */
+static T light_secondary(const zo_ckpt *ck, int op, const T *x0, int h, int w) {
+    int c2 = op == ZO_SOP ? 32 : 64, c3 = op == ZO_SOP ? 32 : 128;
+    T x = upsample(ck, op, "conv2_t", x0, c2);
+    t_move(&x, crop(&x, cdiv(h, 8), cdiv(w, 8)));
+    dump("uv.up", &x);
+    resau(ck, "iact2", &x);
+    dump("uv.act2", &x);
+    t_move(&x, conv3x3(ck, "conv3", &x, c3, 1, 1));
+    dump("uv.conv3", &x);
+    resau(ck, "iact3", &x);
+    dump("uv.act3", &x);
+    t_move(&x, conv1x1(ck, "conv4", &x, 128, 0));
+    t_move(&x, pixel_shuffle_t(&x, 8));
+    return x;
+}
+
+/* HopSecondary::forward (synthesis.rs:723-773) */
+static T hop_secondary(const zo_ckpt *ck, const T *x0, int h, int w) {
+    const int c = 64;
+    T x = convt3(ck, "conv2_t", x0, c);
+    dump("uv.up", &x);
+    t_move(&x, cab(ck, "CAB", &x));
+    t_move(&x, crop(&x, cdiv(h, 8), cdiv(w, 8)));
+    dump("uv.cab", &x);
+    resau(ck, "iact2", &x);
+    dump("uv.act2", &x);
+    t_move(&x, conv1x1(ck, "conv3_t", &x, 4 * c, 1));
+    t_move(&x, pixel_shuffle_t(&x, 2));
+    dump("uv.conv3", &x);
+    tam(ck, "TAM", &x, 0);
+    t_move(&x, crop(&x, cdiv(h, 4), cdiv(w, 4)));
+    dump("uv.tam", &x);
+    resau(ck, "iact3", &x);
+    dump("uv.act3", &x);
+    t_move(&x, convt3(ck, "conv4_t", &x, 8));
+    t_move(&x, pixel_shuffle_t(&x, 2));
+    return x;
+}
+
+int zo_synthesis_secondary(const zo_ckpt *ck, int op, const float *y_hat_luma, int llh,
+                           int llw, const float *y_hat_chroma, int lh, int lw, int h, int w,
+                           float *out) {
+    /* forward_with (synthesis.rs:1004-1038): the luma latent is cropped to the chroma one */
+    if (lh > llh || lw > llw) return -1;
+    T cat = t_new(256, lh, lw);
+    for (int c = 0; c < 160; c++)
+        for (int y = 0; y < lh; y++)
+            memcpy(cat.d + ((size_t)c * lh + y) * lw, y_hat_luma + ((size_t)c * llh + y) * llw,
+                   sizeof(float) * lw);
+    memcpy(cat.d + (size_t)160 * lh * lw, y_hat_chroma, sizeof(float) * 96 * lh * lw);
+    T info = conv3x3(ck, "first_stage.conv1", &cat, 48, 1, 1);
+    t_free(&cat);
+    dump("uv.combine", &info);
+    T x = t_new(144, lh, lw);
+    memcpy(x.d, info.d, sizeof(float) * t_len(&info));
+    memcpy(x.d + t_len(&info), y_hat_chroma, sizeof(float) * 96 * lh * lw);
+    t_free(&info);
+    T o = op == ZO_HOP ? hop_secondary(ck, &x, h, w) : light_secondary(ck, op, &x, h, w);
+    t_free(&x);
+    zo_denormalize(o.d, t_len(&o));
+    dump("uv.out", &o);
+    memcpy(out, o.d, sizeof(float) * t_len(&o));
+    t_free(&o);
+    return 0;
+}
+
+/* ======================================================================================= */
+/* Analysis (analysis.rs:96-311)                                                              */
+/* ======================================================================================= */
+
+/* replicate_pad (analysis.rs:48-71) */
+static T replicate_pad(const T *x, int bottom, int right) {
+    T o = t_new(x->c, x->h + bottom, x->w + right);
+    for (int c = 0; c < x->c; c++)
+        for (int y = 0; y < o.h; y++) {
+            int sy = y < x->h ? y : x->h - 1;
+            const float *src = x->d + ((size_t)c * x->h + sy) * x->w;
+            float *dst = o.d + ((size_t)c * o.h + y) * o.w;
+            memcpy(dst, src, sizeof(float) * x->w);
+            for (int xx = x->w; xx < o.w; xx++) dst[xx] = src[x->w - 1];
+        }
+    return o;
+}
+
+/* pad_for (analysis.rs:74-83) */
+static T pad_for(const T *x, int h, int w, int divider) {
+    if (x->h != cdiv(h, divider) || x->w != cdiv(w, divider)) ZO_FAIL("analysis map size");
+    return replicate_pad(x, zo_pad_amount(h, divider), zo_pad_amount(w, divider));
+}
+
+/* Trunk::forward (analysis.rs:157-206), clip off */
+static T trunk(const zo_ckpt *ck, int op, const T *xin, int tam_ds) {
+    int h = xin->h, w = xin->w;
+    const int C = 128;
+    T n = t_new(xin->c, h, w);
+    zo_normalize(xin->d, t_len(xin), n.d);
+    T p = pad_for(&n, h, w, 1);
+    t_free(&n);
+    T x = conv_layer(ck, "conv1", &p, C, 3, 3, 2, 1, 1, 1, NULL);
+    t_free(&p);
+    resau(ck, "act1", &x);
+    dump("ana.act1", &x);
+    t_move(&x, pad_for(&x, h, w, 2));
+    if (op == ZO_HOP) tam(ck, "TAM", &x, tam_ds);
+    t_move(&x, conv_layer(ck, "conv2", &x, C, 3, 3, 2, 1, 1, 1, NULL));
+    resau(ck, "act2", &x);
+    dump("ana.act2", &x);
+    t_move(&x, pad_for(&x, h, w, 4));
+    if (op == ZO_HOP) t_move(&x, cab(ck, "cab", &x));
+    t_move(&x, conv_layer(ck, "conv3", &x, C, 3, 3, 2, 1, 1, 1, NULL));
+    resau(ck, "act3", &x);
+    dump("ana.act3", &x);
+    return x;
+}
+
+int zo_analysis_primary(const zo_ckpt *ck, int op, const float *xin, int h, int w,
+                        float *out) {
+    if (op == ZO_SOP) return -1;
+    T in = {1, h, w, (float *)xin};
+    T t = trunk(ck, op, &in, 1);
+    t_move(&t, pad_for(&t, h, w, 8));
+    t_move(&t, conv_layer(ck, "conv4", &t, 160, 3, 3, 2, 1, 1, 1, NULL));
+    t_move(&t, conv1x1(ck, "conv5", &t, 160, 0));
+    dump("ana.out", &t);
+    memcpy(out, t.d, sizeof(float) * t_len(&t));
+    t_free(&t);
+    return 0;
+}
+
+int zo_analysis_secondary(const zo_ckpt *ck, int op, const float *xin, int h, int w,
+                          float *out) {
+    if (op == ZO_SOP) return -1;
+    T in = {12, h, w, (float *)xin};
+    T t = trunk(ck, op, &in, 0);
+    t_move(&t, conv1x1(ck, "conv5", &t, 96, 0));
+    dump("ana.uv.out", &t);
+    memcpy(out, t.d, sizeof(float) * t_len(&t));
+    t_free(&t);
+    return 0;
+}
+
+/* ======================================================================================= */
+/* Tiling (tiles.rs:39-119, 220-229) and whole-picture synthesis (reconstruct.rs:274-464)   */
+/* ======================================================================================= */
+
+static int latent_extent(int pos, int len, int latent_len, int *out) {
+    if (len % 16 && cdiv(pos + len, 16) < latent_len) return -1;
+    *out = cdiv(len, 16);
+    return 0;
+}
+
+int zo_synthesis_tiles(int height, int width, int latent_h, int latent_w, int tile_size,
+                       int overlap, zo_tile *tiles, int max_tiles) {
+    if (tile_size <= 0) {
+        if (max_tiles >= 1) {
+            zo_tile t = {0, 0, width, height, 0, 0, latent_w, latent_h,
+                         0, 0, width, height, 0, 0};
+            tiles[0] = t;
+        }
+        return 1;
+    }
+    int tile_h = tile_size < height ? tile_size : height;
+    int tile_w = tile_size < width ? tile_size : width;
+    int half = overlap / 2;
+    if (tile_h <= overlap || tile_w <= overlap) return -1;
+    int n = 0;
+    for (int y = 0; y < height - overlap; y += tile_h - overlap)
+        for (int x = 0; x < width - overlap; x += tile_w - overlap) {
+            zo_tile t;
+            t.img_x = x;
+            t.img_y = y;
+            t.img_w = tile_w < width - x ? tile_w : width - x;
+            t.img_h = tile_h < height - y ? tile_h : height - y;
+            t.lat_x = x / 16;
+            t.lat_y = y / 16;
+            if (latent_extent(t.img_x, t.img_w, latent_w, &t.lat_w)) return -1;
+            if (latent_extent(t.img_y, t.img_h, latent_h, &t.lat_h)) return -1;
+            if (t.lat_x + t.lat_w > latent_w || t.lat_y + t.lat_h > latent_h) return -1;
+            int left = t.img_x == 0 ? 0 : half;
+            int top = t.img_y == 0 ? 0 : half;
+            int right = t.img_x + t.img_w >= width ? 0 : half;
+            int bottom = t.img_y + t.img_h >= height ? 0 : half;
+            if (t.img_w <= left + right || t.img_h <= top + bottom) return -1;
+            t.core_x = t.img_x + left;
+            t.core_y = t.img_y + top;
+            t.core_w = t.img_w - left - right;
+            t.core_h = t.img_h - top - bottom;
+            t.off_x = left;
+            t.off_y = top;
+            if (n < max_tiles) tiles[n] = t;
+            n++;
+        }
+    return n;
+}
+
+/* Tensor::window of a planar latent */
+static T window(const float *src, int c, int h, int w, int x0, int y0, int ww, int hh) {
+    T o = t_new(c, hh, ww);
+    for (int ci = 0; ci < c; ci++)
+        for (int y = 0; y < hh; y++)
+            memcpy(o.d + ((size_t)ci * hh + y) * ww, src + ((size_t)ci * h + y0 + y) * w + x0,
+                   sizeof(float) * ww);
+    return o;
+}
+
+int zo_synthesize(const zo_ckpt *ck_y, const zo_ckpt *ck_uv, int op, const float *y_hat_y,
+                  const float *y_hat_uv, int lh, int lw, int height, int width, int out_h,
+                  int out_w, int tile_size, int overlap, int sv, int sh, float *rec_y,
+                  float *rec_u, float *rec_v) {
+    int nt = zo_synthesis_tiles(height, width, lh, lw, tile_size, overlap, NULL, 0);
+    if (nt <= 0) return -1;
+    zo_tile *tiles = (zo_tile *)malloc(sizeof(zo_tile) * nt);
+    zo_synthesis_tiles(height, width, lh, lw, tile_size, overlap, tiles, nt);
+    int cw = cdiv(out_w, sh);
+    for (int i = 0; i < nt; i++) {
+        zo_tile t = tiles[i];
+        /* synthesize_luma_into (reconstruct.rs:379-411) */
+        T ly = window(y_hat_y, 160, lh, lw, t.lat_x, t.lat_y, t.lat_w, t.lat_h);
+        int oh, ow;
+        zo_synth_out_size(op, 0, t.img_h, t.img_w, &oh, &ow);
+        float *ty = (float *)malloc(sizeof(float) * oh * ow);
+        zo_synthesis_primary(ck_y, op, ly.d, ly.h, ly.w, t.img_h, t.img_w, ty);
+        if (oh < t.off_y + t.core_h || ow < t.off_x + t.core_w) return -1;
+        int cols = t.core_w < out_w - t.core_x ? t.core_w : out_w - t.core_x;
+        if (cols < 0) cols = 0;
+        for (int y = 0; y < t.core_h && t.core_y + y < out_h; y++)
+            memcpy(rec_y + (size_t)(t.core_y + y) * out_w + t.core_x,
+                   ty + (size_t)(t.off_y + y) * ow + t.off_x, sizeof(float) * cols);
+        free(ty);
+        /* synthesize_chroma_into (reconstruct.rs:416-464) */
+        T luv = window(y_hat_uv, 96, lh, lw, t.lat_x, t.lat_y, t.lat_w, t.lat_h);
+        zo_synth_out_size(op, 1, t.img_h, t.img_w, &oh, &ow);
+        float *tuv = (float *)malloc(sizeof(float) * 2 * oh * ow);
+        zo_synthesis_secondary(ck_uv, op, ly.d, ly.h, ly.w, luv.d, luv.h, luv.w, t.img_h,
+                               t.img_w, tuv);
+        if (oh < t.off_y + t.core_h || ow < t.off_x + t.core_w) return -1;
+        for (int c = 0; c < 2; c++) {
+            const float *src = tuv + (size_t)c * oh * ow;
+            float *dst = c == 0 ? rec_u : rec_v;
+            int y_end = t.core_y + t.core_h < out_h ? t.core_y + t.core_h : out_h;
+            int x_end = t.core_x + t.core_w < out_w ? t.core_x + t.core_w : out_w;
+            for (int py = cdiv(t.core_y, sv) * sv; py < y_end; py += sv)
+                for (int px = cdiv(t.core_x, sh) * sh; px < x_end; px += sh)
+                    dst[(size_t)(py / sv) * cw + px / sh] =
+                        src[(size_t)(t.off_y + py - t.core_y) * ow + t.off_x + px - t.core_x];
+        }
+        free(tuv);
+        t_free(&ly);
+        t_free(&luv);
+    }
+    free(tiles);
+    return 0;
+}
+
+/* ======================================================================================= */
+/* Output stage (output.rs:28-438)                                                            */
+/* ======================================================================================= */
+
+static float convert_range(float x, float in_max, float out_max) {
+    return ((x - 0.0f) / in_max) * out_max + 0.0f;
+}
+
+/* quantize_plane_par (output.rs:330-342): clip, scale, round half to even, clip */
+void zo_quantize_plane(const float *x, int64_t n, int bit_depth, uint16_t *out) {
+    float mx = (float)((1u << bit_depth) - 1);
+    for (int64_t i = 0; i < n; i++)
+        out[i] = (uint16_t)clampf(rintf(convert_range(clampf(x[i], 0.0f, 255.0f), 255.0f, mx)),
+                                  0.0f, mx);
+}
+
+static const float CUBIC_A = -0.75f;
+static float cubic1(float x) {
+    float p = fmaf(CUBIC_A + 2.0f, x, -(CUBIC_A + 3.0f));
+    return fmaf(p * x, x, 1.0f);
+}
+static float cubic2(float x) {
+    float p = fmaf(CUBIC_A, x, -5.0f * CUBIC_A);
+    p = fmaf(p, x, 8.0f * CUBIC_A);
+    return fmaf(p, x, -4.0f * CUBIC_A);
+}
+/* dot4 (output.rs:85-91): fma(x3,c3, fma(x2,c2, fma(x0,c0, x1*c1))) */
+static float dot4(const float x[4], const float c[4]) {
+    float acc = x[1] * c[1];
+    acc = fmaf(x[0], c[0], acc);
+    acc = fmaf(x[2], c[2], acc);
+    return fmaf(x[3], c[3], acc);
+}
+static void cubic_taps(int dst, int in_len, int out_len, int idx[4], float wt[4]) {
+    float scale = out_len > 1 ? (float)(in_len - 1) / (float)(out_len - 1) : 0.0f;
+    float real = scale * (float)dst;
+    float base = floorf(real);
+    float t = real - base;
+    int b = (int)base;
+    for (int k = 0; k < 4; k++) {
+        int v = b - 1 + k;
+        idx[k] = v < 0 ? 0 : v > in_len - 1 ? in_len - 1 : v;
+    }
+    float u = 1.0f - t;
+    wt[0] = cubic2(t + 1.0f);
+    wt[1] = cubic1(t);
+    wt[2] = cubic1(u);
+    wt[3] = cubic2(u + 1.0f);
+}
+
+/* resize_bicubic_par (output.rs:103-151), align_corners = True */
+int zo_resize_bicubic(const float *src, int c, int h, int w, int out_h, int out_w,
+                      float *out) {
+    if (h <= 0 || w <= 0) return -1;
+    int *xi = (int *)malloc(sizeof(int) * 4 * out_w);
+    float *xw = (float *)malloc(sizeof(float) * 4 * out_w);
+    int *yi = (int *)malloc(sizeof(int) * 4 * out_h);
+    float *yw = (float *)malloc(sizeof(float) * 4 * out_h);
+    for (int x = 0; x < out_w; x++) cubic_taps(x, w, out_w, xi + 4 * x, xw + 4 * x);
+    for (int y = 0; y < out_h; y++) cubic_taps(y, h, out_h, yi + 4 * y, yw + 4 * y);
+    for (int ci = 0; ci < c; ci++) {
+        const float *sp = src + (size_t)ci * h * w;
+        float *op = out + (size_t)ci * out_h * out_w;
+#pragma omp parallel for schedule(static) num_threads(g_threads)
+        for (int y = 0; y < out_h; y++) {
+            for (int x = 0; x < out_w; x++) {
+                float rows[4];
+                for (int k = 0; k < 4; k++) {
+                    const float *row = sp + (size_t)yi[4 * y + k] * w;
+                    float v[4] = {row[xi[4 * x]], row[xi[4 * x + 1]], row[xi[4 * x + 2]],
+                                  row[xi[4 * x + 3]]};
+                    rows[k] = dot4(v, xw + 4 * x);
+                }
+                op[(size_t)y * out_w + x] = dot4(rows, yw + 4 * y);
+            }
+        }
+    }
+    free(xi);
+    free(xw);
+    free(yi);
+    free(yw);
+    return 0;
+}
+
+/* to_rgb_planes_owned_par (output.rs:218-262) */
+void zo_to_rgb_planes(float *py, float *pu, float *pv, int64_t n) {
+    const double KR = 0.2126, KG = 0.7152, KB = 0.0722, KBY = 1.8556, KRY = 1.5748;
+    float kry = (float)KRY, kby = (float)KBY;
+    float gu = (float)(KB * KBY / KG), gv = (float)(KR * KRY / KG);
+    for (int64_t i = 0; i < n; i++) {
+        float y = convert_range(py[i], 255.0f, 1.0f);
+        float u = convert_range(pu[i], 255.0f, 1.0f) - 0.5f;
+        float v = convert_range(pv[i], 255.0f, 1.0f) - 0.5f;
+        float rv = y + kry * v;
+        float gvv = y - gu * u - gv * v;
+        float bv = y + kby * u;
+        py[i] = clampf(convert_range(rv, 1.0f, 255.0f), 0.0f, 255.0f);
+        pu[i] = clampf(convert_range(gvv, 1.0f, 255.0f), 0.0f, 255.0f);
+        pv[i] = clampf(convert_range(bv, 1.0f, 255.0f), 0.0f, 255.0f);
+    }
+}
+
+/* quantize_par (output.rs:407-438) */
+void zo_quantize_rgb(const float *r, const float *g, const float *b, int64_t n, int bit_depth,
+                     uint16_t *out) {
+    float mx = (float)((1u << bit_depth) - 1);
+    for (int64_t i = 0; i < n; i++) {
+        out[3 * i] = (uint16_t)clampf(rintf(convert_range(r[i], 255.0f, mx)), 0.0f, mx);
+        out[3 * i + 1] = (uint16_t)clampf(rintf(convert_range(g[i], 255.0f, mx)), 0.0f, mx);
+        out[3 * i + 2] = (uint16_t)clampf(rintf(convert_range(b[i], 255.0f, mx)), 0.0f, mx);
+    }
+}

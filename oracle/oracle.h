@@ -1,0 +1,156 @@
+/*
+ * CPU oracle for the JPEG AI synthesis / analysis path (TEST INFRASTRUCTURE ONLY).
+ *
+ * A plain-C restatement of the reference crate's f32 CPU path (imazen/zenjpegai, Rust):
+ * the numeric contract of `src/nn/mod.rs:1-45` (bias-initialised FMA accumulation in
+ * (ic, ky, kx) order over a zero-padded input), the plain loops of `src/nn/reference.rs`,
+ * the pointwise / reduction maths of `src/nn/fast/math.rs` (Cephes exp, f64 sums, `dot8`),
+ * the topologies of `src/model/{synthesis,attention,analysis}.rs`, the tiling of
+ * `src/tools/tiles.rs`, the tile assembly of `src/decoder/reconstruct.rs` and the output
+ * stage of `src/decoder/output.rs`.
+ *
+ * Only the test suite, `__graft_entry__.smoke()` and the `cpu_baseline` leg of `bench.py`
+ * may load this library, and only as the checker / the timed CPU baseline. The product
+ * (`zenjpegai_b200`) never links or calls it.
+ *
+ * Parity pin: the layer functions are checked against the reference's own golden vectors
+ * (the `.bin` files of `tests/vectors/nn/`, torch-computed, converted into `tests/golden/`), with the
+ * reference's tolerance (max |d| / max(|y|, 1) < 2e-6) and bit-exactness for the pure
+ * permutations and resamplers. Whole-network parity to upstream PyTorch is not pinnable here
+ * (no checkpoints, no reference dumps); the topology follows the cited Rust source.
+ */
+#ifndef ZJAI_ORACLE_H
+#define ZJAI_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- threading of the oracle's loops (OpenMP); 1 = serial ---------------------------- */
+void zo_set_threads(int n);
+int zo_get_threads(void);
+
+/* ---- layer functions (planar [c][h][w] f32 tensors, caller-owned buffers) -------------- */
+
+/* Output size of a convolution over an input of h x w with extra padding [t, l, b, r]. */
+void zo_conv2d_out_size(int h, int w, int kh, int kw, int stride, int pad_h, int pad_w,
+                        const int extra[4], int *oh, int *ow);
+
+/* `nn::reference::conv2d` (reference.rs:92-133) with `ConvLayer::with_extra_pad`'s zero
+ * border (layers.rs:100-115). weight [oc][c/groups][kh][kw], bias may be NULL. */
+int zo_conv2d(const float *x, int c, int h, int w, const float *weight, const float *bias,
+              int oc, int kh, int kw, int stride, int pad_h, int pad_w, int groups,
+              const int extra[4], float *out);
+
+/* `nn::reference::conv_transpose2d` (reference.rs:155-236). weight [c][oc][k][k]. */
+void zo_conv_transpose2d_out_size(int h, int w, int k, int stride, int pad, int out_pad,
+                                  int *oh, int *ow);
+int zo_conv_transpose2d(const float *x, int c, int h, int w, const float *weight,
+                        const float *bias, int oc, int k, int stride, int pad, int out_pad,
+                        float *out);
+
+/* `pixel_shuffle` (reference.rs:353-375): [c*r*r, h, w] -> [c, h*r, w*r]. */
+int zo_pixel_shuffle(const float *x, int c, int h, int w, int r, float *out);
+
+/* Elementwise ops (layers.rs:174-229, math.rs:371-397). In place on n values. */
+void zo_relu(float *x, int64_t n);
+void zo_relu6(float *x, int64_t n);
+void zo_add(float *dst, const float *src, int64_t n);
+void zo_gate(float *x, const float *mask, int64_t n);
+void zo_mul(float *a, const float *b, int64_t n);
+void zo_sigmoid(float *x, int64_t n);
+void zo_elu_gate(float *a, const float *b, int64_t n);
+float zo_exp(float x);
+void zo_denormalize(float *x, int64_t n);
+
+/* `math::layer_norm_channels` (math.rs:423-448), in place on [c][h][w]. */
+int zo_layer_norm_channels(float *x, int c, int h, int w, const float *weight,
+                           const float *bias);
+
+/* `math::channel_attention` (math.rs:512-603): qkv [3*dim][h][w] -> out [dim][h][w]. */
+int zo_channel_attention(const float *qkv, int c3, int h, int w, int heads,
+                         const float *temperature, float *out);
+
+/* `dot8` (math.rs:452-465). */
+double zo_dot8(const float *a, const float *b, int64_t n);
+
+/* ---- named parameters (a checkpoint stand-in) ------------------------------------------ */
+typedef struct {
+    const char *name;
+    int ndim;
+    int shape[4];
+    const float *data;
+} zo_param;
+
+typedef struct {
+    const zo_param *params;
+    int n;
+} zo_ckpt;
+
+enum { ZO_SOP = 0, ZO_BOP = 1, ZO_HOP = 2 };
+
+/* Per-layer dump hook: called with each named intermediate map (planar). NULL = off. */
+typedef void (*zo_dump_fn)(const char *name, const float *data, int c, int h, int w);
+void zo_set_dump(zo_dump_fn fn);
+
+/* Output size of a synthesis network for a tile of h x w picture samples. */
+void zo_synth_out_size(int op, int secondary, int h, int w, int *oh, int *ow);
+
+/* `SynthesisPrimary::forward` (synthesis.rs:262-274 -> LightPrimary / HopPrimary):
+ * y_hat [160][lh][lw] -> out [1][oh][ow] in [0, 255] (oh, ow from zo_synth_out_size). */
+int zo_synthesis_primary(const zo_ckpt *ck, int op, const float *y_hat, int lh, int lw,
+                         int h, int w, float *out);
+
+/* `SynthesisSecondary::forward_with` (synthesis.rs:1004-1038): luma latent [160][llh][llw]
+ * and chroma latent [96][lh][lw] -> out [2][oh][ow] in [0, 255]. */
+int zo_synthesis_secondary(const zo_ckpt *ck, int op, const float *y_hat_luma, int llh,
+                           int llw, const float *y_hat_chroma, int lh, int lw, int h, int w,
+                           float *out);
+
+/* `AnalysisPrimary::forward` (analysis.rs:242-269): [1][h][w] in [0,255] ->
+ * [160][ceil(h/16)][ceil(w/16)]. */
+int zo_analysis_primary(const zo_ckpt *ck, int op, const float *x, int h, int w, float *out);
+
+/* `AnalysisSecondary::forward` (analysis.rs:292-311): [12][h][w] -> [96][ceil(h/8)][ceil(w/8)]. */
+int zo_analysis_secondary(const zo_ckpt *ck, int op, const float *x, int h, int w, float *out);
+
+/* ---- tiling (tiles.rs:39-119, without independent regions) ------------------------------ */
+typedef struct {
+    int img_x, img_y, img_w, img_h;
+    int lat_x, lat_y, lat_w, lat_h;
+    int core_x, core_y, core_w, core_h;
+    int off_x, off_y;
+} zo_tile;
+
+/* tile_size <= 0: one tile covering the picture. Returns the tile count, or -1 on malformed
+ * geometry. Writes at most max_tiles entries. */
+int zo_synthesis_tiles(int height, int width, int latent_h, int latent_w, int tile_size,
+                       int overlap, zo_tile *tiles, int max_tiles);
+
+/* `synthesize_with` (reconstruct.rs:274-331, 379-464): whole-picture synthesis into
+ * rec_y [out_h][out_w], rec_u / rec_v [ceil(out_h/sv)][ceil(out_w/sh)]. */
+int zo_synthesize(const zo_ckpt *ck_y, const zo_ckpt *ck_uv, int op, const float *y_hat_y,
+                  const float *y_hat_uv, int lh, int lw, int height, int width, int out_h,
+                  int out_w, int tile_size, int overlap, int sv, int sh, float *rec_y,
+                  float *rec_u, float *rec_v);
+
+/* ---- output stage (output.rs) ---------------------------------------------------------- */
+void zo_quantize_plane(const float *x, int64_t n, int bit_depth, uint16_t *out);
+int zo_resize_bicubic(const float *src, int c, int h, int w, int out_h, int out_w,
+                      float *out);
+/* BT.709 YCbCr -> RGB in place (y->r, u->g, v->b), output.rs:218-262 */
+void zo_to_rgb_planes(float *y, float *u, float *v, int64_t n);
+/* interleaved RGB quantisation, output.rs:407-438 */
+void zo_quantize_rgb(const float *r, const float *g, const float *b, int64_t n, int bit_depth,
+                     uint16_t *out);
+
+/* ---- encoder pre-processing (colour.rs) and analysis helpers ---------------------------- */
+void zo_normalize(const float *x, int64_t n, float *out);
+int zo_pad_amount(int len, int divider);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,213 @@
+"""zenjpegai_b200 — B200 (sm_100a) engine for the JPEG AI synthesis / analysis networks.
+
+Python host side over the C ABI of `include/zjai.h` (library `libzjai.so`, built by
+`zenjpegai_b200/build.py`). It mirrors the reference crate's interfaces for this path:
+
+* `Engine` — the crate's `Engine` (src/nn/fast/mod.rs:127-169): here a CUDA context on one
+  GPU (stream, device arena, kernel status word).
+* `nn` layer calls — `ConvLayer` / `ConvTransposeLayer` / `math::*` (src/nn/fast/layers.rs,
+  math.rs) on planar `[c, h, w]` f32 tensors.
+* `SynthesisPrimary`, `SynthesisSecondary`, `AnalysisPrimary`, `AnalysisSecondary` — the
+  network types of src/model/{synthesis,analysis}.rs: `load(params, op, engine)` +
+  `forward(...)`.
+* `synthesize` / `synthesis_tiles` — src/decoder/reconstruct.rs:274-464 and
+  src/tools/tiles.rs:39-119.
+
+Arrays are numpy float32 (host memory) or torch CUDA float32 tensors (device memory of the
+engine's GPU). Errors raise `ZjaiError` whose `.status` mirrors the crate's `Error` variant.
+There is no CPU fallback: without the CUDA library this package does not import.
+"""
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import (ACT_LEAKY, ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SIGMOID, ANA_UV, ANA_Y, BOP,
+                   HOP, SOP, SYN_UV, SYN_Y, ZjaiError, check)
+
+__all__ = ["Engine", "ZjaiError", "SOP", "BOP", "HOP", "SYN_Y", "SYN_UV", "ANA_Y", "ANA_UV",
+           "ACT_NONE", "ACT_RELU", "ACT_LEAKY", "ACT_SIGMOID", "ACT_RELU6", "Network",
+           "synthesis_tiles", "synth_out_size", "version"]
+
+_lib.lib()  # load now: importing the package without its CUDA library is an error
+
+
+def version():
+    return _lib.lib().zjai_version().decode()
+
+
+def _is_torch(a):
+    return type(a).__module__.startswith("torch")
+
+
+def _arg(a, want_shape=None, writable=False):
+    """(pointer, mem) of a numpy host array or a torch CUDA tensor (float32, contiguous)."""
+    if _is_torch(a):
+        import torch
+        if a.dtype != torch.float32 or not a.is_contiguous():
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "tensor must be contiguous float32")
+        if want_shape is not None and tuple(a.shape) != tuple(want_shape):
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "shape %s, expected %s"
+                            % (tuple(a.shape), tuple(want_shape)))
+        if not a.is_cuda:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "torch tensors must be CUDA tensors")
+        return ctypes.c_void_p(a.data_ptr()), _lib.MEM_DEVICE
+    if not isinstance(a, np.ndarray) or a.dtype != np.float32 or not a.flags.c_contiguous:
+        raise ZjaiError(_lib.INVALID_ARGUMENT, "array must be a contiguous float32 ndarray")
+    if want_shape is not None and tuple(a.shape) != tuple(want_shape):
+        raise ZjaiError(_lib.INVALID_ARGUMENT, "shape %s, expected %s"
+                        % (a.shape, tuple(want_shape)))
+    return ctypes.c_void_p(a.ctypes.data), _lib.MEM_HOST
+
+
+def _like(x, shape):
+    if _is_torch(x):
+        import torch
+        return torch.empty(shape, dtype=torch.float32, device=x.device)
+    return np.empty(shape, np.float32)
+
+
+class Engine:
+    """A CUDA context on one GPU (the crate's `Engine`, GPU kind)."""
+
+    def __init__(self, device=0, arena_bytes=0):
+        h = ctypes.c_void_p()
+        check(_lib.lib().zjai_ctx_create(int(device), int(arena_bytes), ctypes.byref(h)))
+        self.handle = h
+        self.device = device
+
+    def close(self):
+        if self.handle:
+            _lib.lib().zjai_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, cuda_stream_ptr):
+        check(_lib.lib().zjai_ctx_set_stream(self.handle, ctypes.c_void_p(cuda_stream_ptr)))
+
+    def sync(self):
+        check(_lib.lib().zjai_ctx_sync(self.handle))
+
+    @property
+    def launch_count(self):
+        return int(_lib.lib().zjai_ctx_launch_count(self.handle))
+
+    # ---- nn layer interface (src/nn/fast/layers.rs, math.rs) ------------------------------
+    def conv2d(self, x, weight, bias=None, stride=1, pad=(0, 0), groups=1, extra=None,
+               act=ACT_NONE, out=None):
+        c, h, w = x.shape
+        oc, _, kh, kw = weight.shape
+        ex = extra or (0, 0, 0, 0)
+        oh = (h + ex[0] + ex[2] + 2 * pad[0] - kh) // stride + 1
+        ow = (w + ex[1] + ex[3] + 2 * pad[1] - kw) // stride + 1
+        if out is None:
+            out = _like(x, (oc, oh, ow))
+        px, mem = _arg(x)
+        pw, m2 = _arg(weight)
+        pb = _arg(bias)[0] if bias is not None else None
+        po, m3 = _arg(out, (oc, oh, ow))
+        if len({mem, m2, m3}) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        exa = (ctypes.c_int * 4)(*ex)
+        check(_lib.lib().zjai_conv2d(self.handle, px, c, h, w, pw, pb, oc, kh, kw, stride,
+                                     pad[0], pad[1], groups, exa, act, po, mem))
+        return out
+
+    def conv_transpose2d(self, x, weight, bias=None, pad=1, out_pad=0, out=None):
+        c, h, w = x.shape
+        _, oc, k, _ = weight.shape
+        oh = (h - 1) * 2 + k + out_pad - 2 * pad
+        ow = (w - 1) * 2 + k + out_pad - 2 * pad
+        if out is None:
+            out = _like(x, (oc, oh, ow))
+        px, mem = _arg(x)
+        pw, _ = _arg(weight)
+        pb = _arg(bias)[0] if bias is not None else None
+        po, _ = _arg(out, (oc, oh, ow))
+        check(_lib.lib().zjai_conv_transpose2d(self.handle, px, c, h, w, pw, pb, oc, k, pad,
+                                               out_pad, po, mem))
+        return out
+
+    def layer_norm(self, x, weight, bias, out=None):
+        c, h, w = x.shape
+        out = _like(x, x.shape) if out is None else out
+        px, mem = _arg(x)
+        check(_lib.lib().zjai_layer_norm(self.handle, px, c, h, w, _arg(weight)[0],
+                                         _arg(bias)[0], _arg(out, x.shape)[0], mem))
+        return out
+
+    def channel_attention(self, qkv, heads, temperature, out=None):
+        c3, h, w = qkv.shape
+        out = _like(qkv, (c3 // 3, h, w)) if out is None else out
+        px, mem = _arg(qkv)
+        check(_lib.lib().zjai_channel_attention(self.handle, px, c3, h, w, heads,
+                                                _arg(temperature)[0],
+                                                _arg(out, (c3 // 3, h, w))[0], mem))
+        return out
+
+    def depthwise3x3(self, x, weight, out=None):
+        c, h, w = x.shape
+        out = _like(x, x.shape) if out is None else out
+        px, mem = _arg(x)
+        check(_lib.lib().zjai_depthwise3x3(self.handle, px, c, h, w, _arg(weight)[0],
+                                           _arg(out, x.shape)[0], mem))
+        return out
+
+
+def synth_out_size(kind, op, h, w):
+    oh, ow = ctypes.c_int(), ctypes.c_int()
+    check(_lib.lib().zjai_synth_out_size(kind, op, h, w, ctypes.byref(oh), ctypes.byref(ow)))
+    return oh.value, ow.value
+
+
+def synthesis_tiles(height, width, latent_h, latent_w, tile_size=0, overlap=0):
+    """`synthesis_tiles` (src/tools/tiles.rs:39-119): list of tile dicts."""
+    n = ctypes.c_int()
+    check(_lib.lib().zjai_synthesis_tiles(height, width, latent_h, latent_w, tile_size,
+                                          overlap, None, 0, ctypes.byref(n)))
+    arr = (_lib.Tile * n.value)()
+    check(_lib.lib().zjai_synthesis_tiles(height, width, latent_h, latent_w, tile_size,
+                                          overlap, arr, n.value, ctypes.byref(n)))
+    return [{k: getattr(t, k) for k, _ in _lib.Tile._fields_} for t in arr]
+
+
+class Network:
+    """A synthesis / analysis network with GPU-resident packed weights
+    (`SynthesisPrimary::load` etc.). `params` maps checkpoint names to float32 arrays."""
+
+    def __init__(self, engine, kind, op, params):
+        self.engine = engine
+        self.kind = kind
+        self.op = op
+        arrs = {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in params.items()}
+        ps = (_lib.Param * len(arrs))()
+        keep = []
+        for i, (k, v) in enumerate(arrs.items()):
+            nm = k.encode()
+            keep.append(nm)
+            ps[i].name = nm
+            ps[i].ndim = v.ndim
+            for d in range(4):
+                ps[i].shape[d] = v.shape[d] if d < v.ndim else 0
+            ps[i].data = v.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        h = ctypes.c_void_p()
+        check(_lib.lib().zjai_net_create(engine.handle, kind, op, ps, len(arrs),
+                                         ctypes.byref(h)))
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            _lib.lib().zjai_net_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,100 @@
+"""ctypes binding of `libzjai.so` (the C ABI of include/zjai.h).
+
+This is the Python host side above the C ABI. It fails loudly: if the CUDA library is not
+built or cannot be loaded, importing the binding raises; there is no CPU fallback.
+"""
+
+import ctypes
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libzjai.so")
+HEADER = os.path.join(HERE, "..", "include", "zjai.h")
+
+OK, INVALID_ARGUMENT, UNSUPPORTED, LIMIT_EXCEEDED, CANCELLED, MODEL, INVALID_DATA, DEVICE, \
+    DEVICE_TIMEOUT = range(9)
+STATUS_NAMES = ["OK", "INVALID_ARGUMENT", "UNSUPPORTED", "LIMIT_EXCEEDED", "CANCELLED", "MODEL",
+                "INVALID_DATA", "DEVICE", "DEVICE_TIMEOUT"]
+MEM_HOST, MEM_DEVICE = 0, 1
+SOP, BOP, HOP = 0, 1, 2
+SYN_Y, SYN_UV, ANA_Y, ANA_UV = 0, 1, 2, 3
+ACT_NONE, ACT_RELU, ACT_LEAKY, ACT_SIGMOID, ACT_RELU6 = range(5)
+
+
+class ZjaiError(RuntimeError):
+    """A failing zjai call: `.status` is the zjai_status code, mirroring the crate's Error."""
+
+    def __init__(self, status, msg):
+        name = STATUS_NAMES[status] if 0 <= status < len(STATUS_NAMES) else str(status)
+        super().__init__("%s: %s" % (name, msg))
+        self.status = status
+
+
+_f = ctypes.POINTER(ctypes.c_float)
+_i = ctypes.c_int
+_vp = ctypes.c_void_p
+
+
+class Param(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("ndim", _i), ("shape", ctypes.c_int64 * 4),
+                ("data", _f)]
+
+
+class Tile(ctypes.Structure):
+    _fields_ = [(k, _i) for k in (
+        "img_x", "img_y", "img_w", "img_h", "lat_x", "lat_y", "lat_w", "lat_h",
+        "core_x", "core_y", "core_w", "core_h", "off_x", "off_y")]
+
+
+_lib = None
+
+
+def header_functions():
+    """Names of every function declared in include/zjai.h."""
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(zjai_[a-z0-9_]+)\s*\(", src)))
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError("zenjpegai_b200: %s is not built (run zenjpegai_b200/build.py)"
+                          % LIB_PATH)
+    L = ctypes.CDLL(LIB_PATH)
+    L.zjai_version.restype = ctypes.c_char_p
+    L.zjai_last_error_message.restype = ctypes.c_char_p
+    L.zjai_ctx_create.argtypes = [_i, ctypes.c_size_t, ctypes.POINTER(_vp)]
+    L.zjai_ctx_destroy.argtypes = [_vp]
+    L.zjai_ctx_set_stream.argtypes = [_vp, _vp]
+    L.zjai_ctx_sync.argtypes = [_vp]
+    L.zjai_ctx_launch_count.argtypes = [_vp]
+    L.zjai_ctx_launch_count.restype = ctypes.c_int64
+    L.zjai_net_create.argtypes = [_vp, _i, _i, ctypes.POINTER(Param), _i, ctypes.POINTER(_vp)]
+    L.zjai_net_destroy.argtypes = [_vp]
+    L.zjai_synth_out_size.argtypes = [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]
+    L.zjai_synthesis_primary.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _i]
+    L.zjai_synthesis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _vp, _i]
+    L.zjai_analysis_primary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
+    L.zjai_analysis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
+    L.zjai_synthesis_tiles.argtypes = [_i] * 6 + [ctypes.POINTER(Tile), _i, ctypes.POINTER(_i)]
+    L.zjai_synthesize.argtypes = [_vp, _vp, _vp, _vp, _vp] + [_i] * 11 + [_vp, _vp, _vp, _i, _vp]
+    L.zjai_quantize_plane.argtypes = [_vp, _vp, ctypes.c_int64, _i, _vp, _i]
+    L.zjai_yuv_to_rgb.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i]
+    L.zjai_conv2d.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i,
+                              ctypes.POINTER(_i), _i, _vp, _i]
+    L.zjai_conv_transpose2d.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _i, _i, _vp, _i]
+    L.zjai_layer_norm.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]
+    L.zjai_channel_attention.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i]
+    L.zjai_depthwise3x3.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i]
+    _lib = L
+    return L
+
+
+def check(status):
+    if status != OK:
+        msg = lib().zjai_last_error_message().decode(errors="replace")
+        raise ZjaiError(status, msg)

@@ -1,0 +1,213 @@
+// The C ABI (include/zjai.h): contexts and the nn layer entry points. Network, synthesis and
+// output-stage entries live in net.cu / output.cu.
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "api_common.h"
+
+using namespace zjai;
+
+namespace zjai {
+
+int ctx_enter(zjai_ctx* ctx) {
+  if (!ctx) return fail(ZJAI_INVALID_ARGUMENT, "null context");
+  return cuda_check(cudaSetDevice(ctx->device), "cudaSetDevice");
+}
+
+int ctx_check_status(Ctx* ctx) {
+  int err = 0;
+  ZJAI_TRY(cuda_check(cudaMemcpyAsync(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost,
+                                      ctx->stream),
+                      "status word read"));
+  ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "stream sync"));
+  if (err != 0) {
+    cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream);
+    cudaStreamSynchronize(ctx->stream);
+    return fail(ZJAI_DEVICE_TIMEOUT,
+                "a kernel's bounded wait gave up (device status " + std::to_string(err) + ")");
+  }
+  return ZJAI_OK;
+}
+
+// Device copy of a caller tensor (host or device) as f32; returns a device pointer.
+int stage_in(Ctx* ctx, const float* p, size_t n, int mem, const float** out) {
+  if (mem == ZJAI_MEM_DEVICE) {
+    *out = p;
+    return ZJAI_OK;
+  }
+  if (mem != ZJAI_MEM_HOST) return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  float* d = static_cast<float*>(ctx->arena.alloc(n * sizeof(float)));
+  if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (input staging)");
+  ZJAI_TRY(cuda_check(
+      cudaMemcpyAsync(d, p, n * sizeof(float), cudaMemcpyHostToDevice, ctx->stream), "H2D"));
+  *out = d;
+  return ZJAI_OK;
+}
+
+int stage_out_alloc(Ctx* ctx, float* p, size_t n, int mem, float** dev) {
+  if (mem == ZJAI_MEM_DEVICE) {
+    *dev = p;
+    return ZJAI_OK;
+  }
+  if (mem != ZJAI_MEM_HOST) return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  *dev = static_cast<float*>(ctx->arena.alloc(n * sizeof(float)));
+  if (!*dev) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (output staging)");
+  return ZJAI_OK;
+}
+
+int stage_out_finish(Ctx* ctx, float* host, const float* dev, size_t n, int mem) {
+  if (mem == ZJAI_MEM_DEVICE) return ZJAI_OK;
+  return cuda_check(
+      cudaMemcpyAsync(host, dev, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream), "D2H");
+}
+
+// Planar f32 [c][h][w] (device) -> fresh zeroed NHWC f16 tensor.
+int planar_to_tensor(Ctx* ctx, const float* d, int c, int h, int w, TView* out) {
+  ZJAI_TRY(alloc_tensor(ctx, 1, h, w, c, out, true));
+  launch_planar_to_nhwc(d, c, h, w, 0, 0, *out, ctx->stream);
+  ctx->launches++;
+  return cuda_check(cudaGetLastError(), "planar_to_nhwc");
+}
+
+}  // namespace zjai
+
+extern "C" {
+
+const char* zjai_version(void) { return "zjai 0.1.0 (sm_100a tcgen05)"; }
+
+const char* zjai_last_error_message(void) { return zjai::last_error_cstr(); }
+
+int zjai_ctx_create(int device, size_t arena_bytes, zjai_ctx** out) {
+  if (!out) return fail(ZJAI_INVALID_ARGUMENT, "null output handle");
+  *out = nullptr;
+  int ndev = 0;
+  ZJAI_TRY(cuda_check(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount"));
+  if (device < 0 || device >= ndev) return fail(ZJAI_INVALID_ARGUMENT, "no such CUDA device");
+  ZJAI_TRY(cuda_check(cudaSetDevice(device), "cudaSetDevice"));
+  cudaDeviceProp prop;
+  ZJAI_TRY(cuda_check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties"));
+  if (prop.major != 10)
+    return fail(ZJAI_UNSUPPORTED, std::string("zjai needs an sm_100 GPU, found ") + prop.name);
+  zjai_ctx* c = new zjai_ctx();
+  c->device = device;
+  c->sms = prop.multiProcessorCount;
+  if (arena_bytes == 0) arena_bytes = size_t(4) << 30;
+  int st = ZJAI_OK;
+  if ((st = cuda_check(cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking), "stream")) ||
+      (st = cuda_check(cudaStreamCreateWithFlags(&c->stream2, cudaStreamNonBlocking), "stream")) ||
+      (st = cuda_check(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming), "event")) ||
+      (st = cuda_check(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming), "event")) ||
+      (st = cuda_check(cudaMalloc(&c->arena.base, arena_bytes), "arena cudaMalloc")) ||
+      (st = cuda_check(cudaMalloc(&c->d_err, sizeof(int)), "status cudaMalloc")) ||
+      (st = cuda_check(cudaMemset(c->d_err, 0, sizeof(int)), "status memset")) ||
+      (st = cuda_check(cudaDriverGetVersion(&c->driver_version), "driver version"))) {
+    zjai_ctx_destroy(c);
+    return st;
+  }
+  c->arena.cap = arena_bytes;
+  c->stream = c->own;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &c->encode_fn, cudaEnableDefault, &q) !=
+          cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !c->encode_fn) {
+    zjai_ctx_destroy(c);
+    return fail(ZJAI_DEVICE, "cuTensorMapEncodeTiled entry point not available");
+  }
+  *out = c;
+  return ZJAI_OK;
+}
+
+int zjai_ctx_destroy(zjai_ctx* ctx) {
+  if (!ctx) return ZJAI_OK;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->arena.base) cudaFree(ctx->arena.base);
+  if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+  if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
+  if (ctx->stream2) cudaStreamDestroy(ctx->stream2);
+  if (ctx->own) cudaStreamDestroy(ctx->own);
+  delete ctx;
+  return ZJAI_OK;
+}
+
+int zjai_ctx_set_stream(zjai_ctx* ctx, void* s) {
+  ZJAI_TRY(ctx_enter(ctx));
+  ctx->stream = s ? static_cast<cudaStream_t>(s) : ctx->own;
+  return ZJAI_OK;
+}
+
+int zjai_ctx_sync(zjai_ctx* ctx) {
+  ZJAI_TRY(ctx_enter(ctx));
+  return ctx_check_status(ctx);
+}
+
+int64_t zjai_ctx_launch_count(const zjai_ctx* ctx) { return ctx ? (int64_t)ctx->launches : 0; }
+
+int zjai_conv2d(zjai_ctx* ctx, const float* x, int c, int h, int w, const float* weight,
+                const float* bias, int oc, int kh, int kw, int stride, int pad_h, int pad_w,
+                int groups, const int* extra, int act, float* out, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!x || !weight || !out || c <= 0 || h <= 0 || w <= 0 || oc <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "conv2d: bad arguments");
+  if (act < ZJAI_ACT_NONE || act > ZJAI_ACT_RELU6)
+    return fail(ZJAI_INVALID_ARGUMENT, "conv2d: unknown activation");
+  if (groups == c && groups > 1 && oc == c && kh == 3 && kw == 3 && stride == 1 && pad_h == 1 &&
+      pad_w == 1 && !bias && act == ZJAI_ACT_NONE && !(extra && (extra[0] | extra[1] | extra[2] | extra[3])))
+    return zjai_depthwise3x3(ctx, x, c, h, w, weight, out, mem);
+  ArenaScope scope(ctx);
+  ConvLayer L;
+  ZJAI_TRY(pack_conv(ctx, &L, weight, bias, c, oc, kh, kw, stride, pad_h, pad_w, groups, extra, 1));
+  LayerGuard guard(&L);
+  int oh, ow, out_h, out_w;
+  L.out_size(h, w, &oh, &ow, &out_h, &out_w);
+  if (oh <= 0 || ow <= 0) return fail(ZJAI_INVALID_ARGUMENT, "conv2d: input smaller than the kernel");
+  const float* dx;
+  ZJAI_TRY(stage_in(ctx, x, (size_t)c * h * w, mem, &dx));
+  TView tin;
+  ZJAI_TRY(planar_to_tensor(ctx, dx, c, h, w, &tin));
+  float* dout;
+  const size_t nout = (size_t)oc * out_h * out_w;
+  ZJAI_TRY(stage_out_alloc(ctx, out, nout, mem, &dout));
+  ConvOut o;
+  o.act1 = act;
+  o.planar = true;
+  o.pout = dout;
+  o.p_plane = (long long)out_h * out_w;
+  o.p_row = out_w;
+  ZJAI_TRY(run_conv(ctx, L, tin, o));
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, nout, mem));
+  return ctx_check_status(ctx);
+}
+
+int zjai_conv_transpose2d(zjai_ctx* ctx, const float* x, int c, int h, int w,
+                          const float* weight, const float* bias, int oc, int k, int pad,
+                          int out_pad, float* out, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!x || !weight || !out || c <= 0 || h <= 0 || w <= 0 || oc <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "conv_transpose2d: bad arguments");
+  ArenaScope scope(ctx);
+  ConvLayer L;
+  ZJAI_TRY(pack_convT(ctx, &L, weight, bias, c, oc, k, pad, out_pad, 1));
+  LayerGuard guard(&L);
+  int oh, ow, out_h, out_w;
+  L.out_size(h, w, &oh, &ow, &out_h, &out_w);
+  const float* dx;
+  ZJAI_TRY(stage_in(ctx, x, (size_t)c * h * w, mem, &dx));
+  TView tin;
+  ZJAI_TRY(planar_to_tensor(ctx, dx, c, h, w, &tin));
+  float* dout;
+  const size_t nout = (size_t)oc * out_h * out_w;
+  ZJAI_TRY(stage_out_alloc(ctx, out, nout, mem, &dout));
+  ConvOut o;
+  o.planar = true;
+  o.pout = dout;
+  o.p_plane = (long long)out_h * out_w;
+  o.p_row = out_w;
+  ZJAI_TRY(run_conv(ctx, L, tin, o));
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, nout, mem));
+  return ctx_check_status(ctx);
+}
+
+}  // extern "C"

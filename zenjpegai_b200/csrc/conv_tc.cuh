@@ -1,0 +1,78 @@
+// Implicit-GEMM convolution on sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// GEMM view: M = output pixels (a tile of bh x bw = 128 pixels of one picture), N = packed
+// output columns, K = taps x input channels. Activations are NHWC f16; per K step one TMA
+// box [kc channels, bw, bh] of the input is loaded at the tap's offset (out-of-range
+// coordinates read zeros, which is the convolution's zero padding; a crop is a smaller
+// tensor-map extent over the same memory). Weights are packed [tap][N][Cin] f16 and loaded
+// as [kc, bn] boxes. One elected thread issues kind::f16 UMMAs into an f32 accumulator in
+// TMEM (two accumulators, so the epilogue of one tile overlaps the main loop of the next).
+//
+// Epilogue: TMEM -> registers -> scale/bias/activation -> shared staging -> a second pass in
+// output order applies the pixel-shuffle remap (column n = phase * cph + channel, phase =
+// dy * R + dx) and the residual ops (add, ResAU gate, CAB sigmoid-mul-add), then stores NHWC
+// f16 (optionally also relu6 of it) or planar f32 (final layers: denormalize, crop to the
+// tile core, chroma subsampling).
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace zjai {
+
+enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_LEAKY = 2, ACT_SIGMOID = 3, ACT_RELU6 = 4 };
+enum EpiOp : int { OP_NONE = 0, OP_ADD = 1, OP_GATE = 2, OP_CAB = 3 };
+
+struct ConvArgs {
+  // tile grid
+  int tiles_x, tiles_y, n_img, n_tiles, num_tiles;
+  int bw, bh;          // pixel tile, bh * bw == 128
+  // K loop
+  int kw, taps, pad_t, pad_l;
+  int s2;              // 1: stride-2 conv through the 5-D (parity-split) input view
+  int cchunks, kc;     // channel chunks per tap; chunk width (16, 32 or 64)
+  int bn;              // N tile (multiple of 16, <= 256)
+  int stages;
+  int tmem_cols;
+  int oh, ow;          // conv output extent (pixels of the GEMM M space)
+  // epilogue
+  const float* bias;   // [n_tiles * bn] in packed column order, or null
+  float scale;         // weight unscale (power of two)
+  int act1, op, act2;
+  int R, cph;          // pixel-shuffle factor and channels per phase
+  // NHWC f16 output
+  __half* out;
+  long long out_pix, out_row, out_img;
+  int out_h, out_w;    // output extent after the shuffle (crop)
+  const __half* r1;
+  long long r1_pix, r1_row, r1_img;
+  const __half* r2;
+  long long r2_pix, r2_row, r2_img;
+  __half* out2;        // optional relu6(out)
+  long long o2_pix, o2_row, o2_img;
+  // planar f32 output
+  int planar, denorm;
+  float* pout;
+  long long p_plane, p_row, p_img;
+  int py0, px0;        // picture coordinates of output pixel (0, 0)
+  int cy0, cy1, cx0, cx1;
+  int sv, sh;
+  int* err;
+};
+
+constexpr int kConvThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
+constexpr int kStagingBytes = 128 * 32 * 4;
+
+__host__ __device__ inline uint32_t conv_stage_bytes(int kc, int bn) {
+  uint32_t b = 128u * kc * 2u + (uint32_t)bn * kc * 2u;
+  return (b + 1023u) & ~1023u;
+}
+__host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int stages) {
+  // 1 KB alignment slack + stages + staging + barriers/slots
+  return 1024u + stages * conv_stage_bytes(kc, bn) + kStagingBytes + 256u;
+}
+
+void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmB, const ConvArgs& a, int grid,
+                 cudaStream_t stream);
+
+}  // namespace zjai

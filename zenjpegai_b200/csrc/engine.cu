@@ -1,0 +1,441 @@
+// Host engine: errors, context, arena, TMA descriptors, weight packing, conv launch.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "engine.h"
+
+namespace zjai {
+
+// ---- errors -------------------------------------------------------------------------------
+static thread_local std::string g_last_error;
+
+void set_last_error(int code, const std::string& msg) {
+  (void)code;
+  g_last_error = msg;
+}
+
+const char* last_error_cstr() { return g_last_error.c_str(); }
+
+int fail(int code, const std::string& msg) {
+  set_last_error(code, msg);
+  return code;
+}
+
+int cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return ZJAI_OK;
+  return fail(ZJAI_DEVICE, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// ---- arena --------------------------------------------------------------------------------
+void* Arena::alloc(size_t bytes) {
+  size_t start = (top + 255) & ~size_t(255);
+  if (start + bytes > cap) return nullptr;
+  top = start + bytes;
+  peak = std::max(peak, top);
+  return base + start;
+}
+
+int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero) {
+  int cp = (c + 7) & ~7;
+  int ah = (h + 1) & ~1, aw = (w + 1) & ~1;
+  size_t bytes = (size_t)n * ah * aw * cp * sizeof(__half);
+  void* p = ctx->arena.alloc(bytes);
+  if (!p)
+    return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (" + std::to_string(bytes) +
+                                         " more bytes, capacity " +
+                                         std::to_string(ctx->arena.cap) + ")");
+  TView v;
+  v.p = static_cast<__half*>(p);
+  v.n = n;
+  v.h = h;
+  v.w = w;
+  v.c = c;
+  v.pix = cp;
+  v.row = (long long)aw * cp;
+  v.img = (long long)ah * aw * cp;
+  v.alloc_h = ah;
+  v.alloc_w = aw;
+  if (zero) ZJAI_TRY(cuda_check(cudaMemsetAsync(p, 0, bytes, ctx->stream), "memset"));
+  *out = v;
+  return ZJAI_OK;
+}
+
+// ---- TMA descriptors ------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static CUtensorMapSwizzle swizzle_for(int kc) {
+  return kc == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                  : kc == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+}
+
+static int encode(Ctx* ctx, CUtensorMap* m, int rank, void* addr, const cuuint64_t* dims,
+                  const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw,
+                  size_t span_bytes) {
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  if ((reinterpret_cast<uintptr_t>(addr) & 15) != 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "TMA base address not 16-byte aligned");
+  for (int i = 0; i < rank - 1; ++i)
+    if (strides[i] % 16 != 0)
+      return fail(ZJAI_INVALID_ARGUMENT, "TMA stride not a multiple of 16 bytes");
+  auto fn = reinterpret_cast<EncodeTiledFn>(ctx->encode_fn);
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, addr, dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[256];
+    snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d), rank %d", (int)r, rank);
+    return fail(ZJAI_DEVICE, buf);
+  }
+  // Same workaround CUTLASS applies to tiled descriptors of tensors under 128 KiB on drivers
+  // up to 13.1 (cute/atom/copy_traits_sm90_tma.hpp).
+  if (ctx->driver_version <= 13010 && span_bytes < 131072)
+    reinterpret_cast<uint64_t*>(m)[1] &= ~(1ull << 21);
+  return ZJAI_OK;
+}
+
+int make_act_map(Ctx* ctx, CUtensorMap* m, const TView& v, int kc, int bw, int bh) {
+  cuuint64_t dims[4] = {(cuuint64_t)v.c, (cuuint64_t)v.w, (cuuint64_t)v.h, (cuuint64_t)v.n};
+  cuuint64_t strides[3] = {(cuuint64_t)v.pix * 2, (cuuint64_t)v.row * 2, (cuuint64_t)v.img * 2};
+  cuuint32_t box[4] = {(cuuint32_t)kc, (cuuint32_t)bw, (cuuint32_t)bh, 1};
+  size_t span = (size_t)v.img * v.n * 2;
+  return encode(ctx, m, 4, v.p, dims, strides, box, swizzle_for(kc), span);
+}
+
+int make_act_map_s2(Ctx* ctx, CUtensorMap* m, const TView& v, int img, int kc, int bw, int bh) {
+  int h2 = (v.h + 1) / 2, w2 = (v.w + 1) / 2;
+  if (2 * h2 > v.alloc_h || 2 * w2 > v.alloc_w)
+    return fail(ZJAI_INVALID_ARGUMENT, "stride-2 input without an even backing extent");
+  cuuint64_t dims[5] = {(cuuint64_t)v.c, 2, (cuuint64_t)w2, 2, (cuuint64_t)h2};
+  cuuint64_t strides[4] = {(cuuint64_t)v.pix * 2, (cuuint64_t)v.pix * 4, (cuuint64_t)v.row * 2,
+                           (cuuint64_t)v.row * 4};
+  cuuint32_t box[5] = {(cuuint32_t)kc, 1, (cuuint32_t)bw, 1, (cuuint32_t)bh};
+  return encode(ctx, m, 5, v.p + (long long)img * v.img, dims, strides, box, swizzle_for(kc),
+                (size_t)v.img * 2);
+}
+
+int make_weight_map(Ctx* ctx, CUtensorMap* m, const __half* w, int cin_pad, int rows, int kc,
+                    int bn) {
+  cuuint64_t dims[2] = {(cuuint64_t)cin_pad, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cin_pad * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kc, (cuuint32_t)bn};
+  return encode(ctx, m, 2, const_cast<__half*>(w), dims, strides, box, swizzle_for(kc),
+                (size_t)cin_pad * rows * 2);
+}
+
+// ---- packing --------------------------------------------------------------------------------
+static void choose_k(int cin, int* kc, int* cchunks) {
+  *kc = cin > 32 ? 64 : cin > 16 ? 32 : 16;
+  *cchunks = (cin + *kc - 1) / *kc;
+}
+
+static void choose_n(int ncols, int* bn, int* n_tiles) {
+  int nt = (ncols + 255) / 256;
+  int per = (ncols + nt - 1) / nt;
+  *bn = (per + 15) & ~15;
+  *n_tiles = nt;
+}
+
+// Power-of-two scale that brings the largest |w| into [2^13, 2^14): f16 keeps its full
+// 11-bit significand for every weight that matters, far from overflow.
+static float weight_scale(const std::vector<float>& w) {
+  float mx = 0.f;
+  for (float v : w) mx = std::max(mx, std::fabs(v));
+  if (mx == 0.f || !std::isfinite(mx)) return 1.f;
+  int e;
+  std::frexp(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
+  int s = 14 - e;
+  s = std::max(-24, std::min(s, 40));
+  return std::ldexp(1.f, s);
+}
+
+static int upload_layer(Ctx* ctx, ConvLayer* L, const std::vector<float>& wf,
+                        const std::vector<float>& bf) {
+  float s = weight_scale(wf);
+  L->scale = 1.f / s;
+  std::vector<__half> wh(wf.size());
+  for (size_t i = 0; i < wf.size(); ++i) wh[i] = __float2half_rn(wf[i] * s);
+  ZJAI_TRY(cuda_check(cudaMalloc(&L->w, wh.size() * sizeof(__half)), "cudaMalloc weights"));
+  ZJAI_TRY(cuda_check(cudaMemcpy(L->w, wh.data(), wh.size() * sizeof(__half),
+                                 cudaMemcpyHostToDevice),
+                      "upload weights"));
+  ZJAI_TRY(cuda_check(cudaMalloc(&L->bias, bf.size() * sizeof(float)), "cudaMalloc bias"));
+  ZJAI_TRY(cuda_check(
+      cudaMemcpy(L->bias, bf.data(), bf.size() * sizeof(float), cudaMemcpyHostToDevice),
+      "upload bias"));
+  (void)ctx;
+  return ZJAI_OK;
+}
+
+int pack_conv(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, int cout, int kh,
+              int kw, int stride, int pad_h, int pad_w, int groups, const int* extra, int ps) {
+  if (groups <= 0 || cin % groups || cout % groups || kh <= 0 || kw <= 0)
+    return fail(ZJAI_MODEL, "conv2d: inconsistent channel/group/kernel configuration");
+  if (stride != 1 && stride != 2) return fail(ZJAI_UNSUPPORTED, "conv2d: stride must be 1 or 2");
+  if (ps < 1 || cout % (ps * ps)) return fail(ZJAI_INVALID_ARGUMENT, "pixel shuffle factor");
+  const int et = extra ? extra[0] : 0, el = extra ? extra[1] : 0, eb = extra ? extra[2] : 0,
+            er = extra ? extra[3] : 0;
+  if (stride == 2 && (et || el || eb || er))
+    return fail(ZJAI_UNSUPPORTED, "conv2d: extra padding with stride 2");
+  *L = ConvLayer();
+  L->cin = cin;
+  choose_k(cin, &L->kc, &L->cchunks);
+  L->cin_pad = L->kc * L->cchunks;
+  L->kh = kh;
+  L->kw = kw;
+  L->stride = stride;
+  L->pad_t = pad_h + et;
+  L->pad_l = pad_w + el;
+  L->pad_b = pad_h + eb;
+  L->pad_r = pad_w + er;
+  L->R = ps;
+  L->cph = cout / (ps * ps);
+  L->ncols = cout;
+  choose_n(cout, &L->bn, &L->n_tiles);
+  L->npad = L->bn * L->n_tiles;
+  const int taps = kh * kw, icg = cin / groups, ocg = cout / groups, r2 = ps * ps;
+  std::vector<float> wf((size_t)taps * L->npad * L->cin_pad, 0.f), bf(L->npad, 0.f);
+  for (int n = 0; n < cout; ++n) {
+    const int phase = n / L->cph, co = n % L->cph;
+    const int oc = co * r2 + phase;  // PyTorch pixel-shuffle channel order
+    const int g = oc / ocg;
+    if (b) bf[n] = b[oc];
+    for (int i = 0; i < icg; ++i)
+      for (int ky = 0; ky < kh; ++ky)
+        for (int kx = 0; kx < kw; ++kx)
+          wf[((size_t)(ky * kw + kx) * L->npad + n) * L->cin_pad + g * icg + i] =
+              w[(((size_t)oc * icg + i) * kh + ky) * kw + kx];
+  }
+  L->flops_per_px = 2LL * cout * icg * kh * kw;
+  return upload_layer(ctx, L, wf, bf);
+}
+
+int pack_convT(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, int cout, int k,
+               int pad, int out_pad, int post_ps) {
+  if (k <= 0 || pad >= k || out_pad >= 2 || post_ps < 1 || cout % (post_ps * post_ps))
+    return fail(ZJAI_MODEL, "conv_transpose2d: unsupported geometry");
+  *L = ConvLayer();
+  // Output row 2i + p reads input row i + d with kernel row ky = p + pad - 2d.
+  int dmin = 1 << 20, dmax = -(1 << 20);
+  for (int p = 0; p < 2; ++p)
+    for (int d = -k; d <= k; ++d) {
+      int ky = p + pad - 2 * d;
+      if (ky >= 0 && ky < k) {
+        dmin = std::min(dmin, d);
+        dmax = std::max(dmax, d);
+      }
+    }
+  const int win = dmax - dmin + 1;
+  L->cin = cin;
+  choose_k(cin, &L->kc, &L->cchunks);
+  L->cin_pad = L->kc * L->cchunks;
+  L->kh = L->kw = win;
+  L->stride = 1;
+  L->pad_t = L->pad_l = -dmin;
+  L->pad_b = L->pad_r = dmax;
+  L->transposed = 1;
+  L->t_k = k;
+  L->t_pad = pad;
+  L->t_outpad = out_pad;
+  const int r2 = post_ps;
+  L->R = 2 * r2;
+  L->cph = cout / (r2 * r2);
+  L->ncols = 4 * cout;
+  choose_n(L->ncols, &L->bn, &L->n_tiles);
+  L->npad = L->bn * L->n_tiles;
+  const int taps = win * win;
+  std::vector<float> wf((size_t)taps * L->npad * L->cin_pad, 0.f), bf(L->npad, 0.f);
+  long long live = 0;
+  for (int n = 0; n < L->ncols; ++n) {
+    const int q = n / L->cph, cc = n % L->cph;
+    const int Y = q / L->R, X = q % L->R;
+    const int py = Y / r2, dy2 = Y % r2, px = X / r2, dx2 = X % r2;
+    const int co = cc * r2 * r2 + dy2 * r2 + dx2;
+    if (b) bf[n] = b[co];
+    for (int ty = 0; ty < win; ++ty) {
+      const int ky = py + pad - 2 * (ty + dmin);
+      if (ky < 0 || ky >= k) continue;
+      for (int tx = 0; tx < win; ++tx) {
+        const int kx = px + pad - 2 * (tx + dmin);
+        if (kx < 0 || kx >= k) continue;
+        ++live;
+        for (int ci = 0; ci < cin; ++ci)
+          wf[((size_t)(ty * win + tx) * L->npad + n) * L->cin_pad + ci] =
+              w[(((size_t)ci * cout + co) * k + ky) * k + kx];
+      }
+    }
+  }
+  // live (tap, column) pairs summed over all columns = MACs per input pixel / cin
+  L->flops_per_px = 2LL * live * cin;
+  return upload_layer(ctx, L, wf, bf);
+}
+
+void free_conv(ConvLayer* L) {
+  if (L->w) cudaFree(L->w);
+  if (L->bias) cudaFree(L->bias);
+  L->w = nullptr;
+  L->bias = nullptr;
+}
+
+void ConvLayer::out_size(int h, int w, int* oh, int* ow, int* out_h, int* out_w) const {
+  if (!transposed) {
+    *oh = (h + pad_t + pad_b - kh) / stride + 1;
+    *ow = (w + pad_l + pad_r - kw) / stride + 1;
+    *out_h = *oh * R;
+    *out_w = *ow * R;
+  } else {
+    const int th = (h - 1) * 2 + t_k + t_outpad - 2 * t_pad;
+    const int tw = (w - 1) * 2 + t_k + t_outpad - 2 * t_pad;
+    *oh = (th + 1) / 2;
+    *ow = (tw + 1) / 2;
+    *out_h = th * (R / 2);
+    *out_w = tw * (R / 2);
+  }
+}
+
+// ---- launch ---------------------------------------------------------------------------------
+static void pick_tile(int oh, int ow, int* bw, int* bh) {
+  long long best = -1;
+  int bbw = 16;
+  const int cands[5] = {16, 32, 8, 64, 128};
+  for (int c : cands) {
+    int h = 128 / c;
+    long long area = (long long)((ow + c - 1) / c) * c * ((oh + h - 1) / h) * h;
+    if (best < 0 || area < best) {
+      best = area;
+      bbw = c;
+    }
+  }
+  *bw = bbw;
+  *bh = 128 / bbw;
+}
+
+int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
+  if (in.c != L.cin)
+    return fail(ZJAI_INVALID_ARGUMENT, "conv: input channel count mismatch (" +
+                                           std::to_string(in.c) + " vs " +
+                                           std::to_string(L.cin) + ")");
+  if (in.h <= 0 || in.w <= 0) return fail(ZJAI_INVALID_ARGUMENT, "conv: empty input");
+  int oh, ow, out_h, out_w;
+  L.out_size(in.h, in.w, &oh, &ow, &out_h, &out_w);
+  if (oh <= 0 || ow <= 0) return fail(ZJAI_INVALID_ARGUMENT, "conv: input smaller than kernel");
+  // Requested output extent (a crop of the natural one).
+  int want_h = o.planar ? (o.out_h >= 0 ? o.out_h : out_h) : o.out.h;
+  int want_w = o.planar ? (o.out_w >= 0 ? o.out_w : out_w) : o.out.w;
+  if (want_h > out_h || want_w > out_w)
+    return fail(ZJAI_INVALID_ARGUMENT, "conv: output view larger than the layer's output");
+  oh = std::min(oh, (want_h + L.R - 1) / L.R);
+  ow = std::min(ow, (want_w + L.R - 1) / L.R);
+  if (!o.planar && (L.cph % 8 != 0))
+    return fail(ZJAI_UNSUPPORTED, "conv: NHWC output needs a multiple of 8 channels");
+
+  ConvArgs a;
+  memset(&a, 0, sizeof a);
+  pick_tile(oh, ow, &a.bw, &a.bh);
+  a.tiles_x = (ow + a.bw - 1) / a.bw;
+  a.tiles_y = (oh + a.bh - 1) / a.bh;
+  a.n_tiles = L.n_tiles;
+  a.kw = L.kw;
+  a.taps = L.kh * L.kw;
+  a.pad_t = L.pad_t;
+  a.pad_l = L.pad_l;
+  a.s2 = L.stride == 2;
+  a.cchunks = L.cchunks;
+  a.kc = L.kc;
+  a.bn = L.bn;
+  const uint32_t stage = conv_stage_bytes(L.kc, L.bn);
+  a.stages = (int)std::min<uint32_t>(8, (232448u - 1024u - kStagingBytes - 256u) / stage);
+  int tc = 32;
+  while (tc < 2 * L.bn) tc *= 2;
+  a.tmem_cols = tc;
+  a.oh = oh;
+  a.ow = ow;
+  a.bias = L.bias;
+  a.scale = L.scale;
+  a.act1 = o.act1;
+  a.op = o.op;
+  a.act2 = o.act2;
+  a.R = L.R;
+  a.cph = L.cph;
+  a.err = ctx->d_err;
+  if (!o.planar) {
+    a.out = o.out.p;
+    a.out_pix = o.out.pix;
+    a.out_row = o.out.row;
+    a.out_img = o.out.img;
+    a.out_h = want_h;
+    a.out_w = want_w;
+    if (o.op != OP_NONE) {
+      if (!o.r1) return fail(ZJAI_INVALID_ARGUMENT, "conv: residual operand missing");
+      a.r1 = o.r1->p;
+      a.r1_pix = o.r1->pix;
+      a.r1_row = o.r1->row;
+      a.r1_img = o.r1->img;
+    }
+    if (o.op == OP_CAB) {
+      if (!o.r2) return fail(ZJAI_INVALID_ARGUMENT, "conv: CAB operand missing");
+      a.r2 = o.r2->p;
+      a.r2_pix = o.r2->pix;
+      a.r2_row = o.r2->row;
+      a.r2_img = o.r2->img;
+    }
+    if (o.out2) {
+      a.out2 = o.out2->p;
+      a.o2_pix = o.out2->pix;
+      a.o2_row = o.out2->row;
+      a.o2_img = o.out2->img;
+    }
+  } else {
+    a.planar = 1;
+    a.denorm = o.denorm;
+    a.pout = o.pout;
+    a.p_plane = o.p_plane;
+    a.p_row = o.p_row;
+    a.p_img = o.p_img;
+    a.out_h = want_h;
+    a.out_w = want_w;
+    a.py0 = o.py0;
+    a.px0 = o.px0;
+    a.cy0 = o.cy0;
+    a.cy1 = o.cy1;
+    a.cx0 = o.cx0;
+    a.cx1 = o.cx1;
+    a.sv = o.sv;
+    a.sh = o.sh;
+  }
+
+  CUtensorMap tmB;
+  ZJAI_TRY(make_weight_map(ctx, &tmB, L.w, L.cin_pad, a.taps * L.npad, L.kc, L.bn));
+  if (!a.s2) {
+    CUtensorMap tmA;
+    ZJAI_TRY(make_act_map(ctx, &tmA, in, L.kc, a.bw, a.bh));
+    a.n_img = in.n;
+    a.num_tiles = a.tiles_x * a.tiles_y * a.n_img * a.n_tiles;
+    launch_conv(tmA, tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
+    ctx->launches++;
+  } else {
+    // The parity-split 5-D view has no batch axis: one launch per picture.
+    for (int i = 0; i < in.n; ++i) {
+      CUtensorMap tmA;
+      ZJAI_TRY(make_act_map_s2(ctx, &tmA, in, i, L.kc, a.bw, a.bh));
+      ConvArgs ai = a;
+      ai.n_img = 1;
+      ai.num_tiles = a.tiles_x * a.tiles_y * a.n_tiles;
+      if (ai.out) ai.out += i * a.out_img;
+      if (ai.r1) ai.r1 += i * a.r1_img;
+      if (ai.r2) ai.r2 += i * a.r2_img;
+      if (ai.out2) ai.out2 += i * a.o2_img;
+      if (ai.pout) ai.pout += i * a.p_img;
+      launch_conv(tmA, tmB, ai, std::min(ai.num_tiles, ctx->sms), ctx->stream);
+      ctx->launches++;
+    }
+  }
+  return cuda_check(cudaGetLastError(), "conv launch");
+}
+
+}  // namespace zjai

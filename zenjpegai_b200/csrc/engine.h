@@ -1,0 +1,138 @@
+// Host-side engine internals: context, device arena, NHWC tensor views, packed layers.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/zjai.h"
+#include "conv_tc.cuh"
+
+namespace zjai {
+
+// ---- errors -------------------------------------------------------------------------------
+struct Error {
+  int code;
+  std::string msg;
+};
+void set_last_error(int code, const std::string& msg);
+#define ZJAI_TRY(expr)                         \
+  do {                                         \
+    int _st = (expr);                          \
+    if (_st != ZJAI_OK) return _st;            \
+  } while (0)
+int fail(int code, const std::string& msg);  // records and returns code
+int cuda_check(cudaError_t e, const char* what);
+
+// ---- device arena (bump allocator, 256-byte aligned) ---------------------------------------
+struct Arena {
+  char* base = nullptr;
+  size_t cap = 0, top = 0, peak = 0;
+  void* alloc(size_t bytes);  // nullptr when exhausted
+  size_t mark() const { return top; }
+  void release(size_t m) { top = m; }
+};
+
+// NHWC f16 view: element (n, y, x, c) at p[n*img + y*row + x*pix + c]. A crop is a view with
+// smaller h / w over the same memory; a channel slice is a view with an offset pointer.
+struct TView {
+  __half* p = nullptr;
+  int n = 1, h = 0, w = 0, c = 0;
+  long long pix = 0, row = 0, img = 0;
+  // rows / cols actually backed by zeroed memory beyond (h, w) (stride-2 inputs need even)
+  int alloc_h = 0, alloc_w = 0;
+  TView crop(int hh, int ww) const {
+    TView v = *this;
+    v.h = hh;
+    v.w = ww;
+    return v;
+  }
+  TView channels(int c0, int cc) const {
+    TView v = *this;
+    v.p = p + c0;
+    v.c = cc;
+    return v;
+  }
+};
+
+struct Ctx {
+  int device = 0;
+  int sms = 148;
+  cudaStream_t own = nullptr, stream = nullptr, stream2 = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  Arena arena;
+  int* d_err = nullptr;  // kernel status word
+  std::atomic<long long> launches{0};
+  // driver entry point
+  void* encode_fn = nullptr;
+  int driver_version = 0;
+};
+
+// Allocate an NHWC f16 tensor in the arena; channels padded to `cpad` (multiple of 8), and
+// rows / cols rounded up to even so any stride-2 consumer can read it. Zero-filled when
+// `zero` (async on ctx stream).
+int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero = false);
+
+// ---- TMA descriptors ------------------------------------------------------------------------
+int make_act_map(Ctx* ctx, CUtensorMap* m, const TView& v, int kc, int bw, int bh);
+int make_act_map_s2(Ctx* ctx, CUtensorMap* m, const TView& v, int img, int kc, int bw, int bh);
+int make_weight_map(Ctx* ctx, CUtensorMap* m, const __half* w, int cin_pad, int rows, int kc,
+                    int bn);
+
+// ---- packed convolution ---------------------------------------------------------------------
+// A convolution (or a stride-2 transposed convolution rewritten as a phase convolution)
+// packed for conv_tc_kernel: weights [tap][npad][cin_pad] f16 scaled by 2^s, bias [npad] f32
+// in the same (phase-major) column order.
+struct ConvLayer {
+  int cin = 0, kc = 64, cchunks = 1, cin_pad = 64;
+  int kh = 1, kw = 1, pad_t = 0, pad_l = 0, pad_b = 0, pad_r = 0, stride = 1;
+  int ncols = 0, bn = 16, n_tiles = 1, npad = 16;
+  int R = 1, cph = 1;
+  int transposed = 0, t_k = 0, t_pad = 0, t_outpad = 0;  // convT output-size rule
+  float scale = 1.f;
+  __half* w = nullptr;
+  float* bias = nullptr;
+  long long flops_per_px = 0;  // algorithmic MACs*2 per conv-output pixel (live taps only)
+  // conv output extent (GEMM M space) and shuffled output extent for an input of h x w
+  void out_size(int h, int w, int* oh, int* ow, int* out_h, int* out_w) const;
+};
+
+// Pack a PyTorch conv (weight [cout][cin/groups][kh][kw]) with zero border `extra` and an
+// optional pixel shuffle `ps` folded into the column order.
+int pack_conv(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, int cout, int kh,
+              int kw, int stride, int pad_h, int pad_w, int groups, const int* extra, int ps);
+// Pack a PyTorch stride-2 transposed conv (weight [cin][cout][k][k]) as a phase conv; `post_ps`
+// folds a following pixel shuffle (HOP chroma output) into the columns.
+int pack_convT(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, int cout, int k,
+               int pad, int out_pad, int post_ps);
+void free_conv(ConvLayer* L);
+
+// Epilogue / output description for one conv launch.
+struct ConvOut {
+  int act1 = ACT_NONE, op = OP_NONE, act2 = ACT_NONE;
+  TView out;                 // NHWC output (logical extent = crop)
+  const TView* r1 = nullptr;  // residual operands in output space
+  const TView* r2 = nullptr;
+  const TView* out2 = nullptr;  // relu6 copy
+  // planar f32 output
+  bool planar = false, denorm = false;
+  float* pout = nullptr;
+  long long p_plane = 0, p_row = 0, p_img = 0;
+  int py0 = 0, px0 = 0, cy0 = 0, cy1 = 1 << 30, cx0 = 0, cx1 = 1 << 30, sv = 1, sh = 1;
+  int out_h = -1, out_w = -1;  // planar: network output extent clip (-1 = from layer)
+};
+
+int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o);
+
+// ---- elementwise / layout kernels (kernels_misc.cu) ---------------------------------------
+// planar f32 [n][c][h][w] window (y0, x0, h, w of a [c][H][W] source) -> NHWC f16 view
+void launch_planar_to_nhwc(const float* src, int c, int H, int W, int y0, int x0,
+                           const TView& dst, cudaStream_t s);
+void launch_nhwc_to_planar(const TView& src, float* dst, cudaStream_t s);
+void launch_relu6(const TView& src, const TView& dst, cudaStream_t s);
+
+}  // namespace zjai
