@@ -159,6 +159,17 @@ int zjai_synthesize(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, const floa
                     int out_w, int tile_size, int overlap, int sv, int sh, float *rec_y,
                     float *rec_u, float *rec_v, int mem, const volatile int *cancel);
 
+/* The per-tile half of zjai_synthesize (the `par_map` over tiles of reconstruct.rs:390 and
+ * :432): synthesizes only the listed tiles and writes only their cores. Tiles of one shape
+ * run as one batch. This is the unit a multi-GPU scheduler shards (e.g. tile i on GPU
+ * i mod N); planes not covered by the listed cores are left untouched (device) or zero
+ * (host). */
+int zjai_synthesize_tiles(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv,
+                          const float *y_hat_y, const float *y_hat_uv, int lh, int lw,
+                          const zjai_tile *tiles, int ntiles, int out_h, int out_w, int sv,
+                          int sh, float *rec_y, float *rec_u, float *rec_v, int mem,
+                          const volatile int *cancel);
+
 /* ---------------------------------------------------------------------------------------- */
 /* Output stage (src/decoder/output.rs)                                                       */
 /* ---------------------------------------------------------------------------------------- */

@@ -62,6 +62,24 @@ int stage_out_finish(Ctx* ctx, float* host, const float* dev, size_t n, int mem)
       cudaMemcpyAsync(host, dev, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream), "D2H");
 }
 
+// Host copy of a caller array that the host must read (weights, biases, LN parameters):
+// device arrays are copied down, host arrays are used in place.
+int fetch_host(const float* p, size_t n, int mem, std::vector<float>* buf, const float** out) {
+  if (!p) {
+    *out = nullptr;
+    return ZJAI_OK;
+  }
+  if (mem == ZJAI_MEM_HOST) {
+    *out = p;
+    return ZJAI_OK;
+  }
+  buf->resize(n);
+  ZJAI_TRY(cuda_check(cudaMemcpy(buf->data(), p, n * sizeof(float), cudaMemcpyDeviceToHost),
+                      "parameter D2H"));
+  *out = buf->data();
+  return ZJAI_OK;
+}
+
 // Planar f32 [c][h][w] (device) -> fresh zeroed NHWC f16 tensor.
 int planar_to_tensor(Ctx* ctx, const float* d, int c, int h, int w, TView* out) {
   ZJAI_TRY(alloc_tensor(ctx, 1, h, w, c, out, true));
@@ -92,7 +110,8 @@ int zjai_ctx_create(int device, size_t arena_bytes, zjai_ctx** out) {
   zjai_ctx* c = new zjai_ctx();
   c->device = device;
   c->sms = prop.multiProcessorCount;
-  if (arena_bytes == 0) arena_bytes = size_t(4) << 30;
+  if (arena_bytes == 0) arena_bytes = size_t(8) << 30;
+  if (arena_bytes < (size_t(64) << 20)) arena_bytes = size_t(64) << 20;
   int st = ZJAI_OK;
   if ((st = cuda_check(cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking), "stream")) ||
       (st = cuda_check(cudaStreamCreateWithFlags(&c->stream2, cudaStreamNonBlocking), "stream")) ||
@@ -105,7 +124,11 @@ int zjai_ctx_create(int device, size_t arena_bytes, zjai_ctx** out) {
     zjai_ctx_destroy(c);
     return st;
   }
-  c->arena.cap = arena_bytes;
+  // luma / single-stream work gets 5/8 of the arena, the chroma stream the rest
+  const size_t first = (arena_bytes / 8 * 5) & ~size_t(255);
+  c->arena.cap = first;
+  c->arena2.base = c->arena.base + first;
+  c->arena2.cap = arena_bytes - first;
   c->stream = c->own;
   cudaDriverEntryPointQueryResult q;
   if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &c->encode_fn, cudaEnableDefault, &q) !=
@@ -157,8 +180,13 @@ int zjai_conv2d(zjai_ctx* ctx, const float* x, int c, int h, int w, const float*
       pad_w == 1 && !bias && act == ZJAI_ACT_NONE && !(extra && (extra[0] | extra[1] | extra[2] | extra[3])))
     return zjai_depthwise3x3(ctx, x, c, h, w, weight, out, mem);
   ArenaScope scope(ctx);
+  std::vector<float> wbuf, bbuf;
+  const float *hw, *hb;
+  if (groups <= 0 || c % groups) return fail(ZJAI_INVALID_ARGUMENT, "conv2d: groups");
+  ZJAI_TRY(fetch_host(weight, (size_t)oc * (c / groups) * kh * kw, mem, &wbuf, &hw));
+  ZJAI_TRY(fetch_host(bias, (size_t)oc, mem, &bbuf, &hb));
   ConvLayer L;
-  ZJAI_TRY(pack_conv(ctx, &L, weight, bias, c, oc, kh, kw, stride, pad_h, pad_w, groups, extra, 1));
+  ZJAI_TRY(pack_conv(ctx, &L, hw, hb, c, oc, kh, kw, stride, pad_h, pad_w, groups, extra, 1));
   LayerGuard guard(&L);
   int oh, ow, out_h, out_w;
   L.out_size(h, w, &oh, &ow, &out_h, &out_w);
@@ -188,8 +216,12 @@ int zjai_conv_transpose2d(zjai_ctx* ctx, const float* x, int c, int h, int w,
   if (!x || !weight || !out || c <= 0 || h <= 0 || w <= 0 || oc <= 0)
     return fail(ZJAI_INVALID_ARGUMENT, "conv_transpose2d: bad arguments");
   ArenaScope scope(ctx);
+  std::vector<float> wbuf, bbuf;
+  const float *hw, *hb;
+  ZJAI_TRY(fetch_host(weight, (size_t)c * oc * k * k, mem, &wbuf, &hw));
+  ZJAI_TRY(fetch_host(bias, (size_t)oc, mem, &bbuf, &hb));
   ConvLayer L;
-  ZJAI_TRY(pack_convT(ctx, &L, weight, bias, c, oc, k, pad, out_pad, 1));
+  ZJAI_TRY(pack_convT(ctx, &L, hw, hb, c, oc, k, pad, out_pad, 1));
   LayerGuard guard(&L);
   int oh, ow, out_h, out_w;
   L.out_size(h, w, &oh, &ow, &out_h, &out_w);

@@ -1,5 +1,7 @@
 // Shared helpers of the C-ABI translation units.
 #pragma once
+#include <vector>
+
 #include "engine.h"
 
 struct zjai_ctx : zjai::Ctx {};
@@ -13,6 +15,7 @@ int stage_in(Ctx* ctx, const float* p, size_t n, int mem, const float** out);
 int stage_out_alloc(Ctx* ctx, float* p, size_t n, int mem, float** dev);
 int stage_out_finish(Ctx* ctx, float* host, const float* dev, size_t n, int mem);
 int planar_to_tensor(Ctx* ctx, const float* d, int c, int h, int w, TView* out);
+int fetch_host(const float* p, size_t n, int mem, std::vector<float>* buf, const float** out);
 
 // Releases arena allocations made inside a call when the call returns.
 struct ArenaScope {

@@ -280,6 +280,16 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             }
           }
         } else {
+          int py0 = a.py0, px0 = a.px0, cy0 = a.cy0, cy1 = a.cy1, cx0 = a.cx0, cx1 = a.cx1;
+          if (a.img_win) {
+            const int* wv = a.img_win + 6 * tc.img;
+            py0 = wv[0];
+            px0 = wv[1];
+            cy0 = wv[2];
+            cy1 = wv[3];
+            cx0 = wv[4];
+            cx1 = wv[5];
+          }
           for (int it = et; it < 128 * cw; it += 128) {
             const int pm = it / cw, j = it - (it / cw) * cw;
             const int oy = tc.oy0 + pm / a.bw, ox = tc.ox0 + pm % a.bw;
@@ -289,14 +299,15 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             if (p >= a.R * a.R) continue;
             const int Y = oy * a.R + p / a.R, X = ox * a.R + p % a.R;
             if (Y >= a.out_h || X >= a.out_w) continue;
-            const int PY = a.py0 + Y, PX = a.px0 + X;
-            if (PY < a.cy0 || PY >= a.cy1 || PX < a.cx0 || PX >= a.cx1) continue;
+            const int PY = py0 + Y, PX = px0 + X;
+            if (PY < cy0 || PY >= cy1 || PX < cx0 || PX >= cx1) continue;
             if (PY % a.sv || PX % a.sh) continue;
             const float4* rrow = reinterpret_cast<const float4*>(staging + pm * 32);
             const float4 f4 = rrow[(j >> 2) ^ (pm & (nchunk4 - 1))];
             float x = (j & 3) == 0 ? f4.x : (j & 3) == 1 ? f4.y : (j & 3) == 2 ? f4.z : f4.w;
             if (a.denorm) x = fminf(fmaxf(x * 128.f + 127.5f, 0.f), 255.f);
-            a.pout[tc.img * a.p_img + ch * a.p_plane + (PY / a.sv) * a.p_row + PX / a.sh] = x;
+            float* dst = (ch == 1 && a.pout2) ? a.pout2 : a.pout + ch * a.p_plane;
+            dst[(a.img_win ? 0 : tc.img * a.p_img) + (PY / a.sv) * a.p_row + PX / a.sh] = x;
           }
         }
         named_bar_sync(1, 128);

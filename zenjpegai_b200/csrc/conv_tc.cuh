@@ -53,9 +53,11 @@ struct ConvArgs {
   // planar f32 output
   int planar, denorm;
   float* pout;
+  float* pout2;        // plane 1 (when not at pout + p_plane)
   long long p_plane, p_row, p_img;
   int py0, px0;        // picture coordinates of output pixel (0, 0)
   int cy0, cy1, cx0, cx1;
+  const int* img_win;  // per-image {py0, px0, cy0, cy1, cx0, cx1} (device), or null
   int sv, sh;
   int* err;
 };

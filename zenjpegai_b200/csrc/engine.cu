@@ -38,15 +38,18 @@ void* Arena::alloc(size_t bytes) {
   return base + start;
 }
 
-int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero) {
+int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero, Arena* arena,
+                 cudaStream_t stream) {
+  if (!arena) arena = &ctx->arena;
+  if (!stream) stream = ctx->stream;
   int cp = (c + 7) & ~7;
   int ah = (h + 1) & ~1, aw = (w + 1) & ~1;
   size_t bytes = (size_t)n * ah * aw * cp * sizeof(__half);
-  void* p = ctx->arena.alloc(bytes);
+  void* p = arena->alloc(bytes);
   if (!p)
     return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (" + std::to_string(bytes) +
                                          " more bytes, capacity " +
-                                         std::to_string(ctx->arena.cap) + ")");
+                                         std::to_string(arena->cap) + ")");
   TView v;
   v.p = static_cast<__half*>(p);
   v.n = n;
@@ -58,7 +61,7 @@ int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero) {
   v.img = (long long)ah * aw * cp;
   v.alloc_h = ah;
   v.alloc_w = aw;
-  if (zero) ZJAI_TRY(cuda_check(cudaMemsetAsync(p, 0, bytes, ctx->stream), "memset"));
+  if (zero) ZJAI_TRY(cuda_check(cudaMemsetAsync(p, 0, bytes, stream), "memset"));
   *out = v;
   return ZJAI_OK;
 }
@@ -394,6 +397,8 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     a.planar = 1;
     a.denorm = o.denorm;
     a.pout = o.pout;
+    a.pout2 = o.pout2;
+    a.img_win = o.img_win;
     a.p_plane = o.p_plane;
     a.p_row = o.p_row;
     a.p_img = o.p_img;
@@ -430,7 +435,8 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
       if (ai.r1) ai.r1 += i * a.r1_img;
       if (ai.r2) ai.r2 += i * a.r2_img;
       if (ai.out2) ai.out2 += i * a.o2_img;
-      if (ai.pout) ai.pout += i * a.p_img;
+      if (ai.pout && !ai.img_win) ai.pout += i * a.p_img;
+      if (ai.img_win) ai.img_win += 6 * i;
       launch_conv(tmA, tmB, ai, std::min(ai.num_tiles, ctx->sms), ctx->stream);
       ctx->launches++;
     }

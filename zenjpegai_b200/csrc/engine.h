@@ -64,7 +64,8 @@ struct Ctx {
   int sms = 148;
   cudaStream_t own = nullptr, stream = nullptr, stream2 = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
-  Arena arena;
+  Arena arena;   // work of `stream`
+  Arena arena2;  // work of `stream2` (chroma synthesis runs beside luma)
   int* d_err = nullptr;  // kernel status word
   std::atomic<long long> launches{0};
   // driver entry point
@@ -75,7 +76,8 @@ struct Ctx {
 // Allocate an NHWC f16 tensor in the arena; channels padded to `cpad` (multiple of 8), and
 // rows / cols rounded up to even so any stride-2 consumer can read it. Zero-filled when
 // `zero` (async on ctx stream).
-int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero = false);
+int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero = false,
+                 Arena* arena = nullptr, cudaStream_t stream = nullptr);
 
 // ---- TMA descriptors ------------------------------------------------------------------------
 int make_act_map(Ctx* ctx, CUtensorMap* m, const TView& v, int kc, int bw, int bh);
@@ -121,6 +123,8 @@ struct ConvOut {
   // planar f32 output
   bool planar = false, denorm = false;
   float* pout = nullptr;
+  float* pout2 = nullptr;
+  const int* img_win = nullptr;  // per-image output windows (device), see ConvArgs
   long long p_plane = 0, p_row = 0, p_img = 0;
   int py0 = 0, px0 = 0, cy0 = 0, cy1 = 1 << 30, cx0 = 0, cx1 = 1 << 30, sv = 1, sh = 1;
   int out_h = -1, out_w = -1;  // planar: network output extent clip (-1 = from layer)

@@ -1,0 +1,77 @@
+// Network objects and the per-call runner that executes a topology on a batch of tiles.
+#pragma once
+#include <map>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+
+namespace zjai {
+
+// A loaded network: packed conv layers and small f32 parameter vectors, GPU resident.
+struct Net {
+  Ctx* ctx = nullptr;
+  int kind = 0, op = 0;
+  std::map<std::string, ConvLayer> convs;
+  std::map<std::string, float*> vecs;  // LN weight/bias, temperature, depthwise weights [c][9]
+  ~Net();
+};
+
+// Where a synthesis network's final planar output goes.
+struct FinalOut {
+  float* plane0 = nullptr;
+  float* plane1 = nullptr;       // second plane (chroma V); null: plane0 + plane_stride
+  long long plane_stride = 0, row = 0, img = 0;
+  const int* win = nullptr;      // per-tile {py0, px0, cy0, cy1, cx0, cx1} (device) or null
+  int sv = 1, sh = 1;
+  int full_h = -1, full_w = -1;  // clip of the network output extent (-1: natural)
+};
+
+// Executes one network on a batch of `n` same-shape inputs on one stream, allocating its
+// activations from one arena. Temporaries of each block are released when the block has been
+// enqueued (the stream orders their reuse).
+struct Runner {
+  Ctx* ctx = nullptr;
+  Net* net = nullptr;
+  Arena* arena = nullptr;
+  cudaStream_t stream = nullptr;
+  int n = 1;
+  const volatile int* cancel = nullptr;
+  bool count_flops = false;
+  double flops = 0.0;
+
+  int alloc(int h, int w, int c, TView* v);
+  const ConvLayer* layer(const std::string& name);
+  int conv(const std::string& name, const TView& in, ConvOut o);
+  int out_extent(const std::string& name, int h, int w, int* oh, int* ow);
+  int stop_check();
+
+  int resau(const std::string& p, const TView& x, const TView& a, int ch, int cw, TView* y);
+  int rb(const std::string& p, const TView& x, const TView& y, const TView* relu6_out = nullptr);
+  int cab(const std::string& p, const TView& x, const TView& out, const TView* a_out);
+  int tb(const std::string& p, const TView& x);
+  int tam(const std::string& p, const TView& x, bool ds, int ch, int cw, TView* y, TView* a_out);
+  int upsample(const std::string& p, const TView& x, int ch, int cw, TView* y, TView* a_out);
+  int final_planar(const std::string& name, const TView& x, const FinalOut& fo);
+
+  int primary(const TView& y, int h, int w, const FinalOut& fo);
+  int secondary(const TView& cat, const TView& x144, int h, int w, const FinalOut& fo);
+  int analysis(const TView& x, int h, int w, float* out);
+};
+
+struct ArenaMark {
+  Arena* a;
+  size_t m;
+  explicit ArenaMark(Arena* ar) : a(ar), m(ar->mark()) {}
+  ~ArenaMark() { a->release(m); }
+};
+
+int load_network(Ctx* ctx, int kind, int op, const zjai_param* params, int nparams, Net** out);
+int synthesis_tiles(int height, int width, int latent_h, int latent_w, int tile_size,
+                    int overlap, std::vector<zjai_tile>* out);
+void synth_out_size(int kind, int op, int h, int w, int* oh, int* ow);
+
+void launch_replicate_pad(const TView& src, const TView& dst, cudaStream_t s);
+void launch_normalize_pad(const float* src, int c, int h, int w, const TView& dst, cudaStream_t s);
+
+}  // namespace zjai

@@ -1,0 +1,405 @@
+// C ABI of the networks, the tiling scheduler and the attention-block layer entries.
+#include <algorithm>
+#include <map>
+#include <tuple>
+#include <vector>
+
+#include "api_common.h"
+#include "kernels_attn.h"
+#include "net.h"
+
+struct zjai_net : zjai::Net {};
+
+using namespace zjai;
+
+namespace {
+
+int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+int net_enter(zjai_net* net) {
+  if (!net || !net->ctx) return fail(ZJAI_INVALID_ARGUMENT, "null network");
+  return ctx_enter(static_cast<zjai_ctx*>(net->ctx));
+}
+
+// Device int array (arena) holding `v`.
+int upload_ints(Ctx* ctx, Arena* arena, const std::vector<int>& v, cudaStream_t s, int** out) {
+  int* d = static_cast<int*>(arena->alloc(v.size() * sizeof(int) + 16));
+  if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (descriptors)");
+  ZJAI_TRY(cuda_check(cudaMemcpyAsync(d, v.data(), v.size() * sizeof(int), cudaMemcpyHostToDevice, s),
+                      "descriptor H2D"));
+  *out = d;
+  return ZJAI_OK;
+}
+
+Runner make_runner(Ctx* ctx, Net* net, Arena* arena, cudaStream_t s, int n,
+                   const volatile int* cancel) {
+  Runner r;
+  r.ctx = ctx;
+  r.net = net;
+  r.arena = arena;
+  r.stream = s;
+  r.n = n;
+  r.cancel = cancel;
+  return r;
+}
+
+// Sync after a failure so the context and its arena stay usable.
+int settle(Ctx* ctx, int st) {
+  cudaStreamSynchronize(ctx->stream);
+  cudaStreamSynchronize(ctx->stream2);
+  return st;
+}
+
+}  // namespace
+
+namespace zjai {
+
+// Synthesis of the listed tiles: same-shape tiles run as one batch; luma on ctx->stream with
+// ctx->arena, chroma on ctx->stream2 with ctx->arena2 (reconstruct.rs:314-323 runs the two
+// components side by side). Output planes are device pointers.
+int synthesize_tiles_dev(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const float* lat_uv,
+                         int lh, int lw, const std::vector<zjai_tile>& tiles, int out_h, int out_w,
+                         int sv, int sh, float* rec_y, float* rec_u, float* rec_v,
+                         const volatile int* cancel, double* flops) {
+  if (!ny || !nuv || ny->kind != ZJAI_SYN_Y || nuv->kind != ZJAI_SYN_UV || ny->op != nuv->op)
+    return fail(ZJAI_INVALID_ARGUMENT, "synthesize: needs a SYN_Y and a SYN_UV network of one op");
+  if (sv <= 0 || sh <= 0) return fail(ZJAI_INVALID_DATA, "chroma subsampling factor");
+  const int cw_ = cdiv(out_w, sh);
+  // group same-shape tiles
+  std::map<std::tuple<int, int, int, int>, std::vector<int>> groups;
+  for (size_t i = 0; i < tiles.size(); ++i) {
+    const zjai_tile& t = tiles[i];
+    if (t.lat_x < 0 || t.lat_y < 0 || t.lat_x + t.lat_w > lw || t.lat_y + t.lat_h > lh)
+      return fail(ZJAI_INVALID_DATA, "synthesis tile outside the latent");
+    groups[std::make_tuple(t.img_h, t.img_w, t.lat_h, t.lat_w)].push_back((int)i);
+  }
+  cudaStream_t s1 = ctx->stream, s2 = ctx->stream2;
+  ZJAI_TRY(cuda_check(cudaEventRecord(ctx->ev_fork, s1), "event"));
+  ZJAI_TRY(cuda_check(cudaStreamWaitEvent(s2, ctx->ev_fork, 0), "event wait"));
+  for (auto& kv : groups) {
+    if (cancel && *cancel) return fail(ZJAI_CANCELLED, "stopped: cancelled by the caller");
+    const int img_h = std::get<0>(kv.first), img_w = std::get<1>(kv.first);
+    const int lat_h = std::get<2>(kv.first), lat_w = std::get<3>(kv.first);
+    const std::vector<int>& idx = kv.second;
+    const int n = (int)idx.size();
+    std::vector<int> origin, win;
+    for (int i : idx) {
+      const zjai_tile& t = tiles[i];
+      origin.push_back(t.lat_x);
+      origin.push_back(t.lat_y);
+      win.insert(win.end(), {t.img_y, t.img_x, t.core_y, std::min(t.core_y + t.core_h, out_h),
+                             t.core_x, std::min(t.core_x + t.core_w, out_w)});
+    }
+    // each stream reads descriptor copies from its own arena
+    int *d_origin, *d_origin2, *d_win_y, *d_win_uv;
+    ZJAI_TRY(upload_ints(ctx, &ctx->arena, origin, s1, &d_origin));
+    ZJAI_TRY(upload_ints(ctx, &ctx->arena, win, s1, &d_win_y));
+    ZJAI_TRY(upload_ints(ctx, &ctx->arena2, origin, s2, &d_origin2));
+    ZJAI_TRY(upload_ints(ctx, &ctx->arena2, win, s2, &d_win_uv));
+    // latent windows: [n][lat_h][lat_w][256] = luma 160 | chroma 96 (stream 1)
+    TView cat;
+    ZJAI_TRY(alloc_tensor(ctx, n, lat_h, lat_w, 256, &cat, false, &ctx->arena, s1));
+    launch_gather_latent(lat_y, 160, lh, lw, d_origin, cat.channels(0, 160), s1);
+    launch_gather_latent(lat_uv, 96, lh, lw, d_origin, cat.channels(160, 96), s1);
+    ctx->launches += 2;
+    ZJAI_TRY(cuda_check(cudaEventRecord(ctx->ev_fork, s1), "event"));
+    // luma
+    {
+      Runner r = make_runner(ctx, ny, &ctx->arena, s1, n, cancel);
+      r.count_flops = flops != nullptr;
+      FinalOut fo;
+      fo.plane0 = rec_y;
+      fo.row = out_w;
+      fo.win = d_win_y;
+      ZJAI_TRY(r.primary(cat.channels(0, 160), img_h, img_w, fo));
+      if (flops) *flops += r.flops;
+    }
+    // chroma
+    ZJAI_TRY(cuda_check(cudaStreamWaitEvent(s2, ctx->ev_fork, 0), "event wait"));
+    {
+      Runner r = make_runner(ctx, nuv, &ctx->arena2, s2, n, cancel);
+      r.count_flops = flops != nullptr;
+      TView x144;
+      ZJAI_TRY(alloc_tensor(ctx, n, lat_h, lat_w, 144, &x144, false, &ctx->arena2, s2));
+      launch_gather_latent(lat_uv, 96, lh, lw, d_origin2, x144.channels(48, 96), s2);
+      ctx->launches++;
+      FinalOut fo;
+      fo.plane0 = rec_u;
+      fo.plane1 = rec_v;
+      fo.row = cw_;
+      fo.win = d_win_uv;
+      fo.sv = sv;
+      fo.sh = sh;
+      ZJAI_TRY(r.secondary(cat, x144, img_h, img_w, fo));
+      if (flops) *flops += r.flops;
+    }
+  }
+  ZJAI_TRY(cuda_check(cudaEventRecord(ctx->ev_join, s2), "event"));
+  return cuda_check(cudaStreamWaitEvent(s1, ctx->ev_join, 0), "event wait");
+}
+
+}  // namespace zjai
+
+extern "C" {
+
+int zjai_net_create(zjai_ctx* ctx, int kind, int op, const zjai_param* params, int nparams,
+                    zjai_net** out) {
+  if (!out) return fail(ZJAI_INVALID_ARGUMENT, "null output handle");
+  *out = nullptr;
+  ZJAI_TRY(ctx_enter(ctx));
+  if (kind < ZJAI_SYN_Y || kind > ZJAI_ANA_UV) return fail(ZJAI_INVALID_ARGUMENT, "unknown network kind");
+  Net* n = nullptr;
+  ZJAI_TRY(load_network(ctx, kind, op, params, nparams, &n));
+  // the C handle is the same object
+  *out = reinterpret_cast<zjai_net*>(n);
+  return ZJAI_OK;
+}
+
+int zjai_net_destroy(zjai_net* net) {
+  if (!net) return ZJAI_OK;
+  cudaSetDevice(net->ctx->device);
+  cudaDeviceSynchronize();
+  delete reinterpret_cast<Net*>(net);
+  return ZJAI_OK;
+}
+
+int zjai_synth_out_size(int kind, int op, int h, int w, int* out_h, int* out_w) {
+  if (!out_h || !out_w || h <= 0 || w <= 0) return fail(ZJAI_INVALID_ARGUMENT, "synth_out_size");
+  if (kind != ZJAI_SYN_Y && kind != ZJAI_SYN_UV) return fail(ZJAI_INVALID_ARGUMENT, "not a synthesis network");
+  synth_out_size(kind, op, h, w, out_h, out_w);
+  return ZJAI_OK;
+}
+
+int zjai_synthesis_primary(zjai_net* net, const float* y_hat, int lh, int lw, int h, int w,
+                           float* out, int mem) {
+  ZJAI_TRY(net_enter(net));
+  Net* n = reinterpret_cast<Net*>(net);
+  Ctx* ctx = n->ctx;
+  if (n->kind != ZJAI_SYN_Y) return fail(ZJAI_INVALID_ARGUMENT, "not a primary synthesis network");
+  if (!y_hat || !out || lh <= 0 || lw <= 0 || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "synthesis_primary: bad arguments");
+  ArenaScope scope(ctx);
+  int oh, ow;
+  synth_out_size(ZJAI_SYN_Y, n->op, h, w, &oh, &ow);
+  const float* dy;
+  ZJAI_TRY(stage_in(ctx, y_hat, (size_t)160 * lh * lw, mem, &dy));
+  int* d_origin;
+  ZJAI_TRY(upload_ints(ctx, &ctx->arena, {0, 0}, ctx->stream, &d_origin));
+  TView y;
+  ZJAI_TRY(alloc_tensor(ctx, 1, lh, lw, 160, &y));
+  launch_gather_latent(dy, 160, lh, lw, d_origin, y, ctx->stream);
+  float* dout;
+  ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)oh * ow, mem, &dout));
+  Runner r = make_runner(ctx, n, &ctx->arena, ctx->stream, 1, nullptr);
+  FinalOut fo;
+  fo.plane0 = dout;
+  fo.row = ow;
+  fo.img = (long long)oh * ow;
+  int st = r.primary(y, h, w, fo);
+  if (st != ZJAI_OK) return settle(ctx, st);
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)oh * ow, mem));
+  return ctx_check_status(ctx);
+}
+
+int zjai_synthesis_secondary(zjai_net* net, const float* y_hat_luma, int llh, int llw,
+                             const float* y_hat_chroma, int lh, int lw, int h, int w, float* out,
+                             int mem) {
+  ZJAI_TRY(net_enter(net));
+  Net* n = reinterpret_cast<Net*>(net);
+  Ctx* ctx = n->ctx;
+  if (n->kind != ZJAI_SYN_UV) return fail(ZJAI_INVALID_ARGUMENT, "not a secondary synthesis network");
+  if (!y_hat_luma || !y_hat_chroma || !out || lh <= 0 || lw <= 0 || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "synthesis_secondary: bad arguments");
+  if (lh > llh || lw > llw)
+    return fail(ZJAI_INVALID_ARGUMENT, "chroma latent larger than the luma latent");
+  ArenaScope scope(ctx);
+  int oh, ow;
+  synth_out_size(ZJAI_SYN_UV, n->op, h, w, &oh, &ow);
+  const float *dl, *dc;
+  ZJAI_TRY(stage_in(ctx, y_hat_luma, (size_t)160 * llh * llw, mem, &dl));
+  ZJAI_TRY(stage_in(ctx, y_hat_chroma, (size_t)96 * lh * lw, mem, &dc));
+  int* d_origin;
+  ZJAI_TRY(upload_ints(ctx, &ctx->arena, {0, 0}, ctx->stream, &d_origin));
+  TView cat, x144;
+  ZJAI_TRY(alloc_tensor(ctx, 1, lh, lw, 256, &cat));
+  ZJAI_TRY(alloc_tensor(ctx, 1, lh, lw, 144, &x144));
+  launch_gather_latent(dl, 160, llh, llw, d_origin, cat.channels(0, 160), ctx->stream);
+  launch_gather_latent(dc, 96, lh, lw, d_origin, cat.channels(160, 96), ctx->stream);
+  launch_gather_latent(dc, 96, lh, lw, d_origin, x144.channels(48, 96), ctx->stream);
+  float* dout;
+  ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)2 * oh * ow, mem, &dout));
+  Runner r = make_runner(ctx, n, &ctx->arena, ctx->stream, 1, nullptr);
+  FinalOut fo;
+  fo.plane0 = dout;
+  fo.plane_stride = (long long)oh * ow;
+  fo.row = ow;
+  fo.img = 2LL * oh * ow;
+  int st = r.secondary(cat, x144, h, w, fo);
+  if (st != ZJAI_OK) return settle(ctx, st);
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)2 * oh * ow, mem));
+  return ctx_check_status(ctx);
+}
+
+static int analysis_entry(zjai_net* net, int kind, int cin, int cout, int down, const float* x,
+                          int h, int w, float* out, int mem) {
+  ZJAI_TRY(net_enter(net));
+  Net* n = reinterpret_cast<Net*>(net);
+  Ctx* ctx = n->ctx;
+  if (n->kind != kind) return fail(ZJAI_INVALID_ARGUMENT, "wrong analysis network kind");
+  if (!x || !out || h <= 0 || w <= 0) return fail(ZJAI_INVALID_ARGUMENT, "analysis: bad arguments");
+  ArenaScope scope(ctx);
+  const float* dx;
+  ZJAI_TRY(stage_in(ctx, x, (size_t)cin * h * w, mem, &dx));
+  TView t;
+  ZJAI_TRY(alloc_tensor(ctx, 1, 2 * cdiv(h, 2), 2 * cdiv(w, 2), cin, &t, true));
+  launch_normalize_pad(dx, cin, h, w, t, ctx->stream);
+  const size_t nout = (size_t)cout * cdiv(h, down) * cdiv(w, down);
+  float* dout;
+  ZJAI_TRY(stage_out_alloc(ctx, out, nout, mem, &dout));
+  Runner r = make_runner(ctx, n, &ctx->arena, ctx->stream, 1, nullptr);
+  int st = r.analysis(t, h, w, dout);
+  if (st != ZJAI_OK) return settle(ctx, st);
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, nout, mem));
+  return ctx_check_status(ctx);
+}
+
+int zjai_analysis_primary(zjai_net* net, const float* x, int h, int w, float* out, int mem) {
+  return analysis_entry(net, ZJAI_ANA_Y, 1, 160, 16, x, h, w, out, mem);
+}
+
+int zjai_analysis_secondary(zjai_net* net, const float* x, int h, int w, float* out, int mem) {
+  return analysis_entry(net, ZJAI_ANA_UV, 12, 96, 8, x, h, w, out, mem);
+}
+
+int zjai_synthesis_tiles(int height, int width, int latent_h, int latent_w, int tile_size,
+                         int overlap, zjai_tile* tiles, int max_tiles, int* count) {
+  std::vector<zjai_tile> v;
+  ZJAI_TRY(synthesis_tiles(height, width, latent_h, latent_w, tile_size, overlap, &v));
+  if (count) *count = (int)v.size();
+  for (int i = 0; i < (int)v.size() && i < max_tiles && tiles; ++i) tiles[i] = v[i];
+  return ZJAI_OK;
+}
+
+int zjai_synthesize_tiles(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const float* y_hat_y,
+                          const float* y_hat_uv, int lh, int lw, const zjai_tile* tiles,
+                          int ntiles, int out_h, int out_w, int sv, int sh, float* rec_y,
+                          float* rec_u, float* rec_v, int mem, const volatile int* cancel) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!y_hat_y || !y_hat_uv || !rec_y || !rec_u || !rec_v || (ntiles > 0 && !tiles) ||
+      lh <= 0 || lw <= 0 || out_h <= 0 || out_w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "synthesize: bad arguments");
+  if (sv <= 0 || sh <= 0) return fail(ZJAI_INVALID_DATA, "chroma subsampling factor");
+  ArenaScope scope(ctx);
+  const size_t m2 = ctx->arena2.mark();
+  struct Rel {
+    Arena* a;
+    size_t m;
+    ~Rel() { a->release(m); }
+  } rel{&ctx->arena2, m2};
+  const float *dy, *duv;
+  ZJAI_TRY(stage_in(ctx, y_hat_y, (size_t)160 * lh * lw, mem, &dy));
+  ZJAI_TRY(stage_in(ctx, y_hat_uv, (size_t)96 * lh * lw, mem, &duv));
+  const int ch = cdiv(out_h, sv), cw = cdiv(out_w, sh);
+  const size_t ny = (size_t)out_h * out_w, nc = (size_t)ch * cw;
+  float *oy = rec_y, *ou = rec_u, *ov = rec_v;
+  if (mem == ZJAI_MEM_HOST) {
+    oy = static_cast<float*>(ctx->arena.alloc((ny + 2 * nc) * sizeof(float)));
+    if (!oy) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (output planes)");
+    ou = oy + ny;
+    ov = ou + nc;
+    ZJAI_TRY(cuda_check(cudaMemsetAsync(oy, 0, (ny + 2 * nc) * sizeof(float), ctx->stream), "memset"));
+  }
+  std::vector<zjai_tile> tv(tiles, tiles + ntiles);
+  int st = synthesize_tiles_dev(ctx, reinterpret_cast<Net*>(net_y), reinterpret_cast<Net*>(net_uv),
+                                dy, duv, lh, lw, tv, out_h, out_w, sv, sh, oy, ou, ov, cancel,
+                                nullptr);
+  if (st != ZJAI_OK) return settle(ctx, st);
+  if (mem == ZJAI_MEM_HOST) {
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_y, oy, ny * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_u, ou, nc * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_v, ov, nc * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
+  }
+  return ctx_check_status(ctx);
+}
+
+int zjai_synthesize(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const float* y_hat_y,
+                    const float* y_hat_uv, int lh, int lw, int height, int width, int out_h,
+                    int out_w, int tile_size, int overlap, int sv, int sh, float* rec_y,
+                    float* rec_u, float* rec_v, int mem, const volatile int* cancel) {
+  std::vector<zjai_tile> v;
+  ZJAI_TRY(synthesis_tiles(height, width, lh, lw, tile_size, overlap, &v));
+  return zjai_synthesize_tiles(ctx, net_y, net_uv, y_hat_y, y_hat_uv, lh, lw, v.data(),
+                               (int)v.size(), out_h, out_w, sv, sh, rec_y, rec_u, rec_v, mem,
+                               cancel);
+}
+
+// ---- attention-block layer entries ---------------------------------------------------------
+
+int zjai_layer_norm(zjai_ctx* ctx, const float* x, int c, int h, int w, const float* weight,
+                    const float* bias, float* out, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!x || !weight || !bias || !out || c <= 0 || c > 512 || c % 8 || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "layer norm: parameter length");
+  ArenaScope scope(ctx);
+  const float *dx, *dw, *db;
+  ZJAI_TRY(stage_in(ctx, x, (size_t)c * h * w, mem, &dx));
+  ZJAI_TRY(stage_in(ctx, weight, (size_t)c, mem, &dw));
+  ZJAI_TRY(stage_in(ctx, bias, (size_t)c, mem, &db));
+  TView t, o;
+  ZJAI_TRY(planar_to_tensor(ctx, dx, c, h, w, &t));
+  ZJAI_TRY(alloc_tensor(ctx, 1, h, w, c, &o));
+  launch_layer_norm(t, o, dw, db, ctx->stream);
+  float* dout;
+  ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)c * h * w, mem, &dout));
+  launch_nhwc_to_planar(o, dout, ctx->stream);
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)c * h * w, mem));
+  return ctx_check_status(ctx);
+}
+
+int zjai_channel_attention(zjai_ctx* ctx, const float* qkv, int c3, int h, int w, int heads,
+                           const float* temperature, float* out, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!qkv || !temperature || !out || heads <= 0 || c3 % (3 * heads) || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "attention: channel / head counts");
+  const int dim = c3 / 3, c = dim / heads;
+  if (dim % 8 || c % 8 || c > 64 || 2 * dim > 256)
+    return fail(ZJAI_UNSUPPORTED, "attention: head sizes must be multiples of 8, at most 64");
+  ArenaScope scope(ctx);
+  const float *dq, *dt;
+  ZJAI_TRY(stage_in(ctx, qkv, (size_t)c3 * h * w, mem, &dq));
+  ZJAI_TRY(stage_in(ctx, temperature, (size_t)heads, mem, &dt));
+  TView t, o;
+  ZJAI_TRY(planar_to_tensor(ctx, dq, c3, h, w, &t));
+  ZJAI_TRY(alloc_tensor(ctx, 1, h, w, dim, &o));
+  float* scratch =
+      static_cast<float*>(ctx->arena.alloc(attention_scratch_floats(1, dim, heads) * sizeof(float)));
+  if (!scratch) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (attention)");
+  launch_attention(t, o, heads, dt, scratch, ctx->stream);
+  float* dout;
+  ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)dim * h * w, mem, &dout));
+  launch_nhwc_to_planar(o, dout, ctx->stream);
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)dim * h * w, mem));
+  return ctx_check_status(ctx);
+}
+
+int zjai_depthwise3x3(zjai_ctx* ctx, const float* x, int c, int h, int w, const float* weight,
+                      float* out, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!x || !weight || !out || c <= 0 || c % 8 || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "depthwise: bad arguments (channels must be a multiple of 8)");
+  ArenaScope scope(ctx);
+  const float *dx, *dw;
+  ZJAI_TRY(stage_in(ctx, x, (size_t)c * h * w, mem, &dx));
+  ZJAI_TRY(stage_in(ctx, weight, (size_t)c * 9, mem, &dw));
+  TView t, o;
+  ZJAI_TRY(planar_to_tensor(ctx, dx, c, h, w, &t));
+  ZJAI_TRY(alloc_tensor(ctx, 1, h, w, c, &o));
+  launch_dw3x3(t, o, dw, false, ctx->stream);
+  float* dout;
+  ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)c * h * w, mem, &dout));
+  launch_nhwc_to_planar(o, dout, ctx->stream);
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)c * h * w, mem));
+  return ctx_check_status(ctx);
+}
+
+}  // extern "C"

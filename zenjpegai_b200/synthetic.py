@@ -66,29 +66,42 @@ def laplace_latent(seed, name, shape, scale, zero_p=0.442):
 
 
 # ---------------------------------------------------------------------------------------------
-# parameter specs: list of (name, shape, kind, fan_in)
+# parameter specs: list of (name, shape, kind, effective fan_in = fan_in / gain^2)
+#
+# Plain He-normal everywhere (std sqrt(2 / fan_in)) makes the ResAU gates x * (1 + m)
+# compound: HOP activations then pass 1e5 (beyond the f16 range) and 99.9% of the output
+# samples clamp to 0 or 255, which leaves nothing for the 8-bit comparison to check. The
+# weights are therefore normal with std gain * sqrt(1 / fan_in), the gain set by the layer's
+# role: He (sqrt 2) before a ReLU/ReLU6, 1 for linear layers, a small gain on the ResAU mask
+# conv (the gate stays near 1 + small) and on the residual branch, and an output gain that
+# keeps the decoded samples mostly inside [0, 255].
 # ---------------------------------------------------------------------------------------------
+HE = 2.0 ** 0.5
+MASK_GAIN = 0.1
+RES_GAIN = 0.5
+OUT_GAIN = 0.25
 
-def _conv(specs, prefix, cin, cout, kh, kw, groups=1, bias=True):
-    specs.append((prefix + ".weight", (cout, cin // groups, kh, kw), "w", cin // groups * kh * kw))
+def _conv(specs, prefix, cin, cout, kh, kw, groups=1, bias=True, gain=1.0):
+    specs.append((prefix + ".weight", (cout, cin // groups, kh, kw), "w",
+                   cin // groups * kh * kw / gain ** 2))
     if bias:
         specs.append((prefix + ".bias", (cout,), "b", 0))
 
 
-def _convt(specs, prefix, cin, cout, k):
+def _convt(specs, prefix, cin, cout, k, gain=1.0):
     # stride-2 transposed conv: about k*k/4 taps reach each output
-    specs.append((prefix + ".weight", (cin, cout, k, k), "w", max(1, cin * k * k // 4)))
+    specs.append((prefix + ".weight", (cin, cout, k, k), "w", max(1, cin * k * k // 4) / gain ** 2))
     specs.append((prefix + ".bias", (cout,), "b", 0))
 
 
 def _resau(specs, prefix, c, per_group):
-    _conv(specs, prefix + ".conv", c, c, 3, 3, groups=c // per_group, bias=False)
-    _conv(specs, prefix + ".conv2", c, c, 1, 1, bias=False)
+    _conv(specs, prefix + ".conv", c, c, 3, 3, groups=c // per_group, bias=False, gain=HE)
+    _conv(specs, prefix + ".conv2", c, c, 1, 1, bias=False, gain=MASK_GAIN)
 
 
 def _rb(specs, prefix, c):
-    _conv(specs, prefix + ".conv1", c, c, 3, 3)
-    _conv(specs, prefix + ".conv2", c, c, 3, 3)
+    _conv(specs, prefix + ".conv1", c, c, 3, 3, gain=HE)
+    _conv(specs, prefix + ".conv2", c, c, 3, 3, gain=RES_GAIN)
 
 
 def _cab(specs, prefix, c):
@@ -146,7 +159,7 @@ def synthesis_primary_spec(op):
         _conv(s, "conv3_t", c, 4 * c, 1, 1)
         _tam(s, "TAM", c, True)
         _resau(s, "iact3", c, c // 4)
-        _convt(s, "conv4_t", c, 1, 3)
+        _convt(s, "conv4_t", c, 1, 3, gain=OUT_GAIN)
         return s
     c1, c2, c3 = (64, 32, 32) if op == "sop" else (64, 64, 96)
     _conv(s, "first_stage.0.0.conv1", 160, 160, 3, 3)
@@ -156,7 +169,7 @@ def synthesis_primary_spec(op):
     _resau(s, "iact2", c2, 16)
     _conv(s, "conv3", c2, c3, 3, 3)
     _resau(s, "iact3", c3, 16)
-    _conv(s, "conv4", c3, 16, 1, 1, bias=False)
+    _conv(s, "conv4", c3, 16, 1, 1, bias=False, gain=OUT_GAIN)
     return s
 
 
@@ -172,14 +185,14 @@ def synthesis_secondary_spec(op):
         _conv(s, "conv3_t", c, 4 * c, 1, 1)
         _tam(s, "TAM", c, False)
         _resau(s, "iact3", c, c // 4)
-        _convt(s, "conv4_t", c, 8, 3)
+        _convt(s, "conv4_t", c, 8, 3, gain=OUT_GAIN)
         return s
     c2, c3 = (32, 32) if op == "sop" else (64, 128)
     _upsample(s, op, "conv2_t", 144, c2)
     _resau(s, "iact2", c2, 16)
     _conv(s, "conv3", c2, c3, 3, 3)
     _resau(s, "iact3", c3, 16)
-    _conv(s, "conv4", c3, 128, 1, 1, bias=False)
+    _conv(s, "conv4", c3, 128, 1, 1, bias=False, gain=OUT_GAIN)
     return s
 
 
@@ -207,13 +220,13 @@ def analysis_spec(op, secondary):
 
 
 def make_params(spec, seed, tag=""):
-    """He-normal weights (std sqrt(2 / fan_in)), N(0, 0.01^2) biases, LN weight 1 + N(0, 0.1^2)
-    and bias N(0, 0.05^2), attention temperature U(0.5, 2)."""
+    """Normal weights (std sqrt(1 / effective fan_in), see the gains above), N(0, 0.01^2)
+    biases, LN weight 1 + N(0, 0.1^2) and bias N(0, 0.05^2), temperature U(0.5, 2)."""
     out = {}
     for name, shape, kind, fan_in in spec:
         key = tag + name
         if kind == "w":
-            out[name] = normal(seed, key, shape, std=float(np.sqrt(2.0 / fan_in)))
+            out[name] = normal(seed, key, shape, std=float(np.sqrt(1.0 / fan_in)))
         elif kind == "b":
             out[name] = normal(seed, key, shape, std=0.01)
         elif kind == "lnw":
