@@ -90,6 +90,15 @@ int zjai_ctx_sync(zjai_ctx *ctx);
 /* Number of kernels this context has launched since creation (for launch accounting). */
 int64_t zjai_ctx_launch_count(const zjai_ctx *ctx);
 
+/* Kernel timing, the GPU counterpart of the crate's `DecodeStats` probe
+ * (src/decoder/stats.rs:1-40): while enabled, every convolution launch is bracketed by two
+ * CUDA events on its stream. zjai_ctx_profile_read waits for the context's streams and
+ * returns the summed device time (ms), the algorithmic FLOPs (live MACs x 2) and the number
+ * of convolution launches recorded since the previous read. */
+int zjai_ctx_profile(zjai_ctx *ctx, int enable);
+int zjai_ctx_profile_read(zjai_ctx *ctx, double *conv_ms, double *conv_flops,
+                          int64_t *conv_launches);
+
 /* ---------------------------------------------------------------------------------------- */
 /* Networks (model load + GPU-resident packed weights)                                        */
 /* ---------------------------------------------------------------------------------------- */

@@ -73,6 +73,10 @@ def lib():
     L.zjai_ctx_sync.argtypes = [_vp]
     L.zjai_ctx_launch_count.argtypes = [_vp]
     L.zjai_ctx_launch_count.restype = ctypes.c_int64
+    L.zjai_ctx_profile.argtypes = [_vp, _i]
+    L.zjai_ctx_profile_read.argtypes = [_vp, ctypes.POINTER(ctypes.c_double),
+                                        ctypes.POINTER(ctypes.c_double),
+                                        ctypes.POINTER(ctypes.c_int64)]
     L.zjai_net_create.argtypes = [_vp, _i, _i, ctypes.POINTER(Param), _i, ctypes.POINTER(_vp)]
     L.zjai_net_destroy.argtypes = [_vp]
     L.zjai_synth_out_size.argtypes = [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]
@@ -81,7 +85,9 @@ def lib():
     L.zjai_analysis_primary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
     L.zjai_analysis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
     L.zjai_synthesis_tiles.argtypes = [_i] * 6 + [ctypes.POINTER(Tile), _i, ctypes.POINTER(_i)]
-    L.zjai_synthesize.argtypes = [_vp, _vp, _vp, _vp, _vp] + [_i] * 11 + [_vp, _vp, _vp, _i, _vp]
+    L.zjai_synthesize.argtypes = [_vp, _vp, _vp, _vp, _vp] + [_i] * 10 + [_vp, _vp, _vp, _i, _vp]
+    L.zjai_synthesize_tiles.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.POINTER(Tile),
+                                        _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp]
     L.zjai_quantize_plane.argtypes = [_vp, _vp, ctypes.c_int64, _i, _vp, _i]
     L.zjai_yuv_to_rgb.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i]
     L.zjai_conv2d.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i,

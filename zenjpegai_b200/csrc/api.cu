@@ -30,6 +30,13 @@ int ctx_check_status(Ctx* ctx) {
   return ZJAI_OK;
 }
 
+// End of an entry point: host-memory calls are synchronous (wait, then report the kernels'
+// status word); device-memory calls return once their work is enqueued on the stream.
+int finish_call(Ctx* ctx, int mem) {
+  if (mem == ZJAI_MEM_DEVICE) return cuda_check(cudaGetLastError(), "launch");
+  return ctx_check_status(ctx);
+}
+
 // Device copy of a caller tensor (host or device) as f32; returns a device pointer.
 int stage_in(Ctx* ctx, const float* p, size_t n, int mem, const float** out) {
   if (mem == ZJAI_MEM_DEVICE) {
@@ -167,6 +174,33 @@ int zjai_ctx_sync(zjai_ctx* ctx) {
 }
 
 int64_t zjai_ctx_launch_count(const zjai_ctx* ctx) { return ctx ? (int64_t)ctx->launches : 0; }
+
+int zjai_ctx_profile(zjai_ctx* ctx, int enable) {
+  ZJAI_TRY(ctx_enter(ctx));
+  ctx->profiling = enable != 0;
+  return ZJAI_OK;
+}
+
+int zjai_ctx_profile_read(zjai_ctx* ctx, double* conv_ms, double* conv_flops,
+                          int64_t* conv_launches) {
+  ZJAI_TRY(ctx_enter(ctx));
+  ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "stream sync"));
+  ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream2), "stream sync"));
+  double ms = 0.0, fl = 0.0;
+  for (auto& r : ctx->conv_records) {
+    float t = 0.f;
+    ZJAI_TRY(cuda_check(cudaEventElapsedTime(&t, r.start, r.stop), "event time"));
+    ms += t;
+    fl += r.flops;
+    ctx->ev_pool.push_back(r.start);
+    ctx->ev_pool.push_back(r.stop);
+  }
+  if (conv_launches) *conv_launches = (int64_t)ctx->conv_records.size();
+  ctx->conv_records.clear();
+  if (conv_ms) *conv_ms = ms;
+  if (conv_flops) *conv_flops = fl;
+  return ZJAI_OK;
+}
 
 int zjai_conv2d(zjai_ctx* ctx, const float* x, int c, int h, int w, const float* weight,
                 const float* bias, int oc, int kh, int kw, int stride, int pad_h, int pad_w,

@@ -11,6 +11,7 @@ namespace zjai {
 const char* last_error_cstr();
 int ctx_enter(zjai_ctx* ctx);
 int ctx_check_status(Ctx* ctx);
+int finish_call(Ctx* ctx, int mem);
 int stage_in(Ctx* ctx, const float* p, size_t n, int mem, const float** out);
 int stage_out_alloc(Ctx* ctx, float* p, size_t n, int mem, float** dev);
 int stage_out_finish(Ctx* ctx, float* host, const float* dev, size_t n, int mem);

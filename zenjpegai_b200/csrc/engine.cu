@@ -29,6 +29,17 @@ int cuda_check(cudaError_t e, const char* what) {
   return fail(ZJAI_DEVICE, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+cudaEvent_t Ctx::take_event() {
+  if (!ev_pool.empty()) {
+    cudaEvent_t e = ev_pool.back();
+    ev_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
 // ---- arena --------------------------------------------------------------------------------
 void* Arena::alloc(size_t bytes) {
   size_t start = (top + 255) & ~size_t(255);
@@ -302,6 +313,21 @@ void ConvLayer::out_size(int h, int w, int* oh, int* ow, int* out_h, int* out_w)
 }
 
 // ---- launch ---------------------------------------------------------------------------------
+// Launch `f` on ctx->stream; when profiling, bracket it with events and record its FLOPs.
+template <class F>
+static void timed_launch(Ctx* ctx, double flops, F&& f) {
+  ctx->launches++;
+  if (!ctx->profiling) {
+    f();
+    return;
+  }
+  Ctx::ConvRecord r{ctx->take_event(), ctx->take_event(), flops};
+  cudaEventRecord(r.start, ctx->stream);
+  f();
+  cudaEventRecord(r.stop, ctx->stream);
+  ctx->conv_records.push_back(r);
+}
+
 static void pick_tile(int oh, int ow, int* bw, int* bh) {
   long long best = -1;
   int bbw = 16;
@@ -421,8 +447,8 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     ZJAI_TRY(make_act_map(ctx, &tmA, in, L.kc, a.bw, a.bh));
     a.n_img = in.n;
     a.num_tiles = a.tiles_x * a.tiles_y * a.n_img * a.n_tiles;
-    launch_conv(tmA, tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
-    ctx->launches++;
+    const double fl = (double)L.flops_per_px * oh * ow * in.n;
+    timed_launch(ctx, fl, [&] { launch_conv(tmA, tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream); });
   } else {
     // The parity-split 5-D view has no batch axis: one launch per picture.
     for (int i = 0; i < in.n; ++i) {
@@ -437,8 +463,8 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
       if (ai.out2) ai.out2 += i * a.o2_img;
       if (ai.pout && !ai.img_win) ai.pout += i * a.p_img;
       if (ai.img_win) ai.img_win += 6 * i;
-      launch_conv(tmA, tmB, ai, std::min(ai.num_tiles, ctx->sms), ctx->stream);
-      ctx->launches++;
+      const double fl = (double)L.flops_per_px * oh * ow;
+      timed_launch(ctx, fl, [&] { launch_conv(tmA, tmB, ai, std::min(ai.num_tiles, ctx->sms), ctx->stream); });
     }
   }
   return cuda_check(cudaGetLastError(), "conv launch");

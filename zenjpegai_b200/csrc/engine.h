@@ -71,6 +71,16 @@ struct Ctx {
   // driver entry point
   void* encode_fn = nullptr;
   int driver_version = 0;
+  // kernel timing (the crate's DecodeStats probe, per conv launch): when `profiling`, every
+  // conv launch is bracketed by two events and its algorithmic FLOPs are recorded
+  bool profiling = false;
+  std::vector<cudaEvent_t> ev_pool;
+  struct ConvRecord {
+    cudaEvent_t start, stop;
+    double flops;
+  };
+  std::vector<ConvRecord> conv_records;
+  cudaEvent_t take_event();
 };
 
 // Allocate an NHWC f16 tensor in the arena; channels padded to `cpad` (multiple of 8), and

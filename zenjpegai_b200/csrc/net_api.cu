@@ -198,7 +198,7 @@ int zjai_synthesis_primary(zjai_net* net, const float* y_hat, int lh, int lw, in
   int st = r.primary(y, h, w, fo);
   if (st != ZJAI_OK) return settle(ctx, st);
   ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)oh * ow, mem));
-  return ctx_check_status(ctx);
+  return finish_call(ctx, mem);
 }
 
 int zjai_synthesis_secondary(zjai_net* net, const float* y_hat_luma, int llh, int llw,
@@ -237,7 +237,7 @@ int zjai_synthesis_secondary(zjai_net* net, const float* y_hat_luma, int llh, in
   int st = r.secondary(cat, x144, h, w, fo);
   if (st != ZJAI_OK) return settle(ctx, st);
   ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)2 * oh * ow, mem));
-  return ctx_check_status(ctx);
+  return finish_call(ctx, mem);
 }
 
 static int analysis_entry(zjai_net* net, int kind, int cin, int cout, int down, const float* x,
@@ -260,7 +260,7 @@ static int analysis_entry(zjai_net* net, int kind, int cin, int cout, int down, 
   int st = r.analysis(t, h, w, dout);
   if (st != ZJAI_OK) return settle(ctx, st);
   ZJAI_TRY(stage_out_finish(ctx, out, dout, nout, mem));
-  return ctx_check_status(ctx);
+  return finish_call(ctx, mem);
 }
 
 int zjai_analysis_primary(zjai_net* net, const float* x, int h, int w, float* out, int mem) {
@@ -319,7 +319,7 @@ int zjai_synthesize_tiles(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, cons
     ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_u, ou, nc * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
     ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_v, ov, nc * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
   }
-  return ctx_check_status(ctx);
+  return finish_call(ctx, mem);
 }
 
 int zjai_synthesize(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const float* y_hat_y,
@@ -353,7 +353,7 @@ int zjai_layer_norm(zjai_ctx* ctx, const float* x, int c, int h, int w, const fl
   ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)c * h * w, mem, &dout));
   launch_nhwc_to_planar(o, dout, ctx->stream);
   ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)c * h * w, mem));
-  return ctx_check_status(ctx);
+  return finish_call(ctx, mem);
 }
 
 int zjai_channel_attention(zjai_ctx* ctx, const float* qkv, int c3, int h, int w, int heads,
@@ -379,7 +379,7 @@ int zjai_channel_attention(zjai_ctx* ctx, const float* qkv, int c3, int h, int w
   ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)dim * h * w, mem, &dout));
   launch_nhwc_to_planar(o, dout, ctx->stream);
   ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)dim * h * w, mem));
-  return ctx_check_status(ctx);
+  return finish_call(ctx, mem);
 }
 
 int zjai_depthwise3x3(zjai_ctx* ctx, const float* x, int c, int h, int w, const float* weight,
@@ -399,7 +399,7 @@ int zjai_depthwise3x3(zjai_ctx* ctx, const float* x, int c, int h, int w, const 
   ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)c * h * w, mem, &dout));
   launch_nhwc_to_planar(o, dout, ctx->stream);
   ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)c * h * w, mem));
-  return ctx_check_status(ctx);
+  return finish_call(ctx, mem);
 }
 
 }  // extern "C"

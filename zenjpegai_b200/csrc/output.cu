@@ -179,7 +179,7 @@ int zjai_quantize_plane(zjai_ctx* ctx, const float* x, int64_t n, int bit_depth,
   ZJAI_TRY(output_quantize(ctx, dx, n, bit_depth, dout, ctx->stream));
   if (mem == ZJAI_MEM_HOST)
     ZJAI_TRY(cuda_check(cudaMemcpyAsync(out, dout, ob, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
-  return ctx_check_status(ctx);
+  return finish_call(ctx, mem);
 }
 
 int zjai_yuv_to_rgb(zjai_ctx* ctx, const float* y, const float* u, const float* v, int h, int w,
@@ -200,7 +200,7 @@ int zjai_yuv_to_rgb(zjai_ctx* ctx, const float* y, const float* u, const float* 
   ZJAI_TRY(output_yuv_to_rgb(ctx, dy, du, dv, h, w, ch, cw, bit_depth, dout, ctx->stream));
   if (mem == ZJAI_MEM_HOST)
     ZJAI_TRY(cuda_check(cudaMemcpyAsync(rgb, dout, ob, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
-  return ctx_check_status(ctx);
+  return finish_call(ctx, mem);
 }
 
 }  // extern "C"

@@ -1,0 +1,174 @@
+"""Decoder / Encoder front ends of the GPU path, mirroring the crate's public API for the part
+of the pipeline this engine replaces.
+
+`Decoder` stands in for `zenjpegai::Decoder` (src/decoder/api.rs:38-458) from the point where the
+entropy stage has produced the latents: `synthesize` is `synthesize_with`
+(src/decoder/reconstruct.rs:274-331), `finish_yuv` / `finish_rgb` are the output stage
+(src/decoder/output.rs). Entropy decoding stays on the host and is not part of this package.
+`Encoder.analyze` stands in for the analysis transforms the crate's `Encoder` runs
+(src/model/analysis.rs) on pre-processed planes.
+
+Arrays are numpy float32 (host) or torch CUDA tensors (device), as in the package root.
+"""
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import ZjaiError, check
+from . import Engine, Network, SYN_Y, SYN_UV, ANA_Y, ANA_UV, synthesis_tiles, _arg
+
+OPS = {"sop": _lib.SOP, "bop": _lib.BOP, "hop": _lib.HOP}
+
+
+def _op(op):
+    return OPS[op] if isinstance(op, str) else int(op)
+
+
+def _cdiv(a, b):
+    return -(-a // b)
+
+
+class Decoder:
+    """Synthesis networks of one operating point, loaded once (the crate's model cache,
+    api.rs:135-157) and reused for every picture."""
+
+    def __init__(self, engine, op, params_y, params_uv):
+        self.engine = engine
+        self.op = _op(op)
+        self.net_y = Network(engine, SYN_Y, self.op, params_y)
+        self.net_uv = Network(engine, SYN_UV, self.op, params_uv)
+
+    def close(self):
+        self.net_y.close()
+        self.net_uv.close()
+
+    def _planes(self, like, out_h, out_w, sv, sh):
+        ch, cw = _cdiv(out_h, sv), _cdiv(out_w, sh)
+        if type(like).__module__.startswith("torch"):
+            import torch
+            z = lambda s: torch.zeros(s, dtype=torch.float32, device=like.device)
+        else:
+            z = lambda s: np.zeros(s, np.float32)
+        return z((out_h, out_w)), z((ch, cw)), z((ch, cw))
+
+    def synthesize(self, y_hat_y, y_hat_uv, height, width, out_h=None, out_w=None,
+                   tile_size=0, overlap=0, sv=2, sh=2, out=None, cancel=None):
+        """Whole picture: latents [160, lh, lw] / [96, lh, lw] -> planes (y, u, v) in [0, 255]
+        (`synthesize_with`, reconstruct.rs:274-331). `cancel` is an optional ctypes c_int
+        polled between tiles and layers (the crate's `Stop`)."""
+        out_h = height if out_h is None else out_h
+        out_w = width if out_w is None else out_w
+        _, lh, lw = y_hat_y.shape
+        ry, ru, rv = out if out is not None else self._planes(y_hat_y, out_h, out_w, sv, sh)
+        py, mem = _arg(y_hat_y, (160, lh, lw))
+        puv, _ = _arg(y_hat_uv, (96, lh, lw))
+        check(_lib.lib().zjai_synthesize(
+            self.engine.handle, self.net_y.handle, self.net_uv.handle, py, puv, lh, lw, height,
+            width, out_h, out_w, tile_size, overlap, sv, sh, _arg(ry)[0], _arg(ru)[0],
+            _arg(rv)[0], mem, ctypes.byref(cancel) if cancel is not None else None))
+        return ry, ru, rv
+
+    def synthesize_tiles(self, y_hat_y, y_hat_uv, tiles, out_h, out_w, sv=2, sh=2, out=None,
+                         cancel=None):
+        """Only the listed tiles (a shard of `synthesis_tiles`); planes outside their cores
+        are left as they are."""
+        _, lh, lw = y_hat_y.shape
+        ry, ru, rv = out if out is not None else self._planes(y_hat_y, out_h, out_w, sv, sh)
+        arr = (_lib.Tile * max(1, len(tiles)))()
+        for i, t in enumerate(tiles):
+            for k, _ in _lib.Tile._fields_:
+                setattr(arr[i], k, int(t[k]))
+        py, mem = _arg(y_hat_y, (160, lh, lw))
+        puv, _ = _arg(y_hat_uv, (96, lh, lw))
+        check(_lib.lib().zjai_synthesize_tiles(
+            self.engine.handle, self.net_y.handle, self.net_uv.handle, py, puv, lh, lw, arr,
+            len(tiles), out_h, out_w, sv, sh, _arg(ry)[0], _arg(ru)[0], _arg(rv)[0], mem,
+            ctypes.byref(cancel) if cancel is not None else None))
+        return ry, ru, rv
+
+    # ---- output stage (src/decoder/output.rs) -------------------------------------------
+    def quantize_plane(self, x, bit_depth=8, out=None):
+        """`quantize_plane_par` (output.rs:330-342); uint8 for 8-bit, else uint16."""
+        dt = np.uint8 if bit_depth == 8 else np.uint16
+        if out is None:
+            if type(x).__module__.startswith("torch"):
+                import torch
+                out = torch.empty(tuple(x.shape), dtype=torch.uint8 if bit_depth == 8
+                                  else torch.int16, device=x.device)
+            else:
+                out = np.empty(x.shape, dt)
+        px, mem = _arg(x)
+        po = ctypes.c_void_p(out.data_ptr() if hasattr(out, "data_ptr") else out.ctypes.data)
+        n = int(np.prod(tuple(x.shape)))
+        check(_lib.lib().zjai_quantize_plane(self.engine.handle, px, n, bit_depth, po, mem))
+        return out
+
+    def yuv_to_rgb(self, y, u, v, bit_depth=8, out=None):
+        """Bicubic 4:2:0 -> 4:4:4, BT.709, round half to even (output.rs:103-262, 407-438):
+        interleaved RGB [h, w, 3]."""
+        h, w = y.shape
+        ch, cw = u.shape
+        if out is None:
+            if type(y).__module__.startswith("torch"):
+                import torch
+                out = torch.empty((h, w, 3), dtype=torch.uint8 if bit_depth == 8
+                                  else torch.int16, device=y.device)
+            else:
+                out = np.empty((h, w, 3), np.uint8 if bit_depth == 8 else np.uint16)
+        py, mem = _arg(y)
+        po = ctypes.c_void_p(out.data_ptr() if hasattr(out, "data_ptr") else out.ctypes.data)
+        check(_lib.lib().zjai_yuv_to_rgb(self.engine.handle, py, _arg(u)[0], _arg(v)[0], h, w,
+                                         ch, cw, bit_depth, po, mem))
+        return out
+
+
+class Encoder:
+    """Analysis transforms (src/model/analysis.rs) of one operating point (BOP / HOP)."""
+
+    def __init__(self, engine, op, params_y, params_uv):
+        self.engine = engine
+        self.op = _op(op)
+        self.net_y = Network(engine, ANA_Y, self.op, params_y)
+        self.net_uv = Network(engine, ANA_UV, self.op, params_uv)
+
+    def analyze(self, luma, chroma12):
+        """luma [1, h, w] and chroma [12, h/2, w/2] in [0, 255] -> latents
+        ([160, ceil(h/16), ceil(w/16)], [96, ceil(h2/8), ceil(w2/8)])."""
+        _, h, w = luma.shape
+        _, h2, w2 = chroma12.shape
+        if type(luma).__module__.startswith("torch"):
+            import torch
+            ly = torch.empty((160, _cdiv(h, 16), _cdiv(w, 16)), device=luma.device)
+            luv = torch.empty((96, _cdiv(h2, 8), _cdiv(w2, 8)), device=luma.device)
+        else:
+            ly = np.empty((160, _cdiv(h, 16), _cdiv(w, 16)), np.float32)
+            luv = np.empty((96, _cdiv(h2, 8), _cdiv(w2, 8)), np.float32)
+        px, mem = _arg(luma)
+        check(_lib.lib().zjai_analysis_primary(self.net_y.handle, px, h, w, _arg(ly)[0], mem))
+        check(_lib.lib().zjai_analysis_secondary(self.net_uv.handle, _arg(chroma12)[0], h2, w2,
+                                                 _arg(luv)[0], mem))
+        return ly, luv
+
+
+def smoke_check(engine):
+    """One small SOP picture (two tiles) through the whole-picture API, checked against the
+    CPU oracle (used by `__graft_entry__.smoke`; the oracle import happens there)."""
+    import oracle as zo
+    from . import synthetic as syn
+    py, puv = syn.synthesis_params("sop", 2)
+    dec = Decoder(engine, "sop", py, puv)
+    H, W = 96, 176
+    lh, lw = _cdiv(H, 16), _cdiv(W, 16)
+    ly = syn.laplace_latent(1, "smoke/ly", (160, lh, lw), 1.5)
+    luv = syn.laplace_latent(1, "smoke/luv", (96, lh, lw), 1.5)
+    got = dec.synthesize(ly, luv, H, W, tile_size=96, overlap=16)
+    want = zo.synthesize(zo.Checkpoint(py), zo.Checkpoint(puv), zo.SOP, ly, luv, H, W,
+                         tile_size=96, overlap=16)
+    for g, w in zip(got, want):
+        mse = float(np.mean((g.astype(np.float64) - w) ** 2))
+        p = 99.0 if mse == 0 else 10 * np.log10(255.0 ** 2 / mse)
+        if p < 50.0:
+            raise ZjaiError(_lib.DEVICE, "smoke: PSNR %.1f dB against the oracle" % p)
+    dec.close()
