@@ -183,7 +183,9 @@ def main():
     lh, lw = -(-H // 16), -(-W // 16)
     ch, cw = -(-H // 2), -(-W // 2)
     eng = zj.Engine(local, arena_bytes=64 << 30)
-    stream = torch.cuda.current_stream()
+    # one non-default stream shared by torch (copies, events, NCCL) and the engine
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     eng.set_stream(stream.cuda_stream)
     py, puv = syn.synthesis_params(op, cfg["seed"])
     dec = Decoder(eng, op, py, puv)

@@ -6,12 +6,21 @@ namespace zjai {
 
 namespace {
 
-__device__ __forceinline__ float apply_act(float v, int act) {
-  switch (act) {
-    case ACT_RELU: return v > 0.f ? v : 0.f;
-    case ACT_LEAKY: return v > 0.f ? v : v * 0.01f;
-    case ACT_SIGMOID: return 1.f / (1.f + expf(-v));
-    case ACT_RELU6: return fminf(fmaxf(v, 0.f), 6.f);
+template <int ACT>
+__device__ __forceinline__ float act(float v) {
+  if constexpr (ACT == ACT_RELU) return v > 0.f ? v : 0.f;
+  if constexpr (ACT == ACT_LEAKY) return v > 0.f ? v : v * 0.01f;
+  if constexpr (ACT == ACT_SIGMOID) return 1.f / (1.f + expf(-v));
+  if constexpr (ACT == ACT_RELU6) return fminf(fmaxf(v, 0.f), 6.f);
+  return v;
+}
+
+__device__ __forceinline__ float act_rt(float v, int a) {
+  switch (a) {
+    case ACT_RELU: return act<ACT_RELU>(v);
+    case ACT_LEAKY: return act<ACT_LEAKY>(v);
+    case ACT_SIGMOID: return act<ACT_SIGMOID>(v);
+    case ACT_RELU6: return act<ACT_RELU6>(v);
     default: return v;
   }
 }
@@ -34,8 +43,7 @@ __device__ __forceinline__ TileCoord decode_tile(const ConvArgs& a, int t) {
   return c;
 }
 
-__device__ __forceinline__ void load_h8(const __half* p, float (&v)[8]) {
-  uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+__device__ __forceinline__ void unpack_h8(const uint4& u, float (&v)[8]) {
   const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -45,12 +53,151 @@ __device__ __forceinline__ void load_h8(const __half* p, float (&v)[8]) {
   }
 }
 
-__device__ __forceinline__ void store_h8(__half* p, const float (&v)[8]) {
+__device__ __forceinline__ uint4 pack_h8(const float (&v)[8]) {
   uint4 u;
   __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
   for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-  *reinterpret_cast<uint4*>(p) = u;
+  return u;
+}
+
+// Activation of an 8-vector (one uniform branch per group, not per element).
+__device__ __forceinline__ void act8(float (&x)[8], int a) {
+  switch (a) {
+    case ACT_RELU:
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = act<ACT_RELU>(x[e]);
+      break;
+    case ACT_LEAKY:
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = act<ACT_LEAKY>(x[e]);
+      break;
+    case ACT_SIGMOID:
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = act<ACT_SIGMOID>(x[e]);
+      break;
+    case ACT_RELU6:
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = act<ACT_RELU6>(x[e]);
+      break;
+    default:
+      break;
+  }
+}
+
+constexpr int kChunk = 16;  // accumulator columns per TMEM load and epilogue step
+
+// One chunk of accumulator columns [col0, col0 + 16) of this thread's pixel, NHWC f16 out.
+// Column n lands in output pixel (R*oy + dy, R*ox + dx), channel co, with (phase, co) read from
+// the shared table (phase = dy*R + dx). Each 8-column group is one 16-byte store. Residual
+// operands are loaded for both groups before any store (in-place ops read exactly the elements
+// this thread then writes).
+template <int OP>
+__device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kChunk], int col0,
+                                         int img, int oy, int ox, bool valid, const uint32_t* tab) {
+  constexpr int G = kChunk / 8;
+  int Yg[G], Xg[G], cg[G];
+  bool ok[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const uint32_t e = tab[col0 + 8 * g];
+    const int p = (int)(e >> 16);
+    cg[g] = (int)(e & 0xFFFFu);
+    Yg[g] = oy * a.R + (p >> a.lR);
+    Xg[g] = ox * a.R + (p & (a.R - 1));
+    ok[g] = valid && p < a.R * a.R && Yg[g] < a.out_h && Xg[g] < a.out_w;
+  }
+  uint4 r1[G], r2[G];
+  if constexpr (OP != OP_NONE) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      if (ok[g]) {
+        r1[g] = __ldg(reinterpret_cast<const uint4*>(a.r1 + img * a.r1_img + Yg[g] * a.r1_row +
+                                                     Xg[g] * a.r1_pix + cg[g]));
+        if constexpr (OP == OP_CAB)
+          r2[g] = __ldg(reinterpret_cast<const uint4*>(a.r2 + img * a.r2_img + Yg[g] * a.r2_row +
+                                                       Xg[g] * a.r2_pix + cg[g]));
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (!ok[g]) continue;
+    float x[8];
+    if (a.bias) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.bias + col0 + 8 * g));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.bias + col0 + 8 * g + 4));
+      x[0] = v[8 * g + 0] * a.scale + b0.x;
+      x[1] = v[8 * g + 1] * a.scale + b0.y;
+      x[2] = v[8 * g + 2] * a.scale + b0.z;
+      x[3] = v[8 * g + 3] * a.scale + b0.w;
+      x[4] = v[8 * g + 4] * a.scale + b1.x;
+      x[5] = v[8 * g + 5] * a.scale + b1.y;
+      x[6] = v[8 * g + 6] * a.scale + b1.z;
+      x[7] = v[8 * g + 7] * a.scale + b1.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = v[8 * g + e] * a.scale;
+    }
+    act8(x, a.act1);
+    if constexpr (OP != OP_NONE) {
+      float q1[8];
+      unpack_h8(r1[g], q1);
+      if constexpr (OP == OP_ADD) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = x[e] + q1[e];
+      } else if constexpr (OP == OP_GATE) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = q1[e] * (1.f + x[e]);
+      } else {
+        float q2[8];
+        unpack_h8(r2[g], q2);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = q2[e] + q1[e] * x[e];
+      }
+    }
+    act8(x, a.act2);
+    *reinterpret_cast<uint4*>(a.out + img * a.out_img + Yg[g] * a.out_row + Xg[g] * a.out_pix +
+                              cg[g]) = pack_h8(x);
+    if (a.out2) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = fminf(fmaxf(x[k], 0.f), 6.f);
+      *reinterpret_cast<uint4*>(a.out2 + img * a.o2_img + Yg[g] * a.o2_row + Xg[g] * a.o2_pix +
+                                cg[g]) = pack_h8(x);
+    }
+  }
+}
+
+// Planar f32 output (final layers and the layer entry points): one scalar per column.
+__device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[kChunk], int col0,
+                                           int img, int oy, int ox, bool valid,
+                                           const uint32_t* tab) {
+  if (!valid) return;
+  int py0 = a.py0, px0 = a.px0, cy0 = a.cy0, cy1 = a.cy1, cx0 = a.cx0, cx1 = a.cx1;
+  if (a.img_win) {
+    const int* wv = a.img_win + 6 * img;
+    py0 = wv[0];
+    px0 = wv[1];
+    cy0 = wv[2];
+    cy1 = wv[3];
+    cx0 = wv[4];
+    cx1 = wv[5];
+  }
+  for (int j = 0; j < kChunk; ++j) {
+    const uint32_t e = tab[col0 + j];
+    const int p = (int)(e >> 16), ch = (int)(e & 0xFFFFu);
+    if (p >= a.R * a.R) continue;
+    const int Y = oy * a.R + (p >> a.lR), X = ox * a.R + (p & (a.R - 1));
+    if (Y >= a.out_h || X >= a.out_w) continue;
+    const int PY = py0 + Y, PX = px0 + X;
+    if (PY < cy0 || PY >= cy1 || PX < cx0 || PX >= cx1) continue;
+    if (PY % a.sv || PX % a.sh) continue;
+    const float b = a.bias ? __ldg(a.bias + col0 + j) : 0.f;
+    float x = act_rt(v[j] * a.scale + b, a.act1);
+    if (a.denorm) x = fminf(fmaxf(x * 128.f + 127.5f, 0.f), 255.f);
+    float* dst = (ch == 1 && a.pout2) ? a.pout2 : a.pout + ch * a.p_plane;
+    dst[(a.img_win ? 0 : img * a.p_img) + (PY / a.sv) * a.p_row + PX / a.sh] = x;
+  }
 }
 
 }  // namespace
@@ -65,8 +212,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const uint32_t a_bytes = 128u * a.kc * 2u;
   const uint32_t b_bytes = (uint32_t)a.bn * a.kc * 2u;
   const uint32_t stage_bytes = conv_stage_bytes(a.kc, a.bn);
-  float* staging = reinterpret_cast<float*>(smem + S * stage_bytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * stage_bytes + kStagingBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* accf = bars + 2 * S;
@@ -74,9 +220,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint64_t* drain = bars + 2 * S + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint32_t* tab = reinterpret_cast<uint32_t*>(smem + S * stage_bytes + kBarrierBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int npad = a.n_tiles * a.bn;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -85,12 +233,15 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&accf[i]), 1);
-      mbar_init(smem_u32(&acce[i]), 128);
+      mbar_init(smem_u32(&acce[i]), kEpiThreads);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
+  // column -> (phase, channel) table of the packed column order
+  for (int n = threadIdx.x; n < npad; n += blockDim.x)
+    tab[n] = ((uint32_t)(n / a.cph) << 16) | (uint32_t)(n % a.cph);
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -113,13 +264,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       long long issued = 0;
       for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
         const TileCoord tc = decode_tile(a, t);
+        int tap = 0, cc = 0;
         for (int ks = 0; ks < ksteps; ++ks) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, a.err,
                          DEV_TIMEOUT_EMPTY))
             goto producer_done;
-          const int tap = ks / a.cchunks;
-          const int cc = ks - tap * a.cchunks;
-          const int ky = tap / a.kw, kx = tap - (tap / a.kw) * a.kw;
+          const int ky = tap / a.kw, kx = tap - ky * a.kw;
           const uint32_t sA = smem_u32(smem + stage * stage_bytes);
           const uint32_t sB = sA + a_bytes;
           const uint32_t fb = smem_u32(&full[stage]);
@@ -132,11 +282,15 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             tma_load_5d(sA, &tmA, fb, cc * a.kc, dx & 1, tc.ox0 + (dx >> 1), dy & 1,
                         tc.oy0 + (dy >> 1));
           }
-          tma_load_2d(sB, &tmB, fb, cc * a.kc, tap * (a.n_tiles * a.bn) + tc.n0);
+          tma_load_2d(sB, &tmB, fb, cc * a.kc, tap * npad + tc.n0);
           ++issued;
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
+          }
+          if (++cc == a.cchunks) {
+            cc = 0;
+            ++tap;
           }
         }
       }
@@ -196,12 +350,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       mbar_wait_drain(smem_u32(drain), 0, a.err);
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (4 warps)
-    const int q = warp & 3;                 // TMEM lane quarter of this warp
-    const int m = q * 32 + lane;            // accumulator row == pixel index in the tile
-    const int et = threadIdx.x - 64;        // 0..127
-    const int cw = (a.bn % 32) == 0 ? 32 : 16;  // columns per chunk
-    const int nchunk4 = cw / 4;             // float4 chunks per staging row
+    // ------------------------------------------------------------------ epilogue (8 warps)
+    // Two warpgroups; warp w reads TMEM lanes 32*(w%4).. (its accumulator rows = pixels),
+    // warpgroup g takes the column chunks c with c % 2 == g.
+    const int q = warp & 3;
+    const int wg = (warp - 2) >> 2;
+    const int m = q * 32 + lane;  // accumulator row == pixel index in the tile
+    const int nchunks = a.bn / kChunk;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
@@ -209,108 +364,30 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         break;
       tc_fence_after();
       const TileCoord tc = decode_tile(a, t);
-      const int nchunks = a.bn / cw;
-      for (int c = 0; c < nchunks; ++c) {
-        const int col0 = tc.n0 + c * cw;
-        float v[32];
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.bn + c * cw);
-        if (cw == 32)
-          tmem_ld32(taddr, v);
-        else
-          tmem_ld16(taddr, v);
-        if (c == nchunks - 1) {
+      const int oy = tc.oy0 + (m >> a.lbw), ox = tc.ox0 + (m & (a.bw - 1));
+      const bool valid = oy < a.oh && ox < a.ow;
+      if (wg >= nchunks) {
+        tc_fence_before();
+        mbar_arrive(smem_u32(&acce[acc]));
+      }
+      for (int c = wg; c < nchunks; c += 2) {
+        float v[kChunk];
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.bn + c * kChunk), v);
+        if (c + 2 >= nchunks) {  // this thread's last read of the accumulator
           tc_fence_before();
           mbar_arrive(smem_u32(&acce[acc]));
         }
-        // phase 1: scale, bias, activation -> staging row m (float4 chunks XOR-swizzled)
-        float4* srow = reinterpret_cast<float4*>(staging + m * 32);
-#pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          if (j4 < nchunk4) {
-            float r[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int j = j4 * 4 + e;
-              float b = a.bias ? __ldg(a.bias + col0 + j) : 0.f;
-              r[e] = apply_act(v[j] * a.scale + b, a.act1);
-            }
-            srow[j4 ^ (m & (nchunk4 - 1))] = make_float4(r[0], r[1], r[2], r[3]);
-          }
-        }
-        named_bar_sync(1, 128);
-        // phase 2: output-space pass
-        if (!a.planar) {
-          const int groups = cw / 8;
-          for (int it = et; it < 128 * groups; it += 128) {
-            const int pm = it / groups, g = it - (it / groups) * groups;
-            const int oy = tc.oy0 + pm / a.bw, ox = tc.ox0 + pm % a.bw;
-            if (oy >= a.oh || ox >= a.ow) continue;
-            const int n = col0 + 8 * g;
-            const int p = n / a.cph, co = n - (n / a.cph) * a.cph;
-            if (p >= a.R * a.R) continue;
-            const int Y = oy * a.R + p / a.R, X = ox * a.R + p % a.R;
-            if (Y >= a.out_h || X >= a.out_w) continue;
-            const float4* rrow = reinterpret_cast<const float4*>(staging + pm * 32);
-            const float4 lo = rrow[(2 * g) ^ (pm & (nchunk4 - 1))];
-            const float4 hi = rrow[(2 * g + 1) ^ (pm & (nchunk4 - 1))];
-            float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-            if (a.op != OP_NONE) {
-              float r1[8];
-              load_h8(a.r1 + tc.img * a.r1_img + Y * a.r1_row + X * a.r1_pix + co, r1);
-              if (a.op == OP_ADD) {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) x[e] = x[e] + r1[e];
-              } else if (a.op == OP_GATE) {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) x[e] = r1[e] * (1.f + x[e]);
-              } else {
-                float r2[8];
-                load_h8(a.r2 + tc.img * a.r2_img + Y * a.r2_row + X * a.r2_pix + co, r2);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) x[e] = r2[e] + r1[e] * x[e];
-              }
-            }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[e] = apply_act(x[e], a.act2);
-            store_h8(a.out + tc.img * a.out_img + Y * a.out_row + X * a.out_pix + co, x);
-            if (a.out2) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) x[e] = fminf(fmaxf(x[e], 0.f), 6.f);
-              store_h8(a.out2 + tc.img * a.o2_img + Y * a.o2_row + X * a.o2_pix + co, x);
-            }
-          }
+        const int col0 = tc.n0 + c * kChunk;
+        if (a.planar) {
+          epi_planar(a, v, col0, tc.img, oy, ox, valid, tab);
         } else {
-          int py0 = a.py0, px0 = a.px0, cy0 = a.cy0, cy1 = a.cy1, cx0 = a.cx0, cx1 = a.cx1;
-          if (a.img_win) {
-            const int* wv = a.img_win + 6 * tc.img;
-            py0 = wv[0];
-            px0 = wv[1];
-            cy0 = wv[2];
-            cy1 = wv[3];
-            cx0 = wv[4];
-            cx1 = wv[5];
-          }
-          for (int it = et; it < 128 * cw; it += 128) {
-            const int pm = it / cw, j = it - (it / cw) * cw;
-            const int oy = tc.oy0 + pm / a.bw, ox = tc.ox0 + pm % a.bw;
-            if (oy >= a.oh || ox >= a.ow) continue;
-            const int n = col0 + j;
-            const int p = n / a.cph, ch = n - (n / a.cph) * a.cph;
-            if (p >= a.R * a.R) continue;
-            const int Y = oy * a.R + p / a.R, X = ox * a.R + p % a.R;
-            if (Y >= a.out_h || X >= a.out_w) continue;
-            const int PY = py0 + Y, PX = px0 + X;
-            if (PY < cy0 || PY >= cy1 || PX < cx0 || PX >= cx1) continue;
-            if (PY % a.sv || PX % a.sh) continue;
-            const float4* rrow = reinterpret_cast<const float4*>(staging + pm * 32);
-            const float4 f4 = rrow[(j >> 2) ^ (pm & (nchunk4 - 1))];
-            float x = (j & 3) == 0 ? f4.x : (j & 3) == 1 ? f4.y : (j & 3) == 2 ? f4.z : f4.w;
-            if (a.denorm) x = fminf(fmaxf(x * 128.f + 127.5f, 0.f), 255.f);
-            float* dst = (ch == 1 && a.pout2) ? a.pout2 : a.pout + ch * a.p_plane;
-            dst[(a.img_win ? 0 : tc.img * a.p_img) + (PY / a.sv) * a.p_row + PX / a.sh] = x;
+          switch (a.op) {
+            case OP_ADD: epi_nhwc<OP_ADD>(a, v, col0, tc.img, oy, ox, valid, tab); break;
+            case OP_GATE: epi_nhwc<OP_GATE>(a, v, col0, tc.img, oy, ox, valid, tab); break;
+            case OP_CAB: epi_nhwc<OP_CAB>(a, v, col0, tc.img, oy, ox, valid, tab); break;
+            default: epi_nhwc<OP_NONE>(a, v, col0, tc.img, oy, ox, valid, tab); break;
           }
         }
-        named_bar_sync(1, 128);
       }
       if (++acc == 2) {
         acc = 0;
@@ -329,7 +406,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 
 void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmB, const ConvArgs& a, int grid,
                  cudaStream_t stream) {
-  const uint32_t smem = conv_smem_bytes(a.kc, a.bn, a.stages);
+  const uint32_t smem = conv_smem_bytes(a.kc, a.bn, a.stages, a.n_tiles * a.bn);
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);

@@ -39,7 +39,8 @@ struct ConvArgs {
   const float* bias;   // [n_tiles * bn] in packed column order, or null
   float scale;         // weight unscale (power of two)
   int act1, op, act2;
-  int R, cph;          // pixel-shuffle factor and channels per phase
+  int R, cph;          // pixel-shuffle factor (power of two) and channels per phase
+  int lR, lbw;         // log2(R), log2(bw)
   // NHWC f16 output
   __half* out;
   long long out_pix, out_row, out_img;
@@ -62,16 +63,17 @@ struct ConvArgs {
   int* err;
 };
 
-constexpr int kConvThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
-constexpr int kStagingBytes = 128 * 32 * 4;
+constexpr int kConvThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiThreads = 256;
+constexpr int kBarrierBytes = 256;
 
 __host__ __device__ inline uint32_t conv_stage_bytes(int kc, int bn) {
   uint32_t b = 128u * kc * 2u + (uint32_t)bn * kc * 2u;
   return (b + 1023u) & ~1023u;
 }
-__host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int stages) {
-  // 1 KB alignment slack + stages + staging + barriers/slots
-  return 1024u + stages * conv_stage_bytes(kc, bn) + kStagingBytes + 256u;
+// 1 KB alignment slack + stages + barriers/slots + the column table (4 bytes per column)
+__host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int stages, int npad) {
+  return 1024u + stages * conv_stage_bytes(kc, bn) + kBarrierBytes + 4u * (uint32_t)npad;
 }
 
 void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmB, const ConvArgs& a, int grid,

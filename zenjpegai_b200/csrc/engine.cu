@@ -378,7 +378,10 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   a.kc = L.kc;
   a.bn = L.bn;
   const uint32_t stage = conv_stage_bytes(L.kc, L.bn);
-  a.stages = (int)std::min<uint32_t>(8, (232448u - 1024u - kStagingBytes - 256u) / stage);
+  const uint32_t fixed = 1024u + kBarrierBytes + 4u * (uint32_t)L.npad;
+  if (fixed + 2 * stage > 232448u)
+    return fail(ZJAI_UNSUPPORTED, "conv: too many output columns for one launch");
+  a.stages = (int)std::min<uint32_t>(8, (232448u - fixed) / stage);
   int tc = 32;
   while (tc < 2 * L.bn) tc *= 2;
   a.tmem_cols = tc;
@@ -390,6 +393,9 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   a.op = o.op;
   a.act2 = o.act2;
   a.R = L.R;
+  a.lR = __builtin_ctz((unsigned)L.R);
+  a.lbw = __builtin_ctz((unsigned)a.bw);
+  if ((L.R & (L.R - 1)) != 0) return fail(ZJAI_UNSUPPORTED, "conv: shuffle factor must be a power of two");
   a.cph = L.cph;
   a.err = ctx->d_err;
   if (!o.planar) {

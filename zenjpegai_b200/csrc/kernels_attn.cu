@@ -91,59 +91,82 @@ __global__ void layer_norm_kernel(const __half* __restrict__ x, __half* __restri
 }
 
 // ---- depthwise 3x3 ------------------------------------------------------------------------
-// Thread per (pixel, group of 8 channels). Weights [c][9] f32. gate: out has c/2 channels,
-// out[k] = elu(dw[k]) * dw[k + c/2].
-__global__ void dw3x3_kernel(const __half* __restrict__ x, __half* __restrict__ y, int n_img,
-                             int h, int w, int c, long long xpix, long long xrow, long long ximg,
-                             long long ypix, long long yrow, long long yimg,
-                             const float* __restrict__ wt, int gate) {
-  const int cg_out = (gate ? c / 2 : c) / 8;
-  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  long long total = (long long)n_img * h * w * cg_out;
-  if (idx >= total) return;
-  const int cg = (int)(idx % cg_out);
-  long long r = idx / cg_out;
-  const int px = (int)(r % w);
-  r /= w;
-  const int py = (int)(r % h), n = (int)(r / h);
-  const __half* xb = x + n * ximg;
-  const int nsrc = gate ? 2 : 1;
-  float res[2][8];
+// Thread per (group of 8 channels, segment of kDwSeg pixels of one row); consecutive threads
+// take consecutive channel groups, so every 16-byte load of a warp is part of one contiguous
+// run. The 3x3 weights of the thread's 8 channels sit in registers. Weights [c][9] f32.
+// gate: out has c/2 channels, out[k] = elu(dw[k]) * dw[k + c/2] (the FFN gate, math.rs:376).
+constexpr int kDwSeg = 4;
+
+__device__ __forceinline__ void dw_source(const __half* __restrict__ xb, int py, int px0, int h,
+                                          int w, long long xrow, long long xpix, int c0,
+                                          const float* __restrict__ wt, float (&acc)[kDwSeg][8]) {
+  float wr[9][8];
 #pragma unroll
-  for (int s = 0; s < 2; ++s) {
-    if (s >= nsrc) break;
-    const int c0 = cg * 8 + s * (c / 2);
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int ky = 0; ky < 3; ++ky) {
-      const int yy = py + ky - 1;
-      if (yy < 0 || yy >= h) continue;
+    for (int t = 0; t < 9; ++t) wr[t][i] = __ldg(wt + (c0 + i) * 9 + t);
 #pragma unroll
-      for (int kx = 0; kx < 3; ++kx) {
-        const int xx = px + kx - 1;
-        if (xx < 0 || xx >= w) continue;
-        float v[8];
-        ld8(xb + yy * xrow + xx * xpix + c0, v);
+  for (int p = 0; p < kDwSeg; ++p)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = fmaf(__ldg(wt + (c0 + i) * 9 + ky * 3 + kx), v[i], acc[i]);
+    for (int i = 0; i < 8; ++i) acc[p][i] = 0.f;
+#pragma unroll
+  for (int ky = 0; ky < 3; ++ky) {
+    const int yy = py + ky - 1;
+    if (yy < 0 || yy >= h) continue;
+    float v[kDwSeg + 2][8];
+#pragma unroll
+    for (int q = 0; q < kDwSeg + 2; ++q) {
+      const int xx = px0 + q - 1;
+      if (xx >= 0 && xx < w) {
+        ld8(xb + yy * xrow + xx * xpix + c0, v[q]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[q][i] = 0.f;
       }
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) res[s][i] = acc[i];
+    for (int p = 0; p < kDwSeg; ++p)
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[p][i] = fmaf(wr[ky * 3 + kx][i], v[p + kx][i], acc[p][i]);
   }
-  float o[8];
+}
+
+__global__ void __launch_bounds__(256) dw3x3_kernel(const __half* __restrict__ x,
+                                                    __half* __restrict__ y, int n_img, int h,
+                                                    int w, int c, long long xpix, long long xrow,
+                                                    long long ximg, long long ypix,
+                                                    long long yrow, long long yimg,
+                                                    const float* __restrict__ wt, int gate) {
+  const int cg_out = (gate ? c / 2 : c) / 8;
+  const int segs = (w + kDwSeg - 1) / kDwSeg;
+  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  long long total = (long long)n_img * h * segs * cg_out;
+  if (idx >= total) return;
+  const int cg = (int)(idx % cg_out);
+  long long r = idx / cg_out;
+  const int sg = (int)(r % segs);
+  r /= segs;
+  const int py = (int)(r % h), n = (int)(r / h);
+  const int px0 = sg * kDwSeg;
+  const __half* xb = x + n * ximg;
+  float a[kDwSeg][8];
+  dw_source(xb, py, px0, h, w, xrow, xpix, cg * 8, wt, a);
   if (gate) {
+    float b[kDwSeg][8];
+    dw_source(xb, py, px0, h, w, xrow, xpix, cg * 8 + c / 2, wt, b);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float a = res[0][i];
-      const float e = a > 0.f ? a : expf(a) - 1.f;
-      o[i] = e * res[1][i];
-    }
-  } else {
+    for (int p = 0; p < kDwSeg; ++p)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = res[0][i];
+      for (int i = 0; i < 8; ++i) {
+        const float e = a[p][i] > 0.f ? a[p][i] : expf(a[p][i]) - 1.f;
+        a[p][i] = e * b[p][i];
+      }
   }
-  st8(y + n * yimg + py * yrow + px * ypix + cg * 8, o);
+#pragma unroll
+  for (int p = 0; p < kDwSeg; ++p)
+    if (px0 + p < w) st8(y + n * yimg + py * yrow + (px0 + p) * ypix + cg * 8, a[p]);
 }
 
 // ---- channel attention -------------------------------------------------------------------
@@ -241,23 +264,23 @@ __global__ void attn_softmax_kernel(const float* __restrict__ gram, const float*
   for (int j = 0; j < c; ++j) a[j] = vals[j] / sum;
 }
 
-// out[p][h*c+i] = sum_j attn[h][i][j] * v[p][h*c+j]; thread per (pixel, 8 output channels).
-__global__ void attn_apply_kernel(const __half* __restrict__ qkv, const float* __restrict__ attn,
-                                  __half* __restrict__ out, int n_img, int h, int w, int dim,
-                                  int heads, long long pix, long long row, long long img,
-                                  long long opix, long long orow, long long oimg) {
-  extern __shared__ float sa[];  // attn of this image: dim * c floats
+// out[p][h*c+i] = sum_j attn[h][i][j] * v[p][h*c+j]. Block = one group of 8 output channels
+// (blockIdx.y) and 256 pixels (one per thread): every shared-memory read of the attention
+// rows is a broadcast.
+__global__ void __launch_bounds__(256) attn_apply_kernel(
+    const __half* __restrict__ qkv, const float* __restrict__ attn, __half* __restrict__ out,
+    int n_img, int h, int w, int dim, int heads, long long pix, long long row, long long img,
+    long long opix, long long orow, long long oimg) {
+  __shared__ float sa[8 * 64];  // the 8 attention rows of this channel group (c <= 64)
   const int c = dim / heads;
-  const int n = blockIdx.y;
-  for (int t = threadIdx.x; t < dim * c; t += blockDim.x) sa[t] = attn[(long long)n * dim * c + t];
-  __syncthreads();
-  const int groups = dim / 8;
-  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (long long)h * w * groups) return;
-  const int g = (int)(idx % groups);
-  const long long p = idx / groups;
-  const int py = (int)(p / w), px = (int)(p % w);
+  const int n = blockIdx.z, g = blockIdx.y;
   const int i0 = g * 8, hd = i0 / c;
+  for (int t = threadIdx.x; t < 8 * c; t += blockDim.x)
+    sa[t] = attn[(long long)n * dim * c + (long long)i0 * c + t];
+  __syncthreads();
+  const long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= (long long)h * w) return;
+  const int py = (int)(p / w), px = (int)(p % w);
   const __half* vp = qkv + n * img + py * row + px * pix + 2 * dim + hd * c;
   float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   for (int j0 = 0; j0 < c; j0 += 8) {
@@ -266,7 +289,7 @@ __global__ void attn_apply_kernel(const __half* __restrict__ qkv, const float* _
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = fmaf(sa[(i0 + i) * c + j0 + jj], v[jj], o[i]);
+      for (int i = 0; i < 8; ++i) o[i] = fmaf(sa[i * c + j0 + jj], v[jj], o[i]);
     }
   }
   st8(out + n * oimg + py * orow + px * opix + i0, o);
@@ -305,7 +328,8 @@ void launch_layer_norm(const TView& x, const TView& y, const float* gamma, const
 
 void launch_dw3x3(const TView& x, const TView& y, const float* wt, bool gate, cudaStream_t s) {
   const int cg_out = (gate ? x.c / 2 : x.c) / 8;
-  long long total = (long long)x.n * x.h * x.w * cg_out;
+  const int segs = (x.w + kDwSeg - 1) / kDwSeg;
+  long long total = (long long)x.n * x.h * segs * cg_out;
   dw3x3_kernel<<<blocks_for(total, 256), 256, 0, s>>>(x.p, y.p, x.n, x.h, x.w, x.c, x.pix, x.row,
                                                        x.img, y.pix, y.row, y.img, wt, gate ? 1 : 0);
 }
@@ -327,10 +351,9 @@ void launch_attention(const TView& qkv, const TView& out, int heads, const float
       qkv.p, n, npix, qkv.w, dim, heads, qkv.pix, qkv.row, qkv.img, gram, sq, cpb);
   attn_softmax_kernel<<<blocks_for((long long)n * dim, 128), 128, 0, s>>>(gram, sq, temp, attn, n,
                                                                          dim, heads);
-  dim3 g3(blocks_for((long long)npix * (dim / 8), 256), n);
-  attn_apply_kernel<<<g3, 256, dim * c * sizeof(float), s>>>(qkv.p, attn, out.p, n, qkv.h, qkv.w,
-                                                             dim, heads, qkv.pix, qkv.row, qkv.img,
-                                                             out.pix, out.row, out.img);
+  dim3 g3(blocks_for((long long)npix, 256), dim / 8, n);
+  attn_apply_kernel<<<g3, 256, 0, s>>>(qkv.p, attn, out.p, n, qkv.h, qkv.w, dim, heads, qkv.pix,
+                                       qkv.row, qkv.img, out.pix, out.row, out.img);
 }
 
 size_t attention_scratch_floats(int n_img, int dim, int heads) {

@@ -1,14 +1,10 @@
 // Thin inline-PTX wrappers for sm_100a: mbarriers, TMA tensor copies, tcgen05 (TMEM alloc,
-// UMMA issue/commit, TMEM loads). Every wait is bounded: after ZJAI_WAIT_NS of wall time a
-// wait gives up, records an error word in global memory and reports failure, so a broken
-// pipeline ends the kernel with a status instead of hanging the GPU.
+// UMMA issue/commit, TMEM loads). Every wait is bounded: after kWaitCycles SM cycles (about
+// 2 s) a wait gives up, records an error word in global memory and reports failure, so a
+// broken pipeline ends the kernel with a status instead of hanging the GPU.
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
-
-#ifndef ZJAI_WAIT_NS
-#define ZJAI_WAIT_NS 2000000000ull  // 2 s
-#endif
 
 namespace zjai {
 
@@ -59,31 +55,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Wait limits are counted in SM clock cycles (clock64 is a cheap register read, unlike the
+// global timer): 4e9 cycles is about 2 s at the B200's 1.965 GHz boost clock and longer at
+// lower clocks.
+constexpr long long kWaitCycles = 4000000000LL;
+
 // Bounded wait for the phase with `parity` to complete. Returns false (and records `code`
 // in *err and sets *abort) on timeout, or when another role has already aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer();
+  const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if ((it & 63u) == 0) {
-      if (globaltimer() - t0 > ZJAI_WAIT_NS) {
-        atomicCAS(err, 0, code);
-        *abort = 1;
-        return false;
-      }
+    if ((it & 63u) == 0 && clock64() - t0 > kWaitCycles) {
+      atomicCAS(err, 0, code);
+      *abort = 1;
+      return false;
     }
   }
 }
 
 // Bounded wait that ignores the abort flag (used to drain in-flight work before exit).
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
-  uint64_t t0 = globaltimer();
+  const long long t0 = clock64();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 63u && globaltimer() - t0 > ZJAI_WAIT_NS) {
+    if ((it & 63u) == 63u && clock64() - t0 > kWaitCycles) {
       atomicCAS(err, 0, DEV_TIMEOUT_DRAIN);
       return false;
     }
@@ -178,7 +177,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[32]) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -191,8 +190,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[32]) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-#pragma unroll
-  for (int i = 16; i < 32; ++i) v[i] = 0.f;
 }
 
 // Shared-memory matrix descriptor (tcgen05 format): K-major operand whose rows are
