@@ -222,6 +222,19 @@ int zjai_channel_attention(zjai_ctx *ctx, const float *qkv, int c3, int h, int w
 int zjai_depthwise3x3(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,
                       float *out, int mem);
 
+/* Channel attention that allocates nothing. It has no counterpart in the reference: it is
+ * zjai_channel_attention for callers that must not allocate device memory during a call
+ * (code running under an external allocator or a strict memory budget, callers that only
+ * hand in pre-allocated buffers). qkv [3*dim][h][w], temperature [heads] and out [dim][h][w]
+ * are caller-owned DEVICE buffers (planar f32); the call's scratch is one fixed-size device
+ * array in the library, so dim <= 256 and dim / heads <= 64, and larger sizes return
+ * ZJAI_LIMIT_EXCEEDED. The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress); make that first call before any stream capture. All calls share
+ * the array: calls that overlap on the GPU (other streams or contexts) race. The work is
+ * enqueued on the context's stream and the call returns without waiting. */
+int zjai_channel_attention_static(zjai_ctx *ctx, const float *qkv, int c3, int h, int w,
+                                  int heads, const float *temperature, float *out);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif
