@@ -176,7 +176,7 @@ def main():
                                 device_id=torch.device("cuda", local))
 
     import zenjpegai_b200 as zj
-    from zenjpegai_b200 import _lib, synthetic as syn
+    from zenjpegai_b200 import _lib, sharding, synthetic as syn
     from zenjpegai_b200.decoder import Decoder
 
     H, W, op = cfg["H"], cfg["W"], cfg["op"]
@@ -194,7 +194,7 @@ def main():
     ly_h, luv_h = ly_h.pin_memory(), luv_h.pin_memory()
     ly, luv = ly_h.cuda(), luv_h.cuda()
     tiles = zj.synthesis_tiles(H, W, lh, lw, cfg["tile"], cfg["overlap"])
-    mine = [t for i, t in enumerate(tiles) if i % world == rank]
+    mine = sharding.shard_tiles(tiles, rank, world)
     planes = (torch.zeros((H, W), device="cuda"), torch.zeros((ch, cw), device="cuda"),
               torch.zeros((ch, cw), device="cuda"))
     out8 = torch.zeros(H * W + 2 * ch * cw, dtype=torch.uint8, device="cuda")
@@ -209,8 +209,7 @@ def main():
         dec.quantize_plane(planes[0], out=out8[:H * W])
         dec.quantize_plane(planes[1], out=out8[H * W:H * W + ch * cw])
         dec.quantize_plane(planes[2], out=out8[H * W + ch * cw:])
-        if world > 1:
-            dist.reduce(out8, dst=0, op=dist.ReduceOp.SUM)
+        sharding.gather_cores(out8, dist)
         if from_host and rank == 0:
             out8_host.copy_(out8, non_blocking=True)
 

@@ -222,6 +222,16 @@ int zjai_channel_attention(zjai_ctx *ctx, const float *qkv, int c3, int h, int w
 int zjai_depthwise3x3(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,
                       float *out, int mem);
 
+/* Layer-level timing harness, the GPU counterpart of the crate's conv microbenchmark
+ * (benches/conv_kernels.rs:165-187: `PackedConv::new` + `forward` on layer shapes): packs a
+ * random conv (or, with `transposed`, a stride-2 transposed conv: k 3 -> p1 op1, k 4 -> p1) of
+ * the given geometry, runs it `reps` times on n pseudo-random NHWC f16 maps of h x w in the
+ * context arena (ReLU epilogue, plus a residual add when `residual`) and returns the mean
+ * device time per launch in *ms and the algorithmic FLOPs per launch in *flops (may be NULL). */
+int zjai_conv_bench(zjai_ctx *ctx, int n, int h, int w, int cin, int cout, int k, int stride,
+                    int groups, int transposed, int residual, int reps, double *ms,
+                    double *flops);
+
 /* Channel attention that allocates nothing. It has no counterpart in the reference: it is
  * zjai_channel_attention for callers that must not allocate device memory during a call
  * (code running under an external allocator or a strict memory budget, callers that only

@@ -227,3 +227,49 @@ def test_model_errors(eng):
     with pytest.raises(zj.ZjaiError) as e:
         zj.Network(eng, zj.SYN_Y, zj.SOP, bad)
     assert e.value.status == 5 and "expected" in str(e.value)
+
+
+def test_cancel_and_reuse(eng):
+    """The caller's stop flag (the crate's `enough::Stop`, reconstruct.rs:391) is polled
+    between tiles and layers: a set flag returns ZJAI_CANCELLED and the context stays usable."""
+    import ctypes
+    import zenjpegai_b200 as zj
+    from zenjpegai_b200.decoder import Decoder
+    from zenjpegai_b200 import synthetic as syn
+    py, puv, ny, nuv = nets(eng, "sop")
+    dec = Decoder.__new__(Decoder)
+    dec.engine, dec.op, dec.net_y, dec.net_uv = eng, zj.SOP, ny, nuv
+    H, W = 128, 192
+    ly = syn.laplace_latent(40, "c/ly", (160, H // 16, W // 16), 1.5)
+    luv = syn.laplace_latent(40, "c/luv", (96, H // 16, W // 16), 1.5)
+    with pytest.raises(zj.ZjaiError) as e:
+        dec.synthesize(ly, luv, H, W, tile_size=64, overlap=16, cancel=ctypes.c_int(1))
+    assert e.value.status == 4  # ZJAI_CANCELLED
+    got = dec.synthesize(ly, luv, H, W, tile_size=64, overlap=16, cancel=ctypes.c_int(0))
+    want = zo.synthesize(zo.Checkpoint(py), zo.Checkpoint(puv), zo.SOP, ly, luv, H, W,
+                         tile_size=64, overlap=16)
+    assert psnr(got[0], want[0]) >= 50.0
+
+
+def test_arena_limit_and_bad_geometry():
+    """Arena exhaustion fails with ZJAI_LIMIT_EXCEEDED (Error::LimitExceeded) and malformed tile
+    geometry with ZJAI_INVALID_DATA (tiles.rs:71-76); the context remains usable."""
+    import zenjpegai_b200 as zj
+    from zenjpegai_b200.decoder import Decoder
+    from zenjpegai_b200 import synthetic as syn
+    small = zj.Engine(0, arena_bytes=64 << 20)
+    py, puv = syn.synthesis_params("hop", 3)
+    dec = Decoder(small, "hop", py, puv)
+    H, W = 1024, 1024
+    ly = syn.laplace_latent(41, "l/ly", (160, 64, 64), 1.5)
+    luv = syn.laplace_latent(41, "l/luv", (96, 64, 64), 1.5)
+    with pytest.raises(zj.ZjaiError) as e:
+        dec.synthesize(ly, luv, H, W)
+    assert e.value.status == 3  # ZJAI_LIMIT_EXCEEDED
+    with pytest.raises(zj.ZjaiError) as e:
+        dec.synthesize(ly, luv, H, W, tile_size=16, overlap=16)
+    assert e.value.status == 6  # ZJAI_INVALID_DATA
+    out = dec.synthesize(ly[:, :4, :4].copy(), luv[:, :4, :4].copy(), 64, 64)
+    assert np.isfinite(out[0]).all()
+    dec.close()
+    small.close()
