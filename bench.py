@@ -157,6 +157,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="hop4k", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", action="store_true",
+                    help="print the per-layer conv time of one profiled step to stderr")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
@@ -254,6 +256,14 @@ def main():
     ms, fl, nl = ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
     _lib.lib().zjai_ctx_profile_read(eng_h, ctypes.byref(ms), ctypes.byref(fl), ctypes.byref(nl))
     _lib.lib().zjai_ctx_profile(eng_h, 0)
+    if args.layers and rank == 0:
+        buf = ctypes.create_string_buffer(1 << 20)
+        _lib.lib().zjai_ctx_profile_report(eng_h, buf, len(buf))
+        rows = [ln.split("\t") for ln in buf.value.decode().splitlines()[1:]]
+        rows.sort(key=lambda r: -float(r[2]))
+        sys.stderr.write("per-layer conv time of one step (layer, launches, ms, GFLOP, TFLOP/s):\n")
+        for r in rows:
+            sys.stderr.write("  %-44s %4s %9s %9s %7s\n" % tuple(r))
     stats = torch.tensor([ms.value, fl.value, float(nl.value), float(launches)],
                          dtype=torch.float64, device="cuda")
     if world > 1:

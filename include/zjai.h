@@ -96,6 +96,10 @@ int64_t zjai_ctx_launch_count(const zjai_ctx *ctx);
  * returns the summed device time (ms), the algorithmic FLOPs (live MACs x 2) and the number
  * of convolution launches recorded since the previous read. */
 int zjai_ctx_profile(zjai_ctx *ctx, int enable);
+/* Per-layer totals of the recorded launches (tab-separated text: layer, launches, ms, GFLOP,
+ * TFLOP/s; layers of networks are tagged "<kind><batch>:<parameter prefix>") accumulated by
+ * zjai_ctx_profile_read since the previous report; written NUL-terminated into buf. */
+int zjai_ctx_profile_report(zjai_ctx *ctx, char *buf, size_t len);
 int zjai_ctx_profile_read(zjai_ctx *ctx, double *conv_ms, double *conv_flops,
                           int64_t *conv_launches);
 

@@ -192,6 +192,15 @@ int zjai_ctx_profile_read(zjai_ctx* ctx, double* conv_ms, double* conv_flops,
     ZJAI_TRY(cuda_check(cudaEventElapsedTime(&t, r.start, r.stop), "event time"));
     ms += t;
     fl += r.flops;
+    auto it = std::find_if(ctx->tag_totals.begin(), ctx->tag_totals.end(),
+                           [&](const std::pair<std::string, Ctx::TagTotal>& p) { return p.first == r.tag; });
+    if (it == ctx->tag_totals.end()) {
+      ctx->tag_totals.push_back({r.tag, Ctx::TagTotal()});
+      it = ctx->tag_totals.end() - 1;
+    }
+    it->second.launches++;
+    it->second.ms += t;
+    it->second.flops += r.flops;
     ctx->ev_pool.push_back(r.start);
     ctx->ev_pool.push_back(r.stop);
   }
@@ -199,6 +208,25 @@ int zjai_ctx_profile_read(zjai_ctx* ctx, double* conv_ms, double* conv_flops,
   ctx->conv_records.clear();
   if (conv_ms) *conv_ms = ms;
   if (conv_flops) *conv_flops = fl;
+  return ZJAI_OK;
+}
+
+int zjai_ctx_profile_report(zjai_ctx* ctx, char* buf, size_t len) {
+  ZJAI_TRY(ctx_enter(ctx));
+  std::string s = "layer\tlaunches\tms\tGFLOP\tTFLOP/s\n";
+  for (auto& p : ctx->tag_totals) {
+    char line[512];
+    snprintf(line, sizeof line, "%s\t%lld\t%.4f\t%.3f\t%.1f\n", p.first.c_str(),
+             p.second.launches, p.second.ms, p.second.flops / 1e9,
+             p.second.ms > 0 ? p.second.flops / (p.second.ms * 1e9) : 0.0);
+    s += line;
+  }
+  ctx->tag_totals.clear();
+  if (buf && len) {
+    const size_t n = std::min(len - 1, s.size());
+    memcpy(buf, s.data(), n);
+    buf[n] = 0;
+  }
   return ZJAI_OK;
 }
 

@@ -244,7 +244,6 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     tab[n] = ((uint32_t)(n / a.cph) << 16) | (uint32_t)(n % a.cph);
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), (uint32_t)a.tmem_cols);
@@ -279,10 +278,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                         tc.img);
           } else {
             const int dx = kx - a.pad_l, dy = ky - a.pad_t;
-            tma_load_5d(sA, &tmA, fb, cc * a.kc, dx & 1, tc.ox0 + (dx >> 1), dy & 1,
+            tma_load_5d(sA, a.tmA_img + tc.img, fb, cc * a.kc, dx & 1, tc.ox0 + (dx >> 1), dy & 1,
                         tc.oy0 + (dy >> 1));
           }
-          tma_load_2d(sB, &tmB, fb, cc * a.kc, tap * npad + tc.n0);
+          bulk_load(sB,
+                    a.wblk + ((size_t)(tap * a.cchunks + cc) * a.n_tiles + tc.n0 / a.bn) *
+                                 ((size_t)a.bn * a.kc),
+                    b_bytes, fb);
           ++issued;
           if (++stage == S) {
             stage = 0;

@@ -30,11 +30,15 @@ struct ConvArgs {
   // K loop
   int kw, taps, pad_t, pad_l;
   int s2;              // 1: stride-2 conv through the 5-D (parity-split) input view
+  const CUtensorMap* tmA_img;  // s2: per-picture tensor maps in device memory (64 B aligned)
   int cchunks, kc;     // channel chunks per tap; chunk width (16, 32 or 64)
   int bn;              // N tile (multiple of 16, <= 256)
   int stages;
   int tmem_cols;
   int oh, ow;          // conv output extent (pixels of the GEMM M space)
+  // weights as contiguous K-step blocks [bn][kc] in the shared-memory (swizzled) image, block
+  // index (tap * cchunks + cc) * n_tiles + n_tile: one bulk copy per K step
+  const __half* wblk;
   // epilogue
   const float* bias;   // [n_tiles * bn] in packed column order, or null
   float scale;         // weight unscale (power of two)

@@ -168,12 +168,31 @@ static float weight_scale(const std::vector<float>& w) {
   return std::ldexp(1.f, s);
 }
 
+// `wf` is [tap][npad][cin_pad]. The device copy is one contiguous block per K step and N tile
+// — [bn rows][kc columns] f16, block (tap * cchunks + cc) * n_tiles + nt — already in the
+// swizzled shared-memory image the MMA reads (16-byte chunk j of row r stored at j ^ f(r), the
+// same XOR the TMA applies for 128/64/32-byte swizzles), so the kernel fetches each block with
+// one bulk copy.
 static int upload_layer(Ctx* ctx, ConvLayer* L, const std::vector<float>& wf,
                         const std::vector<float>& bf) {
   float s = weight_scale(wf);
   L->scale = 1.f / s;
+  const int taps = L->kh * L->kw, kc = L->kc, bn = L->bn;
+  const int chunks16 = kc / 8;  // 16-byte chunks per row
   std::vector<__half> wh(wf.size());
-  for (size_t i = 0; i < wf.size(); ++i) wh[i] = __float2half_rn(wf[i] * s);
+  size_t blk = 0;
+  for (int tap = 0; tap < taps; ++tap)
+    for (int cc = 0; cc < L->cchunks; ++cc)
+      for (int nt = 0; nt < L->n_tiles; ++nt, ++blk) {
+        __half* dst = wh.data() + blk * (size_t)bn * kc;
+        for (int r = 0; r < bn; ++r) {
+          const int f = kc == 64 ? (r & 7) : kc == 32 ? ((r >> 1) & 3) : ((r >> 2) & 1);
+          const float* src = wf.data() + ((size_t)tap * L->npad + nt * bn + r) * L->cin_pad + cc * kc;
+          for (int j = 0; j < chunks16; ++j)
+            for (int e = 0; e < 8; ++e)
+              dst[(size_t)r * kc + ((j ^ f) * 8) + e] = __float2half_rn(src[j * 8 + e] * s);
+        }
+      }
   ZJAI_TRY(cuda_check(cudaMalloc(&L->w, wh.size() * sizeof(__half)), "cudaMalloc weights"));
   ZJAI_TRY(cuda_check(cudaMemcpy(L->w, wh.data(), wh.size() * sizeof(__half),
                                  cudaMemcpyHostToDevice),
@@ -321,7 +340,7 @@ static void timed_launch(Ctx* ctx, double flops, F&& f) {
     f();
     return;
   }
-  Ctx::ConvRecord r{ctx->take_event(), ctx->take_event(), flops};
+  Ctx::ConvRecord r{ctx->take_event(), ctx->take_event(), flops, ctx->tag};
   cudaEventRecord(r.start, ctx->stream);
   f();
   cudaEventRecord(r.stop, ctx->stream);
@@ -446,8 +465,9 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     a.sh = o.sh;
   }
 
-  CUtensorMap tmB;
-  ZJAI_TRY(make_weight_map(ctx, &tmB, L.w, L.cin_pad, a.taps * L.npad, L.kc, L.bn));
+  CUtensorMap tmB;  // unused by the kernel: weights arrive as bulk copies of a.wblk
+  memset(&tmB, 0, sizeof tmB);
+  a.wblk = L.w;
   if (!a.s2) {
     CUtensorMap tmA;
     ZJAI_TRY(make_act_map(ctx, &tmA, in, L.kc, a.bw, a.bh));
@@ -456,22 +476,23 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     const double fl = (double)L.flops_per_px * oh * ow * in.n;
     timed_launch(ctx, fl, [&] { launch_conv(tmA, tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream); });
   } else {
-    // The parity-split 5-D view has no batch axis: one launch per picture.
-    for (int i = 0; i < in.n; ++i) {
-      CUtensorMap tmA;
-      ZJAI_TRY(make_act_map_s2(ctx, &tmA, in, i, L.kc, a.bw, a.bh));
-      ConvArgs ai = a;
-      ai.n_img = 1;
-      ai.num_tiles = a.tiles_x * a.tiles_y * a.n_tiles;
-      if (ai.out) ai.out += i * a.out_img;
-      if (ai.r1) ai.r1 += i * a.r1_img;
-      if (ai.r2) ai.r2 += i * a.r2_img;
-      if (ai.out2) ai.out2 += i * a.o2_img;
-      if (ai.pout && !ai.img_win) ai.pout += i * a.p_img;
-      if (ai.img_win) ai.img_win += 6 * i;
-      const double fl = (double)L.flops_per_px * oh * ow;
-      timed_launch(ctx, fl, [&] { launch_conv(tmA, tmB, ai, std::min(ai.num_tiles, ctx->sms), ctx->stream); });
-    }
+    // The parity-split 5-D view has no batch axis: one tensor map per picture, kept in a
+    // device array (from the caller's arena, ordered on its stream) that the producer indexes
+    // by the tile's picture. One launch covers the whole batch.
+    std::vector<CUtensorMap> maps(in.n);
+    for (int i = 0; i < in.n; ++i)
+      ZJAI_TRY(make_act_map_s2(ctx, &maps[i], in, i, L.kc, a.bw, a.bh));
+    Arena* ar = ctx->cur_arena ? ctx->cur_arena : &ctx->arena;
+    void* dmaps = ar->alloc(sizeof(CUtensorMap) * maps.size());
+    if (!dmaps) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (tensor maps)");
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(dmaps, maps.data(), sizeof(CUtensorMap) * maps.size(),
+                                        cudaMemcpyHostToDevice, ctx->stream),
+                        "tensor map upload"));
+    a.tmA_img = static_cast<const CUtensorMap*>(dmaps);
+    a.n_img = in.n;
+    a.num_tiles = a.tiles_x * a.tiles_y * a.n_img * a.n_tiles;
+    const double fl = (double)L.flops_per_px * oh * ow * in.n;
+    timed_launch(ctx, fl, [&] { launch_conv(maps[0], tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream); });
   }
   return cuda_check(cudaGetLastError(), "conv launch");
 }

@@ -66,6 +66,7 @@ struct Ctx {
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   Arena arena;   // work of `stream`
   Arena arena2;  // work of `stream2` (chroma synthesis runs beside luma)
+  Arena* cur_arena = nullptr;  // arena of the network runner currently launching (or null)
   int* d_err = nullptr;  // kernel status word
   std::atomic<long long> launches{0};
   // driver entry point
@@ -78,8 +79,16 @@ struct Ctx {
   struct ConvRecord {
     cudaEvent_t start, stop;
     double flops;
+    std::string tag;
   };
   std::vector<ConvRecord> conv_records;
+  std::string tag;  // name of the layer being launched (for the profile report)
+  // per-tag totals accumulated by zjai_ctx_profile_read: launches, ms, flops
+  struct TagTotal {
+    long long launches = 0;
+    double ms = 0.0, flops = 0.0;
+  };
+  std::vector<std::pair<std::string, TagTotal>> tag_totals;
   cudaEvent_t take_event();
 };
 

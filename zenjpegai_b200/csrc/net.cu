@@ -255,13 +255,22 @@ const ConvLayer* Runner::layer(const std::string& name) {
   return it == net->convs.end() ? nullptr : &it->second;
 }
 
+// Profile tag prefix: network kind and batch size ("Y28:" = luma, 28 tiles).
+std::string Runner::kind_tag() const {
+  static const char* k[] = {"Y", "UV", "AY", "AUV"};
+  return std::string(k[net->kind & 3]) + std::to_string(n) + ":";
+}
+
 int Runner::conv(const std::string& name, const TView& in, ConvOut o) {
   const ConvLayer* L = layer(name);
   if (!L) return fail(ZJAI_MODEL, name + ": layer not loaded");
   cudaStream_t saved = ctx->stream;
   ctx->stream = stream;
+  ctx->cur_arena = arena;
+  if (ctx->profiling) ctx->tag = kind_tag() + name;
   int st = run_conv(ctx, *L, in, o);
   ctx->stream = saved;
+  ctx->cur_arena = nullptr;
   if (st == ZJAI_OK && count_flops) {
     int oh, ow, out_h, out_w;
     L->out_size(in.h, in.w, &oh, &ow, &out_h, &out_w);

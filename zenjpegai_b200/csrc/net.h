@@ -43,6 +43,7 @@ struct Runner {
   int alloc(int h, int w, int c, TView* v);
   const ConvLayer* layer(const std::string& name);
   int conv(const std::string& name, const TView& in, ConvOut o);
+  std::string kind_tag() const;
   int out_extent(const std::string& name, int h, int w, int* oh, int* ow);
   int stop_check();
 

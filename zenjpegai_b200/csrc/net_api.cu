@@ -73,7 +73,8 @@ int synthesize_tiles_dev(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const 
       return fail(ZJAI_INVALID_DATA, "synthesis tile outside the latent");
     groups[std::make_tuple(t.img_h, t.img_w, t.lat_h, t.lat_w)].push_back((int)i);
   }
-  cudaStream_t s1 = ctx->stream, s2 = ctx->stream2;
+  // while profiling, chroma runs after luma on one stream so per-layer events see no overlap
+  cudaStream_t s1 = ctx->stream, s2 = ctx->profiling ? ctx->stream : ctx->stream2;
   ZJAI_TRY(cuda_check(cudaEventRecord(ctx->ev_fork, s1), "event"));
   ZJAI_TRY(cuda_check(cudaStreamWaitEvent(s2, ctx->ev_fork, 0), "event wait"));
   for (auto& kv : groups) {
