@@ -91,82 +91,129 @@ __global__ void layer_norm_kernel(const __half* __restrict__ x, __half* __restri
 }
 
 // ---- depthwise 3x3 ------------------------------------------------------------------------
-// Thread per (group of 8 channels, segment of kDwSeg pixels of one row); consecutive threads
-// take consecutive channel groups, so every 16-byte load of a warp is part of one contiguous
-// run. The 3x3 weights of the thread's 8 channels sit in registers. Weights [c][9] f32.
-// gate: out has c/2 channels, out[k] = elu(dw[k]) * dw[k + c/2] (the FFN gate, math.rs:376).
-constexpr int kDwSeg = 4;
+// Block = a tile of kDwTH rows x TW columns x 64 output channels. Its input (with the
+// one-pixel halo) is staged in shared memory by 16-byte cp.async copies, zero-filled outside
+// the picture (the convolution's zero padding), as [row][col][8-channel group] chunks.
+// Thread = (8-channel group of one source, column): it walks the tile's input rows top to
+// bottom, adding each row into the three output rows that it feeds (accumulators in
+// registers, the thread's 3x3 weights too) and writing an output row as soon as its last
+// input row is in. Per output the taps accumulate in (ky, kx) row-major order. Weights [c][9].
+// gate: out has c/2 channels, out[k] = elu(dw[k]) * dw[k + c/2] (the FFN gate, math.rs:376);
+// the thread of group g of the first half and the thread of group g of the second half sit 8
+// lanes apart, and the second hands its sums to the first by a shuffle.
+constexpr int kDwTH = 8;
 
-__device__ __forceinline__ void dw_source(const __half* __restrict__ xb, int py, int px0, int h,
-                                          int w, long long xrow, long long xpix, int c0,
-                                          const float* __restrict__ wt, float (&acc)[kDwSeg][8]) {
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
+               "r"(src_bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <bool GATE>
+struct DwShape {
+  static constexpr int G = GATE ? 16 : 8;  // source channel groups per block
+  static constexpr int TW = 256 / G;       // tile columns (one thread per group and column)
+  static constexpr int SW = TW + 2, SH = kDwTH + 2;
+  static constexpr int smem = SH * SW * G * 16;
+};
+
+template <bool GATE>
+__global__ void __launch_bounds__(256, 2)
+    dw3x3_kernel(const __half* __restrict__ x, __half* __restrict__ y, int h, int w, int c,
+                 long long xpix, long long xrow, long long ximg, long long ypix, long long yrow,
+                 long long yimg, const float* __restrict__ wt, int tiles_x, int tiles_y,
+                 int cblocks) {
+  using S = DwShape<GATE>;
+  extern __shared__ __align__(16) uint4 dw_tile[];
+  const int cg_out = (GATE ? c / 2 : c) / 8;
+  int b = blockIdx.x;
+  const int cb = b % cblocks;
+  b /= cblocks;
+  const int tx = b % tiles_x;
+  b /= tiles_x;
+  const int ty = b % tiles_y;
+  const int n = b / tiles_y;
+  const int x0 = tx * S::TW, y0 = ty * kDwTH;
+  const __half* xb = x + n * ximg;
+
+  for (int j = threadIdx.x; j < S::SH * S::SW * S::G; j += 256) {
+    const int g = j % S::G;
+    const int q = j / S::G;
+    const int cx = q % S::SW, r = q / S::SW;
+    const int yy = y0 - 1 + r, xx = x0 - 1 + cx;
+    const int grp = cb * 8 + (g & 7);
+    const int ch = (GATE && g >= 8 ? c / 2 : 0) + grp * 8;
+    const bool ok = grp < cg_out && yy >= 0 && yy < h && xx >= 0 && xx < w;
+    cp_async16(dw_tile + j, ok ? xb + yy * xrow + xx * xpix + ch : x, ok ? 16 : 0);
+  }
+
+  const int g = threadIdx.x % S::G, xl = threadIdx.x / S::G;
+  const int grp = cb * 8 + (g & 7);
+  const bool gvalid = grp < cg_out;
+  const int ch = (GATE && g >= 8 ? c / 2 : 0) + grp * 8;
   float wr[9][8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int t = 0; t < 9; ++t) wr[t][i] = __ldg(wt + (c0 + i) * 9 + t);
+    for (int t = 0; t < 9; ++t) wr[t][i] = gvalid ? __ldg(wt + (ch + i) * 9 + t) : 0.f;
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+  __syncthreads();
+
+  const bool xvalid = gvalid && x0 + xl < w;
+  __half* yb = y + n * yimg + (x0 + xl) * ypix + grp * 8;
+  float acc[3][8];
 #pragma unroll
-  for (int p = 0; p < kDwSeg; ++p)
+  for (int k = 0; k < 3; ++k)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[p][i] = 0.f;
+    for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
 #pragma unroll
-  for (int ky = 0; ky < 3; ++ky) {
-    const int yy = py + ky - 1;
-    if (yy < 0 || yy >= h) continue;
-    float v[kDwSeg + 2][8];
+  for (int r = 0; r < S::SH; ++r) {
 #pragma unroll
-    for (int q = 0; q < kDwSeg + 2; ++q) {
-      const int xx = px0 + q - 1;
-      if (xx >= 0 && xx < w) {
-        ld8(xb + yy * xrow + xx * xpix + c0, v[q]);
-      } else {
+    for (int kx = 0; kx < 3; ++kx) {
+      float v[8];
+      unpack8(dw_tile[(r * S::SW + xl + kx) * S::G + g], v);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[q][i] = 0.f;
+      for (int ky = 0; ky < 3; ++ky) {
+        const int o = r - ky;
+        if (o >= 0 && o < kDwTH) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[o % 3][i] = fmaf(wr[ky * 3 + kx][i], v[i], acc[o % 3][i]);
+        }
       }
     }
+    if (r >= 2) {
+      const int o = r - 2;
+      float(&a)[8] = acc[o % 3];
+      if (GATE) {
+        float bv[8];
 #pragma unroll
-    for (int p = 0; p < kDwSeg; ++p)
+        for (int i = 0; i < 8; ++i) bv[i] = __shfl_down_sync(0xffffffffu, a[i], 8);
+        if (g < 8 && xvalid && y0 + o < h) {
 #pragma unroll
-      for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[p][i] = fmaf(wr[ky * 3 + kx][i], v[p + kx][i], acc[p][i]);
-  }
-}
-
-__global__ void __launch_bounds__(256) dw3x3_kernel(const __half* __restrict__ x,
-                                                    __half* __restrict__ y, int n_img, int h,
-                                                    int w, int c, long long xpix, long long xrow,
-                                                    long long ximg, long long ypix,
-                                                    long long yrow, long long yimg,
-                                                    const float* __restrict__ wt, int gate) {
-  const int cg_out = (gate ? c / 2 : c) / 8;
-  const int segs = (w + kDwSeg - 1) / kDwSeg;
-  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  long long total = (long long)n_img * h * segs * cg_out;
-  if (idx >= total) return;
-  const int cg = (int)(idx % cg_out);
-  long long r = idx / cg_out;
-  const int sg = (int)(r % segs);
-  r /= segs;
-  const int py = (int)(r % h), n = (int)(r / h);
-  const int px0 = sg * kDwSeg;
-  const __half* xb = x + n * ximg;
-  float a[kDwSeg][8];
-  dw_source(xb, py, px0, h, w, xrow, xpix, cg * 8, wt, a);
-  if (gate) {
-    float b[kDwSeg][8];
-    dw_source(xb, py, px0, h, w, xrow, xpix, cg * 8 + c / 2, wt, b);
-#pragma unroll
-    for (int p = 0; p < kDwSeg; ++p)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float e = a[p][i] > 0.f ? a[p][i] : expf(a[p][i]) - 1.f;
-        a[p][i] = e * b[p][i];
+          for (int i = 0; i < 8; ++i) {
+            const float e = a[i] > 0.f ? a[i] : expf(a[i]) - 1.f;
+            a[i] = e * bv[i];
+          }
+          st8(yb + (y0 + o) * yrow, a);
+        }
+      } else if (xvalid && y0 + o < h) {
+        st8(yb + (y0 + o) * yrow, a);
       }
-  }
 #pragma unroll
-  for (int p = 0; p < kDwSeg; ++p)
-    if (px0 + p < w) st8(y + n * yimg + py * yrow + (px0 + p) * ypix + cg * 8, a[p]);
+      for (int i = 0; i < 8; ++i) a[i] = 0.f;
+    }
+  }
 }
 
 // ---- channel attention -------------------------------------------------------------------
@@ -328,10 +375,21 @@ void launch_layer_norm(const TView& x, const TView& y, const float* gamma, const
 
 void launch_dw3x3(const TView& x, const TView& y, const float* wt, bool gate, cudaStream_t s) {
   const int cg_out = (gate ? x.c / 2 : x.c) / 8;
-  const int segs = (x.w + kDwSeg - 1) / kDwSeg;
-  long long total = (long long)x.n * x.h * segs * cg_out;
-  dw3x3_kernel<<<blocks_for(total, 256), 256, 0, s>>>(x.p, y.p, x.n, x.h, x.w, x.c, x.pix, x.row,
-                                                       x.img, y.pix, y.row, y.img, wt, gate ? 1 : 0);
+  const int cblocks = (cg_out + 7) / 8;
+  const int tiles_y = (x.h + kDwTH - 1) / kDwTH;
+  if (gate) {
+    using S = DwShape<true>;
+    const int tiles_x = (x.w + S::TW - 1) / S::TW;
+    dw3x3_kernel<true><<<x.n * tiles_y * tiles_x * cblocks, 256, S::smem, s>>>(
+        x.p, y.p, x.h, x.w, x.c, x.pix, x.row, x.img, y.pix, y.row, y.img, wt, tiles_x, tiles_y,
+        cblocks);
+  } else {
+    using S = DwShape<false>;
+    const int tiles_x = (x.w + S::TW - 1) / S::TW;
+    dw3x3_kernel<false><<<x.n * tiles_y * tiles_x * cblocks, 256, S::smem, s>>>(
+        x.p, y.p, x.h, x.w, x.c, x.pix, x.row, x.img, y.pix, y.row, y.img, wt, tiles_x, tiles_y,
+        cblocks);
+  }
 }
 
 void launch_attention(const TView& qkv, const TView& out, int heads, const float* temp,
