@@ -94,7 +94,8 @@ constexpr int kChunk = 16;  // accumulator columns per TMEM load and epilogue st
 // this thread then writes).
 template <int OP>
 __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kChunk], int col0,
-                                         int img, int oy, int ox, bool valid, const uint32_t* tab) {
+                                         int img, int oy, int ox, bool valid, const uint32_t* tab,
+                                         const float* btab) {
   constexpr int G = kChunk / 8;
   int Yg[G], Xg[G], cg[G];
   bool ok[G];
@@ -124,21 +125,16 @@ __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kCh
   for (int g = 0; g < G; ++g) {
     if (!ok[g]) continue;
     float x[8];
-    if (a.bias) {
-      const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.bias + col0 + 8 * g));
-      const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.bias + col0 + 8 * g + 4));
-      x[0] = v[8 * g + 0] * a.scale + b0.x;
-      x[1] = v[8 * g + 1] * a.scale + b0.y;
-      x[2] = v[8 * g + 2] * a.scale + b0.z;
-      x[3] = v[8 * g + 3] * a.scale + b0.w;
-      x[4] = v[8 * g + 4] * a.scale + b1.x;
-      x[5] = v[8 * g + 5] * a.scale + b1.y;
-      x[6] = v[8 * g + 6] * a.scale + b1.z;
-      x[7] = v[8 * g + 7] * a.scale + b1.w;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = v[8 * g + e] * a.scale;
-    }
+    const float4 b0 = *reinterpret_cast<const float4*>(btab + col0 + 8 * g);
+    const float4 b1 = *reinterpret_cast<const float4*>(btab + col0 + 8 * g + 4);
+    x[0] = v[8 * g + 0] * a.scale + b0.x;
+    x[1] = v[8 * g + 1] * a.scale + b0.y;
+    x[2] = v[8 * g + 2] * a.scale + b0.z;
+    x[3] = v[8 * g + 3] * a.scale + b0.w;
+    x[4] = v[8 * g + 4] * a.scale + b1.x;
+    x[5] = v[8 * g + 5] * a.scale + b1.y;
+    x[6] = v[8 * g + 6] * a.scale + b1.z;
+    x[7] = v[8 * g + 7] * a.scale + b1.w;
     act8(x, a.act1);
     if constexpr (OP != OP_NONE) {
       float q1[8];
@@ -171,7 +167,7 @@ __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kCh
 // Planar f32 output (final layers and the layer entry points): one scalar per column.
 __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[kChunk], int col0,
                                            int img, int oy, int ox, bool valid,
-                                           const uint32_t* tab) {
+                                           const uint32_t* tab, const float* btab) {
   if (!valid) return;
   int py0 = a.py0, px0 = a.px0, cy0 = a.cy0, cy1 = a.cy1, cx0 = a.cx0, cx1 = a.cx1;
   if (a.img_win) {
@@ -183,6 +179,7 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
     cx0 = wv[4];
     cx1 = wv[5];
   }
+#pragma unroll
   for (int j = 0; j < kChunk; ++j) {
     const uint32_t e = tab[col0 + j];
     const int p = (int)(e >> 16), ch = (int)(e & 0xFFFFu);
@@ -192,8 +189,7 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
     const int PY = py0 + Y, PX = px0 + X;
     if (PY < cy0 || PY >= cy1 || PX < cx0 || PX >= cx1) continue;
     if (PY % a.sv || PX % a.sh) continue;
-    const float b = a.bias ? __ldg(a.bias + col0 + j) : 0.f;
-    float x = act_rt(v[j] * a.scale + b, a.act1);
+    float x = act_rt(v[j] * a.scale + btab[col0 + j], a.act1);
     if (a.denorm) x = fminf(fmaxf(x * 128.f + 127.5f, 0.f), 255.f);
     float* dst = (ch == 1 && a.pout2) ? a.pout2 : a.pout + ch * a.p_plane;
     dst[(a.img_win ? 0 : img * a.p_img) + (PY / a.sv) * a.p_row + PX / a.sh] = x;
@@ -221,10 +217,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* tab = reinterpret_cast<uint32_t*>(smem + S * stage_bytes + kBarrierBytes);
+  const int npad = a.n_tiles * a.bn;
+  float* btab = reinterpret_cast<float*>(tab + npad);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int npad = a.n_tiles * a.bn;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -239,9 +236,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  // column -> (phase, channel) table of the packed column order
-  for (int n = threadIdx.x; n < npad; n += blockDim.x)
+  // column -> (phase, channel) table of the packed column order, and the bias per column
+  for (int n = threadIdx.x; n < npad; n += blockDim.x) {
     tab[n] = ((uint32_t)(n / a.cph) << 16) | (uint32_t)(n % a.cph);
+    btab[n] = a.bias ? a.bias[n] : 0.f;
+  }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
   }
@@ -352,9 +351,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       mbar_wait_drain(smem_u32(drain), 0, a.err);
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (8 warps)
-    // Two warpgroups; warp w reads TMEM lanes 32*(w%4).. (its accumulator rows = pixels),
-    // warpgroup g takes the column chunks c with c % 2 == g.
+    // ------------------------------------------------------------------ epilogue
+    // kEpiWarpgroups warpgroups; warp w reads TMEM lanes 32*(w%4).. (its accumulator rows =
+    // pixels), warpgroup g takes the column chunks c with c % kEpiWarpgroups == g.
     const int q = warp & 3;
     const int wg = (warp - 2) >> 2;
     const int m = q * 32 + lane;  // accumulator row == pixel index in the tile
@@ -372,22 +371,22 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         tc_fence_before();
         mbar_arrive(smem_u32(&acce[acc]));
       }
-      for (int c = wg; c < nchunks; c += 2) {
+      for (int c = wg; c < nchunks; c += kEpiWarpgroups) {
         float v[kChunk];
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.bn + c * kChunk), v);
-        if (c + 2 >= nchunks) {  // this thread's last read of the accumulator
+        if (c + kEpiWarpgroups >= nchunks) {  // this thread's last read of the accumulator
           tc_fence_before();
           mbar_arrive(smem_u32(&acce[acc]));
         }
         const int col0 = tc.n0 + c * kChunk;
         if (a.planar) {
-          epi_planar(a, v, col0, tc.img, oy, ox, valid, tab);
+          epi_planar(a, v, col0, tc.img, oy, ox, valid, tab, btab);
         } else {
           switch (a.op) {
-            case OP_ADD: epi_nhwc<OP_ADD>(a, v, col0, tc.img, oy, ox, valid, tab); break;
-            case OP_GATE: epi_nhwc<OP_GATE>(a, v, col0, tc.img, oy, ox, valid, tab); break;
-            case OP_CAB: epi_nhwc<OP_CAB>(a, v, col0, tc.img, oy, ox, valid, tab); break;
-            default: epi_nhwc<OP_NONE>(a, v, col0, tc.img, oy, ox, valid, tab); break;
+            case OP_ADD: epi_nhwc<OP_ADD>(a, v, col0, tc.img, oy, ox, valid, tab, btab); break;
+            case OP_GATE: epi_nhwc<OP_GATE>(a, v, col0, tc.img, oy, ox, valid, tab, btab); break;
+            case OP_CAB: epi_nhwc<OP_CAB>(a, v, col0, tc.img, oy, ox, valid, tab, btab); break;
+            default: epi_nhwc<OP_NONE>(a, v, col0, tc.img, oy, ox, valid, tab, btab); break;
           }
         }
       }

@@ -67,17 +67,23 @@ struct ConvArgs {
   int* err;
 };
 
-constexpr int kConvThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr int kEpiThreads = 256;
+// warp 0 TMA, warp 1 MMA, then kEpiWarpgroups warpgroups of epilogue (warpgroup g takes the
+// accumulator column chunks c with c % kEpiWarpgroups == g)
+constexpr int kEpiWarpgroups = 4;
+constexpr int kEpiThreads = 128 * kEpiWarpgroups;
+constexpr int kConvThreads = 64 + kEpiThreads;
 constexpr int kBarrierBytes = 256;
 
 __host__ __device__ inline uint32_t conv_stage_bytes(int kc, int bn) {
   uint32_t b = 128u * kc * 2u + (uint32_t)bn * kc * 2u;
   return (b + 1023u) & ~1023u;
 }
-// 1 KB alignment slack + stages + barriers/slots + the column table (4 bytes per column)
+// 1 KB alignment slack + barriers/slots + the column table and the bias (4 + 4 bytes per column)
+__host__ __device__ inline uint32_t conv_fixed_smem(int npad) {
+  return 1024u + kBarrierBytes + 8u * (uint32_t)npad;
+}
 __host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int stages, int npad) {
-  return 1024u + stages * conv_stage_bytes(kc, bn) + kBarrierBytes + 4u * (uint32_t)npad;
+  return stages * conv_stage_bytes(kc, bn) + conv_fixed_smem(npad);
 }
 
 void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmB, const ConvArgs& a, int grid,

@@ -397,7 +397,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   a.kc = L.kc;
   a.bn = L.bn;
   const uint32_t stage = conv_stage_bytes(L.kc, L.bn);
-  const uint32_t fixed = 1024u + kBarrierBytes + 4u * (uint32_t)L.npad;
+  const uint32_t fixed = conv_fixed_smem(L.npad);
   if (fixed + 2 * stage > 232448u)
     return fail(ZJAI_UNSUPPORTED, "conv: too many output columns for one launch");
   a.stages = (int)std::min<uint32_t>(8, (232448u - fixed) / stage);
