@@ -261,9 +261,16 @@ def main():
         _lib.lib().zjai_ctx_profile_report(eng_h, buf, len(buf))
         rows = [ln.split("\t") for ln in buf.value.decode().splitlines()[1:]]
         rows.sort(key=lambda r: -float(r[2]))
-        sys.stderr.write("per-layer conv time of one step (layer, launches, ms, GFLOP, TFLOP/s):\n")
+        sys.stderr.write("per-layer kernel time of one step, luma and chroma serialised "
+                         "(layer, launches, ms, GFLOP, TFLOP/s, GB, GB/s):\n")
         for r in rows:
-            sys.stderr.write("  %-44s %4s %9s %9s %7s\n" % tuple(r))
+            sys.stderr.write("  %-48s %4s %9s %9s %7s %8s %6s\n" % tuple(r))
+        kinds = {}
+        for r in rows:
+            k = r[0].split("[")[-1].rstrip("]") if r[0].endswith("]") else "conv"
+            kinds[k] = kinds.get(k, 0.0) + float(r[2])
+        sys.stderr.write("per kernel kind (ms): %s\n" % ", ".join(
+            "%s %.3f" % kv for kv in sorted(kinds.items(), key=lambda kv: -kv[1])))
     stats = torch.tensor([ms.value, fl.value, float(nl.value), float(launches)],
                          dtype=torch.float64, device="cuda")
     if world > 1:

@@ -179,8 +179,9 @@ def test_depthwise(eng, c):
     assert rel_l2(got, want) < REL_L2
 
 
-@pytest.mark.parametrize("dim,h,w", [(128, 40, 52), (64, 64, 64)])
+@pytest.mark.parametrize("dim,h,w", [(128, 40, 52), (64, 64, 64), (96, 17, 29)])
 def test_channel_attention(eng, dim, h, w):
+    # 128 / 64: register-tiled Gram and per-head apply (head width 32 / 16); 96: generic kernels
     from zenjpegai_b200 import synthetic as syn
     qkv = syn.normal(8, "qkv", (3 * dim, h, w))
     t = syn.uniform(8, "t", (4,), 0.5, 2.0)

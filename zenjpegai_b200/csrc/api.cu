@@ -187,11 +187,15 @@ int zjai_ctx_profile_read(zjai_ctx* ctx, double* conv_ms, double* conv_flops,
   ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "stream sync"));
   ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream2), "stream sync"));
   double ms = 0.0, fl = 0.0;
+  int64_t nconv = 0;
   for (auto& r : ctx->conv_records) {
     float t = 0.f;
     ZJAI_TRY(cuda_check(cudaEventElapsedTime(&t, r.start, r.stop), "event time"));
-    ms += t;
-    fl += r.flops;
+    if (r.conv) {
+      ms += t;
+      fl += r.flops;
+      ++nconv;
+    }
     auto it = std::find_if(ctx->tag_totals.begin(), ctx->tag_totals.end(),
                            [&](const std::pair<std::string, Ctx::TagTotal>& p) { return p.first == r.tag; });
     if (it == ctx->tag_totals.end()) {
@@ -201,10 +205,11 @@ int zjai_ctx_profile_read(zjai_ctx* ctx, double* conv_ms, double* conv_flops,
     it->second.launches++;
     it->second.ms += t;
     it->second.flops += r.flops;
+    it->second.bytes += r.bytes;
     ctx->ev_pool.push_back(r.start);
     ctx->ev_pool.push_back(r.stop);
   }
-  if (conv_launches) *conv_launches = (int64_t)ctx->conv_records.size();
+  if (conv_launches) *conv_launches = nconv;
   ctx->conv_records.clear();
   if (conv_ms) *conv_ms = ms;
   if (conv_flops) *conv_flops = fl;
@@ -213,12 +218,14 @@ int zjai_ctx_profile_read(zjai_ctx* ctx, double* conv_ms, double* conv_flops,
 
 int zjai_ctx_profile_report(zjai_ctx* ctx, char* buf, size_t len) {
   ZJAI_TRY(ctx_enter(ctx));
-  std::string s = "layer\tlaunches\tms\tGFLOP\tTFLOP/s\n";
+  std::string s = "layer\tlaunches\tms\tGFLOP\tTFLOP/s\tGB\tGB/s\n";
   for (auto& p : ctx->tag_totals) {
     char line[512];
-    snprintf(line, sizeof line, "%s\t%lld\t%.4f\t%.3f\t%.1f\n", p.first.c_str(),
-             p.second.launches, p.second.ms, p.second.flops / 1e9,
-             p.second.ms > 0 ? p.second.flops / (p.second.ms * 1e9) : 0.0);
+    const double ms = p.second.ms;
+    snprintf(line, sizeof line, "%s\t%lld\t%.4f\t%.3f\t%.1f\t%.4f\t%.0f\n", p.first.c_str(),
+             p.second.launches, ms, p.second.flops / 1e9,
+             ms > 0 ? p.second.flops / (ms * 1e9) : 0.0, p.second.bytes / 1e9,
+             ms > 0 ? p.second.bytes / (ms * 1e6) : 0.0);
     s += line;
   }
   ctx->tag_totals.clear();

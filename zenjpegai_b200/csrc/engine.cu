@@ -332,21 +332,6 @@ void ConvLayer::out_size(int h, int w, int* oh, int* ow, int* out_h, int* out_w)
 }
 
 // ---- launch ---------------------------------------------------------------------------------
-// Launch `f` on ctx->stream; when profiling, bracket it with events and record its FLOPs.
-template <class F>
-static void timed_launch(Ctx* ctx, double flops, F&& f) {
-  ctx->launches++;
-  if (!ctx->profiling) {
-    f();
-    return;
-  }
-  Ctx::ConvRecord r{ctx->take_event(), ctx->take_event(), flops, ctx->tag};
-  cudaEventRecord(r.start, ctx->stream);
-  f();
-  cudaEventRecord(r.stop, ctx->stream);
-  ctx->conv_records.push_back(r);
-}
-
 static void pick_tile(int oh, int ow, int* bw, int* bh) {
   long long best = -1;
   int bbw = 16;
@@ -474,7 +459,10 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     a.n_img = in.n;
     a.num_tiles = a.tiles_x * a.tiles_y * a.n_img * a.n_tiles;
     const double fl = (double)L.flops_per_px * oh * ow * in.n;
-    timed_launch(ctx, fl, [&] { launch_conv(tmA, tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream); });
+    ctx->launches++;
+    timed_launch(ctx, true, fl, 0.0, [&] {
+      launch_conv(tmA, tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
+    });
   } else {
     // The parity-split 5-D view has no batch axis: one tensor map per picture, kept in a
     // device array (from the caller's arena, ordered on its stream) that the producer indexes
@@ -492,7 +480,10 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     a.n_img = in.n;
     a.num_tiles = a.tiles_x * a.tiles_y * a.n_img * a.n_tiles;
     const double fl = (double)L.flops_per_px * oh * ow * in.n;
-    timed_launch(ctx, fl, [&] { launch_conv(maps[0], tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream); });
+    ctx->launches++;
+    timed_launch(ctx, true, fl, 0.0, [&] {
+      launch_conv(maps[0], tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
+    });
   }
   return cuda_check(cudaGetLastError(), "conv launch");
 }

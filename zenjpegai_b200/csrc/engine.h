@@ -72,25 +72,42 @@ struct Ctx {
   // driver entry point
   void* encode_fn = nullptr;
   int driver_version = 0;
-  // kernel timing (the crate's DecodeStats probe, per conv launch): when `profiling`, every
-  // conv launch is bracketed by two events and its algorithmic FLOPs are recorded
+  // kernel timing (the crate's DecodeStats probe, per launch): when `profiling`, every conv
+  // launch (and every memory-bound kernel of the networks) is bracketed by two events and its
+  // algorithmic FLOPs (conv) or bytes (the others) are recorded
   bool profiling = false;
   std::vector<cudaEvent_t> ev_pool;
   struct ConvRecord {
     cudaEvent_t start, stop;
-    double flops;
+    double flops, bytes;
     std::string tag;
+    bool conv;
   };
   std::vector<ConvRecord> conv_records;
   std::string tag;  // name of the layer being launched (for the profile report)
-  // per-tag totals accumulated by zjai_ctx_profile_read: launches, ms, flops
+  // per-tag totals accumulated by zjai_ctx_profile_read: launches, ms, flops, bytes
   struct TagTotal {
     long long launches = 0;
-    double ms = 0.0, flops = 0.0;
+    double ms = 0.0, flops = 0.0, bytes = 0.0;
   };
   std::vector<std::pair<std::string, TagTotal>> tag_totals;
   cudaEvent_t take_event();
 };
+
+// Launch `f` on ctx->stream; when profiling, bracket it with events and record its work
+// (algorithmic FLOPs for a conv, algorithmic bytes for a memory-bound kernel) under ctx->tag.
+template <class F>
+void timed_launch(Ctx* ctx, bool conv, double flops, double bytes, F&& f) {
+  if (!ctx->profiling) {
+    f();
+    return;
+  }
+  Ctx::ConvRecord r{ctx->take_event(), ctx->take_event(), flops, bytes, ctx->tag, conv};
+  cudaEventRecord(r.start, ctx->stream);
+  f();
+  cudaEventRecord(r.stop, ctx->stream);
+  ctx->conv_records.push_back(r);
+}
 
 // Allocate an NHWC f16 tensor in the arena; channels padded to `cpad` (multiple of 8), and
 // rows / cols rounded up to even so any stride-2 consumer can read it. Zero-filled when

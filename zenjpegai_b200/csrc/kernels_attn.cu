@@ -7,6 +7,8 @@
 #include "engine.h"
 #include "kernels_attn.h"
 
+#include <algorithm>
+
 namespace zjai {
 
 namespace {
@@ -128,25 +130,21 @@ struct DwShape {
   static constexpr int smem = SH * SW * G * 16;
 };
 
+// Spatial tile s of picture n at (ty, tx): s = (n * tiles_y + ty) * tiles_x + tx.
+struct DwTiles {
+  int tiles_x, tiles_y, count;
+};
+
+// Issue the cp.async copies of spatial tile `s` (channel block cb) into `buf`.
 template <bool GATE>
-__global__ void __launch_bounds__(256, 2)
-    dw3x3_kernel(const __half* __restrict__ x, __half* __restrict__ y, int h, int w, int c,
-                 long long xpix, long long xrow, long long ximg, long long ypix, long long yrow,
-                 long long yimg, const float* __restrict__ wt, int tiles_x, int tiles_y,
-                 int cblocks) {
+__device__ __forceinline__ void dw_stage(uint4* buf, const __half* __restrict__ x, int s,
+                                         const DwTiles& T, int cb, int h, int w, int c,
+                                         long long xpix, long long xrow, long long ximg) {
   using S = DwShape<GATE>;
-  extern __shared__ __align__(16) uint4 dw_tile[];
   const int cg_out = (GATE ? c / 2 : c) / 8;
-  int b = blockIdx.x;
-  const int cb = b % cblocks;
-  b /= cblocks;
-  const int tx = b % tiles_x;
-  b /= tiles_x;
-  const int ty = b % tiles_y;
-  const int n = b / tiles_y;
+  const int tx = s % T.tiles_x, ty = (s / T.tiles_x) % T.tiles_y, n = s / (T.tiles_x * T.tiles_y);
   const int x0 = tx * S::TW, y0 = ty * kDwTH;
   const __half* xb = x + n * ximg;
-
   for (int j = threadIdx.x; j < S::SH * S::SW * S::G; j += 256) {
     const int g = j % S::G;
     const int q = j / S::G;
@@ -155,65 +153,97 @@ __global__ void __launch_bounds__(256, 2)
     const int grp = cb * 8 + (g & 7);
     const int ch = (GATE && g >= 8 ? c / 2 : 0) + grp * 8;
     const bool ok = grp < cg_out && yy >= 0 && yy < h && xx >= 0 && xx < w;
-    cp_async16(dw_tile + j, ok ? xb + yy * xrow + xx * xpix + ch : x, ok ? 16 : 0);
+    cp_async16(buf + j, ok ? xb + yy * xrow + xx * xpix + ch : x, ok ? 16 : 0);
   }
+}
 
+// Persistent: block b keeps channel block cb = b % cblocks (its weights stay in registers) and
+// walks the spatial tiles s = b / cblocks, + gridDim.x / cblocks, ...; the copies of the next
+// tile run while the current one is computed (two shared-memory buffers).
+template <bool GATE>
+__global__ void __launch_bounds__(256, 2)
+    dw3x3_kernel(const __half* __restrict__ x, __half* __restrict__ y, int h, int w, int c,
+                 long long xpix, long long xrow, long long ximg, long long ypix, long long yrow,
+                 long long yimg, const float* __restrict__ wt, DwTiles T, int cblocks) {
+  using S = DwShape<GATE>;
+  extern __shared__ __align__(16) uint4 dw_tile[];
+  const int cg_out = (GATE ? c / 2 : c) / 8;
+  const int cb = blockIdx.x % cblocks;
+  const int sstep = gridDim.x / cblocks;
   const int g = threadIdx.x % S::G, xl = threadIdx.x / S::G;
   const int grp = cb * 8 + (g & 7);
   const bool gvalid = grp < cg_out;
   const int ch = (GATE && g >= 8 ? c / 2 : 0) + grp * 8;
+
+  int s = blockIdx.x / cblocks;
+  if (s < T.count) dw_stage<GATE>(dw_tile, x, s, T, cb, h, w, c, xpix, xrow, ximg);
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
   float wr[9][8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int t = 0; t < 9; ++t) wr[t][i] = gvalid ? __ldg(wt + (ch + i) * 9 + t) : 0.f;
-  asm volatile("cp.async.wait_all;\n" ::: "memory");
-  __syncthreads();
 
-  const bool xvalid = gvalid && x0 + xl < w;
-  __half* yb = y + n * yimg + (x0 + xl) * ypix + grp * 8;
-  float acc[3][8];
+  for (int it = 0; s < T.count; s += sstep, ++it) {
+    uint4* cur = dw_tile + (it & 1) * (S::smem / 16);
+    if (s + sstep < T.count)
+      dw_stage<GATE>(dw_tile + ((it + 1) & 1) * (S::smem / 16), x, s + sstep, T, cb, h, w, c,
+                     xpix, xrow, ximg);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    __syncthreads();
+
+    const int tx = s % T.tiles_x, ty = (s / T.tiles_x) % T.tiles_y;
+    const int n = s / (T.tiles_x * T.tiles_y);
+    const int x0 = tx * S::TW, y0 = ty * kDwTH;
+    const bool xvalid = gvalid && x0 + xl < w;
+    __half* yb = y + n * yimg + (x0 + xl) * ypix + grp * 8;
+    float acc[3][8];
 #pragma unroll
-  for (int k = 0; k < 3; ++k)
+    for (int k = 0; k < 3; ++k)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
+      for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
 #pragma unroll
-  for (int r = 0; r < S::SH; ++r) {
+    for (int r = 0; r < S::SH; ++r) {
 #pragma unroll
-    for (int kx = 0; kx < 3; ++kx) {
-      float v[8];
-      unpack8(dw_tile[(r * S::SW + xl + kx) * S::G + g], v);
+      for (int kx = 0; kx < 3; ++kx) {
+        float v[8];
+        unpack8(cur[(r * S::SW + xl + kx) * S::G + g], v);
 #pragma unroll
-      for (int ky = 0; ky < 3; ++ky) {
-        const int o = r - ky;
-        if (o >= 0 && o < kDwTH) {
+        for (int ky = 0; ky < 3; ++ky) {
+          const int o = r - ky;
+          if (o >= 0 && o < kDwTH) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[o % 3][i] = fmaf(wr[ky * 3 + kx][i], v[i], acc[o % 3][i]);
+            for (int i = 0; i < 8; ++i)
+              acc[o % 3][i] = fmaf(wr[ky * 3 + kx][i], v[i], acc[o % 3][i]);
+          }
         }
       }
-    }
-    if (r >= 2) {
-      const int o = r - 2;
-      float(&a)[8] = acc[o % 3];
-      if (GATE) {
-        float bv[8];
+      if (r >= 2) {
+        const int o = r - 2;
+        float(&a)[8] = acc[o % 3];
+        if (GATE) {
+          float bv[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) bv[i] = __shfl_down_sync(0xffffffffu, a[i], 8);
-        if (g < 8 && xvalid && y0 + o < h) {
+          for (int i = 0; i < 8; ++i) bv[i] = __shfl_down_sync(0xffffffffu, a[i], 8);
+          if (g < 8 && xvalid && y0 + o < h) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float e = a[i] > 0.f ? a[i] : expf(a[i]) - 1.f;
-            a[i] = e * bv[i];
+            for (int i = 0; i < 8; ++i) {
+              const float e = a[i] > 0.f ? a[i] : expf(a[i]) - 1.f;
+              a[i] = e * bv[i];
+            }
+            st8(yb + (y0 + o) * yrow, a);
           }
+        } else if (xvalid && y0 + o < h) {
           st8(yb + (y0 + o) * yrow, a);
         }
-      } else if (xvalid && y0 + o < h) {
-        st8(yb + (y0 + o) * yrow, a);
-      }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) a[i] = 0.f;
+        for (int i = 0; i < 8; ++i) a[i] = 0.f;
+      }
     }
+    __syncthreads();  // all reads of `cur` done before the next iteration refills it
   }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
 }
 
 // ---- channel attention -------------------------------------------------------------------
@@ -282,6 +312,96 @@ __global__ void attn_gram_kernel(const __half* __restrict__ qkv, int n_img, int 
   if (threadIdx.x < 2 * dim) atomicAdd(sq + (long long)n * 2 * dim + threadIdx.x, sqacc);
 }
 
+// Register-tiled Gram for head widths c with c % 4 == 0: thread = (head, 4 rows i, 4 columns
+// j) of G, block = heads * (c/4)^2 threads over a contiguous pixel range of one picture
+// (blockIdx.y). Pixels arrive in chunks of kGram2Pix as f16 [pixel][q | k] rows by 16-byte
+// cp.async copies, double-buffered so the next chunk lands while this one is summed. Each
+// pixel costs a thread two 8-byte shared loads and 16 FMAs; the threads of row block 0 (column
+// block 0) also sum k_j^2 (q_i^2). Partial sums go to gram / sq by atomics at the end.
+constexpr int kGram2Pix = 64;
+
+__global__ void __launch_bounds__(1024) attn_gram_tiled_kernel(
+    const __half* __restrict__ qkv, int npix, int w, int dim, int heads, long long pix,
+    long long row, long long img, float* __restrict__ gram, float* __restrict__ sq,
+    int px_per_block) {
+  extern __shared__ __align__(16) __half gsm[];  // [2][kGram2Pix][2 * dim]
+  const int n = blockIdx.y;
+  const int c = dim / heads, cb = c / 4;
+  const int hd = threadIdx.x / (cb * cb), ij = threadIdx.x % (cb * cb);
+  const int i0 = hd * c + (ij / cb) * 4, j0 = hd * c + (ij % cb) * 4;
+  const bool do_q = (ij % cb) == 0, do_k = (ij / cb) == 0;
+  const int rowh = 2 * dim;       // halves per staged pixel
+  const int groups = rowh / 8;    // 16-byte chunks per staged pixel
+  const __half* base = qkv + n * img;
+  const int p_begin = blockIdx.x * px_per_block;
+  const int p_end = min(npix, p_begin + px_per_block);
+  const int nchunks = (p_end - p_begin + kGram2Pix - 1) / kGram2Pix;
+
+  auto stage = [&](int chunk, int buf) {
+    __half* dst = gsm + buf * kGram2Pix * rowh;
+    const int p0 = p_begin + chunk * kGram2Pix;
+    for (int t = threadIdx.x; t < kGram2Pix * groups; t += blockDim.x) {
+      const int pp = t / groups, g = t % groups;
+      const int p = p0 + pp;
+      const bool ok = p < p_end;
+      cp_async16(dst + pp * rowh + g * 8, ok ? base + (p / w) * row + (p % w) * pix + g * 8 : qkv,
+                 ok ? 16 : 0);
+    }
+  };
+
+  float acc[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+  float qs[4] = {0.f, 0.f, 0.f, 0.f}, ks[4] = {0.f, 0.f, 0.f, 0.f};
+  if (nchunks > 0) stage(0, 0);
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  for (int ch = 0; ch < nchunks; ++ch) {
+    if (ch + 1 < nchunks) stage(ch + 1, (ch + 1) & 1);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    __syncthreads();
+    const __half* src = gsm + (ch & 1) * kGram2Pix * rowh;
+#pragma unroll 4
+    for (int pp = 0; pp < kGram2Pix; ++pp) {
+      const uint2 uq = *reinterpret_cast<const uint2*>(src + pp * rowh + i0);
+      const uint2 uk = *reinterpret_cast<const uint2*>(src + pp * rowh + dim + j0);
+      const float2 q01 = __half22float2(*reinterpret_cast<const __half2*>(&uq.x));
+      const float2 q23 = __half22float2(*reinterpret_cast<const __half2*>(&uq.y));
+      const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&uk.x));
+      const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&uk.y));
+      const float q[4] = {q01.x, q01.y, q23.x, q23.y}, k[4] = {k01.x, k01.y, k23.x, k23.y};
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(q[a], k[b], acc[a][b]);
+      if (do_q) {
+#pragma unroll
+        for (int a = 0; a < 4; ++a) qs[a] = fmaf(q[a], q[a], qs[a]);
+      }
+      if (do_k) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) ks[b] = fmaf(k[b], k[b], ks[b]);
+      }
+    }
+    __syncthreads();  // all reads of this buffer done before it is refilled
+  }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+  float* gn = gram + (long long)n * dim * c;
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) atomicAdd(gn + (i0 + a) * c + (j0 - hd * c) + b, acc[a][b]);
+  float* sn = sq + (long long)n * 2 * dim;
+  if (do_q)
+#pragma unroll
+    for (int a = 0; a < 4; ++a) atomicAdd(sn + i0 + a, qs[a]);
+  if (do_k)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) atomicAdd(sn + dim + j0 + b, ks[b]);
+}
+
 // attn[n][h][i][j] = softmax_j( G_ij / (max(|q_i|, eps) max(|k_j|, eps)) * T[h] )
 __global__ void attn_softmax_kernel(const float* __restrict__ gram, const float* __restrict__ sq,
                                     const float* __restrict__ temp, float* __restrict__ attn,
@@ -342,6 +462,55 @@ __global__ void __launch_bounds__(256) attn_apply_kernel(
   st8(out + n * oimg + py * orow + px * opix + i0, o);
 }
 
+// out[p][h*C+i] = sum_j attn[h][i][j] * v[p][h*C+j] for head width C (16 or 32): thread =
+// (pixel, head), warp = 32 pixels of one head, so every shared-memory read of the attention
+// matrix is a broadcast; v is read once. Block = 256 threads = 8 warps over heads x pixels.
+template <int C>
+__global__ void __launch_bounds__(256) attn_apply_head_kernel(
+    const __half* __restrict__ qkv, const float* __restrict__ attn, __half* __restrict__ out,
+    int h, int w, int dim, int heads, long long pix, long long row, long long img, long long opix,
+    long long orow, long long oimg) {
+  extern __shared__ __align__(16) float sa[];  // [heads][C][C] of picture n
+  const int n = blockIdx.y;
+  for (int t = threadIdx.x; t < dim * C; t += blockDim.x) sa[t] = attn[(long long)n * dim * C + t];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hd = warp % heads;
+  const int pw = 8 / heads;  // pixel warps per block
+  const long long p = ((long long)blockIdx.x * pw + warp / heads) * 32 + lane;
+  if (warp >= pw * heads || p >= (long long)h * w) return;
+  const int py = (int)(p / w), px = (int)(p % w);
+  const __half* vp = qkv + n * img + py * row + px * pix + 2 * dim + hd * C;
+  float v[C];
+#pragma unroll
+  for (int j0 = 0; j0 < C; j0 += 8) {
+    float t8[8];
+    ld8(vp + j0, t8);
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) v[j0 + jj] = t8[jj];
+  }
+  const float* A = sa + hd * C * C;
+  __half* op = out + n * oimg + py * orow + px * opix + hd * C;
+#pragma unroll
+  for (int i0 = 0; i0 < C; i0 += 8) {
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < C; j += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(A + (i0 + i) * C + j);
+        s = fmaf(a4.x, v[j], s);
+        s = fmaf(a4.y, v[j + 1], s);
+        s = fmaf(a4.z, v[j + 2], s);
+        s = fmaf(a4.w, v[j + 3], s);
+      }
+      o[i] = s;
+    }
+    st8(op + i0, o);
+  }
+}
+
 // planar f32 latent [C][LH][LW] -> NHWC f16 [n][h][w] at channel offset; per-image window
 // origins (x, y) in `origin` (device int pairs).
 __global__ void gather_latent_kernel(const float* __restrict__ src, int C, int LH, int LW,
@@ -373,27 +542,37 @@ void launch_layer_norm(const TView& x, const TView& y, const float* gamma, const
                                                           gamma, beta);
 }
 
-void launch_dw3x3(const TView& x, const TView& y, const float* wt, bool gate, cudaStream_t s) {
-  const int cg_out = (gate ? x.c / 2 : x.c) / 8;
-  const int cblocks = (cg_out + 7) / 8;
-  const int tiles_y = (x.h + kDwTH - 1) / kDwTH;
-  if (gate) {
-    using S = DwShape<true>;
-    const int tiles_x = (x.w + S::TW - 1) / S::TW;
-    dw3x3_kernel<true><<<x.n * tiles_y * tiles_x * cblocks, 256, S::smem, s>>>(
-        x.p, y.p, x.h, x.w, x.c, x.pix, x.row, x.img, y.pix, y.row, y.img, wt, tiles_x, tiles_y,
-        cblocks);
-  } else {
-    using S = DwShape<false>;
-    const int tiles_x = (x.w + S::TW - 1) / S::TW;
-    dw3x3_kernel<false><<<x.n * tiles_y * tiles_x * cblocks, 256, S::smem, s>>>(
-        x.p, y.p, x.h, x.w, x.c, x.pix, x.row, x.img, y.pix, y.row, y.img, wt, tiles_x, tiles_y,
-        cblocks);
+template <bool GATE>
+static void launch_dw3x3_t(const TView& x, const TView& y, const float* wt, int sms,
+                           cudaStream_t s) {
+  using S = DwShape<GATE>;
+  static bool attr_set = false;  // two tile buffers exceed the default 48 KB window
+  if (!attr_set) {
+    cudaFuncSetAttribute(dw3x3_kernel<GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         2 * S::smem);
+    attr_set = true;
   }
+  const int cg_out = (GATE ? x.c / 2 : x.c) / 8;
+  const int cblocks = (cg_out + 7) / 8;
+  DwTiles T;
+  T.tiles_x = (x.w + S::TW - 1) / S::TW;
+  T.tiles_y = (x.h + kDwTH - 1) / kDwTH;
+  T.count = x.n * T.tiles_x * T.tiles_y;
+  const int per = std::max(1, std::min(T.count, 2 * sms / cblocks));  // two CTAs per SM
+  dw3x3_kernel<GATE><<<cblocks * per, 256, 2 * S::smem, s>>>(
+      x.p, y.p, x.h, x.w, x.c, x.pix, x.row, x.img, y.pix, y.row, y.img, wt, T, cblocks);
+}
+
+void launch_dw3x3(const TView& x, const TView& y, const float* wt, bool gate, int sms,
+                  cudaStream_t s) {
+  if (gate)
+    launch_dw3x3_t<true>(x, y, wt, sms, s);
+  else
+    launch_dw3x3_t<false>(x, y, wt, sms, s);
 }
 
 void launch_attention(const TView& qkv, const TView& out, int heads, const float* temp,
-                      float* scratch, cudaStream_t s) {
+                      float* scratch, int sms, cudaStream_t s) {
   const int dim = qkv.c / 3;
   const int c = dim / heads;
   const int n = qkv.n;
@@ -402,16 +581,50 @@ void launch_attention(const TView& qkv, const TView& out, int heads, const float
   float* attn = sq + (size_t)n * 2 * dim;             // n * dim * c
   cudaMemsetAsync(gram, 0, sizeof(float) * ((size_t)n * dim * c + (size_t)n * 2 * dim), s);
   const int npix = qkv.h * qkv.w;
-  const int chunks = (npix + kGramPix - 1) / kGramPix;
-  const int cpb = std::max(1, chunks / 64);
-  dim3 g1((chunks + cpb - 1) / cpb, n);
-  attn_gram_kernel<<<g1, 256, kGramPix * 2 * dim * sizeof(float), s>>>(
-      qkv.p, n, npix, qkv.w, dim, heads, qkv.pix, qkv.row, qkv.img, gram, sq, cpb);
+  const int gram_threads = heads * (c / 4) * (c / 4);
+  if (c % 4 == 0 && dim <= 256 && gram_threads >= 32 && gram_threads <= 1024 &&
+      gram_threads % 32 == 0) {
+    const int smem = 2 * kGram2Pix * 2 * dim * (int)sizeof(__half);
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(attn_gram_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           2 * kGram2Pix * 2 * 256 * (int)sizeof(__half));
+      attr_set = true;
+    }
+    // about four blocks per SM over the whole batch, whole chunks per block
+    const int chunks = (npix + kGram2Pix - 1) / kGram2Pix;
+    const int splits = std::max(1, std::min(chunks, (4 * sms + n - 1) / n));
+    const int px_per_block = ((chunks + splits - 1) / splits) * kGram2Pix;
+    dim3 g1((npix + px_per_block - 1) / px_per_block, n);
+    attn_gram_tiled_kernel<<<g1, gram_threads, smem, s>>>(qkv.p, npix, qkv.w, dim, heads,
+                                                          qkv.pix, qkv.row, qkv.img, gram, sq,
+                                                          px_per_block);
+  } else {
+    const int chunks = (npix + kGramPix - 1) / kGramPix;
+    const int cpb = std::max(1, chunks / 64);
+    dim3 g1((chunks + cpb - 1) / cpb, n);
+    attn_gram_kernel<<<g1, 256, kGramPix * 2 * dim * sizeof(float), s>>>(
+        qkv.p, n, npix, qkv.w, dim, heads, qkv.pix, qkv.row, qkv.img, gram, sq, cpb);
+  }
   attn_softmax_kernel<<<blocks_for((long long)n * dim, 128), 128, 0, s>>>(gram, sq, temp, attn, n,
                                                                          dim, heads);
-  dim3 g3(blocks_for((long long)npix, 256), dim / 8, n);
-  attn_apply_kernel<<<g3, 256, 0, s>>>(qkv.p, attn, out.p, n, qkv.h, qkv.w, dim, heads, qkv.pix,
-                                       qkv.row, qkv.img, out.pix, out.row, out.img);
+  if ((c == 16 || c == 32) && 8 % heads == 0) {
+    const int px_per_block = 32 * (8 / heads);
+    dim3 g3(blocks_for((long long)npix, px_per_block), n);
+    const size_t smem = sizeof(float) * dim * c;
+    if (c == 32)
+      attn_apply_head_kernel<32><<<g3, 256, smem, s>>>(qkv.p, attn, out.p, qkv.h, qkv.w, dim,
+                                                       heads, qkv.pix, qkv.row, qkv.img, out.pix,
+                                                       out.row, out.img);
+    else
+      attn_apply_head_kernel<16><<<g3, 256, smem, s>>>(qkv.p, attn, out.p, qkv.h, qkv.w, dim,
+                                                       heads, qkv.pix, qkv.row, qkv.img, out.pix,
+                                                       out.row, out.img);
+  } else {
+    dim3 g3(blocks_for((long long)npix, 256), dim / 8, n);
+    attn_apply_kernel<<<g3, 256, 0, s>>>(qkv.p, attn, out.p, n, qkv.h, qkv.w, dim, heads,
+                                         qkv.pix, qkv.row, qkv.img, out.pix, out.row, out.img);
+  }
 }
 
 size_t attention_scratch_floats(int n_img, int dim, int heads) {

@@ -373,35 +373,43 @@ int Runner::tb(const std::string& p, const TView& x) {
   ZJAI_TRY(alloc(x.h, x.w, 3 * d, &qkv));
   ZJAI_TRY(alloc(x.h, x.w, 3 * d, &qkv2));
   ZJAI_TRY(alloc(x.h, x.w, d, &att));
-  launch_layer_norm(x, ln, vec(p + ".prep_data.norm1.weight"), vec(p + ".prep_data.norm1.bias"),
-                    stream);
-  ctx->launches++;
+  // algorithmic bytes per pixel of a d-channel f16 map
+  const double px = (double)n * x.h * x.w, b16 = 2.0 * px;
+  mem_kernel(p + ".prep_data.norm1", "ln", 2 * b16 * d, 1, [&] {
+    launch_layer_norm(x, ln, vec(p + ".prep_data.norm1.weight"),
+                      vec(p + ".prep_data.norm1.bias"), stream);
+  });
   ConvOut o;
   o.out = qkv;
   ZJAI_TRY(conv(p + ".prep_data.conv1", ln, o));
-  launch_dw3x3(qkv, qkv2, vec(p + ".prep_data.conv2"), false, stream);
-  ctx->launches++;
+  mem_kernel(p + ".prep_data.conv2", "dw", 2 * b16 * 3 * d, 1, [&] {
+    launch_dw3x3(qkv, qkv2, vec(p + ".prep_data.conv2"), false, ctx->sms, stream);
+  });
   float* scratch = static_cast<float*>(
       arena->alloc(attention_scratch_floats(n, d, 4) * sizeof(float)));
   if (!scratch) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (attention scratch)");
-  launch_attention(qkv2, att, 4, vec(p + ".attn.temperature"), scratch, stream);
-  ctx->launches += 3;
+  // Gram reads q and k, the apply reads v and writes the output
+  mem_kernel(p + ".attn", "attn", b16 * 4 * d, 3, [&] {
+    launch_attention(qkv2, att, 4, vec(p + ".attn.temperature"), scratch, ctx->sms, stream);
+  });
   if (count_flops) flops += 2.0 * 2.0 * (double)n * x.h * x.w * d * (d / 4);
   ConvOut oa;
   oa.out = x;
   oa.op = OP_ADD;
   oa.r1 = &x;
   ZJAI_TRY(conv(p + ".attn.project_out", att, oa));
-  launch_layer_norm(x, ln, vec(p + ".ffn.norm1.weight"), vec(p + ".ffn.norm1.bias"), stream);
-  ctx->launches++;
+  mem_kernel(p + ".ffn.norm1", "ln", 2 * b16 * d, 1, [&] {
+    launch_layer_norm(x, ln, vec(p + ".ffn.norm1.weight"), vec(p + ".ffn.norm1.bias"), stream);
+  });
   TView f, g;
   ZJAI_TRY(alloc(x.h, x.w, 2 * hidden, &f));
   ZJAI_TRY(alloc(x.h, x.w, hidden, &g));
   ConvOut oi;
   oi.out = f;
   ZJAI_TRY(conv(p + ".ffn.project_in", ln, oi));
-  launch_dw3x3(f, g, vec(p + ".ffn.dwconv"), true, stream);
-  ctx->launches++;
+  mem_kernel(p + ".ffn.dwconv", "dw", b16 * 3 * hidden, 1, [&] {
+    launch_dw3x3(f, g, vec(p + ".ffn.dwconv"), true, ctx->sms, stream);
+  });
   ConvOut of;
   of.out = x;
   of.op = OP_ADD;

@@ -44,6 +44,17 @@ struct Runner {
   const ConvLayer* layer(const std::string& name);
   int conv(const std::string& name, const TView& in, ConvOut o);
   std::string kind_tag() const;
+  // A memory-bound kernel (`launches` launches issued by `f` on this runner's stream), profiled
+  // under "<kind tag><name>[<kind>]" with its algorithmic bytes.
+  template <class F>
+  void mem_kernel(const std::string& name, const char* kind, double bytes, int launches, F&& f) {
+    cudaStream_t saved = ctx->stream;
+    ctx->stream = stream;
+    if (ctx->profiling) ctx->tag = kind_tag() + name + "[" + kind + "]";
+    timed_launch(ctx, false, 0.0, bytes, f);
+    ctx->stream = saved;
+    ctx->launches += launches;
+  }
   int out_extent(const std::string& name, int h, int w, int* oh, int* ow);
   int stop_check();
 

@@ -375,7 +375,7 @@ int zjai_channel_attention(zjai_ctx* ctx, const float* qkv, int c3, int h, int w
   float* scratch =
       static_cast<float*>(ctx->arena.alloc(attention_scratch_floats(1, dim, heads) * sizeof(float)));
   if (!scratch) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (attention)");
-  launch_attention(t, o, heads, dt, scratch, ctx->stream);
+  launch_attention(t, o, heads, dt, scratch, ctx->sms, ctx->stream);
   float* dout;
   ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)dim * h * w, mem, &dout));
   launch_nhwc_to_planar(o, dout, ctx->stream);
@@ -395,7 +395,7 @@ int zjai_depthwise3x3(zjai_ctx* ctx, const float* x, int c, int h, int w, const 
   TView t, o;
   ZJAI_TRY(planar_to_tensor(ctx, dx, c, h, w, &t));
   ZJAI_TRY(alloc_tensor(ctx, 1, h, w, c, &o));
-  launch_dw3x3(t, o, dw, false, ctx->stream);
+  launch_dw3x3(t, o, dw, false, ctx->sms, ctx->stream);
   float* dout;
   ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)c * h * w, mem, &dout));
   launch_nhwc_to_planar(o, dout, ctx->stream);
