@@ -1,9 +1,13 @@
-"""Layer-level timing of the tcgen05 convolution kernel (`zjai_conv_bench`).
+"""Layer-level timing of the tcgen05 convolution kernel (`zjai_conv_bench`) and of the
+memory-bound kernels of the HOP transformer blocks (`zjai_kernel_bench`).
 
 The GPU counterpart of the crate's conv microbenchmark (benches/conv_kernels.rs:165-187): the
 BOP luma layer shapes at the latent size 131x88, plus the HOP shapes of a 4K picture's 28
-interior 512x512 tiles run as one batch. Prints one line per layer (ms, TFLOP/s, fraction of
-the measured bf16 peak). Usage: python -m zenjpegai_b200.conv_bench [--only NAME] [--reps R]
+interior 512x512 tiles run as one batch. Prints one line per layer: ms and TFLOP/s against
+the measured bf16 peak (convolutions), or GB/s of algorithmic traffic against the measured
+HBM copy bandwidth (the others).
+
+Usage: python -m zenjpegai_b200.conv_bench [--only NAME] [--reps R] [--arena-gib G]
 """
 
 import argparse
@@ -31,25 +35,35 @@ LAYERS = [
     ("hop_subscale_s2_128@H4x1", 1, 128, 128, 128, 128, 3, 2, 1, 0, 0),
 ]
 
+KB_DW, KB_DW_GATE, KB_LN, KB_ATTN = 0, 1, 2, 3
+# name, kind, n, h, w, c (HOP luma transformer blocks at 1/4 scale: dim 128, hidden 512)
+KERNELS = [
+    ("hop_ffn_dwgate_1024@H4x28", KB_DW_GATE, 28, 128, 128, 1024),
+    ("hop_qkv_dw_384@H4x28", KB_DW, 28, 128, 128, 384),
+    ("hop_ln_128@H4x28", KB_LN, 28, 128, 128, 128),
+    ("hop_attn_128@H4x28", KB_ATTN, 28, 128, 128, 128),
+    ("hop_uv_attn_64@H4x28", KB_ATTN, 28, 128, 128, 64),
+]
 
-def peak():
+
+def _peaks():
     try:
         with open(os.path.join(os.path.dirname(__file__), "..", "MEASURED_PEAKS.json")) as f:
-            return float(json.load(f)["bf16_tflops"])
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
     except Exception:
-        return 1590.0
+        return 1590.0, 6650.0, "fallback"
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None)
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--arena-gib", type=int, default=16)
     args = ap.parse_args()
     L = _lib.lib()
-    L.zjai_conv_bench.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 11 + [
-        ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
-    eng = Engine(0, arena_bytes=16 << 30)
-    pk = peak()
+    eng = Engine(0, arena_bytes=args.arena_gib << 30)
+    pk, hbm, src = _peaks()
     for row in LAYERS:
         name = row[0]
         if args.only and args.only not in name:
@@ -58,8 +72,18 @@ def main():
         _lib.check(L.zjai_conv_bench(eng.handle, *row[1:], args.reps, ctypes.byref(ms),
                                      ctypes.byref(fl)))
         tf = fl.value / (ms.value * 1e-3) / 1e12
-        print("%-32s %8.3f ms %8.1f TFLOP/s %6.1f%% of %.0f" % (name, ms.value, tf,
-                                                               100 * tf / pk, pk), flush=True)
+        print("%-32s %8.3f ms %8.1f TFLOP/s %6.1f%% of %.0f (%s)" % (
+            name, ms.value, tf, 100 * tf / pk, pk, src), flush=True)
+    for row in KERNELS:
+        name = row[0]
+        if args.only and args.only not in name:
+            continue
+        ms, by = ctypes.c_double(), ctypes.c_double()
+        _lib.check(L.zjai_kernel_bench(eng.handle, *row[1:], args.reps, ctypes.byref(ms),
+                                       ctypes.byref(by)))
+        gbs = by.value / (ms.value * 1e-3) / 1e9
+        print("%-32s %8.3f ms %8.0f GB/s    %6.1f%% of %.0f (%s)" % (
+            name, ms.value, gbs, 100 * gbs / hbm, hbm, src), flush=True)
     eng.close()
 
 

@@ -1,9 +1,11 @@
-// Layer-level timing harness: the GPU counterpart of the crate's benches/conv_kernels.rs
-// (PackedConv::new + forward on network layer shapes), timing conv_tc_kernel alone.
+// Layer-level timing harnesses: the GPU counterpart of the crate's benches/conv_kernels.rs
+// (PackedConv::new + forward on network layer shapes), timing conv_tc_kernel alone, and the
+// same for the memory-bound kernels of the transformer blocks.
 #include <random>
 #include <vector>
 
 #include "api_common.h"
+#include "kernels_attn.h"
 
 namespace zjai {
 namespace {
@@ -76,5 +78,65 @@ extern "C" int zjai_conv_bench(zjai_ctx* ctx, int n, int h, int w, int cin, int 
   cudaEventDestroy(e1);
   *ms = (double)t / reps;
   if (flops) *flops = (double)L.flops_per_px * oh * ow * n;
+  return ctx_check_status(ctx);
+}
+
+extern "C" int zjai_kernel_bench(zjai_ctx* ctx, int kind, int n, int h, int w, int c, int reps,
+                                 double* ms, double* bytes) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (kind < ZJAI_KB_DW || kind > ZJAI_KB_ATTN || n <= 0 || h <= 0 || w <= 0 || c <= 0 ||
+      c % 8 || reps <= 0 || !ms)
+    return fail(ZJAI_INVALID_ARGUMENT, "kernel_bench: bad arguments");
+  if ((kind == ZJAI_KB_DW_GATE && c % 16) || (kind == ZJAI_KB_LN && c > 512) ||
+      (kind == ZJAI_KB_ATTN && c % 4))
+    return fail(ZJAI_UNSUPPORTED, "kernel_bench: channel count not supported by this kernel");
+  ArenaScope scope(ctx);
+  const int cin = kind == ZJAI_KB_ATTN ? 3 * c : c;
+  const int cout = kind == ZJAI_KB_DW_GATE ? c / 2 : c;
+  TView x, y;
+  ZJAI_TRY(alloc_tensor(ctx, n, h, w, cin, &x));
+  ZJAI_TRY(alloc_tensor(ctx, n, h, w, cout, &y));
+  fill_kernel<<<1024, 256, 0, ctx->stream>>>(x.p, (long long)n * x.img, 17u);
+  // per-channel parameters: depthwise weights [c][9], or gamma / beta, or the temperatures
+  std::vector<float> hp((size_t)c * 9 + 2 * c + 4);
+  std::mt19937 rng(99);
+  std::uniform_real_distribution<float> ud(-0.3f, 0.3f);
+  for (auto& v : hp) v = ud(rng);
+  for (int i = 0; i < 4; ++i) hp[(size_t)c * 9 + 2 * c + i] = 1.f + 0.25f * i;
+  float* dp = static_cast<float*>(ctx->arena.alloc(hp.size() * sizeof(float)));
+  float* scratch = static_cast<float*>(
+      ctx->arena.alloc(attention_scratch_floats(n, c, 4) * sizeof(float)));
+  if (!dp || !scratch) return fail(ZJAI_LIMIT_EXCEEDED, "kernel_bench: arena exhausted");
+  ZJAI_TRY(cuda_check(cudaMemcpyAsync(dp, hp.data(), hp.size() * sizeof(float),
+                                      cudaMemcpyHostToDevice, ctx->stream),
+                      "kernel_bench params"));
+  const float* wt = dp;
+  const float* gamma = dp + (size_t)c * 9;
+  const float* temp = gamma + 2 * c;
+  auto run = [&] {
+    switch (kind) {
+      case ZJAI_KB_DW: launch_dw3x3(x, y, wt, false, ctx->sms, ctx->stream); break;
+      case ZJAI_KB_DW_GATE: launch_dw3x3(x, y, wt, true, ctx->sms, ctx->stream); break;
+      case ZJAI_KB_LN: launch_layer_norm(x, y, gamma, gamma + c, ctx->stream); break;
+      default: launch_attention(x, y, 4, temp, scratch, ctx->sms, ctx->stream); break;
+    }
+  };
+  run();  // warm-up
+  cudaEvent_t e0, e1;
+  ZJAI_TRY(cuda_check(cudaEventCreate(&e0), "event"));
+  ZJAI_TRY(cuda_check(cudaEventCreate(&e1), "event"));
+  cudaEventRecord(e0, ctx->stream);
+  for (int i = 0; i < reps; ++i) run();
+  cudaEventRecord(e1, ctx->stream);
+  ZJAI_TRY(cuda_check(cudaEventSynchronize(e1), "event sync"));
+  float t = 0.f;
+  cudaEventElapsedTime(&t, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  ZJAI_TRY(cuda_check(cudaGetLastError(), "kernel_bench launch"));
+  *ms = (double)t / reps;
+  // attention reads q, k (Gram) and v (apply) and writes the output
+  const double px = (double)n * h * w;
+  if (bytes) *bytes = 2.0 * px * (kind == ZJAI_KB_ATTN ? 4.0 * c : (double)(cin + cout));
   return ctx_check_status(ctx);
 }

@@ -141,21 +141,41 @@ __device__ __forceinline__ void dw_stage(uint4* buf, const __half* __restrict__ 
                                          const DwTiles& T, int cb, int h, int w, int c,
                                          long long xpix, long long xrow, long long ximg) {
   using S = DwShape<GATE>;
+  constexpr int P = 256 / S::G;  // positions advanced per pass (< SW)
   const int cg_out = (GATE ? c / 2 : c) / 8;
   const int tx = s % T.tiles_x, ty = (s / T.tiles_x) % T.tiles_y, n = s / (T.tiles_x * T.tiles_y);
   const int x0 = tx * S::TW, y0 = ty * kDwTH;
-  const __half* xb = x + n * ximg;
-  for (int j = threadIdx.x; j < S::SH * S::SW * S::G; j += 256) {
-    const int g = j % S::G;
-    const int q = j / S::G;
-    const int cx = q % S::SW, r = q / S::SW;
+  // thread = (channel group g, first position q0); position q = r * SW + cx
+  const int g = threadIdx.x % S::G;
+  const int grp = cb * 8 + (g & 7);
+  const bool gok = grp < cg_out;
+  const __half* xb = x + n * ximg + (GATE && g >= 8 ? c / 2 : 0) + grp * 8;
+  int cx = threadIdx.x / S::G, r = 0;
+  for (int q = cx; q < S::SH * S::SW; q += P) {
     const int yy = y0 - 1 + r, xx = x0 - 1 + cx;
-    const int grp = cb * 8 + (g & 7);
-    const int ch = (GATE && g >= 8 ? c / 2 : 0) + grp * 8;
-    const bool ok = grp < cg_out && yy >= 0 && yy < h && xx >= 0 && xx < w;
-    cp_async16(buf + j, ok ? xb + yy * xrow + xx * xpix + ch : x, ok ? 16 : 0);
+    const bool ok = gok && yy >= 0 && yy < h && xx >= 0 && xx < w;
+    cp_async16(buf + q * S::G + g, ok ? xb + yy * xrow + xx * xpix : x, ok ? 16 : 0);
+    cx += P;
+    if (cx >= S::SW) {
+      cx -= S::SW;
+      ++r;
+    }
   }
 }
+
+// Packed f32 pair FMA (sm_100 FFMA2): per lane exactly fmaf(a, b, c).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long d, ua, ub, uc;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ua) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ub) : "f"(b.x), "f"(b.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(uc) : "f"(c.x), "f"(c.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(ua), "l"(ub), "l"(uc));
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+  return r;
+}
+
+__device__ __forceinline__ float elu1(float a) { return a > 0.f ? a : __expf(a) - 1.f; }
 
 // Persistent: block b keeps channel block cb = b % cblocks (its weights stay in registers) and
 // walks the spatial tiles s = b / cblocks, + gridDim.x / cblocks, ...; the copies of the next
@@ -178,11 +198,14 @@ __global__ void __launch_bounds__(256, 2)
   int s = blockIdx.x / cblocks;
   if (s < T.count) dw_stage<GATE>(dw_tile, x, s, T, cb, h, w, c, xpix, xrow, ximg);
   asm volatile("cp.async.commit_group;\n" ::: "memory");
-  float wr[9][8];
+  float2 wr[9][4];  // channel pairs (2k, 2k + 1)
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int k = 0; k < 4; ++k)
 #pragma unroll
-    for (int t = 0; t < 9; ++t) wr[t][i] = gvalid ? __ldg(wt + (ch + i) * 9 + t) : 0.f;
+    for (int t = 0; t < 9; ++t)
+      wr[t][k] = gvalid ? make_float2(__ldg(wt + (ch + 2 * k) * 9 + t),
+                                      __ldg(wt + (ch + 2 * k + 1) * 9 + t))
+                        : make_float2(0.f, 0.f);
 
   for (int it = 0; s < T.count; s += sstep, ++it) {
     uint4* cur = dw_tile + (it & 1) * (S::smem / 16);
@@ -197,48 +220,70 @@ __global__ void __launch_bounds__(256, 2)
     const int n = s / (T.tiles_x * T.tiles_y);
     const int x0 = tx * S::TW, y0 = ty * kDwTH;
     const bool xvalid = gvalid && x0 + xl < w;
-    __half* yb = y + n * yimg + (x0 + xl) * ypix + grp * 8;
-    float acc[3][8];
+    // gate: the first-half thread writes output channels 0..3 of the group, the second-half
+    // thread channels 4..7
+    const bool hi = GATE && g >= 8;
+    __half* yb = y + n * yimg + (x0 + xl) * ypix + grp * 8 + (hi ? 4 : 0);
+    float2 acc[3][4];
 #pragma unroll
     for (int k = 0; k < 3; ++k)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
+      for (int i = 0; i < 4; ++i) acc[k][i] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int r = 0; r < S::SH; ++r) {
 #pragma unroll
       for (int kx = 0; kx < 3; ++kx) {
-        float v[8];
-        unpack8(cur[(r * S::SW + xl + kx) * S::G + g], v);
+        const uint4 u = cur[(r * S::SW + xl + kx) * S::G + g];
+        const __half2* hv = reinterpret_cast<const __half2*>(&u);
+        float2 v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __half22float2(hv[i]);
 #pragma unroll
         for (int ky = 0; ky < 3; ++ky) {
           const int o = r - ky;
           if (o >= 0 && o < kDwTH) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              acc[o % 3][i] = fmaf(wr[ky * 3 + kx][i], v[i], acc[o % 3][i]);
+            for (int i = 0; i < 4; ++i)
+              acc[o % 3][i] = ffma2(wr[ky * 3 + kx][i], v[i], acc[o % 3][i]);
           }
         }
       }
       if (r >= 2) {
         const int o = r - 2;
-        float(&a)[8] = acc[o % 3];
+        float2(&a)[4] = acc[o % 3];
+        const bool store = xvalid && y0 + o < h;
         if (GATE) {
-          float bv[8];
+          // swap halves with the partner 8 lanes away: the first-half thread sends pairs 2, 3
+          // and receives the second half's pairs 0, 1 (and the other way round)
+          float2 snd[2] = {hi ? a[0] : a[2], hi ? a[1] : a[3]}, rcv[2];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) bv[i] = __shfl_down_sync(0xffffffffu, a[i], 8);
-          if (g < 8 && xvalid && y0 + o < h) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float e = a[i] > 0.f ? a[i] : expf(a[i]) - 1.f;
-              a[i] = e * bv[i];
-            }
-            st8(yb + (y0 + o) * yrow, a);
+          for (int i = 0; i < 2; ++i) {
+            rcv[i].x = __shfl_xor_sync(0xffffffffu, snd[i].x, 8);
+            rcv[i].y = __shfl_xor_sync(0xffffffffu, snd[i].y, 8);
           }
-        } else if (xvalid && y0 + o < h) {
-          st8(yb + (y0 + o) * yrow, a);
+          if (store) {
+            float o4[4];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const float2 e = hi ? rcv[i] : a[i];      // first-half (ELU) operand
+              const float2 m = hi ? a[2 + i] : rcv[i];  // second-half (multiplier) operand
+              o4[2 * i] = elu1(e.x) * m.x;
+              o4[2 * i + 1] = elu1(e.y) * m.y;
+            }
+            uint2 pk;
+            *reinterpret_cast<__half2*>(&pk.x) = __floats2half2_rn(o4[0], o4[1]);
+            *reinterpret_cast<__half2*>(&pk.y) = __floats2half2_rn(o4[2], o4[3]);
+            *reinterpret_cast<uint2*>(yb + (y0 + o) * yrow) = pk;
+          }
+        } else if (store) {
+          uint4 pk;
+          __half2* ph = reinterpret_cast<__half2*>(&pk);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) ph[i] = __floats2half2_rn(a[i].x, a[i].y);
+          *reinterpret_cast<uint4*>(yb + (y0 + o) * yrow) = pk;
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) a[i] = 0.f;
+        for (int i = 0; i < 4; ++i) a[i] = make_float2(0.f, 0.f);
       }
     }
     __syncthreads();  // all reads of `cur` done before the next iteration refills it
