@@ -161,11 +161,14 @@ def test_output_stage_bit_exact(eng):
     assert np.array_equal(rgb.astype(np.uint16), want)
 
 
-def test_layer_norm(eng):
+@pytest.mark.parametrize("c", [128, 64, 40, 200, 384])
+def test_layer_norm(eng, c):
+    # c <= 256: pixel-segment kernel (8 / 16 / 32 lanes per pixel, idle lanes at 40 and 200);
+    # 384: warp-per-pixel kernel
     from zenjpegai_b200 import synthetic as syn
-    x = syn.normal(5, "x", (128, 23, 37), std=3.0, mean=0.5)
-    wt = syn.normal(5, "w", (128,), std=0.1, mean=1.0)
-    b = syn.normal(5, "b", (128,), std=0.05)
+    x = syn.normal(5, "x", (c, 23, 37), std=3.0, mean=0.5)
+    wt = syn.normal(5, "w", (c,), std=0.1, mean=1.0)
+    b = syn.normal(5, "b", (c,), std=0.05)
     assert rel_l2(eng.layer_norm(x, wt, b), zo.layer_norm_channels(x, wt, b)) < REL_L2
 
 

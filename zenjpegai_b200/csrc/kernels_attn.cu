@@ -92,6 +92,73 @@ __global__ void layer_norm_kernel(const __half* __restrict__ x, __half* __restri
   }
 }
 
+// Layer norm for c <= 256: a pixel is a segment of LPP lanes (LPP = c/8 rounded up to a power
+// of two), lane l of a segment holding channels 8l .. 8l+7; sums are segment-local shuffles.
+// A thread handles kLnPix pixels (their loads issued together), its gamma / beta stay in
+// registers. Same arithmetic as layer_norm_kernel: two-pass mean and variance in f32.
+constexpr int kLnPix = 2;
+
+template <int LPP>
+__global__ void __launch_bounds__(256) layer_norm_seg_kernel(
+    const __half* __restrict__ x, __half* __restrict__ y, long long npix, int h, int w, int c,
+    long long xpix, long long xrow, long long ximg, long long ypix, long long yrow,
+    long long yimg, const float* __restrict__ gamma, const float* __restrict__ beta) {
+  constexpr int SEGS = 256 / LPP;  // pixels per block and pass
+  const int sub = threadIdx.x % LPP;
+  const int c0 = sub * 8;
+  const bool act = c0 < c;
+  float gm[8], bt[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    gm[i] = act ? __ldg(gamma + c0 + i) : 0.f;
+    bt[i] = act ? __ldg(beta + c0 + i) : 0.f;
+  }
+  float v[kLnPix][8];
+  long long pxl[kLnPix];
+#pragma unroll
+  for (int k = 0; k < kLnPix; ++k) {
+    pxl[k] = ((long long)blockIdx.x * kLnPix + k) * SEGS + threadIdx.x / LPP;
+    const long long p = pxl[k];
+    if (act && p < npix) {
+      const int px = (int)(p % w);
+      const long long r = p / w;
+      ld8(x + (r / h) * ximg + (r % h) * xrow + px * xpix + c0, v[k]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[k][i] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kLnPix; ++k) {
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sum += v[k][i];
+#pragma unroll
+    for (int o = LPP / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum / (float)c;
+    float sq = 0.f;
+    if (act) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[k][i] - mean;
+        sq += d * d;
+      }
+    }
+#pragma unroll
+    for (int o = LPP / 2; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float denom = sqrtf(sq / (float)c + 1e-5f);
+    const long long p = pxl[k];
+    if (act && p < npix) {
+      float o8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = (v[k][i] - mean) / denom * gm[i] + bt[i];
+      const int px = (int)(p % w);
+      const long long r = p / w;
+      st8(y + (r / h) * yimg + (r % h) * yrow + px * ypix + c0, o8);
+    }
+  }
+}
+
 // ---- depthwise 3x3 ------------------------------------------------------------------------
 // Block = a tile of kDwTH rows x TW columns x 64 output channels. Its input (with the
 // one-pixel halo) is staged in shared memory by 16-byte cp.async copies, zero-filled outside
@@ -582,6 +649,21 @@ __global__ void gather_latent_kernel(const float* __restrict__ src, int C, int L
 void launch_layer_norm(const TView& x, const TView& y, const float* gamma, const float* beta,
                        cudaStream_t s) {
   long long pixels = (long long)x.n * x.h * x.w;
+  if (x.c <= 256) {
+    const int lpp = x.c <= 64 ? 8 : x.c <= 128 ? 16 : 32;
+    const int grid = blocks_for(pixels, kLnPix * (256 / lpp));
+#define ZJAI_LN_SEG(L)                                                                       \
+  layer_norm_seg_kernel<L><<<grid, 256, 0, s>>>(x.p, y.p, pixels, x.h, x.w, x.c, x.pix, x.row, \
+                                                x.img, y.pix, y.row, y.img, gamma, beta)
+    if (lpp == 8)
+      ZJAI_LN_SEG(8);
+    else if (lpp == 16)
+      ZJAI_LN_SEG(16);
+    else
+      ZJAI_LN_SEG(32);
+#undef ZJAI_LN_SEG
+    return;
+  }
   layer_norm_kernel<<<blocks_for(pixels, 8), 256, 0, s>>>(x.p, y.p, x.n, x.h, x.w, x.c, x.pix,
                                                           x.row, x.img, y.pix, y.row, y.img,
                                                           gamma, beta);
