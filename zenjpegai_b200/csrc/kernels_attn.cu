@@ -424,49 +424,79 @@ __global__ void attn_gram_kernel(const __half* __restrict__ qkv, int n_img, int 
   if (threadIdx.x < 2 * dim) atomicAdd(sq + (long long)n * 2 * dim + threadIdx.x, sqacc);
 }
 
-// Register-tiled Gram for head widths c with c % 4 == 0: thread = (head, 4 rows i, 4 columns
-// j) of G, block = heads * (c/4)^2 threads over a contiguous pixel range of one picture
-// (blockIdx.y). Pixels arrive in chunks of kGram2Pix as f16 [pixel][q | k] rows by 16-byte
-// cp.async copies, double-buffered so the next chunk lands while this one is summed. Each
-// pixel costs a thread two 8-byte shared loads and 16 FMAs; the threads of row block 0 (column
-// block 0) also sum k_j^2 (q_i^2). Partial sums go to gram / sq by atomics at the end.
-constexpr int kGram2Pix = 64;
+// Gram on the tensor cores (mma.sync m16n8k16, f16 in, f32 accumulate) for head widths
+// HC = 16 or 32 and heads dividing 8. Block = 8 warps over a contiguous pixel range of one
+// picture (blockIdx.y); pixels arrive in chunks of kGramChunk as f16 rows [q | k] (row pitch
+// padded by 16 bytes so the 8 rows of an ldmatrix hit 8 distinct bank groups), by 16-byte
+// cp.async copies, double-buffered. Warp w takes head w % heads and a 1/(8/heads) slice of
+// each chunk's pixels. With S the staged rows [pixel][channel]: G_h = Q_h^T K_h is an MMA whose
+// A operand (channels x pixels) and B operand (pixels x channels) both come from S through
+// ldmatrix.trans. The squared norms sum_p q_i^2 and sum_p k_j^2 are the diagonals of Q_h^T Q_h
+// and K_h^T K_h, taken from the diagonal 8x8 blocks only. Partial sums go to gram / sq by
+// atomics at the end.
+constexpr int kGramChunk = 64;
 
-__global__ void __launch_bounds__(1024) attn_gram_tiled_kernel(
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int HC>
+__global__ void __launch_bounds__(256) attn_gram_mma_kernel(
     const __half* __restrict__ qkv, int npix, int w, int dim, int heads, long long pix,
     long long row, long long img, float* __restrict__ gram, float* __restrict__ sq,
     int px_per_block) {
-  extern __shared__ __align__(16) __half gsm[];  // [2][kGram2Pix][2 * dim]
+  constexpr int MT = HC / 16, NT = HC / 8;
+  extern __shared__ __align__(16) __half gsm[];  // [2][kGramChunk][rs]
+  const int rs = 2 * dim + 8;                    // padded row pitch (halves)
   const int n = blockIdx.y;
-  const int c = dim / heads, cb = c / 4;
-  const int hd = threadIdx.x / (cb * cb), ij = threadIdx.x % (cb * cb);
-  const int i0 = hd * c + (ij / cb) * 4, j0 = hd * c + (ij % cb) * 4;
-  const bool do_q = (ij % cb) == 0, do_k = (ij / cb) == 0;
-  const int rowh = 2 * dim;       // halves per staged pixel
-  const int groups = rowh / 8;    // 16-byte chunks per staged pixel
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hd = warp % heads, slice = warp / heads, nslices = 8 / heads;
+  const int kpw = kGramChunk / nslices / 16;  // 16-pixel k-steps per warp and chunk
+  const int groups = 2 * dim / 8;
   const __half* base = qkv + n * img;
   const int p_begin = blockIdx.x * px_per_block;
   const int p_end = min(npix, p_begin + px_per_block);
-  const int nchunks = (p_end - p_begin + kGram2Pix - 1) / kGram2Pix;
+  const int nchunks = (p_end - p_begin + kGramChunk - 1) / kGramChunk;
 
   auto stage = [&](int chunk, int buf) {
-    __half* dst = gsm + buf * kGram2Pix * rowh;
-    const int p0 = p_begin + chunk * kGram2Pix;
-    for (int t = threadIdx.x; t < kGram2Pix * groups; t += blockDim.x) {
+    __half* dst = gsm + buf * kGramChunk * rs;
+    const int p0 = p_begin + chunk * kGramChunk;
+    for (int t = threadIdx.x; t < kGramChunk * groups; t += 256) {
       const int pp = t / groups, g = t % groups;
       const int p = p0 + pp;
       const bool ok = p < p_end;
-      cp_async16(dst + pp * rowh + g * 8, ok ? base + (p / w) * row + (p % w) * pix + g * 8 : qkv,
+      cp_async16(dst + pp * rs + g * 8, ok ? base + (p / w) * row + (p % w) * pix + g * 8 : qkv,
                  ok ? 16 : 0);
     }
   };
 
-  float acc[4][4];
+  float G[MT][NT][4], Dq[MT][2][4], Dk[MT][2][4];
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int a = 0; a < MT; ++a) {
 #pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-  float qs[4] = {0.f, 0.f, 0.f, 0.f}, ks[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int b = 0; b < NT; ++b)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) G[a][b][e] = 0.f;
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) Dq[a][b][e] = Dk[a][b][e] = 0.f;
+  }
+  // ldmatrix row address of this lane: matrix mi = lane / 8, row r = lane % 8
+  const int mi = lane >> 3, r8 = lane & 7;
+  const int qcol = hd * HC, kcol = dim + hd * HC;
+
   if (nchunks > 0) stage(0, 0);
   asm volatile("cp.async.commit_group;\n" ::: "memory");
   for (int ch = 0; ch < nchunks; ++ch) {
@@ -474,44 +504,79 @@ __global__ void __launch_bounds__(1024) attn_gram_tiled_kernel(
     asm volatile("cp.async.commit_group;\n" ::: "memory");
     asm volatile("cp.async.wait_group 1;\n" ::: "memory");
     __syncthreads();
-    const __half* src = gsm + (ch & 1) * kGram2Pix * rowh;
-#pragma unroll 4
-    for (int pp = 0; pp < kGram2Pix; ++pp) {
-      const uint2 uq = *reinterpret_cast<const uint2*>(src + pp * rowh + i0);
-      const uint2 uk = *reinterpret_cast<const uint2*>(src + pp * rowh + dim + j0);
-      const float2 q01 = __half22float2(*reinterpret_cast<const __half2*>(&uq.x));
-      const float2 q23 = __half22float2(*reinterpret_cast<const __half2*>(&uq.y));
-      const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&uk.x));
-      const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&uk.y));
-      const float q[4] = {q01.x, q01.y, q23.x, q23.y}, k[4] = {k01.x, k01.y, k23.x, k23.y};
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(gsm + (ch & 1) * kGramChunk * rs);
+    for (int ks = 0; ks < kpw; ++ks) {
+      const int p0 = (slice * kpw + ks) * 16;
+      // A operands (channels x pixels): matrices (m 0-7, k 0-7), (m 8-15, k 0-7),
+      // (m 0-7, k 8-15), (m 8-15, k 8-15)
+      uint32_t aq[MT][4], ak[MT][4];
+      const int arow = p0 + ((mi & 2) ? 8 : 0) + r8;
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(q[a], k[b], acc[a][b]);
-      if (do_q) {
-#pragma unroll
-        for (int a = 0; a < 4; ++a) qs[a] = fmaf(q[a], q[a], qs[a]);
+      for (int mt = 0; mt < MT; ++mt) {
+        const int acol = mt * 16 + ((mi & 1) ? 8 : 0);
+        ldsm_x4_t(sbase + (uint32_t)(arow * rs + qcol + acol) * 2u, aq[mt]);
+        ldsm_x4_t(sbase + (uint32_t)(arow * rs + kcol + acol) * 2u, ak[mt]);
       }
-      if (do_k) {
+      // B operands (pixels x channels), two n-tiles per ldmatrix: (k 0-7, j), (k 8-15, j),
+      // (k 0-7, j+1), (k 8-15, j+1)
+      uint32_t bk[NT][2], bq[NT][2];
+      const int brow = p0 + ((mi & 1) ? 8 : 0) + r8;
 #pragma unroll
-        for (int b = 0; b < 4; ++b) ks[b] = fmaf(k[b], k[b], ks[b]);
+      for (int j = 0; j < NT; j += 2) {
+        const int bcol = (j + (mi >> 1)) * 8;
+        uint32_t t[4];
+        ldsm_x4_t(sbase + (uint32_t)(brow * rs + kcol + bcol) * 2u, t);
+        bk[j][0] = t[0];
+        bk[j][1] = t[1];
+        bk[j + 1][0] = t[2];
+        bk[j + 1][1] = t[3];
+        ldsm_x4_t(sbase + (uint32_t)(brow * rs + qcol + bcol) * 2u, t);
+        bq[j][0] = t[0];
+        bq[j][1] = t[1];
+        bq[j + 1][0] = t[2];
+        bq[j + 1][1] = t[3];
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816(G[mt][nt], aq[mt], bk[nt][0], bk[nt][1]);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          mma16816(Dq[mt][e], aq[mt], bq[2 * mt + e][0], bq[2 * mt + e][1]);
+          mma16816(Dk[mt][e], ak[mt], bk[2 * mt + e][0], bk[2 * mt + e][1]);
+        }
       }
     }
     __syncthreads();  // all reads of this buffer done before it is refilled
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
-  float* gn = gram + (long long)n * dim * c;
+
+  // accumulator element e of a tile: row gid (+8 for e >= 2), column 2 * tig + (e & 1)
+  const int gid = lane >> 2, tig = lane & 3;
+  float* gn = gram + (long long)n * dim * HC;
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) atomicAdd(gn + (i0 + a) * c + (j0 - hd * c) + b, acc[a][b]);
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = mt * 16 + gid + (e >= 2 ? 8 : 0), j = nt * 8 + 2 * tig + (e & 1);
+        atomicAdd(gn + (hd * HC + i) * HC + j, G[mt][nt][e]);
+      }
+  // diagonals: n-tile 2mt holds rows mt*16 + 0..7 (elements 0, 1), n-tile 2mt+1 rows
+  // mt*16 + 8..15 (elements 2, 3); element (gid, 2 tig + b) is diagonal when gid == 2 tig + b
   float* sn = sq + (long long)n * 2 * dim;
-  if (do_q)
 #pragma unroll
-    for (int a = 0; a < 4; ++a) atomicAdd(sn + i0 + a, qs[a]);
-  if (do_k)
+  for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) atomicAdd(sn + dim + j0 + b, ks[b]);
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+        if (gid == 2 * tig + b) {
+          const int i = mt * 16 + e * 8 + gid;
+          atomicAdd(sn + hd * HC + i, Dq[mt][e][2 * e + b]);
+          atomicAdd(sn + dim + hd * HC + i, Dk[mt][e][2 * e + b]);
+        }
 }
 
 // attn[n][h][i][j] = softmax_j( G_ij / (max(|q_i|, eps) max(|k_j|, eps)) * T[h] )
@@ -708,24 +773,28 @@ void launch_attention(const TView& qkv, const TView& out, int heads, const float
   float* attn = sq + (size_t)n * 2 * dim;             // n * dim * c
   cudaMemsetAsync(gram, 0, sizeof(float) * ((size_t)n * dim * c + (size_t)n * 2 * dim), s);
   const int npix = qkv.h * qkv.w;
-  const int gram_threads = heads * (c / 4) * (c / 4);
-  if (c % 4 == 0 && dim <= 256 && gram_threads >= 32 && gram_threads <= 1024 &&
-      gram_threads % 32 == 0) {
-    const int smem = 2 * kGram2Pix * 2 * dim * (int)sizeof(__half);
+  if ((c == 16 || c == 32) && (heads == 2 || heads == 4 || heads == 8)) {
+    const int smem = 2 * kGramChunk * (2 * dim + 8) * (int)sizeof(__half);
     static bool attr_set = false;
-    if (!attr_set) {
-      cudaFuncSetAttribute(attn_gram_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           2 * kGram2Pix * 2 * 256 * (int)sizeof(__half));
+    if (!attr_set) {  // covers dim <= 8 * 32
+      const int most = 2 * kGramChunk * (2 * 256 + 8) * (int)sizeof(__half);
+      cudaFuncSetAttribute(attn_gram_mma_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           most);
+      cudaFuncSetAttribute(attn_gram_mma_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           most);
       attr_set = true;
     }
-    // about four blocks per SM over the whole batch, whole chunks per block
-    const int chunks = (npix + kGram2Pix - 1) / kGram2Pix;
-    const int splits = std::max(1, std::min(chunks, (4 * sms + n - 1) / n));
-    const int px_per_block = ((chunks + splits - 1) / splits) * kGram2Pix;
+    // about three blocks per SM over the whole batch, whole chunks per block
+    const int chunks = (npix + kGramChunk - 1) / kGramChunk;
+    const int splits = std::max(1, std::min(chunks, (3 * sms + n - 1) / n));
+    const int px_per_block = ((chunks + splits - 1) / splits) * kGramChunk;
     dim3 g1((npix + px_per_block - 1) / px_per_block, n);
-    attn_gram_tiled_kernel<<<g1, gram_threads, smem, s>>>(qkv.p, npix, qkv.w, dim, heads,
-                                                          qkv.pix, qkv.row, qkv.img, gram, sq,
-                                                          px_per_block);
+    if (c == 32)
+      attn_gram_mma_kernel<32><<<g1, 256, smem, s>>>(qkv.p, npix, qkv.w, dim, heads, qkv.pix,
+                                                     qkv.row, qkv.img, gram, sq, px_per_block);
+    else
+      attn_gram_mma_kernel<16><<<g1, 256, smem, s>>>(qkv.p, npix, qkv.w, dim, heads, qkv.pix,
+                                                     qkv.row, qkv.img, gram, sq, px_per_block);
   } else {
     const int chunks = (npix + kGramPix - 1) / kGramPix;
     const int cpb = std::max(1, chunks / 64);
