@@ -281,7 +281,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                         tc.oy0 + (dy >> 1));
           }
           bulk_load(sB,
-                    a.wblk + ((size_t)(tap * a.cchunks + cc) * a.n_tiles + tc.n0 / a.bn) *
+                    a.wblk + (size_t)tc.img * a.wblk_img +
+                        ((size_t)(tap * a.cchunks + cc) * a.n_tiles + tc.n0 / a.bn) *
                                  ((size_t)a.bn * a.kc),
                     b_bytes, fb);
           ++issued;

@@ -39,6 +39,7 @@ struct ConvArgs {
   // weights as contiguous K-step blocks [bn][kc] in the shared-memory (swizzled) image, block
   // index (tap * cchunks + cc) * n_tiles + n_tile: one bulk copy per K step
   const __half* wblk;
+  long long wblk_img;  // per-picture weight sets: stride in halves (0: one set for all)
   // epilogue
   const float* bias;   // [n_tiles * bn] in packed column order, or null
   float scale;         // weight unscale (power of two)

@@ -157,9 +157,9 @@ static void choose_n(int ncols, int* bn, int* n_tiles) {
 
 // Power-of-two scale that brings the largest |w| into [2^13, 2^14): f16 keeps its full
 // 11-bit significand for every weight that matters, far from overflow.
-static float weight_scale(const std::vector<float>& w) {
+float pow2_weight_scale(const float* w, size_t n) {
   float mx = 0.f;
-  for (float v : w) mx = std::max(mx, std::fabs(v));
+  for (size_t i = 0; i < n; ++i) mx = std::max(mx, std::fabs(w[i]));
   if (mx == 0.f || !std::isfinite(mx)) return 1.f;
   int e;
   std::frexp(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
@@ -175,7 +175,7 @@ static float weight_scale(const std::vector<float>& w) {
 // one bulk copy.
 static int upload_layer(Ctx* ctx, ConvLayer* L, const std::vector<float>& wf,
                         const std::vector<float>& bf) {
-  float s = weight_scale(wf);
+  float s = pow2_weight_scale(wf.data(), wf.size());
   L->scale = 1.f / s;
   const int taps = L->kh * L->kw, kc = L->kc, bn = L->bn;
   const int chunks16 = kc / 8;  // 16-byte chunks per row
@@ -453,6 +453,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   CUtensorMap tmB;  // unused by the kernel: weights arrive as bulk copies of a.wblk
   memset(&tmB, 0, sizeof tmB);
   a.wblk = L.w;
+  a.wblk_img = L.w_img;
   if (!a.s2) {
     CUtensorMap tmA;
     ZJAI_TRY(make_act_map(ctx, &tmA, in, L.kc, a.bw, a.bh));

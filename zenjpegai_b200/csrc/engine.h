@@ -133,6 +133,7 @@ struct ConvLayer {
   int transposed = 0, t_k = 0, t_pad = 0, t_outpad = 0;  // convT output-size rule
   float scale = 1.f;
   __half* w = nullptr;
+  long long w_img = 0;  // per-picture weight sets (stride in halves), 0: one set
   float* bias = nullptr;
   long long flops_per_px = 0;  // algorithmic MACs*2 per conv-output pixel (live taps only)
   // conv output extent (GEMM M space) and shuffled output extent for an input of h x w
@@ -148,6 +149,8 @@ int pack_conv(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, i
 int pack_convT(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, int cout, int k,
                int pad, int out_pad, int post_ps);
 void free_conv(ConvLayer* L);
+// Power-of-two scale that brings max |w| into [2^13, 2^14) (the packed f16 weight scale).
+float pow2_weight_scale(const float* w, size_t n);
 
 // Epilogue / output description for one conv launch.
 struct ConvOut {

@@ -166,10 +166,12 @@ __global__ void __launch_bounds__(256) layer_norm_seg_kernel(
 // Thread = (8-channel group of one source, column): it walks the tile's input rows top to
 // bottom, adding each row into the three output rows that it feeds (accumulators in
 // registers, the thread's 3x3 weights too) and writing an output row as soon as its last
-// input row is in. Per output the taps accumulate in (ky, kx) row-major order. Weights [c][9].
+// input row is in. Per output the taps accumulate in (ky, kx) row-major order, two channels
+// per packed f32x2 FMA. Weights [c][9].
 // gate: out has c/2 channels, out[k] = elu(dw[k]) * dw[k + c/2] (the FFN gate, math.rs:376);
 // the thread of group g of the first half and the thread of group g of the second half sit 8
-// lanes apart, and the second hands its sums to the first by a shuffle.
+// lanes apart and swap half their sums by shuffles: the first writes output channels 0..3 of
+// the group, the second channels 4..7.
 constexpr int kDwTH = 8;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
@@ -688,6 +690,31 @@ __global__ void __launch_bounds__(256) attn_apply_head_kernel(
   }
 }
 
+// The attention apply folded into the following 1x1 projection (attention.rs:328-372 applies
+// project_out to A.V): W'_n[k][h*c + j] = sum_i W_o[k][h*c + i] * A_n[h][i][j], one weight set
+// per picture, scaled by `s` and written as f16 straight into conv_tc_kernel's blocked weight
+// image (K-step blocks [bn][kc], 16-byte chunk j of row r at j ^ f(r)). Rows / columns beyond
+// dim (padding of the packed layer) are zero. W_o is PyTorch [dim][dim] f32.
+__global__ void attn_fold_kernel(const float* __restrict__ wo, const float* __restrict__ attn,
+                                 int dim, int c, float s, __half* __restrict__ wout, int npad,
+                                 int cin_pad, int kc, int bn) {
+  const int n = blockIdx.y;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= npad * cin_pad) return;
+  const int r = idx / cin_pad, j = idx % cin_pad;
+  float acc = 0.f;
+  if (r < dim && j < dim) {
+    const int hd = j / c, jj = j % c;
+    const float* A = attn + (long long)n * dim * c + (long long)hd * c * c;
+    const float* W = wo + (long long)r * dim + hd * c;
+    for (int i = 0; i < c; ++i) acc = fmaf(__ldg(W + i), __ldg(A + i * c + jj), acc);
+  }
+  const int cc = j / kc, col = j % kc, nt = r / bn, rr = r % bn;
+  const int f = kc == 64 ? (rr & 7) : kc == 32 ? ((rr >> 1) & 3) : ((rr >> 2) & 1);
+  __half* blk = wout + (long long)n * npad * cin_pad + ((long long)cc * (npad / bn) + nt) * bn * kc;
+  blk[rr * kc + (((col >> 3) ^ f) << 3) + (col & 7)] = __float2half_rn(acc * s);
+}
+
 // planar f32 latent [C][LH][LW] -> NHWC f16 [n][h][w] at channel offset; per-image window
 // origins (x, y) in `origin` (device int pairs).
 __global__ void gather_latent_kernel(const float* __restrict__ src, int C, int LH, int LW,
@@ -763,8 +790,9 @@ void launch_dw3x3(const TView& x, const TView& y, const float* wt, bool gate, in
     launch_dw3x3_t<false>(x, y, wt, sms, s);
 }
 
-void launch_attention(const TView& qkv, const TView& out, int heads, const float* temp,
-                      float* scratch, int sms, cudaStream_t s) {
+// Gram, norms and softmax: the attention matrices attn[n][h][i][j] (scratch + attn_offset).
+static float* attention_weights(const TView& qkv, int heads, const float* temp, float* scratch,
+                                int sms, cudaStream_t s) {
   const int dim = qkv.c / 3;
   const int c = dim / heads;
   const int n = qkv.n;
@@ -804,6 +832,26 @@ void launch_attention(const TView& qkv, const TView& out, int heads, const float
   }
   attn_softmax_kernel<<<blocks_for((long long)n * dim, 128), 128, 0, s>>>(gram, sq, temp, attn, n,
                                                                          dim, heads);
+  return attn;
+}
+
+void launch_attention_fold(const TView& qkv, int heads, const float* temp, const float* wo,
+                           float wscale, const ConvLayer& L, __half* wout, float* scratch,
+                           int sms, cudaStream_t s) {
+  const int dim = qkv.c / 3;
+  const float* attn = attention_weights(qkv, heads, temp, scratch, sms, s);
+  dim3 g(blocks_for((long long)L.npad * L.cin_pad, 256), qkv.n);
+  attn_fold_kernel<<<g, 256, 0, s>>>(wo, attn, dim, dim / heads, wscale, wout, L.npad,
+                                     L.cin_pad, L.kc, L.bn);
+}
+
+void launch_attention(const TView& qkv, const TView& out, int heads, const float* temp,
+                      float* scratch, int sms, cudaStream_t s) {
+  const int dim = qkv.c / 3;
+  const int c = dim / heads;
+  const int n = qkv.n;
+  const int npix = qkv.h * qkv.w;
+  const float* attn = attention_weights(qkv, heads, temp, scratch, sms, s);
   if ((c == 16 || c == 32) && 8 % heads == 0) {
     const int px_per_block = 32 * (8 / heads);
     dim3 g3(blocks_for((long long)npix, px_per_block), n);

@@ -13,6 +13,14 @@ void launch_dw3x3(const TView& x, const TView& y, const float* wt, bool gate, in
 void launch_attention(const TView& qkv, const TView& out, int heads, const float* temp,
                       float* scratch, int sms, cudaStream_t s);
 size_t attention_scratch_floats(int n_img, int dim, int heads);
+// The attention up to its matrices A_n, then A folded into the following 1x1 projection
+// W_o (f32 [dim][dim], device): writes n per-picture weight sets in the blocked layout of the
+// packed layer L (which holds W_o), scaled by `wscale`, at wout (n * L.npad * L.cin_pad
+// halves). Running L with w = wout, w_img = L.npad * L.cin_pad, scale = 1 / wscale on the v
+// slice of qkv gives project_out(attention(qkv)).
+void launch_attention_fold(const TView& qkv, int heads, const float* temp, const float* wo,
+                           float wscale, const ConvLayer& L, __half* wout, float* scratch,
+                           int sms, cudaStream_t s);
 void launch_gather_latent(const float* src, int C, int LH, int LW, const int* origin,
                           const TView& dst, cudaStream_t s);
 

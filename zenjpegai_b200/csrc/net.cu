@@ -121,6 +121,15 @@ struct Loader {
     ZJAI_TRY(dw(p + ".prep_data.conv2", 3 * dim));
     ZJAI_TRY(vec(p + ".attn.temperature", {4, 1, 1}));
     ZJAI_TRY(conv(p + ".attn.project_out", dim, dim, 1, 1, 1, 0, 1, false));
+    // f32 copy of W_o for the per-picture fold W_o . blockdiag(A). Its f16 scale: every column
+    // of A sums to at most c = dim / 4 (rows are softmax distributions), so
+    // |W'| <= c max|W_o| and the packed scale of W_o divided by 2^ceil(log2 c) cannot overflow.
+    const float* wo;
+    ZJAI_TRY(get(p + ".attn.project_out.weight", {dim, dim, 1, 1}, &wo));
+    ZJAI_TRY(vec(p + ".attn.project_out.weight", {dim, dim, 1, 1}));
+    int lc = 0;
+    while ((1 << lc) < dim / 4) ++lc;
+    net->fold_scale[p] = std::ldexp(pow2_weight_scale(wo, (size_t)dim * dim), -lc);
     ZJAI_TRY(vec(p + ".ffn.norm1.weight", {dim}));
     ZJAI_TRY(vec(p + ".ffn.norm1.bias", {dim}));
     ZJAI_TRY(conv(p + ".ffn.project_in", dim, 2 * hidden, 1, 1, 1, 0, 1, false));
@@ -264,6 +273,12 @@ std::string Runner::kind_tag() const {
 int Runner::conv(const std::string& name, const TView& in, ConvOut o) {
   const ConvLayer* L = layer(name);
   if (!L) return fail(ZJAI_MODEL, name + ": layer not loaded");
+  return conv_layer(name, *L, in, o);
+}
+
+int Runner::conv_layer(const std::string& name, const ConvLayer& layer_ref, const TView& in,
+                       ConvOut o) {
+  const ConvLayer* L = &layer_ref;
   cudaStream_t saved = ctx->stream;
   ctx->stream = stream;
   ctx->cur_arena = arena;
@@ -368,11 +383,10 @@ int Runner::tb(const std::string& p, const TView& x) {
   const int d = x.c, hidden = 4 * d;
   auto vec = [&](const std::string& k) { return net->vecs.at(k); };
   ArenaMark mark(arena);
-  TView ln, qkv, qkv2, att;
+  TView ln, qkv, qkv2;
   ZJAI_TRY(alloc(x.h, x.w, d, &ln));
   ZJAI_TRY(alloc(x.h, x.w, 3 * d, &qkv));
   ZJAI_TRY(alloc(x.h, x.w, 3 * d, &qkv2));
-  ZJAI_TRY(alloc(x.h, x.w, d, &att));
   // algorithmic bytes per pixel of a d-channel f16 map
   const double px = (double)n * x.h * x.w, b16 = 2.0 * px;
   mem_kernel(p + ".prep_data.norm1", "ln", 2 * b16 * d, 1, [&] {
@@ -388,16 +402,30 @@ int Runner::tb(const std::string& p, const TView& x) {
   float* scratch = static_cast<float*>(
       arena->alloc(attention_scratch_floats(n, d, 4) * sizeof(float)));
   if (!scratch) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (attention scratch)");
-  // Gram reads q and k, the apply reads v and writes the output
-  mem_kernel(p + ".attn", "attn", b16 * 4 * d, 3, [&] {
-    launch_attention(qkv2, att, 4, vec(p + ".attn.temperature"), scratch, ctx->sms, stream);
+  // x += W_o (A . v): the attention matrices A_n, folded into per-picture projection weights
+  // W_o . blockdiag(A_n), then one tcgen05 1x1 conv over the v slice of qkv2. The Gram reads
+  // q and k; the conv reads v.
+  const ConvLayer* Lo = layer(p + ".attn.project_out");
+  if (!Lo) return fail(ZJAI_MODEL, p + ".attn.project_out: layer not loaded");
+  const long long wset = (long long)Lo->npad * Lo->cin_pad;
+  __half* wfold = static_cast<__half*>(arena->alloc((size_t)n * wset * sizeof(__half)));
+  if (!wfold) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (folded weights)");
+  const float fs = net->fold_scale.at(p);
+  mem_kernel(p + ".attn", "attn", b16 * 2 * d, 3, [&] {
+    launch_attention_fold(qkv2, 4, vec(p + ".attn.temperature"),
+                          vec(p + ".attn.project_out.weight"), fs, *Lo, wfold, scratch, ctx->sms,
+                          stream);
   });
   if (count_flops) flops += 2.0 * 2.0 * (double)n * x.h * x.w * d * (d / 4);
+  ConvLayer Lf = *Lo;
+  Lf.w = wfold;
+  Lf.w_img = wset;
+  Lf.scale = 1.f / fs;
   ConvOut oa;
   oa.out = x;
   oa.op = OP_ADD;
   oa.r1 = &x;
-  ZJAI_TRY(conv(p + ".attn.project_out", att, oa));
+  ZJAI_TRY(conv_layer(p + ".attn.project_out", Lf, qkv2.channels(2 * d, d), oa));
   mem_kernel(p + ".ffn.norm1", "ln", 2 * b16 * d, 1, [&] {
     launch_layer_norm(x, ln, vec(p + ".ffn.norm1.weight"), vec(p + ".ffn.norm1.bias"), stream);
   });

@@ -14,6 +14,9 @@ struct Net {
   int kind = 0, op = 0;
   std::map<std::string, ConvLayer> convs;
   std::map<std::string, float*> vecs;  // LN weight/bias, temperature, depthwise weights [c][9]
+  // f16 scale of the per-picture weights W_o . blockdiag(A) of each transformer block's folded
+  // attention projection (keyed by the block prefix)
+  std::map<std::string, float> fold_scale;
   ~Net();
 };
 
@@ -43,6 +46,8 @@ struct Runner {
   int alloc(int h, int w, int c, TView* v);
   const ConvLayer* layer(const std::string& name);
   int conv(const std::string& name, const TView& in, ConvOut o);
+  // conv with an explicit packed layer (a variant of the loaded layer `name`)
+  int conv_layer(const std::string& name, const ConvLayer& L, const TView& in, ConvOut o);
   std::string kind_tag() const;
   // A memory-bound kernel (`launches` launches issued by `f` on this runner's stream), profiled
   // under "<kind tag><name>[<kind>]" with its algorithmic bytes.
