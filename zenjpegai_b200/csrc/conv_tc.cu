@@ -164,6 +164,71 @@ __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kCh
   }
 }
 
+// NHWC f16 output without a pixel shuffle (R == 1): column n is channel n of this thread's
+// pixel. The chunk's 16 f16 results go to this lane's 32 bytes of the warp's staging slot
+// (`dst`), from which one TMA store writes the warp's 32 pixels; the store clips pixels and
+// channels outside the output view, so lanes outside it (or columns at or past cph, packing
+// padding) may stage anything but must not read residuals. The element offsets of the pixel in
+// r1 / r2 / out2 (p1, p2, p2o) are computed once per tile; residuals are read before the
+// results are staged (in-place ops read exactly what this warp's store then overwrites).
+template <int OP>
+__device__ __forceinline__ void epi_r1(const ConvArgs& a, const float (&v)[kChunk], int col0,
+                                       long long p1, long long p2, long long p2o, bool valid,
+                                       const float* btab, uint4* dst) {
+  constexpr int G = kChunk / 8;
+  uint4 r1[G], r2[G];
+  if constexpr (OP != OP_NONE) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int c = col0 + 8 * g;
+      r1[g] = r2[g] = make_uint4(0u, 0u, 0u, 0u);
+      if (valid && c < a.cph) {
+        r1[g] = __ldg(reinterpret_cast<const uint4*>(a.r1 + p1 + c));
+        if constexpr (OP == OP_CAB) r2[g] = __ldg(reinterpret_cast<const uint4*>(a.r2 + p2 + c));
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int c = col0 + 8 * g;
+    float x[8];
+    const float4 b0 = *reinterpret_cast<const float4*>(btab + c);
+    const float4 b1 = *reinterpret_cast<const float4*>(btab + c + 4);
+    x[0] = v[8 * g + 0] * a.scale + b0.x;
+    x[1] = v[8 * g + 1] * a.scale + b0.y;
+    x[2] = v[8 * g + 2] * a.scale + b0.z;
+    x[3] = v[8 * g + 3] * a.scale + b0.w;
+    x[4] = v[8 * g + 4] * a.scale + b1.x;
+    x[5] = v[8 * g + 5] * a.scale + b1.y;
+    x[6] = v[8 * g + 6] * a.scale + b1.z;
+    x[7] = v[8 * g + 7] * a.scale + b1.w;
+    act8(x, a.act1);
+    if constexpr (OP != OP_NONE) {
+      float q1[8];
+      unpack_h8(r1[g], q1);
+      if constexpr (OP == OP_ADD) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = x[e] + q1[e];
+      } else if constexpr (OP == OP_GATE) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = q1[e] * (1.f + x[e]);
+      } else {
+        float q2[8];
+        unpack_h8(r2[g], q2);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = q2[e] + q1[e] * x[e];
+      }
+    }
+    act8(x, a.act2);
+    dst[g] = pack_h8(x);
+    if (a.out2 && valid && c < a.cph) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = fminf(fmaxf(x[k], 0.f), 6.f);
+      *reinterpret_cast<uint4*>(a.out2 + p2o + c) = pack_h8(x);
+    }
+  }
+}
+
 // Planar f32 output (final layers and the layer entry points): one scalar per column.
 __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[kChunk], int col0,
                                            int img, int oy, int ox, bool valid,
@@ -198,8 +263,13 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
 
 }  // namespace
 
-__global__ void __launch_bounds__(kConvThreads, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+// Epilogue output modes: NHWC without a pixel shuffle, NHWC through the shuffle table, planar.
+constexpr int kModeR1 = 0, kModeShuffle = 1, kModePlanar = 2;
+
+// One CTA of kConvThreads (18 warps) per SM: 18 x 32 x 112 registers fill the register file.
+template <int MODE, int OP>
+__global__ void __maxnreg__(112)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmO,
                    const ConvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
@@ -219,6 +289,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint32_t* tab = reinterpret_cast<uint32_t*>(smem + S * stage_bytes + kBarrierBytes);
   const int npad = a.n_tiles * a.bn;
   float* btab = reinterpret_cast<float*>(tab + npad);
+  // TMA-store staging: two kEpiSlotBytes slots per epilogue warp (128-byte aligned)
+  uint8_t* staging = reinterpret_cast<uint8_t*>(btab + npad);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -359,6 +431,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     const int wg = (warp - 2) >> 2;
     const int m = q * 32 + lane;  // accumulator row == pixel index in the tile
     const int nchunks = a.bn / kChunk;
+    // TMA-store mode: this warp's two staging slots, and the origin of its 32-pixel box
+    // [16, bx, 32 / bx] relative to the tile (pixels m0 .. m0 + 31 of the tile, raster order)
+    uint8_t* wslots = staging + (warp - 2) * 2 * kEpiSlotBytes;
+    int slot = 0;
+    const int m0 = q * 32;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
@@ -368,6 +445,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const TileCoord tc = decode_tile(a, t);
       const int oy = tc.oy0 + (m >> a.lbw), ox = tc.ox0 + (m & (a.bw - 1));
       const bool valid = oy < a.oh && ox < a.ow;
+      long long p1 = 0, p2 = 0, p2o = 0;
+      if constexpr (MODE == kModeR1) {
+        if constexpr (OP != OP_NONE) p1 = tc.img * a.r1_img + oy * a.r1_row + ox * a.r1_pix;
+        if constexpr (OP == OP_CAB) p2 = tc.img * a.r2_img + oy * a.r2_row + ox * a.r2_pix;
+        p2o = tc.img * a.o2_img + oy * a.o2_row + ox * a.o2_pix;
+      }
       if (wg >= nchunks) {
         tc_fence_before();
         mbar_arrive(smem_u32(&acce[acc]));
@@ -380,21 +463,34 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           mbar_arrive(smem_u32(&acce[acc]));
         }
         const int col0 = tc.n0 + c * kChunk;
-        if (a.planar) {
+        if constexpr (MODE == kModeR1) {
+          // the slot about to be filled was last stored two chunks ago: wait for that read
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+          uint8_t* sl = wslots + slot * kEpiSlotBytes;
+          epi_r1<OP>(a, v, col0, p1, p2, p2o, valid, btab, reinterpret_cast<uint4*>(sl + lane * 32));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_4d(&tmO, smem_u32(sl), col0, tc.ox0 + (m0 & (a.bw - 1)),
+                         tc.oy0 + (m0 >> a.lbw), tc.img);
+            bulk_commit();
+          }
+          slot ^= 1;
+        } else if constexpr (MODE == kModePlanar) {
           epi_planar(a, v, col0, tc.img, oy, ox, valid, tab, btab);
         } else {
-          switch (a.op) {
-            case OP_ADD: epi_nhwc<OP_ADD>(a, v, col0, tc.img, oy, ox, valid, tab, btab); break;
-            case OP_GATE: epi_nhwc<OP_GATE>(a, v, col0, tc.img, oy, ox, valid, tab, btab); break;
-            case OP_CAB: epi_nhwc<OP_CAB>(a, v, col0, tc.img, oy, ox, valid, tab, btab); break;
-            default: epi_nhwc<OP_NONE>(a, v, col0, tc.img, oy, ox, valid, tab, btab); break;
-          }
+          epi_nhwc<OP>(a, v, col0, tc.img, oy, ox, valid, tab, btab);
         }
       }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
+    }
+    // every TMA store of this warp complete before the CTA (and its shared memory) ends
+    if constexpr (MODE == kModeR1) {
+      if (lane == 0) bulk_wait_all();
     }
   }
 
@@ -406,15 +502,28 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   }
 }
 
-void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmB, const ConvArgs& a, int grid,
+void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const ConvArgs& a, int grid,
                  cudaStream_t stream) {
-  const uint32_t smem = conv_smem_bytes(a.kc, a.bn, a.stages, a.n_tiles * a.bn);
+  const uint32_t smem =
+      conv_smem_bytes(a.kc, a.bn, a.stages, a.n_tiles * a.bn, !a.planar && a.R == 1);
+  // one instantiation per (output mode, epilogue op), each with its own register allocation
+  using K = void (*)(CUtensorMap, CUtensorMap, ConvArgs);
+  static const K kernels[3][4] = {
+      {conv_tc_kernel<kModeR1, OP_NONE>, conv_tc_kernel<kModeR1, OP_ADD>,
+       conv_tc_kernel<kModeR1, OP_GATE>, conv_tc_kernel<kModeR1, OP_CAB>},
+      {conv_tc_kernel<kModeShuffle, OP_NONE>, conv_tc_kernel<kModeShuffle, OP_ADD>,
+       conv_tc_kernel<kModeShuffle, OP_GATE>, conv_tc_kernel<kModeShuffle, OP_CAB>},
+      {conv_tc_kernel<kModePlanar, OP_NONE>, conv_tc_kernel<kModePlanar, OP_NONE>,
+       conv_tc_kernel<kModePlanar, OP_NONE>, conv_tc_kernel<kModePlanar, OP_NONE>}};
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    for (auto& row : kernels)
+      for (K k : row)
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
     attr_set = true;
   }
-  conv_tc_kernel<<<grid, kConvThreads, smem, stream>>>(tmA, tmB, a);
+  const int mode = a.planar ? kModePlanar : a.R == 1 ? kModeR1 : kModeShuffle;
+  kernels[mode][a.op & 3]<<<grid, kConvThreads, smem, stream>>>(tmA, tmO, a);
 }
 
 }  // namespace zjai

@@ -79,15 +79,23 @@ __host__ __device__ inline uint32_t conv_stage_bytes(int kc, int bn) {
   uint32_t b = 128u * kc * 2u + (uint32_t)bn * kc * 2u;
   return (b + 1023u) & ~1023u;
 }
+// Unshuffled NHWC outputs leave through TMA stores: each epilogue warp stages its 32 pixels x
+// 16 columns (1 KB of f16) in one of two slots, then one lane stores the box [16, bx, 32/bx].
+constexpr uint32_t kEpiSlotBytes = 1024u;
+constexpr uint32_t kEpiStagingBytes = 2u * kEpiSlotBytes * (kEpiThreads / 32);
+
 // 1 KB alignment slack + barriers/slots + the column table and the bias (4 + 4 bytes per column)
-__host__ __device__ inline uint32_t conv_fixed_smem(int npad) {
-  return 1024u + kBarrierBytes + 8u * (uint32_t)npad;
+// + the epilogue staging slots when the output goes out through TMA stores
+__host__ __device__ inline uint32_t conv_fixed_smem(int npad, bool staged) {
+  return 1024u + kBarrierBytes + 8u * (uint32_t)npad + (staged ? kEpiStagingBytes : 0u);
 }
-__host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int stages, int npad) {
-  return stages * conv_stage_bytes(kc, bn) + conv_fixed_smem(npad);
+__host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int stages, int npad,
+                                                    bool staged) {
+  return stages * conv_stage_bytes(kc, bn) + conv_fixed_smem(npad, staged);
 }
 
-void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmB, const ConvArgs& a, int grid,
+// tmO: the output tensor map (TMA-store epilogue, R == 1 NHWC output), unused otherwise.
+void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const ConvArgs& a, int grid,
                  cudaStream_t stream);
 
 }  // namespace zjai

@@ -133,13 +133,12 @@ int make_act_map_s2(Ctx* ctx, CUtensorMap* m, const TView& v, int img, int kc, i
                 (size_t)v.img * 2);
 }
 
-int make_weight_map(Ctx* ctx, CUtensorMap* m, const __half* w, int cin_pad, int rows, int kc,
-                    int bn) {
-  cuuint64_t dims[2] = {(cuuint64_t)cin_pad, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cin_pad * 2};
-  cuuint32_t box[2] = {(cuuint32_t)kc, (cuuint32_t)bn};
-  return encode(ctx, m, 2, const_cast<__half*>(w), dims, strides, box, swizzle_for(kc),
-                (size_t)cin_pad * rows * 2);
+int make_store_map(Ctx* ctx, CUtensorMap* m, const TView& v, int bx, int by) {
+  cuuint64_t dims[4] = {(cuuint64_t)v.c, (cuuint64_t)v.w, (cuuint64_t)v.h, (cuuint64_t)v.n};
+  cuuint64_t strides[3] = {(cuuint64_t)v.pix * 2, (cuuint64_t)v.row * 2, (cuuint64_t)v.img * 2};
+  cuuint32_t box[4] = {16, (cuuint32_t)bx, (cuuint32_t)by, 1};
+  return encode(ctx, m, 4, v.p, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE,
+                (size_t)v.img * v.n * 2);
 }
 
 // ---- packing --------------------------------------------------------------------------------
@@ -382,7 +381,9 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   a.kc = L.kc;
   a.bn = L.bn;
   const uint32_t stage = conv_stage_bytes(L.kc, L.bn);
-  const uint32_t fixed = conv_fixed_smem(L.npad);
+  // unshuffled NHWC outputs leave through the TMA-store epilogue (staging slots in smem)
+  const bool staged = !o.planar && L.R == 1;
+  const uint32_t fixed = conv_fixed_smem(L.npad, staged);
   if (fixed + 2 * stage > 232448u)
     return fail(ZJAI_UNSUPPORTED, "conv: too many output columns for one launch");
   a.stages = (int)std::min<uint32_t>(8, (232448u - fixed) / stage);
@@ -450,8 +451,12 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     a.sh = o.sh;
   }
 
-  CUtensorMap tmB;  // unused by the kernel: weights arrive as bulk copies of a.wblk
-  memset(&tmB, 0, sizeof tmB);
+  CUtensorMap tmO;  // output map of the TMA-store epilogue (unused in the other modes)
+  memset(&tmO, 0, sizeof tmO);
+  if (staged) {
+    const int bx = std::min(a.bw, 32);
+    ZJAI_TRY(make_store_map(ctx, &tmO, o.out, bx, 32 / bx));
+  }
   a.wblk = L.w;
   a.wblk_img = L.w_img;
   if (!a.s2) {
@@ -462,7 +467,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     const double fl = (double)L.flops_per_px * oh * ow * in.n;
     ctx->launches++;
     timed_launch(ctx, true, fl, 0.0, [&] {
-      launch_conv(tmA, tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
+      launch_conv(tmA, tmO, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
     });
   } else {
     // The parity-split 5-D view has no batch axis: one tensor map per picture, kept in a
@@ -483,7 +488,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     const double fl = (double)L.flops_per_px * oh * ow * in.n;
     ctx->launches++;
     timed_launch(ctx, true, fl, 0.0, [&] {
-      launch_conv(maps[0], tmB, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
+      launch_conv(maps[0], tmO, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
     });
   }
   return cuda_check(cudaGetLastError(), "conv launch");

@@ -118,8 +118,8 @@ int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero = f
 // ---- TMA descriptors ------------------------------------------------------------------------
 int make_act_map(Ctx* ctx, CUtensorMap* m, const TView& v, int kc, int bw, int bh);
 int make_act_map_s2(Ctx* ctx, CUtensorMap* m, const TView& v, int img, int kc, int bw, int bh);
-int make_weight_map(Ctx* ctx, CUtensorMap* m, const __half* w, int cin_pad, int rows, int kc,
-                    int bn);
+// output map of the TMA-store epilogue: box [16 channels, bx, by] over an NHWC f16 view
+int make_store_map(Ctx* ctx, CUtensorMap* m, const TView& v, int bx, int by);
 
 // ---- packed convolution ---------------------------------------------------------------------
 // A convolution (or a stride-2 transposed convolution rewritten as a phase convolution)
