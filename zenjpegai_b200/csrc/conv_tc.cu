@@ -37,7 +37,7 @@ __device__ __forceinline__ TileCoord decode_tile(const ConvArgs& a, int t) {
   int rest = mt / a.tiles_x;
   int ty = rest % a.tiles_y;
   c.img = rest / a.tiles_y;
-  c.oy0 = ty * a.bh;
+  c.oy0 = ty * a.bh * a.msub;
   c.ox0 = tx * a.bw;
   c.n0 = nt * a.bn;
   return c;
@@ -275,18 +275,28 @@ __global__ void __maxnreg__(112)
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
-  const uint32_t a_bytes = 128u * a.kc * 2u;
-  const uint32_t b_bytes = (uint32_t)a.bn * a.kc * 2u;
-  const uint32_t stage_bytes = conv_stage_bytes(a.kc, a.bn);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
+  const uint32_t sub_bytes = 128u * a.kc * 2u;      // A tile of one subtile
+  const uint32_t a_bytes = sub_bytes * a.msub;      // A tiles of a stage
+  const int brows = a.grp_n ? a.grp_n : a.bn;  // rows of one weight block (UMMA N)
+  const uint32_t b_bytes = (uint32_t)brows * a.kc * 2u;
+  // stage = A tiles + B block; in halo mode a stage holds only the B block and the A halos
+  // have their own kHaloSlots-slot ring after the stages
+  const uint32_t stage_bytes =
+      a.halo ? conv_bstage_bytes(a.kc, brows) : conv_stage_bytes(a.kc, brows, a.msub);
+  const uint32_t ring_bytes =
+      conv_ring_bytes(a.kc, brows, a.msub, S, a.halo ? a.halo_bytes : 0u);
+  uint8_t* halo_ring = smem + S * stage_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ring_bytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* accf = bars + 2 * S;
   uint64_t* acce = bars + 2 * S + 2;
   uint64_t* drain = bars + 2 * S + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  uint64_t* fullA = bars + 2 * S + 5;            // halo ring
+  uint64_t* emptyA = bars + 2 * S + 5 + kHaloSlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5 + 2 * kHaloSlots);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint32_t* tab = reinterpret_cast<uint32_t*>(smem + S * stage_bytes + kBarrierBytes);
+  uint32_t* tab = reinterpret_cast<uint32_t*>(smem + ring_bytes + kBarrierBytes);
   const int npad = a.n_tiles * a.bn;
   float* btab = reinterpret_cast<float*>(tab + npad);
   // TMA-store staging: two kEpiSlotBytes slots per epilogue warp (128-byte aligned)
@@ -305,6 +315,10 @@ __global__ void __maxnreg__(112)
       mbar_init(smem_u32(&acce[i]), kEpiThreads);
     }
     mbar_init(smem_u32(drain), 1);
+    for (int i = 0; i < kHaloSlots; ++i) {
+      mbar_init(smem_u32(&fullA[i]), 1);
+      mbar_init(smem_u32(&emptyA[i]), 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -328,43 +342,113 @@ __global__ void __maxnreg__(112)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    // One thread; everything per K step is adds and compares (a single thread's dependent
+    // instruction chain is what bounds the K-step rate, so no divisions here).
+    if (lane == 0 && a.halo) {
+      // halo mode: per tile and channel chunk cc, one halo box into the halo ring, then the
+      // taps' B blocks (block tap * cchunks + cc) into the stage ring
+      int stage = 0, hs = 0;
+      uint32_t phase = 0, hphase = 0;
+      long long issued = 0, hissued = 0;
+      const uint32_t s_base = smem_u32(smem), fb_base = smem_u32(full), eb_base = smem_u32(empty);
+      const uint32_t h_base = smem_u32(halo_ring);
+      const uint32_t hfb = smem_u32(fullA), heb = smem_u32(emptyA);
+      const uint32_t hbox = (uint32_t)a.hw * a.hh * a.kc * 2u;  // bytes the halo box delivers
+      const size_t kstride = (size_t)a.n_tiles * brows * a.kc;
+      for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
+        const TileCoord tc = decode_tile(a, t);
+        const int nt = tc.n0 / a.bn;
+        const __half* wbase = a.wblk + (size_t)tc.img * a.wblk_img + (size_t)nt * brows * a.kc;
+        for (int cc = 0; cc < a.cchunks; ++cc) {
+          if (!mbar_wait(heb + 8u * hs, hphase ^ 1u, abort_flag, a.err, DEV_TIMEOUT_EMPTY))
+            goto halo_done;
+          mbar_arrive_expect_tx(hfb + 8u * hs, hbox);
+          tma_load_4d(h_base + hs * a.halo_bytes, &tmA, hfb + 8u * hs, cc * a.kc,
+                      tc.ox0 - a.pad_l, tc.oy0 - a.pad_t, tc.img);
+          ++hissued;
+          if (++hs == kHaloSlots) {
+            hs = 0;
+            hphase ^= 1u;
+          }
+          for (int tap = 0; tap < a.taps; ++tap) {
+            if (!mbar_wait(eb_base + 8u * stage, phase ^ 1u, abort_flag, a.err,
+                           DEV_TIMEOUT_EMPTY))
+              goto halo_done;
+            const uint32_t fb = fb_base + 8u * stage;
+            mbar_arrive_expect_tx(fb, b_bytes);
+            bulk_load(s_base + stage * stage_bytes,
+                      wbase + (size_t)(tap * a.cchunks + cc) * kstride, b_bytes, fb);
+            ++issued;
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+        }
+      }
+    halo_done:
+      for (int s = 0; s < S; ++s) {
+        if (issued > s) {
+          long long last = ((issued - 1 - s) / S) * S + s;
+          mbar_wait_drain(smem_u32(&full[s]), (uint32_t)((last / S) & 1), a.err);
+        }
+      }
+      for (int s = 0; s < kHaloSlots; ++s) {
+        if (hissued > s) {
+          long long last = ((hissued - 1 - s) / kHaloSlots) * kHaloSlots + s;
+          mbar_wait_drain(smem_u32(&fullA[s]), (uint32_t)((last / kHaloSlots) & 1), a.err);
+        }
+      }
+    } else if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
+      const uint32_t s_base = smem_u32(smem), fb_base = smem_u32(full), eb_base = smem_u32(empty);
+      const uint32_t tx_bytes = a_bytes + b_bytes;
+      const size_t kstride = (size_t)a.n_tiles * brows * a.kc;  // halves per K step of weights
       for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
         const TileCoord tc = decode_tile(a, t);
-        int tap = 0, cc = 0;
-        for (int ks = 0; ks < ksteps; ++ks) {
-          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, a.err,
-                         DEV_TIMEOUT_EMPTY))
+        const int nt = tc.n0 / a.bn;
+        const int k0 = a.koff ? a.koff[nt] : 0, k1 = a.koff ? a.koff[nt + 1] : ksteps;
+        const __half* wbase = a.wblk + (size_t)tc.img * a.wblk_img + (size_t)nt * brows * a.kc;
+        const CUtensorMap* tm5 = a.s2 ? a.tmA_img + tc.img : nullptr;
+        int ky = 0, kx = 0, cc = 0, kidx = 0;  // dense order: tap-major, chunk-minor
+        for (int i = k0; i < k1; ++i) {
+          if (a.klist) {  // kidx | kx << 16 | ky << 21 | cc << 26
+            const uint32_t e = __ldg(a.klist + i);
+            kidx = (int)(e & 0xFFFFu);
+            kx = (int)((e >> 16) & 31u);
+            ky = (int)((e >> 21) & 31u);
+            cc = (int)(e >> 26);
+          }
+          if (!mbar_wait(eb_base + 8u * stage, phase ^ 1u, abort_flag, a.err, DEV_TIMEOUT_EMPTY))
             goto producer_done;
-          const int ky = tap / a.kw, kx = tap - ky * a.kw;
-          const uint32_t sA = smem_u32(smem + stage * stage_bytes);
-          const uint32_t sB = sA + a_bytes;
-          const uint32_t fb = smem_u32(&full[stage]);
-          mbar_arrive_expect_tx(fb, a_bytes + b_bytes);
+          const uint32_t sA = s_base + stage * stage_bytes;
+          const uint32_t fb = fb_base + 8u * stage;
+          mbar_arrive_expect_tx(fb, tx_bytes);
           if (!a.s2) {
             tma_load_4d(sA, &tmA, fb, cc * a.kc, tc.ox0 + kx - a.pad_l, tc.oy0 + ky - a.pad_t,
                         tc.img);
           } else {
             const int dx = kx - a.pad_l, dy = ky - a.pad_t;
-            tma_load_5d(sA, a.tmA_img + tc.img, fb, cc * a.kc, dx & 1, tc.ox0 + (dx >> 1), dy & 1,
+            tma_load_5d(sA, tm5, fb, cc * a.kc, dx & 1, tc.ox0 + (dx >> 1), dy & 1,
                         tc.oy0 + (dy >> 1));
           }
-          bulk_load(sB,
-                    a.wblk + (size_t)tc.img * a.wblk_img +
-                        ((size_t)(tap * a.cchunks + cc) * a.n_tiles + tc.n0 / a.bn) *
-                                 ((size_t)a.bn * a.kc),
-                    b_bytes, fb);
+          bulk_load(sA + a_bytes, wbase + (size_t)kidx * kstride, b_bytes, fb);
           ++issued;
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
-          if (++cc == a.cchunks) {
-            cc = 0;
-            ++tap;
+          if (!a.klist) {
+            ++kidx;
+            if (++cc == a.cchunks) {
+              cc = 0;
+              if (++kx == a.kw) {
+                kx = 0;
+                ++ky;
+              }
+            }
           }
         }
       }
@@ -379,9 +463,97 @@ __global__ void __maxnreg__(112)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f16((uint32_t)a.bn);
-      const uint32_t row_bytes = (uint32_t)a.kc * 2u;
+    // One thread. The operand descriptors of stage 0 are built once; stage s adds
+    // s * stage_bytes / 16 to the start-address field, the B operand a_bytes / 16, and K slice
+    // k of a chunk 2 * k (32 bytes), so a K step is a few adds and kc / 16 UMMA issues.
+    if (lane == 0 && a.halo) {
+      // halo mode: per tile and chunk, wait for the halo, then per tap wait for its B block and
+      // issue 4 UMMAs whose A operand starts at halo pixel (ky, kx)
+      const uint32_t idesc = idesc_f16((uint32_t)brows);
+      const uint64_t dB0 = smem_desc(smem_u32(smem), 128u), dstage = stage_bytes >> 4;
+      const uint32_t fb_base = smem_u32(full), eb_base = smem_u32(empty);
+      const uint32_t h_base = smem_u32(halo_ring);
+      const uint32_t hfb = smem_u32(fullA), heb = smem_u32(emptyA);
+      const uint64_t hsbo = (uint64_t)((a.hw * 128) >> 4) << 32;
+      int stage = 0, hs = 0;
+      uint32_t phase = 0, hphase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
+        if (!mbar_wait(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, a.err,
+                       DEV_TIMEOUT_ACC_EMPTY))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * a.msub * a.bn);
+        const uint32_t d1 = d + (uint32_t)a.bn;  // subtile 1's accumulator
+        const uint64_t sub_off = (uint64_t)((a.bh * a.hw * 128) >> 4);  // subtile 1: bh rows down
+        bool ok = true;
+        uint32_t accum = 0u;
+        for (int cc = 0; cc < a.cchunks && ok; ++cc) {
+          if (!mbar_wait(hfb + 8u * hs, hphase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          const uint32_t hstart = h_base + hs * a.halo_bytes;
+          int ky = 0, kx = 0;
+          for (int tap = 0; tap < a.taps; ++tap) {
+            if (!mbar_wait(fb_base + 8u * stage, phase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t st = hstart + (uint32_t)(ky * a.hw + kx) * 128u;
+            const uint64_t da = (uint64_t)((st >> 4) & 0x3FFFu) | (1ull << 16) | hsbo |
+                                (1ull << 46) | (2ull << 61);
+            const uint64_t db = dB0 + (uint64_t)stage * dstage;
+            if (a.msub == 2) {
+              const uint64_t da1 = da + sub_off;
+              umma_f16(d, da, db, idesc, accum);
+              umma_f16(d1, da1, db, idesc, accum);
+              umma_f16(d, da + 2, db + 2, idesc, 1u);
+              umma_f16(d1, da1 + 2, db + 2, idesc, 1u);
+              umma_f16(d, da + 4, db + 4, idesc, 1u);
+              umma_f16(d1, da1 + 4, db + 4, idesc, 1u);
+              umma_f16(d, da + 6, db + 6, idesc, 1u);
+              umma_f16(d1, da1 + 6, db + 6, idesc, 1u);
+            } else {
+              umma_f16(d, da, db, idesc, accum);
+              umma_f16(d, da + 2, db + 2, idesc, 1u);
+              umma_f16(d, da + 4, db + 4, idesc, 1u);
+              umma_f16(d, da + 6, db + 6, idesc, 1u);
+            }
+            accum = 1u;
+            umma_commit(eb_base + 8u * stage);
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            if (++kx == a.kw) {
+              kx = 0;
+              ++ky;
+            }
+          }
+          umma_commit(heb + 8u * hs);  // the halo is free once this chunk's UMMAs complete
+          if (++hs == kHaloSlots) {
+            hs = 0;
+            hphase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&accf[acc]));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      umma_commit(smem_u32(drain));
+      mbar_wait_drain(smem_u32(drain), 0, a.err);
+    } else if (lane == 0) {
+      const uint32_t idesc = idesc_f16((uint32_t)brows);
+      const uint64_t dA0 = smem_desc(smem_u32(smem), (uint32_t)a.kc * 2u);
+      const uint64_t dBoff = a_bytes >> 4, dstage = stage_bytes >> 4;
+      const uint32_t fb_base = smem_u32(full), eb_base = smem_u32(empty);
+      const int kk = a.kc >> 4;  // UMMAs per K step: 4, 2 or 1
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -391,22 +563,49 @@ __global__ void __maxnreg__(112)
                        DEV_TIMEOUT_ACC_EMPTY))
           break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * a.bn);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * a.msub * a.bn);
+        const uint64_t sub_off = sub_bytes >> 4;  // subtile 1's A tile follows subtile 0's
+        const int nt = t % a.n_tiles;
+        const int k0 = a.koff ? a.koff[nt] : 0, k1 = a.koff ? a.koff[nt + 1] : ksteps;
         bool ok = true;
-        for (int ks = 0; ks < ksteps; ++ks) {
-          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
+        uint32_t accum = 0u;  // the tile's first UMMA overwrites the accumulator
+        int gcc = 0;          // grouped: chunk (= group) of this K step; taps advance after all
+        uint32_t gfirst = 1u; // grouped: still in tap 0 (each group's first UMMA overwrites)
+        for (int i = k0; i < k1; ++i) {
+          if (!mbar_wait(fb_base + 8u * stage, phase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sA = smem_u32(smem + stage * stage_bytes);
-          const uint32_t sB = sA + a_bytes;
-          for (int k = 0; k < a.kc / 16; ++k) {
-            const uint64_t ad = smem_desc(sA + k * 32u, row_bytes);
-            const uint64_t bd = smem_desc(sB + k * 32u, row_bytes);
-            umma_f16(d_tmem, ad, bd, idesc, (ks | k) != 0 ? 1u : 0u);
+          const uint64_t da = dA0 + (uint64_t)stage * dstage, db = da + dBoff;
+          uint32_t d = d_tmem;
+          if (a.grp_n) {
+            d += (uint32_t)(gcc * a.grp_n);
+            accum = gfirst ^ 1u;
+            if (++gcc == a.cchunks) {
+              gcc = 0;
+              gfirst = 0u;
+            }
           }
-          umma_commit(smem_u32(&empty[stage]));
+          if (a.msub == 2) {  // alternate the two subtiles' accumulators
+            const uint32_t d1 = d + (uint32_t)a.bn;
+            const uint64_t da1 = da + sub_off;
+            umma_f16(d, da, db, idesc, accum);
+            umma_f16(d1, da1, db, idesc, accum);
+            for (int k = 1; k < kk; ++k) {
+              umma_f16(d, da + 2 * k, db + 2 * k, idesc, 1u);
+              umma_f16(d1, da1 + 2 * k, db + 2 * k, idesc, 1u);
+            }
+          } else {
+            umma_f16(d, da, db, idesc, accum);
+            if (kk >= 2) umma_f16(d, da + 2, db + 2, idesc, 1u);
+            if (kk == 4) {
+              umma_f16(d, da + 4, db + 4, idesc, 1u);
+              umma_f16(d, da + 6, db + 6, idesc, 1u);
+            }
+          }
+          accum = 1u;
+          umma_commit(eb_base + 8u * stage);
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
@@ -443,44 +642,49 @@ __global__ void __maxnreg__(112)
         break;
       tc_fence_after();
       const TileCoord tc = decode_tile(a, t);
-      const int oy = tc.oy0 + (m >> a.lbw), ox = tc.ox0 + (m & (a.bw - 1));
-      const bool valid = oy < a.oh && ox < a.ow;
-      long long p1 = 0, p2 = 0, p2o = 0;
-      if constexpr (MODE == kModeR1) {
-        if constexpr (OP != OP_NONE) p1 = tc.img * a.r1_img + oy * a.r1_row + ox * a.r1_pix;
-        if constexpr (OP == OP_CAB) p2 = tc.img * a.r2_img + oy * a.r2_row + ox * a.r2_pix;
-        p2o = tc.img * a.o2_img + oy * a.o2_row + ox * a.o2_pix;
-      }
       if (wg >= nchunks) {
         tc_fence_before();
         mbar_arrive(smem_u32(&acce[acc]));
       }
-      for (int c = wg; c < nchunks; c += kEpiWarpgroups) {
-        float v[kChunk];
-        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.bn + c * kChunk), v);
-        if (c + kEpiWarpgroups >= nchunks) {  // this thread's last read of the accumulator
-          tc_fence_before();
-          mbar_arrive(smem_u32(&acce[acc]));
-        }
-        const int col0 = tc.n0 + c * kChunk;
+      for (int sub = 0; sub < a.msub; ++sub) {
+        const int sy0 = tc.oy0 + sub * a.bh;  // first row of this subtile
+        const int oy = sy0 + (m >> a.lbw), ox = tc.ox0 + (m & (a.bw - 1));
+        const bool valid = oy < a.oh && ox < a.ow;
+        long long p1 = 0, p2 = 0, p2o = 0;
         if constexpr (MODE == kModeR1) {
-          // the slot about to be filled was last stored two chunks ago: wait for that read
-          if (lane == 0) bulk_wait_read<1>();
-          __syncwarp();
-          uint8_t* sl = wslots + slot * kEpiSlotBytes;
-          epi_r1<OP>(a, v, col0, p1, p2, p2o, valid, btab, reinterpret_cast<uint4*>(sl + lane * 32));
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_4d(&tmO, smem_u32(sl), col0, tc.ox0 + (m0 & (a.bw - 1)),
-                         tc.oy0 + (m0 >> a.lbw), tc.img);
-            bulk_commit();
+          if constexpr (OP != OP_NONE) p1 = tc.img * a.r1_img + oy * a.r1_row + ox * a.r1_pix;
+          if constexpr (OP == OP_CAB) p2 = tc.img * a.r2_img + oy * a.r2_row + ox * a.r2_pix;
+          p2o = tc.img * a.o2_img + oy * a.o2_row + ox * a.o2_pix;
+        }
+        const uint32_t tcol = (uint32_t)((acc * a.msub + sub) * a.bn);
+        for (int c = wg; c < nchunks; c += kEpiWarpgroups) {
+          float v[kChunk];
+          tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + tcol + (uint32_t)(c * kChunk), v);
+          if (sub == a.msub - 1 && c + kEpiWarpgroups >= nchunks) {  // last read of the tile
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acce[acc]));
           }
-          slot ^= 1;
-        } else if constexpr (MODE == kModePlanar) {
-          epi_planar(a, v, col0, tc.img, oy, ox, valid, tab, btab);
-        } else {
-          epi_nhwc<OP>(a, v, col0, tc.img, oy, ox, valid, tab, btab);
+          const int col0 = tc.n0 + c * kChunk;
+          if constexpr (MODE == kModeR1) {
+            // the slot about to be filled was last stored two chunks ago: wait for that read
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+            uint8_t* sl = wslots + slot * kEpiSlotBytes;
+            epi_r1<OP>(a, v, col0, p1, p2, p2o, valid, btab,
+                       reinterpret_cast<uint4*>(sl + lane * 32));
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_4d(&tmO, smem_u32(sl), col0, tc.ox0 + (m0 & (a.bw - 1)),
+                           sy0 + (m0 >> a.lbw), tc.img);
+              bulk_commit();
+            }
+            slot ^= 1;
+          } else if constexpr (MODE == kModePlanar) {
+            epi_planar(a, v, col0, tc.img, oy, ox, valid, tab, btab);
+          } else {
+            epi_nhwc<OP>(a, v, col0, tc.img, oy, ox, valid, tab, btab);
+          }
         }
       }
       if (++acc == 2) {
@@ -505,7 +709,8 @@ __global__ void __maxnreg__(112)
 void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const ConvArgs& a, int grid,
                  cudaStream_t stream) {
   const uint32_t smem =
-      conv_smem_bytes(a.kc, a.bn, a.stages, a.n_tiles * a.bn, !a.planar && a.R == 1);
+      conv_smem_bytes(a.kc, a.grp_n ? a.grp_n : a.bn, a.msub, a.stages, a.n_tiles * a.bn,
+                      !a.planar && a.R == 1, a.halo ? a.halo_bytes : 0u);
   // one instantiation per (output mode, epilogue op), each with its own register allocation
   using K = void (*)(CUtensorMap, CUtensorMap, ConvArgs);
   static const K kernels[3][4] = {

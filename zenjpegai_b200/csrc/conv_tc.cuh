@@ -26,7 +26,12 @@ enum EpiOp : int { OP_NONE = 0, OP_ADD = 1, OP_GATE = 2, OP_CAB = 3 };
 struct ConvArgs {
   // tile grid
   int tiles_x, tiles_y, n_img, n_tiles, num_tiles;
-  int bw, bh;          // pixel tile, bh * bw == 128
+  int bw, bh;          // pixel subtile, bh * bw == 128 (one UMMA M)
+  // M subtiles per tile (1 or 2): a tile is bw x (bh * msub) pixels; subtile s (rows s * bh ..)
+  // accumulates into its own TMEM columns and the UMMAs of a K step alternate between the
+  // subtiles, so two independent accumulation chains keep the tensor pipe busy (a chain into
+  // one accumulator waits for the previous UMMA) and each weight block serves 256 pixels
+  int msub;
   // K loop
   int kw, taps, pad_t, pad_l;
   int s2;              // 1: stride-2 conv through the 5-D (parity-split) input view
@@ -40,6 +45,26 @@ struct ConvArgs {
   // index (tap * cchunks + cc) * n_tiles + n_tile: one bulk copy per K step
   const __half* wblk;
   long long wblk_img;  // per-picture weight sets: stride in halves (0: one set for all)
+  // Sparse K: the K steps whose weight block is not all zero, for N tile nt at
+  // klist[koff[nt] .. koff[nt + 1]) (device arrays; null: every K step of every tile), each
+  // entry kidx | kx << 16 | ky << 21 | cc << 26 with kidx = (ky * kw + kx) * cchunks + cc.
+  // Grouped convolutions (one N tile per group) and stride-2 transposed ones (phases that use
+  // a subset of the taps) skip the rest.
+  const uint32_t* klist;
+  const int* koff;
+  // Grouped convolution (grp_n > 0): chunk cc of every tap holds the input channels of group
+  // cc, whose grp_n output columns are accumulator columns [cc * grp_n, (cc + 1) * grp_n); a
+  // K step is grp_n-wide UMMAs into that slice and its weight block is [grp_n][kc].
+  int grp_n;
+  // Halo mode (stride-1 kh x kw conv, kc == 64, tile bw = 8 x bh = 16): per channel chunk one
+  // TMA box of the tile plus its halo, [64, hw = bw + kw - 1, hh = bh + kh - 1] in the 128-byte
+  // swizzle, serves every tap: tap (ky, kx) is the UMMA A operand starting at halo pixel
+  // (ky, kx), rows 128 bytes apart, 8-row groups (one tile row of 8 pixels) hw * 128 bytes
+  // apart. The swizzle is a function of the shared-memory address bits, the same for the TMA
+  // write and the UMMA read, so a window that starts mid-pattern needs no descriptor base
+  // offset. halo_bytes: one halo slot (1 KB multiple).
+  int halo, hw, hh;
+  uint32_t halo_bytes;
   // epilogue
   const float* bias;   // [n_tiles * bn] in packed column order, or null
   float scale;         // weight unscale (power of two)
@@ -73,10 +98,12 @@ struct ConvArgs {
 constexpr int kEpiWarpgroups = 4;
 constexpr int kEpiThreads = 128 * kEpiWarpgroups;
 constexpr int kConvThreads = 64 + kEpiThreads;
-constexpr int kBarrierBytes = 256;
+constexpr int kBarrierBytes = 512;  // 2 * stages + 5 mbarriers (stages <= 16), slots
+constexpr int kMaxStages = 16;
 
-__host__ __device__ inline uint32_t conv_stage_bytes(int kc, int bn) {
-  uint32_t b = 128u * kc * 2u + (uint32_t)bn * kc * 2u;
+// a stage: the A tiles of msub subtiles (128 rows each) + the B block of bn rows
+__host__ __device__ inline uint32_t conv_stage_bytes(int kc, int bn, int msub) {
+  uint32_t b = 128u * msub * kc * 2u + (uint32_t)bn * kc * 2u;
   return (b + 1023u) & ~1023u;
 }
 // Unshuffled NHWC outputs leave through TMA stores: each epilogue warp stages its 32 pixels x
@@ -89,9 +116,21 @@ constexpr uint32_t kEpiStagingBytes = 2u * kEpiSlotBytes * (kEpiThreads / 32);
 __host__ __device__ inline uint32_t conv_fixed_smem(int npad, bool staged) {
   return 1024u + kBarrierBytes + 8u * (uint32_t)npad + (staged ? kEpiStagingBytes : 0u);
 }
-__host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int stages, int npad,
-                                                    bool staged) {
-  return stages * conv_stage_bytes(kc, bn) + conv_fixed_smem(npad, staged);
+constexpr int kHaloSlots = 2;
+// a stage holding only the B block (halo mode)
+__host__ __device__ inline uint32_t conv_bstage_bytes(int kc, int bn) {
+  return ((uint32_t)bn * kc * 2u + 1023u) & ~1023u;
+}
+// The operand rings: `stages` stages of A tile + B block, or (halo_bytes > 0) stages of B
+// blocks only plus kHaloSlots halo slots.
+__host__ __device__ inline uint32_t conv_ring_bytes(int kc, int bn, int msub, int stages,
+                                                    uint32_t halo_bytes) {
+  return halo_bytes ? stages * conv_bstage_bytes(kc, bn) + kHaloSlots * halo_bytes
+                    : stages * conv_stage_bytes(kc, bn, msub);
+}
+__host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int msub, int stages,
+                                                    int npad, bool staged, uint32_t halo_bytes) {
+  return conv_ring_bytes(kc, bn, msub, stages, halo_bytes) + conv_fixed_smem(npad, staged);
 }
 
 // tmO: the output tensor map (TMA-store epilogue, R == 1 NHWC output), unused otherwise.

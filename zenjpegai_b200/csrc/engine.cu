@@ -142,6 +142,8 @@ int make_store_map(Ctx* ctx, CUtensorMap* m, const TView& v, int bx, int by) {
 }
 
 // ---- packing --------------------------------------------------------------------------------
+// Grouped convolutions packed per group (ConvArgs::grp_n) instead of dense-ified.
+constexpr bool kGroupedPacking = false;
 static void choose_k(int cin, int* kc, int* cchunks) {
   *kc = cin > 32 ? 64 : cin > 16 ? 32 : 16;
   *cchunks = (cin + *kc - 1) / *kc;
@@ -171,22 +173,26 @@ float pow2_weight_scale(const float* w, size_t n) {
 // — [bn rows][kc columns] f16, block (tap * cchunks + cc) * n_tiles + nt — already in the
 // swizzled shared-memory image the MMA reads (16-byte chunk j of row r stored at j ^ f(r), the
 // same XOR the TMA applies for 128/64/32-byte swizzles), so the kernel fetches each block with
-// one bulk copy.
+// one bulk copy. A grouped layer (grp_n > 0, one N tile) keeps only block (tap, cc)'s diagonal
+// part: rows cc * grp_n .. + grp_n, i.e. [grp_n rows][kc columns]. With `sparse_k` the K steps
+// whose block is all zero are listed per N tile (ConvArgs::klist) so the kernel skips them.
 static int upload_layer(Ctx* ctx, ConvLayer* L, const std::vector<float>& wf,
-                        const std::vector<float>& bf) {
+                        const std::vector<float>& bf, bool sparse_k) {
   float s = pow2_weight_scale(wf.data(), wf.size());
   L->scale = 1.f / s;
   const int taps = L->kh * L->kw, kc = L->kc, bn = L->bn;
+  const int brows = L->grp_n ? L->grp_n : bn;
   const int chunks16 = kc / 8;  // 16-byte chunks per row
-  std::vector<__half> wh(wf.size());
+  std::vector<__half> wh((size_t)taps * L->cchunks * L->n_tiles * brows * kc);
   size_t blk = 0;
   for (int tap = 0; tap < taps; ++tap)
     for (int cc = 0; cc < L->cchunks; ++cc)
       for (int nt = 0; nt < L->n_tiles; ++nt, ++blk) {
-        __half* dst = wh.data() + blk * (size_t)bn * kc;
-        for (int r = 0; r < bn; ++r) {
+        __half* dst = wh.data() + blk * (size_t)brows * kc;
+        const int row0 = L->grp_n ? cc * L->grp_n : nt * bn;
+        for (int r = 0; r < brows; ++r) {
           const int f = kc == 64 ? (r & 7) : kc == 32 ? ((r >> 1) & 3) : ((r >> 2) & 1);
-          const float* src = wf.data() + ((size_t)tap * L->npad + nt * bn + r) * L->cin_pad + cc * kc;
+          const float* src = wf.data() + ((size_t)tap * L->npad + row0 + r) * L->cin_pad + cc * kc;
           for (int j = 0; j < chunks16; ++j)
             for (int e = 0; e < 8; ++e)
               dst[(size_t)r * kc + ((j ^ f) * 8) + e] = __float2half_rn(src[j * 8 + e] * s);
@@ -200,6 +206,40 @@ static int upload_layer(Ctx* ctx, ConvLayer* L, const std::vector<float>& wf,
   ZJAI_TRY(cuda_check(
       cudaMemcpy(L->bias, bf.data(), bf.size() * sizeof(float), cudaMemcpyHostToDevice),
       "upload bias"));
+  // Live K steps per N tile: a block [bn rows][kc columns] of tap `tap`, chunk cc that is all
+  // zero contributes nothing. A tile keeps at least its first K step (it initialises the
+  // accumulator). When every block is live the kernel runs the dense loop (no lists).
+  if (!sparse_k || L->grp_n) return ZJAI_OK;
+  const int ksteps = taps * L->cchunks;
+  std::vector<int> koff(1, 0);
+  std::vector<uint32_t> klist;
+  for (int nt = 0; nt < L->n_tiles; ++nt) {
+    const size_t before = klist.size();
+    for (int kidx = 0; kidx < ksteps; ++kidx) {
+      const int tap = kidx / L->cchunks, cc = kidx % L->cchunks;
+      bool live = false;
+      for (int r = 0; r < bn && !live; ++r) {
+        const float* src =
+            wf.data() + ((size_t)tap * L->npad + nt * bn + r) * L->cin_pad + cc * kc;
+        for (int j = 0; j < kc && !live; ++j) live = src[j] != 0.f;
+      }
+      if (live)
+        klist.push_back((uint32_t)kidx | (uint32_t)(tap % L->kw) << 16 |
+                        (uint32_t)(tap / L->kw) << 21 | (uint32_t)cc << 26);
+    }
+    if (klist.size() == before) klist.push_back(0u);  // (tap 0, chunk 0)
+    koff.push_back((int)klist.size());
+  }
+  if (klist.size() < (size_t)ksteps * L->n_tiles) {
+    ZJAI_TRY(cuda_check(cudaMalloc(&L->klist, klist.size() * sizeof(uint32_t)), "cudaMalloc"));
+    ZJAI_TRY(cuda_check(cudaMemcpy(L->klist, klist.data(), klist.size() * sizeof(uint32_t),
+                                   cudaMemcpyHostToDevice),
+                        "upload K list"));
+    ZJAI_TRY(cuda_check(cudaMalloc(&L->koff, koff.size() * sizeof(int)), "cudaMalloc"));
+    ZJAI_TRY(cuda_check(
+        cudaMemcpy(L->koff, koff.data(), koff.size() * sizeof(int), cudaMemcpyHostToDevice),
+        "upload K offsets"));
+  }
   (void)ctx;
   return ZJAI_OK;
 }
@@ -216,7 +256,21 @@ int pack_conv(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, i
     return fail(ZJAI_UNSUPPORTED, "conv2d: extra padding with stride 2");
   *L = ConvLayer();
   L->cin = cin;
-  choose_k(cin, &L->kc, &L->cchunks);
+  // A grouped conv whose input group fits one K chunk packs one K chunk per group and keeps only
+  // the diagonal weight blocks: K step (tap, group g) multiplies the group's input channels
+  // into its own ocg output columns (ConvArgs::grp_n), never the zeros of the other groups.
+  // (Kept off: with 32-column UMMAs the per-group chains run slower than the dense-ified
+  // weights through the halo / two-subtile path, which do 4x the MACs at full tensor rate.)
+  const int icg0 = cin / groups, ocg0 = cout / groups;
+  const bool per_group = kGroupedPacking && groups > 1 && ps == 1 &&
+                         (icg0 == 16 || icg0 == 32 || icg0 == 64) && ocg0 % 16 == 0 &&
+                         cout <= 256;
+  if (per_group) {
+    L->kc = icg0;
+    L->cchunks = groups;
+  } else {
+    choose_k(cin, &L->kc, &L->cchunks);
+  }
   L->cin_pad = L->kc * L->cchunks;
   L->kh = kh;
   L->kw = kw;
@@ -229,6 +283,7 @@ int pack_conv(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, i
   L->cph = cout / (ps * ps);
   L->ncols = cout;
   choose_n(cout, &L->bn, &L->n_tiles);
+  if (per_group) L->grp_n = ocg0;
   L->npad = L->bn * L->n_tiles;
   const int taps = kh * kw, icg = cin / groups, ocg = cout / groups, r2 = ps * ps;
   std::vector<float> wf((size_t)taps * L->npad * L->cin_pad, 0.f), bf(L->npad, 0.f);
@@ -244,7 +299,7 @@ int pack_conv(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, i
               w[(((size_t)oc * icg + i) * kh + ky) * kw + kx];
   }
   L->flops_per_px = 2LL * cout * icg * kh * kw;
-  return upload_layer(ctx, L, wf, bf);
+  return upload_layer(ctx, L, wf, bf, false);
 }
 
 int pack_convT(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, int cout, int k,
@@ -304,14 +359,18 @@ int pack_convT(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, 
   }
   // live (tap, column) pairs summed over all columns = MACs per input pixel / cin
   L->flops_per_px = 2LL * live * cin;
-  return upload_layer(ctx, L, wf, bf);
+  return upload_layer(ctx, L, wf, bf, false);
 }
 
 void free_conv(ConvLayer* L) {
   if (L->w) cudaFree(L->w);
   if (L->bias) cudaFree(L->bias);
+  if (L->klist) cudaFree(L->klist);
+  if (L->koff) cudaFree(L->koff);
   L->w = nullptr;
   L->bias = nullptr;
+  L->klist = nullptr;
+  L->koff = nullptr;
 }
 
 void ConvLayer::out_size(int h, int w, int* oh, int* ow, int* out_h, int* out_w) const {
@@ -368,9 +427,26 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
 
   ConvArgs a;
   memset(&a, 0, sizeof a);
-  pick_tile(oh, ow, &a.bw, &a.bh);
+  // Halo mode: a stride-1 conv with several taps and 64-channel chunks reads each chunk's
+  // input once per tile (tile 8 x 16 plus its halo) instead of once per tap.
+  a.halo = L.stride == 1 && L.kh * L.kw > 1 && L.kc == 64 && !L.grp_n && !L.klist &&
+           L.kw <= 9 && L.kh <= 9;
+  if (a.halo) {
+    a.bw = 8;
+    a.bh = 16;
+  } else {
+    pick_tile(oh, ow, &a.bw, &a.bh);
+  }
+  // Two M subtiles per tile (two accumulators of bn columns each, double-buffered: 4 bn TMEM
+  // columns) when the N tile allows it and the picture is taller than one subtile.
+  a.msub = (L.bn <= 128 && !L.grp_n && oh > a.bh) ? 2 : 1;
+  if (a.halo) {
+    a.hw = a.bw + L.kw - 1;
+    a.hh = a.bh * a.msub + L.kh - 1;
+    a.halo_bytes = ((uint32_t)a.hw * a.hh * L.kc * 2u + 1023u) & ~1023u;
+  }
   a.tiles_x = (ow + a.bw - 1) / a.bw;
-  a.tiles_y = (oh + a.bh - 1) / a.bh;
+  a.tiles_y = (oh + a.bh * a.msub - 1) / (a.bh * a.msub);
   a.n_tiles = L.n_tiles;
   a.kw = L.kw;
   a.taps = L.kh * L.kw;
@@ -380,15 +456,18 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   a.cchunks = L.cchunks;
   a.kc = L.kc;
   a.bn = L.bn;
-  const uint32_t stage = conv_stage_bytes(L.kc, L.bn);
+  const int brows = L.grp_n ? L.grp_n : L.bn;
+  const uint32_t stage =
+      a.halo ? conv_bstage_bytes(L.kc, brows) : conv_stage_bytes(L.kc, brows, a.msub);
+  a.grp_n = L.grp_n;
   // unshuffled NHWC outputs leave through the TMA-store epilogue (staging slots in smem)
   const bool staged = !o.planar && L.R == 1;
-  const uint32_t fixed = conv_fixed_smem(L.npad, staged);
+  const uint32_t fixed = conv_fixed_smem(L.npad, staged) + (a.halo ? kHaloSlots * a.halo_bytes : 0u);
   if (fixed + 2 * stage > 232448u)
     return fail(ZJAI_UNSUPPORTED, "conv: too many output columns for one launch");
-  a.stages = (int)std::min<uint32_t>(8, (232448u - fixed) / stage);
+  a.stages = (int)std::min<uint32_t>(kMaxStages, (232448u - fixed) / stage);
   int tc = 32;
-  while (tc < 2 * L.bn) tc *= 2;
+  while (tc < 2 * a.msub * L.bn) tc *= 2;
   a.tmem_cols = tc;
   a.oh = oh;
   a.ow = ow;
@@ -459,9 +538,14 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   }
   a.wblk = L.w;
   a.wblk_img = L.w_img;
+  a.klist = L.klist;
+  a.koff = L.koff;
   if (!a.s2) {
     CUtensorMap tmA;
-    ZJAI_TRY(make_act_map(ctx, &tmA, in, L.kc, a.bw, a.bh));
+    if (a.halo)
+      ZJAI_TRY(make_act_map(ctx, &tmA, in, L.kc, a.hw, a.hh));
+    else
+      ZJAI_TRY(make_act_map(ctx, &tmA, in, L.kc, a.bw, a.bh * a.msub));
     a.n_img = in.n;
     a.num_tiles = a.tiles_x * a.tiles_y * a.n_img * a.n_tiles;
     const double fl = (double)L.flops_per_px * oh * ow * in.n;
@@ -475,7 +559,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     // by the tile's picture. One launch covers the whole batch.
     std::vector<CUtensorMap> maps(in.n);
     for (int i = 0; i < in.n; ++i)
-      ZJAI_TRY(make_act_map_s2(ctx, &maps[i], in, i, L.kc, a.bw, a.bh));
+      ZJAI_TRY(make_act_map_s2(ctx, &maps[i], in, i, L.kc, a.bw, a.bh * a.msub));
     Arena* ar = ctx->cur_arena ? ctx->cur_arena : &ctx->arena;
     void* dmaps = ar->alloc(sizeof(CUtensorMap) * maps.size());
     if (!dmaps) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (tensor maps)");

@@ -134,6 +134,11 @@ struct ConvLayer {
   float scale = 1.f;
   __half* w = nullptr;
   long long w_img = 0;  // per-picture weight sets (stride in halves), 0: one set
+  // live K steps per N tile (ConvArgs::klist / koff), null when every block is live
+  uint32_t* klist = nullptr;
+  int* koff = nullptr;
+  // grouped packing (ConvArgs::grp_n): output columns per group, 0 for a dense layer
+  int grp_n = 0;
   float* bias = nullptr;
   long long flops_per_px = 0;  // algorithmic MACs*2 per conv-output pixel (live taps only)
   // conv output extent (GEMM M space) and shuffled output extent for an input of h x w

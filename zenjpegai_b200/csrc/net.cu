@@ -420,6 +420,8 @@ int Runner::tb(const std::string& p, const TView& x) {
   ConvLayer Lf = *Lo;
   Lf.w = wfold;
   Lf.w_img = wset;
+  Lf.klist = nullptr;  // W_o . blockdiag(A) has its own zero pattern: run every K step
+  Lf.koff = nullptr;
   Lf.scale = 1.f / fs;
   ConvOut oa;
   oa.out = x;
