@@ -1,4 +1,7 @@
 // tcgen05 implicit-GEMM convolution kernel (see conv_tc.cuh for the scheme).
+#include <cstdio>
+#include <cstring>
+
 #include "conv_tc.cuh"
 #include "ptx.cuh"
 
@@ -164,23 +167,25 @@ __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kCh
   }
 }
 
-// NHWC f16 output without a pixel shuffle (R == 1): column n is channel n of this thread's
-// pixel. The chunk's 16 f16 results go to this lane's 32 bytes of the warp's staging slot
-// (`dst`), from which one TMA store writes the warp's 32 pixels; the store clips pixels and
-// channels outside the output view, so lanes outside it (or columns at or past cph, packing
-// padding) may stage anything but must not read residuals. The element offsets of the pixel in
-// r1 / r2 / out2 (p1, p2, p2o) are computed once per tile; residuals are read before the
-// results are staged (in-place ops read exactly what this warp's store then overwrites).
+// NHWC f16 output through the TMA store (R == 1, or a shuffled output whose 16-column chunk
+// lies in one phase): packed columns col0 .. col0 + 15 are channels ch0 .. ch0 + 15 of this
+// thread's output pixel. The chunk's 16 f16 results go to this lane's 32 bytes of the warp's
+// staging slot (`dst`), from which one TMA store writes the warp's 32 pixels; the store clips
+// pixels and channels outside the output view, so lanes outside it (or channels at or past cph,
+// packing padding) may stage anything but must not read residuals. p1 / p2 / p2o are the
+// element offsets of the output pixel in r1 / r2 / out2; residuals are read before the results
+// are staged (in-place ops read exactly what this warp's store then overwrites).
 template <int OP>
-__device__ __forceinline__ void epi_r1(const ConvArgs& a, const float (&v)[kChunk], int col0,
-                                       long long p1, long long p2, long long p2o, bool valid,
-                                       const float* btab, uint4* dst) {
+__device__ __forceinline__ void epi_staged(const ConvArgs& a, const float (&v)[kChunk],
+                                           int col0, int ch0, long long p1, long long p2,
+                                           long long p2o, bool valid, const float* btab,
+                                           uint4* dst) {
   constexpr int G = kChunk / 8;
   uint4 r1[G], r2[G];
   if constexpr (OP != OP_NONE) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const int c = col0 + 8 * g;
+      const int c = ch0 + 8 * g;
       r1[g] = r2[g] = make_uint4(0u, 0u, 0u, 0u);
       if (valid && c < a.cph) {
         r1[g] = __ldg(reinterpret_cast<const uint4*>(a.r1 + p1 + c));
@@ -190,10 +195,10 @@ __device__ __forceinline__ void epi_r1(const ConvArgs& a, const float (&v)[kChun
   }
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    const int c = col0 + 8 * g;
+    const int c = ch0 + 8 * g;
     float x[8];
-    const float4 b0 = *reinterpret_cast<const float4*>(btab + c);
-    const float4 b1 = *reinterpret_cast<const float4*>(btab + c + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(btab + col0 + 8 * g);
+    const float4 b1 = *reinterpret_cast<const float4*>(btab + col0 + 8 * g + 4);
     x[0] = v[8 * g + 0] * a.scale + b0.x;
     x[1] = v[8 * g + 1] * a.scale + b0.y;
     x[2] = v[8 * g + 2] * a.scale + b0.z;
@@ -264,11 +269,14 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
 }  // namespace
 
 // Epilogue output modes: NHWC without a pixel shuffle, NHWC through the shuffle table, planar.
-constexpr int kModeR1 = 0, kModeShuffle = 1, kModePlanar = 2;
+// kModeShuffleStore: shuffled NHWC through TMA stores of one phase per 16-column chunk.
+constexpr int kModeR1 = 0, kModeShuffle = 1, kModePlanar = 2, kModeShuffleStore = 3;
 
-// One CTA of kConvThreads (18 warps) per SM: 18 x 32 x 112 registers fill the register file.
+// One CTA of kConvThreads (18 warps) per SM. The launch bound makes ptxas fit the register
+// allocation to 18 warps (at most 96 registers a thread: allocations are rounded per warp and
+// warps per four).
 template <int MODE, int OP>
-__global__ void __maxnreg__(112)
+__global__ void __launch_bounds__(kConvThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmO,
                    const ConvArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -670,8 +678,8 @@ __global__ void __maxnreg__(112)
             if (lane == 0) bulk_wait_read<1>();
             __syncwarp();
             uint8_t* sl = wslots + slot * kEpiSlotBytes;
-            epi_r1<OP>(a, v, col0, p1, p2, p2o, valid, btab,
-                       reinterpret_cast<uint4*>(sl + lane * 32));
+            epi_staged<OP>(a, v, col0, col0, p1, p2, p2o, valid, btab,
+                           reinterpret_cast<uint4*>(sl + lane * 32));
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -680,6 +688,31 @@ __global__ void __maxnreg__(112)
               bulk_commit();
             }
             slot ^= 1;
+          } else if constexpr (MODE == kModeShuffleStore) {
+            // the chunk is channels ch0 .. ch0 + 15 of phase p = (dy, dx): output pixel
+            // (R oy + dy, R ox + dx); columns of phases >= R^2 are packing padding
+            const uint32_t e = tab[col0];
+            const int p = (int)(e >> 16), ch0 = (int)(e & 0xFFFFu);
+            if (p < a.R * a.R) {
+              const int dy = p >> a.lR, dx = p & (a.R - 1);
+              const long long Y = (long long)oy * a.R + dy, X = (long long)ox * a.R + dx;
+              const long long q1 = tc.img * a.r1_img + Y * a.r1_row + X * a.r1_pix;
+              const long long q2 = tc.img * a.r2_img + Y * a.r2_row + X * a.r2_pix;
+              const long long q2o = tc.img * a.o2_img + Y * a.o2_row + X * a.o2_pix;
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
+              uint8_t* sl = wslots + slot * kEpiSlotBytes;
+              epi_staged<OP>(a, v, col0, ch0, q1, q2, q2o, valid, btab,
+                             reinterpret_cast<uint4*>(sl + lane * 32));
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_5d(a.tmO_img + tc.img, smem_u32(sl), ch0, dx,
+                             tc.ox0 + (m0 & (a.bw - 1)), dy, sy0 + (m0 >> a.lbw));
+                bulk_commit();
+              }
+              slot ^= 1;
+            }
           } else if constexpr (MODE == kModePlanar) {
             epi_planar(a, v, col0, tc.img, oy, ox, valid, tab, btab);
           } else {
@@ -693,7 +726,7 @@ __global__ void __maxnreg__(112)
       }
     }
     // every TMA store of this warp complete before the CTA (and its shared memory) ends
-    if constexpr (MODE == kModeR1) {
+    if constexpr (MODE == kModeR1 || MODE == kModeShuffleStore) {
       if (lane == 0) bulk_wait_all();
     }
   }
@@ -706,20 +739,22 @@ __global__ void __maxnreg__(112)
   }
 }
 
-void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const ConvArgs& a, int grid,
-                 cudaStream_t stream) {
+cudaError_t launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const ConvArgs& a,
+                        int grid, cudaStream_t stream, char* detail, int detail_len) {
   const uint32_t smem =
       conv_smem_bytes(a.kc, a.grp_n ? a.grp_n : a.bn, a.msub, a.stages, a.n_tiles * a.bn,
-                      !a.planar && a.R == 1, a.halo ? a.halo_bytes : 0u);
+                      conv_staged_output(a), a.halo ? a.halo_bytes : 0u);
   // one instantiation per (output mode, epilogue op), each with its own register allocation
   using K = void (*)(CUtensorMap, CUtensorMap, ConvArgs);
-  static const K kernels[3][4] = {
+  static const K kernels[4][4] = {
       {conv_tc_kernel<kModeR1, OP_NONE>, conv_tc_kernel<kModeR1, OP_ADD>,
        conv_tc_kernel<kModeR1, OP_GATE>, conv_tc_kernel<kModeR1, OP_CAB>},
       {conv_tc_kernel<kModeShuffle, OP_NONE>, conv_tc_kernel<kModeShuffle, OP_ADD>,
        conv_tc_kernel<kModeShuffle, OP_GATE>, conv_tc_kernel<kModeShuffle, OP_CAB>},
       {conv_tc_kernel<kModePlanar, OP_NONE>, conv_tc_kernel<kModePlanar, OP_NONE>,
-       conv_tc_kernel<kModePlanar, OP_NONE>, conv_tc_kernel<kModePlanar, OP_NONE>}};
+       conv_tc_kernel<kModePlanar, OP_NONE>, conv_tc_kernel<kModePlanar, OP_NONE>},
+      {conv_tc_kernel<kModeShuffleStore, OP_NONE>, conv_tc_kernel<kModeShuffleStore, OP_ADD>,
+       conv_tc_kernel<kModeShuffleStore, OP_GATE>, conv_tc_kernel<kModeShuffleStore, OP_CAB>}};
   static bool attr_set = false;
   if (!attr_set) {
     for (auto& row : kernels)
@@ -727,8 +762,23 @@ void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const ConvArgs&
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
     attr_set = true;
   }
-  const int mode = a.planar ? kModePlanar : a.R == 1 ? kModeR1 : kModeShuffle;
+  const int mode = a.planar ? kModePlanar
+                   : a.R == 1 ? kModeR1
+                   : a.tmO_img ? kModeShuffleStore
+                               : kModeShuffle;
   kernels[mode][a.op & 3]<<<grid, kConvThreads, smem, stream>>>(tmA, tmO, a);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess && detail) {
+    cudaFuncAttributes fa;
+    memset(&fa, 0, sizeof fa);
+    cudaFuncGetAttributes(&fa, kernels[mode][a.op & 3]);
+    snprintf(detail, detail_len,
+             "mode %d op %d smem %u stages %d grid %d (kernel: %d registers, %d threads max, "
+             "%d dynamic smem max, %zu static smem): %s",
+             mode, a.op, smem, a.stages, grid, fa.numRegs, fa.maxThreadsPerBlock,
+             fa.maxDynamicSharedSizeBytes, fa.sharedSizeBytes, cudaGetErrorString(e));
+  }
+  return e;
 }
 
 }  // namespace zjai

@@ -81,6 +81,9 @@ struct ConvArgs {
   long long r2_pix, r2_row, r2_img;
   __half* out2;        // optional relu6(out)
   long long o2_pix, o2_row, o2_img;
+  // shuffled NHWC output through TMA stores: per picture a 5-D map of the output viewed as
+  // {C, R (dx), W / R, R (dy), H / R}, box [16, 1, bx, 1, 32 / bx] (device array, or null)
+  const CUtensorMap* tmO_img;
   // planar f32 output
   int planar, denorm;
   float* pout;
@@ -133,8 +136,15 @@ __host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int msub, in
   return conv_ring_bytes(kc, bn, msub, stages, halo_bytes) + conv_fixed_smem(npad, staged);
 }
 
+// The output leaves through the TMA-store epilogue (staging slots): unshuffled NHWC, or
+// shuffled NHWC with per-picture phase maps.
+__host__ __device__ inline bool conv_staged_output(const ConvArgs& a) {
+  return !a.planar && (a.R == 1 || a.tmO_img != nullptr);
+}
+
 // tmO: the output tensor map (TMA-store epilogue, R == 1 NHWC output), unused otherwise.
-void launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const ConvArgs& a, int grid,
-                 cudaStream_t stream);
+// Returns the launch status; on an error `detail` (if given) describes the launch.
+cudaError_t launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const ConvArgs& a,
+                        int grid, cudaStream_t stream, char* detail, int detail_len);
 
 }  // namespace zjai

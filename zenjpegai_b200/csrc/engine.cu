@@ -141,6 +141,19 @@ int make_store_map(Ctx* ctx, CUtensorMap* m, const TView& v, int bx, int by) {
                 (size_t)v.img * v.n * 2);
 }
 
+// Picture `img` of an NHWC view as {C, R (dx), W / R, R (dy), H / R}: element (c, dx, X, dy, Y)
+// is pixel (R Y + dy, R X + dx), so a box [16, 1, bx, 1, by] is one phase of bx x by pixels.
+static int make_phase_store_map(Ctx* ctx, CUtensorMap* m, const TView& v, int img, int R, int bx,
+                                int by) {
+  cuuint64_t dims[5] = {(cuuint64_t)v.c, (cuuint64_t)R, (cuuint64_t)(v.w / R), (cuuint64_t)R,
+                        (cuuint64_t)(v.h / R)};
+  cuuint64_t strides[4] = {(cuuint64_t)v.pix * 2, (cuuint64_t)v.pix * 2 * R,
+                           (cuuint64_t)v.row * 2, (cuuint64_t)v.row * 2 * R};
+  cuuint32_t box[5] = {16, 1, (cuuint32_t)bx, 1, (cuuint32_t)by};
+  return encode(ctx, m, 5, v.p + (long long)img * v.img, dims, strides, box,
+                CU_TENSOR_MAP_SWIZZLE_NONE, (size_t)v.img * 2);
+}
+
 // ---- packing --------------------------------------------------------------------------------
 // Grouped convolutions packed per group (ConvArgs::grp_n) instead of dense-ified.
 constexpr bool kGroupedPacking = false;
@@ -460,8 +473,12 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   const uint32_t stage =
       a.halo ? conv_bstage_bytes(L.kc, brows) : conv_stage_bytes(L.kc, brows, a.msub);
   a.grp_n = L.grp_n;
-  // unshuffled NHWC outputs leave through the TMA-store epilogue (staging slots in smem)
-  const bool staged = !o.planar && L.R == 1;
+  // NHWC outputs leave through the TMA-store epilogue (staging slots in smem): unshuffled ones,
+  // and shuffled ones whose phases are whole 16-channel chunks over an extent divisible by R
+  // (so the phase maps clip exactly at the view's edge)
+  const bool shuffle_store = !o.planar && L.R > 1 && L.cph % 16 == 0 &&
+                             want_w % L.R == 0 && want_h % L.R == 0;
+  const bool staged = !o.planar && (L.R == 1 || shuffle_store);
   const uint32_t fixed = conv_fixed_smem(L.npad, staged) + (a.halo ? kHaloSlots * a.halo_bytes : 0u);
   if (fixed + 2 * stage > 232448u)
     return fail(ZJAI_UNSUPPORTED, "conv: too many output columns for one launch");
@@ -532,14 +549,29 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
 
   CUtensorMap tmO;  // output map of the TMA-store epilogue (unused in the other modes)
   memset(&tmO, 0, sizeof tmO);
-  if (staged) {
-    const int bx = std::min(a.bw, 32);
-    ZJAI_TRY(make_store_map(ctx, &tmO, o.out, bx, 32 / bx));
+  const int sbx = std::min(a.bw, 32);
+  if (staged && !shuffle_store) ZJAI_TRY(make_store_map(ctx, &tmO, o.out, sbx, 32 / sbx));
+  if (shuffle_store) {
+    // per-picture phase maps in device memory (from the caller's arena, ordered on its stream)
+    std::vector<CUtensorMap> pm(o.out.n);
+    for (int i = 0; i < o.out.n; ++i)
+      ZJAI_TRY(make_phase_store_map(ctx, &pm[i], o.out, i, L.R, sbx, 32 / sbx));
+    Arena* ar = ctx->cur_arena ? ctx->cur_arena : &ctx->arena;
+    void* dm = ar->alloc(sizeof(CUtensorMap) * pm.size());
+    if (!dm) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (tensor maps)");
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(dm, pm.data(), sizeof(CUtensorMap) * pm.size(),
+                                        cudaMemcpyHostToDevice, ctx->stream),
+                        "tensor map upload"));
+    a.tmO_img = static_cast<const CUtensorMap*>(dm);
   }
   a.wblk = L.w;
   a.wblk_img = L.w_img;
   a.klist = L.klist;
   a.koff = L.koff;
+  cudaError_t lerr = cudaSuccess;
+  char detail[256] = "";
+  // an error left by an earlier asynchronous launch must not be reported as this one's
+  ZJAI_TRY(cuda_check(cudaGetLastError(), "before conv launch"));
   if (!a.s2) {
     CUtensorMap tmA;
     if (a.halo)
@@ -551,7 +583,8 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     const double fl = (double)L.flops_per_px * oh * ow * in.n;
     ctx->launches++;
     timed_launch(ctx, true, fl, 0.0, [&] {
-      launch_conv(tmA, tmO, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
+      lerr = launch_conv(tmA, tmO, a, std::min(a.num_tiles, ctx->sms), ctx->stream, detail,
+                         (int)sizeof detail);
     });
   } else {
     // The parity-split 5-D view has no batch axis: one tensor map per picture, kept in a
@@ -572,10 +605,12 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     const double fl = (double)L.flops_per_px * oh * ow * in.n;
     ctx->launches++;
     timed_launch(ctx, true, fl, 0.0, [&] {
-      launch_conv(maps[0], tmO, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
+      lerr = launch_conv(maps[0], tmO, a, std::min(a.num_tiles, ctx->sms), ctx->stream, detail,
+                         (int)sizeof detail);
     });
   }
-  return cuda_check(cudaGetLastError(), "conv launch");
+  if (lerr != cudaSuccess) return fail(ZJAI_DEVICE, std::string("conv launch: ") + detail);
+  return ZJAI_OK;
 }
 
 }  // namespace zjai
