@@ -51,6 +51,20 @@ def peaks():
         return 1590.0, "fallback (1.59 PFLOP/s)"
 
 
+def conv_traffic(config):
+    """DRAM bytes (read + write) of one step's conv_tc_kernel launches, from the committed ncu
+    capture summary profiles/conv_tc_<config>_step_dram.txt (`dram_bytes_per_step: N`), or None."""
+    path = os.path.join(ROOT, "profiles", "conv_tc_%s_step_dram.txt" % config)
+    try:
+        with open(path) as f:
+            for ln in f:
+                if ln.startswith("dram_bytes_per_step:"):
+                    return float(ln.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
 
@@ -321,7 +335,10 @@ def main():
                 "peak_source": peak_src,
                 "launches_per_step": conv_n,
                 "flops_per_step": conv_fl,
-                "traffic": None,
+                # bytes per step (all conv launches of the step, like `achieved`), from the
+                # committed single-pass ncu capture of this workload
+                "traffic": conv_traffic(args.config),
+                "traffic_unit": "bytes per step (DRAM read + write, ncu)",
             },
             "cpu_baseline": cpu,
             "e2e": {

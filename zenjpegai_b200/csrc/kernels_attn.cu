@@ -234,14 +234,7 @@ __device__ __forceinline__ void dw_stage(uint4* buf, const __half* __restrict__ 
 
 // Packed f32 pair FMA (sm_100 FFMA2): per lane exactly fmaf(a, b, c).
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  unsigned long long d, ua, ub, uc;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(ua) : "f"(a.x), "f"(a.y));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(ub) : "f"(b.x), "f"(b.y));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(uc) : "f"(c.x), "f"(c.y));
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(ua), "l"(ub), "l"(uc));
-  float2 r;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
-  return r;
+  return __ffma2_rn(a, b, c);
 }
 
 __device__ __forceinline__ float elu1(float a) { return a > 0.f ? a : __expf(a) - 1.f; }
