@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const int S = a.stages;
   const uint32_t sub_bytes = 128u * a.kc * 2u;      // A tile of one subtile
   const uint32_t a_bytes = sub_bytes * a.msub;      // A tiles of a stage
-  const int brows = a.grp_n ? a.grp_n : a.bn;  // rows of one weight block (UMMA N)
+  const int brows = a.grp_pc ? a.grp_pc * a.grp_n : a.bn;  // rows of one weight block
   const uint32_t b_bytes = (uint32_t)brows * a.kc * 2u;
   // stage = A tiles + B block; in halo mode a stage holds only the B block and the A halos
   // have their own kHaloSlots-slot ring after the stages
@@ -478,6 +478,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       // halo mode: per tile and chunk, wait for the halo, then per tap wait for its B block and
       // issue 4 UMMAs whose A operand starts at halo pixel (ky, kx)
       const uint32_t idesc = idesc_f16((uint32_t)brows);
+      const uint32_t idesc_g = idesc_f16((uint32_t)(a.grp_pc ? a.grp_n : brows));
       const uint64_t dB0 = smem_desc(smem_u32(smem), 128u), dstage = stage_bytes >> 4;
       const uint32_t fb_base = smem_u32(full), eb_base = smem_u32(empty);
       const uint32_t h_base = smem_u32(halo_ring);
@@ -514,21 +515,26 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             const uint64_t da = (uint64_t)((st >> 4) & 0x3FFFu) | (1ull << 16) | hsbo |
                                 (1ull << 46) | (2ull << 61);
             const uint64_t db = dB0 + (uint64_t)stage * dstage;
+            // grouped: this chunk's (pseudo-)group owns accumulator columns cc * grp_n ..
+            // (grp_n wide); its first tap starts the slice's accumulation
+            const uint32_t gcol = a.grp_pc ? (uint32_t)(cc * a.grp_n) : 0u;
+            const uint32_t idc = a.grp_pc ? idesc_g : idesc;
+            const uint32_t acc0 = a.grp_pc ? (tap == 0 ? 0u : 1u) : accum;
             if (a.msub == 2) {
               const uint64_t da1 = da + sub_off;
-              umma_f16(d, da, db, idesc, accum);
-              umma_f16(d1, da1, db, idesc, accum);
-              umma_f16(d, da + 2, db + 2, idesc, 1u);
-              umma_f16(d1, da1 + 2, db + 2, idesc, 1u);
-              umma_f16(d, da + 4, db + 4, idesc, 1u);
-              umma_f16(d1, da1 + 4, db + 4, idesc, 1u);
-              umma_f16(d, da + 6, db + 6, idesc, 1u);
-              umma_f16(d1, da1 + 6, db + 6, idesc, 1u);
+              umma_f16(d + gcol, da, db, idc, acc0);
+              umma_f16(d1 + gcol, da1, db, idc, acc0);
+              umma_f16(d + gcol, da + 2, db + 2, idc, 1u);
+              umma_f16(d1 + gcol, da1 + 2, db + 2, idc, 1u);
+              umma_f16(d + gcol, da + 4, db + 4, idc, 1u);
+              umma_f16(d1 + gcol, da1 + 4, db + 4, idc, 1u);
+              umma_f16(d + gcol, da + 6, db + 6, idc, 1u);
+              umma_f16(d1 + gcol, da1 + 6, db + 6, idc, 1u);
             } else {
-              umma_f16(d, da, db, idesc, accum);
-              umma_f16(d, da + 2, db + 2, idesc, 1u);
-              umma_f16(d, da + 4, db + 4, idesc, 1u);
-              umma_f16(d, da + 6, db + 6, idesc, 1u);
+              umma_f16(d + gcol, da, db, idc, acc0);
+              umma_f16(d + gcol, da + 2, db + 2, idc, 1u);
+              umma_f16(d + gcol, da + 4, db + 4, idc, 1u);
+              umma_f16(d + gcol, da + 6, db + 6, idc, 1u);
             }
             accum = 1u;
             umma_commit(eb_base + 8u * stage);
@@ -577,8 +583,6 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const int k0 = a.koff ? a.koff[nt] : 0, k1 = a.koff ? a.koff[nt + 1] : ksteps;
         bool ok = true;
         uint32_t accum = 0u;  // the tile's first UMMA overwrites the accumulator
-        int gcc = 0;          // grouped: chunk (= group) of this K step; taps advance after all
-        uint32_t gfirst = 1u; // grouped: still in tap 0 (each group's first UMMA overwrites)
         for (int i = k0; i < k1; ++i) {
           if (!mbar_wait(fb_base + 8u * stage, phase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
             ok = false;
@@ -586,15 +590,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           }
           tc_fence_after();
           const uint64_t da = dA0 + (uint64_t)stage * dstage, db = da + dBoff;
-          uint32_t d = d_tmem;
-          if (a.grp_n) {
-            d += (uint32_t)(gcc * a.grp_n);
-            accum = gfirst ^ 1u;
-            if (++gcc == a.cchunks) {
-              gcc = 0;
-              gfirst = 0u;
-            }
-          }
+          const uint32_t d = d_tmem;
           if (a.msub == 2) {  // alternate the two subtiles' accumulators
             const uint32_t d1 = d + (uint32_t)a.bn;
             const uint64_t da1 = da + sub_off;
@@ -650,25 +646,38 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         break;
       tc_fence_after();
       const TileCoord tc = decode_tile(a, t);
-      if (wg >= nchunks) {
-        tc_fence_before();
-        mbar_arrive(smem_u32(&acce[acc]));
-      }
-      for (int sub = 0; sub < a.msub; ++sub) {
-        const int sy0 = tc.oy0 + sub * a.bh;  // first row of this subtile
-        const int oy = sy0 + (m >> a.lbw), ox = tc.ox0 + (m & (a.bw - 1));
-        const bool valid = oy < a.oh && ox < a.ow;
-        long long p1 = 0, p2 = 0, p2o = 0;
+      // this thread's pixel in subtile `sub` and its residual / copy offsets
+      struct Geo {
+        int sy0, oy, ox;
+        bool valid;
+        long long p1, p2, p2o;
+      };
+      auto geo = [&](int sub) {
+        Geo g;
+        g.sy0 = tc.oy0 + sub * a.bh;  // first row of the subtile
+        g.oy = g.sy0 + (m >> a.lbw);
+        g.ox = tc.ox0 + (m & (a.bw - 1));
+        g.valid = g.oy < a.oh && g.ox < a.ow;
+        g.p1 = g.p2 = g.p2o = 0;
         if constexpr (MODE == kModeR1) {
-          if constexpr (OP != OP_NONE) p1 = tc.img * a.r1_img + oy * a.r1_row + ox * a.r1_pix;
-          if constexpr (OP == OP_CAB) p2 = tc.img * a.r2_img + oy * a.r2_row + ox * a.r2_pix;
-          p2o = tc.img * a.o2_img + oy * a.o2_row + ox * a.o2_pix;
+          if constexpr (OP != OP_NONE)
+            g.p1 = tc.img * a.r1_img + g.oy * a.r1_row + g.ox * a.r1_pix;
+          if constexpr (OP == OP_CAB)
+            g.p2 = tc.img * a.r2_img + g.oy * a.r2_row + g.ox * a.r2_pix;
+          g.p2o = tc.img * a.o2_img + g.oy * a.o2_row + g.ox * a.o2_pix;
         }
+        return g;
+      };
+      // column chunk c of subtile `sub`; `last`: this thread's last TMEM read of the tile
+      auto chunk = [&](const Geo& g, int sub, int c, bool last) {
+        const int sy0 = g.sy0, oy = g.oy, ox = g.ox;
+        const bool valid = g.valid;
+        const long long p1 = g.p1, p2 = g.p2, p2o = g.p2o;
         const uint32_t tcol = (uint32_t)((acc * a.msub + sub) * a.bn);
-        for (int c = wg; c < nchunks; c += kEpiWarpgroups) {
+        {
           float v[kChunk];
           tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + tcol + (uint32_t)(c * kChunk), v);
-          if (sub == a.msub - 1 && c + kEpiWarpgroups >= nchunks) {  // last read of the tile
+          if (last) {
             tc_fence_before();
             mbar_arrive(smem_u32(&acce[acc]));
           }
@@ -719,6 +728,26 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             epi_nhwc<OP>(a, v, col0, tc.img, oy, ox, valid, tab, btab);
           }
         }
+      };
+      if (nchunks >= kEpiWarpgroups) {
+        // warpgroup wg takes the chunks wg, wg + kEpiWarpgroups, .. of every subtile
+        for (int sub = 0; sub < a.msub; ++sub) {
+          const Geo g = geo(sub);
+          for (int c = wg; c < nchunks; c += kEpiWarpgroups)
+            chunk(g, sub, c, sub == a.msub - 1 && c + kEpiWarpgroups >= nchunks);
+        }
+      } else {
+        // narrow accumulators: the items (subtile, chunk) = (it / nchunks, it % nchunks) are
+        // dealt round-robin to the warpgroups, so the subtiles of a tile drain in parallel
+        const int items = a.msub * nchunks;
+        if (wg >= items) {
+          tc_fence_before();
+          mbar_arrive(smem_u32(&acce[acc]));
+        }
+        for (int it = wg; it < items; it += kEpiWarpgroups) {
+          const int sub = it / nchunks;
+          chunk(geo(sub), sub, it - sub * nchunks, it + kEpiWarpgroups >= items);
+        }
       }
       if (++acc == 2) {
         acc = 0;
@@ -742,7 +771,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 cudaError_t launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const ConvArgs& a,
                         int grid, cudaStream_t stream, char* detail, int detail_len) {
   const uint32_t smem =
-      conv_smem_bytes(a.kc, a.grp_n ? a.grp_n : a.bn, a.msub, a.stages, a.n_tiles * a.bn,
+      conv_smem_bytes(a.kc, a.grp_pc ? a.grp_pc * a.grp_n : a.bn, a.msub, a.stages,
+                      a.n_tiles * a.bn,
                       conv_staged_output(a), a.halo ? a.halo_bytes : 0u);
   // one instantiation per (output mode, epilogue op), each with its own register allocation
   using K = void (*)(CUtensorMap, CUtensorMap, ConvArgs);

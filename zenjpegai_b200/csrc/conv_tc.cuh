@@ -52,10 +52,11 @@ struct ConvArgs {
   // a subset of the taps) skip the rest.
   const uint32_t* klist;
   const int* koff;
-  // Grouped convolution (grp_n > 0): chunk cc of every tap holds the input channels of group
-  // cc, whose grp_n output columns are accumulator columns [cc * grp_n, (cc + 1) * grp_n); a
-  // K step is grp_n-wide UMMAs into that slice and its weight block is [grp_n][kc].
-  int grp_n;
+  // Grouped convolution (grp_pc == 1, halo mode): the groups of a 64-channel chunk cc form one
+  // pseudo-group (their weights block-diagonal) owning output columns [cc * grp_n, + grp_n); a
+  // K step is grp_n-wide UMMAs into that slice, and the chunk's weight block is [grp_n][64]
+  // instead of [bn][64] of the dense-ified layer.
+  int grp_n, grp_pc;
   // Halo mode (stride-1 kh x kw conv, kc == 64, tile bw = 8 x bh = 16): per channel chunk one
   // TMA box of the tile plus its halo, [64, hw = bw + kw - 1, hh = bh + kh - 1] in the 128-byte
   // swizzle, serves every tap: tap (ky, kx) is the UMMA A operand starting at halo pixel

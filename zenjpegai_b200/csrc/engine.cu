@@ -155,8 +155,6 @@ static int make_phase_store_map(Ctx* ctx, CUtensorMap* m, const TView& v, int im
 }
 
 // ---- packing --------------------------------------------------------------------------------
-// Grouped convolutions packed per group (ConvArgs::grp_n) instead of dense-ified.
-constexpr bool kGroupedPacking = false;
 static void choose_k(int cin, int* kc, int* cchunks) {
   *kc = cin > 32 ? 64 : cin > 16 ? 32 : 16;
   *cchunks = (cin + *kc - 1) / *kc;
@@ -186,15 +184,15 @@ float pow2_weight_scale(const float* w, size_t n) {
 // — [bn rows][kc columns] f16, block (tap * cchunks + cc) * n_tiles + nt — already in the
 // swizzled shared-memory image the MMA reads (16-byte chunk j of row r stored at j ^ f(r), the
 // same XOR the TMA applies for 128/64/32-byte swizzles), so the kernel fetches each block with
-// one bulk copy. A grouped layer (grp_n > 0, one N tile) keeps only block (tap, cc)'s diagonal
-// part: rows cc * grp_n .. + grp_n, i.e. [grp_n rows][kc columns]. With `sparse_k` the K steps
+// one bulk copy. A grouped layer (grp_pc > 0, one N tile) keeps only the output rows of the
+// chunk's groups: rows cc * grp_pc * grp_n .. + grp_pc * grp_n. With `sparse_k` the K steps
 // whose block is all zero are listed per N tile (ConvArgs::klist) so the kernel skips them.
 static int upload_layer(Ctx* ctx, ConvLayer* L, const std::vector<float>& wf,
                         const std::vector<float>& bf, bool sparse_k) {
   float s = pow2_weight_scale(wf.data(), wf.size());
   L->scale = 1.f / s;
   const int taps = L->kh * L->kw, kc = L->kc, bn = L->bn;
-  const int brows = L->grp_n ? L->grp_n : bn;
+  const int brows = L->grp_pc ? L->grp_pc * L->grp_n : bn;
   const int chunks16 = kc / 8;  // 16-byte chunks per row
   std::vector<__half> wh((size_t)taps * L->cchunks * L->n_tiles * brows * kc);
   size_t blk = 0;
@@ -202,7 +200,7 @@ static int upload_layer(Ctx* ctx, ConvLayer* L, const std::vector<float>& wf,
     for (int cc = 0; cc < L->cchunks; ++cc)
       for (int nt = 0; nt < L->n_tiles; ++nt, ++blk) {
         __half* dst = wh.data() + blk * (size_t)brows * kc;
-        const int row0 = L->grp_n ? cc * L->grp_n : nt * bn;
+        const int row0 = L->grp_pc ? cc * brows : nt * bn;
         for (int r = 0; r < brows; ++r) {
           const int f = kc == 64 ? (r & 7) : kc == 32 ? ((r >> 1) & 3) : ((r >> 2) & 1);
           const float* src = wf.data() + ((size_t)tap * L->npad + row0 + r) * L->cin_pad + cc * kc;
@@ -222,7 +220,7 @@ static int upload_layer(Ctx* ctx, ConvLayer* L, const std::vector<float>& wf,
   // Live K steps per N tile: a block [bn rows][kc columns] of tap `tap`, chunk cc that is all
   // zero contributes nothing. A tile keeps at least its first K step (it initialises the
   // accumulator). When every block is live the kernel runs the dense loop (no lists).
-  if (!sparse_k || L->grp_n) return ZJAI_OK;
+  if (!sparse_k || L->grp_pc) return ZJAI_OK;
   const int ksteps = taps * L->cchunks;
   std::vector<int> koff(1, 0);
   std::vector<uint32_t> klist;
@@ -269,21 +267,15 @@ int pack_conv(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, i
     return fail(ZJAI_UNSUPPORTED, "conv2d: extra padding with stride 2");
   *L = ConvLayer();
   L->cin = cin;
-  // A grouped conv whose input group fits one K chunk packs one K chunk per group and keeps only
-  // the diagonal weight blocks: K step (tap, group g) multiplies the group's input channels
-  // into its own ocg output columns (ConvArgs::grp_n), never the zeros of the other groups.
-  // (Kept off: with 32-column UMMAs the per-group chains run slower than the dense-ified
-  // weights through the halo / two-subtile path, which do 4x the MACs at full tensor rate.)
+  // A stride-1 multi-tap grouped conv whose groups tile 64-channel chunks (16 or 32 input
+  // channels a group) runs in halo mode without the zeros of the other groups: each K step
+  // multiplies only a group's own channels into its own ocg output columns (ConvArgs::grp_pc).
+  // Other grouped convs are dense-ified (zero weights between the groups).
   const int icg0 = cin / groups, ocg0 = cout / groups;
-  const bool per_group = kGroupedPacking && groups > 1 && ps == 1 &&
-                         (icg0 == 16 || icg0 == 32 || icg0 == 64) && ocg0 % 16 == 0 &&
-                         cout <= 256;
-  if (per_group) {
-    L->kc = icg0;
-    L->cchunks = groups;
-  } else {
-    choose_k(cin, &L->kc, &L->cchunks);
-  }
+  const bool per_group = groups > 1 && ps == 1 && stride == 1 && kh * kw > 1 &&
+                         (icg0 == 16 || icg0 == 32) && cin % 64 == 0 && ocg0 % 16 == 0 &&
+                         cout <= 256 && !extra;
+  choose_k(cin, &L->kc, &L->cchunks);
   L->cin_pad = L->kc * L->cchunks;
   L->kh = kh;
   L->kw = kw;
@@ -296,7 +288,12 @@ int pack_conv(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, i
   L->cph = cout / (ps * ps);
   L->ncols = cout;
   choose_n(cout, &L->bn, &L->n_tiles);
-  if (per_group) L->grp_n = ocg0;
+  if (per_group) {
+    // one pseudo-group per 64-channel chunk: the chunk's groups side by side (their weights
+    // block-diagonal), 64 / icg0 * ocg0 output columns, one UMMA chain per subtile and chunk
+    L->grp_n = ocg0 * (64 / icg0);
+    L->grp_pc = 1;
+  }
   L->npad = L->bn * L->n_tiles;
   const int taps = kh * kw, icg = cin / groups, ocg = cout / groups, r2 = ps * ps;
   std::vector<float> wf((size_t)taps * L->npad * L->cin_pad, 0.f), bf(L->npad, 0.f);
@@ -442,8 +439,9 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   memset(&a, 0, sizeof a);
   // Halo mode: a stride-1 conv with several taps and 64-channel chunks reads each chunk's
   // input once per tile (tile 8 x 16 plus its halo) instead of once per tap.
-  a.halo = L.stride == 1 && L.kh * L.kw > 1 && L.kc == 64 && !L.grp_n && !L.klist &&
-           L.kw <= 9 && L.kh <= 9;
+  // (A grouped layer is packed for halo mode and always qualifies.)
+  a.halo = L.stride == 1 && L.kh * L.kw > 1 && L.kc == 64 && !L.klist && L.kw <= 9 &&
+           L.kh <= 9;
   if (a.halo) {
     a.bw = 8;
     a.bh = 16;
@@ -452,7 +450,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   }
   // Two M subtiles per tile (two accumulators of bn columns each, double-buffered: 4 bn TMEM
   // columns) when the N tile allows it and the picture is taller than one subtile.
-  a.msub = (L.bn <= 128 && !L.grp_n && oh > a.bh) ? 2 : 1;
+  a.msub = (L.bn <= 128 && oh > a.bh) ? 2 : 1;
   if (a.halo) {
     a.hw = a.bw + L.kw - 1;
     a.hh = a.bh * a.msub + L.kh - 1;
@@ -469,10 +467,11 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   a.cchunks = L.cchunks;
   a.kc = L.kc;
   a.bn = L.bn;
-  const int brows = L.grp_n ? L.grp_n : L.bn;
+  const int brows = L.grp_pc ? L.grp_pc * L.grp_n : L.bn;
   const uint32_t stage =
       a.halo ? conv_bstage_bytes(L.kc, brows) : conv_stage_bytes(L.kc, brows, a.msub);
   a.grp_n = L.grp_n;
+  a.grp_pc = L.grp_pc;
   // NHWC outputs leave through the TMA-store epilogue (staging slots in smem): unshuffled ones,
   // and shuffled ones whose phases are whole 16-channel chunks over an extent divisible by R
   // (so the phase maps clip exactly at the view's edge)

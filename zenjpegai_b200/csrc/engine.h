@@ -137,8 +137,9 @@ struct ConvLayer {
   // live K steps per N tile (ConvArgs::klist / koff), null when every block is live
   uint32_t* klist = nullptr;
   int* koff = nullptr;
-  // grouped packing (ConvArgs::grp_n): output columns per group, 0 for a dense layer
-  int grp_n = 0;
+  // grouped packing (ConvArgs::grp_n / grp_pc): output columns per group and groups per
+  // 64-channel chunk, 0 for a dense layer
+  int grp_n = 0, grp_pc = 0;
   float* bias = nullptr;
   long long flops_per_px = 0;  // algorithmic MACs*2 per conv-output pixel (live taps only)
   // conv output extent (GEMM M space) and shuffled output extent for an input of h x w
