@@ -226,6 +226,12 @@ int zjai_channel_attention(zjai_ctx *ctx, const float *qkv, int c3, int h, int w
 int zjai_depthwise3x3(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,
                       float *out, int mem);
 
+/* The FFN's depthwise 3x3 followed by its ELU gate (TransformerBlock::forward,
+ * attention.rs:347-355: `ffn_dw.forward` then `math::elu_gate(x1, x2)`, math.rs:376), fused:
+ * x [c][h][w] (c a multiple of 16) -> out [c/2][h][w], out[k] = elu(dw[k]) * dw[k + c/2]. */
+int zjai_depthwise3x3_elu_gate(zjai_ctx *ctx, const float *x, int c, int h, int w,
+                               const float *weight, float *out, int mem);
+
 /* Layer-level timing harness, the GPU counterpart of the crate's conv microbenchmark
  * (benches/conv_kernels.rs:165-187: `PackedConv::new` + `forward` on layer shapes): packs a
  * random conv (or, with `transposed`, a stride-2 transposed conv: k 3 -> p1 op1, k 4 -> p1) of

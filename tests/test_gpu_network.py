@@ -172,13 +172,29 @@ def test_layer_norm(eng, c):
     assert rel_l2(eng.layer_norm(x, wt, b), zo.layer_norm_channels(x, wt, b)) < REL_L2
 
 
-@pytest.mark.parametrize("c", [384, 1024])
-def test_depthwise(eng, c):
+@pytest.mark.parametrize("c,h,w", [(384, 19, 33), (1024, 19, 33), (40, 70, 130), (8, 5, 3),
+                                   (192, 131, 66)])
+def test_depthwise(eng, c, h, w):
+    # row-streaming kernel: 64-column strips, 64-row bands, 64-channel blocks (ragged at
+    # 40 / 8 channels, 130 columns, 70 and 131 rows)
     from zenjpegai_b200 import synthetic as syn
-    x = syn.normal(6, "x", (c, 19, 33))
+    x = syn.normal(6, "x", (c, h, w))
     wt = syn.normal(6, "w", (c, 1, 3, 3), std=0.3)
     got = eng.depthwise3x3(x, wt)
     want = zo.conv2d(x, wt, None, pad=(1, 1), groups=c)
+    assert rel_l2(got, want) < REL_L2
+
+
+@pytest.mark.parametrize("c,h,w", [(1024, 19, 33), (512, 70, 97), (48, 9, 40), (16, 3, 2)])
+def test_depthwise_elu_gate(eng, c, h, w):
+    # FFN depthwise + ELU gate fused: 32-column strips, two 64-channel slabs per block
+    from zenjpegai_b200 import synthetic as syn
+    x = syn.normal(7, "x", (c, h, w))
+    wt = syn.normal(7, "w", (c, 1, 3, 3), std=0.3)
+    got = eng.depthwise3x3_elu_gate(x, wt)
+    d = zo.conv2d(x, wt, None, pad=(1, 1), groups=c)
+    want = zo.elu_gate(d[: c // 2], d[c // 2:])
+    assert got.shape == (c // 2, h, w)
     assert rel_l2(got, want) < REL_L2
 
 

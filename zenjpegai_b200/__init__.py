@@ -159,6 +159,17 @@ class Engine:
                                            _arg(out, x.shape)[0], mem))
         return out
 
+    def depthwise3x3_elu_gate(self, x, weight, out=None):
+        """The FFN's depthwise conv then `math::elu_gate` (attention.rs:347-355), fused:
+        [c, h, w] -> [c/2, h, w]."""
+        c, h, w = x.shape
+        shape = (c // 2, h, w)
+        out = _like(x, shape) if out is None else out
+        px, mem = _arg(x)
+        check(_lib.lib().zjai_depthwise3x3_elu_gate(self.handle, px, c, h, w, _arg(weight)[0],
+                                                    _arg(out, shape)[0], mem))
+        return out
+
 
 def synth_out_size(kind, op, h, w):
     oh, ow = ctypes.c_int(), ctypes.c_int()

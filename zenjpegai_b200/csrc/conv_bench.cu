@@ -115,8 +115,8 @@ extern "C" int zjai_kernel_bench(zjai_ctx* ctx, int kind, int n, int h, int w, i
   const float* temp = gamma + 2 * c;
   auto run = [&] {
     switch (kind) {
-      case ZJAI_KB_DW: launch_dw3x3(x, y, wt, false, ctx->sms, ctx->stream); break;
-      case ZJAI_KB_DW_GATE: launch_dw3x3(x, y, wt, true, ctx->sms, ctx->stream); break;
+      case ZJAI_KB_DW: launch_dw3x3(ctx, x, y, wt, false, ctx->stream); break;
+      case ZJAI_KB_DW_GATE: launch_dw3x3(ctx, x, y, wt, true, ctx->stream); break;
       case ZJAI_KB_LN: launch_layer_norm(x, y, gamma, gamma + c, ctx->stream); break;
       default: launch_attention(x, y, 4, temp, scratch, ctx->sms, ctx->stream); break;
     }

@@ -133,12 +133,16 @@ int make_act_map_s2(Ctx* ctx, CUtensorMap* m, const TView& v, int img, int kc, i
                 (size_t)v.img * 2);
 }
 
-int make_store_map(Ctx* ctx, CUtensorMap* m, const TView& v, int bx, int by) {
+int make_tile_map(Ctx* ctx, CUtensorMap* m, const TView& v, int bc, int bx, int by) {
   cuuint64_t dims[4] = {(cuuint64_t)v.c, (cuuint64_t)v.w, (cuuint64_t)v.h, (cuuint64_t)v.n};
   cuuint64_t strides[3] = {(cuuint64_t)v.pix * 2, (cuuint64_t)v.row * 2, (cuuint64_t)v.img * 2};
-  cuuint32_t box[4] = {16, (cuuint32_t)bx, (cuuint32_t)by, 1};
+  cuuint32_t box[4] = {(cuuint32_t)bc, (cuuint32_t)bx, (cuuint32_t)by, 1};
   return encode(ctx, m, 4, v.p, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE,
                 (size_t)v.img * v.n * 2);
+}
+
+int make_store_map(Ctx* ctx, CUtensorMap* m, const TView& v, int bx, int by) {
+  return make_tile_map(ctx, m, v, 16, bx, by);
 }
 
 // Picture `img` of an NHWC view as {C, R (dx), W / R, R (dy), H / R}: element (c, dx, X, dy, Y)

@@ -118,6 +118,9 @@ int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero = f
 // ---- TMA descriptors ------------------------------------------------------------------------
 int make_act_map(Ctx* ctx, CUtensorMap* m, const TView& v, int kc, int bw, int bh);
 int make_act_map_s2(Ctx* ctx, CUtensorMap* m, const TView& v, int img, int kc, int bw, int bh);
+// box [bc channels, bx, by] over an NHWC f16 view, no swizzle (shared-memory image
+// [by][bx][bc])
+int make_tile_map(Ctx* ctx, CUtensorMap* m, const TView& v, int bc, int bx, int by);
 // output map of the TMA-store epilogue: box [16 channels, bx, by] over an NHWC f16 view
 int make_store_map(Ctx* ctx, CUtensorMap* m, const TView& v, int bx, int by);
 

@@ -6,8 +6,10 @@
 // Plus the latent gather that turns planar f32 latent windows into NHWC f16 tile batches.
 #include "engine.h"
 #include "kernels_attn.h"
+#include "ptx.cuh"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace zjai {
 
@@ -95,14 +97,25 @@ __global__ void layer_norm_kernel(const __half* __restrict__ x, __half* __restri
 // Layer norm for c <= 256: a pixel is a segment of LPP lanes (LPP = c/8 rounded up to a power
 // of two), lane l of a segment holding channels 8l .. 8l+7; sums are segment-local shuffles.
 // A thread handles kLnPix pixels (their loads issued together), its gamma / beta stay in
-// registers. Same arithmetic as layer_norm_kernel: two-pass mean and variance in f32.
-constexpr int kLnPix = 2;
+// registers. Two-pass mean and variance in f32 like layer_norm_kernel; the normalisation
+// multiplies by one reciprocal of the deviation per pixel.
+constexpr int kLnPix = 4;
+
+// Element offset of pixel p (raster order over n, h, w) in a view; `dense`: the view's pixels
+// are contiguous (row == w * pix, img == h * row), so no division is needed.
+__device__ __forceinline__ long long pix_off(int p, int h, int w, long long pix, long long row,
+                                             long long img, bool dense) {
+  if (dense) return (long long)p * pix;
+  const int r = p / w;
+  return (long long)(r / h) * img + (long long)(r % h) * row + (long long)(p - r * w) * pix;
+}
 
 template <int LPP>
 __global__ void __launch_bounds__(256) layer_norm_seg_kernel(
-    const __half* __restrict__ x, __half* __restrict__ y, long long npix, int h, int w, int c,
-    long long xpix, long long xrow, long long ximg, long long ypix, long long yrow,
-    long long yimg, const float* __restrict__ gamma, const float* __restrict__ beta) {
+    const __half* __restrict__ x, __half* __restrict__ y, int npix, int h, int w, int c,
+    long long xpix, long long xrow, long long ximg, bool xdense, long long ypix,
+    long long yrow, long long yimg, bool ydense, const float* __restrict__ gamma,
+    const float* __restrict__ beta) {
   constexpr int SEGS = 256 / LPP;  // pixels per block and pass
   const int sub = threadIdx.x % LPP;
   const int c0 = sub * 8;
@@ -114,15 +127,13 @@ __global__ void __launch_bounds__(256) layer_norm_seg_kernel(
     bt[i] = act ? __ldg(beta + c0 + i) : 0.f;
   }
   float v[kLnPix][8];
-  long long pxl[kLnPix];
+  int pxl[kLnPix];
 #pragma unroll
   for (int k = 0; k < kLnPix; ++k) {
-    pxl[k] = ((long long)blockIdx.x * kLnPix + k) * SEGS + threadIdx.x / LPP;
-    const long long p = pxl[k];
+    pxl[k] = (blockIdx.x * kLnPix + k) * SEGS + threadIdx.x / LPP;
+    const int p = pxl[k];
     if (act && p < npix) {
-      const int px = (int)(p % w);
-      const long long r = p / w;
-      ld8(x + (r / h) * ximg + (r % h) * xrow + px * xpix + c0, v[k]);
+      ld8(x + pix_off(p, h, w, xpix, xrow, ximg, xdense) + c0, v[k]);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[k][i] = 0.f;
@@ -146,15 +157,13 @@ __global__ void __launch_bounds__(256) layer_norm_seg_kernel(
     }
 #pragma unroll
     for (int o = LPP / 2; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    const float denom = sqrtf(sq / (float)c + 1e-5f);
-    const long long p = pxl[k];
+    const float inv = 1.f / sqrtf(sq / (float)c + 1e-5f);  // one division per pixel
+    const int p = pxl[k];
     if (act && p < npix) {
       float o8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o8[i] = (v[k][i] - mean) / denom * gm[i] + bt[i];
-      const int px = (int)(p % w);
-      const long long r = p / w;
-      st8(y + (r / h) * yimg + (r % h) * yrow + px * ypix + c0, o8);
+      for (int i = 0; i < 8; ++i) o8[i] = (v[k][i] - mean) * inv * gm[i] + bt[i];
+      st8(y + pix_off(p, h, w, ypix, yrow, yimg, ydense) + c0, o8);
     }
   }
 }
@@ -351,6 +360,227 @@ __global__ void __launch_bounds__(256, 2)
     __syncthreads();  // all reads of `cur` done before the next iteration refills it
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+
+// ---- depthwise 3x3, row-streaming ----------------------------------------------------------
+// Work unit = (picture, strip of TW columns, band of kDsBand rows, block of 64 output
+// channels). A producer warp streams the unit's input rows with their one-pixel halo (band
+// rows + 2 rows of TW + 2 columns) through a ring of kDsStages shared-memory stages, one TMA
+// box [64 channels, TW + 2, 1 row] per 64-channel slab (gate: two slabs, the block's channels
+// of the first and of the second half); rows and columns outside the picture arrive as zeros,
+// the convolution's padding. 256 compute threads = (column pair, slab, 8-channel group): per
+// input row a thread reads its four staged columns (8 channels each) once, adds them into the
+// three output rows they feed for both of its output columns (rolling accumulators), and
+// stores an output row as soon as its last input row is in. Per output the taps accumulate in
+// (ky, kx) row-major order, two channels per packed f32x2 FMA (as in dw3x3_kernel).
+constexpr int kDsThreads = 512;  // compute threads; one more warp produces
+constexpr int kDsStages = 16;
+constexpr int kDsBand = 64;
+
+template <bool GATE>
+struct DsShape {
+  static constexpr int NS = GATE ? 2 : 1;               // 64-channel slabs per staged row
+  // threads per column pair: a thread holds 2 channel pairs (gate: one ELU pair and its
+  // multiplier pair; plain: 4 consecutive channels)
+  static constexpr int LPC = GATE ? 32 : 16;
+  static constexpr int TW = 2 * kDsThreads / LPC;       // strip width: gate 32, plain 64
+  static constexpr int SW = TW + 2;                     // staged columns
+  static constexpr uint32_t slab = SW * 128u;           // bytes of one slab row
+  static constexpr uint32_t stage = NS * slab;
+  static constexpr uint32_t smem = kDsStages * stage + 2u * kDsStages * 8u + 16u;
+};
+
+// unit u: cb = u % cblocks, band, strip, picture in that order of significance
+struct DsUnits {
+  int strips, bands, cblocks, count;
+};
+
+template <bool GATE>
+__global__ void __launch_bounds__(kDsThreads + 32, 1)
+    dw3x3_stream_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ y, int h,
+                        int w, int c, long long ypix, long long yrow, long long yimg,
+                        const float* __restrict__ wt, DsUnits U, int* err) {
+  using S = DsShape<GATE>;
+  extern __shared__ __align__(128) uint8_t ds_smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(ds_smem + kDsStages * S::stage);
+  uint64_t* empty = full + kDsStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kDsStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cout = GATE ? c / 2 : c;  // output channels (first-half offset of the gate)
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kDsStages; ++i) {
+      mbar_init(smem_u32(&full[i]), 1);
+      mbar_init(smem_u32(&empty[i]), kDsThreads / 32);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kDsThreads / 32) {
+    // ---- producer: one lane issues the row copies of every unit of this CTA
+    if (lane != 0) return;
+    tma_prefetch_desc(&tm);
+    int stage = 0;
+    uint32_t phase = 0;
+    long long issued = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < U.count; u += gridDim.x) {
+      const int cb = u % U.cblocks;
+      int rest = u / U.cblocks;
+      const int band = rest % U.bands;
+      rest /= U.bands;
+      const int strip = rest % U.strips, n = rest / U.strips;
+      const int x0 = strip * S::TW, y0 = band * kDsBand;
+      const int rows = min(kDsBand, h - y0);
+      for (int r = 0; r < rows + 2; ++r) {
+        if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, err, DEV_TIMEOUT_EMPTY)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb = smem_u32(&full[stage]);
+        const uint32_t dst = smem_u32(ds_smem + stage * S::stage);
+        mbar_arrive_expect_tx(fb, S::stage);
+        tma_load_4d(dst, &tm, fb, cb * 64, x0 - 1, y0 - 1 + r, n);
+        if (GATE) tma_load_4d(dst + S::slab, &tm, fb, cout + cb * 64, x0 - 1, y0 - 1 + r, n);
+        ++issued;
+        if (++stage == kDsStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // every copy issued has landed before the CTA's shared memory goes away (consumers that
+    // gave up do not wait for the last ones)
+    const int last = issued < kDsStages ? (int)issued : kDsStages;
+    for (int k = 0; k < last; ++k) {
+      int st = stage - 1 - k;
+      uint32_t ph = phase;
+      if (st < 0) {
+        st += kDsStages;
+        ph ^= 1u;
+      }
+      mbar_wait_drain(smem_u32(&full[st]), ph, err);
+    }
+    return;
+  }
+
+  // ---- compute threads: (column pair, two channel pairs). Plain: channels 4l .. 4l+3 of the
+  // block for lane l of the column pair; gate: ELU-operand pair (2l, 2l+1) of the block's first
+  // half as pair 0 and the matching multiplier pair of the second half as pair 1, so the gate
+  // needs no exchange between threads.
+  const int t = threadIdx.x;
+  const int lane_ch = t % S::LPC;
+  const int cp = t / S::LPC;  // column pair
+  // staged row: column 2 cp (staged column 0 is picture column x0 - 1)
+  const uint32_t my_off = (2 * cp) * 128u + lane_ch * (GATE ? 4u : 8u);
+  int stage = 0;
+  uint32_t phase = 0;
+  int wcb = -1;
+  float2 wr[9][2];  // the thread's two channel pairs, per tap
+  for (int u = blockIdx.x; u < U.count; u += gridDim.x) {
+    const int cb = u % U.cblocks;
+    int rest = u / U.cblocks;
+    const int band = rest % U.bands;
+    rest /= U.bands;
+    const int strip = rest % U.strips, n = rest / U.strips;
+    const int x0 = strip * S::TW, y0 = band * kDsBand;
+    const int rows = min(kDsBand, h - y0);
+    const int ch0 = cb * 64 + lane_ch * (GATE ? 2 : 4);  // first output channel
+    const bool cvalid = ch0 < cout;
+    if (cb != wcb) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int ch = GATE ? ch0 + k * cout : ch0 + 2 * k;
+#pragma unroll
+        for (int tp = 0; tp < 9; ++tp)
+          wr[tp][k] = cvalid ? make_float2(__ldg(wt + ch * 9 + tp), __ldg(wt + (ch + 1) * 9 + tp))
+                             : make_float2(0.f, 0.f);
+      }
+      wcb = cb;
+    }
+    const int xo = x0 + 2 * cp;  // the thread's first output column
+    const bool st0 = cvalid && xo < w, st1 = cvalid && xo + 1 < w;
+    __half* yb = y + n * yimg + (long long)xo * ypix + ch0;
+    // acc[o % 3][column][pair]: output row o is started (first tap a product) by input row o
+    // and complete after input row o + 2; rows outside the band fill slots nobody stores
+    float2 acc[3][2][2];
+
+    // staged column j of the current stage as the thread's 2 channel pairs
+    auto load_col = [&](const uint8_t* src, int j, float2 (&v)[2]) {
+      if (GATE) {
+        const uint32_t e = *reinterpret_cast<const uint32_t*>(src + j * 128);
+        const uint32_t m = *reinterpret_cast<const uint32_t*>(src + S::slab + j * 128);
+        v[0] = __half22float2(*reinterpret_cast<const __half2*>(&e));
+        v[1] = __half22float2(*reinterpret_cast<const __half2*>(&m));
+      } else {
+        const uint2 q = *reinterpret_cast<const uint2*>(src + j * 128);
+        v[0] = __half22float2(*reinterpret_cast<const __half2*>(&q.x));
+        v[1] = __half22float2(*reinterpret_cast<const __half2*>(&q.y));
+      }
+    };
+    // input row r (picture row y0 - 1 + r) with J = r % 3 known at compile time, so the
+    // accumulator slot of output row r - ky ((J - ky) mod 3) is static
+    auto row = [&](auto JJ, int r) -> bool {
+      constexpr int J = decltype(JJ)::value;
+      if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, err, DEV_TIMEOUT_FULL))
+        return false;
+      const uint8_t* src = ds_smem + stage * S::stage + my_off;
+      float2 v[4][2];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) load_col(src, j, v[j]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
+      if (++stage == kDsStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+      // per output the taps go in (ky, kx) order: this row is tap row ky of output r - ky
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+        for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            float2(&a)[2][2] = acc[(J - ky + 3) % 3];
+            const float2 wv = wr[ky * 3 + kx][i];
+            if (ky == 0 && kx == 0) {
+              a[0][i] = __fmul2_rn(wv, v[0][i]);
+              a[1][i] = __fmul2_rn(wv, v[1][i]);
+            } else {
+              a[0][i] = ffma2(wv, v[kx][i], a[0][i]);
+              a[1][i] = ffma2(wv, v[kx + 1][i], a[1][i]);
+            }
+          }
+      const int o = r - 2;  // complete with this row
+      if (o >= 0 && o < rows) {
+        const float2(&ao)[2][2] = acc[(J + 1) % 3];
+        __half* yr = yb + (long long)(y0 + o) * yrow;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const float2(&a)[2] = ao[q];
+          if (!(q == 0 ? st0 : st1)) continue;
+          if (GATE) {
+            *reinterpret_cast<__half2*>(yr + q * ypix) =
+                __floats2half2_rn(elu1(a[0].x) * a[1].x, elu1(a[0].y) * a[1].y);
+          } else {
+            uint2 pk;
+            *reinterpret_cast<__half2*>(&pk.x) = __floats2half2_rn(a[0].x, a[0].y);
+            *reinterpret_cast<__half2*>(&pk.y) = __floats2half2_rn(a[1].x, a[1].y);
+            *reinterpret_cast<uint2*>(yr + q * ypix) = pk;
+          }
+        }
+      }
+      return true;
+    };
+    bool ok = true;
+    for (int r = 0; ok && r < rows + 2; r += 3) {
+      ok = row(std::integral_constant<int, 0>{}, r);
+      if (ok && r + 1 < rows + 2) ok = row(std::integral_constant<int, 1>{}, r + 1);
+      if (ok && r + 2 < rows + 2) ok = row(std::integral_constant<int, 2>{}, r + 2);
+    }
+    if (!ok) return;
+  }
 }
 
 // ---- channel attention -------------------------------------------------------------------
@@ -734,12 +964,15 @@ __global__ void gather_latent_kernel(const float* __restrict__ src, int C, int L
 void launch_layer_norm(const TView& x, const TView& y, const float* gamma, const float* beta,
                        cudaStream_t s) {
   long long pixels = (long long)x.n * x.h * x.w;
-  if (x.c <= 256) {
+  if (x.c <= 256 && pixels < (1ll << 30)) {
     const int lpp = x.c <= 64 ? 8 : x.c <= 128 ? 16 : 32;
     const int grid = blocks_for(pixels, kLnPix * (256 / lpp));
+    const bool xd = x.row == x.w * x.pix && x.img == x.h * x.row;
+    const bool yd = y.row == y.w * y.pix && y.img == y.h * y.row;
 #define ZJAI_LN_SEG(L)                                                                       \
-  layer_norm_seg_kernel<L><<<grid, 256, 0, s>>>(x.p, y.p, pixels, x.h, x.w, x.c, x.pix, x.row, \
-                                                x.img, y.pix, y.row, y.img, gamma, beta)
+  layer_norm_seg_kernel<L><<<grid, 256, 0, s>>>(x.p, y.p, (int)pixels, x.h, x.w, x.c, x.pix,  \
+                                                x.row, x.img, xd, y.pix, y.row, y.img, yd,    \
+                                                gamma, beta)
     if (lpp == 8)
       ZJAI_LN_SEG(8);
     else if (lpp == 16)
@@ -775,12 +1008,44 @@ static void launch_dw3x3_t(const TView& x, const TView& y, const float* wt, int 
       x.p, y.p, x.h, x.w, x.c, x.pix, x.row, x.img, y.pix, y.row, y.img, wt, T, cblocks);
 }
 
-void launch_dw3x3(const TView& x, const TView& y, const float* wt, bool gate, int sms,
-                  cudaStream_t s) {
+template <bool GATE>
+static int launch_dw3x3_stream(Ctx* ctx, const TView& x, const TView& y, const float* wt,
+                               cudaStream_t s) {
+  using S = DsShape<GATE>;
+  CUtensorMap tm;
+  ZJAI_TRY(make_tile_map(ctx, &tm, x, 64, S::SW, 1));
+  static bool attr_set = false;  // the stage ring exceeds the default 48 KB window
+  if (!attr_set) {
+    cudaFuncSetAttribute(dw3x3_stream_kernel<GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         S::smem);
+    attr_set = true;
+  }
+  DsUnits U;
+  U.strips = (x.w + S::TW - 1) / S::TW;
+  U.bands = (x.h + kDsBand - 1) / kDsBand;
+  U.cblocks = ((GATE ? x.c / 2 : x.c) + 63) / 64;
+  U.count = x.n * U.strips * U.bands * U.cblocks;
+  const int grid = std::min(U.count, ctx->sms);
+  dw3x3_stream_kernel<GATE><<<grid, kDsThreads + 32, S::smem, s>>>(
+      tm, y.p, x.h, x.w, x.c, y.pix, y.row, y.img, wt, U, ctx->d_err);
+  return cuda_check(cudaGetLastError(), "dw3x3_stream_kernel launch");
+}
+
+int launch_dw3x3(Ctx* ctx, const TView& x, const TView& y, const float* wt, bool gate,
+                 cudaStream_t s) {
+  if (x.n * x.h * x.w == 0 || x.c == 0) return ZJAI_OK;
+  // the streaming kernel's TMA boxes start at channel multiples of 8 (16 bytes): the gate's
+  // second half must start on one
+  const bool tma_ok = (reinterpret_cast<uintptr_t>(x.p) & 15) == 0 && x.pix % 8 == 0 &&
+                      x.row % 8 == 0 && x.img % 8 == 0 && (!gate || (x.c / 2) % 8 == 0);
+  if (tma_ok)
+    return gate ? launch_dw3x3_stream<true>(ctx, x, y, wt, s)
+                : launch_dw3x3_stream<false>(ctx, x, y, wt, s);
   if (gate)
-    launch_dw3x3_t<true>(x, y, wt, sms, s);
+    launch_dw3x3_t<true>(x, y, wt, ctx->sms, s);
   else
-    launch_dw3x3_t<false>(x, y, wt, sms, s);
+    launch_dw3x3_t<false>(x, y, wt, ctx->sms, s);
+  return cuda_check(cudaGetLastError(), "dw3x3_kernel launch");
 }
 
 // Gram, norms and softmax: the attention matrices attn[n][h][i][j] (scratch + attn_offset).

@@ -6,9 +6,10 @@ namespace zjai {
 
 void launch_layer_norm(const TView& x, const TView& y, const float* gamma, const float* beta,
                        cudaStream_t s);
-// sms: multiprocessor count of the device (the kernel is persistent, two CTAs per SM)
-void launch_dw3x3(const TView& x, const TView& y, const float* wt, bool gate, int sms,
-                  cudaStream_t s);
+// Depthwise 3x3 (weights [c][9] f32), with gate: y has c/2 channels, y[k] = elu(dw[k]) *
+// dw[k + c/2]. Persistent kernels over ctx->sms multiprocessors; returns the launch status.
+int launch_dw3x3(Ctx* ctx, const TView& x, const TView& y, const float* wt, bool gate,
+                 cudaStream_t s);
 // scratch: attention_scratch_floats(n, dim, heads) floats of device memory
 void launch_attention(const TView& qkv, const TView& out, int heads, const float* temp,
                       float* scratch, int sms, cudaStream_t s);

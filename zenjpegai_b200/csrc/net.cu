@@ -396,9 +396,11 @@ int Runner::tb(const std::string& p, const TView& x) {
   ConvOut o;
   o.out = qkv;
   ZJAI_TRY(conv(p + ".prep_data.conv1", ln, o));
+  int st = ZJAI_OK;
   mem_kernel(p + ".prep_data.conv2", "dw", 2 * b16 * 3 * d, 1, [&] {
-    launch_dw3x3(qkv, qkv2, vec(p + ".prep_data.conv2"), false, ctx->sms, stream);
+    st = launch_dw3x3(ctx, qkv, qkv2, vec(p + ".prep_data.conv2"), false, stream);
   });
+  ZJAI_TRY(st);
   float* scratch = static_cast<float*>(
       arena->alloc(attention_scratch_floats(n, d, 4) * sizeof(float)));
   if (!scratch) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (attention scratch)");
@@ -438,8 +440,9 @@ int Runner::tb(const std::string& p, const TView& x) {
   oi.out = f;
   ZJAI_TRY(conv(p + ".ffn.project_in", ln, oi));
   mem_kernel(p + ".ffn.dwconv", "dw", b16 * 3 * hidden, 1, [&] {
-    launch_dw3x3(f, g, vec(p + ".ffn.dwconv"), true, ctx->sms, stream);
+    st = launch_dw3x3(ctx, f, g, vec(p + ".ffn.dwconv"), true, stream);
   });
+  ZJAI_TRY(st);
   ConvOut of;
   of.out = x;
   of.op = OP_ADD;

@@ -383,24 +383,37 @@ int zjai_channel_attention(zjai_ctx* ctx, const float* qkv, int c3, int h, int w
   return finish_call(ctx, mem);
 }
 
-int zjai_depthwise3x3(zjai_ctx* ctx, const float* x, int c, int h, int w, const float* weight,
-                      float* out, int mem) {
+static int depthwise_call(zjai_ctx* ctx, const float* x, int c, int h, int w,
+                          const float* weight, float* out, int mem, bool gate) {
   ZJAI_TRY(ctx_enter(ctx));
-  if (!x || !weight || !out || c <= 0 || c % 8 || h <= 0 || w <= 0)
-    return fail(ZJAI_INVALID_ARGUMENT, "depthwise: bad arguments (channels must be a multiple of 8)");
+  if (!x || !weight || !out || c <= 0 || c % (gate ? 16 : 8) || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT,
+                gate ? "depthwise elu gate: bad arguments (channels must be a multiple of 16)"
+                     : "depthwise: bad arguments (channels must be a multiple of 8)");
   ArenaScope scope(ctx);
   const float *dx, *dw;
   ZJAI_TRY(stage_in(ctx, x, (size_t)c * h * w, mem, &dx));
   ZJAI_TRY(stage_in(ctx, weight, (size_t)c * 9, mem, &dw));
+  const int co = gate ? c / 2 : c;
   TView t, o;
   ZJAI_TRY(planar_to_tensor(ctx, dx, c, h, w, &t));
-  ZJAI_TRY(alloc_tensor(ctx, 1, h, w, c, &o));
-  launch_dw3x3(t, o, dw, false, ctx->sms, ctx->stream);
+  ZJAI_TRY(alloc_tensor(ctx, 1, h, w, co, &o));
+  ZJAI_TRY(launch_dw3x3(ctx, t, o, dw, gate, ctx->stream));
   float* dout;
-  ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)c * h * w, mem, &dout));
+  ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)co * h * w, mem, &dout));
   launch_nhwc_to_planar(o, dout, ctx->stream);
-  ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)c * h * w, mem));
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)co * h * w, mem));
   return finish_call(ctx, mem);
+}
+
+int zjai_depthwise3x3(zjai_ctx* ctx, const float* x, int c, int h, int w, const float* weight,
+                      float* out, int mem) {
+  return depthwise_call(ctx, x, c, h, w, weight, out, mem, false);
+}
+
+int zjai_depthwise3x3_elu_gate(zjai_ctx* ctx, const float* x, int c, int h, int w,
+                               const float* weight, float* out, int mem) {
+  return depthwise_call(ctx, x, c, h, w, weight, out, mem, true);
 }
 
 }  // extern "C"
