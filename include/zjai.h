@@ -236,8 +236,9 @@ int zjai_depthwise3x3_elu_gate(zjai_ctx *ctx, const float *x, int c, int h, int 
  * (benches/conv_kernels.rs:165-187: `PackedConv::new` + `forward` on layer shapes): packs a
  * random conv (or, with `transposed`, a stride-2 transposed conv: k 3 -> p1 op1, k 4 -> p1) of
  * the given geometry, runs it `reps` times on n pseudo-random NHWC f16 maps of h x w in the
- * context arena (ReLU epilogue, plus a residual add when `residual`) and returns the mean
- * device time per launch in *ms and the algorithmic FLOPs per launch in *flops (may be NULL). */
+ * context arena (`residual` 0: ReLU epilogue; 1: ReLU plus a residual add; 2: the planar f32
+ * output of a network's final layer, denormalised) and returns the mean device time per
+ * launch in *ms and the algorithmic FLOPs per launch in *flops (may be NULL). */
 int zjai_conv_bench(zjai_ctx *ctx, int n, int h, int w, int cin, int cout, int k, int stride,
                     int groups, int transposed, int residual, int reps, double *ms,
                     double *flops);

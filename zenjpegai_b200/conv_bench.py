@@ -33,6 +33,8 @@ LAYERS = [
     ("hop_ffn_out_1x1_512_128@H4x28", 28, 128, 128, 512, 128, 1, 1, 1, 0, 1),
     ("hop_us_convT3_128@H4x28", 28, 128, 128, 128, 128, 3, 1, 1, 1, 0),
     ("hop_subscale_s2_128@H4x1", 1, 128, 128, 128, 128, 3, 2, 1, 0, 0),
+    # residual 2: the network's final layer (planar f32 output, denormalised)
+    ("hop_conv4_t_128_1_planar@H2x28", 28, 256, 256, 128, 1, 3, 1, 1, 1, 2),
 ]
 
 KB_DW, KB_DW_GATE, KB_LN, KB_ATTN = 0, 1, 2, 3

@@ -54,15 +54,28 @@ extern "C" int zjai_conv_bench(zjai_ctx* ctx, int n, int h, int w, int cin, int 
   L.out_size(h, w, &oh, &ow, &out_h, &out_w);
   TView x, y;
   ZJAI_TRY(alloc_tensor(ctx, n, h, w, cin, &x));
-  ZJAI_TRY(alloc_tensor(ctx, n, out_h, out_w, L.cph, &y));
   fill_kernel<<<1024, 256, 0, ctx->stream>>>(x.p, (long long)n * x.img, 17u);
-  fill_kernel<<<1024, 256, 0, ctx->stream>>>(y.p, (long long)n * y.img, 29u);
   ConvOut o;
-  o.out = y;
-  o.act1 = ACT_RELU;
-  if (residual) {
-    o.op = OP_ADD;
-    o.r1 = &y;
+  if (residual == 2) {
+    // a synthesis network's final layer: planar f32 planes [n][cph][out_h][out_w], denormalised
+    const long long plane = (long long)out_h * out_w;
+    float* pl = static_cast<float*>(ctx->arena.alloc(sizeof(float) * plane * L.cph * n));
+    if (!pl) return fail(ZJAI_LIMIT_EXCEEDED, "conv_bench: arena exhausted");
+    o.planar = true;
+    o.denorm = true;
+    o.pout = pl;
+    o.p_plane = plane;
+    o.p_row = out_w;
+    o.p_img = plane * L.cph;
+  } else {
+    ZJAI_TRY(alloc_tensor(ctx, n, out_h, out_w, L.cph, &y));
+    fill_kernel<<<1024, 256, 0, ctx->stream>>>(y.p, (long long)n * y.img, 29u);
+    o.out = y;
+    o.act1 = ACT_RELU;
+    if (residual) {
+      o.op = OP_ADD;
+      o.r1 = &y;
+    }
   }
   ZJAI_TRY(run_conv(ctx, L, x, o));  // warm-up
   cudaEvent_t e0, e1;

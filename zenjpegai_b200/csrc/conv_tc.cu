@@ -258,11 +258,22 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
     if (Y >= a.out_h || X >= a.out_w) continue;
     const int PY = py0 + Y, PX = px0 + X;
     if (PY < cy0 || PY >= cy1 || PX < cx0 || PX >= cx1) continue;
-    if (PY % a.sv || PX % a.sh) continue;
+    // chroma subsampling: keep the samples on the sv x sh grid (power-of-two factors by
+    // shifts and masks)
+    int SY, SX;
+    if (a.lsv >= 0) {
+      if ((PY & ((1 << a.lsv) - 1)) | (PX & ((1 << a.lsh) - 1))) continue;
+      SY = PY >> a.lsv;
+      SX = PX >> a.lsh;
+    } else {
+      if (PY % a.sv || PX % a.sh) continue;
+      SY = PY / a.sv;
+      SX = PX / a.sh;
+    }
     float x = act_rt(v[j] * a.scale + btab[col0 + j], a.act1);
     if (a.denorm) x = fminf(fmaxf(x * 128.f + 127.5f, 0.f), 255.f);
     float* dst = (ch == 1 && a.pout2) ? a.pout2 : a.pout + ch * a.p_plane;
-    dst[(a.img_win ? 0 : img * a.p_img) + (PY / a.sv) * a.p_row + PX / a.sh] = x;
+    dst[(a.img_win ? 0 : img * a.p_img) + (long long)SY * a.p_row + SX] = x;
   }
 }
 
@@ -288,11 +299,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const int brows = a.grp_pc ? a.grp_pc * a.grp_n : a.bn;  // rows of one weight block
   const uint32_t b_bytes = (uint32_t)brows * a.kc * 2u;
   // stage = A tiles + B block; in halo mode a stage holds only the B block and the A halos
-  // have their own kHaloSlots-slot ring after the stages
+  // have their own a.hslots-slot ring after the stages
   const uint32_t stage_bytes =
       a.halo ? conv_bstage_bytes(a.kc, brows) : conv_stage_bytes(a.kc, brows, a.msub);
   const uint32_t ring_bytes =
-      conv_ring_bytes(a.kc, brows, a.msub, S, a.halo ? a.halo_bytes : 0u);
+      conv_ring_bytes(a.kc, brows, a.msub, S, a.halo ? a.halo_bytes : 0u, a.hslots);
   uint8_t* halo_ring = smem + S * stage_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ring_bytes);
   uint64_t* full = bars;
@@ -301,8 +312,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint64_t* acce = bars + 2 * S + 2;
   uint64_t* drain = bars + 2 * S + 4;
   uint64_t* fullA = bars + 2 * S + 5;            // halo ring
-  uint64_t* emptyA = bars + 2 * S + 5 + kHaloSlots;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5 + 2 * kHaloSlots);
+  uint64_t* emptyA = bars + 2 * S + 5 + kMaxHaloSlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5 + 2 * kMaxHaloSlots);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* tab = reinterpret_cast<uint32_t*>(smem + ring_bytes + kBarrierBytes);
   const int npad = a.n_tiles * a.bn;
@@ -323,7 +334,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       mbar_init(smem_u32(&acce[i]), kEpiThreads);
     }
     mbar_init(smem_u32(drain), 1);
-    for (int i = 0; i < kHaloSlots; ++i) {
+    for (int i = 0; i < a.hslots; ++i) {
       mbar_init(smem_u32(&fullA[i]), 1);
       mbar_init(smem_u32(&emptyA[i]), 1);
     }
@@ -374,7 +385,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           tma_load_4d(h_base + hs * a.halo_bytes, &tmA, hfb + 8u * hs, cc * a.kc,
                       tc.ox0 - a.pad_l, tc.oy0 - a.pad_t, tc.img);
           ++hissued;
-          if (++hs == kHaloSlots) {
+          if (++hs == a.hslots) {
             hs = 0;
             hphase ^= 1u;
           }
@@ -401,10 +412,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           mbar_wait_drain(smem_u32(&full[s]), (uint32_t)((last / S) & 1), a.err);
         }
       }
-      for (int s = 0; s < kHaloSlots; ++s) {
+      for (int s = 0; s < a.hslots; ++s) {
         if (hissued > s) {
-          long long last = ((hissued - 1 - s) / kHaloSlots) * kHaloSlots + s;
-          mbar_wait_drain(smem_u32(&fullA[s]), (uint32_t)((last / kHaloSlots) & 1), a.err);
+          long long last = ((hissued - 1 - s) / a.hslots) * a.hslots + s;
+          mbar_wait_drain(smem_u32(&fullA[s]), (uint32_t)((last / a.hslots) & 1), a.err);
         }
       }
     } else if (lane == 0) {
@@ -477,15 +488,21 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     if (lane == 0 && a.halo) {
       // halo mode: per tile and chunk, wait for the halo, then per tap wait for its B block and
       // issue 4 UMMAs whose A operand starts at halo pixel (ky, kx)
-      const uint32_t idesc = idesc_f16((uint32_t)brows);
-      const uint32_t idesc_g = idesc_f16((uint32_t)(a.grp_pc ? a.grp_n : brows));
+      const uint32_t idesc = idesc_f16((uint32_t)(a.grp_pc ? a.grp_n : brows));
       const uint64_t dB0 = smem_desc(smem_u32(smem), 128u), dstage = stage_bytes >> 4;
       const uint32_t fb_base = smem_u32(full), eb_base = smem_u32(empty);
-      const uint32_t h_base = smem_u32(halo_ring);
       const uint32_t hfb = smem_u32(fullA), heb = smem_u32(emptyA);
-      const uint64_t hsbo = (uint64_t)((a.hw * 128) >> 4) << 32;
+      // A descriptor of halo slot 0's window at tap (0, 0): rows 128 bytes apart, 8-row groups
+      // (one tile row) hw * 128 bytes apart; a tap or a slot moves only the start address
+      // field (16-byte units, no carry out of its 14 bits below 256 KB), so the per-tap
+      // descriptors are additions: +8 per kx, +8 (hw - kw) more at the end of a tap row
+      const uint64_t dH0 = (uint64_t)((smem_u32(halo_ring) >> 4) & 0x3FFFu) | (1ull << 16) |
+                           ((uint64_t)((a.hw * 128) >> 4) << 32) | (1ull << 46) | (2ull << 61);
+      const uint64_t dslot = a.halo_bytes >> 4, row_skip = (uint64_t)(a.hw - a.kw) * 8u;
+      const uint64_t sub_off = (uint64_t)((a.bh * a.hw * 128) >> 4);  // subtile 1: bh rows down
       int stage = 0, hs = 0;
       uint32_t phase = 0, hphase = 0;
+      uint64_t db = dB0;
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
@@ -493,62 +510,58 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                        DEV_TIMEOUT_ACC_EMPTY))
           break;
         tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(acc * a.msub * a.bn);
-        const uint32_t d1 = d + (uint32_t)a.bn;  // subtile 1's accumulator
-        const uint64_t sub_off = (uint64_t)((a.bh * a.hw * 128) >> 4);  // subtile 1: bh rows down
+        const uint32_t d0 = tmem_base + (uint32_t)(acc * a.msub * a.bn);
         bool ok = true;
-        uint32_t accum = 0u;
         for (int cc = 0; cc < a.cchunks && ok; ++cc) {
           if (!mbar_wait(hfb + 8u * hs, hphase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
             ok = false;
             break;
           }
-          const uint32_t hstart = h_base + hs * a.halo_bytes;
-          int ky = 0, kx = 0;
+          // grouped: this chunk's (pseudo-)group owns accumulator columns cc * grp_n ..
+          // (grp_n wide) and its first tap starts them; dense: the tile's first UMMA starts all
+          const uint32_t d = d0 + (a.grp_pc ? (uint32_t)(cc * a.grp_n) : 0u);
+          const uint32_t d1 = d + (uint32_t)a.bn;  // subtile 1's accumulator
+          const bool fresh = a.grp_pc || cc == 0;
+          uint64_t da = dH0 + (uint64_t)hs * dslot;
+          int kx = 0;
           for (int tap = 0; tap < a.taps; ++tap) {
             if (!mbar_wait(fb_base + 8u * stage, phase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t st = hstart + (uint32_t)(ky * a.hw + kx) * 128u;
-            const uint64_t da = (uint64_t)((st >> 4) & 0x3FFFu) | (1ull << 16) | hsbo |
-                                (1ull << 46) | (2ull << 61);
-            const uint64_t db = dB0 + (uint64_t)stage * dstage;
-            // grouped: this chunk's (pseudo-)group owns accumulator columns cc * grp_n ..
-            // (grp_n wide); its first tap starts the slice's accumulation
-            const uint32_t gcol = a.grp_pc ? (uint32_t)(cc * a.grp_n) : 0u;
-            const uint32_t idc = a.grp_pc ? idesc_g : idesc;
-            const uint32_t acc0 = a.grp_pc ? (tap == 0 ? 0u : 1u) : accum;
+            const uint32_t acc0 = (fresh && tap == 0) ? 0u : 1u;
             if (a.msub == 2) {
               const uint64_t da1 = da + sub_off;
-              umma_f16(d + gcol, da, db, idc, acc0);
-              umma_f16(d1 + gcol, da1, db, idc, acc0);
-              umma_f16(d + gcol, da + 2, db + 2, idc, 1u);
-              umma_f16(d1 + gcol, da1 + 2, db + 2, idc, 1u);
-              umma_f16(d + gcol, da + 4, db + 4, idc, 1u);
-              umma_f16(d1 + gcol, da1 + 4, db + 4, idc, 1u);
-              umma_f16(d + gcol, da + 6, db + 6, idc, 1u);
-              umma_f16(d1 + gcol, da1 + 6, db + 6, idc, 1u);
+              umma_f16(d, da, db, idesc, acc0);
+              umma_f16(d1, da1, db, idesc, acc0);
+              umma_f16(d, da + 2, db + 2, idesc, 1u);
+              umma_f16(d1, da1 + 2, db + 2, idesc, 1u);
+              umma_f16(d, da + 4, db + 4, idesc, 1u);
+              umma_f16(d1, da1 + 4, db + 4, idesc, 1u);
+              umma_f16(d, da + 6, db + 6, idesc, 1u);
+              umma_f16(d1, da1 + 6, db + 6, idesc, 1u);
             } else {
-              umma_f16(d + gcol, da, db, idc, acc0);
-              umma_f16(d + gcol, da + 2, db + 2, idc, 1u);
-              umma_f16(d + gcol, da + 4, db + 4, idc, 1u);
-              umma_f16(d + gcol, da + 6, db + 6, idc, 1u);
+              umma_f16(d, da, db, idesc, acc0);
+              umma_f16(d, da + 2, db + 2, idesc, 1u);
+              umma_f16(d, da + 4, db + 4, idesc, 1u);
+              umma_f16(d, da + 6, db + 6, idesc, 1u);
             }
-            accum = 1u;
             umma_commit(eb_base + 8u * stage);
+            db += dstage;
             if (++stage == S) {
               stage = 0;
               phase ^= 1u;
+              db = dB0;
             }
+            da += 8;
             if (++kx == a.kw) {
               kx = 0;
-              ++ky;
+              da += row_skip;
             }
           }
           umma_commit(heb + 8u * hs);  // the halo is free once this chunk's UMMAs complete
-          if (++hs == kHaloSlots) {
+          if (++hs == a.hslots) {
             hs = 0;
             hphase ^= 1u;
           }
@@ -570,6 +583,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const int kk = a.kc >> 4;  // UMMAs per K step: 4, 2 or 1
       int stage = 0;
       uint32_t phase = 0;
+      uint64_t da = dA0;  // stage's A descriptor (B follows at dBoff)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
@@ -577,7 +591,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                        DEV_TIMEOUT_ACC_EMPTY))
           break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * a.msub * a.bn);
+        const uint32_t d = tmem_base + (uint32_t)(acc * a.msub * a.bn);
+        const uint32_t d1 = d + (uint32_t)a.bn;  // subtile 1's accumulator
         const uint64_t sub_off = sub_bytes >> 4;  // subtile 1's A tile follows subtile 0's
         const int nt = t % a.n_tiles;
         const int k0 = a.koff ? a.koff[nt] : 0, k1 = a.koff ? a.koff[nt + 1] : ksteps;
@@ -589,16 +604,21 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t da = dA0 + (uint64_t)stage * dstage, db = da + dBoff;
-          const uint32_t d = d_tmem;
+          const uint64_t db = da + dBoff;
           if (a.msub == 2) {  // alternate the two subtiles' accumulators
-            const uint32_t d1 = d + (uint32_t)a.bn;
             const uint64_t da1 = da + sub_off;
             umma_f16(d, da, db, idesc, accum);
             umma_f16(d1, da1, db, idesc, accum);
-            for (int k = 1; k < kk; ++k) {
-              umma_f16(d, da + 2 * k, db + 2 * k, idesc, 1u);
-              umma_f16(d1, da1 + 2 * k, db + 2 * k, idesc, 1u);
+            if (kk == 4) {
+              umma_f16(d, da + 2, db + 2, idesc, 1u);
+              umma_f16(d1, da1 + 2, db + 2, idesc, 1u);
+              umma_f16(d, da + 4, db + 4, idesc, 1u);
+              umma_f16(d1, da1 + 4, db + 4, idesc, 1u);
+              umma_f16(d, da + 6, db + 6, idesc, 1u);
+              umma_f16(d1, da1 + 6, db + 6, idesc, 1u);
+            } else if (kk == 2) {
+              umma_f16(d, da + 2, db + 2, idesc, 1u);
+              umma_f16(d1, da1 + 2, db + 2, idesc, 1u);
             }
           } else {
             umma_f16(d, da, db, idesc, accum);
@@ -610,9 +630,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           }
           accum = 1u;
           umma_commit(eb_base + 8u * stage);
+          da += dstage;
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
+            da = dA0;
           }
         }
         if (!ok) break;
@@ -773,7 +795,7 @@ cudaError_t launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const Co
   const uint32_t smem =
       conv_smem_bytes(a.kc, a.grp_pc ? a.grp_pc * a.grp_n : a.bn, a.msub, a.stages,
                       a.n_tiles * a.bn,
-                      conv_staged_output(a), a.halo ? a.halo_bytes : 0u);
+                      conv_staged_output(a), a.halo ? a.halo_bytes : 0u, a.hslots);
   // one instantiation per (output mode, epilogue op), each with its own register allocation
   using K = void (*)(CUtensorMap, CUtensorMap, ConvArgs);
   static const K kernels[4][4] = {

@@ -63,8 +63,9 @@ struct ConvArgs {
   // (ky, kx), rows 128 bytes apart, 8-row groups (one tile row of 8 pixels) hw * 128 bytes
   // apart. The swizzle is a function of the shared-memory address bits, the same for the TMA
   // write and the UMMA read, so a window that starts mid-pattern needs no descriptor base
-  // offset. halo_bytes: one halo slot (1 KB multiple).
-  int halo, hw, hh;
+  // offset. halo_bytes: one halo slot (1 KB multiple); hslots: slots in the halo ring (2 ..
+  // kMaxHaloSlots: layers with little MMA work per halo keep more halos in flight).
+  int halo, hw, hh, hslots;
   uint32_t halo_bytes;
   // epilogue
   const float* bias;   // [n_tiles * bn] in packed column order, or null
@@ -94,6 +95,7 @@ struct ConvArgs {
   int cy0, cy1, cx0, cx1;
   const int* img_win;  // per-image {py0, px0, cy0, cy1, cx0, cx1} (device), or null
   int sv, sh;
+  int lsv, lsh;        // log2 of sv / sh when both are powers of two, else -1
   int* err;
 };
 
@@ -102,7 +104,7 @@ struct ConvArgs {
 constexpr int kEpiWarpgroups = 4;
 constexpr int kEpiThreads = 128 * kEpiWarpgroups;
 constexpr int kConvThreads = 64 + kEpiThreads;
-constexpr int kBarrierBytes = 512;  // 2 * stages + 5 mbarriers (stages <= 16), slots
+constexpr int kBarrierBytes = 512;  // 2 * stages + 5 + 2 * halo slots mbarriers, slots
 constexpr int kMaxStages = 16;
 
 // a stage: the A tiles of msub subtiles (128 rows each) + the B block of bn rows
@@ -120,21 +122,23 @@ constexpr uint32_t kEpiStagingBytes = 2u * kEpiSlotBytes * (kEpiThreads / 32);
 __host__ __device__ inline uint32_t conv_fixed_smem(int npad, bool staged) {
   return 1024u + kBarrierBytes + 8u * (uint32_t)npad + (staged ? kEpiStagingBytes : 0u);
 }
-constexpr int kHaloSlots = 2;
+constexpr int kMaxHaloSlots = 4;
 // a stage holding only the B block (halo mode)
 __host__ __device__ inline uint32_t conv_bstage_bytes(int kc, int bn) {
   return ((uint32_t)bn * kc * 2u + 1023u) & ~1023u;
 }
 // The operand rings: `stages` stages of A tile + B block, or (halo_bytes > 0) stages of B
-// blocks only plus kHaloSlots halo slots.
+// blocks only plus hslots halo slots.
 __host__ __device__ inline uint32_t conv_ring_bytes(int kc, int bn, int msub, int stages,
-                                                    uint32_t halo_bytes) {
-  return halo_bytes ? stages * conv_bstage_bytes(kc, bn) + kHaloSlots * halo_bytes
+                                                    uint32_t halo_bytes, int hslots) {
+  return halo_bytes ? stages * conv_bstage_bytes(kc, bn) + hslots * halo_bytes
                     : stages * conv_stage_bytes(kc, bn, msub);
 }
 __host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int msub, int stages,
-                                                    int npad, bool staged, uint32_t halo_bytes) {
-  return conv_ring_bytes(kc, bn, msub, stages, halo_bytes) + conv_fixed_smem(npad, staged);
+                                                    int npad, bool staged, uint32_t halo_bytes,
+                                                    int hslots) {
+  return conv_ring_bytes(kc, bn, msub, stages, halo_bytes, hslots) +
+         conv_fixed_smem(npad, staged);
 }
 
 // The output leaves through the TMA-store epilogue (staging slots): unshuffled NHWC, or

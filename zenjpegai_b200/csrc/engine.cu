@@ -482,10 +482,22 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   const bool shuffle_store = !o.planar && L.R > 1 && L.cph % 16 == 0 &&
                              want_w % L.R == 0 && want_h % L.R == 0;
   const bool staged = !o.planar && (L.R == 1 || shuffle_store);
-  const uint32_t fixed = conv_fixed_smem(L.npad, staged) + (a.halo ? kHaloSlots * a.halo_bytes : 0u);
-  if (fixed + 2 * stage > 232448u)
+  // Halo ring depth: a layer with little MMA work per halo (narrow N) is bound by the halo
+  // loads' latency, so it keeps up to kMaxHaloSlots halos in flight while at least 8 weight
+  // stages still fit; the others keep 2 and spend the memory on weight stages.
+  constexpr uint32_t kSmemMax = 232448u;
+  a.hslots = 2;
+  if (a.halo)
+    for (int hs = kMaxHaloSlots; hs > 2; --hs)
+      if (conv_fixed_smem(L.npad, staged) + hs * a.halo_bytes + 8 * stage <= kSmemMax) {
+        a.hslots = hs;
+        break;
+      }
+  const uint32_t fixed =
+      conv_fixed_smem(L.npad, staged) + (a.halo ? a.hslots * a.halo_bytes : 0u);
+  if (fixed + 2 * stage > kSmemMax)
     return fail(ZJAI_UNSUPPORTED, "conv: too many output columns for one launch");
-  a.stages = (int)std::min<uint32_t>(kMaxStages, (232448u - fixed) / stage);
+  a.stages = (int)std::min<uint32_t>(kMaxStages, (kSmemMax - fixed) / stage);
   int tc = 32;
   while (tc < 2 * a.msub * L.bn) tc *= 2;
   a.tmem_cols = tc;
@@ -548,6 +560,9 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     a.cx1 = o.cx1;
     a.sv = o.sv;
     a.sh = o.sh;
+    const bool pow2 = (o.sv & (o.sv - 1)) == 0 && (o.sh & (o.sh - 1)) == 0;
+    a.lsv = pow2 ? __builtin_ctz((unsigned)o.sv) : -1;
+    a.lsh = pow2 ? __builtin_ctz((unsigned)o.sh) : -1;
   }
 
   CUtensorMap tmO;  // output map of the TMA-store epilogue (unused in the other modes)
