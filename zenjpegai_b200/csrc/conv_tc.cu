@@ -283,8 +283,8 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
 // kModeShuffleStore: shuffled NHWC through TMA stores of one phase per 16-column chunk.
 constexpr int kModeR1 = 0, kModeShuffle = 1, kModePlanar = 2, kModeShuffleStore = 3;
 
-// One CTA of kConvThreads (18 warps) per SM. The launch bound makes ptxas fit the register
-// allocation to 18 warps (at most 96 registers a thread: allocations are rounded per warp and
+// One CTA of kConvThreads (19 warps) per SM. The launch bound makes ptxas fit the register
+// allocation to 19 warps (at most 96 registers a thread: allocations are rounded per warp and
 // warps per four).
 template <int MODE, int OP>
 __global__ void __launch_bounds__(kConvThreads, 1)
@@ -325,18 +325,19 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
+    // the MMA issuers' commits arrive on the empty, accumulator-full and drain barriers
     for (int i = 0; i < S; ++i) {
       mbar_init(smem_u32(&full[i]), 1);
-      mbar_init(smem_u32(&empty[i]), 1);
+      mbar_init(smem_u32(&empty[i]), (uint32_t)a.msub);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&accf[i]), 1);
+      mbar_init(smem_u32(&accf[i]), (uint32_t)a.msub);
       mbar_init(smem_u32(&acce[i]), kEpiThreads);
     }
-    mbar_init(smem_u32(drain), 1);
+    mbar_init(smem_u32(drain), (uint32_t)a.msub);
     for (int i = 0; i < a.hslots; ++i) {
       mbar_init(smem_u32(&fullA[i]), 1);
-      mbar_init(smem_u32(&emptyA[i]), 1);
+      mbar_init(smem_u32(&emptyA[i]), (uint32_t)a.msub);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -480,26 +481,33 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    // One thread. The operand descriptors of stage 0 are built once; stage s adds
-    // s * stage_bytes / 16 to the start-address field, the B operand a_bytes / 16, and K slice
-    // k of a chunk 2 * k (32 bytes), so a K step is a few adds and kc / 16 UMMA issues.
-    if (lane == 0 && a.halo) {
+  } else if (warp == 1 || warp == kMma2Warp) {
+    // ------------------------------------------------------------------ MMA issuers
+    // One thread per M subtile: lane 0 of warp 1 issues subtile 0, lane 0 of the last warp
+    // subtile 1 (msub == 2), so the two serial issue chains (barrier tests, descriptor
+    // arithmetic, commits) overlap. Both follow the same stage / halo / accumulator sequence,
+    // test the same full barriers and commit to the same empty / accumulator barriers
+    // (arrival count msub). Descriptors of stage 0 are built once; a stage, tap or K slice
+    // moves only the start address field (16-byte units).
+    const int j = warp == 1 ? 0 : 1;  // subtile
+    const uint32_t idesc = idesc_f16((uint32_t)(a.grp_pc ? a.grp_n : brows));
+    const uint32_t d_off = (uint32_t)(j * a.bn);  // the subtile's accumulator columns
+    if (lane == 0 && j < a.msub && a.halo) {
       // halo mode: per tile and chunk, wait for the halo, then per tap wait for its B block and
       // issue 4 UMMAs whose A operand starts at halo pixel (ky, kx)
-      const uint32_t idesc = idesc_f16((uint32_t)(a.grp_pc ? a.grp_n : brows));
-      const uint64_t dB0 = smem_desc(smem_u32(smem), 128u), dstage = stage_bytes >> 4;
+      const uint64_t dB0 = smem_desc(smem_u32(smem), 128u);
+      const uint64_t dstage = stage_bytes >> 4;
       const uint32_t fb_base = smem_u32(full), eb_base = smem_u32(empty);
       const uint32_t hfb = smem_u32(fullA), heb = smem_u32(emptyA);
       // A descriptor of halo slot 0's window at tap (0, 0): rows 128 bytes apart, 8-row groups
       // (one tile row) hw * 128 bytes apart; a tap or a slot moves only the start address
-      // field (16-byte units, no carry out of its 14 bits below 256 KB), so the per-tap
-      // descriptors are additions: +8 per kx, +8 (hw - kw) more at the end of a tap row
-      const uint64_t dH0 = (uint64_t)((smem_u32(halo_ring) >> 4) & 0x3FFFu) | (1ull << 16) |
-                           ((uint64_t)((a.hw * 128) >> 4) << 32) | (1ull << 46) | (2ull << 61);
+      // field (no carry out of its 14 bits below 256 KB), so the per-tap descriptors are
+      // additions: +8 per kx, +8 (hw - kw) more at the end of a tap row. Subtile 1 starts bh
+      // tile rows down.
+      const uint64_t dH0 = ((uint64_t)((smem_u32(halo_ring) >> 4) & 0x3FFFu) | (1ull << 16) |
+                            ((uint64_t)((a.hw * 128) >> 4) << 32) | (1ull << 46) | (2ull << 61)) +
+                           (uint64_t)j * (uint64_t)((a.bh * a.hw * 128) >> 4);
       const uint64_t dslot = a.halo_bytes >> 4, row_skip = (uint64_t)(a.hw - a.kw) * 8u;
-      const uint64_t sub_off = (uint64_t)((a.bh * a.hw * 128) >> 4);  // subtile 1: bh rows down
       int stage = 0, hs = 0;
       uint32_t phase = 0, hphase = 0;
       uint64_t db = dB0;
@@ -510,7 +518,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                        DEV_TIMEOUT_ACC_EMPTY))
           break;
         tc_fence_after();
-        const uint32_t d0 = tmem_base + (uint32_t)(acc * a.msub * a.bn);
+        const uint32_t d0 = tmem_base + (uint32_t)(acc * a.msub * a.bn) + d_off;
         bool ok = true;
         for (int cc = 0; cc < a.cchunks && ok; ++cc) {
           if (!mbar_wait(hfb + 8u * hs, hphase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
@@ -520,7 +528,6 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           // grouped: this chunk's (pseudo-)group owns accumulator columns cc * grp_n ..
           // (grp_n wide) and its first tap starts them; dense: the tile's first UMMA starts all
           const uint32_t d = d0 + (a.grp_pc ? (uint32_t)(cc * a.grp_n) : 0u);
-          const uint32_t d1 = d + (uint32_t)a.bn;  // subtile 1's accumulator
           const bool fresh = a.grp_pc || cc == 0;
           uint64_t da = dH0 + (uint64_t)hs * dslot;
           int kx = 0;
@@ -530,23 +537,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t acc0 = (fresh && tap == 0) ? 0u : 1u;
-            if (a.msub == 2) {
-              const uint64_t da1 = da + sub_off;
-              umma_f16(d, da, db, idesc, acc0);
-              umma_f16(d1, da1, db, idesc, acc0);
-              umma_f16(d, da + 2, db + 2, idesc, 1u);
-              umma_f16(d1, da1 + 2, db + 2, idesc, 1u);
-              umma_f16(d, da + 4, db + 4, idesc, 1u);
-              umma_f16(d1, da1 + 4, db + 4, idesc, 1u);
-              umma_f16(d, da + 6, db + 6, idesc, 1u);
-              umma_f16(d1, da1 + 6, db + 6, idesc, 1u);
-            } else {
-              umma_f16(d, da, db, idesc, acc0);
-              umma_f16(d, da + 2, db + 2, idesc, 1u);
-              umma_f16(d, da + 4, db + 4, idesc, 1u);
-              umma_f16(d, da + 6, db + 6, idesc, 1u);
-            }
+            umma_f16(d, da, db, idesc, (fresh && tap == 0) ? 0u : 1u);
+            umma_f16(d, da + 2, db + 2, idesc, 1u);
+            umma_f16(d, da + 4, db + 4, idesc, 1u);
+            umma_f16(d, da + 6, db + 6, idesc, 1u);
             umma_commit(eb_base + 8u * stage);
             db += dstage;
             if (++stage == S) {
@@ -575,15 +569,17 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       }
       umma_commit(smem_u32(drain));
       mbar_wait_drain(smem_u32(drain), 0, a.err);
-    } else if (lane == 0) {
-      const uint32_t idesc = idesc_f16((uint32_t)brows);
-      const uint64_t dA0 = smem_desc(smem_u32(smem), (uint32_t)a.kc * 2u);
-      const uint64_t dBoff = a_bytes >> 4, dstage = stage_bytes >> 4;
+    } else if (lane == 0 && j < a.msub) {
+      // subtile 1's A tile follows subtile 0's; B follows the A tiles of the stage
+      const uint64_t dA0 = smem_desc(smem_u32(smem), (uint32_t)a.kc * 2u) +
+                           (uint64_t)j * (sub_bytes >> 4);
+      const uint64_t dBoff = (a_bytes >> 4) - (uint64_t)j * (sub_bytes >> 4);
+      const uint64_t dstage = stage_bytes >> 4;
       const uint32_t fb_base = smem_u32(full), eb_base = smem_u32(empty);
       const int kk = a.kc >> 4;  // UMMAs per K step: 4, 2 or 1
       int stage = 0;
       uint32_t phase = 0;
-      uint64_t da = dA0;  // stage's A descriptor (B follows at dBoff)
+      uint64_t da = dA0;  // stage's A descriptor (B at dBoff from it)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
@@ -591,9 +587,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                        DEV_TIMEOUT_ACC_EMPTY))
           break;
         tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(acc * a.msub * a.bn);
-        const uint32_t d1 = d + (uint32_t)a.bn;  // subtile 1's accumulator
-        const uint64_t sub_off = sub_bytes >> 4;  // subtile 1's A tile follows subtile 0's
+        const uint32_t d = tmem_base + (uint32_t)(acc * a.msub * a.bn) + d_off;
         const int nt = t % a.n_tiles;
         const int k0 = a.koff ? a.koff[nt] : 0, k1 = a.koff ? a.koff[nt + 1] : ksteps;
         bool ok = true;
@@ -605,28 +599,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           }
           tc_fence_after();
           const uint64_t db = da + dBoff;
-          if (a.msub == 2) {  // alternate the two subtiles' accumulators
-            const uint64_t da1 = da + sub_off;
-            umma_f16(d, da, db, idesc, accum);
-            umma_f16(d1, da1, db, idesc, accum);
-            if (kk == 4) {
-              umma_f16(d, da + 2, db + 2, idesc, 1u);
-              umma_f16(d1, da1 + 2, db + 2, idesc, 1u);
-              umma_f16(d, da + 4, db + 4, idesc, 1u);
-              umma_f16(d1, da1 + 4, db + 4, idesc, 1u);
-              umma_f16(d, da + 6, db + 6, idesc, 1u);
-              umma_f16(d1, da1 + 6, db + 6, idesc, 1u);
-            } else if (kk == 2) {
-              umma_f16(d, da + 2, db + 2, idesc, 1u);
-              umma_f16(d1, da1 + 2, db + 2, idesc, 1u);
-            }
-          } else {
-            umma_f16(d, da, db, idesc, accum);
-            if (kk >= 2) umma_f16(d, da + 2, db + 2, idesc, 1u);
-            if (kk == 4) {
-              umma_f16(d, da + 4, db + 4, idesc, 1u);
-              umma_f16(d, da + 6, db + 6, idesc, 1u);
-            }
+          umma_f16(d, da, db, idesc, accum);
+          if (kk >= 2) umma_f16(d, da + 2, db + 2, idesc, 1u);
+          if (kk == 4) {
+            umma_f16(d, da + 4, db + 4, idesc, 1u);
+            umma_f16(d, da + 6, db + 6, idesc, 1u);
           }
           accum = 1u;
           umma_commit(eb_base + 8u * stage);

@@ -5,8 +5,8 @@
 // box [kc channels, bw, bh] of the input is loaded at the tap's offset (out-of-range
 // coordinates read zeros, which is the convolution's zero padding; a crop is a smaller
 // tensor-map extent over the same memory). Weights are packed [tap][N][Cin] f16 and loaded
-// as [kc, bn] boxes. One elected thread issues kind::f16 UMMAs into an f32 accumulator in
-// TMEM (two accumulators, so the epilogue of one tile overlaps the main loop of the next).
+// as [kc, bn] boxes. One thread per M subtile issues kind::f16 UMMAs into f32 accumulators in
+// TMEM (two accumulator sets, so the epilogue of one tile overlaps the main loop of the next).
 //
 // Epilogue: TMEM -> registers -> scale/bias/activation -> shared staging -> a second pass in
 // output order applies the pixel-shuffle remap (column n = phase * cph + channel, phase =
@@ -99,11 +99,13 @@ struct ConvArgs {
   int* err;
 };
 
-// warp 0 TMA, warp 1 MMA, then kEpiWarpgroups warpgroups of epilogue (warpgroup g takes the
-// accumulator column chunks c with c % kEpiWarpgroups == g)
+// warp 0 TMA, warp 1 MMA issuer 0, then kEpiWarpgroups warpgroups of epilogue (warpgroup g
+// takes the accumulator column chunks c with c % kEpiWarpgroups == g), then the warp of MMA
+// issuer 1
 constexpr int kEpiWarpgroups = 4;
 constexpr int kEpiThreads = 128 * kEpiWarpgroups;
-constexpr int kConvThreads = 64 + kEpiThreads;
+constexpr int kMma2Warp = 2 + kEpiThreads / 32;
+constexpr int kConvThreads = 32 * (kMma2Warp + 1);
 constexpr int kBarrierBytes = 512;  // 2 * stages + 5 + 2 * halo slots mbarriers, slots
 constexpr int kMaxStages = 16;
 
