@@ -13,7 +13,10 @@ template <int ACT>
 __device__ __forceinline__ float act(float v) {
   if constexpr (ACT == ACT_RELU) return v > 0.f ? v : 0.f;
   if constexpr (ACT == ACT_LEAKY) return v > 0.f ? v : v * 0.01f;
-  if constexpr (ACT == ACT_SIGMOID) return 1.f / (1.f + expf(-v));
+  // sigma(v) = 1 / (1 + e^-v) (math.rs:370-373) with the fast exponential and division: a
+  // few ulp of f32, far below the f16 the result is stored in (a denominator beyond 2^126,
+  // v < -87, gives 0)
+  if constexpr (ACT == ACT_SIGMOID) return __fdividef(1.f, 1.f + __expf(-v));
   if constexpr (ACT == ACT_RELU6) return fminf(fmaxf(v, 0.f), 6.f);
   return v;
 }
@@ -175,11 +178,13 @@ __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kCh
 // packing padding) may stage anything but must not read residuals. p1 / p2 / p2o are the
 // element offsets of the output pixel in r1 / r2 / out2; residuals are read before the results
 // are staged (in-place ops read exactly what this warp's store then overwrites).
+// rs1 / rs2: the thread's residual channels ch0 .. ch0 + 15 already in shared memory (the
+// prefetched boxes), or null to load them from global memory here.
 template <int OP>
 __device__ __forceinline__ void epi_staged(const ConvArgs& a, const float (&v)[kChunk],
                                            int col0, int ch0, long long p1, long long p2,
                                            long long p2o, bool valid, const float* btab,
-                                           uint4* dst) {
+                                           uint4* dst, const uint4* rs1, const uint4* rs2) {
   constexpr int G = kChunk / 8;
   uint4 r1[G], r2[G];
   if constexpr (OP != OP_NONE) {
@@ -187,7 +192,10 @@ __device__ __forceinline__ void epi_staged(const ConvArgs& a, const float (&v)[k
     for (int g = 0; g < G; ++g) {
       const int c = ch0 + 8 * g;
       r1[g] = r2[g] = make_uint4(0u, 0u, 0u, 0u);
-      if (valid && c < a.cph) {
+      if (rs1) {
+        r1[g] = rs1[g];
+        if constexpr (OP == OP_CAB) r2[g] = rs2[g];
+      } else if (valid && c < a.cph) {
         r1[g] = __ldg(reinterpret_cast<const uint4*>(a.r1 + p1 + c));
         if constexpr (OP == OP_CAB) r2[g] = __ldg(reinterpret_cast<const uint4*>(a.r2 + p2 + c));
       }
@@ -281,7 +289,9 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
 
 // Epilogue output modes: NHWC without a pixel shuffle, NHWC through the shuffle table, planar.
 // kModeShuffleStore: shuffled NHWC through TMA stores of one phase per 16-column chunk.
-constexpr int kModeR1 = 0, kModeShuffle = 1, kModePlanar = 2, kModeShuffleStore = 3;
+// kModeR1Pre: kModeR1 with the residual prefetch (1x1 convs with a residual op).
+constexpr int kModeR1 = 0, kModeShuffle = 1, kModePlanar = 2, kModeShuffleStore = 3,
+              kModeR1Pre = 4;
 
 // One CTA of kConvThreads (19 warps) per SM. The launch bound makes ptxas fit the register
 // allocation to 19 warps (at most 96 registers a thread: allocations are rounded per warp and
@@ -315,10 +325,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint64_t* emptyA = bars + 2 * S + 5 + kMaxHaloSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5 + 2 * kMaxHaloSlots);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* rbar = bars + 2 * S + 5 + 2 * kMaxHaloSlots + 1;  // 2 per epilogue warp
   uint32_t* tab = reinterpret_cast<uint32_t*>(smem + ring_bytes + kBarrierBytes);
   const int npad = a.n_tiles * a.bn;
   float* btab = reinterpret_cast<float*>(tab + npad);
-  // TMA-store staging: two kEpiSlotBytes slots per epilogue warp (128-byte aligned)
+  // TMA-store staging: two kEpiSlotBytes slots per epilogue warp (128-byte aligned), then
+  // the same again per prefetched residual operand
   uint8_t* staging = reinterpret_cast<uint8_t*>(btab + npad);
 
   const int warp = threadIdx.x >> 5;
@@ -339,6 +351,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       mbar_init(smem_u32(&fullA[i]), 1);
       mbar_init(smem_u32(&emptyA[i]), (uint32_t)a.msub);
     }
+    if (a.nres)
+      for (int i = 0; i < 2 * (kEpiThreads / 32); ++i) mbar_init(smem_u32(&rbar[i]), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -638,6 +652,65 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     uint8_t* wslots = staging + (warp - 2) * 2 * kEpiSlotBytes;
     int slot = 0;
     const int m0 = q * 32;
+    // Residual prefetch (kModeR1Pre): while it finishes one work item (subtile, chunk) the
+    // warp has the residual box(es) of its next one loaded into its two residual slots (r1, and
+    // r2 kEpiStagingBytes further), one mbarrier per slot.
+    constexpr bool pre = MODE == kModeR1Pre && OP != OP_NONE;
+    uint8_t* rslots = staging + kEpiStagingBytes + (warp - 2) * 2 * kEpiSlotBytes;
+    const uint32_t rb0 = smem_u32(&rbar[(warp - 2) * 2]);
+    uint32_t rissue = 0, ruse = 0;  // residual boxes issued / consumed by this warp
+    // issue the residual box(es) of item (subtile sub, chunk c) of the tile at tcn
+    auto res_issue = [&](const TileCoord& tcn, int sub, int c) {
+      const int col0 = tcn.n0 + c * kChunk;
+      const int y = tcn.oy0 + sub * a.bh + (m0 >> a.lbw), x = tcn.ox0 + (m0 & (a.bw - 1));
+      const uint32_t sl = rissue & 1u;
+      __syncwarp();  // every lane's reads of this slot (two items ago) are done
+      if (lane == 0) {
+        fence_proxy_async_smem();
+        const uint32_t bar = rb0 + 8u * sl;
+        const uint32_t dst = smem_u32(rslots + sl * kEpiSlotBytes);
+        mbar_arrive_expect_tx(bar, (uint32_t)a.nres * kEpiSlotBytes);
+        tma_load_4d(dst, &a.tmR[0], bar, col0, x, y, tcn.img);
+        if constexpr (OP == OP_CAB)
+          tma_load_4d(dst + kEpiStagingBytes, &a.tmR[1], bar, col0, x, y, tcn.img);
+      }
+      ++rissue;
+    };
+    // this warpgroup's items of a tile: wide accumulators (nchunks >= kEpiWarpgroups) take
+    // chunks wg, wg + kEpiWarpgroups, .. of every subtile; narrow ones deal the items
+    // it = sub * nchunks + c round-robin to the warpgroups
+    const bool wide = nchunks >= kEpiWarpgroups;
+    const int items = a.msub * nchunks;
+    // first item of a tile (false: this warpgroup has none)
+    auto first_item = [&](int& sub, int& c) {
+      if (wide) {
+        sub = 0;
+        c = wg;
+        return true;
+      }
+      sub = wg / nchunks;
+      c = wg - sub * nchunks;
+      return wg < items;
+    };
+    // item after (sub, c) in the same tile (false: none)
+    auto next_item = [&](int& sub, int& c) {
+      if (wide) {
+        if (c + kEpiWarpgroups < nchunks) {
+          c += kEpiWarpgroups;
+          return true;
+        }
+        c = wg;
+        return ++sub < a.msub;
+      }
+      const int it = sub * nchunks + c + kEpiWarpgroups;
+      sub = it / nchunks;
+      c = it - sub * nchunks;
+      return it < items;
+    };
+    if (pre && (int)blockIdx.x < a.num_tiles) {
+      int s0, c0;
+      if (first_item(s0, c0)) res_issue(decode_tile(a, blockIdx.x), s0, c0);
+    }
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
@@ -645,6 +718,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         break;
       tc_fence_after();
       const TileCoord tc = decode_tile(a, t);
+      const int tnext = t + (int)gridDim.x;
       // this thread's pixel in subtile `sub` and its residual / copy offsets
       struct Geo {
         int sy0, oy, ox;
@@ -658,7 +732,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         g.ox = tc.ox0 + (m & (a.bw - 1));
         g.valid = g.oy < a.oh && g.ox < a.ow;
         g.p1 = g.p2 = g.p2o = 0;
-        if constexpr (MODE == kModeR1) {
+        if constexpr (MODE == kModeR1 || MODE == kModeR1Pre) {
           if constexpr (OP != OP_NONE)
             g.p1 = tc.img * a.r1_img + g.oy * a.r1_row + g.ox * a.r1_pix;
           if constexpr (OP == OP_CAB)
@@ -673,6 +747,22 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const bool valid = g.valid;
         const long long p1 = g.p1, p2 = g.p2, p2o = g.p2o;
         const uint32_t tcol = (uint32_t)((acc * a.msub + sub) * a.bn);
+        const int col0 = tc.n0 + c * kChunk;
+        // residuals: start the next item's boxes, then take this item's
+        const uint4 *rs1 = nullptr, *rs2 = nullptr;
+        if constexpr (pre) {
+          int ns = sub, nc = c;
+          if (next_item(ns, nc)) {
+            res_issue(tc, ns, nc);
+          } else if (tnext < a.num_tiles && first_item(ns, nc)) {
+            res_issue(decode_tile(a, tnext), ns, nc);
+          }
+          const uint32_t sl = ruse & 1u;
+          mbar_wait(rb0 + 8u * sl, (ruse >> 1) & 1u, abort_flag, a.err, DEV_TIMEOUT_FULL);
+          rs1 = reinterpret_cast<const uint4*>(rslots + sl * kEpiSlotBytes + lane * 32);
+          rs2 = rs1 + kEpiStagingBytes / 16;
+          ++ruse;
+        }
         {
           float v[kChunk];
           tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + tcol + (uint32_t)(c * kChunk), v);
@@ -680,14 +770,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             tc_fence_before();
             mbar_arrive(smem_u32(&acce[acc]));
           }
-          const int col0 = tc.n0 + c * kChunk;
-          if constexpr (MODE == kModeR1) {
+          if constexpr (MODE == kModeR1 || MODE == kModeR1Pre) {
             // the slot about to be filled was last stored two chunks ago: wait for that read
             if (lane == 0) bulk_wait_read<1>();
             __syncwarp();
             uint8_t* sl = wslots + slot * kEpiSlotBytes;
             epi_staged<OP>(a, v, col0, col0, p1, p2, p2o, valid, btab,
-                           reinterpret_cast<uint4*>(sl + lane * 32));
+                           reinterpret_cast<uint4*>(sl + lane * 32), rs1, rs2);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -711,7 +800,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
               __syncwarp();
               uint8_t* sl = wslots + slot * kEpiSlotBytes;
               epi_staged<OP>(a, v, col0, ch0, q1, q2, q2o, valid, btab,
-                             reinterpret_cast<uint4*>(sl + lane * 32));
+                             reinterpret_cast<uint4*>(sl + lane * 32), rs1, rs2);
               fence_proxy_async_smem();
               __syncwarp();
               if (lane == 0) {
@@ -728,7 +817,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           }
         }
       };
-      if (nchunks >= kEpiWarpgroups) {
+      if (wide) {
         // warpgroup wg takes the chunks wg, wg + kEpiWarpgroups, .. of every subtile
         for (int sub = 0; sub < a.msub; ++sub) {
           const Geo g = geo(sub);
@@ -738,7 +827,6 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       } else {
         // narrow accumulators: the items (subtile, chunk) = (it / nchunks, it % nchunks) are
         // dealt round-robin to the warpgroups, so the subtiles of a tile drain in parallel
-        const int items = a.msub * nchunks;
         if (wg >= items) {
           tc_fence_before();
           mbar_arrive(smem_u32(&acce[acc]));
@@ -753,8 +841,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    // residual boxes still in flight (a wait gave up) land before shared memory goes away
+    for (; ruse < rissue; ++ruse) mbar_wait_drain(rb0 + 8u * (ruse & 1u), (ruse >> 1) & 1u, a.err);
     // every TMA store of this warp complete before the CTA (and its shared memory) ends
-    if constexpr (MODE == kModeR1 || MODE == kModeShuffleStore) {
+    if constexpr (MODE == kModeR1 || MODE == kModeR1Pre || MODE == kModeShuffleStore) {
       if (lane == 0) bulk_wait_all();
     }
   }
@@ -772,10 +862,10 @@ cudaError_t launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const Co
   const uint32_t smem =
       conv_smem_bytes(a.kc, a.grp_pc ? a.grp_pc * a.grp_n : a.bn, a.msub, a.stages,
                       a.n_tiles * a.bn,
-                      conv_staged_output(a), a.halo ? a.halo_bytes : 0u, a.hslots);
+                      conv_staged_output(a), a.halo ? a.halo_bytes : 0u, a.hslots, a.nres);
   // one instantiation per (output mode, epilogue op), each with its own register allocation
   using K = void (*)(CUtensorMap, CUtensorMap, ConvArgs);
-  static const K kernels[4][4] = {
+  static const K kernels[5][4] = {
       {conv_tc_kernel<kModeR1, OP_NONE>, conv_tc_kernel<kModeR1, OP_ADD>,
        conv_tc_kernel<kModeR1, OP_GATE>, conv_tc_kernel<kModeR1, OP_CAB>},
       {conv_tc_kernel<kModeShuffle, OP_NONE>, conv_tc_kernel<kModeShuffle, OP_ADD>,
@@ -783,7 +873,9 @@ cudaError_t launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const Co
       {conv_tc_kernel<kModePlanar, OP_NONE>, conv_tc_kernel<kModePlanar, OP_NONE>,
        conv_tc_kernel<kModePlanar, OP_NONE>, conv_tc_kernel<kModePlanar, OP_NONE>},
       {conv_tc_kernel<kModeShuffleStore, OP_NONE>, conv_tc_kernel<kModeShuffleStore, OP_ADD>,
-       conv_tc_kernel<kModeShuffleStore, OP_GATE>, conv_tc_kernel<kModeShuffleStore, OP_CAB>}};
+       conv_tc_kernel<kModeShuffleStore, OP_GATE>, conv_tc_kernel<kModeShuffleStore, OP_CAB>},
+      {conv_tc_kernel<kModeR1, OP_NONE>, conv_tc_kernel<kModeR1Pre, OP_ADD>,
+       conv_tc_kernel<kModeR1Pre, OP_GATE>, conv_tc_kernel<kModeR1Pre, OP_CAB>}};
   static bool attr_set = false;
   if (!attr_set) {
     for (auto& row : kernels)
@@ -792,7 +884,7 @@ cudaError_t launch_conv(const CUtensorMap& tmA, const CUtensorMap& tmO, const Co
     attr_set = true;
   }
   const int mode = a.planar ? kModePlanar
-                   : a.R == 1 ? kModeR1
+                   : a.R == 1 ? (a.nres ? kModeR1Pre : kModeR1)
                    : a.tmO_img ? kModeShuffleStore
                                : kModeShuffle;
   kernels[mode][a.op & 3]<<<grid, kConvThreads, smem, stream>>>(tmA, tmO, a);

@@ -86,6 +86,13 @@ struct ConvArgs {
   // shuffled NHWC output through TMA stores: per picture a 5-D map of the output viewed as
   // {C, R (dx), W / R, R (dy), H / R}, box [16, 1, bx, 1, 32 / bx] (device array, or null)
   const CUtensorMap* tmO_img;
+  // Residual prefetch of the TMA-store epilogue: nres (0, 1 or 2) residual operands whose box
+  // of the next work item each epilogue warp loads into shared memory while it finishes the
+  // current one. tmR (device array): the maps of r1 then r2 with the output map's box, one
+  // each (unshuffled output) or one per picture each (shuffled output: n_img maps of r1, then
+  // n_img of r2).
+  const CUtensorMap* tmR;
+  int nres;
   // planar f32 output
   int planar, denorm;
   float* pout;
@@ -106,7 +113,9 @@ constexpr int kEpiWarpgroups = 4;
 constexpr int kEpiThreads = 128 * kEpiWarpgroups;
 constexpr int kMma2Warp = 2 + kEpiThreads / 32;
 constexpr int kConvThreads = 32 * (kMma2Warp + 1);
-constexpr int kBarrierBytes = 512;  // 2 * stages + 5 + 2 * halo slots mbarriers, slots
+// 2 * stages + 5 + 2 * halo slots mbarriers, the TMEM slot / abort word, 2 residual
+// mbarriers per epilogue warp
+constexpr int kBarrierBytes = 1024;
 constexpr int kMaxStages = 16;
 
 // a stage: the A tiles of msub subtiles (128 rows each) + the B block of bn rows
@@ -120,9 +129,11 @@ constexpr uint32_t kEpiSlotBytes = 1024u;
 constexpr uint32_t kEpiStagingBytes = 2u * kEpiSlotBytes * (kEpiThreads / 32);
 
 // 1 KB alignment slack + barriers/slots + the column table and the bias (4 + 4 bytes per column)
-// + the epilogue staging slots when the output goes out through TMA stores
-__host__ __device__ inline uint32_t conv_fixed_smem(int npad, bool staged) {
-  return 1024u + kBarrierBytes + 8u * (uint32_t)npad + (staged ? kEpiStagingBytes : 0u);
+// + the epilogue staging slots when the output goes out through TMA stores, and as many again
+// per prefetched residual operand
+__host__ __device__ inline uint32_t conv_fixed_smem(int npad, bool staged, int nres) {
+  return 1024u + kBarrierBytes + 8u * (uint32_t)npad +
+         (staged ? (1u + (uint32_t)nres) * kEpiStagingBytes : 0u);
 }
 constexpr int kMaxHaloSlots = 4;
 // a stage holding only the B block (halo mode)
@@ -138,9 +149,9 @@ __host__ __device__ inline uint32_t conv_ring_bytes(int kc, int bn, int msub, in
 }
 __host__ __device__ inline uint32_t conv_smem_bytes(int kc, int bn, int msub, int stages,
                                                     int npad, bool staged, uint32_t halo_bytes,
-                                                    int hslots) {
+                                                    int hslots, int nres) {
   return conv_ring_bytes(kc, bn, msub, stages, halo_bytes, hslots) +
-         conv_fixed_smem(npad, staged);
+         conv_fixed_smem(npad, staged, nres);
 }
 
 // The output leaves through the TMA-store epilogue (staging slots): unshuffled NHWC, or

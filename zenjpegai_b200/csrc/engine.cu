@@ -486,15 +486,22 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   // loads' latency, so it keeps up to kMaxHaloSlots halos in flight while at least 8 weight
   // stages still fit; the others keep 2 and spend the memory on weight stages.
   constexpr uint32_t kSmemMax = 232448u;
+  // Residual prefetch: a TMA-store epilogue with a residual op loads each work item's residual
+  // box(es) into shared memory one item ahead. Only 1x1 convs, whose few K steps leave the
+  // epilogue on the critical path; a multi-tap conv keeps that memory for weight stages.
+  a.nres = staged && o.op != OP_NONE && L.kh * L.kw == 1 ? (o.op == OP_CAB ? 2 : 1) : 0;
+  if (a.nres && conv_fixed_smem(L.npad, staged, a.nres) + (a.halo ? 2 * a.halo_bytes : 0u) +
+                        2 * stage > kSmemMax)
+    a.nres = 0;
   a.hslots = 2;
   if (a.halo)
     for (int hs = kMaxHaloSlots; hs > 2; --hs)
-      if (conv_fixed_smem(L.npad, staged) + hs * a.halo_bytes + 8 * stage <= kSmemMax) {
+      if (conv_fixed_smem(L.npad, staged, a.nres) + hs * a.halo_bytes + 8 * stage <= kSmemMax) {
         a.hslots = hs;
         break;
       }
   const uint32_t fixed =
-      conv_fixed_smem(L.npad, staged) + (a.halo ? a.hslots * a.halo_bytes : 0u);
+      conv_fixed_smem(L.npad, staged, a.nres) + (a.halo ? a.hslots * a.halo_bytes : 0u);
   if (fixed + 2 * stage > kSmemMax)
     return fail(ZJAI_UNSUPPORTED, "conv: too many output columns for one launch");
   a.stages = (int)std::min<uint32_t>(kMaxStages, (kSmemMax - fixed) / stage);
@@ -581,6 +588,31 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
                                         cudaMemcpyHostToDevice, ctx->stream),
                         "tensor map upload"));
     a.tmO_img = static_cast<const CUtensorMap*>(dm);
+  }
+  if (a.nres) {
+    // residual maps with the output map's box: r1 then r2, one each or one per picture each
+    const TView* rv[2] = {o.r1, o.r2};
+    std::vector<CUtensorMap> rm;
+    for (int k = 0; k < a.nres; ++k) {
+      if (!shuffle_store) {
+        CUtensorMap m;
+        ZJAI_TRY(make_store_map(ctx, &m, *rv[k], sbx, 32 / sbx));
+        rm.push_back(m);
+      } else {
+        for (int i = 0; i < o.out.n; ++i) {
+          CUtensorMap m;
+          ZJAI_TRY(make_phase_store_map(ctx, &m, *rv[k], i, L.R, sbx, 32 / sbx));
+          rm.push_back(m);
+        }
+      }
+    }
+    Arena* ar = ctx->cur_arena ? ctx->cur_arena : &ctx->arena;
+    void* dm = ar->alloc(sizeof(CUtensorMap) * rm.size());
+    if (!dm) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (tensor maps)");
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(dm, rm.data(), sizeof(CUtensorMap) * rm.size(),
+                                        cudaMemcpyHostToDevice, ctx->stream),
+                        "tensor map upload"));
+    a.tmR = static_cast<const CUtensorMap*>(dm);
   }
   a.wblk = L.w;
   a.wblk_img = L.w_img;
