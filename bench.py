@@ -66,18 +66,48 @@ def conv_traffic(config):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock and clock-event (throttle) reasons of the bench's GPU, sampled every 10 ms by
+    NVML (read-only queries) from before the timed region to after it; only the samples taken
+    inside the timed window (`mark_start` .. `mark_stop`) are reported, or the first one after
+    it when the window is shorter than the sampling period. Falls back to `nvidia-smi -lms 200`
+    when NVML is unavailable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40}
 
     def __init__(self, gpu):
         self.gpu = gpu
         self.proc = None
+        self.nvml = None
         self.lines = []
+        self.samples = []  # (time, sm_mhz, max_mhz, reason bits)
+        self.t0 = self.t1 = None
+        self.running = False
 
     def start(self):
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            try:
+                bus = torch.cuda.get_device_properties(self.gpu).pci_bus_id
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(
+                    "%08X:%02X:%02X.0" % (torch.cuda.get_device_properties(self.gpu).pci_domain_id,
+                                          bus, torch.cuda.get_device_properties(self.gpu).pci_device_id))
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.nvml, self.handle = pynvml, h
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.running = True
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
@@ -88,11 +118,48 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    def _poll(self):
+        nv, h = self.nvml, self.handle
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        while self.running:
+            try:
+                self.samples.append((time.monotonic(),
+                                     float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                     self.max_mhz, int(get_reasons(h))))
+            except Exception:
+                pass
+            time.sleep(0.01)
+
     def _read(self):
         for ln in self.proc.stdout:
             self.lines.append(ln.strip())
 
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_stop(self):
+        self.t1 = time.monotonic()
+
     def stop(self):
+        if self.nvml:
+            time.sleep(0.03)  # at least one sample after the window
+            self.running = False
+            self.thread.join(timeout=1)
+            t0 = self.t0 if self.t0 is not None else 0.0
+            t1 = self.t1 if self.t1 is not None else float("inf")
+            win = [s for s in self.samples if t0 <= s[0] <= t1]
+            if not win:
+                win = [s for s in self.samples if s[0] > t1][:1]
+            reasons = set()
+            for s in win:
+                for nm, bit in self.REASONS.items():
+                    if s[3] & bit:
+                        reasons.add(nm)
+            sm = [s[1] for s in win]
+            return {"sm_mhz": float(np.median(sm)) if sm else None,
+                    "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                    "samples": len(sm), "source": "nvml, 10 ms"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -116,7 +183,7 @@ class ClockSampler:
                     reasons.add(nm)
         return {"sm_mhz": float(np.median(sm)) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
 def cpu_sample(cfg, threads):
@@ -255,8 +322,11 @@ def main():
         dist.barrier()
     clocks = ClockSampler(local)
     clocks.start()
+    time.sleep(0.05)
     n0 = eng.launch_count
+    clocks.mark_start()
     total_ms = timed(args.steps)
+    clocks.mark_stop()
     launches = eng.launch_count - n0
     clk = clocks.stop()
     eng.sync()
