@@ -248,6 +248,21 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
 
 __device__ __forceinline__ float elu1(float a) { return a > 0.f ? a : __expf(a) - 1.f; }
 
+// 2^x by the SFU (flush-to-zero: 2^x below 2^-126 is 0)
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The FFN gate elu(e) * m (math.rs:376) for a channel pair: elu(e) = e for e > 0, else
+// e^e - 1 = 2^(e log2 e) - 1; the product with m is one packed multiply either way.
+__device__ __forceinline__ float2 elu_gate2(float2 e, float2 m) {
+  const float2 t = __fmul2_rn(e, make_float2(1.44269504088896341f, 1.44269504088896341f));
+  const float2 em1 = __fadd2_rn(make_float2(ex2_ftz(t.x), ex2_ftz(t.y)), make_float2(-1.f, -1.f));
+  return __fmul2_rn(make_float2(e.x > 0.f ? e.x : em1.x, e.y > 0.f ? e.y : em1.y), m);
+}
+
 // Persistent: block b keeps channel block cb = b % cblocks (its weights stay in registers) and
 // walks the spatial tiles s = b / cblocks, + gridDim.x / cblocks, ...; the copies of the next
 // tile run while the current one is computed (two shared-memory buffers).
@@ -561,8 +576,7 @@ __global__ void __launch_bounds__(kDsThreads + 32, 1)
           const float2(&a)[2] = ao[q];
           if (!(q == 0 ? st0 : st1)) continue;
           if (GATE) {
-            *reinterpret_cast<__half2*>(yr + q * ypix) =
-                __floats2half2_rn(elu1(a[0].x) * a[1].x, elu1(a[0].y) * a[1].y);
+            *reinterpret_cast<__half2*>(yr + q * ypix) = __float22half2_rn(elu_gate2(a[0], a[1]));
           } else {
             uint2 pk;
             *reinterpret_cast<__half2*>(&pk.x) = __floats2half2_rn(a[0].x, a[0].y);
@@ -679,7 +693,7 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 template <int HC>
 __global__ void __launch_bounds__(256) attn_gram_mma_kernel(
     const __half* __restrict__ qkv, int npix, int w, int dim, int heads, long long pix,
-    long long row, long long img, float* __restrict__ gram, float* __restrict__ sq,
+    long long row, long long img, bool dense, float* __restrict__ gram, float* __restrict__ sq,
     int px_per_block) {
   constexpr int MT = HC / 16, NT = HC / 8;
   extern __shared__ __align__(16) __half gsm[];  // [2][kGramChunk][rs]
@@ -694,15 +708,18 @@ __global__ void __launch_bounds__(256) attn_gram_mma_kernel(
   const int p_end = min(npix, p_begin + px_per_block);
   const int nchunks = (p_end - p_begin + kGramChunk - 1) / kGramChunk;
 
+  // thread = (8-channel group g0, pixel pp0 + k * pstep of each chunk); groups divides 256
+  const int g0 = threadIdx.x % groups, pstep = 256 / groups;
   auto stage = [&](int chunk, int buf) {
-    __half* dst = gsm + buf * kGramChunk * rs;
+    __half* dst = gsm + buf * kGramChunk * rs + g0 * 8;
     const int p0 = p_begin + chunk * kGramChunk;
-    for (int t = threadIdx.x; t < kGramChunk * groups; t += 256) {
-      const int pp = t / groups, g = t % groups;
+    for (int pp = threadIdx.x / groups; pp < kGramChunk; pp += pstep) {
       const int p = p0 + pp;
       const bool ok = p < p_end;
-      cp_async16(dst + pp * rs + g * 8, ok ? base + (p / w) * row + (p % w) * pix + g * 8 : qkv,
-                 ok ? 16 : 0);
+      // contiguous views need no division
+      const long long off =
+          dense ? (long long)p * pix : (long long)(p / w) * row + (long long)(p % w) * pix;
+      cp_async16(dst + pp * rs, ok ? base + off + g0 * 8 : qkv, ok ? 16 : 0);
     }
   };
 
@@ -1070,17 +1087,21 @@ static float* attention_weights(const TView& qkv, int heads, const float* temp, 
                            most);
       attr_set = true;
     }
-    // about three blocks per SM over the whole batch, whole chunks per block
+    // at most three blocks per SM over the whole batch (one wave: the shared-memory budget
+    // holds three), whole chunks per block
     const int chunks = (npix + kGramChunk - 1) / kGramChunk;
-    const int splits = std::max(1, std::min(chunks, (3 * sms + n - 1) / n));
+    const int splits = std::max(1, std::min(chunks, (3 * sms) / n));
     const int px_per_block = ((chunks + splits - 1) / splits) * kGramChunk;
     dim3 g1((npix + px_per_block - 1) / px_per_block, n);
+    const bool dense = qkv.row == qkv.w * qkv.pix;  // rows contiguous within a picture
     if (c == 32)
       attn_gram_mma_kernel<32><<<g1, 256, smem, s>>>(qkv.p, npix, qkv.w, dim, heads, qkv.pix,
-                                                     qkv.row, qkv.img, gram, sq, px_per_block);
+                                                     qkv.row, qkv.img, dense, gram, sq,
+                                                     px_per_block);
     else
       attn_gram_mma_kernel<16><<<g1, 256, smem, s>>>(qkv.p, npix, qkv.w, dim, heads, qkv.pix,
-                                                     qkv.row, qkv.img, gram, sq, px_per_block);
+                                                     qkv.row, qkv.img, dense, gram, sq,
+                                                     px_per_block);
   } else {
     const int chunks = (npix + kGramPix - 1) / kGramPix;
     const int cpb = std::max(1, chunks / 64);
