@@ -691,7 +691,7 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 }
 
 template <int HC>
-__global__ void __launch_bounds__(256) attn_gram_mma_kernel(
+__global__ void __launch_bounds__(256, 2) attn_gram_mma_kernel(
     const __half* __restrict__ qkv, int npix, int w, int dim, int heads, long long pix,
     long long row, long long img, bool dense, float* __restrict__ gram, float* __restrict__ sq,
     int px_per_block) {
@@ -1087,10 +1087,10 @@ static float* attention_weights(const TView& qkv, int heads, const float* temp, 
                            most);
       attr_set = true;
     }
-    // at most three blocks per SM over the whole batch (one wave: the shared-memory budget
-    // holds three), whole chunks per block
+    // two blocks per SM (registers allow two) over the whole batch, one wave, whole chunks per
+    // block
     const int chunks = (npix + kGramChunk - 1) / kGramChunk;
-    const int splits = std::max(1, std::min(chunks, (3 * sms) / n));
+    const int splits = std::max(1, std::min(chunks, (2 * sms) / n));
     const int px_per_block = ((chunks + splits - 1) / splits) * kGramChunk;
     dim3 g1((npix + px_per_block - 1) / px_per_block, n);
     const bool dense = qkv.row == qkv.w * qkv.pix;  // rows contiguous within a picture
