@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const int nt = tc.n0 / a.bn;
         const __half* wbase = a.wblk + (size_t)tc.img * a.wblk_img + (size_t)nt * brows * a.kc;
         for (int cc = 0; cc < a.cchunks; ++cc) {
-          if (!mbar_wait(heb + 8u * hs, hphase ^ 1u, abort_flag, a.err, DEV_TIMEOUT_EMPTY))
+          if (!mbar_wait_idle(heb + 8u * hs, hphase ^ 1u, abort_flag, a.err, DEV_TIMEOUT_EMPTY, 64))
             goto halo_done;
           mbar_arrive_expect_tx(hfb + 8u * hs, hbox);
           tma_load_4d(h_base + hs * a.halo_bytes, &tmA, hfb + 8u * hs, cc * a.kc,
@@ -405,8 +405,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             hphase ^= 1u;
           }
           for (int tap = 0; tap < a.taps; ++tap) {
-            if (!mbar_wait(eb_base + 8u * stage, phase ^ 1u, abort_flag, a.err,
-                           DEV_TIMEOUT_EMPTY))
+            if (!mbar_wait_idle(eb_base + 8u * stage, phase ^ 1u, abort_flag, a.err,
+                                DEV_TIMEOUT_EMPTY, 64))
               goto halo_done;
             const uint32_t fb = fb_base + 8u * stage;
             mbar_arrive_expect_tx(fb, b_bytes);
@@ -455,7 +455,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             ky = (int)((e >> 21) & 31u);
             cc = (int)(e >> 26);
           }
-          if (!mbar_wait(eb_base + 8u * stage, phase ^ 1u, abort_flag, a.err, DEV_TIMEOUT_EMPTY))
+          if (!mbar_wait_idle(eb_base + 8u * stage, phase ^ 1u, abort_flag, a.err,
+                              DEV_TIMEOUT_EMPTY, 64))
             goto producer_done;
           const uint32_t sA = s_base + stage * stage_bytes;
           const uint32_t fb = fb_base + 8u * stage;
@@ -528,8 +529,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
-        if (!mbar_wait(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, a.err,
-                       DEV_TIMEOUT_ACC_EMPTY))
+        if (!mbar_wait_idle(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, a.err,
+                            DEV_TIMEOUT_ACC_EMPTY, 64))
           break;
         tc_fence_after();
         const uint32_t d0 = tmem_base + (uint32_t)(acc * a.msub * a.bn) + d_off;
@@ -597,8 +598,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
-        if (!mbar_wait(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, a.err,
-                       DEV_TIMEOUT_ACC_EMPTY))
+        if (!mbar_wait_idle(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, a.err,
+                            DEV_TIMEOUT_ACC_EMPTY, 64))
           break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * a.msub * a.bn) + d_off;
@@ -714,7 +715,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
-      if (!mbar_wait(smem_u32(&accf[acc]), acc_phase, abort_flag, a.err, DEV_TIMEOUT_ACC_FULL))
+      if (!mbar_wait_idle(smem_u32(&accf[acc]), acc_phase, abort_flag, a.err, DEV_TIMEOUT_ACC_FULL,
+                          128))
         break;
       tc_fence_after();
       const TileCoord tc = decode_tile(a, t);

@@ -91,6 +91,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// mbar_wait for roles whose wake-up latency is not on the critical path (a producer waiting
+// for a free stage, the MMA issuer waiting for a free accumulator, the epilogue waiting for a
+// full one): after the first polls it sleeps `ns` between tests, leaving the issue slots of
+// its SM sub-partition to the warps that have work.
+__device__ __forceinline__ bool mbar_wait_idle(uint32_t bar, uint32_t parity, volatile int* abort,
+                                               int* err, int code, uint32_t ns) {
+  if (mbar_test(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if ((it & 63u) == 0 && clock64() - t0 > kWaitCycles) {
+      atomicCAS(err, 0, code);
+      *abort = 1;
+      return false;
+    }
+    if (it > 4) __nanosleep(ns);
+  }
+}
+
 // Bounded wait that ignores the abort flag (used to drain in-flight work before exit).
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
   const long long t0 = clock64();
