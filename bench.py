@@ -4,8 +4,9 @@
 Default workload: HOP synthesis of a 3840x2160 4:2:0 picture from
 synthetic latents (luma 160x135x240, chroma 96x135x240, integer Laplace(1.5) with ~60% zeros)
 in 512-sample tiles with a 16-sample overlap (40 tiles), random-init weights (seed 3), tiles
-distributed round-robin over the ranks (tile i on rank i mod N), each rank quantising its
-cores to 8-bit YUV 4:2:0 and a final sum-reduce of the disjoint 8-bit cores to rank 0 over
+distributed round-robin over the ranks (tile i on rank i mod N), each rank's final layers
+writing its cores as 8-bit YUV 4:2:0 samples (the fused output stage, quantize_plane_par in the
+epilogue) and a final sum-reduce of the disjoint 8-bit cores to rank 0 over
 NCCL (the "final gather"). One step = one picture. `--config sop1080` runs config 3 (SOP
 1920x1080, one tile).
 
@@ -278,9 +279,10 @@ def main():
     ly, luv = ly_h.cuda(), luv_h.cuda()
     tiles = zj.synthesis_tiles(H, W, lh, lw, cfg["tile"], cfg["overlap"])
     mine = sharding.shard_tiles(tiles, rank, world)
-    planes = (torch.zeros((H, W), device="cuda"), torch.zeros((ch, cw), device="cuda"),
-              torch.zeros((ch, cw), device="cuda"))
     out8 = torch.zeros(H * W + 2 * ch * cw, dtype=torch.uint8, device="cuda")
+    # the 8-bit planes of the picture, written by the final layers (fused output stage)
+    planes8 = (out8[:H * W].view(H, W), out8[H * W:H * W + ch * cw].view(ch, cw),
+               out8[H * W + ch * cw:].view(ch, cw))
     out8_host = torch.empty_like(out8, device="cpu").pin_memory()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
@@ -288,10 +290,7 @@ def main():
         if from_host:
             ly.copy_(ly_h, non_blocking=True)
             luv.copy_(luv_h, non_blocking=True)
-        dec.synthesize_tiles(ly, luv, mine, H, W, out=planes)
-        dec.quantize_plane(planes[0], out=out8[:H * W])
-        dec.quantize_plane(planes[1], out=out8[H * W:H * W + ch * cw])
-        dec.quantize_plane(planes[2], out=out8[H * W + ch * cw:])
+        dec.synthesize_tiles(ly, luv, mine, H, W, out=planes8, bit_depth=8)
         sharding.gather_cores(out8, dist)
         if from_host and rank == 0:
             out8_host.copy_(out8, non_blocking=True)

@@ -183,6 +183,22 @@ int zjai_synthesize_tiles(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv,
                           int sh, float *rec_y, float *rec_u, float *rec_v, int mem,
                           const volatile int *cancel);
 
+/* Fused output stage (the `emit_output` step the reference's GPU backend fuses,
+ * gpu/src/kernels.rs:715,910): zjai_synthesize_tiles / zjai_synthesize with the planes
+ * quantized by the final layers' epilogue, exactly as `quantize_plane_par` (output.rs:330-342)
+ * quantizes the f32 planes: uint8 samples for bit_depth 8, else uint16 (bit_depth 9..16). No
+ * f32 planes are written. */
+int zjai_synthesize_tiles_q(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv,
+                            const float *y_hat_y, const float *y_hat_uv, int lh, int lw,
+                            const zjai_tile *tiles, int ntiles, int out_h, int out_w, int sv,
+                            int sh, int bit_depth, void *rec_y, void *rec_u, void *rec_v,
+                            int mem, const volatile int *cancel);
+int zjai_synthesize_q(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, const float *y_hat_y,
+                      const float *y_hat_uv, int lh, int lw, int height, int width, int out_h,
+                      int out_w, int tile_size, int overlap, int sv, int sh, int bit_depth,
+                      void *rec_y, void *rec_u, void *rec_v, int mem,
+                      const volatile int *cancel);
+
 /* ---------------------------------------------------------------------------------------- */
 /* Output stage (src/decoder/output.rs)                                                       */
 /* ---------------------------------------------------------------------------------------- */

@@ -136,6 +136,37 @@ def test_synthesize_tiled(eng, op, H, W, tile, overlap):
         assert frac >= 0.999, (frac, worst)
 
 
+@pytest.mark.parametrize("op,H,W,tile,overlap,bits", [
+    ("sop", 136, 200, 0, 0, 8),
+    ("hop", 272, 400, 128, 32, 8),
+    ("hop", 130, 142, 0, 0, 10),
+])
+def test_synthesize_fused_output(eng, op, H, W, tile, overlap, bits):
+    """The fused output stage (zjai_synthesize_q: samples quantized in the final layers'
+    epilogue) equals quantize_plane_par of the f32 planes zjai_synthesize writes, to the bit."""
+    import ctypes
+    import zenjpegai_b200 as zj
+    from zenjpegai_b200 import _lib
+    from zenjpegai_b200 import synthetic as syn
+    py, puv, ny, nuv = nets(eng, op)
+    lh, lw = -(-H // 16), -(-W // 16)
+    ly = syn.laplace_latent(12, "ly", (160, lh, lw), 1.5)
+    luv = syn.laplace_latent(12, "luv", (96, lh, lw), 1.5)
+    ch, cw = -(-H // 2), -(-W // 2)
+    p = lambda a: ctypes.c_void_p(a.ctypes.data)
+    f = [np.zeros(s, np.float32) for s in ((H, W), (ch, cw), (ch, cw))]
+    zj.check(_lib.lib().zjai_synthesize(eng.handle, ny.handle, nuv.handle, p(ly), p(luv), lh, lw,
+                                        H, W, H, W, tile, overlap, 2, 2, p(f[0]), p(f[1]),
+                                        p(f[2]), 0, None))
+    dt = np.uint8 if bits == 8 else np.uint16
+    q = [np.zeros(a.shape, dt) for a in f]
+    zj.check(_lib.lib().zjai_synthesize_q(eng.handle, ny.handle, nuv.handle, p(ly), p(luv), lh,
+                                          lw, H, W, H, W, tile, overlap, 2, 2, bits, p(q[0]),
+                                          p(q[1]), p(q[2]), 0, None))
+    for got, plane in zip(q, f):
+        assert np.array_equal(got.astype(np.uint16), zo.quantize_plane(plane, bits))
+
+
 def test_output_stage_bit_exact(eng):
     """Given identical planes, the GPU output stage equals the oracle's to the bit
     (quantize_plane_par, bicubic 4:2:0 -> 4:4:4, BT.709, round half to even)."""

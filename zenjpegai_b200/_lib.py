@@ -86,8 +86,12 @@ def lib():
     L.zjai_analysis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
     L.zjai_synthesis_tiles.argtypes = [_i] * 6 + [ctypes.POINTER(Tile), _i, ctypes.POINTER(_i)]
     L.zjai_synthesize.argtypes = [_vp, _vp, _vp, _vp, _vp] + [_i] * 10 + [_vp, _vp, _vp, _i, _vp]
+    L.zjai_synthesize_q.argtypes = [_vp, _vp, _vp, _vp, _vp] + [_i] * 11 + [_vp, _vp, _vp, _i,
+                                                                            _vp]
     L.zjai_synthesize_tiles.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.POINTER(Tile),
                                         _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp]
+    L.zjai_synthesize_tiles_q.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.POINTER(Tile),
+                                          _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp]
     L.zjai_quantize_plane.argtypes = [_vp, _vp, ctypes.c_int64, _i, _vp, _i]
     L.zjai_yuv_to_rgb.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i]
     L.zjai_conv2d.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i,

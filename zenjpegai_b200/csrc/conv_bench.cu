@@ -118,7 +118,7 @@ extern "C" int zjai_kernel_bench(zjai_ctx* ctx, int kind, int n, int h, int w, i
   for (int i = 0; i < 4; ++i) hp[(size_t)c * 9 + 2 * c + i] = 1.f + 0.25f * i;
   float* dp = static_cast<float*>(ctx->arena.alloc(hp.size() * sizeof(float)));
   float* scratch = static_cast<float*>(
-      ctx->arena.alloc(attention_scratch_floats(n, c, 4) * sizeof(float)));
+      ctx->arena.alloc(attention_scratch_floats(n, c, 4, h * w, ctx->sms) * sizeof(float)));
   if (!dp || !scratch) return fail(ZJAI_LIMIT_EXCEEDED, "kernel_bench: arena exhausted");
   ZJAI_TRY(cuda_check(cudaMemcpyAsync(dp, hp.data(), hp.size() * sizeof(float),
                                       cudaMemcpyHostToDevice, ctx->stream),

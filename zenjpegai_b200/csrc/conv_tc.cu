@@ -3,6 +3,7 @@
 #include <cstring>
 
 #include "conv_tc.cuh"
+#include "sample.cuh"
 #include "ptx.cuh"
 
 namespace zjai {
@@ -68,6 +69,18 @@ __device__ __forceinline__ uint4 pack_h8(const float (&v)[8]) {
 }
 
 // Activation of an 8-vector (one uniform branch per group, not per element).
+__device__ __forceinline__ void act8(float (&x)[8], int a);
+// The common activations (none, ReLU) without a switch; the rest through act8.
+__device__ __forceinline__ void act8_fast(float (&x)[8], int a) {
+  if (a == ACT_NONE) return;
+  if (a == ACT_RELU) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = x[e] > 0.f ? x[e] : 0.f;
+    return;
+  }
+  act8(x, a);
+}
+
 __device__ __forceinline__ void act8(float (&x)[8], int a) {
   switch (a) {
     case ACT_RELU:
@@ -141,7 +154,7 @@ __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kCh
     x[5] = v[8 * g + 5] * a.scale + b1.y;
     x[6] = v[8 * g + 6] * a.scale + b1.z;
     x[7] = v[8 * g + 7] * a.scale + b1.w;
-    act8(x, a.act1);
+    act8_fast(x, a.act1);
     if constexpr (OP != OP_NONE) {
       float q1[8];
       unpack_h8(r1[g], q1);
@@ -158,7 +171,7 @@ __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kCh
         for (int e = 0; e < 8; ++e) x[e] = q2[e] + q1[e] * x[e];
       }
     }
-    act8(x, a.act2);
+    act8_fast(x, a.act2);
     *reinterpret_cast<uint4*>(a.out + img * a.out_img + Yg[g] * a.out_row + Xg[g] * a.out_pix +
                               cg[g]) = pack_h8(x);
     if (a.out2) {
@@ -215,7 +228,7 @@ __device__ __forceinline__ void epi_staged(const ConvArgs& a, const float (&v)[k
     x[5] = v[8 * g + 5] * a.scale + b1.y;
     x[6] = v[8 * g + 6] * a.scale + b1.z;
     x[7] = v[8 * g + 7] * a.scale + b1.w;
-    act8(x, a.act1);
+    act8_fast(x, a.act1);
     if constexpr (OP != OP_NONE) {
       float q1[8];
       unpack_h8(r1[g], q1);
@@ -232,7 +245,7 @@ __device__ __forceinline__ void epi_staged(const ConvArgs& a, const float (&v)[k
         for (int e = 0; e < 8; ++e) x[e] = q2[e] + q1[e] * x[e];
       }
     }
-    act8(x, a.act2);
+    act8_fast(x, a.act2);
     dst[g] = pack_h8(x);
     if (a.out2 && valid && c < a.cph) {
 #pragma unroll
@@ -280,8 +293,20 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
     }
     float x = act_rt(v[j] * a.scale + btab[col0 + j], a.act1);
     if (a.denorm) x = fminf(fmaxf(x * 128.f + 127.5f, 0.f), 255.f);
-    float* dst = (ch == 1 && a.pout2) ? a.pout2 : a.pout + ch * a.p_plane;
-    dst[(a.img_win ? 0 : img * a.p_img) + (long long)SY * a.p_row + SX] = x;
+    const long long ei = (a.img_win ? 0 : img * a.p_img) + (long long)SY * a.p_row + SX;
+    const bool second = ch == 1 && a.pout2;  // plane 1 has its own pointer
+    if (a.qbytes) {
+      // fused output stage: the sample quantize_plane_par would make of x
+      const unsigned qv = quantize_sample(x, a.qmax);
+      char* base = reinterpret_cast<char*>(second ? a.pout2 : a.pout) +
+                   (second ? 0 : (long long)ch * a.p_plane * a.qbytes);
+      if (a.qbytes == 1)
+        reinterpret_cast<uint8_t*>(base)[ei] = (uint8_t)qv;
+      else
+        reinterpret_cast<uint16_t*>(base)[ei] = (uint16_t)qv;
+    } else {
+      (second ? a.pout2 : a.pout + ch * a.p_plane)[ei] = x;
+    }
   }
 }
 

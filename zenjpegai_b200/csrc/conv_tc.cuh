@@ -103,6 +103,11 @@ struct ConvArgs {
   const int* img_win;  // per-image {py0, px0, cy0, cy1, cx0, cx1} (device), or null
   int sv, sh;
   int lsv, lsh;        // log2 of sv / sh when both are powers of two, else -1
+  // fused output stage: qbytes 1 (uint8) or 2 (uint16) writes quantized samples
+  // (quantize_plane_par to qmax = 2^depth - 1) instead of f32; pout / pout2 are then the
+  // integer planes and the strides count samples
+  int qbytes;
+  float qmax;
   int* err;
 };
 

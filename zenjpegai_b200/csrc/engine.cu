@@ -567,6 +567,8 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     a.cx1 = o.cx1;
     a.sv = o.sv;
     a.sh = o.sh;
+    a.qbytes = o.qbytes;
+    a.qmax = o.qmax;
     const bool pow2 = (o.sv & (o.sv - 1)) == 0 && (o.sh & (o.sh - 1)) == 0;
     a.lsv = pow2 ? __builtin_ctz((unsigned)o.sv) : -1;
     a.lsh = pow2 ? __builtin_ctz((unsigned)o.sh) : -1;

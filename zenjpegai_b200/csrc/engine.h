@@ -176,6 +176,9 @@ struct ConvOut {
   long long p_plane = 0, p_row = 0, p_img = 0;
   int py0 = 0, px0 = 0, cy0 = 0, cy1 = 1 << 30, cx0 = 0, cx1 = 1 << 30, sv = 1, sh = 1;
   int out_h = -1, out_w = -1;  // planar: network output extent clip (-1 = from layer)
+  // planar: quantized samples (1 = uint8, 2 = uint16, to qmax) instead of f32 (ConvArgs)
+  int qbytes = 0;
+  float qmax = 255.f;
 };
 
 int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o);

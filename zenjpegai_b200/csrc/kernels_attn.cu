@@ -604,8 +604,7 @@ constexpr int kGramPix = 32;
 
 __global__ void attn_gram_kernel(const __half* __restrict__ qkv, int n_img, int npix, int w,
                                  int dim, int heads, long long pix, long long row, long long img,
-                                 float* __restrict__ gram, float* __restrict__ sq,
-                                 int chunks_per_block) {
+                                 float* __restrict__ part, int nparts, int chunks_per_block) {
   extern __shared__ float sm[];  // [kGramPix][2*dim]
   const int n = blockIdx.y;
   const int c = dim / heads;
@@ -656,11 +655,13 @@ __global__ void attn_gram_kernel(const __half* __restrict__ qkv, int n_img, int 
       sqacc += s;
     }
   }
+  // this block's partial slot: Gram [dim][c] then the squared norms [2 dim]
+  float* slot = part + ((long long)n * nparts + blockIdx.x) * (entries + 2 * dim);
   for (int e = 0; e < per_thread; ++e) {
     const int id = threadIdx.x + e * blockDim.x;
-    if (id < entries) atomicAdd(gram + (long long)n * entries + id, acc[e]);
+    if (id < entries) slot[id] = acc[e];
   }
-  if (threadIdx.x < 2 * dim) atomicAdd(sq + (long long)n * 2 * dim + threadIdx.x, sqacc);
+  if (threadIdx.x < 2 * dim) slot[entries + threadIdx.x] = sqacc;
 }
 
 // Gram on the tensor cores (mma.sync m16n8k16, f16 in, f32 accumulate) for head widths
@@ -693,7 +694,7 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 template <int HC>
 __global__ void __launch_bounds__(256, 2) attn_gram_mma_kernel(
     const __half* __restrict__ qkv, int npix, int w, int dim, int heads, long long pix,
-    long long row, long long img, bool dense, float* __restrict__ gram, float* __restrict__ sq,
+    long long row, long long img, bool dense, float* __restrict__ part, int nparts,
     int px_per_block) {
   constexpr int MT = HC / 16, NT = HC / 8;
   extern __shared__ __align__(16) __half gsm[];  // [2][kGramChunk][rs]
@@ -793,9 +794,12 @@ __global__ void __launch_bounds__(256, 2) attn_gram_mma_kernel(
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
 
+  // The partial slot of (block, pixel slice): Gram [dim][HC] then the squared norms [2 dim];
+  // this warp writes its head's rows and norms, each entry once (no atomics: the softmax sums
+  // the slots in a fixed order, so the result does not depend on scheduling).
   // accumulator element e of a tile: row gid (+8 for e >= 2), column 2 * tig + (e & 1)
   const int gid = lane >> 2, tig = lane & 3;
-  float* gn = gram + (long long)n * dim * HC;
+  float* gn = part + ((long long)n * nparts + blockIdx.x * nslices + slice) * (dim * HC + 2 * dim);
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -803,11 +807,11 @@ __global__ void __launch_bounds__(256, 2) attn_gram_mma_kernel(
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int i = mt * 16 + gid + (e >= 2 ? 8 : 0), j = nt * 8 + 2 * tig + (e & 1);
-        atomicAdd(gn + (hd * HC + i) * HC + j, G[mt][nt][e]);
+        gn[(hd * HC + i) * HC + j] = G[mt][nt][e];
       }
   // diagonals: n-tile 2mt holds rows mt*16 + 0..7 (elements 0, 1), n-tile 2mt+1 rows
   // mt*16 + 8..15 (elements 2, 3); element (gid, 2 tig + b) is diagonal when gid == 2 tig + b
-  float* sn = sq + (long long)n * 2 * dim;
+  float* sn = gn + dim * HC;
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -816,27 +820,41 @@ __global__ void __launch_bounds__(256, 2) attn_gram_mma_kernel(
       for (int b = 0; b < 2; ++b)
         if (gid == 2 * tig + b) {
           const int i = mt * 16 + e * 8 + gid;
-          atomicAdd(sn + hd * HC + i, Dq[mt][e][2 * e + b]);
-          atomicAdd(sn + dim + hd * HC + i, Dk[mt][e][2 * e + b]);
+          sn[hd * HC + i] = Dq[mt][e][2 * e + b];
+          sn[dim + hd * HC + i] = Dk[mt][e][2 * e + b];
         }
 }
 
 // attn[n][h][i][j] = softmax_j( G_ij / (max(|q_i|, eps) max(|k_j|, eps)) * T[h] )
-__global__ void attn_softmax_kernel(const float* __restrict__ gram, const float* __restrict__ sq,
-                                    const float* __restrict__ temp, float* __restrict__ attn,
-                                    int n_img, int dim, int heads) {
+// red[n][e] = sum over the nparts partial slots of part[n][k][e], k in order (one thread per
+// element, coalesced): the Gram [dim][c] and squared norms [2 dim] of each picture.
+__global__ void attn_reduce_kernel(const float* __restrict__ part, int nparts, long long stride,
+                                   int n_img, float* __restrict__ red) {
+  const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= (long long)n_img * stride) return;
+  const long long n = id / stride, e = id - n * stride;
+  const float* p = part + n * nparts * stride + e;
+  float acc = 0.f;
+  for (int k = 0; k < nparts; ++k) acc += p[k * stride];
+  red[id] = acc;
+}
+
+// One attention row (picture n, row ri = h*c + i) from the reduced Gram and norms.
+__global__ void attn_softmax_kernel(const float* __restrict__ red, const float* __restrict__ temp,
+                                    float* __restrict__ attn, int n_img, int dim, int heads) {
   const int c = dim / heads;
   long long row = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= (long long)n_img * dim) return;
   const int n = (int)(row / dim), ri = (int)(row % dim);
   const int hd = ri / c;
-  const float* g = gram + (long long)n * dim * c + (long long)ri * c;
-  const float* s = sq + (long long)n * 2 * dim;
-  const float nq = fmaxf(sqrtf(s[ri]), 1e-12f);
+  const long long stride = (long long)dim * c + 2 * dim;
+  const float* g = red + n * stride + (long long)ri * c;
+  const float* sq = red + n * stride + (long long)dim * c;
+  const float nq = fmaxf(sqrtf(sq[ri]), 1e-12f);
   float vals[64];
   float mx = -INFINITY;
   for (int j = 0; j < c; ++j) {
-    const float nk = fmaxf(sqrtf(s[dim + hd * c + j]), 1e-12f);
+    const float nk = fmaxf(sqrtf(sq[dim + hd * c + j]), 1e-12f);
     const float v = g[j] / (nq * nk) * temp[hd];
     vals[j] = v;
     mx = fmaxf(mx, v);
@@ -1065,18 +1083,48 @@ int launch_dw3x3(Ctx* ctx, const TView& x, const TView& y, const float* wt, bool
   return cuda_check(cudaGetLastError(), "dw3x3_kernel launch");
 }
 
-// Gram, norms and softmax: the attention matrices attn[n][h][i][j] (scratch + attn_offset).
+// Launch geometry of the Gram step: `blocks` per picture, `per_block` pixels (mma path) or
+// pixel chunks (generic path) per block, and the partial slots per picture (one per block and
+// pixel slice) that the softmax sums.
+struct GramPlan {
+  bool mma;
+  int blocks, per_block, nparts;
+};
+static GramPlan gram_plan(int n, int dim, int heads, int npix, int sms) {
+  const int c = dim / heads;
+  GramPlan g;
+  g.mma = (c == 16 || c == 32) && (heads == 2 || heads == 4 || heads == 8);
+  if (g.mma) {
+    // two blocks per SM (registers allow two) over the whole batch, one wave, whole chunks
+    // per block; 8 / heads warps share a head's pixels (the slices)
+    const int chunks = (npix + kGramChunk - 1) / kGramChunk;
+    // (at most 32 blocks per picture: small batches keep few partial slots to sum)
+    const int splits = std::max(1, std::min(std::min(chunks, 32), (2 * sms) / std::max(1, n)));
+    g.per_block = ((chunks + splits - 1) / splits) * kGramChunk;
+    g.blocks = (npix + g.per_block - 1) / g.per_block;
+    g.nparts = g.blocks * (8 / heads);
+  } else {
+    const int chunks = (npix + kGramPix - 1) / kGramPix;
+    g.per_block = std::max(1, chunks / 64);
+    g.blocks = (chunks + g.per_block - 1) / g.per_block;
+    g.nparts = g.blocks;
+  }
+  return g;
+}
+
+// Gram, norms and softmax: the attention matrices attn[n][h][i][j] (in the scratch).
 static float* attention_weights(const TView& qkv, int heads, const float* temp, float* scratch,
                                 int sms, cudaStream_t s) {
   const int dim = qkv.c / 3;
   const int c = dim / heads;
   const int n = qkv.n;
-  float* gram = scratch;                              // n * dim * c
-  float* sq = gram + (size_t)n * dim * c;             // n * 2 * dim
-  float* attn = sq + (size_t)n * 2 * dim;             // n * dim * c
-  cudaMemsetAsync(gram, 0, sizeof(float) * ((size_t)n * dim * c + (size_t)n * 2 * dim), s);
   const int npix = qkv.h * qkv.w;
-  if ((c == 16 || c == 32) && (heads == 2 || heads == 4 || heads == 8)) {
+  const GramPlan gp = gram_plan(n, dim, heads, npix, sms);
+  const long long stride = (long long)dim * c + 2 * dim;  // Gram [dim][c], norms [2 dim]
+  float* part = scratch;                                  // n * nparts partial slots
+  float* red = part + (size_t)n * gp.nparts * stride;     // n reduced slots
+  float* attn = red + (size_t)n * stride;                 // n * dim * c
+  if (gp.mma) {
     const int smem = 2 * kGramChunk * (2 * dim + 8) * (int)sizeof(__half);
     static bool attr_set = false;
     if (!attr_set) {  // covers dim <= 8 * 32
@@ -1087,30 +1135,26 @@ static float* attention_weights(const TView& qkv, int heads, const float* temp, 
                            most);
       attr_set = true;
     }
-    // two blocks per SM (registers allow two) over the whole batch, one wave, whole chunks per
-    // block
-    const int chunks = (npix + kGramChunk - 1) / kGramChunk;
-    const int splits = std::max(1, std::min(chunks, (2 * sms) / n));
-    const int px_per_block = ((chunks + splits - 1) / splits) * kGramChunk;
-    dim3 g1((npix + px_per_block - 1) / px_per_block, n);
+    dim3 g1(gp.blocks, n);
     const bool dense = qkv.row == qkv.w * qkv.pix;  // rows contiguous within a picture
     if (c == 32)
       attn_gram_mma_kernel<32><<<g1, 256, smem, s>>>(qkv.p, npix, qkv.w, dim, heads, qkv.pix,
-                                                     qkv.row, qkv.img, dense, gram, sq,
-                                                     px_per_block);
+                                                     qkv.row, qkv.img, dense, part, gp.nparts,
+                                                     gp.per_block);
     else
       attn_gram_mma_kernel<16><<<g1, 256, smem, s>>>(qkv.p, npix, qkv.w, dim, heads, qkv.pix,
-                                                     qkv.row, qkv.img, dense, gram, sq,
-                                                     px_per_block);
+                                                     qkv.row, qkv.img, dense, part, gp.nparts,
+                                                     gp.per_block);
   } else {
-    const int chunks = (npix + kGramPix - 1) / kGramPix;
-    const int cpb = std::max(1, chunks / 64);
-    dim3 g1((chunks + cpb - 1) / cpb, n);
+    dim3 g1(gp.blocks, n);
     attn_gram_kernel<<<g1, 256, kGramPix * 2 * dim * sizeof(float), s>>>(
-        qkv.p, n, npix, qkv.w, dim, heads, qkv.pix, qkv.row, qkv.img, gram, sq, cpb);
+        qkv.p, n, npix, qkv.w, dim, heads, qkv.pix, qkv.row, qkv.img, part, gp.nparts,
+        gp.per_block);
   }
-  attn_softmax_kernel<<<blocks_for((long long)n * dim, 128), 128, 0, s>>>(gram, sq, temp, attn, n,
-                                                                         dim, heads);
+  attn_reduce_kernel<<<blocks_for((long long)n * stride, 256), 256, 0, s>>>(part, gp.nparts,
+                                                                           stride, n, red);
+  attn_softmax_kernel<<<blocks_for((long long)n * dim, 128), 128, 0, s>>>(red, temp, attn, n, dim,
+                                                                         heads);
   return attn;
 }
 
@@ -1150,9 +1194,11 @@ void launch_attention(const TView& qkv, const TView& out, int heads, const float
   }
 }
 
-size_t attention_scratch_floats(int n_img, int dim, int heads) {
+size_t attention_scratch_floats(int n_img, int dim, int heads, int npix, int sms) {
   const int c = dim / heads;
-  return (size_t)n_img * (2 * (size_t)dim * c + 2 * (size_t)dim);
+  const GramPlan gp = gram_plan(n_img, dim, heads, npix, sms);
+  return (size_t)n_img * ((size_t)(gp.nparts + 1) * ((size_t)dim * c + 2 * (size_t)dim) +
+                          (size_t)dim * c);
 }
 
 void launch_gather_latent(const float* src, int C, int LH, int LW, const int* origin,

@@ -10,10 +10,12 @@ void launch_layer_norm(const TView& x, const TView& y, const float* gamma, const
 // dw[k + c/2]. Persistent kernels over ctx->sms multiprocessors; returns the launch status.
 int launch_dw3x3(Ctx* ctx, const TView& x, const TView& y, const float* wt, bool gate,
                  cudaStream_t s);
-// scratch: attention_scratch_floats(n, dim, heads) floats of device memory
+// scratch: attention_scratch_floats(n, dim, heads, h * w, sms) floats of device memory
 void launch_attention(const TView& qkv, const TView& out, int heads, const float* temp,
                       float* scratch, int sms, cudaStream_t s);
-size_t attention_scratch_floats(int n_img, int dim, int heads);
+// Scratch of the attention of n pictures of npix pixels: the Gram kernel's partial slots
+// (summed in a fixed order, so the result is independent of scheduling) and the matrices.
+size_t attention_scratch_floats(int n_img, int dim, int heads, int npix, int sms);
 // The attention up to its matrices A_n, then A folded into the following 1x1 projection
 // W_o (f32 [dim][dim], device): writes n per-picture weight sets in the blocked layout of the
 // packed layer L (which holds W_o), scaled by `wscale`, at wout (n * L.npad * L.cin_pad

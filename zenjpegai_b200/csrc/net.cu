@@ -402,7 +402,7 @@ int Runner::tb(const std::string& p, const TView& x) {
   });
   ZJAI_TRY(st);
   float* scratch = static_cast<float*>(
-      arena->alloc(attention_scratch_floats(n, d, 4) * sizeof(float)));
+      arena->alloc(attention_scratch_floats(n, d, 4, x.h * x.w, ctx->sms) * sizeof(float)));
   if (!scratch) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (attention scratch)");
   // x += W_o (A . v): the attention matrices A_n, folded into per-picture projection weights
   // W_o . blockdiag(A_n), then one tcgen05 1x1 conv over the v slice of qkv2. The Gram reads
@@ -413,7 +413,7 @@ int Runner::tb(const std::string& p, const TView& x) {
   __half* wfold = static_cast<__half*>(arena->alloc((size_t)n * wset * sizeof(__half)));
   if (!wfold) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (folded weights)");
   const float fs = net->fold_scale.at(p);
-  mem_kernel(p + ".attn", "attn", b16 * 2 * d, 3, [&] {
+  mem_kernel(p + ".attn", "attn", b16 * 2 * d, 4, [&] {
     launch_attention_fold(qkv2, 4, vec(p + ".attn.temperature"),
                           vec(p + ".attn.project_out.weight"), fs, *Lo, wfold, scratch, ctx->sms,
                           stream);
@@ -514,6 +514,8 @@ int Runner::final_planar(const std::string& name, const TView& x, const FinalOut
   o.img_win = fo.win;
   o.sv = fo.sv;
   o.sh = fo.sh;
+  o.qbytes = fo.qbytes;
+  o.qmax = fo.qmax;
   if (fo.full_h > 0) {
     o.out_h = fo.full_h;
     o.out_w = fo.full_w;

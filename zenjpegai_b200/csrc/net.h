@@ -28,6 +28,9 @@ struct FinalOut {
   const int* win = nullptr;      // per-tile {py0, px0, cy0, cy1, cx0, cx1} (device) or null
   int sv = 1, sh = 1;
   int full_h = -1, full_w = -1;  // clip of the network output extent (-1: natural)
+  // fused output stage: planes of quantized samples (1 = uint8, 2 = uint16, to qmax)
+  int qbytes = 0;
+  float qmax = 255.f;
 };
 
 // Executes one network on a batch of `n` same-shape inputs on one stream, allocating its

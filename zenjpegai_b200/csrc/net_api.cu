@@ -60,7 +60,11 @@ namespace zjai {
 int synthesize_tiles_dev(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const float* lat_uv,
                          int lh, int lw, const std::vector<zjai_tile>& tiles, int out_h, int out_w,
                          int sv, int sh, float* rec_y, float* rec_u, float* rec_v,
-                         const volatile int* cancel, double* flops) {
+                         const volatile int* cancel, double* flops, int bit_depth) {
+  // bit_depth > 0: the final layers write quantized samples (uint8 for 8 bits, else uint16)
+  // into rec_* instead of f32 planes
+  const int qbytes = bit_depth <= 0 ? 0 : bit_depth == 8 ? 1 : 2;
+  const float qmax = bit_depth <= 0 ? 255.f : (float)((1u << bit_depth) - 1);
   if (!ny || !nuv || ny->kind != ZJAI_SYN_Y || nuv->kind != ZJAI_SYN_UV || ny->op != nuv->op)
     return fail(ZJAI_INVALID_ARGUMENT, "synthesize: needs a SYN_Y and a SYN_UV network of one op");
   if (sv <= 0 || sh <= 0) return fail(ZJAI_INVALID_DATA, "chroma subsampling factor");
@@ -112,6 +116,8 @@ int synthesize_tiles_dev(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const 
       fo.plane0 = rec_y;
       fo.row = out_w;
       fo.win = d_win_y;
+      fo.qbytes = qbytes;
+      fo.qmax = qmax;
       ZJAI_TRY(r.primary(cat.channels(0, 160), img_h, img_w, fo));
       if (flops) *flops += r.flops;
     }
@@ -131,6 +137,8 @@ int synthesize_tiles_dev(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const 
       fo.win = d_win_uv;
       fo.sv = sv;
       fo.sh = sh;
+      fo.qbytes = qbytes;
+      fo.qmax = qmax;
       ZJAI_TRY(r.secondary(cat, x144, img_h, img_w, fo));
       if (flops) *flops += r.flops;
     }
@@ -281,15 +289,23 @@ int zjai_synthesis_tiles(int height, int width, int latent_h, int latent_w, int 
   return ZJAI_OK;
 }
 
-int zjai_synthesize_tiles(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const float* y_hat_y,
-                          const float* y_hat_uv, int lh, int lw, const zjai_tile* tiles,
-                          int ntiles, int out_h, int out_w, int sv, int sh, float* rec_y,
-                          float* rec_u, float* rec_v, int mem, const volatile int* cancel) {
+}  // extern "C"
+
+// zjai_synthesize_tiles with f32 planes (bit_depth 0) or quantized sample planes (8: uint8,
+// else uint16), written by the final layers' epilogue.
+static int synthesize_tiles_entry(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv,
+                                  const float* y_hat_y, const float* y_hat_uv, int lh, int lw,
+                                  const zjai_tile* tiles, int ntiles, int out_h, int out_w,
+                                  int sv, int sh, int bit_depth, void* rec_y, void* rec_u,
+                                  void* rec_v, int mem, const volatile int* cancel) {
   ZJAI_TRY(ctx_enter(ctx));
   if (!y_hat_y || !y_hat_uv || !rec_y || !rec_u || !rec_v || (ntiles > 0 && !tiles) ||
       lh <= 0 || lw <= 0 || out_h <= 0 || out_w <= 0)
     return fail(ZJAI_INVALID_ARGUMENT, "synthesize: bad arguments");
   if (sv <= 0 || sh <= 0) return fail(ZJAI_INVALID_DATA, "chroma subsampling factor");
+  if (bit_depth < 0 || bit_depth > 16 || (bit_depth > 0 && bit_depth < 8))
+    return fail(ZJAI_INVALID_ARGUMENT, "synthesize: bit depth must be 8..16 (or 0 for f32)");
+  const size_t es = bit_depth == 0 ? sizeof(float) : bit_depth == 8 ? 1 : 2;  // sample bytes
   ArenaScope scope(ctx);
   const size_t m2 = ctx->arena2.mark();
   struct Rel {
@@ -302,25 +318,48 @@ int zjai_synthesize_tiles(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, cons
   ZJAI_TRY(stage_in(ctx, y_hat_uv, (size_t)96 * lh * lw, mem, &duv));
   const int ch = cdiv(out_h, sv), cw = cdiv(out_w, sh);
   const size_t ny = (size_t)out_h * out_w, nc = (size_t)ch * cw;
-  float *oy = rec_y, *ou = rec_u, *ov = rec_v;
+  char *oy = static_cast<char*>(rec_y), *ou = static_cast<char*>(rec_u),
+       *ov = static_cast<char*>(rec_v);
   if (mem == ZJAI_MEM_HOST) {
-    oy = static_cast<float*>(ctx->arena.alloc((ny + 2 * nc) * sizeof(float)));
+    oy = static_cast<char*>(ctx->arena.alloc((ny + 2 * nc) * es));
     if (!oy) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (output planes)");
-    ou = oy + ny;
-    ov = ou + nc;
-    ZJAI_TRY(cuda_check(cudaMemsetAsync(oy, 0, (ny + 2 * nc) * sizeof(float), ctx->stream), "memset"));
+    ou = oy + ny * es;
+    ov = ou + nc * es;
+    ZJAI_TRY(cuda_check(cudaMemsetAsync(oy, 0, (ny + 2 * nc) * es, ctx->stream), "memset"));
   }
   std::vector<zjai_tile> tv(tiles, tiles + ntiles);
   int st = synthesize_tiles_dev(ctx, reinterpret_cast<Net*>(net_y), reinterpret_cast<Net*>(net_uv),
-                                dy, duv, lh, lw, tv, out_h, out_w, sv, sh, oy, ou, ov, cancel,
-                                nullptr);
+                                dy, duv, lh, lw, tv, out_h, out_w, sv, sh,
+                                reinterpret_cast<float*>(oy), reinterpret_cast<float*>(ou),
+                                reinterpret_cast<float*>(ov), cancel, nullptr, bit_depth);
   if (st != ZJAI_OK) return settle(ctx, st);
   if (mem == ZJAI_MEM_HOST) {
-    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_y, oy, ny * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
-    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_u, ou, nc * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
-    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_v, ov, nc * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_y, oy, ny * es, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_u, ou, nc * es, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_v, ov, nc * es, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
   }
   return finish_call(ctx, mem);
+}
+
+extern "C" {
+
+int zjai_synthesize_tiles(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const float* y_hat_y,
+                          const float* y_hat_uv, int lh, int lw, const zjai_tile* tiles,
+                          int ntiles, int out_h, int out_w, int sv, int sh, float* rec_y,
+                          float* rec_u, float* rec_v, int mem, const volatile int* cancel) {
+  return synthesize_tiles_entry(ctx, net_y, net_uv, y_hat_y, y_hat_uv, lh, lw, tiles, ntiles,
+                                out_h, out_w, sv, sh, 0, rec_y, rec_u, rec_v, mem, cancel);
+}
+
+int zjai_synthesize_tiles_q(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv,
+                            const float* y_hat_y, const float* y_hat_uv, int lh, int lw,
+                            const zjai_tile* tiles, int ntiles, int out_h, int out_w, int sv,
+                            int sh, int bit_depth, void* rec_y, void* rec_u, void* rec_v,
+                            int mem, const volatile int* cancel) {
+  if (bit_depth < 8) return fail(ZJAI_INVALID_ARGUMENT, "synthesize: bit depth must be 8..16");
+  return synthesize_tiles_entry(ctx, net_y, net_uv, y_hat_y, y_hat_uv, lh, lw, tiles, ntiles,
+                                out_h, out_w, sv, sh, bit_depth, rec_y, rec_u, rec_v, mem,
+                                cancel);
 }
 
 int zjai_synthesize(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const float* y_hat_y,
@@ -332,6 +371,18 @@ int zjai_synthesize(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const floa
   return zjai_synthesize_tiles(ctx, net_y, net_uv, y_hat_y, y_hat_uv, lh, lw, v.data(),
                                (int)v.size(), out_h, out_w, sv, sh, rec_y, rec_u, rec_v, mem,
                                cancel);
+}
+
+int zjai_synthesize_q(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const float* y_hat_y,
+                      const float* y_hat_uv, int lh, int lw, int height, int width, int out_h,
+                      int out_w, int tile_size, int overlap, int sv, int sh, int bit_depth,
+                      void* rec_y, void* rec_u, void* rec_v, int mem,
+                      const volatile int* cancel) {
+  std::vector<zjai_tile> v;
+  ZJAI_TRY(synthesis_tiles(height, width, lh, lw, tile_size, overlap, &v));
+  return zjai_synthesize_tiles_q(ctx, net_y, net_uv, y_hat_y, y_hat_uv, lh, lw, v.data(),
+                                 (int)v.size(), out_h, out_w, sv, sh, bit_depth, rec_y, rec_u,
+                                 rec_v, mem, cancel);
 }
 
 // ---- attention-block layer entries ---------------------------------------------------------
@@ -373,7 +424,7 @@ int zjai_channel_attention(zjai_ctx* ctx, const float* qkv, int c3, int h, int w
   ZJAI_TRY(planar_to_tensor(ctx, dq, c3, h, w, &t));
   ZJAI_TRY(alloc_tensor(ctx, 1, h, w, dim, &o));
   float* scratch =
-      static_cast<float*>(ctx->arena.alloc(attention_scratch_floats(1, dim, heads) * sizeof(float)));
+      static_cast<float*>(ctx->arena.alloc(attention_scratch_floats(1, dim, heads, h * w, ctx->sms) * sizeof(float)));
   if (!scratch) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (attention)");
   launch_attention(t, o, heads, dt, scratch, ctx->sms, ctx->stream);
   float* dout;

@@ -3,6 +3,7 @@
 // intrinsics keep the compiler from contracting a multiply and an add that the reference
 // rounds separately, and `__fmaf_rn` is used exactly where the reference fuses.
 #include "api_common.h"
+#include "sample.cuh"
 
 namespace zjai {
 
@@ -10,27 +11,13 @@ namespace {
 
 inline int blocks_for(long long n, int t) { return (int)((n + t - 1) / t); }
 
-__device__ __forceinline__ float clampf(float v, float lo, float hi) {
-  return v < lo ? lo : (v > hi ? hi : v);
-}
-
-// RangesOps.convert_range for ranges starting at zero: ((x - 0) / in_max) * out_max + 0
-__device__ __forceinline__ float convert_range(float x, float in_max, float out_max) {
-  return __fadd_rn(__fmul_rn(__fdiv_rn(__fsub_rn(x, 0.f), in_max), out_max), 0.f);
-}
-
-// f32 -> integer sample, round half to even, clamped to [0, mx]; NaN -> 0 (Rust's `as`).
-__device__ __forceinline__ unsigned q_sample(float v, float mx) {
-  v = clampf(rintf(v), 0.f, mx);
-  return v == v ? (unsigned)v : 0u;
-}
 
 // quantize_plane_par (output.rs:330-342)
 __global__ void quantize_plane_kernel(const float* __restrict__ x, long long n, float mx,
                                       int bytes, void* out) {
   long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  const unsigned q = q_sample(convert_range(clampf(x[i], 0.f, 255.f), 255.f, mx), mx);
+  const unsigned q = quantize_sample(x[i], mx);
   if (bytes == 1)
     static_cast<uint8_t*>(out)[i] = (uint8_t)q;
   else

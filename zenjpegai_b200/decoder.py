@@ -30,6 +30,11 @@ def _cdiv(a, b):
     return -(-a // b)
 
 
+def _ptr(a):
+    """Address of an integer sample plane (torch tensor or numpy array)."""
+    return ctypes.c_void_p(a.data_ptr() if hasattr(a, "data_ptr") else a.ctypes.data)
+
+
 class Decoder:
     """Synthesis networks of one operating point, loaded once (the crate's model cache,
     api.rs:135-157) and reused for every picture."""
@@ -44,48 +49,71 @@ class Decoder:
         self.net_y.close()
         self.net_uv.close()
 
-    def _planes(self, like, out_h, out_w, sv, sh):
+    def _planes(self, like, out_h, out_w, sv, sh, bit_depth=None):
+        """Zeroed output planes: f32, or the integer samples of `bit_depth` (uint8 for 8 bits,
+        else uint16; int16 storage for torch, which has no uint16)."""
         ch, cw = _cdiv(out_h, sv), _cdiv(out_w, sh)
         if type(like).__module__.startswith("torch"):
             import torch
-            z = lambda s: torch.zeros(s, dtype=torch.float32, device=like.device)
+            dt = (torch.float32 if bit_depth is None else
+                  torch.uint8 if bit_depth == 8 else torch.int16)
+            z = lambda s: torch.zeros(s, dtype=dt, device=like.device)
         else:
-            z = lambda s: np.zeros(s, np.float32)
+            dt = np.float32 if bit_depth is None else np.uint8 if bit_depth == 8 else np.uint16
+            z = lambda s: np.zeros(s, dt)
         return z((out_h, out_w)), z((ch, cw)), z((ch, cw))
 
     def synthesize(self, y_hat_y, y_hat_uv, height, width, out_h=None, out_w=None,
-                   tile_size=0, overlap=0, sv=2, sh=2, out=None, cancel=None):
+                   tile_size=0, overlap=0, sv=2, sh=2, out=None, cancel=None, bit_depth=None):
         """Whole picture: latents [160, lh, lw] / [96, lh, lw] -> planes (y, u, v) in [0, 255]
         (`synthesize_with`, reconstruct.rs:274-331). `cancel` is an optional ctypes c_int
-        polled between tiles and layers (the crate's `Stop`)."""
+        polled between tiles and layers (the crate's `Stop`). With `bit_depth`, the planes are
+        the quantized samples (`quantize_plane_par`, output.rs:330-342) written by the final
+        layers directly (the fused output stage)."""
         out_h = height if out_h is None else out_h
         out_w = width if out_w is None else out_w
         _, lh, lw = y_hat_y.shape
-        ry, ru, rv = out if out is not None else self._planes(y_hat_y, out_h, out_w, sv, sh)
+        ry, ru, rv = out if out is not None else self._planes(y_hat_y, out_h, out_w, sv, sh,
+                                                              bit_depth)
         py, mem = _arg(y_hat_y, (160, lh, lw))
         puv, _ = _arg(y_hat_uv, (96, lh, lw))
-        check(_lib.lib().zjai_synthesize(
-            self.engine.handle, self.net_y.handle, self.net_uv.handle, py, puv, lh, lw, height,
-            width, out_h, out_w, tile_size, overlap, sv, sh, _arg(ry)[0], _arg(ru)[0],
-            _arg(rv)[0], mem, ctypes.byref(cancel) if cancel is not None else None))
+        stop = ctypes.byref(cancel) if cancel is not None else None
+        if bit_depth is None:
+            check(_lib.lib().zjai_synthesize(
+                self.engine.handle, self.net_y.handle, self.net_uv.handle, py, puv, lh, lw,
+                height, width, out_h, out_w, tile_size, overlap, sv, sh, _arg(ry)[0],
+                _arg(ru)[0], _arg(rv)[0], mem, stop))
+        else:
+            check(_lib.lib().zjai_synthesize_q(
+                self.engine.handle, self.net_y.handle, self.net_uv.handle, py, puv, lh, lw,
+                height, width, out_h, out_w, tile_size, overlap, sv, sh, bit_depth,
+                _ptr(ry), _ptr(ru), _ptr(rv), mem, stop))
         return ry, ru, rv
 
     def synthesize_tiles(self, y_hat_y, y_hat_uv, tiles, out_h, out_w, sv=2, sh=2, out=None,
-                         cancel=None):
+                         cancel=None, bit_depth=None):
         """Only the listed tiles (a shard of `synthesis_tiles`); planes outside their cores
-        are left as they are."""
+        are left as they are. `bit_depth`: quantized sample planes as in `synthesize`."""
         _, lh, lw = y_hat_y.shape
-        ry, ru, rv = out if out is not None else self._planes(y_hat_y, out_h, out_w, sv, sh)
+        ry, ru, rv = out if out is not None else self._planes(y_hat_y, out_h, out_w, sv, sh,
+                                                              bit_depth)
         arr = (_lib.Tile * max(1, len(tiles)))()
         for i, t in enumerate(tiles):
             for k, _ in _lib.Tile._fields_:
                 setattr(arr[i], k, int(t[k]))
         py, mem = _arg(y_hat_y, (160, lh, lw))
         puv, _ = _arg(y_hat_uv, (96, lh, lw))
-        check(_lib.lib().zjai_synthesize_tiles(
-            self.engine.handle, self.net_y.handle, self.net_uv.handle, py, puv, lh, lw, arr,
-            len(tiles), out_h, out_w, sv, sh, _arg(ry)[0], _arg(ru)[0], _arg(rv)[0], mem,
-            ctypes.byref(cancel) if cancel is not None else None))
+        stop = ctypes.byref(cancel) if cancel is not None else None
+        if bit_depth is None:
+            check(_lib.lib().zjai_synthesize_tiles(
+                self.engine.handle, self.net_y.handle, self.net_uv.handle, py, puv, lh, lw, arr,
+                len(tiles), out_h, out_w, sv, sh, _arg(ry)[0], _arg(ru)[0], _arg(rv)[0], mem,
+                stop))
+        else:
+            check(_lib.lib().zjai_synthesize_tiles_q(
+                self.engine.handle, self.net_y.handle, self.net_uv.handle, py, puv, lh, lw, arr,
+                len(tiles), out_h, out_w, sv, sh, bit_depth, _ptr(ry), _ptr(ru), _ptr(rv), mem,
+                stop))
         return ry, ru, rv
 
     # ---- output stage (src/decoder/output.rs) -------------------------------------------
