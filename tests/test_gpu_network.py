@@ -100,7 +100,7 @@ def test_synthesis_tile(eng, op, h, w):
         assert frac >= 0.999, (op, frac, worst)
 
 
-def _synth_both(eng, op, H, W, tile, overlap, sv=2, sh=2):
+def _synth_gpu(eng, op, H, W, tile, overlap, sv=2, sh=2):
     import ctypes
     import zenjpegai_b200 as zj
     from zenjpegai_b200 import _lib
@@ -117,9 +117,14 @@ def _synth_both(eng, op, H, W, tile, overlap, sv=2, sh=2):
     zj.check(_lib.lib().zjai_synthesize(eng.handle, ny.handle, nuv.handle, p(ly), p(luv), lh, lw,
                                         H, W, H, W, tile, overlap, sv, sh, p(ry), p(ru), p(rv),
                                         0, None))
+    return (ry, ru, rv), (py, puv, ly, luv)
+
+
+def _synth_both(eng, op, H, W, tile, overlap, sv=2, sh=2):
+    got, (py, puv, ly, luv) = _synth_gpu(eng, op, H, W, tile, overlap, sv, sh)
     wy, wu, wv = zo.synthesize(zo.Checkpoint(py), zo.Checkpoint(puv), zo.OPS[op], ly, luv, H, W,
                                tile_size=tile, overlap=overlap, sv=sv, sh=sh)
-    return (ry, ru, rv), (wy, wu, wv)
+    return got, (wy, wu, wv)
 
 
 @pytest.mark.parametrize("op,H,W,tile,overlap", [
@@ -165,6 +170,16 @@ def test_synthesize_fused_output(eng, op, H, W, tile, overlap, bits):
                                           p(q[1]), p(q[2]), 0, None))
     for got, plane in zip(q, f):
         assert np.array_equal(got.astype(np.uint16), zo.quantize_plane(plane, bits))
+
+
+def test_synthesize_deterministic(eng):
+    """Two runs of the same tiled HOP synthesis give identical planes (no atomics or
+    scheduling-dependent reductions anywhere on the path; the crate asserts bit-identity across
+    thread counts, tests/decode_ref.rs:378)."""
+    a, _ = _synth_gpu(eng, "hop", 272, 400, 128, 32)
+    b, _ = _synth_gpu(eng, "hop", 272, 400, 128, 32)
+    for x, y in zip(a, b):
+        assert np.array_equal(x, y)
 
 
 def test_output_stage_bit_exact(eng):
