@@ -190,16 +190,6 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src
                : "memory");
 }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
-  const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 f = __half22float2(h[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-
 template <bool GATE>
 struct DwShape {
   static constexpr int G = GATE ? 16 : 8;  // source channel groups per block
