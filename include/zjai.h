@@ -248,6 +248,15 @@ int zjai_depthwise3x3(zjai_ctx *ctx, const float *x, int c, int h, int w, const 
 int zjai_depthwise3x3_elu_gate(zjai_ctx *ctx, const float *x, int c, int h, int w,
                                const float *weight, float *out, int mem);
 
+/* The feed-forward half of `TransformerBlock::forward` (attention.rs:346-371) on one picture:
+ * out = x + W_out . gate(dw3x3(W_in . layer_norm(x))), gate(t) = elu(t[:hidden]) * t[hidden:]
+ * (math.rs:376). x / out [c][h][w], norm weight / bias [c], w_in [2 hidden][c], w_dw
+ * [2 hidden][9], w_out [c][hidden]; c 64 or 128, hidden a multiple of 64. Runs the layer norm
+ * and the fused tcgen05 FFN kernel (the 2 hidden-channel intermediates stay on chip). */
+int zjai_transformer_ffn(zjai_ctx *ctx, const float *x, int c, int h, int w, int hidden,
+                         const float *norm_weight, const float *norm_bias, const float *w_in,
+                         const float *w_dw, const float *w_out, float *out, int mem);
+
 /* Layer-level timing harness, the GPU counterpart of the crate's conv microbenchmark
  * (benches/conv_kernels.rs:165-187: `PackedConv::new` + `forward` on layer shapes): packs a
  * random conv (or, with `transposed`, a stride-2 transposed conv: k 3 -> p1 op1, k 4 -> p1) of

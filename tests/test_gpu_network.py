@@ -244,6 +244,34 @@ def test_depthwise_elu_gate(eng, c, h, w):
     assert rel_l2(got, want) < REL_L2
 
 
+@pytest.mark.parametrize("dim,hidden,h,w", [
+    (128, 512, 40, 52),  # HOP luma width: 8 chunks, two 64-channel slabs of K, ragged tiles
+    (64, 256, 37, 29),   # HOP chroma width: 4 chunks, one slab
+    (128, 512, 12, 16),  # exactly one tile
+    (64, 256, 5, 7),     # smaller than a tile
+    (128, 256, 26, 33),  # other hidden width
+])
+def test_transformer_ffn(eng, dim, hidden, h, w):
+    # fused FFN kernel (project_in -> depthwise 3x3 + ELU gate -> project_out + residual in one
+    # tcgen05 kernel) after the layer norm, against the oracle's layers composed
+    from zenjpegai_b200 import synthetic as syn
+    x = syn.normal(9, "x", (dim, h, w))
+    nw = syn.uniform(9, "nw", (dim,), 0.5, 1.5)
+    nb = syn.normal(9, "nb", (dim,), std=0.1)
+    wi = syn.normal(9, "wi", (2 * hidden, dim, 1, 1), std=dim ** -0.5)
+    wd = syn.normal(9, "wd", (2 * hidden, 1, 3, 3), std=0.3)
+    wo = syn.normal(9, "wo", (dim, hidden, 1, 1), std=hidden ** -0.5)
+    got = eng.transformer_ffn(x, nw, nb, wi, wd, wo)
+    t = zo.layer_norm_channels(x, nw, nb)
+    t = zo.conv2d(t, wi)
+    t = zo.conv2d(t, wd, None, pad=(1, 1), groups=2 * hidden)
+    t = zo.elu_gate(t[:hidden], t[hidden:])
+    t = zo.conv2d(t, wo)
+    assert got.shape == x.shape
+    # the FFN's own contribution (residual removed) within the layer tolerance
+    assert rel_l2(got - x, t) < REL_L2
+
+
 @pytest.mark.parametrize("dim,h,w", [(128, 40, 52), (64, 64, 64), (96, 17, 29)])
 def test_channel_attention(eng, dim, h, w):
     # 128 / 64: register-tiled Gram and per-head apply (head width 32 / 16); 96: generic kernels

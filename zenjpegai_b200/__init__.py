@@ -170,6 +170,19 @@ class Engine:
                                                     _arg(out, shape)[0], mem))
         return out
 
+    def transformer_ffn(self, x, norm_weight, norm_bias, w_in, w_dw, w_out, out=None):
+        """The feed-forward half of `TransformerBlock::forward` (attention.rs:346-371):
+        x + W_out . gate(dw3x3(W_in . layer_norm(x))) for x [c, h, w], w_in [2 hidden, c(,1,1)],
+        w_dw [2 hidden(,1), 3, 3], w_out [c, hidden(,1,1)]."""
+        c, h, w = x.shape
+        hidden = w_in.shape[0] // 2
+        out = _like(x, (c, h, w)) if out is None else out
+        px, mem = _arg(x)
+        check(_lib.lib().zjai_transformer_ffn(
+            self.handle, px, c, h, w, hidden, _arg(norm_weight)[0], _arg(norm_bias)[0],
+            _arg(w_in)[0], _arg(w_dw)[0], _arg(w_out)[0], _arg(out, (c, h, w))[0], mem))
+        return out
+
 
 def synth_out_size(kind, op, h, w):
     oh, ow = ctypes.c_int(), ctypes.c_int()

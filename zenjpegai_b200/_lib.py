@@ -101,6 +101,7 @@ def lib():
     L.zjai_channel_attention.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i]
     L.zjai_depthwise3x3.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i]
     L.zjai_depthwise3x3_elu_gate.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i]
+    L.zjai_transformer_ffn.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i]
     _dp = ctypes.POINTER(ctypes.c_double)
     L.zjai_conv_bench.argtypes = [_vp] + [_i] * 11 + [_dp, _dp]
     L.zjai_kernel_bench.argtypes = [_vp] + [_i] * 6 + [_dp, _dp]

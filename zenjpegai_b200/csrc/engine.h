@@ -183,6 +183,24 @@ struct ConvOut {
 
 int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o);
 
+// Fused feed-forward half of a transformer block (ffn_tc.cu): W_in [2 hidden][dim] and
+// W_out [dim][hidden] packed into the kernel's 128-row / dim-row blocks, the depthwise weights
+// [2 hidden][9] regrouped per chunk, tap and channel pair.
+struct FfnLayer {
+  int dim = 0, hidden = 0;
+  __half* win = nullptr;
+  __half* wout = nullptr;
+  float* wdw = nullptr;
+  float scale_in = 1.f, scale_out = 1.f;
+};
+// The fused kernel's shapes: dim 64 or 128, hidden a multiple of 64.
+bool ffn_fusable(int dim, int hidden);
+int pack_ffn(Ctx* ctx, FfnLayer* L, const float* w_in, const float* w_dw, const float* w_out,
+             int dim, int hidden);
+void free_ffn(FfnLayer* L);
+// x += W_out . gate(dw3x3(W_in . ln)) in place on x (NHWC f16, dim channels), on ctx->stream.
+int run_ffn(Ctx* ctx, const FfnLayer& L, const TView& ln, const TView& x);
+
 // ---- elementwise / layout kernels (kernels_misc.cu) ---------------------------------------
 // planar f32 [n][c][h][w] window (y0, x0, h, w of a [c][H][W] source) -> NHWC f16 view
 void launch_planar_to_nhwc(const float* src, int c, int H, int W, int y0, int x0,

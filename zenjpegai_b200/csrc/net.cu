@@ -134,7 +134,16 @@ struct Loader {
     ZJAI_TRY(vec(p + ".ffn.norm1.bias", {dim}));
     ZJAI_TRY(conv(p + ".ffn.project_in", dim, 2 * hidden, 1, 1, 1, 0, 1, false));
     ZJAI_TRY(dw(p + ".ffn.dwconv", 2 * hidden));
-    return conv(p + ".ffn.project_out", hidden, dim, 1, 1, 1, 0, 1, false);
+    ZJAI_TRY(conv(p + ".ffn.project_out", hidden, dim, 1, 1, 1, 0, 1, false));
+    if (!ffn_fusable(dim, hidden)) return ZJAI_OK;
+    const float *wi, *wd, *wo2;
+    ZJAI_TRY(get(p + ".ffn.project_in.weight", {2 * hidden, dim, 1, 1}, &wi));
+    ZJAI_TRY(get(p + ".ffn.dwconv.weight", {2 * hidden, 1, 3, 3}, &wd));
+    ZJAI_TRY(get(p + ".ffn.project_out.weight", {dim, hidden, 1, 1}, &wo2));
+    FfnLayer F;
+    ZJAI_TRY(pack_ffn(net->ctx, &F, wi, wd, wo2, dim, hidden));
+    net->ffns[p] = F;
+    return ZJAI_OK;
   }
   int tam(const std::string& p, int dim, bool ds) {  // Tam::load (attention.rs:509-528)
     if (ds) {
@@ -248,6 +257,7 @@ int load_network(Ctx* ctx, int kind, int op, const zjai_param* params, int npara
 
 Net::~Net() {
   for (auto& kv : convs) free_conv(&kv.second);
+  for (auto& kv : ffns) free_ffn(&kv.second);
   for (auto& kv : vecs) cudaFree(kv.second);
 }
 
@@ -433,6 +443,18 @@ int Runner::tb(const std::string& p, const TView& x) {
   mem_kernel(p + ".ffn.norm1", "ln", 2 * b16 * d, 1, [&] {
     launch_layer_norm(x, ln, vec(p + ".ffn.norm1.weight"), vec(p + ".ffn.norm1.bias"), stream);
   });
+  auto fz = net->ffns.find(p);
+  if (fz != net->ffns.end()) {
+    // project_in, depthwise + gate and project_out in one kernel (ffn_tc.cu)
+    cudaStream_t saved = ctx->stream;
+    ctx->stream = stream;
+    if (ctx->profiling) ctx->tag = kind_tag() + p + ".ffn[fused]";
+    st = run_ffn(ctx, fz->second, ln, x);
+    ctx->stream = saved;
+    if (st == ZJAI_OK && count_flops)
+      flops += 2.0 * px * 3.0 * hidden * d;
+    return st;
+  }
   TView f, g;
   ZJAI_TRY(alloc(x.h, x.w, 2 * hidden, &f));
   ZJAI_TRY(alloc(x.h, x.w, hidden, &g));

@@ -17,6 +17,9 @@ struct Net {
   // f16 scale of the per-picture weights W_o . blockdiag(A) of each transformer block's folded
   // attention projection (keyed by the block prefix)
   std::map<std::string, float> fold_scale;
+  // fused FFN weights of each transformer block whose shape the fused kernel takes (keyed by
+  // the block prefix)
+  std::map<std::string, FfnLayer> ffns;
   ~Net();
 };
 

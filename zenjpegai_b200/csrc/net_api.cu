@@ -467,4 +467,46 @@ int zjai_depthwise3x3_elu_gate(zjai_ctx* ctx, const float* x, int c, int h, int 
   return depthwise_call(ctx, x, c, h, w, weight, out, mem, true);
 }
 
+// The feed-forward half of TransformerBlock::forward (attention.rs:346-371) on one picture:
+// out = x + W_out . gate(dw3x3(W_in . layer_norm(x))), the LN kernel then the fused FFN kernel.
+int zjai_transformer_ffn(zjai_ctx* ctx, const float* x, int c, int h, int w, int hidden,
+                         const float* norm_weight, const float* norm_bias, const float* w_in,
+                         const float* w_dw, const float* w_out, float* out, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!x || !norm_weight || !norm_bias || !w_in || !w_dw || !w_out || !out || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "transformer ffn: bad arguments");
+  if (!ffn_fusable(c, hidden))
+    return fail(ZJAI_UNSUPPORTED, "transformer ffn: channels must be 64 or 128 and the hidden "
+                                  "width a multiple of 64");
+  ArenaScope scope(ctx);
+  std::vector<float> bi, bd, bo;
+  const float *hi, *hd, *ho;
+  ZJAI_TRY(fetch_host(w_in, (size_t)2 * hidden * c, mem, &bi, &hi));
+  ZJAI_TRY(fetch_host(w_dw, (size_t)2 * hidden * 9, mem, &bd, &hd));
+  ZJAI_TRY(fetch_host(w_out, (size_t)c * hidden, mem, &bo, &ho));
+  FfnLayer F;
+  struct Guard {
+    FfnLayer* f;
+    ~Guard() {
+      cudaDeviceSynchronize();
+      free_ffn(f);
+    }
+  } guard{&F};
+  ZJAI_TRY(pack_ffn(ctx, &F, hi, hd, ho, c, hidden));
+  const float *dx, *dnw, *dnb;
+  ZJAI_TRY(stage_in(ctx, x, (size_t)c * h * w, mem, &dx));
+  ZJAI_TRY(stage_in(ctx, norm_weight, (size_t)c, mem, &dnw));
+  ZJAI_TRY(stage_in(ctx, norm_bias, (size_t)c, mem, &dnb));
+  TView t, ln;
+  ZJAI_TRY(planar_to_tensor(ctx, dx, c, h, w, &t));
+  ZJAI_TRY(alloc_tensor(ctx, 1, h, w, c, &ln));
+  launch_layer_norm(t, ln, dnw, dnb, ctx->stream);
+  ZJAI_TRY(run_ffn(ctx, F, ln, t));
+  float* dout;
+  ZJAI_TRY(stage_out_alloc(ctx, out, (size_t)c * h * w, mem, &dout));
+  launch_nhwc_to_planar(t, dout, ctx->stream);
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, (size_t)c * h * w, mem));
+  return finish_call(ctx, mem);
+}
+
 }  // extern "C"
