@@ -10,6 +10,7 @@ namespace {
 constexpr uint32_t kXChunkBytes = 256u * 128u;  // one 64-channel slab of the halo, 256 rows
 constexpr uint32_t kWinBytes = 128u * 128u;     // one W_in block [128][64]
 constexpr uint32_t kGBytes = 256u * 128u;       // gated block, 2 subtiles x 128 rows x 64 ch
+constexpr uint32_t kWdBytes = 9u * 32u * 16u;    // depthwise weights of a chunk, f32
 // f16 halo image: 128 channels (256 B) per pixel at a 264-byte pitch, so the drain's lanes
 // (consecutive pixels, one 8-byte channel-pair slot) and the depthwise lanes (one pixel, 32
 // consecutive slots) both hit distinct banks
@@ -21,8 +22,10 @@ constexpr uint32_t kBarBytes = 256u;  // mbarriers, TMEM address, abort word
 enum FfnBar : int {
   B_XF, B_XE,             // halo slabs full / free
   B_WIF, B_WIE = B_WIF + 2,  // W_in ring (2 slots)
-  B_WOF = B_WIE + 2, B_WOE = B_WOF + 2,  // W_out ring (2 slots)
-  B_INF = B_WOE + 2,      // project_in accumulators of a chunk complete
+  B_WOF = B_WIE + 2, B_WOE,  // W_out block (1 slot: reloaded while the next chunk's
+                             // depthwise runs)
+  B_WDF, B_WDE = B_WDF + 2,  // depthwise weights (2 slots)
+  B_INF = B_WDE + 2,      // project_in accumulators of a chunk complete
   B_INE,                  // ... drained (compute threads)
   B_HF,                   // f16 halo image written (compute threads)
   B_HE,                   // ... read by every compute thread
@@ -47,8 +50,8 @@ __device__ __forceinline__ uint32_t f2h(float a, float b) {
 
 size_t ffn_smem_bytes(int dim) {
   const size_t x = (size_t)(dim / 64) * kXChunkBytes;
-  const size_t wo = 2u * (size_t)dim * 128u;
-  return 1024 + x + 2u * kWinBytes + wo + kGBytes + kHBytes + kBarBytes;
+  const size_t wo = (size_t)dim * 128u;
+  return 1024 + x + 2u * kWinBytes + wo + kGBytes + kHBytes + 2u * kWdBytes + kBarBytes;
 }
 
 __global__ void __launch_bounds__(kFfnThreads, 1)
@@ -61,9 +64,10 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
   uint8_t* sX = smem;
   uint8_t* sWin = sX + kxn * kXChunkBytes;
   uint8_t* sWout = sWin + 2 * kWinBytes;
-  uint8_t* sG = sWout + 2 * wob;
+  uint8_t* sG = sWout + wob;
   uint8_t* sH = sG + kGBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sH + kHBytes);  // kBarBytes
+  uint8_t* sWd = sH + kHBytes;  // 2 slots of kWdBytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sWd + 2 * kWdBytes);  // kBarBytes
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_COUNT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
@@ -76,9 +80,11 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(B_WIF + i), 1);
       mbar_init(bar(B_WIE + i), 1);
-      mbar_init(bar(B_WOF + i), 1);
-      mbar_init(bar(B_WOE + i), 1);
+      mbar_init(bar(B_WDF + i), 1);
+      mbar_init(bar(B_WDE + i), kCT);
     }
+    mbar_init(bar(B_WOF), 1);
+    mbar_init(bar(B_WOE), 1);
     mbar_init(bar(B_INF), 1);
     mbar_init(bar(B_INE), kCT);
     mbar_init(bar(B_HF), kCT);
@@ -105,7 +111,7 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      long long xi = 0, wi = 0, wo = 0;  // loads issued per barrier set
+      long long xi = 0, wi = 0, wo = 0, wd = 0;  // loads issued per barrier set
       const uint32_t xbox = (uint32_t)kFfnHalo * 128u;
       for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
         const int tx = t % a.tiles_x, rest = t / a.tiles_x;
@@ -133,15 +139,23 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
             ++wi;
           }
           if (!ok) break;
-          const int s = (int)(wo & 1);
-          if (!mbar_wait_idle(bar(B_WOE + s), (uint32_t)((wo >> 1) & 1) ^ 1u, abort_flag, a.err,
+          const int s = (int)(wd & 1);
+          if (!mbar_wait_idle(bar(B_WDE + s), (uint32_t)((wd >> 1) & 1) ^ 1u, abort_flag, a.err,
                               DEV_TIMEOUT_EMPTY, 64)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(bar(B_WOF + s), wob);
-          bulk_load(smem_u32(sWout) + s * wob, a.wout + (size_t)c * a.dim * 64, wob,
-                    bar(B_WOF + s));
+          mbar_arrive_expect_tx(bar(B_WDF + s), kWdBytes);
+          bulk_load(smem_u32(sWd) + s * kWdBytes, a.wdw + (size_t)c * (kWdBytes / 4), kWdBytes,
+                    bar(B_WDF + s));
+          ++wd;
+          if (!mbar_wait_idle(bar(B_WOE), (uint32_t)(wo & 1) ^ 1u, abort_flag, a.err,
+                              DEV_TIMEOUT_EMPTY, 64)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar(B_WOF), wob);
+          bulk_load(smem_u32(sWout), a.wout + (size_t)c * a.dim * 64, wob, bar(B_WOF));
           ++wo;
         }
         if (!ok) break;
@@ -153,11 +167,12 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
           const long long last = ((wi - 1 - s) / 2) * 2 + s;
           mbar_wait_drain(bar(B_WIF + s), (uint32_t)((last >> 1) & 1), a.err);
         }
-        if (wo > s) {
-          const long long last = ((wo - 1 - s) / 2) * 2 + s;
-          mbar_wait_drain(bar(B_WOF + s), (uint32_t)((last >> 1) & 1), a.err);
+        if (wd > s) {
+          const long long last = ((wd - 1 - s) / 2) * 2 + s;
+          mbar_wait_drain(bar(B_WDF + s), (uint32_t)((last >> 1) & 1), a.err);
         }
       }
+      if (wo > 0) mbar_wait_drain(bar(B_WOF), (uint32_t)((wo - 1) & 1), a.err);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
@@ -179,8 +194,8 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
         for (int c = 0; c <= nchunk && ok; ++c) {
           const long long g = (long long)it * nchunk + c;  // global chunk index
           if (c < nchunk) {
-            if (!mbar_wait_idle(bar(B_INE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
-                                DEV_TIMEOUT_ACC_EMPTY, 32)) {
+            if (!mbar_wait_sleep(bar(B_INE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
+                                 DEV_TIMEOUT_ACC_EMPTY)) {
               ok = false;
               break;
             }
@@ -210,18 +225,17 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
             if (c == nchunk - 1) umma_commit(bar(B_XE));  // the halo slabs are free
           }
           if (c > 0) {
-            const int s = (int)(wo & 1);
-            if (!mbar_wait(bar(B_GF), (uint32_t)((g - 1) & 1), abort_flag, a.err,
+            if (!mbar_wait_sleep(bar(B_GF), (uint32_t)((g - 1) & 1), abort_flag, a.err,
+                                 DEV_TIMEOUT_FULL) ||
+                !mbar_wait(bar(B_WOF), (uint32_t)(wo & 1), abort_flag, a.err,
                            DEV_TIMEOUT_FULL) ||
-                !mbar_wait(bar(B_WOF + s), (uint32_t)((wo >> 1) & 1), abort_flag, a.err,
-                           DEV_TIMEOUT_FULL) ||
-                (c == 1 && !mbar_wait_idle(bar(B_OE), (uint32_t)(it & 1) ^ 1u, abort_flag, a.err,
-                                           DEV_TIMEOUT_ACC_EMPTY, 32))) {
+                (c == 1 && !mbar_wait_sleep(bar(B_OE), (uint32_t)(it & 1) ^ 1u, abort_flag, a.err,
+                                            DEV_TIMEOUT_ACC_EMPTY))) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint64_t db = dWo + (uint64_t)((s * wob) >> 4);
+            const uint64_t db = dWo;
 #pragma unroll
             for (int sub = 0; sub < 2; ++sub) {
               const uint64_t da = dG + (uint64_t)((sub * 16384u) >> 4);
@@ -230,7 +244,7 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
                 umma_f16(tmem + 256 + sub * a.dim, da + 2 * kk, db + 2 * kk, id_out,
                          (c > 1 || kk) ? 1u : 0u);
             }
-            umma_commit(bar(B_WOE + s));
+            umma_commit(bar(B_WOE));
             umma_commit(bar(B_GE));
             ++wo;
             if (c == nchunk) umma_commit(bar(B_OF));
@@ -250,9 +264,6 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
     const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
     // depthwise role: output columns 2 cp, 2 cp + 1, rows 6 rh .. 6 rh + 5, channel pair j
     const int cp = cw & 7, rh = cw >> 3, j = lane;
-    // depthwise weights of the thread's channels {elu 2j, 2j + 1, multipliers 2j, 2j + 1} per
-    // tap, [chunk][tap][pair] (one coalesced 16-byte load per tap)
-    const float4* wdw4 = reinterpret_cast<const float4*>(a.wdw) + j;
     bool ok = true;
     int it = 0;
     for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x, ++it) {
@@ -262,9 +273,9 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
         const long long g = (long long)it * nchunk + c;
         // ---- drain project_in: f16 halo image, pixel p at p * kHPitch, channel pair k in
         // the 8-byte slot k: {elu operands 2k, 2k + 1, multipliers 2k, 2k + 1}
-        if (!mbar_wait_idle(bar(B_INF), (uint32_t)(g & 1), abort_flag, a.err,
-                            DEV_TIMEOUT_ACC_FULL, 32) ||
-            !mbar_wait(bar(B_HE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
+        if (!mbar_wait_sleep(bar(B_INF), (uint32_t)(g & 1), abort_flag, a.err,
+                            DEV_TIMEOUT_ACC_FULL) ||
+            !mbar_wait_sleep(bar(B_HE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
                        DEV_TIMEOUT_ACC_FULL)) {
           ok = false;
           break;
@@ -276,15 +287,14 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
           uint32_t hv[2][8][2];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            float v[16];
-            tmem_ld16(trow + dsub * 128 + 32 * dh + 16 * hh, v);
+            float ve[16], vm[16];
+            tmem_ld16x2(trow + dsub * 128 + 32 * dh + 16 * hh,
+                        trow + dsub * 128 + 64 + 32 * dh + 16 * hh, ve, vm);
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              hv[hh][i][0] = f2h(v[2 * i] * a.scale_in + 0.f, v[2 * i + 1] * a.scale_in + 0.f);
-            tmem_ld16(trow + dsub * 128 + 64 + 32 * dh + 16 * hh, v);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              hv[hh][i][1] = f2h(v[2 * i] * a.scale_in + 0.f, v[2 * i + 1] * a.scale_in + 0.f);
+            for (int i = 0; i < 8; ++i) {
+              hv[hh][i][0] = f2h(ve[2 * i] * a.scale_in + 0.f, ve[2 * i + 1] * a.scale_in + 0.f);
+              hv[hh][i][1] = f2h(vm[2 * i] * a.scale_in + 0.f, vm[2 * i + 1] * a.scale_in + 0.f);
+            }
           }
           tc_fence_before();
           mbar_arrive(bar(B_INE));
@@ -297,14 +307,21 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
           }
         }
         mbar_arrive(bar(B_HF));
-        float4 wr[9];
-#pragma unroll
-        for (int tp = 0; tp < 9; ++tp) wr[tp] = __ldg(wdw4 + (c * 9 + tp) * 32);
-        if (!mbar_wait(bar(B_HF), (uint32_t)(g & 1), abort_flag, a.err, DEV_TIMEOUT_ACC_FULL) ||
-            !mbar_wait(bar(B_GE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
+        if (!mbar_wait_sleep(bar(B_HF), (uint32_t)(g & 1), abort_flag, a.err, DEV_TIMEOUT_ACC_FULL) ||
+            !mbar_wait_sleep(bar(B_WDF + (int)(g & 1)), (uint32_t)((g >> 1) & 1), abort_flag, a.err,
+                             DEV_TIMEOUT_FULL) ||
+            !mbar_wait_sleep(bar(B_GE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
                        DEV_TIMEOUT_ACC_FULL)) {
           ok = false;
           break;
+        }
+        // depthwise weights of the thread's channels {elu 2j, 2j + 1, multipliers 2j, 2j + 1}
+        // per tap ([tap][pair] in the chunk's slot)
+        float4 wr[9];
+        {
+          const float4* ws = reinterpret_cast<const float4*>(sWd + (g & 1) * kWdBytes) + j;
+#pragma unroll
+          for (int tp = 0; tp < 9; ++tp) wr[tp] = ws[tp * 32];
         }
         // ---- depthwise 3x3 + gate over halo rows 6 rh .. 6 rh + 7 (rolling 3-row
         // accumulators; per output the taps in (ky, kx) order, the first one a product)
@@ -354,8 +371,7 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
               }
             }
           };
-          // not unrolled: a fully unrolled band hoists all 32 halo loads and spills
-#pragma unroll 1
+#pragma unroll
           for (int i = 0; i < 8; i += 3) {
             row(std::integral_constant<int, 0>{}, i);
             row(std::integral_constant<int, 1>{}, i + 1);
@@ -365,11 +381,11 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
         fence_proxy_async_smem();  // the gated block is read by the tensor cores
         mbar_arrive(bar(B_GF));
         mbar_arrive(bar(B_HE));
+        mbar_arrive(bar(B_WDE + (int)(g & 1)));
       }
       if (!ok) break;
       // ---- output: x += W_out . gate(..) for the tile's 192 pixels
-      if (!mbar_wait_idle(bar(B_OF), (uint32_t)(it & 1), abort_flag, a.err, DEV_TIMEOUT_ACC_FULL,
-                          32)) {
+      if (!mbar_wait_sleep(bar(B_OF), (uint32_t)(it & 1), abort_flag, a.err, DEV_TIMEOUT_ACC_FULL)) {
         ok = false;
         break;
       }

@@ -55,6 +55,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not yet complete sleeps in the
+// barrier unit until the phase completes or about `ns` nanoseconds pass, instead of returning
+// at once and spinning (no issue slots taken from the warps that have work).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait limits are counted in SM clock cycles (clock64 is a cheap register read, unlike the
 // global timer): 4e9 cycles is about 2 s at the B200's 1.965 GHz boost clock and longer at
 // lower clocks.
@@ -108,6 +123,23 @@ __device__ __forceinline__ bool mbar_wait_idle(uint32_t bar, uint32_t parity, vo
       return false;
     }
     if (it > 4) __nanosleep(ns);
+  }
+}
+
+// mbar_wait whose polls sleep in the barrier unit (up to 20 us each) while the phase is
+// incomplete: for many threads waiting on one barrier at once.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity,
+                                                volatile int* abort, int* err, int code) {
+  if (mbar_test(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(err, 0, code);
+      *abort = 1;
+      return false;
+    }
   }
 }
 
@@ -268,6 +300,30 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Two 16-column loads (columns at taddr0 and taddr1) under one wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t taddr0, uint32_t taddr1, float (&v0)[16],
+                                            float (&v1)[16]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%33];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr0), "r"(taddr1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    v0[i] = __uint_as_float(r[i]);
+    v1[i] = __uint_as_float(r[16 + i]);
+  }
 }
 
 // Shared-memory matrix descriptor (tcgen05 format): K-major operand whose rows are
