@@ -274,9 +274,7 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
         // ---- drain project_in: f16 halo image, pixel p at p * kHPitch, channel pair k in
         // the 8-byte slot k: {elu operands 2k, 2k + 1, multipliers 2k, 2k + 1}
         if (!mbar_wait_sleep(bar(B_INF), (uint32_t)(g & 1), abort_flag, a.err,
-                            DEV_TIMEOUT_ACC_FULL) ||
-            !mbar_wait_sleep(bar(B_HE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
-                       DEV_TIMEOUT_ACC_FULL)) {
+                             DEV_TIMEOUT_ACC_FULL)) {
           ok = false;
           break;
         }
@@ -298,6 +296,13 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
           }
           tc_fence_before();
           mbar_arrive(bar(B_INE));
+          // the accumulators are in registers; the halo image is free once every thread has
+          // finished the previous chunk's depthwise
+          if (!mbar_wait_sleep(bar(B_HE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
+                               DEV_TIMEOUT_ACC_FULL)) {
+            ok = false;
+            break;
+          }
           if (p < kFfnHalo) {
             uint2* hp = reinterpret_cast<uint2*>(sH + p * kHPitch) + 16 * dh;
 #pragma unroll
