@@ -13,9 +13,9 @@ NCCL (the "final gather"). One step = one picture. `--config sop1080` runs confi
 value: output Mpixel/s of the whole job, timed on the device (CUDA events bracketing each
 step on the engine's stream, L2 flushed between steps, max over ranks). e2e: the same through
 the public API with the latents copied from pinned host memory and the 8-bit picture read
-back, every step. roofline: the tcgen05 convolution kernel (all its launches of one step),
-algorithmic FLOPs (live MACs x 2) / summed CUDA-event duration, against the measured bf16
-dense peak. cpu_baseline / --impl reference: the CPU oracle (a C restatement of the crate's
+back, every step. roofline: the tcgen05 kernels (the implicit-GEMM convolution and the fused
+FFN, all their launches of one step), algorithmic FLOPs (live MACs x 2) / summed CUDA-event
+duration, against the measured bf16 dense peak. cpu_baseline / --impl reference: the CPU oracle (a C restatement of the crate's
 f32 path) on a bounded sample of the same workload, all host threads.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -53,9 +53,10 @@ def peaks():
 
 
 def conv_traffic(config):
-    """DRAM bytes (read + write) of one step's conv_tc_kernel launches, from the committed ncu
-    capture summary profiles/conv_tc_<config>_step_dram.txt (`dram_bytes_per_step: N`), or None."""
-    path = os.path.join(ROOT, "profiles", "conv_tc_%s_step_dram.txt" % config)
+    """DRAM bytes (read + write) of one step's tcgen05 kernel launches (conv_tc_kernel and
+    ffn_tc_kernel), from the committed ncu capture summary
+    profiles/tcgen05_<config>_step_dram.txt (`dram_bytes_per_step: N`), or None."""
+    path = os.path.join(ROOT, "profiles", "tcgen05_%s_step_dram.txt" % config)
     try:
         with open(path) as f:
             for ln in f:
@@ -330,7 +331,7 @@ def main():
     clk = clocks.stop()
     eng.sync()
     e2e_ms = timed(args.steps, from_host=True)
-    # live roofline of the tcgen05 convolution kernel over one profiled step
+    # live roofline of the tcgen05 kernels over one profiled step
     eng_h = eng.handle
     _lib.lib().zjai_ctx_profile(eng_h, 1)
     flush.zero_()
@@ -396,7 +397,8 @@ def main():
             },
             "roofline": {
                 "bound": "tensor",
-                "kernel": "conv_tc_kernel (tcgen05 implicit-GEMM conv, all launches of a step)",
+                "kernel": "conv_tc_kernel + ffn_tc_kernel (tcgen05 implicit-GEMM conv and fused "
+                          "FFN, all launches of a step)",
                 "achieved": achieved,
                 "peak": peak,
                 "unit": "TFLOP/s",
@@ -404,7 +406,7 @@ def main():
                 "peak_source": peak_src,
                 "launches_per_step": conv_n,
                 "flops_per_step": conv_fl,
-                # bytes per step (all conv launches of the step, like `achieved`), from the
+                # bytes per step (all tcgen05 launches of the step, like `achieved`), from the
                 # committed single-pass ncu capture of this workload
                 "traffic": conv_traffic(args.config),
                 "traffic_unit": "bytes per step (DRAM read + write, ncu)",

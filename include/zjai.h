@@ -268,14 +268,16 @@ int zjai_conv_bench(zjai_ctx *ctx, int n, int h, int w, int cin, int cout, int k
                     int groups, int transposed, int residual, int reps, double *ms,
                     double *flops);
 
-/* Kernels of the HOP transformer blocks timed alone (the same harness for the memory-bound
- * steps of attention.rs:328-372): `kind` is ZJAI_KB_DW (depthwise 3x3 over c channels),
+/* Kernels of the HOP transformer blocks timed alone (the same harness for the steps of
+ * attention.rs:328-372): `kind` is ZJAI_KB_DW (depthwise 3x3 over c channels),
  * ZJAI_KB_DW_GATE (depthwise 3x3 over c channels fused with the FFN's ELU gate, c/2 out),
- * ZJAI_KB_LN (layer norm over c channels) or ZJAI_KB_ATTN (channel attention on a 3c-channel
- * qkv map, 4 heads). Runs `reps` times on n pseudo-random NHWC f16 maps of h x w in the
- * context arena; returns the mean device time per run in *ms and the algorithmic bytes per
- * run (each input element read once, each output element written once) in *bytes. */
-enum { ZJAI_KB_DW = 0, ZJAI_KB_DW_GATE = 1, ZJAI_KB_LN = 2, ZJAI_KB_ATTN = 3 };
+ * ZJAI_KB_LN (layer norm over c channels), ZJAI_KB_ATTN (channel attention on a 3c-channel
+ * qkv map, 4 heads) or ZJAI_KB_FFN (the fused FFN kernel, x += W_out . gate(dw3x3(W_in . ln))
+ * with dim c (64 or 128) and hidden 4c, random weights). Runs `reps` times on n pseudo-random
+ * NHWC f16 maps of h x w in the context arena; returns the mean device time per run in *ms
+ * and the algorithmic bytes per run (each input element read once, each output element
+ * written once) in *bytes. */
+enum { ZJAI_KB_DW = 0, ZJAI_KB_DW_GATE = 1, ZJAI_KB_LN = 2, ZJAI_KB_ATTN = 3, ZJAI_KB_FFN = 4 };
 int zjai_kernel_bench(zjai_ctx *ctx, int kind, int n, int h, int w, int c, int reps, double *ms,
                       double *bytes);
 

@@ -1,5 +1,6 @@
 """Layer-level timing of the tcgen05 convolution kernel (`zjai_conv_bench`) and of the
-memory-bound kernels of the HOP transformer blocks (`zjai_kernel_bench`).
+other kernels of the HOP transformer blocks (`zjai_kernel_bench`: the memory-bound ones and
+the fused tcgen05 FFN).
 
 The GPU counterpart of the crate's conv microbenchmark (benches/conv_kernels.rs:165-187): the
 BOP luma layer shapes at the latent size 131x88, plus the HOP shapes of a 4K picture's 28
@@ -37,7 +38,7 @@ LAYERS = [
     ("hop_conv4_t_128_1_planar@H2x28", 28, 256, 256, 128, 1, 3, 1, 1, 1, 2),
 ]
 
-KB_DW, KB_DW_GATE, KB_LN, KB_ATTN = 0, 1, 2, 3
+KB_DW, KB_DW_GATE, KB_LN, KB_ATTN, KB_FFN = 0, 1, 2, 3, 4
 # name, kind, n, h, w, c (HOP luma transformer blocks at 1/4 scale: dim 128, hidden 512)
 KERNELS = [
     ("hop_ffn_dwgate_1024@H4x28", KB_DW_GATE, 28, 128, 128, 1024),
@@ -45,6 +46,9 @@ KERNELS = [
     ("hop_ln_128@H4x28", KB_LN, 28, 128, 128, 128),
     ("hop_attn_128@H4x28", KB_ATTN, 28, 128, 128, 128),
     ("hop_uv_attn_64@H4x28", KB_ATTN, 28, 128, 128, 64),
+    # fused FFN (project_in + depthwise + ELU gate + project_out + residual), tcgen05
+    ("hop_ffn_fused_128@H4x28", KB_FFN, 28, 128, 128, 128),
+    ("hop_uv_ffn_fused_64@H4x28", KB_FFN, 28, 128, 128, 64),
 ]
 
 
@@ -84,6 +88,13 @@ def main():
         _lib.check(L.zjai_kernel_bench(eng.handle, *row[1:], args.reps, ctypes.byref(ms),
                                        ctypes.byref(by)))
         gbs = by.value / (ms.value * 1e-3) / 1e9
+        if row[1] == KB_FFN:
+            # algorithmic FLOPs of project_in + project_out (dim c, hidden 4c)
+            n, h, w, c = row[2:]
+            tf = 2.0 * n * h * w * 3 * 4 * c * c / (ms.value * 1e-3) / 1e12
+            print("%-32s %8.3f ms %8.1f TFLOP/s %6.1f%% of %.0f (%s)" % (
+                name, ms.value, tf, 100 * tf / pk, pk, src), flush=True)
+            continue
         print("%-32s %8.3f ms %8.0f GB/s    %6.1f%% of %.0f (%s)" % (
             name, ms.value, gbs, 100 * gbs / hbm, hbm, src), flush=True)
     eng.close()

@@ -97,11 +97,11 @@ extern "C" int zjai_conv_bench(zjai_ctx* ctx, int n, int h, int w, int cin, int 
 extern "C" int zjai_kernel_bench(zjai_ctx* ctx, int kind, int n, int h, int w, int c, int reps,
                                  double* ms, double* bytes) {
   ZJAI_TRY(ctx_enter(ctx));
-  if (kind < ZJAI_KB_DW || kind > ZJAI_KB_ATTN || n <= 0 || h <= 0 || w <= 0 || c <= 0 ||
+  if (kind < ZJAI_KB_DW || kind > ZJAI_KB_FFN || n <= 0 || h <= 0 || w <= 0 || c <= 0 ||
       c % 8 || reps <= 0 || !ms)
     return fail(ZJAI_INVALID_ARGUMENT, "kernel_bench: bad arguments");
   if ((kind == ZJAI_KB_DW_GATE && c % 16) || (kind == ZJAI_KB_LN && c > 512) ||
-      (kind == ZJAI_KB_ATTN && c % 4))
+      (kind == ZJAI_KB_ATTN && c % 4) || (kind == ZJAI_KB_FFN && !ffn_fusable(c, 4 * c)))
     return fail(ZJAI_UNSUPPORTED, "kernel_bench: channel count not supported by this kernel");
   ArenaScope scope(ctx);
   const int cin = kind == ZJAI_KB_ATTN ? 3 * c : c;
@@ -126,8 +126,30 @@ extern "C" int zjai_kernel_bench(zjai_ctx* ctx, int kind, int n, int h, int w, i
   const float* wt = dp;
   const float* gamma = dp + (size_t)c * 9;
   const float* temp = gamma + 2 * c;
+  // fused FFN: random W_in [8c][c], depthwise [8c][9], W_out [c][4c] (x = ln, y = residual)
+  FfnLayer F;
+  struct Guard {
+    FfnLayer* f;
+    ~Guard() {
+      cudaDeviceSynchronize();
+      free_ffn(f);
+    }
+  } guard{&F};
+  if (kind == ZJAI_KB_FFN) {
+    const int hidden = 4 * c;
+    std::vector<float> wi((size_t)2 * hidden * c), wd((size_t)2 * hidden * 9),
+        wo((size_t)c * hidden);
+    std::uniform_real_distribution<float> wdist(-0.1f, 0.1f);
+    for (auto& v : wi) v = wdist(rng);
+    for (auto& v : wd) v = ud(rng);
+    for (auto& v : wo) v = wdist(rng);
+    ZJAI_TRY(pack_ffn(ctx, &F, wi.data(), wd.data(), wo.data(), c, hidden));
+    fill_kernel<<<1024, 256, 0, ctx->stream>>>(y.p, (long long)n * y.img, 23u);
+  }
+  int st = ZJAI_OK;
   auto run = [&] {
     switch (kind) {
+      case ZJAI_KB_FFN: st = run_ffn(ctx, F, x, y); break;
       case ZJAI_KB_DW: launch_dw3x3(ctx, x, y, wt, false, ctx->stream); break;
       case ZJAI_KB_DW_GATE: launch_dw3x3(ctx, x, y, wt, true, ctx->stream); break;
       case ZJAI_KB_LN: launch_layer_norm(x, y, gamma, gamma + c, ctx->stream); break;
@@ -135,6 +157,7 @@ extern "C" int zjai_kernel_bench(zjai_ctx* ctx, int kind, int n, int h, int w, i
     }
   };
   run();  // warm-up
+  ZJAI_TRY(st);
   cudaEvent_t e0, e1;
   ZJAI_TRY(cuda_check(cudaEventCreate(&e0), "event"));
   ZJAI_TRY(cuda_check(cudaEventCreate(&e1), "event"));
@@ -150,6 +173,10 @@ extern "C" int zjai_kernel_bench(zjai_ctx* ctx, int kind, int n, int h, int w, i
   *ms = (double)t / reps;
   // attention reads q, k (Gram) and v (apply) and writes the output
   const double px = (double)n * h * w;
-  if (bytes) *bytes = 2.0 * px * (kind == ZJAI_KB_ATTN ? 4.0 * c : (double)(cin + cout));
+  // the fused FFN reads ln and the residual and writes x
+  if (bytes)
+    *bytes = 2.0 * px * (kind == ZJAI_KB_ATTN ? 4.0 * c
+                         : kind == ZJAI_KB_FFN ? 3.0 * c
+                                               : (double)(cin + cout));
   return ctx_check_status(ctx);
 }
