@@ -8,33 +8,36 @@ namespace zjai {
 namespace {
 
 constexpr uint32_t kXChunkBytes = 256u * 128u;  // one 64-channel slab of the halo, 256 rows
-constexpr uint32_t kWinBytes = 128u * 128u;     // one W_in block [128][64]
-constexpr uint32_t kGBytes = 256u * 128u;       // gated block, 2 subtiles x 128 rows x 64 ch
-constexpr uint32_t kWdBytes = 9u * 32u * 16u;    // depthwise weights of a chunk, f32
-// f16 halo image: 128 channels (256 B) per pixel at a 264-byte pitch, so the drain's lanes
-// (consecutive pixels, one 8-byte channel-pair slot) and the depthwise lanes (one pixel, 32
-// consecutive slots) both hit distinct banks
-constexpr uint32_t kHPitch = 264u;
+constexpr uint32_t kWinBytes = 64u * 128u;      // one W_in block [64][64] (a slice, K 64)
+constexpr int kWinSlots = 4;
+constexpr int kWoSlots = 2;                      // W_out blocks [dim][32]
+constexpr uint32_t kGBytes = 256u * 64u;        // gated block of a slice: 2 x 128 rows x 32 ch
+// f16 halo image of a slice: 64 channels (128 B) per pixel at a 136-byte pitch, so the
+// drain's lanes (consecutive pixels, one 8-byte channel-pair slot) and the depthwise lanes
+// (16 slots of one pixel per half-warp) both hit distinct banks
+constexpr uint32_t kHPitch = 136u;
 constexpr uint32_t kHBytes = (((uint32_t)kFfnHalo * kHPitch) + 127u) & ~127u;
-
-constexpr uint32_t kBarBytes = 256u;  // mbarriers, TMEM address, abort word
+constexpr uint32_t kWdBytes = 9u * 16u * 16u;   // depthwise weights of a slice, f32
+constexpr int kWdSlots = 4;
+constexpr uint32_t kBarBytes = 512u;  // mbarriers, TMEM address, abort word
+constexpr uint32_t kGroupThreads = 32u * kFfnGroupWarps;
 
 enum FfnBar : int {
-  B_XF, B_XE,             // halo slabs full / free
-  B_WIF, B_WIE = B_WIF + 2,  // W_in ring (2 slots)
-  B_WOF = B_WIE + 2, B_WOE,  // W_out block (1 slot: reloaded while the next chunk's
-                             // depthwise runs)
-  B_WDF, B_WDE = B_WDF + 2,  // depthwise weights (2 slots)
-  B_INF = B_WDE + 2,      // project_in accumulators of a chunk complete
-  B_INE,                  // ... drained (compute threads)
-  B_HF,                   // f16 halo image written (compute threads)
-  B_HE,                   // ... read by every compute thread
-  B_GF,                   // gated block written (compute threads)
-  B_GE,                   // ... consumed by project_out
-  B_OF,                   // project_out accumulators of a tile complete
-  B_OE,                   // ... drained (compute threads)
-  B_DRAIN,
-  B_COUNT
+  B_XF, B_XE,                                  // halo slabs full / free
+  B_WIF, B_WIE = B_WIF + kWinSlots,            // W_in ring
+  B_WOF = B_WIE + kWinSlots, B_WOE = B_WOF + kWoSlots,  // W_out ring
+  B_WDF = B_WOE + kWoSlots, B_WDE = B_WDF + kWdSlots,  // depthwise weights ring
+  // per warp group g (slices of parity g), two of each:
+  B_INF = B_WDE + kWdSlots,  // project_in accumulator of the group's slice complete
+  B_INE = B_INF + 2,         // ... drained (group threads)
+  B_HF = B_INE + 2,          // halo image written (group threads)
+  B_HE = B_HF + 2,           // ... read by every group thread
+  B_GF = B_HE + 2,           // gated block written (group threads)
+  B_GE = B_GF + 2,           // ... consumed by project_out
+  B_OF = B_GE + 2,           // project_out accumulators of a tile complete
+  B_OE,                      // ... drained (all compute threads)
+  B_DRAIN,                   // the two issuers' end-of-kernel drains
+  B_COUNT = B_DRAIN + 2
 };
 static_assert(B_COUNT * 8 + 8 <= (int)kBarBytes, "FFN barrier area");
 
@@ -50,8 +53,9 @@ __device__ __forceinline__ uint32_t f2h(float a, float b) {
 
 size_t ffn_smem_bytes(int dim) {
   const size_t x = (size_t)(dim / 64) * kXChunkBytes;
-  const size_t wo = (size_t)dim * 128u;
-  return 1024 + x + 2u * kWinBytes + wo + kGBytes + kHBytes + 2u * kWdBytes + kBarBytes;
+  const size_t wo = (size_t)kWoSlots * dim * 64u;
+  return 1024 + x + kWinSlots * kWinBytes + wo + 2u * kGBytes + 2u * kHBytes +
+         kWdSlots * kWdBytes + kBarBytes;
 }
 
 __global__ void __launch_bounds__(kFfnThreads, 1)
@@ -59,41 +63,46 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int kxn = a.dim >> 6;  // 64-channel slabs of ln (K blocks of project_in)
-  const uint32_t wob = (uint32_t)a.dim * 128u;  // one W_out block [dim][64]
+  const int kxn = a.dim >> 6;                   // 64-channel slabs of ln (K blocks of project_in)
+  const uint32_t wob = (uint32_t)a.dim * 64u;  // one W_out block [dim][32]
   uint8_t* sX = smem;
   uint8_t* sWin = sX + kxn * kXChunkBytes;
-  uint8_t* sWout = sWin + 2 * kWinBytes;
-  uint8_t* sG = sWout + wob;
-  uint8_t* sH = sG + kGBytes;
-  uint8_t* sWd = sH + kHBytes;  // 2 slots of kWdBytes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sWd + 2 * kWdBytes);  // kBarBytes
+  uint8_t* sWout = sWin + kWinSlots * kWinBytes;
+  uint8_t* sG = sWout + kWoSlots * wob;  // 2 (per group)
+  uint8_t* sH = sG + 2 * kGBytes;        // 2 (per group)
+  uint8_t* sWd = sH + 2 * kHBytes;       // kWdSlots
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sWd + kWdSlots * kWdBytes);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_COUNT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr uint32_t kCT = 32u * kFfnComputeWarps;  // compute threads (per-thread arrivals)
   if (threadIdx.x == 0) {
     mbar_init(bar(B_XF), 1);
     mbar_init(bar(B_XE), 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kWinSlots; ++i) {
       mbar_init(bar(B_WIF + i), 1);
       mbar_init(bar(B_WIE + i), 1);
-      mbar_init(bar(B_WDF + i), 1);
-      mbar_init(bar(B_WDE + i), kCT);
     }
-    mbar_init(bar(B_WOF), 1);
-    mbar_init(bar(B_WOE), 1);
-    mbar_init(bar(B_INF), 1);
-    mbar_init(bar(B_INE), kCT);
-    mbar_init(bar(B_HF), kCT);
-    mbar_init(bar(B_HE), kCT);
-    mbar_init(bar(B_GF), kCT);
-    mbar_init(bar(B_GE), 1);
+    for (int i = 0; i < kWoSlots; ++i) {
+      mbar_init(bar(B_WOF + i), 1);
+      mbar_init(bar(B_WOE + i), 1);
+    }
+    for (int i = 0; i < kWdSlots; ++i) {
+      mbar_init(bar(B_WDF + i), 1);
+      mbar_init(bar(B_WDE + i), kGroupThreads);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(bar(B_INF + g), 1);
+      mbar_init(bar(B_INE + g), kGroupThreads);
+      mbar_init(bar(B_HF + g), kGroupThreads);
+      mbar_init(bar(B_HE + g), kGroupThreads);
+      mbar_init(bar(B_GF + g), kGroupThreads);
+      mbar_init(bar(B_GE + g), 1);
+      mbar_init(bar(B_DRAIN + g), 1);
+    }
     mbar_init(bar(B_OF), 1);
-    mbar_init(bar(B_OE), kCT);
-    mbar_init(bar(B_DRAIN), 1);
+    mbar_init(bar(B_OE), 2 * kGroupThreads);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -106,14 +115,18 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int nchunk = a.nchunk;
+  const int S = a.nslice;  // slices per tile (even)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
+    // Per tile the halo slabs, then per slice its W_in blocks and depthwise weights (the
+    // project_out warp loads its own W_out blocks); the rings are deep enough that a wait here
+    // does not hold back the next slice's project_in.
     if (lane == 0) {
-      long long xi = 0, wi = 0, wo = 0, wd = 0;  // loads issued per barrier set
+      long long xi = 0, wi = 0, wd = 0;  // loads issued per ring
       const uint32_t xbox = (uint32_t)kFfnHalo * 128u;
-      for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
+      bool ok = true;
+      for (int t = blockIdx.x; t < a.num_tiles && ok && !*abort_flag; t += gridDim.x) {
         const int tx = t % a.tiles_x, rest = t / a.tiles_x;
         const int ty = rest % a.tiles_y, n = rest / a.tiles_y;
         if (!mbar_wait_idle(bar(B_XE), (uint32_t)(xi & 1) ^ 1u, abort_flag, a.err,
@@ -124,230 +137,262 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
           tma_load_4d(smem_u32(sX) + kx * kXChunkBytes, &tmX, bar(B_XF), 64 * kx,
                       tx * kFfnTW - 1, ty * kFfnTH - 1, n);
         ++xi;
-        bool ok = true;
-        for (int c = 0; c < nchunk && ok; ++c) {
-          for (int kx = 0; kx < kxn; ++kx) {
-            const int s = (int)(wi & 1);
-            if (!mbar_wait_idle(bar(B_WIE + s), (uint32_t)((wi >> 1) & 1) ^ 1u, abort_flag, a.err,
-                                DEV_TIMEOUT_EMPTY, 64)) {
-              ok = false;
-              break;
-            }
+        for (int c = 0; c < S && ok; ++c) {
+          for (int kx = 0; kx < kxn && ok; ++kx) {
+            const int s = (int)(wi % kWinSlots);
+            ok = mbar_wait_idle(bar(B_WIE + s), (uint32_t)((wi / kWinSlots) & 1) ^ 1u,
+                                abort_flag, a.err, DEV_TIMEOUT_EMPTY, 64);
+            if (!ok) break;
             mbar_arrive_expect_tx(bar(B_WIF + s), kWinBytes);
-            bulk_load(smem_u32(sWin) + s * kWinBytes, a.win + (size_t)(c * kxn + kx) * 8192,
+            bulk_load(smem_u32(sWin) + s * kWinBytes, a.win + (size_t)(c * kxn + kx) * 4096,
                       kWinBytes, bar(B_WIF + s));
             ++wi;
           }
           if (!ok) break;
-          const int s = (int)(wd & 1);
-          if (!mbar_wait_idle(bar(B_WDE + s), (uint32_t)((wd >> 1) & 1) ^ 1u, abort_flag, a.err,
-                              DEV_TIMEOUT_EMPTY, 64)) {
-            ok = false;
-            break;
+          {
+            const int s = (int)(wd % kWdSlots);
+            ok = mbar_wait_idle(bar(B_WDE + s), (uint32_t)((wd / kWdSlots) & 1) ^ 1u,
+                                abort_flag, a.err, DEV_TIMEOUT_EMPTY, 64);
+            if (!ok) break;
+            mbar_arrive_expect_tx(bar(B_WDF + s), kWdBytes);
+            bulk_load(smem_u32(sWd) + s * kWdBytes, a.wdw + (size_t)c * (kWdBytes / 4),
+                      kWdBytes, bar(B_WDF + s));
+            ++wd;
           }
-          mbar_arrive_expect_tx(bar(B_WDF + s), kWdBytes);
-          bulk_load(smem_u32(sWd) + s * kWdBytes, a.wdw + (size_t)c * (kWdBytes / 4), kWdBytes,
-                    bar(B_WDF + s));
-          ++wd;
-          if (!mbar_wait_idle(bar(B_WOE), (uint32_t)(wo & 1) ^ 1u, abort_flag, a.err,
-                              DEV_TIMEOUT_EMPTY, 64)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(bar(B_WOF), wob);
-          bulk_load(smem_u32(sWout), a.wout + (size_t)c * a.dim * 64, wob, bar(B_WOF));
-          ++wo;
         }
-        if (!ok) break;
       }
       // every copy issued lands before the CTA's shared memory goes away
       if (xi > 0) mbar_wait_drain(bar(B_XF), (uint32_t)((xi - 1) & 1), a.err);
-      for (int s = 0; s < 2; ++s) {
-        if (wi > s) {
-          const long long last = ((wi - 1 - s) / 2) * 2 + s;
-          mbar_wait_drain(bar(B_WIF + s), (uint32_t)((last >> 1) & 1), a.err);
-        }
-        if (wd > s) {
-          const long long last = ((wd - 1 - s) / 2) * 2 + s;
-          mbar_wait_drain(bar(B_WDF + s), (uint32_t)((last >> 1) & 1), a.err);
-        }
-      }
-      if (wo > 0) mbar_wait_drain(bar(B_WOF), (uint32_t)((wo - 1) & 1), a.err);
+      auto drain_ring = [&](int base, int slots, long long issued) {
+        for (int s = 0; s < slots; ++s)
+          if (issued > s) {
+            const long long last = ((issued - 1 - s) / slots) * slots + s;
+            mbar_wait_drain(bar(base + s), (uint32_t)((last / slots) & 1), a.err);
+          }
+      };
+      drain_ring(B_WIF, kWinSlots, wi);
+      drain_ring(B_WDF, kWdSlots, wd);
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    // Per tile: in(0), then for c = 1 .. nchunk: in(c) (c < nchunk) and out(c - 1). in(c) is
-    // 2 subtiles x dim / 16 UMMAs (M 128, N 128) into TMEM columns [0, 256); out(c) 2 x 4
-    // UMMAs (N = dim) into columns [256, 256 + 2 dim).
+    // ---------------------------------------------------------------- project_in issuer
+    // Slice c (global index gc) goes into TMEM columns [128 g, 128 g + 128) of its group
+    // g = c & 1 (two subtiles of N = 64: 32 ELU operands, 32 multipliers), once that group has
+    // drained its previous slice.
     if (lane == 0) {
-      const uint32_t id_in = idesc_f16(128u), id_out = idesc_f16((uint32_t)a.dim);
+      const uint32_t id_in = idesc_f16(64u);
       const uint64_t dX = smem_desc(smem_u32(sX), 128u);
       const uint64_t dWi = smem_desc(smem_u32(sWin), 128u);
-      const uint64_t dWo = smem_desc(smem_u32(sWout), 128u);
-      const uint64_t dG = smem_desc(smem_u32(sG), 128u);
-      long long wi = 0, wo = 0;
+      long long wi = 0;
       bool ok = true;
       int it = 0;
       for (int t = blockIdx.x; t < a.num_tiles && ok && !*abort_flag; t += gridDim.x, ++it) {
         if (!mbar_wait(bar(B_XF), (uint32_t)(it & 1), abort_flag, a.err, DEV_TIMEOUT_FULL)) break;
         tc_fence_after();
-        for (int c = 0; c <= nchunk && ok; ++c) {
-          const long long g = (long long)it * nchunk + c;  // global chunk index
-          if (c < nchunk) {
-            if (!mbar_wait_sleep(bar(B_INE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
-                                 DEV_TIMEOUT_ACC_EMPTY)) {
+        for (int c = 0; c < S && ok; ++c) {
+          const long long gc = (long long)it * S + c;
+          const int g = c & 1;
+          if (!mbar_wait_sleep(bar(B_INE + g), (uint32_t)((gc >> 1) & 1) ^ 1u, abort_flag, a.err,
+                               DEV_TIMEOUT_ACC_EMPTY)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int kx = 0; kx < kxn; ++kx) {
+            const int s = (int)(wi % kWinSlots);
+            if (!mbar_wait(bar(B_WIF + s), (uint32_t)((wi / kWinSlots) & 1), abort_flag, a.err,
+                           DEV_TIMEOUT_FULL)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            for (int kx = 0; kx < kxn; ++kx) {
-              const int s = (int)(wi & 1);
-              if (!mbar_wait(bar(B_WIF + s), (uint32_t)((wi >> 1) & 1), abort_flag, a.err,
-                             DEV_TIMEOUT_FULL)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint64_t db = dWi + (uint64_t)((s * kWinBytes) >> 4);
+            const uint64_t db = dWi + (uint64_t)((s * kWinBytes) >> 4);
+            const uint64_t da = dX + (uint64_t)((kx * kXChunkBytes) >> 4);
+            // the two subtiles' chains interleaved: consecutive UMMAs into one accumulator
+            // serialise, independent ones overlap
 #pragma unroll
-              for (int sub = 0; sub < 2; ++sub) {
-                const uint64_t da = dX + (uint64_t)((kx * kXChunkBytes + sub * 16384u) >> 4);
+            for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                  umma_f16(tmem + sub * 128, da + 2 * kk, db + 2 * kk, id_in,
-                           (kx | kk) ? 1u : 0u);
-              }
-              umma_commit(bar(B_WIE + s));
-              ++wi;
-            }
-            if (!ok) break;
-            umma_commit(bar(B_INF));
-            if (c == nchunk - 1) umma_commit(bar(B_XE));  // the halo slabs are free
+              for (int sub = 0; sub < 2; ++sub)
+                umma_f16(tmem + g * 128 + sub * 64, da + (uint64_t)sub * (16384u >> 4) + 2 * kk,
+                         db + 2 * kk, id_in, (kx | kk) ? 1u : 0u);
+            umma_commit(bar(B_WIE + s));
+            ++wi;
           }
-          if (c > 0) {
-            if (!mbar_wait_sleep(bar(B_GF), (uint32_t)((g - 1) & 1), abort_flag, a.err,
-                                 DEV_TIMEOUT_FULL) ||
-                !mbar_wait(bar(B_WOF), (uint32_t)(wo & 1), abort_flag, a.err,
-                           DEV_TIMEOUT_FULL) ||
-                (c == 1 && !mbar_wait_sleep(bar(B_OE), (uint32_t)(it & 1) ^ 1u, abort_flag, a.err,
-                                            DEV_TIMEOUT_ACC_EMPTY))) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint64_t db = dWo;
-#pragma unroll
-            for (int sub = 0; sub < 2; ++sub) {
-              const uint64_t da = dG + (uint64_t)((sub * 16384u) >> 4);
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                umma_f16(tmem + 256 + sub * a.dim, da + 2 * kk, db + 2 * kk, id_out,
-                         (c > 1 || kk) ? 1u : 0u);
-            }
-            umma_commit(bar(B_WOE));
-            umma_commit(bar(B_GE));
-            ++wo;
-            if (c == nchunk) umma_commit(bar(B_OF));
-          }
+          if (!ok) break;
+          umma_commit(bar(B_INF + g));
         }
+        if (ok) umma_commit(bar(B_XE));  // the halo slabs are free
       }
       umma_commit(bar(B_DRAIN));
       mbar_wait_drain(bar(B_DRAIN), 0, a.err);
     }
+  } else if (warp == kFfnOutWarp) {
+    // ---------------------------------------------------------------- project_out issuer
+    // Slice c's gated block (K = 32) times W_out[:, 32 c .. 32 c + 31] accumulates into TMEM
+    // columns [256, 256 + 2 dim), in slice order. This thread also streams the W_out blocks
+    // through a two-slot ring: after issuing slice gc it loads slice gc + 1's block into the
+    // slot slice gc - 1 used (a slice's depthwise takes far longer than the copy).
+    if (lane == 0) {
+      const uint32_t id_out = idesc_f16((uint32_t)a.dim);
+      const uint64_t dWo = smem_desc(smem_u32(sWout), 64u);
+      const uint64_t dG = smem_desc(smem_u32(sG), 64u);
+      long long wo = 0, wl = 0;  // slices issued, W_out blocks loaded
+      auto load_wo = [&](int c) {
+        const int s = (int)(wl & 1);
+        mbar_arrive_expect_tx(bar(B_WOF + s), wob);
+        bulk_load(smem_u32(sWout) + s * wob, a.wout + (size_t)c * a.dim * 32, wob,
+                  bar(B_WOF + s));
+        ++wl;
+      };
+      if (blockIdx.x < a.num_tiles) load_wo(0);
+      bool ok = true;
+      int it = 0;
+      for (int t = blockIdx.x; t < a.num_tiles && ok && !*abort_flag; t += gridDim.x, ++it) {
+        for (int c = 0; c < S; ++c) {
+          const long long gc = (long long)it * S + c;
+          const int g = c & 1, s = (int)(wo & 1);
+          if (!mbar_wait_sleep(bar(B_GF + g), (uint32_t)((gc >> 1) & 1), abort_flag, a.err,
+                               DEV_TIMEOUT_FULL) ||
+              !mbar_wait(bar(B_WOF + s), (uint32_t)((wo >> 1) & 1), abort_flag, a.err,
+                         DEV_TIMEOUT_FULL) ||
+              (c == 0 && !mbar_wait_sleep(bar(B_OE), (uint32_t)(it & 1) ^ 1u, abort_flag, a.err,
+                                          DEV_TIMEOUT_ACC_EMPTY))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t db = dWo + (uint64_t)((s * wob) >> 4);
+          const uint64_t da = dG + (uint64_t)((g * kGBytes) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+            for (int sub = 0; sub < 2; ++sub)
+              umma_f16(tmem + 256 + sub * a.dim, da + (uint64_t)sub * (8192u >> 4) + 2 * kk,
+                       db + 2 * kk, id_out, (c > 0 || kk) ? 1u : 0u);
+          umma_commit(bar(B_WOE + s));
+          umma_commit(bar(B_GE + g));
+          ++wo;
+          // the next slice's W_out block (the next tile's first after the last), into the slot
+          // of slice gc - 1 once its UMMAs are complete
+          if (c + 1 < S || t + (int)gridDim.x < a.num_tiles) {
+            if (wo >= 2 &&
+                !mbar_wait(bar(B_WOE + (int)(wl & 1)), (uint32_t)(((wl - 2) >> 1) & 1), abort_flag,
+                           a.err, DEV_TIMEOUT_EMPTY)) {
+              ok = false;
+              break;
+            }
+            load_wo(c + 1 < S ? c + 1 : 0);
+          }
+        }
+        if (ok) umma_commit(bar(B_OF));
+      }
+      // the W_out copies in flight land before shared memory goes away
+      for (int s = 0; s < 2; ++s)
+        if (wl > s) {
+          const long long last = ((wl - 1 - s) / 2) * 2 + s;
+          mbar_wait_drain(bar(B_WOF + s), (uint32_t)((last >> 1) & 1), a.err);
+        }
+      umma_commit(bar(B_DRAIN + 1));
+      mbar_wait_drain(bar(B_DRAIN + 1), 0, a.err);
+    }
   } else {
     // ---------------------------------------------------------------- compute warps
-    const int cw = warp - 2;
+    // Two groups of 8 warps; group g takes the slices c = g, g + 2, ..: drains its project_in
+    // accumulator into its f16 halo image, then runs the depthwise 3x3 + ELU gate into its
+    // gated block while the other group drains or computes the neighbouring slice.
+    const int cw = warp - 2;  // 0 .. 15
+    const int g = cw >> 3, w8 = cw & 7;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    // drain role: subtile `dsub`, channel pairs [16 dh, 16 dh + 16) of the chunk
-    const int dsub = (cw >> 2) >> 1, dh = (cw >> 2) & 1;
-    const int p = dsub * 128 + 32 * q + lane;  // halo pixel of this thread's TMEM row
     const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
-    // depthwise role: output columns 2 cp, 2 cp + 1, rows 6 rh .. 6 rh + 5, channel pair j
-    const int cp = cw & 7, rh = cw >> 3, j = lane;
+    // drain role: subtile dsub, TMEM row 32 q + lane = halo pixel p
+    const int dsub = w8 >> 2;
+    const int p = dsub * 128 + 32 * q + lane;
+    // depthwise role: output columns 2 cp, 2 cp + 1, rows 6 rh .. 6 rh + 5, channel pair j of
+    // the slice (ELU operands 2j, 2j + 1 and their multipliers)
+    const int j = lane & 15, cp = 2 * (w8 & 3) + (lane >> 4), rh = w8 >> 2;
+    uint8_t* const hbuf = sH + g * kHBytes;
+    uint8_t* const gbuf = sG + g * kGBytes;
     bool ok = true;
     int it = 0;
     for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x, ++it) {
       const int tx = t % a.tiles_x, rest = t / a.tiles_x;
       const int ty = rest % a.tiles_y, n = rest / a.tiles_y;
-      for (int c = 0; c < nchunk; ++c) {
-        const long long g = (long long)it * nchunk + c;
-        // ---- drain project_in: f16 halo image, pixel p at p * kHPitch, channel pair k in
-        // the 8-byte slot k: {elu operands 2k, 2k + 1, multipliers 2k, 2k + 1}
-        if (!mbar_wait_sleep(bar(B_INF), (uint32_t)(g & 1), abort_flag, a.err,
-                             DEV_TIMEOUT_ACC_FULL)) {
+      for (int c = g; c < S; c += 2) {
+        const long long gc = (long long)it * S + c;
+        const uint32_t ph = (uint32_t)((gc >> 1) & 1);  // phase of this group's barriers
+        // ---- drain project_in: halo pixel p at p * kHPitch, channel pair k in the 8-byte
+        // slot k: {elu operands 2k, 2k + 1, multipliers 2k, 2k + 1}
+        if (!mbar_wait_sleep(bar(B_INF + g), ph, abort_flag, a.err, DEV_TIMEOUT_ACC_FULL)) {
           ok = false;
           break;
         }
         tc_fence_after();
         {
-          // f16 of acc * scale + 0 (the unfused layer's epilogue with its zero bias), 16
-          // channel pairs in two halves of 8
-          uint32_t hv[2][8][2];
+          // f16 of acc * scale + 0 (the unfused layer's epilogue with its zero bias)
+          uint32_t hv[16][2];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             float ve[16], vm[16];
-            tmem_ld16x2(trow + dsub * 128 + 32 * dh + 16 * hh,
-                        trow + dsub * 128 + 64 + 32 * dh + 16 * hh, ve, vm);
+            tmem_ld16x2(trow + g * 128 + dsub * 64 + 16 * hh,
+                        trow + g * 128 + dsub * 64 + 32 + 16 * hh, ve, vm);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              hv[hh][i][0] = f2h(ve[2 * i] * a.scale_in + 0.f, ve[2 * i + 1] * a.scale_in + 0.f);
-              hv[hh][i][1] = f2h(vm[2 * i] * a.scale_in + 0.f, vm[2 * i + 1] * a.scale_in + 0.f);
+              hv[8 * hh + i][0] =
+                  f2h(ve[2 * i] * a.scale_in + 0.f, ve[2 * i + 1] * a.scale_in + 0.f);
+              hv[8 * hh + i][1] =
+                  f2h(vm[2 * i] * a.scale_in + 0.f, vm[2 * i + 1] * a.scale_in + 0.f);
             }
           }
           tc_fence_before();
-          mbar_arrive(bar(B_INE));
-          // the accumulators are in registers; the halo image is free once every thread has
-          // finished the previous chunk's depthwise
-          if (!mbar_wait_sleep(bar(B_HE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
-                               DEV_TIMEOUT_ACC_FULL)) {
+          mbar_arrive(bar(B_INE + g));
+          // the accumulator is in registers; the halo image is free once every thread of the
+          // group has finished the group's previous slice
+          if (!mbar_wait_sleep(bar(B_HE + g), ph ^ 1u, abort_flag, a.err, DEV_TIMEOUT_ACC_FULL)) {
             ok = false;
             break;
           }
           if (p < kFfnHalo) {
-            uint2* hp = reinterpret_cast<uint2*>(sH + p * kHPitch) + 16 * dh;
+            uint2* hp = reinterpret_cast<uint2*>(hbuf + p * kHPitch);
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-              for (int i = 0; i < 8; ++i) hp[8 * hh + i] = make_uint2(hv[hh][i][0], hv[hh][i][1]);
+            for (int k = 0; k < 16; ++k) hp[k] = make_uint2(hv[k][0], hv[k][1]);
           }
         }
-        mbar_arrive(bar(B_HF));
-        if (!mbar_wait_sleep(bar(B_HF), (uint32_t)(g & 1), abort_flag, a.err, DEV_TIMEOUT_ACC_FULL) ||
-            !mbar_wait_sleep(bar(B_WDF + (int)(g & 1)), (uint32_t)((g >> 1) & 1), abort_flag, a.err,
+        mbar_arrive(bar(B_HF + g));
+        const int ws = (int)(gc % kWdSlots);
+        if (!mbar_wait_sleep(bar(B_HF + g), ph, abort_flag, a.err, DEV_TIMEOUT_ACC_FULL) ||
+            !mbar_wait_sleep(bar(B_WDF + ws), (uint32_t)((gc / kWdSlots) & 1), abort_flag, a.err,
                              DEV_TIMEOUT_FULL) ||
-            !mbar_wait_sleep(bar(B_GE), (uint32_t)(g & 1) ^ 1u, abort_flag, a.err,
-                       DEV_TIMEOUT_ACC_FULL)) {
+            !mbar_wait_sleep(bar(B_GE + g), ph ^ 1u, abort_flag, a.err, DEV_TIMEOUT_ACC_FULL)) {
           ok = false;
           break;
         }
-        // depthwise weights of the thread's channels {elu 2j, 2j + 1, multipliers 2j, 2j + 1}
-        // per tap ([tap][pair] in the chunk's slot)
+        // depthwise weights of the thread's channels per tap ([tap][pair] in the slice's slot)
         float4 wr[9];
         {
-          const float4* ws = reinterpret_cast<const float4*>(sWd + (g & 1) * kWdBytes) + j;
+          const float4* wsrc = reinterpret_cast<const float4*>(sWd + ws * kWdBytes) + j;
 #pragma unroll
-          for (int tp = 0; tp < 9; ++tp) wr[tp] = ws[tp * 32];
+          for (int tp = 0; tp < 9; ++tp) wr[tp] = wsrc[tp * 16];
         }
         // ---- depthwise 3x3 + gate over halo rows 6 rh .. 6 rh + 7 (rolling 3-row
         // accumulators; per output the taps in (ky, kx) order, the first one a product)
         {
-          // gated block row op = (6 rh + o) * 16 + 2 cp + col: 128 bytes per row, the channel
-          // pair's 4 bytes in 16-byte chunk (j / 4) ^ (op & 7), and op & 7 = (2 cp + col) & 7
+          // gated block row op = (6 rh + o) * 16 + 2 cp + col: 64 bytes per row (64-byte
+          // swizzle), the channel pair's 4 bytes in 16-byte chunk (j / 4) ^ ((op / 2) & 3), and
+          // (op / 2) & 3 = cp & 3
           uint8_t* gcol[2];
 #pragma unroll
           for (int col = 0; col < 2; ++col)
-            gcol[col] = sG + (6 * rh * kFfnTW + 2 * cp + col) * 128 +
-                        (((j >> 2) ^ ((2 * cp + col) & 7)) << 4) + ((j & 3) << 2);
+            gcol[col] = gbuf + (6 * rh * kFfnTW + 2 * cp + col) * 64 +
+                        (((j >> 2) ^ (cp & 3)) << 4) + ((j & 3) << 2);
+          const uint8_t* hrow = hbuf + (6 * rh * kFfnHW + 2 * cp) * kHPitch + 8 * j;
           float2 acc[3][2][2];
           auto row = [&](auto JJ, int i) {
             constexpr int J = decltype(JJ)::value;
-            const int p0 = (6 * rh + i) * kFfnHW + 2 * cp;
             // halo column jx is tap kx = jx of output column 0 and kx = jx - 1 of column 1:
             // per accumulator the taps of a row still come in kx order
 #pragma unroll
             for (int jx = 0; jx < 4; ++jx) {
-              const int pp = p0 + jx;
-              const uint2 u = *reinterpret_cast<const uint2*>(sH + pp * kHPitch + 8 * j);
+              const uint2 u = *reinterpret_cast<const uint2*>(hrow + (i * kFfnHW + jx) * kHPitch);
               const float2 v[2] = {h2f(u.x), h2f(u.y)};
 #pragma unroll
               for (int ky = 0; ky < 3; ++ky)
@@ -372,7 +417,7 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
 #pragma unroll
               for (int col = 0; col < 2; ++col) {
                 const float2 y = elu_gate2(so[col][0], so[col][1]);
-                *reinterpret_cast<uint32_t*>(gcol[col] + o * (kFfnTW * 128)) = f2h(y.x, y.y);
+                *reinterpret_cast<uint32_t*>(gcol[col] + o * (kFfnTW * 64)) = f2h(y.x, y.y);
               }
             }
           };
@@ -384,27 +429,29 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
           }
         }
         fence_proxy_async_smem();  // the gated block is read by the tensor cores
-        mbar_arrive(bar(B_GF));
-        mbar_arrive(bar(B_HE));
-        mbar_arrive(bar(B_WDE + (int)(g & 1)));
+        mbar_arrive(bar(B_GF + g));
+        mbar_arrive(bar(B_HE + g));
+        mbar_arrive(bar(B_WDE + ws));
       }
       if (!ok) break;
-      // ---- output: x += W_out . gate(..) for the tile's 192 pixels
-      if (!mbar_wait_sleep(bar(B_OF), (uint32_t)(it & 1), abort_flag, a.err, DEV_TIMEOUT_ACC_FULL)) {
+      // ---- output: x += W_out . gate(..) for the tile's 192 pixels (both groups)
+      if (!mbar_wait_sleep(bar(B_OF), (uint32_t)(it & 1), abort_flag, a.err,
+                           DEV_TIMEOUT_ACC_FULL)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (!(dsub == 1 && q >= 2)) {  // subtile 1 holds 64 pixels
-        const int o = dsub * 128 + 32 * q + lane;
+      const int osub = (cw >> 2) >> 1, oh = (cw >> 2) & 1;
+      if (!(osub == 1 && q >= 2)) {  // subtile 1 holds 64 pixels
+        const int o = osub * 128 + 32 * q + lane;
         const int Y = ty * kFfnTH + (o >> 4), X = tx * kFfnTW + (o & 15);
         const bool valid = Y < a.h && X < a.w;
         const int half = a.dim >> 1;
         __half* xp = a.x + n * a.x_img + (long long)Y * a.x_row + (long long)X * a.x_pix +
-                     dh * half;
+                     oh * half;
         for (int cb = 0; cb < half; cb += 32) {
           float v[32];
-          tmem_ld32(trow + 256 + dsub * a.dim + dh * half + cb, v);
+          tmem_ld32(trow + 256 + osub * a.dim + oh * half + cb, v);
           if (valid) {
 #pragma unroll
             for (int g8 = 0; g8 < 4; ++g8) {
@@ -461,11 +508,12 @@ bool ffn_fusable(int dim, int hidden) {
   return (dim == 64 || dim == 128) && hidden > 0 && hidden % 64 == 0;
 }
 
-// One 128-byte-swizzled row of 64 halves: 16-byte chunk j of row r at j ^ (r & 7).
-static void put_row(__half* dst, int r, const float* src, int stride, float s) {
-  for (int k = 0; k < 64; ++k)
-    dst[(size_t)r * 64 + (((k >> 3) ^ (r & 7)) << 3) + (k & 7)] =
-        __float2half_rn(src[(size_t)k * stride] * s);
+// One swizzled row of `len` (64 or 32) halves: 16-byte chunk j of row r at j ^ (r & 7) (128-byte
+// rows) or j ^ ((r / 2) & 3) (64-byte rows), the shared-memory image the UMMA descriptors read.
+static void put_row(__half* dst, int r, int len, const float* src, float s) {
+  const int f = len == 64 ? (r & 7) : ((r >> 1) & 3);
+  for (int k = 0; k < len; ++k)
+    dst[(size_t)r * len + (((k >> 3) ^ f) << 3) + (k & 7)] = __float2half_rn(src[k] * s);
 }
 
 int pack_ffn(Ctx* ctx, FfnLayer* L, const float* w_in, const float* w_dw, const float* w_out,
@@ -480,27 +528,27 @@ int pack_ffn(Ctx* ctx, FfnLayer* L, const float* w_in, const float* w_dw, const 
   const float so = pow2_weight_scale(w_out, (size_t)dim * hidden);
   L->scale_in = 1.f / si;
   L->scale_out = 1.f / so;
-  const int nchunk = hidden / 64, kxn = dim / 64;
-  std::vector<__half> wi((size_t)nchunk * kxn * 128 * 64), wo((size_t)nchunk * dim * 64);
-  for (int c = 0; c < nchunk; ++c)
+  const int ns = hidden / 32, kxn = dim / 64;
+  std::vector<__half> wi((size_t)ns * kxn * 64 * 64), wo((size_t)ns * dim * 32);
+  for (int c = 0; c < ns; ++c)
     for (int kx = 0; kx < kxn; ++kx) {
-      __half* blk = wi.data() + (size_t)(c * kxn + kx) * 128 * 64;
-      for (int r = 0; r < 128; ++r) {
-        const int oc = r < 64 ? 64 * c + r : hidden + 64 * c + (r - 64);
-        put_row(blk, r, w_in + (size_t)oc * dim + 64 * kx, 1, si);
+      __half* blk = wi.data() + (size_t)(c * kxn + kx) * 64 * 64;
+      for (int r = 0; r < 64; ++r) {
+        const int oc = r < 32 ? 32 * c + r : hidden + 32 * c + (r - 32);
+        put_row(blk, r, 64, w_in + (size_t)oc * dim + 64 * kx, si);
       }
     }
-  for (int c = 0; c < nchunk; ++c)
+  for (int c = 0; c < ns; ++c)
     for (int r = 0; r < dim; ++r)
-      put_row(wo.data() + (size_t)c * dim * 64, r, w_out + (size_t)r * hidden + 64 * c, 1, so);
-  // depthwise weights [chunk][tap][pair j] {w[64c + 2j], w[64c + 2j + 1], w[hidden + 64c + 2j],
-  // w[hidden + 64c + 2j + 1]} at the tap
-  std::vector<float> wd((size_t)nchunk * 9 * 32 * 4);
-  for (int c = 0; c < nchunk; ++c)
+      put_row(wo.data() + (size_t)c * dim * 32, r, 32, w_out + (size_t)r * hidden + 32 * c, so);
+  // depthwise weights [slice][tap][pair j] {w[32c + 2j], w[32c + 2j + 1], w[hidden + 32c + 2j],
+  // w[hidden + 32c + 2j + 1]} at the tap
+  std::vector<float> wd((size_t)ns * 9 * 16 * 4);
+  for (int c = 0; c < ns; ++c)
     for (int tp = 0; tp < 9; ++tp)
-      for (int j = 0; j < 32; ++j) {
-        const int e0 = 64 * c + 2 * j, m0 = hidden + e0;
-        float* d = wd.data() + ((size_t)(c * 9 + tp) * 32 + j) * 4;
+      for (int j = 0; j < 16; ++j) {
+        const int e0 = 32 * c + 2 * j, m0 = hidden + e0;
+        float* d = wd.data() + ((size_t)(c * 9 + tp) * 16 + j) * 4;
         d[0] = w_dw[(size_t)e0 * 9 + tp];
         d[1] = w_dw[(size_t)(e0 + 1) * 9 + tp];
         d[2] = w_dw[(size_t)m0 * 9 + tp];
@@ -542,7 +590,7 @@ int run_ffn(Ctx* ctx, const FfnLayer& L, const TView& ln, const TView& x) {
   a.h = x.h;
   a.w = x.w;
   a.dim = L.dim;
-  a.nchunk = L.hidden / 64;
+  a.nslice = L.hidden / 32;
   a.tiles_x = (x.w + kFfnTW - 1) / kFfnTW;
   a.tiles_y = (x.h + kFfnTH - 1) / kFfnTH;
   a.num_tiles = a.tiles_x * a.tiles_y * x.n;
