@@ -100,7 +100,7 @@ __global__ void layer_norm_kernel(const __half* __restrict__ x, __half* __restri
 // A thread handles kLnPix pixels (their loads issued together), its gamma / beta stay in
 // registers. Two-pass mean and variance in f32 like layer_norm_kernel; the normalisation
 // multiplies by one reciprocal of the deviation per pixel.
-constexpr int kLnPix = 4;
+constexpr int kLnPix = 8;
 
 // Element offset of pixel p (raster order over n, h, w) in a view; `dense`: the view's pixels
 // are contiguous (row == w * pix, img == h * row), so no division is needed.
@@ -127,24 +127,32 @@ __global__ void __launch_bounds__(256) layer_norm_seg_kernel(
     gm[i] = act ? __ldg(gamma + c0 + i) : 0.f;
     bt[i] = act ? __ldg(beta + c0 + i) : 0.f;
   }
-  float v[kLnPix][8];
+  // the pixels' raw f16 (16 bytes each) in flight together, unpacked one pixel at a time
+  uint4 raw[kLnPix];
   int pxl[kLnPix];
 #pragma unroll
   for (int k = 0; k < kLnPix; ++k) {
     pxl[k] = (blockIdx.x * kLnPix + k) * SEGS + threadIdx.x / LPP;
     const int p = pxl[k];
-    if (act && p < npix) {
-      ld8(x + pix_off(p, h, w, xpix, xrow, ximg, xdense) + c0, v[k]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[k][i] = 0.f;
-    }
+    raw[k] = (act && p < npix)
+                 ? *reinterpret_cast<const uint4*>(x + pix_off(p, h, w, xpix, xrow, ximg, xdense) + c0)
+                 : make_uint4(0u, 0u, 0u, 0u);
   }
 #pragma unroll
   for (int k = 0; k < kLnPix; ++k) {
+    float v[8];
+    {
+      const __half2* hh = reinterpret_cast<const __half2*>(&raw[k]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(hh[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    }
     float sum = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) sum += v[k][i];
+    for (int i = 0; i < 8; ++i) sum += v[i];
 #pragma unroll
     for (int o = LPP / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     const float mean = sum / (float)c;
@@ -152,7 +160,7 @@ __global__ void __launch_bounds__(256) layer_norm_seg_kernel(
     if (act) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float d = v[k][i] - mean;
+        const float d = v[i] - mean;
         sq += d * d;
       }
     }
@@ -163,7 +171,7 @@ __global__ void __launch_bounds__(256) layer_norm_seg_kernel(
     if (act && p < npix) {
       float o8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o8[i] = (v[k][i] - mean) * inv * gm[i] + bt[i];
+      for (int i = 0; i < 8; ++i) o8[i] = (v[i] - mean) * inv * gm[i] + bt[i];
       st8(y + pix_off(p, h, w, ypix, yrow, yimg, ydense) + c0, o8);
     }
   }
