@@ -952,6 +952,65 @@ __global__ void attn_fold_kernel(const float* __restrict__ wo, const float* __re
   blk[rr * kc + (((col >> 3) ^ f) << 3) + (col & 7)] = __float2half_rn(acc * s);
 }
 
+// attn_reduce_kernel + attn_softmax_kernel + attn_fold_kernel in one launch for the common
+// shapes (c = 16 or 32, packed layer without padding rows or columns): block (head hd,
+// picture n) sums the head's Gram block and norms over the partial slots in slot order,
+// takes the c x c softmax (one thread per row) and writes the head's columns of
+// W_o . blockdiag(A) in the packed layout: the same operations in the same order as the three
+// kernels, with two launches fewer per attention.
+template <int C>
+__global__ void __launch_bounds__(256) attn_fold_fused_kernel(
+    const float* __restrict__ part, int nparts, long long stride, const float* __restrict__ temp,
+    const float* __restrict__ wo, int dim, float s, __half* __restrict__ wout, int npad,
+    int cin_pad, int kc, int bn) {
+  __shared__ float sa[C * C];   // the head's Gram block, then its attention matrix
+  __shared__ float sn[2 * C];   // q norms of its rows, k norms of its columns
+  const int hd = blockIdx.x, n = blockIdx.y;
+  const float* p = part + (long long)n * nparts * stride;
+  for (int e = threadIdx.x; e < C * C + 2 * C; e += blockDim.x) {
+    const long long off = e < C * C     ? (long long)(hd * C + e / C) * C + e % C
+                          : e < C * C + C ? (long long)dim * C + hd * C + (e - C * C)
+                                          : (long long)dim * C + dim + hd * C + (e - C * C - C);
+    float acc = 0.f;
+    for (int k = 0; k < nparts; ++k) acc += p[k * stride + off];
+    if (e < C * C)
+      sa[e] = acc;
+    else
+      sn[e - C * C] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x < C) {
+    const int i = threadIdx.x;
+    const float nq = fmaxf(sqrtf(sn[i]), 1e-12f);
+    float vals[C];
+    float mx = -INFINITY;
+    for (int j = 0; j < C; ++j) {
+      const float nk = fmaxf(sqrtf(sn[C + j]), 1e-12f);
+      const float v = sa[i * C + j] / (nq * nk) * temp[hd];
+      vals[j] = v;
+      mx = fmaxf(mx, v);
+    }
+    float sum = 0.f;
+    for (int j = 0; j < C; ++j) {
+      vals[j] = expf(vals[j] - mx);
+      sum += vals[j];
+    }
+    for (int j = 0; j < C; ++j) sa[i * C + j] = vals[j] / sum;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < dim * C; idx += blockDim.x) {
+    const int r = idx / C, jj = idx % C, j = hd * C + jj;
+    const float* W = wo + (long long)r * dim + hd * C;
+    float acc = 0.f;
+    for (int i = 0; i < C; ++i) acc = fmaf(__ldg(W + i), sa[i * C + jj], acc);
+    const int cc = j / kc, col = j % kc, nt = r / bn, rr = r % bn;
+    const int f = kc == 64 ? (rr & 7) : kc == 32 ? ((rr >> 1) & 3) : ((rr >> 2) & 1);
+    __half* blk =
+        wout + (long long)n * npad * cin_pad + ((long long)cc * (npad / bn) + nt) * bn * kc;
+    blk[rr * kc + (((col >> 3) ^ f) << 3) + (col & 7)] = __float2half_rn(acc * s);
+  }
+}
+
 // planar f32 latent [C][LH][LW] -> NHWC f16 [n][h][w] at channel offset; per-image window
 // origins (x, y) in `origin` (device int pairs).
 __global__ void gather_latent_kernel(const float* __restrict__ src, int C, int LH, int LW,
@@ -1092,8 +1151,10 @@ static GramPlan gram_plan(int n, int dim, int heads, int npix, int sms) {
 }
 
 // Gram, norms and softmax: the attention matrices attn[n][h][i][j] (in the scratch).
+// The Gram partial slots (at scratch), then (unless gram_only) their ordered sum and the
+// softmax; returns the attention matrices [n][dim][c].
 static float* attention_weights(const TView& qkv, int heads, const float* temp, float* scratch,
-                                int sms, cudaStream_t s) {
+                                int sms, cudaStream_t s, bool gram_only = false) {
   const int dim = qkv.c / 3;
   const int c = dim / heads;
   const int n = qkv.n;
@@ -1130,6 +1191,7 @@ static float* attention_weights(const TView& qkv, int heads, const float* temp, 
         qkv.p, n, npix, qkv.w, dim, heads, qkv.pix, qkv.row, qkv.img, part, gp.nparts,
         gp.per_block);
   }
+  if (gram_only) return attn;
   attn_reduce_kernel<<<blocks_for((long long)n * stride, 256), 256, 0, s>>>(part, gp.nparts,
                                                                            stride, n, red);
   attn_softmax_kernel<<<blocks_for((long long)n * dim, 128), 128, 0, s>>>(red, temp, attn, n, dim,
@@ -1137,10 +1199,33 @@ static float* attention_weights(const TView& qkv, int heads, const float* temp, 
   return attn;
 }
 
+static bool fold_fused(int dim, int heads, const ConvLayer& L) {
+  const int c = dim / heads;
+  return (c == 16 || c == 32) && L.npad == dim && L.cin_pad == dim;
+}
+
+int attention_fold_launches(int dim, int heads, const ConvLayer& L) {
+  return fold_fused(dim, heads, L) ? 2 : 4;
+}
+
 void launch_attention_fold(const TView& qkv, int heads, const float* temp, const float* wo,
                            float wscale, const ConvLayer& L, __half* wout, float* scratch,
                            int sms, cudaStream_t s) {
   const int dim = qkv.c / 3;
+  const int c = dim / heads;
+  if (fold_fused(dim, heads, L)) {
+    const GramPlan gp = gram_plan(qkv.n, dim, heads, qkv.h * qkv.w, sms);
+    const long long stride = (long long)dim * c + 2 * dim;
+    attention_weights(qkv, heads, temp, scratch, sms, s, /*gram_only=*/true);
+    dim3 g(heads, qkv.n);
+    if (c == 32)
+      attn_fold_fused_kernel<32><<<g, 256, 0, s>>>(scratch, gp.nparts, stride, temp, wo, dim,
+                                                   wscale, wout, L.npad, L.cin_pad, L.kc, L.bn);
+    else
+      attn_fold_fused_kernel<16><<<g, 256, 0, s>>>(scratch, gp.nparts, stride, temp, wo, dim,
+                                                   wscale, wout, L.npad, L.cin_pad, L.kc, L.bn);
+    return;
+  }
   const float* attn = attention_weights(qkv, heads, temp, scratch, sms, s);
   dim3 g(blocks_for((long long)L.npad * L.cin_pad, 256), qkv.n);
   attn_fold_kernel<<<g, 256, 0, s>>>(wo, attn, dim, dim / heads, wscale, wout, L.npad,

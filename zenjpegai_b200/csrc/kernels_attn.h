@@ -24,6 +24,9 @@ size_t attention_scratch_floats(int n_img, int dim, int heads, int npix, int sms
 void launch_attention_fold(const TView& qkv, int heads, const float* temp, const float* wo,
                            float wscale, const ConvLayer& L, __half* wout, float* scratch,
                            int sms, cudaStream_t s);
+// Kernel launches launch_attention_fold makes (the Gram, then one fused reduce + softmax +
+// fold kernel for heads of 16 or 32 channels, else three).
+int attention_fold_launches(int dim, int heads, const ConvLayer& L);
 void launch_gather_latent(const float* src, int C, int LH, int LW, const int* origin,
                           const TView& dst, cudaStream_t s);
 

@@ -423,7 +423,7 @@ int Runner::tb(const std::string& p, const TView& x) {
   __half* wfold = static_cast<__half*>(arena->alloc((size_t)n * wset * sizeof(__half)));
   if (!wfold) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (folded weights)");
   const float fs = net->fold_scale.at(p);
-  mem_kernel(p + ".attn", "attn", b16 * 2 * d, 4, [&] {
+  mem_kernel(p + ".attn", "attn", b16 * 2 * d, attention_fold_launches(d, 4, *Lo), [&] {
     launch_attention_fold(qkv2, 4, vec(p + ".attn.temperature"),
                           vec(p + ".attn.project_out.weight"), fs, *Lo, wfold, scratch, ctx->sms,
                           stream);
