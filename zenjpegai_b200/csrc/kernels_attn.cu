@@ -1032,6 +1032,33 @@ __global__ void gather_latent_kernel(const float* __restrict__ src, int C, int L
   if (C & 1) d[C - 1] = __float2half_rn(__ldg(s + (C - 1) * plane));
 }
 
+// The same gather with one thread per (pixel, group of 8 channels), x fastest: the 8 plane
+// reads of a warp are coalesced along x and each thread writes one 16-byte store (C % 8 == 0
+// and 16-byte aligned channel groups).
+__global__ void gather_latent8_kernel(const float* __restrict__ src, int C, int LH, int LW,
+                                      const int* __restrict__ origin, __half* __restrict__ dst,
+                                      int n_img, int h, int w, long long pix, long long row,
+                                      long long img) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int groups = C >> 3;
+  const long long total = (long long)n_img * h * w * groups;
+  if (idx >= total) return;
+  const int x = (int)(idx % w);
+  long long r = idx / w;
+  const int g = (int)(r % groups);
+  r /= groups;
+  const int y = (int)(r % h), n = (int)(r / h);
+  const int sx = origin[2 * n] + x, sy = origin[2 * n + 1] + y;
+  const long long plane = (long long)LH * LW;
+  const float* sp = src + (long long)(8 * g) * plane + (long long)sy * LW + sx;
+  uint4 u;
+  __half2* hv = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    hv[i] = __floats2half2_rn(__ldg(sp + (2 * i) * plane), __ldg(sp + (2 * i + 1) * plane));
+  *reinterpret_cast<uint4*>(dst + n * img + (long long)y * row + (long long)x * pix + 8 * g) = u;
+}
+
 }  // namespace
 
 void launch_layer_norm(const TView& x, const TView& y, const float* gamma, const float* beta,
@@ -1268,6 +1295,12 @@ size_t attention_scratch_floats(int n_img, int dim, int heads, int npix, int sms
 void launch_gather_latent(const float* src, int C, int LH, int LW, const int* origin,
                           const TView& dst, cudaStream_t s) {
   long long total = (long long)dst.n * dst.h * dst.w;
+  if (C % 8 == 0 && dst.pix % 8 == 0 && dst.row % 8 == 0 && dst.img % 8 == 0 &&
+      (reinterpret_cast<uintptr_t>(dst.p) & 15) == 0) {
+    gather_latent8_kernel<<<blocks_for(total * (C / 8), 256), 256, 0, s>>>(
+        src, C, LH, LW, origin, dst.p, dst.n, dst.h, dst.w, dst.pix, dst.row, dst.img);
+    return;
+  }
   gather_latent_kernel<<<blocks_for(total, 256), 256, 0, s>>>(src, C, LH, LW, origin, dst.p, dst.n,
                                                                dst.h, dst.w, dst.pix, dst.row,
                                                                dst.img);
