@@ -35,7 +35,7 @@ enum FfnBar : int {
   B_GF = B_HE + 2,           // gated block written (group threads)
   B_GE = B_GF + 2,           // ... consumed by project_out
   B_OF = B_GE + 2,           // project_out accumulators of a tile complete
-  B_OE,                      // ... drained (all compute threads)
+  B_OE,                      // ... drained (group 1's threads)
   B_DRAIN,                   // the two issuers' end-of-kernel drains
   B_COUNT = B_DRAIN + 2
 };
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
       mbar_init(bar(B_DRAIN + g), 1);
     }
     mbar_init(bar(B_OF), 1);
-    mbar_init(bar(B_OE), 2 * kGroupThreads);
+    mbar_init(bar(B_OE), kGroupThreads);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -137,6 +137,15 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
           tma_load_4d(smem_u32(sX) + kx * kXChunkBytes, &tmX, bar(B_XF), 64 * kx,
                       tx * kFfnTW - 1, ty * kFfnTH - 1, n);
         ++xi;
+        {  // the tile's residual rows into L2 for its output stage, a whole tile later
+          const int y0 = ty * kFfnTH, x0 = tx * kFfnTW;
+          const int cols = min(kFfnTW, a.w - x0);
+          const uint32_t rb = (uint32_t)(cols * a.x_pix * 2);
+          for (int r = 0; r < kFfnTH && y0 + r < a.h; ++r)
+            bulk_prefetch_l2(a.x + n * a.x_img + (long long)(y0 + r) * a.x_row +
+                                 (long long)x0 * a.x_pix,
+                             rb);
+        }
         for (int c = 0; c < S && ok; ++c) {
           for (int kx = 0; kx < kxn && ok; ++kx) {
             const int s = (int)(wi % kWinSlots);
@@ -434,45 +443,65 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
         mbar_arrive(bar(B_WDE + ws));
       }
       if (!ok) break;
-      // ---- output: x += W_out . gate(..) for the tile's 192 pixels (both groups)
-      if (!mbar_wait_sleep(bar(B_OF), (uint32_t)(it & 1), abort_flag, a.err,
-                           DEV_TIMEOUT_ACC_FULL)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int osub = (cw >> 2) >> 1, oh = (cw >> 2) & 1;
-      if (!(osub == 1 && q >= 2)) {  // subtile 1 holds 64 pixels
-        const int o = osub * 128 + 32 * q + lane;
-        const int Y = ty * kFfnTH + (o >> 4), X = tx * kFfnTW + (o & 15);
-        const bool valid = Y < a.h && X < a.w;
-        const int half = a.dim >> 1;
-        __half* xp = a.x + n * a.x_img + (long long)Y * a.x_row + (long long)X * a.x_pix +
-                     oh * half;
-        for (int cb = 0; cb < half; cb += 32) {
-          float v[32];
-          tmem_ld32(trow + 256 + osub * a.dim + oh * half + cb, v);
-          if (valid) {
+      // ---- output: x += W_out . gate(..) for the tile's 192 pixels, by group 1 (which has
+      // the tile's last slice) while group 0 goes on with the next tile's first slice. Warp
+      // (q, part) of the group takes channels [part * dim / 2, + dim / 2) of its TMEM lane
+      // quarter's pixels in both subtiles (subtile 1 holds 64 pixels: quarters 0 and 1). The
+      // residual loads (L2 hits: the producer prefetched the tile's rows) of the first subtile
+      // are issued before waiting for the last slice's project_out.
+      if (g == 1) {
+        const int part = w8 >> 2;
+        const int half = a.dim >> 1;  // 64 or 32 channels per thread and pixel
+        bool first = true;
+        for (int osub = 0; osub < 2; ++osub) {
+          if (osub == 1 && q >= 2) break;  // warp-uniform
+          const int o = osub * 128 + 32 * q + lane;
+          const int Y = ty * kFfnTH + (o >> 4), X = tx * kFfnTW + (o & 15);
+          const bool valid = Y < a.h && X < a.w;
+          __half* xp = a.x + n * a.x_img + (long long)Y * a.x_row + (long long)X * a.x_pix +
+                       part * half;
+          uint4 res[8];
 #pragma unroll
-            for (int g8 = 0; g8 < 4; ++g8) {
-              uint4* pp = reinterpret_cast<uint4*>(xp + cb + 8 * g8);
-              const uint4 r = *pp;
-              const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
-              uint32_t w4[4];
+          for (int k = 0; k < 8; ++k)
+            res[k] = (valid && 8 * k < half) ? *reinterpret_cast<const uint4*>(xp + 8 * k)
+                                             : make_uint4(0u, 0u, 0u, 0u);
+          if (first) {
+            if (!mbar_wait_sleep(bar(B_OF), (uint32_t)(it & 1), abort_flag, a.err,
+                                 DEV_TIMEOUT_ACC_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            first = false;
+          }
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 rf = h2f(rr[e]);
-                const float y0 = __fmul_rn(v[8 * g8 + 2 * e], a.scale_out) + rf.x;
-                const float y1 = __fmul_rn(v[8 * g8 + 2 * e + 1], a.scale_out) + rf.y;
-                w4[e] = f2h(y0, y1);
+          for (int cb = 0; cb < 64; cb += 32) {
+            if (cb >= half) break;
+            float v[32];
+            tmem_ld32(trow + 256 + osub * a.dim + part * half + cb, v);
+            if (valid) {
+#pragma unroll
+              for (int g8 = 0; g8 < 4; ++g8) {
+                uint4* pp = reinterpret_cast<uint4*>(xp + cb + 8 * g8);
+                const uint4 r = res[cb / 8 + g8];
+                const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+                uint32_t w4[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 rf = h2f(rr[e]);
+                  const float y0 = __fmul_rn(v[8 * g8 + 2 * e], a.scale_out) + rf.x;
+                  const float y1 = __fmul_rn(v[8 * g8 + 2 * e + 1], a.scale_out) + rf.y;
+                  w4[e] = f2h(y0, y1);
+                }
+                *pp = make_uint4(w4[0], w4[1], w4[2], w4[3]);
               }
-              *pp = make_uint4(w4[0], w4[1], w4[2], w4[3]);
             }
           }
         }
+        if (!ok) break;
+        tc_fence_before();
+        mbar_arrive(bar(B_OE));
       }
-      tc_fence_before();
-      mbar_arrive(bar(B_OE));
     }
   }
 
