@@ -1,8 +1,8 @@
 // Channel attention that allocates nothing (zjai_channel_attention_static).
 //
 // Some callers cannot allocate device memory at call time: code running under an external
-// allocator or a memory budget that forbids new allocations, callers replaying work inside
-// captured CUDA graphs, and embedders that only hand in pre-allocated buffers. This entry
+// allocator or a memory budget that forbids new allocations, and embedders that only hand in
+// pre-allocated buffers. This entry
 // point works on the caller's device buffers alone: the per-call scratch of the transposed
 // attention (the c x c Gram per head, the squared norms, the softmax rows) lives in one
 // file-scope device array of fixed size, and the kernels read the planar f32 tensors in place
@@ -26,7 +26,8 @@ constexpr int kStaticMaxC = 64;
 // gram: dim * c, squared norms: 2 * dim, softmax rows: dim * c
 constexpr int kStaticScratchFloats = 2 * kStaticMaxDim * kStaticMaxC + 2 * kStaticMaxDim;
 
-__device__ __align__(256) float g_attention_scratch[kStaticScratchFloats];
+// held by every GPU that loads the library, until the process exits (132 KiB)
+static __device__ __align__(256) float g_attention_scratch[kStaticScratchFloats];
 
 constexpr int kMaxDevices = 64;
 float* g_scratch_ptr[kMaxDevices] = {nullptr};
