@@ -22,7 +22,9 @@
 //    buffered, one per group);
 //  - the project_out warp accumulates each gated block times W_out[:, k .. k + 31] into a
 //    second TMEM accumulator (N = dim), in slice order;
-//  - after the last slice all compute warps add the residual and store x in place.
+//  - after the last slice, group 1 (which holds it) adds the residual (its rows prefetched
+//    into L2 by the producer a tile earlier) and stores x in place, while group 0 starts the
+//    next tile.
 // Weights stream from L2 by bulk copies into small rings. Every wait is bounded.
 #pragma once
 #include <cuda.h>
