@@ -140,7 +140,7 @@ __host__ __device__ inline uint32_t conv_fixed_smem(int npad, bool staged, int n
   return 1024u + kBarrierBytes + 8u * (uint32_t)npad +
          (staged ? (1u + (uint32_t)nres) * kEpiStagingBytes : 0u);
 }
-constexpr int kMaxHaloSlots = 4;
+constexpr int kMaxHaloSlots = 6;
 // a stage holding only the B block (halo mode)
 __host__ __device__ inline uint32_t conv_bstage_bytes(int kc, int bn) {
   return ((uint32_t)bn * kc * 2u + 1023u) & ~1023u;
