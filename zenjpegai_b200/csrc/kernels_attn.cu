@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(256, 2)
 }
 
 // ---- depthwise 3x3, row-streaming ----------------------------------------------------------
-// Work unit = (picture, strip of TW columns, band of kDsBand rows, block of 64 output
+// Work unit = (picture, strip of TW columns, band of U.band rows, block of 64 output
 // channels). A producer warp streams the unit's input rows with their one-pixel halo (band
 // rows + 2 rows of TW + 2 columns) through a ring of kDsStages shared-memory stages, one TMA
 // box [64 channels, TW + 2, 1 row] per 64-channel slab (gate: two slabs, the block's channels
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(256, 2)
 // (ky, kx) row-major order, two channels per packed f32x2 FMA (as in dw3x3_kernel).
 constexpr int kDsThreads = 512;  // compute threads; one more warp produces
 constexpr int kDsStages = 16;
-constexpr int kDsBand = 64;
+constexpr int kDsBand = 64;  // tallest band
 
 template <bool GATE>
 struct DsShape {
@@ -387,6 +387,7 @@ struct DsShape {
 // unit u: cb = u % cblocks, band, strip, picture in that order of significance
 struct DsUnits {
   int strips, bands, cblocks, count;
+  int band;  // rows per band (8 .. kDsBand)
 };
 
 template <bool GATE>
@@ -425,8 +426,8 @@ __global__ void __launch_bounds__(kDsThreads + 32, 1)
       const int band = rest % U.bands;
       rest /= U.bands;
       const int strip = rest % U.strips, n = rest / U.strips;
-      const int x0 = strip * S::TW, y0 = band * kDsBand;
-      const int rows = min(kDsBand, h - y0);
+      const int x0 = strip * S::TW, y0 = band * U.band;
+      const int rows = min(U.band, h - y0);
       for (int r = 0; r < rows + 2; ++r) {
         if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, err, DEV_TIMEOUT_EMPTY)) {
           ok = false;
@@ -478,8 +479,8 @@ __global__ void __launch_bounds__(kDsThreads + 32, 1)
     const int band = rest % U.bands;
     rest /= U.bands;
     const int strip = rest % U.strips, n = rest / U.strips;
-    const int x0 = strip * S::TW, y0 = band * kDsBand;
-    const int rows = min(kDsBand, h - y0);
+    const int x0 = strip * S::TW, y0 = band * U.band;
+    const int rows = min(U.band, h - y0);
     const int ch0 = cb * 64 + lane_ch * (GATE ? 2 : 4);  // first output channel
     const bool cvalid = ch0 < cout;
     if (cb != wcb) {
@@ -1122,8 +1123,21 @@ static int launch_dw3x3_stream(Ctx* ctx, const TView& x, const TView& y, const f
   }
   DsUnits U;
   U.strips = (x.w + S::TW - 1) / S::TW;
-  U.bands = (x.h + kDsBand - 1) / kDsBand;
   U.cblocks = ((GATE ? x.c / 2 : x.c) + 63) / 64;
+  // Band height: a multiprocessor's time is about its rounds of units times the rows a unit
+  // stages (band + 2 halo rows); take the band that minimises that product (the tallest on a
+  // tie), so that the last round of units does not leave most multiprocessors idle.
+  U.band = kDsBand;
+  long long best = -1;
+  for (int b = kDsBand; b >= 8; --b) {
+    const long long units = (long long)x.n * U.strips * ((x.h + b - 1) / b) * U.cblocks;
+    const long long cost = (units + ctx->sms - 1) / ctx->sms * (b + 2);
+    if (best < 0 || cost < best) {
+      best = cost;
+      U.band = b;
+    }
+  }
+  U.bands = (x.h + U.band - 1) / U.band;
   U.count = x.n * U.strips * U.bands * U.cblocks;
   const int grid = std::min(U.count, ctx->sms);
   dw3x3_stream_kernel<GATE><<<grid, kDsThreads + 32, S::smem, s>>>(
