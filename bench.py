@@ -191,7 +191,7 @@ class ClockSampler:
 def cpu_sample(cfg, threads):
     """The oracle on one full-size tile (luma + chroma) of the workload: (Mpixel/s, desc)."""
     import oracle as zo
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     zo.set_threads(threads)
     op = cfg["op"]
     py, puv = syn.synthesis_params(op, cfg["seed"])
@@ -261,7 +261,8 @@ def main():
                                 device_id=torch.device("cuda", local))
 
     import zenjpegai_b200 as zj
-    from zenjpegai_b200 import _lib, sharding, synthetic as syn
+    import synthetic as syn
+    from zenjpegai_b200 import _lib, sharding
     from zenjpegai_b200.decoder import Decoder
 
     H, W, op = cfg["H"], cfg["W"], cfg["op"]
@@ -291,6 +292,9 @@ def main():
         if from_host:
             ly.copy_(ly_h, non_blocking=True)
             luv.copy_(luv_h, non_blocking=True)
+        # every rank starts from a zero picture: the reduce sums the ranks' disjoint cores, so
+        # a plane still holding last step's picture would add it in again
+        out8.zero_()
         dec.synthesize_tiles(ly, luv, mine, H, W, out=planes8, bit_depth=8)
         sharding.gather_cores(out8, dist)
         if from_host and rank == 0:

@@ -4,8 +4,8 @@
  * Plain C ABI (no C++ or torch types): opaque handles, plain pointers and sizes, an int
  * status. It replaces the float-network path of the imazen/zenjpegai crate behind the
  * crate's own interfaces; each entry names the reference interface it stands in for
- * (paths are files of that crate). A Rust `extern "C"` binding of this header is mechanical
- * (see INTEGRATION.md).
+ * (paths are files of that crate). A Rust `extern "C"` binding of this header is mechanical:
+ * one `extern "C"` declaration per function, `#[repr(C)]` mirrors of the two structs.
  *
  * Conventions
  *  - Tensors crossing the ABI are planar f32 `[c][h][w]`, like the crate's `Tensor<f32>`
@@ -87,6 +87,15 @@ int zjai_ctx_set_stream(zjai_ctx *ctx, void *cuda_stream);
  * (ZJAI_DEVICE_TIMEOUT) if a bounded wait gave up. */
 int zjai_ctx_sync(zjai_ctx *ctx);
 
+/* Limit of the convolution kernel's pipeline waits (a stage, a halo or an accumulator that
+ * does not arrive), in SM clock cycles; 0 restores the default of 4e9 cycles (about 2 s at
+ * the boost clock). A wait that runs out makes the kernel record its status word, drain the
+ * copies and MMAs it has in flight and end; the next synchronising call on the context then
+ * returns ZJAI_DEVICE_TIMEOUT, clears the status word, and the context stays usable. No
+ * counterpart in the reference (its CPU path has no device waits): a watchdog bound for
+ * callers that prefer to fail fast, and the way the timeout path is exercised in tests. */
+int zjai_ctx_set_wait_limit(zjai_ctx *ctx, int64_t cycles);
+
 /* Number of kernels this context has launched since creation (for launch accounting). */
 int64_t zjai_ctx_launch_count(const zjai_ctx *ctx);
 
@@ -147,6 +156,20 @@ int zjai_analysis_primary(zjai_net *net, const float *x, int h, int w, float *ou
 /* `AnalysisSecondary::forward` (analysis.rs:292-311): x [12][h][w] ->
  * [96][ceil(h/8)][ceil(w/8)]. */
 int zjai_analysis_secondary(zjai_net *net, const float *x, int h, int w, float *out, int mem);
+
+/* A convolution stage composed from the crate's layer primitives, for the single-layer and
+ * upsampling-stage configurations of the benchmark (the crate has no such network): a conv
+ * `conv.weight` [cout * shuffle^2][cin][k][k] (odd k, stride 1, zero pad k / 2, `conv.bias`
+ * optional) followed by `act` and, when shuffle > 1, the depth-to-space `pixel_shuffle`
+ * (src/nn/fast/layers.rs:233-261); then residual blocks `res.<i>.conv{1,2}.{weight,bias}`
+ * ([cout][cout][3][3], i = 0, 1, .. while present), each `ResidualBlock::forward`
+ * (src/model/attention.rs:36-43: conv1 -> `res_act` -> conv2, plus the block's input) with
+ * `res_act` in place of its ReLU (ZJAI_ACT_LEAKY for LeakyReLU(0.01)). Weights are packed
+ * once, GPU resident, like zjai_net_create (destroy with zjai_net_destroy). */
+int zjai_stage_create(zjai_ctx *ctx, int shuffle, int act, int res_act, const zjai_param *params,
+                      int nparams, zjai_net **out);
+/* Runs a stage: x [cin][h][w] -> out [cout][h * shuffle][w * shuffle], planar f32. */
+int zjai_stage_forward(zjai_net *net, const float *x, int c, int h, int w, float *out, int mem);
 
 /* One synthesis tile (src/tools/tiles.rs:26-32 `SynthesisTile`). */
 typedef struct {
@@ -285,12 +308,15 @@ int zjai_kernel_bench(zjai_ctx *ctx, int kind, int n, int h, int w, int c, int r
  * zjai_channel_attention for callers that must not allocate device memory during a call
  * (code running under an external allocator or a strict memory budget, callers that only
  * hand in pre-allocated buffers). qkv [3*dim][h][w], temperature [heads] and out [dim][h][w]
- * are caller-owned DEVICE buffers (planar f32); the call's scratch is one fixed-size device
- * array in the library, so dim <= 256 and dim / heads <= 64, and larger sizes return
- * ZJAI_LIMIT_EXCEEDED. The first call on a device looks the array's address up
- * (cudaGetSymbolAddress); make that first call before any stream capture. All calls share
- * the array: calls that overlap on the GPU (other streams or contexts) race. The work is
- * enqueued on the context's stream and the call returns without waiting. */
+ * are caller-owned DEVICE buffers of the context's GPU (planar f32); host memory (pageable or
+ * pinned) is rejected with ZJAI_INVALID_ARGUMENT before anything runs. The call's scratch is
+ * one fixed-size device array in the library (130 KiB, held by every GPU that loads the
+ * library), so dim <= 256 and dim / heads <= 64, and larger sizes return ZJAI_LIMIT_EXCEEDED.
+ * The first call on a device looks the array's address up (cudaGetSymbolAddress); make that
+ * first call before any stream capture. All calls share the array: calls that overlap on the
+ * GPU (other streams or contexts) race. The Gram reduction runs in a fixed order (no atomics),
+ * so repeated calls give identical results. The work is enqueued on the context's stream and
+ * the call returns without waiting. */
 int zjai_channel_attention_static(zjai_ctx *ctx, const float *qkv, int c3, int h, int w,
                                   int heads, const float *temperature, float *out);
 

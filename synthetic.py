@@ -249,3 +249,27 @@ def synthesis_params(op, seed):
 def analysis_params(op, seed):
     return (make_params(analysis_spec(op, False), seed, "AY/"),
             make_params(analysis_spec(op, True), seed, "AUV/"))
+
+
+def conv_layer_params(seed=0):
+    """conv 3x3 128 -> 128, weights N(0, 1/(9*128)), bias N(0, 0.01^2)
+    (read as standard deviation 0.01), as a conv stage's `conv.*` parameters."""
+    return {"conv.weight": normal(seed, "w", (128, 128, 3, 3),
+                                  std=float(np.sqrt(1.0 / (9 * 128)))),
+            "conv.bias": normal(seed, "b", (128,), std=0.01)}
+
+
+def upsample_stage_params(seed=1, cin=192, cout=128, nres=2):
+    """conv 3x3 cin -> 4 cout (then depth-to-space 2) and `nres` residual
+    blocks of two 3x3 convs at cout channels; He-normal weights (variance 2 / fan_in), zero
+    biases (the configuration names no bias law)."""
+    he = lambda name, shape: normal(seed, name, shape,
+                                    std=float(np.sqrt(2.0 / (shape[1] * shape[2] * shape[3]))))
+    out = {"conv.weight": he("up/w", (4 * cout, cin, 3, 3)),
+           "conv.bias": np.zeros(4 * cout, np.float32)}
+    for i in range(nres):
+        for j in (1, 2):
+            p = "res.%d.conv%d" % (i, j)
+            out[p + ".weight"] = he(p + "/w", (cout, cout, 3, 3))
+            out[p + ".bias"] = np.zeros(cout, np.float32)
+    return out

@@ -115,7 +115,7 @@ def test_convt_random(eng, cin, cout, h, w, k, op):
 def test_config1_conv_leaky(eng):
     """3x3 128->128 at 128x128, U(-1,1) input, N(0, 1/(9*128)) weights,
     N(0, 0.01^2) bias, seed 0, then LeakyReLU(0.01); compared elementwise with the oracle."""
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     import zenjpegai_b200 as zj
     x = syn.uniform(0, "x", (128, 128, 128), -1.0, 1.0)
     w = syn.normal(0, "w", (128, 128, 3, 3), std=float(np.sqrt(1.0 / (9 * 128))))
@@ -124,3 +124,29 @@ def test_config1_conv_leaky(eng):
     want = zo.leaky_relu(zo.conv2d(x, w, b, pad=(1, 1)))
     assert rel_l2(got, want) < REL_L2
     assert np.max(np.abs(got - want)) < 1e-2
+
+
+def test_device_timeout_then_recovery():
+    """Failure detection without a GPU fault: with the convolution kernel's pipeline waits
+    limited to 300 SM cycles (less than one TMA load takes to land), the first wait of every
+    CTA runs out, the kernel records its status word, drains the copies and MMAs it has in
+    flight, frees its TMEM and ends; the call reports ZJAI_DEVICE_TIMEOUT. The same context,
+    back on the default limit, then computes the layer correctly."""
+    import synthetic as syn
+    import zenjpegai_b200 as zj
+    e = zj.Engine(0, arena_bytes=256 << 20)
+    try:
+        x = syn.uniform(30, "to/x", (128, 48, 64), -1.0, 1.0)
+        w = syn.normal(30, "to/w", (128, 128, 3, 3), std=float(np.sqrt(1.0 / (9 * 128))))
+        b = syn.normal(30, "to/b", (128,), std=0.01)
+        e.set_wait_limit(300)
+        with pytest.raises(zj.ZjaiError) as err:
+            e.conv2d(x, w, b, pad=(1, 1))
+        assert err.value.status == 8  # ZJAI_DEVICE_TIMEOUT
+        assert "bounded wait" in str(err.value)
+        e.set_wait_limit(0)
+        got = e.conv2d(x, w, b, pad=(1, 1))
+        assert rel_l2(got, zo.conv2d(x, w, b, pad=(1, 1))) < REL_L2
+        e.sync()  # the status word was cleared by the failing call
+    finally:
+        e.close()

@@ -47,7 +47,7 @@ _NETS = {}
 
 def nets(eng, op):
     import zenjpegai_b200 as zj
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     if op not in _NETS:
         py, puv = syn.synthesis_params(op, 2)
         _NETS[op] = (py, puv, zj.Network(eng, zj.SYN_Y, zo.OPS[op], py),
@@ -83,7 +83,7 @@ def run_secondary(net, yl, yc, h, w):
 @pytest.mark.parametrize("op", ["sop", "bop", "hop"])
 @pytest.mark.parametrize("h,w", [(128, 192), (120, 200)])
 def test_synthesis_tile(eng, op, h, w):
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     py, puv, ny, nuv = nets(eng, op)
     lh, lw = -(-h // 16), -(-w // 16)
     ly = syn.laplace_latent(7, "ly", (160, lh, lw), 1.5)
@@ -104,7 +104,7 @@ def _synth_gpu(eng, op, H, W, tile, overlap, sv=2, sh=2):
     import ctypes
     import zenjpegai_b200 as zj
     from zenjpegai_b200 import _lib
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     py, puv, ny, nuv = nets(eng, op)
     lh, lw = -(-H // 16), -(-W // 16)
     ly = syn.laplace_latent(11, "ly", (160, lh, lw), 1.5)
@@ -152,7 +152,7 @@ def test_synthesize_fused_output(eng, op, H, W, tile, overlap, bits):
     import ctypes
     import zenjpegai_b200 as zj
     from zenjpegai_b200 import _lib
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     py, puv, ny, nuv = nets(eng, op)
     lh, lw = -(-H // 16), -(-W // 16)
     ly = syn.laplace_latent(12, "ly", (160, lh, lw), 1.5)
@@ -188,7 +188,7 @@ def test_output_stage_bit_exact(eng):
     import ctypes
     import zenjpegai_b200 as zj
     from zenjpegai_b200 import _lib
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     h, w = 135, 241
     y = syn.uniform(3, "y", (h, w), -5.0, 260.0)
     u = syn.uniform(3, "u", ((h + 1) // 2, (w + 1) // 2), -5.0, 260.0)
@@ -211,7 +211,7 @@ def test_output_stage_bit_exact(eng):
 def test_layer_norm(eng, c):
     # c <= 256: pixel-segment kernel (8 / 16 / 32 lanes per pixel, idle lanes at 40 and 200);
     # 384: warp-per-pixel kernel
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     x = syn.normal(5, "x", (c, 23, 37), std=3.0, mean=0.5)
     wt = syn.normal(5, "w", (c,), std=0.1, mean=1.0)
     b = syn.normal(5, "b", (c,), std=0.05)
@@ -223,7 +223,7 @@ def test_layer_norm(eng, c):
 def test_depthwise(eng, c, h, w):
     # row-streaming kernel: 64-column strips, 64-row bands, 64-channel blocks (ragged at
     # 40 / 8 channels, 130 columns, 70 and 131 rows)
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     x = syn.normal(6, "x", (c, h, w))
     wt = syn.normal(6, "w", (c, 1, 3, 3), std=0.3)
     got = eng.depthwise3x3(x, wt)
@@ -234,7 +234,7 @@ def test_depthwise(eng, c, h, w):
 @pytest.mark.parametrize("c,h,w", [(1024, 19, 33), (512, 70, 97), (48, 9, 40), (16, 3, 2)])
 def test_depthwise_elu_gate(eng, c, h, w):
     # FFN depthwise + ELU gate fused: 32-column strips, two 64-channel slabs per block
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     x = syn.normal(7, "x", (c, h, w))
     wt = syn.normal(7, "w", (c, 1, 3, 3), std=0.3)
     got = eng.depthwise3x3_elu_gate(x, wt)
@@ -254,7 +254,7 @@ def test_depthwise_elu_gate(eng, c, h, w):
 def test_transformer_ffn(eng, dim, hidden, h, w):
     # fused FFN kernel (project_in -> depthwise 3x3 + ELU gate -> project_out + residual in one
     # tcgen05 kernel) after the layer norm, against the oracle's layers composed
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     x = syn.normal(9, "x", (dim, h, w))
     nw = syn.uniform(9, "nw", (dim,), 0.5, 1.5)
     nb = syn.normal(9, "nb", (dim,), std=0.1)
@@ -275,7 +275,7 @@ def test_transformer_ffn(eng, dim, hidden, h, w):
 @pytest.mark.parametrize("dim,h,w", [(128, 40, 52), (64, 64, 64), (96, 17, 29)])
 def test_channel_attention(eng, dim, h, w):
     # 128 / 64: register-tiled Gram and per-head apply (head width 32 / 16); 96: generic kernels
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     qkv = syn.normal(8, "qkv", (3 * dim, h, w))
     t = syn.uniform(8, "t", (4,), 0.5, 2.0)
     got = eng.channel_attention(qkv, 4, t)
@@ -288,7 +288,7 @@ def test_analysis(eng, op):
     import ctypes
     import zenjpegai_b200 as zj
     from zenjpegai_b200 import _lib
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     pa, pauv = syn.analysis_params(op, 4)
     h, w = 120, 200
     x = np.floor(syn.uniform(9, "rgb", (1, h, w), 0.0, 256.0)).astype(np.float32)
@@ -309,7 +309,7 @@ def test_analysis(eng, op):
 def test_model_errors(eng):
     """Missing / mis-shaped parameters fail like the crate's loaders (Error::Model)."""
     import zenjpegai_b200 as zj
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     py, _ = syn.synthesis_params("sop", 2)
     bad = dict(py)
     del bad["conv3.bias"]
@@ -329,7 +329,7 @@ def test_cancel_and_reuse(eng):
     import ctypes
     import zenjpegai_b200 as zj
     from zenjpegai_b200.decoder import Decoder
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     py, puv, ny, nuv = nets(eng, "sop")
     dec = Decoder.__new__(Decoder)
     dec.engine, dec.op, dec.net_y, dec.net_uv = eng, zj.SOP, ny, nuv
@@ -350,7 +350,7 @@ def test_arena_limit_and_bad_geometry():
     geometry with ZJAI_INVALID_DATA (tiles.rs:71-76); the context remains usable."""
     import zenjpegai_b200 as zj
     from zenjpegai_b200.decoder import Decoder
-    from zenjpegai_b200 import synthetic as syn
+    import synthetic as syn
     small = zj.Engine(0, arena_bytes=64 << 20)
     py, puv = syn.synthesis_params("hop", 3)
     dec = Decoder(small, "hop", py, puv)

@@ -15,7 +15,7 @@ import torch.multiprocessing as mp
 
 import oracle as zo
 from zenjpegai_b200 import sharding
-from zenjpegai_b200 import synthetic as syn
+import synthetic as syn
 
 H, W, TILE, OVERLAP = 160, 272, 96, 16
 

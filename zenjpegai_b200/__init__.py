@@ -27,7 +27,7 @@ from ._lib import (ACT_LEAKY, ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SIGMOID, ANA_UV
                    HOP, SOP, SYN_UV, SYN_Y, ZjaiError, check)
 
 __all__ = ["Engine", "ZjaiError", "SOP", "BOP", "HOP", "SYN_Y", "SYN_UV", "ANA_Y", "ANA_UV",
-           "ACT_NONE", "ACT_RELU", "ACT_LEAKY", "ACT_SIGMOID", "ACT_RELU6", "Network",
+           "ACT_NONE", "ACT_RELU", "ACT_LEAKY", "ACT_SIGMOID", "ACT_RELU6", "Network", "Stage",
            "synthesis_tiles", "synth_out_size", "version"]
 
 _lib.lib()  # load now: importing the package without its CUDA library is an error
@@ -93,6 +93,10 @@ class Engine:
 
     def sync(self):
         check(_lib.lib().zjai_ctx_sync(self.handle))
+
+    def set_wait_limit(self, cycles):
+        """Limit of the convolution kernel's pipeline waits in SM cycles (0: default)."""
+        check(_lib.lib().zjai_ctx_set_wait_limit(self.handle, int(cycles)))
 
     @property
     def launch_count(self):
@@ -201,6 +205,23 @@ def synthesis_tiles(height, width, latent_h, latent_w, tile_size=0, overlap=0):
     return [{k: getattr(t, k) for k, _ in _lib.Tile._fields_} for t in arr]
 
 
+def _param_array(params):
+    """ctypes array of zjai_param over float32 copies of `params` (name -> array), and the
+    objects that must stay alive while it is used."""
+    arrs = {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in params.items()}
+    ps = (_lib.Param * max(1, len(arrs)))()
+    keep = [arrs]
+    for i, (k, v) in enumerate(arrs.items()):
+        nm = k.encode()
+        keep.append(nm)
+        ps[i].name = nm
+        ps[i].ndim = v.ndim
+        for d in range(4):
+            ps[i].shape[d] = v.shape[d] if d < v.ndim else 0
+        ps[i].data = v.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    return ps, len(arrs), keep
+
+
 class Network:
     """A synthesis / analysis network with GPU-resident packed weights
     (`SynthesisPrimary::load` etc.). `params` maps checkpoint names to float32 arrays."""
@@ -209,20 +230,9 @@ class Network:
         self.engine = engine
         self.kind = kind
         self.op = op
-        arrs = {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in params.items()}
-        ps = (_lib.Param * len(arrs))()
-        keep = []
-        for i, (k, v) in enumerate(arrs.items()):
-            nm = k.encode()
-            keep.append(nm)
-            ps[i].name = nm
-            ps[i].ndim = v.ndim
-            for d in range(4):
-                ps[i].shape[d] = v.shape[d] if d < v.ndim else 0
-            ps[i].data = v.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        ps, n, keep = _param_array(params)
         h = ctypes.c_void_p()
-        check(_lib.lib().zjai_net_create(engine.handle, kind, op, ps, len(arrs),
-                                         ctypes.byref(h)))
+        check(_lib.lib().zjai_net_create(engine.handle, kind, op, ps, n, ctypes.byref(h)))
         self.handle = h
 
     def close(self):
@@ -235,3 +245,33 @@ class Network:
             self.close()
         except Exception:
             pass
+
+
+class Stage(Network):
+    """A conv stage (zjai_stage_create): conv k x k (+ `act`, + depth-to-space `shuffle`) then
+    the residual blocks `res.<i>` with `res_act` between their convs."""
+
+    def __init__(self, engine, params, shuffle=1, act=ACT_NONE, res_act=ACT_RELU):
+        self.engine = engine
+        self.kind, self.op = 4, 0
+        w = params["conv.weight"]
+        self.cin = int(w.shape[1])
+        self.cout = int(w.shape[0]) // (shuffle * shuffle)
+        self.shuffle = shuffle
+        ps, n, keep = _param_array(params)
+        h = ctypes.c_void_p()
+        check(_lib.lib().zjai_stage_create(engine.handle, shuffle, act, res_act, ps, n,
+                                           ctypes.byref(h)))
+        self.handle = h
+
+    def forward(self, x, out=None):
+        c, h, w = x.shape
+        shape = (self.cout, h * self.shuffle, w * self.shuffle)
+        if out is None:
+            out = _like(x, shape)
+        px, mem = _arg(x)
+        po, m2 = _arg(out, shape)
+        if mem != m2:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        check(_lib.lib().zjai_stage_forward(self.handle, px, c, h, w, po, mem))
+        return out

@@ -71,6 +71,7 @@ def lib():
     L.zjai_ctx_destroy.argtypes = [_vp]
     L.zjai_ctx_set_stream.argtypes = [_vp, _vp]
     L.zjai_ctx_sync.argtypes = [_vp]
+    L.zjai_ctx_set_wait_limit.argtypes = [_vp, ctypes.c_int64]
     L.zjai_ctx_launch_count.argtypes = [_vp]
     L.zjai_ctx_launch_count.restype = ctypes.c_int64
     L.zjai_ctx_profile.argtypes = [_vp, _i]
@@ -84,6 +85,9 @@ def lib():
     L.zjai_synthesis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _vp, _i]
     L.zjai_analysis_primary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
     L.zjai_analysis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
+    L.zjai_stage_create.argtypes = [_vp, _i, _i, _i, ctypes.POINTER(Param), _i,
+                                     ctypes.POINTER(_vp)]
+    L.zjai_stage_forward.argtypes = [_vp, _vp, _i, _i, _i, _vp, _i]
     L.zjai_synthesis_tiles.argtypes = [_i] * 6 + [ctypes.POINTER(Tile), _i, ctypes.POINTER(_i)]
     L.zjai_synthesize.argtypes = [_vp, _vp, _vp, _vp, _vp] + [_i] * 10 + [_vp, _vp, _vp, _i, _vp]
     L.zjai_synthesize_q.argtypes = [_vp, _vp, _vp, _vp, _vp] + [_i] * 11 + [_vp, _vp, _vp, _i,

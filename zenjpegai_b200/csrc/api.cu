@@ -173,6 +173,13 @@ int zjai_ctx_sync(zjai_ctx* ctx) {
   return ctx_check_status(ctx);
 }
 
+int zjai_ctx_set_wait_limit(zjai_ctx* ctx, int64_t cycles) {
+  if (!ctx) return fail(ZJAI_INVALID_ARGUMENT, "null context");
+  if (cycles < 0) return fail(ZJAI_INVALID_ARGUMENT, "wait limit must be >= 0 (0: default)");
+  ctx->wait_cycles = cycles;
+  return ZJAI_OK;
+}
+
 int64_t zjai_ctx_launch_count(const zjai_ctx* ctx) { return ctx ? (int64_t)ctx->launches : 0; }
 
 int zjai_ctx_profile(zjai_ctx* ctx, int enable) {

@@ -10,9 +10,10 @@
 // cudaGetSymbolAddress; the array's name is not a device address in host code.
 //
 // Limits: dim = c3 / 3 <= 256 and per-head channels c = dim / heads <= 64. All calls on a GPU
-// share the array and it keeps the previous call's contents (the accumulators are cleared at
-// the start of every call), so calls whose work overlaps on the GPU (different streams or
-// contexts) race on it.
+// share the array and it keeps the previous call's contents; every call writes each scratch
+// entry before reading it (nothing is accumulated across calls), but calls whose work overlaps
+// on the GPU (different streams or contexts) race on it. The Gram is reduced in a fixed order
+// (no atomics), so a call gives the same bits every time.
 #include <mutex>
 
 #include "api_common.h"
@@ -26,7 +27,7 @@ constexpr int kStaticMaxC = 64;
 // gram: dim * c, squared norms: 2 * dim, softmax rows: dim * c
 constexpr int kStaticScratchFloats = 2 * kStaticMaxDim * kStaticMaxC + 2 * kStaticMaxDim;
 
-// held by every GPU that loads the library, until the process exits (132 KiB)
+// held by every GPU that loads the library, until the process exits (33280 floats = 130 KiB)
 static __device__ __align__(256) float g_attention_scratch[kStaticScratchFloats];
 
 constexpr int kMaxDevices = 64;
@@ -46,63 +47,81 @@ int scratch_address(int device, float** out) {
   return ZJAI_OK;
 }
 
-__global__ void zero_kernel(float* p, int n) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = 0.f;
+// ZJAI_OK when `p` is device (or managed) memory usable on `device`, ZJAI_INVALID_ARGUMENT
+// for host memory or another GPU's memory.
+int device_buffer(int device, const void* p, const char* what) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();  // clear the error the query recorded
+    return fail(ZJAI_INVALID_ARGUMENT,
+                std::string("zjai_channel_attention_static: ") + what + " is not a device pointer");
+  }
+  if (at.type == cudaMemoryTypeManaged) return ZJAI_OK;
+  if (at.type != cudaMemoryTypeDevice || at.device != device)
+    return fail(ZJAI_INVALID_ARGUMENT, std::string("zjai_channel_attention_static: ") + what +
+                                           " must be device memory of the context's GPU");
+  return ZJAI_OK;
 }
 
-constexpr int kPix = 64;  // pixels per shared-memory chunk of the Gram kernel
+constexpr int kPix = 64;   // pixels per shared-memory chunk of the Gram kernel
+constexpr int kGramRows = 16;  // Gram rows (query channels) per block
 
-// gram[h][i][j] += sum_p q[h*c+i][p] * k[h*c+j][p]; sq[ch] += x[ch][p]^2 for q and k rows.
-// Block (pixel chunk group, head): q and k rows of the head staged per 64-pixel chunk.
+// gram[h][i][j] = sum_p q[h*c+i][p] * k[h*c+j][p] and the squared norms of the q and k rows,
+// in a fixed order: block (row group, head) owns kGramRows rows i of the head's c x c Gram and
+// walks every pixel of the picture in 64-pixel chunks; each thread keeps its (up to four)
+// entries in registers and adds the chunks' partial sums in pixel order, so every call gives
+// the same bits. Row group 0 also writes the head's k-row norms, every group its q-row norms.
 __global__ void __launch_bounds__(256) static_gram_kernel(const float* __restrict__ qkv, int dim,
                                                           int c, long long npix, float* gram,
-                                                          float* sq, int chunks_per_block) {
-  __shared__ float sq_s[2 * kStaticMaxC][kPix + 1];
-  const int hd = blockIdx.y;
-  const float* q = qkv + (long long)hd * c * npix;
+                                                          float* sq) {
+  __shared__ float qs[kGramRows][kPix + 1];
+  __shared__ float ks[kStaticMaxC][kPix + 1];
+  const int hd = blockIdx.y, i0 = blockIdx.x * kGramRows;
+  const int rows = min(kGramRows, c - i0);
+  const float* q = qkv + ((long long)hd * c + i0) * npix;
   const float* k = qkv + ((long long)dim + (long long)hd * c) * npix;
-  const int entries = c * c;
-  float acc[16];
-#pragma unroll
-  for (int e = 0; e < 16; ++e) acc[e] = 0.f;
-  float sacc = 0.f;
-  for (int ch = 0; ch < chunks_per_block; ++ch) {
-    const long long p0 = ((long long)blockIdx.x * chunks_per_block + ch) * kPix;
-    if (p0 >= npix) break;
+  const int entries = rows * c;  // <= 16 * 64 = 1024 = 4 per thread
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float sacc = 0.f;  // thread t < rows + c: squared norm of q row t (t < rows) or k row t - rows
+  for (long long p0 = 0; p0 < npix; p0 += kPix) {
     __syncthreads();
-    for (int t = threadIdx.x; t < 2 * c * kPix; t += blockDim.x) {
-      const int r = t / kPix, pp = t % kPix;
+    for (int t = threadIdx.x; t < (rows + c) * kPix; t += blockDim.x) {
+      const int r = t / kPix, pp = t - r * kPix;
       const long long p = p0 + pp;
-      const float* src = r < c ? q + (long long)r * npix : k + (long long)(r - c) * npix;
-      sq_s[r][pp] = p < npix ? src[p] : 0.f;
+      float v = 0.f;
+      if (p < npix) v = r < rows ? q[(long long)r * npix + p] : k[(long long)(r - rows) * npix + p];
+      if (r < rows)
+        qs[r][pp] = v;
+      else
+        ks[r - rows][pp] = v;
     }
     __syncthreads();
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
+    for (int e = 0; e < 4; ++e) {
       const int id = threadIdx.x + e * 256;
       if (id < entries) {
-        const int i = id / c, j = id % c;
+        const int i = id / c, j = id - (id / c) * c;
         float s = 0.f;
-        for (int pp = 0; pp < kPix; ++pp) s = fmaf(sq_s[i][pp], sq_s[c + j][pp], s);
+        for (int pp = 0; pp < kPix; ++pp) s = fmaf(qs[i][pp], ks[j][pp], s);
         acc[e] += s;
       }
     }
-    if (threadIdx.x < 2 * c) {
+    if (threadIdx.x < rows + c) {
+      const int r = threadIdx.x;
+      const float* row = r < rows ? qs[r] : ks[r - rows];
       float s = 0.f;
-      for (int pp = 0; pp < kPix; ++pp) s = fmaf(sq_s[threadIdx.x][pp], sq_s[threadIdx.x][pp], s);
+      for (int pp = 0; pp < kPix; ++pp) s = fmaf(row[pp], row[pp], s);
       sacc += s;
     }
   }
 #pragma unroll
-  for (int e = 0; e < 16; ++e) {
+  for (int e = 0; e < 4; ++e) {
     const int id = threadIdx.x + e * 256;
-    if (id < entries) atomicAdd(gram + (long long)hd * entries + id, acc[e]);
+    if (id < entries) gram[((long long)hd * c + i0) * c + id] = acc[e];
   }
-  if (threadIdx.x < 2 * c) {
-    const int r = threadIdx.x;
-    const int row = r < c ? hd * c + r : dim + hd * c + (r - c);
-    atomicAdd(sq + row, sacc);
-  }
+  if (threadIdx.x < rows) sq[hd * c + i0 + threadIdx.x] = sacc;
+  else if (blockIdx.x == 0 && threadIdx.x < rows + c)
+    sq[dim + hd * c + (threadIdx.x - rows)] = sacc;
 }
 
 // Row softmax of the normalised Gram times the head's temperature (math.rs:549-570).
@@ -166,6 +185,10 @@ extern "C" int zjai_channel_attention_static(zjai_ctx* ctx, const float* qkv, in
     return fail(ZJAI_LIMIT_EXCEEDED,
                 "zjai_channel_attention_static: dim " + std::to_string(dim) + " / head size " +
                     std::to_string(c) + " exceed the static scratch (dim <= 256, head <= 64)");
+  // the kernels dereference these pointers: host memory (pageable or pinned) is refused here
+  ZJAI_TRY(device_buffer(ctx->device, qkv, "qkv"));
+  ZJAI_TRY(device_buffer(ctx->device, temperature, "temperature"));
+  ZJAI_TRY(device_buffer(ctx->device, out, "out"));
   float* scratch = nullptr;
   ZJAI_TRY(scratch_address(ctx->device, &scratch));
   float* gram = scratch;
@@ -173,14 +196,11 @@ extern "C" int zjai_channel_attention_static(zjai_ctx* ctx, const float* qkv, in
   float* attn = sq + 2 * (size_t)dim;
   const long long npix = (long long)h * w;
   cudaStream_t s = ctx->stream;
-  zero_kernel<<<16, 256, 0, s>>>(gram, dim * c + 2 * dim);
-  const long long chunks = (npix + kPix - 1) / kPix;
-  const int cpb = (int)std::max<long long>(1, chunks / 128);
-  dim3 g1((unsigned)((chunks + cpb - 1) / cpb), heads);
-  static_gram_kernel<<<g1, 256, 0, s>>>(qkv, dim, c, npix, gram, sq, cpb);
+  dim3 g1((unsigned)((c + kGramRows - 1) / kGramRows), heads);
+  static_gram_kernel<<<g1, 256, 0, s>>>(qkv, dim, c, npix, gram, sq);
   static_softmax_kernel<<<(dim + 127) / 128, 128, 0, s>>>(gram, sq, temperature, attn, dim, c);
   dim3 g3((unsigned)((npix + 255) / 256), heads);
   static_apply_kernel<<<g3, 256, 0, s>>>(qkv, attn, out, dim, c, npix);
-  ctx->launches += 4;
+  ctx->launches += 3;
   return cuda_check(cudaGetLastError(), "attention launch");
 }

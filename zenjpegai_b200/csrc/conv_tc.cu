@@ -360,6 +360,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // limit of the pipeline waits (the drain waits keep kWaitCycles)
+  const long long wl = a.wait_cycles > 0 ? a.wait_cycles : kWaitCycles;
 
   if (threadIdx.x == 0) {
     // the MMA issuers' commits arrive on the empty, accumulator-full and drain barriers
@@ -419,7 +421,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const int nt = tc.n0 / a.bn;
         const __half* wbase = a.wblk + (size_t)tc.img * a.wblk_img + (size_t)nt * brows * a.kc;
         for (int cc = 0; cc < a.cchunks; ++cc) {
-          if (!mbar_wait_idle(heb + 8u * hs, hphase ^ 1u, abort_flag, a.err, DEV_TIMEOUT_EMPTY, 64))
+          if (!mbar_wait_idle(heb + 8u * hs, hphase ^ 1u, abort_flag, a.err, DEV_TIMEOUT_EMPTY, 64, wl))
             goto halo_done;
           mbar_arrive_expect_tx(hfb + 8u * hs, hbox);
           tma_load_4d(h_base + hs * a.halo_bytes, &tmA, hfb + 8u * hs, cc * a.kc,
@@ -431,7 +433,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           }
           for (int tap = 0; tap < a.taps; ++tap) {
             if (!mbar_wait_idle(eb_base + 8u * stage, phase ^ 1u, abort_flag, a.err,
-                                DEV_TIMEOUT_EMPTY, 64))
+                                DEV_TIMEOUT_EMPTY, 64, wl))
               goto halo_done;
             const uint32_t fb = fb_base + 8u * stage;
             mbar_arrive_expect_tx(fb, b_bytes);
@@ -481,7 +483,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             cc = (int)(e >> 26);
           }
           if (!mbar_wait_idle(eb_base + 8u * stage, phase ^ 1u, abort_flag, a.err,
-                              DEV_TIMEOUT_EMPTY, 64))
+                              DEV_TIMEOUT_EMPTY, 64, wl))
             goto producer_done;
           const uint32_t sA = s_base + stage * stage_bytes;
           const uint32_t fb = fb_base + 8u * stage;
@@ -555,13 +557,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       uint32_t acc_phase = 0;
       for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
         if (!mbar_wait_idle(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, a.err,
-                            DEV_TIMEOUT_ACC_EMPTY, 64))
+                            DEV_TIMEOUT_ACC_EMPTY, 64, wl))
           break;
         tc_fence_after();
         const uint32_t d0 = tmem_base + (uint32_t)(acc * a.msub * a.bn) + d_off;
         bool ok = true;
         for (int cc = 0; cc < a.cchunks && ok; ++cc) {
-          if (!mbar_wait(hfb + 8u * hs, hphase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
+          if (!mbar_wait(hfb + 8u * hs, hphase, abort_flag, a.err, DEV_TIMEOUT_FULL, wl)) {
             ok = false;
             break;
           }
@@ -572,7 +574,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           uint64_t da = dH0 + (uint64_t)hs * dslot;
           int kx = 0;
           for (int tap = 0; tap < a.taps; ++tap) {
-            if (!mbar_wait(fb_base + 8u * stage, phase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
+            if (!mbar_wait(fb_base + 8u * stage, phase, abort_flag, a.err, DEV_TIMEOUT_FULL, wl)) {
               ok = false;
               break;
             }
@@ -624,7 +626,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       uint32_t acc_phase = 0;
       for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
         if (!mbar_wait_idle(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, a.err,
-                            DEV_TIMEOUT_ACC_EMPTY, 64))
+                            DEV_TIMEOUT_ACC_EMPTY, 64, wl))
           break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * a.msub * a.bn) + d_off;
@@ -633,7 +635,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         bool ok = true;
         uint32_t accum = 0u;  // the tile's first UMMA overwrites the accumulator
         for (int i = k0; i < k1; ++i) {
-          if (!mbar_wait(fb_base + 8u * stage, phase, abort_flag, a.err, DEV_TIMEOUT_FULL)) {
+          if (!mbar_wait(fb_base + 8u * stage, phase, abort_flag, a.err, DEV_TIMEOUT_FULL, wl)) {
             ok = false;
             break;
           }
@@ -741,7 +743,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
       if (!mbar_wait_idle(smem_u32(&accf[acc]), acc_phase, abort_flag, a.err, DEV_TIMEOUT_ACC_FULL,
-                          128))
+                          128, wl))
         break;
       tc_fence_after();
       const TileCoord tc = decode_tile(a, t);
@@ -785,7 +787,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             res_issue(decode_tile(a, tnext), ns, nc);
           }
           const uint32_t sl = ruse & 1u;
-          mbar_wait(rb0 + 8u * sl, (ruse >> 1) & 1u, abort_flag, a.err, DEV_TIMEOUT_FULL);
+          mbar_wait(rb0 + 8u * sl, (ruse >> 1) & 1u, abort_flag, a.err, DEV_TIMEOUT_FULL, wl);
           rs1 = reinterpret_cast<const uint4*>(rslots + sl * kEpiSlotBytes + lane * 32);
           rs2 = rs1 + kEpiStagingBytes / 16;
           ++ruse;

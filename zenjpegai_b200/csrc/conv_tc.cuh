@@ -109,6 +109,9 @@ struct ConvArgs {
   int qbytes;
   float qmax;
   int* err;
+  // limit of the kernel's pipeline waits in SM cycles (0: the default of about 2 s); a wait
+  // that runs out records DEV_TIMEOUT_* in *err and the CTA drains its copies and MMAs and ends
+  long long wait_cycles;
 };
 
 // warp 0 TMA, warp 1 MMA issuer 0, then kEpiWarpgroups warpgroups of epilogue (warpgroup g

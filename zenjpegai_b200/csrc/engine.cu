@@ -521,6 +521,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   if ((L.R & (L.R - 1)) != 0) return fail(ZJAI_UNSUPPORTED, "conv: shuffle factor must be a power of two");
   a.cph = L.cph;
   a.err = ctx->d_err;
+  a.wait_cycles = ctx->wait_cycles;
   if (!o.planar) {
     a.out = o.out.p;
     a.out_pix = o.out.pix;

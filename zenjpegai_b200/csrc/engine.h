@@ -68,6 +68,9 @@ struct Ctx {
   Arena arena2;  // work of `stream2` (chroma synthesis runs beside luma)
   Arena* cur_arena = nullptr;  // arena of the network runner currently launching (or null)
   int* d_err = nullptr;  // kernel status word
+  // limit of the convolution kernel's pipeline waits in SM cycles (0: the kernel's default of
+  // about 2 s), zjai_ctx_set_wait_limit
+  long long wait_cycles = 0;
   std::atomic<long long> launches{0};
   // driver entry point
   void* encode_fn = nullptr;

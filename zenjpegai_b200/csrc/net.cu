@@ -255,6 +255,50 @@ int load_network(Ctx* ctx, int kind, int op, const zjai_param* params, int npara
   return ZJAI_OK;
 }
 
+// A conv stage composed from the crate's primitives: "conv" (k x k, stride 1, pad k / 2, bias
+// optional, `shuffle` folded into its columns) followed by the residual blocks "res.<i>"
+// (ResidualBlock::load, attention.rs:22-34) while their parameters are present.
+int load_stage(Ctx* ctx, int shuffle, int act, int res_act, const zjai_param* params,
+               int nparams, Net** out) {
+  *out = nullptr;
+  if (shuffle != 1 && shuffle != 2 && shuffle != 4)
+    return fail(ZJAI_INVALID_ARGUMENT, "stage: shuffle must be 1, 2 or 4");
+  if (act < ACT_NONE || act > ACT_RELU6 || res_act < ACT_NONE || res_act > ACT_RELU6)
+    return fail(ZJAI_INVALID_ARGUMENT, "stage: unknown activation");
+  if (nparams < 0 || (nparams > 0 && !params)) return fail(ZJAI_INVALID_ARGUMENT, "params");
+  std::unique_ptr<Net> n(new Net());
+  n->ctx = ctx;
+  n->kind = kStageKind;
+  Loader L;
+  L.net = n.get();
+  for (int i = 0; i < nparams; ++i) {
+    if (!params[i].name) return fail(ZJAI_MODEL, "parameter without a name");
+    L.byname[params[i].name] = &params[i];
+  }
+  auto it = L.byname.find("conv.weight");
+  if (it == L.byname.end() || it->second->ndim != 4)
+    return fail(ZJAI_MODEL, "conv.weight: missing or not 4-D");
+  const int64_t* sh = it->second->shape;
+  const int oc = (int)sh[0], cin = (int)sh[1], k = (int)sh[2];
+  if (oc <= 0 || cin <= 0 || k <= 0 || sh[3] != k || k % 2 == 0 || oc % (shuffle * shuffle))
+    return fail(ZJAI_MODEL, "conv.weight: needs [cout * shuffle^2][cin][k][k] with odd k");
+  const int cout = oc / (shuffle * shuffle);
+  ZJAI_TRY(L.conv("conv", cin, oc, k, k, 1, k / 2, 1, L.has("conv.bias"), nullptr, shuffle));
+  int nres = 0;
+  while (L.has("res." + std::to_string(nres) + ".conv1.weight")) {
+    ZJAI_TRY(L.rb("res." + std::to_string(nres), cout));
+    ++nres;
+  }
+  n->st_act = act;
+  n->st_shuffle = shuffle;
+  n->st_res_act = res_act;
+  n->st_nres = nres;
+  n->st_cin = cin;
+  n->st_cout = cout;
+  *out = n.release();
+  return ZJAI_OK;
+}
+
 Net::~Net() {
   for (auto& kv : convs) free_conv(&kv.second);
   for (auto& kv : ffns) free_ffn(&kv.second);
@@ -343,13 +387,15 @@ int Runner::resau(const std::string& p, const TView& x, const TView& a, int ch, 
 }
 
 // ResidualBlock::forward (attention.rs:36-43): conv2(relu(conv1 x)) + x -> *y (may alias x).
-int Runner::rb(const std::string& p, const TView& x, const TView& y, const TView* relu6_out) {
+// `act` replaces the ReLU between the convs (LeakyReLU in the conv stages of BASELINE configs).
+int Runner::rb(const std::string& p, const TView& x, const TView& y, const TView* relu6_out,
+               int act) {
   ArenaMark mark(arena);
   TView t;
   ZJAI_TRY(alloc(x.h, x.w, x.c, &t));
   ConvOut o1;
   o1.out = t;
-  o1.act1 = ACT_RELU;
+  o1.act1 = act;
   ZJAI_TRY(conv(p + ".conv1", x, o1));
   ConvOut o2;
   o2.out = y;
@@ -802,6 +848,39 @@ int Runner::analysis(const TView& x, int h, int w, float* out) {
   of.p_row = w4;
   of.p_img = 160LL * h4 * w4;
   return conv("conv5", x4, of);
+}
+
+// Conv stage: the first conv (activation, pixel shuffle in its epilogue), then the residual
+// blocks in place. Without residual blocks the conv's epilogue writes the planar output.
+int Runner::stage(const TView& x, float* out) {
+  const ConvLayer* L0 = layer("conv");
+  if (!L0) return fail(ZJAI_MODEL, "conv: layer not loaded");
+  int oh, ow;
+  ZJAI_TRY(out_extent("conv", x.h, x.w, &oh, &ow));
+  const int c = net->st_cout;
+  if (net->st_nres == 0) {
+    ConvOut o;
+    o.act1 = net->st_act;
+    o.planar = true;
+    o.pout = out;
+    o.p_plane = (long long)oh * ow;
+    o.p_row = ow;
+    o.p_img = (long long)c * oh * ow;
+    return conv("conv", x, o);
+  }
+  TView y;
+  ZJAI_TRY(alloc(oh, ow, c, &y));
+  ConvOut o;
+  o.out = y;
+  o.act1 = net->st_act;
+  ZJAI_TRY(conv("conv", x, o));
+  for (int i = 0; i < net->st_nres; ++i) {
+    ZJAI_TRY(stop_check());
+    ZJAI_TRY(rb("res." + std::to_string(i), y, y, nullptr, net->st_res_act));
+  }
+  launch_nhwc_to_planar(y, out, stream);
+  ctx->launches++;
+  return cuda_check(cudaGetLastError(), "nhwc_to_planar");
 }
 
 // ---------------------------------------------------------------------------------------------

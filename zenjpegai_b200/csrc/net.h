@@ -20,8 +20,14 @@ struct Net {
   // fused FFN weights of each transformer block whose shape the fused kernel takes (keyed by
   // the block prefix)
   std::map<std::string, FfnLayer> ffns;
+  // conv stage (zjai_stage_create): activation of the first conv, its pixel shuffle, the
+  // activation inside the residual blocks, their number, input and output channels
+  int st_act = 0, st_shuffle = 1, st_res_act = 0, st_nres = 0, st_cin = 0, st_cout = 0;
   ~Net();
 };
+
+// Net::kind of a conv stage (not one of the crate's network kinds)
+constexpr int kStageKind = 4;
 
 // Where a synthesis network's final planar output goes.
 struct FinalOut {
@@ -70,7 +76,8 @@ struct Runner {
   int stop_check();
 
   int resau(const std::string& p, const TView& x, const TView& a, int ch, int cw, TView* y);
-  int rb(const std::string& p, const TView& x, const TView& y, const TView* relu6_out = nullptr);
+  int rb(const std::string& p, const TView& x, const TView& y, const TView* relu6_out = nullptr,
+         int act = ACT_RELU);
   int cab(const std::string& p, const TView& x, const TView& out, const TView* a_out);
   int tb(const std::string& p, const TView& x);
   int tam(const std::string& p, const TView& x, bool ds, int ch, int cw, TView* y, TView* a_out);
@@ -80,6 +87,8 @@ struct Runner {
   int primary(const TView& y, int h, int w, const FinalOut& fo);
   int secondary(const TView& cat, const TView& x144, int h, int w, const FinalOut& fo);
   int analysis(const TView& x, int h, int w, float* out);
+  // conv stage: x (NHWC, st_cin channels) -> planar f32 out [st_cout][h * r][w * r]
+  int stage(const TView& x, float* out);
 };
 
 struct ArenaMark {
@@ -90,6 +99,8 @@ struct ArenaMark {
 };
 
 int load_network(Ctx* ctx, int kind, int op, const zjai_param* params, int nparams, Net** out);
+int load_stage(Ctx* ctx, int shuffle, int act, int res_act, const zjai_param* params,
+               int nparams, Net** out);
 int synthesis_tiles(int height, int width, int latent_h, int latent_w, int tile_size,
                     int overlap, std::vector<zjai_tile>* out);
 void synth_out_size(int kind, int op, int h, int w, int* oh, int* ow);

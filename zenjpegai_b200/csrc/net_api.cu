@@ -280,6 +280,40 @@ int zjai_analysis_secondary(zjai_net* net, const float* x, int h, int w, float* 
   return analysis_entry(net, ZJAI_ANA_UV, 12, 96, 8, x, h, w, out, mem);
 }
 
+int zjai_stage_create(zjai_ctx* ctx, int shuffle, int act, int res_act, const zjai_param* params,
+                      int nparams, zjai_net** out) {
+  if (!out) return fail(ZJAI_INVALID_ARGUMENT, "null output handle");
+  *out = nullptr;
+  ZJAI_TRY(ctx_enter(ctx));
+  Net* n = nullptr;
+  ZJAI_TRY(load_stage(ctx, shuffle, act, res_act, params, nparams, &n));
+  *out = reinterpret_cast<zjai_net*>(n);
+  return ZJAI_OK;
+}
+
+int zjai_stage_forward(zjai_net* net, const float* x, int c, int h, int w, float* out, int mem) {
+  ZJAI_TRY(net_enter(net));
+  Net* n = reinterpret_cast<Net*>(net);
+  Ctx* ctx = n->ctx;
+  if (n->kind != kStageKind) return fail(ZJAI_INVALID_ARGUMENT, "not a conv stage");
+  if (!x || !out || h <= 0 || w <= 0 || c != n->st_cin)
+    return fail(ZJAI_INVALID_ARGUMENT, "stage: input must be [" + std::to_string(n->st_cin) +
+                                           "][h][w] and an output given");
+  ArenaScope scope(ctx);
+  const float* dx;
+  ZJAI_TRY(stage_in(ctx, x, (size_t)c * h * w, mem, &dx));
+  TView t;
+  ZJAI_TRY(planar_to_tensor(ctx, dx, c, h, w, &t));
+  const size_t nout = (size_t)n->st_cout * h * n->st_shuffle * w * n->st_shuffle;
+  float* dout;
+  ZJAI_TRY(stage_out_alloc(ctx, out, nout, mem, &dout));
+  Runner r = make_runner(ctx, n, &ctx->arena, ctx->stream, 1, nullptr);
+  int st = r.stage(t, dout);
+  if (st != ZJAI_OK) return settle(ctx, st);
+  ZJAI_TRY(stage_out_finish(ctx, out, dout, nout, mem));
+  return finish_call(ctx, mem);
+}
+
 int zjai_synthesis_tiles(int height, int width, int latent_h, int latent_w, int tile_size,
                          int overlap, zjai_tile* tiles, int max_tiles, int* count) {
   std::vector<zjai_tile> v;

@@ -89,16 +89,16 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with `parity` to complete. Returns false (and records `code`
-// in *err and sets *abort) on timeout, or when another role has already aborted. The common
-// case (phase already complete) takes one non-blocking test.
+// in *err and sets *abort) after `limit` SM cycles, or when another role has already aborted.
+// The common case (phase already complete) takes one non-blocking test.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          int* err, int code) {
+                                          int* err, int code, long long limit = kWaitCycles) {
   if (mbar_test(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if ((it & 63u) == 0 && clock64() - t0 > kWaitCycles) {
+    if ((it & 63u) == 0 && clock64() - t0 > limit) {
       atomicCAS(err, 0, code);
       *abort = 1;
       return false;
@@ -108,16 +108,19 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 
 // mbar_wait for roles whose wake-up latency is not on the critical path (a producer waiting
 // for a free stage, the MMA issuer waiting for a free accumulator, the epilogue waiting for a
-// full one): after the first polls it sleeps `ns` between tests, leaving the issue slots of
-// its SM sub-partition to the warps that have work.
+// full one): each poll suspends in the barrier unit for at most 100 ns, the limit is checked
+// after every poll (so a short `limit` expires within a few hundred cycles of it), and after
+// the first polls it sleeps `ns` between tests, leaving the issue slots of its SM
+// sub-partition to the warps that have work.
 __device__ __forceinline__ bool mbar_wait_idle(uint32_t bar, uint32_t parity, volatile int* abort,
-                                               int* err, int code, uint32_t ns) {
+                                               int* err, int code, uint32_t ns,
+                                               long long limit = kWaitCycles) {
   if (mbar_test(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 100u)) return true;
     if (*abort) return false;
-    if ((it & 63u) == 0 && clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       atomicCAS(err, 0, code);
       *abort = 1;
       return false;
@@ -129,13 +132,14 @@ __device__ __forceinline__ bool mbar_wait_idle(uint32_t bar, uint32_t parity, vo
 // mbar_wait whose polls sleep in the barrier unit (up to 20 us each) while the phase is
 // incomplete: for many threads waiting on one barrier at once.
 __device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity,
-                                                volatile int* abort, int* err, int code) {
+                                                volatile int* abort, int* err, int code,
+                                                long long limit = kWaitCycles) {
   if (mbar_test(bar, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       atomicCAS(err, 0, code);
       *abort = 1;
       return false;
@@ -143,7 +147,9 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity,
   }
 }
 
-// Bounded wait that ignores the abort flag (used to drain in-flight work before exit).
+// Bounded wait that ignores the abort flag (used to drain in-flight work before exit). Its limit
+// is always kWaitCycles, whatever a kernel's pipeline waits use: in-flight copies and MMAs
+// complete on their own, and the CTA must not exit (or free TMEM) before they have.
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
   const long long t0 = clock64();
   for (uint32_t it = 0;; ++it) {

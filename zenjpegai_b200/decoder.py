@@ -178,25 +178,3 @@ class Encoder:
         check(_lib.lib().zjai_analysis_secondary(self.net_uv.handle, _arg(chroma12)[0], h2, w2,
                                                  _arg(luv)[0], mem))
         return ly, luv
-
-
-def smoke_check(engine):
-    """One small SOP picture (two tiles) through the whole-picture API, checked against the
-    CPU oracle (used by `__graft_entry__.smoke`; the oracle import happens there)."""
-    import oracle as zo
-    from . import synthetic as syn
-    py, puv = syn.synthesis_params("sop", 2)
-    dec = Decoder(engine, "sop", py, puv)
-    H, W = 96, 176
-    lh, lw = _cdiv(H, 16), _cdiv(W, 16)
-    ly = syn.laplace_latent(1, "smoke/ly", (160, lh, lw), 1.5)
-    luv = syn.laplace_latent(1, "smoke/luv", (96, lh, lw), 1.5)
-    got = dec.synthesize(ly, luv, H, W, tile_size=96, overlap=16)
-    want = zo.synthesize(zo.Checkpoint(py), zo.Checkpoint(puv), zo.SOP, ly, luv, H, W,
-                         tile_size=96, overlap=16)
-    for g, w in zip(got, want):
-        mse = float(np.mean((g.astype(np.float64) - w) ** 2))
-        p = 99.0 if mse == 0 else 10 * np.log10(255.0 ** 2 / mse)
-        if p < 50.0:
-            raise ZjaiError(_lib.DEVICE, "smoke: PSNR %.1f dB against the oracle" % p)
-    dec.close()
