@@ -6,17 +6,21 @@ synthetic latents (luma 160x135x240, chroma 96x135x240, integer Laplace(1.5) wit
 in 512-sample tiles with a 16-sample overlap (40 tiles), random-init weights (seed 3), tiles
 distributed round-robin over the ranks (tile i on rank i mod N), each rank's final layers
 writing its cores as 8-bit YUV 4:2:0 samples (the fused output stage, quantize_plane_par in the
-epilogue) and a final sum-reduce of the disjoint 8-bit cores to rank 0 over
-NCCL (the "final gather"). One step = one picture. `--config sop1080` runs config 3 (SOP
-1920x1080, one tile).
+epilogue) and a final sum-reduce of the disjoint 8-bit cores to rank 0 over NCCL (the "final
+gather"). One step = one picture. `--config sop1080` runs config 3 (SOP 1920x1080, one tile);
+`--config conv1` / `up2` run configs 1 and 2 (a single conv layer; the upsampling stage)
+through the conv-stage entry, as replicas when N > 1.
 
 value: output Mpixel/s of the whole job, timed on the device (CUDA events bracketing each
 step on the engine's stream, L2 flushed between steps, max over ranks). e2e: the same through
-the public API with the latents copied from pinned host memory and the 8-bit picture read
-back, every step. roofline: the tcgen05 kernels (the implicit-GEMM convolution and the fused
-FFN, all their launches of one step), algorithmic FLOPs (live MACs x 2) / summed CUDA-event
-duration, against the measured bf16 dense peak. cpu_baseline / --impl reference: the CPU oracle (a C restatement of the crate's
-f32 path) on a bounded sample of the same workload, all host threads.
+the public API with the inputs copied from pinned host memory and the output read back, every
+step. roofline: the tcgen05 kernels (the implicit-GEMM convolution and the fused FFN, all
+their launches of one step), algorithmic FLOPs (live MACs x 2) / summed CUDA-event duration,
+against the measured bf16 dense peak. cpu_baseline and --impl reference: the crate's nn::fast
+CPU algorithm restated in oracle/fast.c (bit-identical to the oracle's nn::reference loops) on
+the box's host cores, counting output (core) pixels only: the reference arm sweeps the
+picture's tile rows, one per step; cpu_baseline times one tile row on all threads and one tile
+on one thread.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
        (N > 1 under torchrun, one process per GPU)
@@ -35,11 +39,23 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+SYNTH_METRIC = "synthesis decode Mpixel/s"
+STAGE_METRIC = "conv stage output Mpixel/s"
 CONFIGS = {
-    "hop4k": dict(op="hop", H=2160, W=3840, tile=512, overlap=16, seed=3, lat_seed=100,
+    "hop4k": dict(kind="synth", op="hop", H=2160, W=3840, tile=512, overlap=16, seed=3,
+                  lat_seed=100, metric=SYNTH_METRIC, scaling="strong",
                   desc="BASELINE config 4: HOP synthesis, 3840x2160 4:2:0, 512/16 tiles"),
-    "sop1080": dict(op="sop", H=1080, W=1920, tile=0, overlap=0, seed=2, lat_seed=100,
+    "sop1080": dict(kind="synth", op="sop", H=1080, W=1920, tile=0, overlap=0, seed=2,
+                    lat_seed=100, metric=SYNTH_METRIC, scaling="strong",
                     desc="BASELINE config 3: SOP synthesis, 1920x1080 4:2:0, one tile"),
+    "conv1": dict(kind="stage", shuffle=1, act="leaky", nres=0, metric=STAGE_METRIC,
+                  scaling="weak",
+                  desc="BASELINE config 1: conv 3x3 128->128 on 128x128, LeakyReLU(0.01)",
+                  weights="N(0, 1/(9*128)) weights, N(0, 0.01^2) bias, seed 0"),
+    "up2": dict(kind="stage", shuffle=2, act=None, nres=2, metric=STAGE_METRIC, scaling="weak",
+                desc="BASELINE config 2: conv 3x3 192->512 + depth-to-space 2 on 68x120, two "
+                     "residual blocks (conv3x3-LeakyReLU-conv3x3 + skip) at 128 channels",
+                weights="He-normal weights, zero biases, seed 1"),
 }
 
 
@@ -188,48 +204,219 @@ class ClockSampler:
                 "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
-def cpu_sample(cfg, threads):
-    """The oracle on one full-size tile (luma + chroma) of the workload: (Mpixel/s, desc)."""
+# ---------------------------------------------------------------------------------------------
+# CPU side: the crate's nn::fast algorithm restated in oracle/fast.c (bit-identical to the
+# oracle's nn::reference loops), timed on the box's host cores
+# ---------------------------------------------------------------------------------------------
+
+def _tile_rows(cfg):
+    """The workload's tiles (oracle tiling, tools/tiles.rs:39-119) grouped by tile row."""
     import oracle as zo
+    H, W = cfg["H"], cfg["W"]
+    lh, lw = -(-H // 16), -(-W // 16)
+    tiles = zo.synthesis_tiles(H, W, lh, lw, cfg["tile"], cfg["overlap"])
+    rows = {}
+    for t in tiles:
+        rows.setdefault(t["img_y"], []).append(t)
+    return [rows[k] for k in sorted(rows)]
+
+
+class CpuSynth:
+    """The CPU baseline of a synthesis config: luma + chroma synthesis of whole tiles (overlap
+    included, as the crate computes them), counting only the tiles' core (output) pixels."""
+
+    def __init__(self, cfg):
+        import oracle as zo
+        import synthetic as syn
+        self.zo, self.cfg = zo, cfg
+        H, W = cfg["H"], cfg["W"]
+        lh, lw = -(-H // 16), -(-W // 16)
+        py, puv = syn.synthesis_params(cfg["op"], cfg["seed"])
+        self.cky, self.ckuv = zo.Checkpoint(py), zo.Checkpoint(puv)
+        self.ly = syn.laplace_latent(cfg["lat_seed"], "ly", (160, lh, lw), 1.5)
+        self.luv = syn.laplace_latent(cfg["lat_seed"], "luv", (96, lh, lw), 1.5)
+        self.rows = _tile_rows(cfg)
+
+    def run(self, tiles, threads):
+        """(core pixels, seconds) of synthesising `tiles` on `threads` host threads."""
+        zo = self.zo
+        zo.set_fast(True)
+        zo.set_threads(threads)
+        op = zo.OPS[self.cfg["op"]]
+        px = 0
+        t0 = time.perf_counter()
+        for t in tiles:
+            win = (slice(None), slice(t["lat_y"], t["lat_y"] + t["lat_h"]),
+                   slice(t["lat_x"], t["lat_x"] + t["lat_w"]))
+            wy = np.ascontiguousarray(self.ly[win])
+            wuv = np.ascontiguousarray(self.luv[win])
+            zo.synthesis_primary(self.cky, op, wy, t["img_h"], t["img_w"])
+            zo.synthesis_secondary(self.ckuv, op, wy, wuv, t["img_h"], t["img_w"])
+            px += t["core_h"] * t["core_w"]
+        return px, time.perf_counter() - t0
+
+
+class CpuStage:
+    """The CPU baseline of a conv-stage config: the same layers composed from the oracle's
+    primitives (conv, pixel shuffle, LeakyReLU, residual add) on the nn::fast restatement."""
+
+    def __init__(self, cfg):
+        import oracle as zo
+        import synthetic as syn
+        self.zo, self.cfg = zo, cfg
+        self.prm, self.x = stage_inputs(cfg)
+
+    def run(self, threads):
+        zo, cfg, prm = self.zo, self.cfg, self.prm
+        zo.set_fast(True)
+        zo.set_threads(threads)
+        t0 = time.perf_counter()
+        y = zo.conv2d(self.x, prm["conv.weight"], prm["conv.bias"], pad=(1, 1))
+        if cfg["act"] == "leaky":
+            y = zo.leaky_relu(y)
+        if cfg["shuffle"] > 1:
+            y = zo.pixel_shuffle(y, cfg["shuffle"])
+        for i in range(cfg["nres"]):
+            p = "res.%d." % i
+            t = zo.leaky_relu(zo.conv2d(y, prm[p + "conv1.weight"], prm[p + "conv1.bias"],
+                                        pad=(1, 1)))
+            y = zo.add(zo.conv2d(t, prm[p + "conv2.weight"], prm[p + "conv2.bias"],
+                                 pad=(1, 1)), y)
+        return y.shape[1] * y.shape[2], time.perf_counter() - t0
+
+
+def stage_inputs(cfg):
     import synthetic as syn
-    zo.set_threads(threads)
-    op = cfg["op"]
-    py, puv = syn.synthesis_params(op, cfg["seed"])
-    cky, ckuv = zo.Checkpoint(py), zo.Checkpoint(puv)
-    th = cfg["tile"] or cfg["H"]
-    tw = cfg["tile"] or cfg["W"]
-    lh, lw = -(-th // 16), -(-tw // 16)
-    ly = syn.laplace_latent(cfg["lat_seed"], "cpu/ly", (160, lh, lw), 1.5)
-    luv = syn.laplace_latent(cfg["lat_seed"], "cpu/luv", (96, lh, lw), 1.5)
-    t = time.perf_counter()
-    zo.synthesis_primary(cky, zo.OPS[op], ly, th, tw)
-    zo.synthesis_secondary(ckuv, zo.OPS[op], ly, luv, th, tw)
-    dt = time.perf_counter() - t
-    return th * tw / dt / 1e6, "one %dx%d tile (luma + chroma synthesis) of the workload" % (th, tw)
+    if cfg["name"] == "conv1":
+        return syn.conv_layer_params(0), syn.uniform(0, "x", (128, 128, 128), -1.0, 1.0)
+    return syn.upsample_stage_params(1), syn.normal(1, "x", (192, 68, 120))
+
+
+def cpu_baseline(cfg):
+    """Rank 0, N = 1: the nn::fast restatement on all host threads and on one thread, on a
+    bounded sample of the workload (a few seconds each)."""
+    threads = os.cpu_count() or 1
+    if cfg["kind"] == "stage":
+        c = CpuStage(cfg)
+        c.run(threads)
+        px, dt = c.run(threads)
+        px1, dt1 = c.run(1)
+        return {"value": px / dt / 1e6, "unit": "Mpixel/s", "cores": threads, "kind": "port",
+                "value_1core": px1 / dt1 / 1e6,
+                "sample": "the whole stage once (oracle/fast.c, the crate's nn::fast "
+                          "convolution algorithm restated, bit-identical to nn::reference)"}
+    c = CpuSynth(cfg)
+    rows = c.rows
+    row = rows[1] if len(rows) > 1 else rows[0]  # an interior tile row
+    px, dt = c.run(row, threads)
+    px1, dt1 = c.run(row[:1], 1)
+    return {"value": px / dt / 1e6, "unit": "Mpixel/s", "cores": threads, "kind": "port",
+            "value_1core": px1 / dt1 / 1e6,
+            "sample": "tile row 1 (%d tiles, luma + chroma, output pixels of their cores) on %d "
+                      "threads; its first tile on 1 thread; oracle/fast.c, the crate's nn::fast "
+                      "convolution algorithm restated (bit-identical to nn::reference)"
+                      % (len(row), threads)}
+
+
+def config_dict(args, cfg, world):
+    """The workload description both arms print (the same dict)."""
+    if cfg["kind"] == "stage":
+        return {"workload": args.config + ": " + cfg["desc"],
+                "parallelism": "replicas: the same stage on each of %d GPU(s)" % world,
+                "weights": cfg["weights"],
+                "precision": "f16 operands, f32 accumulation (TMEM); the CPU arm computes f32"}
+    return {"workload": args.config + ": " + cfg["desc"],
+            "picture": "%dx%d 4:2:0, 8-bit YUV out" % (cfg["W"], cfg["H"]),
+            "tiles": cfg.get("ntiles"),
+            "parallelism": "tiles round-robin over %d GPU(s), NCCL reduce of 8-bit cores" % world,
+            "weights": "random-init, seed %d (role-scaled normal)" % cfg["seed"],
+            "l2": "flushed between steps (256 MiB write, outside the timed events)",
+            "precision": "f16 operands, f32 accumulation (TMEM); the CPU arm computes f32"}
 
 
 def run_reference(args, cfg):
+    """The reference's CPU path (the nn::fast restatement in oracle/, on every host thread) on
+    the same workload: each step synthesises one tile row (the rows taken in turn, so the steps
+    sweep the whole picture) and counts the output pixels of its tiles' cores. Imports nothing
+    from the GPU package."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    for _ in range(args.warmup):
-        cpu_sample(cfg, threads)
-    vals = [cpu_sample(cfg, threads) for _ in range(args.steps)]
-    v = float(np.mean([x[0] for x in vals]))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if cfg["kind"] == "stage":
+        c = CpuStage(cfg)
+        run = lambda s: c.run(threads)
+        sample = "the whole stage per step"
+    else:
+        c = CpuSynth(cfg)
+        nrow = len(c.rows)
+        run = lambda s: c.run(c.rows[s % nrow], threads)
+        sample = ("one tile row per step (%d rows in turn, %d tiles in all), luma + chroma, "
+                  "output pixels of the cores" % (nrow, sum(len(r) for r in c.rows)))
+    for s in range(args.warmup):
+        run(s)
+    px = dt = 0.0
+    for s in range(args.steps):
+        p, d = run(args.warmup + s)
+        px += p
+        dt += d
+    v = px / dt / 1e6
     line = {
-        "impl": "reference", "metric": "synthesis decode Mpixel/s", "value": v,
-        "unit": "Mpixel/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": None, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.config + ": " + cfg["desc"]},
+        "impl": "reference", "metric": cfg["metric"], "value": v, "unit": "Mpixel/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": cfg["scaling"], "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args, cfg, world),
         "cpu_baseline": {"value": v, "unit": "Mpixel/s", "cores": threads, "kind": "port",
-                         "sample": vals[0][1] + ", per step"},
+                         "sample": sample + "; oracle/fast.c, the crate's nn::fast convolution "
+                                            "algorithm restated (bit-identical to nn::reference)"},
         "e2e": {"value": v, "unit": "Mpixel/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "note": "the reference crate (Rust) cannot be built here; its f32 CPU path is timed "
-                "through the C restatement in oracle/ on all host threads",
+        "note": "the reference crate (Rust) cannot be built here (no Rust toolchain); its CPU "
+                "path is timed through its algorithm restated in C (oracle/)",
     }
     print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------------------------
+
+def profile_step(eng, step, flush):
+    """Algorithmic FLOPs, summed CUDA-event ms and launches of the tcgen05 kernels over one
+    profiled step."""
+    import ctypes
+    import torch
+    from zenjpegai_b200 import _lib
+    L = _lib.lib()
+    L.zjai_ctx_profile(eng.handle, 1)
+    flush.zero_()
+    torch.cuda.synchronize()
+    step()
+    ms, fl, nl = ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
+    L.zjai_ctx_profile_read(eng.handle, ctypes.byref(ms), ctypes.byref(fl), ctypes.byref(nl))
+    L.zjai_ctx_profile(eng.handle, 0)
+    return ms.value, fl.value, nl.value
+
+
+def layer_report(eng):
+    import ctypes
+    from zenjpegai_b200 import _lib
+    buf = ctypes.create_string_buffer(1 << 20)
+    _lib.lib().zjai_ctx_profile_report(eng.handle, buf, len(buf))
+    rows = [ln.split("\t") for ln in buf.value.decode().splitlines()[1:]]
+    rows.sort(key=lambda r: -float(r[2]))
+    sys.stderr.write("per-layer kernel time of one step, luma and chroma serialised "
+                     "(layer, launches, ms, GFLOP, TFLOP/s, GB, GB/s):\n")
+    for r in rows:
+        sys.stderr.write("  %-48s %4s %9s %9s %7s %8s %6s\n" % tuple(r))
+    kinds = {}
+    for r in rows:
+        k = r[0].split("[")[-1].rstrip("]") if r[0].endswith("]") else "conv"
+        kinds[k] = kinds.get(k, 0.0) + float(r[2])
+    sys.stderr.write("per kernel kind (ms): %s\n" % ", ".join(
+        "%s %.3f" % kv for kv in sorted(kinds.items(), key=lambda kv: -kv[1])))
 
 
 def main():
@@ -243,11 +430,13 @@ def main():
     ap.add_argument("--layers", action="store_true",
                     help="print the per-layer conv time of one profiled step to stderr")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config], name=args.config)
+    if cfg["kind"] == "synth":
+        H, W = cfg["H"], cfg["W"]
+        cfg["ntiles"] = sum(len(r) for r in _tile_rows(cfg)) if cfg["tile"] else 1
     if args.impl == "reference":
         return run_reference(args, cfg)
 
-    import ctypes
     import torch
     import torch.distributed as dist
 
@@ -260,45 +449,74 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
 
-    import zenjpegai_b200 as zj
     import synthetic as syn
-    from zenjpegai_b200 import _lib, sharding
+    import zenjpegai_b200 as zj
+    from zenjpegai_b200 import sharding
     from zenjpegai_b200.decoder import Decoder
 
-    H, W, op = cfg["H"], cfg["W"], cfg["op"]
-    lh, lw = -(-H // 16), -(-W // 16)
-    ch, cw = -(-H // 2), -(-W // 2)
-    eng = zj.Engine(local, arena_bytes=64 << 30)
+    eng = zj.Engine(local, arena_bytes=(64 << 30) if cfg["kind"] == "synth" else (4 << 30))
     # one non-default stream shared by torch (copies, events, NCCL) and the engine
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     eng.set_stream(stream.cuda_stream)
-    py, puv = syn.synthesis_params(op, cfg["seed"])
-    dec = Decoder(eng, op, py, puv)
-    ly_h = torch.from_numpy(syn.laplace_latent(cfg["lat_seed"], "ly", (160, lh, lw), 1.5))
-    luv_h = torch.from_numpy(syn.laplace_latent(cfg["lat_seed"], "luv", (96, lh, lw), 1.5))
-    ly_h, luv_h = ly_h.pin_memory(), luv_h.pin_memory()
-    ly, luv = ly_h.cuda(), luv_h.cuda()
-    tiles = zj.synthesis_tiles(H, W, lh, lw, cfg["tile"], cfg["overlap"])
-    mine = sharding.shard_tiles(tiles, rank, world)
-    out8 = torch.zeros(H * W + 2 * ch * cw, dtype=torch.uint8, device="cuda")
-    # the 8-bit planes of the picture, written by the final layers (fused output stage)
-    planes8 = (out8[:H * W].view(H, W), out8[H * W:H * W + ch * cw].view(ch, cw),
-               out8[H * W + ch * cw:].view(ch, cw))
-    out8_host = torch.empty_like(out8, device="cpu").pin_memory()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    closers = []
 
-    def step(from_host=False):
-        if from_host:
-            ly.copy_(ly_h, non_blocking=True)
-            luv.copy_(luv_h, non_blocking=True)
-        # every rank starts from a zero picture: the reduce sums the ranks' disjoint cores, so
-        # a plane still holding last step's picture would add it in again
-        out8.zero_()
-        dec.synthesize_tiles(ly, luv, mine, H, W, out=planes8, bit_depth=8)
-        sharding.gather_cores(out8, dist)
-        if from_host and rank == 0:
-            out8_host.copy_(out8, non_blocking=True)
+    if cfg["kind"] == "synth":
+        op = cfg["op"]
+        lh, lw = -(-H // 16), -(-W // 16)
+        ch, cw = -(-H // 2), -(-W // 2)
+        py, puv = syn.synthesis_params(op, cfg["seed"])
+        dec = Decoder(eng, op, py, puv)
+        closers.append(dec.close)
+        ly_h = torch.from_numpy(syn.laplace_latent(cfg["lat_seed"], "ly", (160, lh, lw), 1.5))
+        luv_h = torch.from_numpy(syn.laplace_latent(cfg["lat_seed"], "luv", (96, lh, lw), 1.5))
+        ly_h, luv_h = ly_h.pin_memory(), luv_h.pin_memory()
+        ly, luv = ly_h.cuda(), luv_h.cuda()
+        tiles = zj.synthesis_tiles(H, W, lh, lw, cfg["tile"], cfg["overlap"])
+        mine = sharding.shard_tiles(tiles, rank, world)
+        out8 = torch.zeros(H * W + 2 * ch * cw, dtype=torch.uint8, device="cuda")
+        # the 8-bit planes of the picture, written by the final layers (fused output stage)
+        planes8 = (out8[:H * W].view(H, W), out8[H * W:H * W + ch * cw].view(ch, cw),
+                   out8[H * W + ch * cw:].view(ch, cw))
+        out8_host = torch.empty_like(out8, device="cpu").pin_memory()
+        out_px = H * W
+        h2d = world * (ly_h.numel() + luv_h.numel()) * 4
+        d2h = out8.numel()
+
+        def step(from_host=False):
+            if from_host:
+                ly.copy_(ly_h, non_blocking=True)
+                luv.copy_(luv_h, non_blocking=True)
+            # every rank starts from a zero picture: the reduce sums the ranks' disjoint
+            # cores, so a plane still holding last step's picture would add it in again
+            out8.zero_()
+            dec.synthesize_tiles(ly, luv, mine, H, W, out=planes8, bit_depth=8)
+            sharding.gather_cores(out8, dist)
+            if from_host and rank == 0:
+                out8_host.copy_(out8, non_blocking=True)
+    else:
+        prm, x_np = stage_inputs(cfg)
+        st = zj.Stage(eng, prm, shuffle=cfg["shuffle"],
+                      act=zj.ACT_LEAKY if cfg["act"] == "leaky" else zj.ACT_NONE,
+                      res_act=zj.ACT_LEAKY)
+        closers.append(st.close)
+        x_h = torch.from_numpy(x_np).pin_memory()
+        x_d = x_h.cuda()
+        r = cfg["shuffle"]
+        oshape = (st.cout, x_np.shape[1] * r, x_np.shape[2] * r)
+        y_d = torch.empty(oshape, device="cuda")
+        y_h = torch.empty(oshape).pin_memory()
+        out_px = oshape[1] * oshape[2] * world  # replicas: every rank's output counts
+        h2d = x_h.numel() * 4
+        d2h = y_h.numel() * 4
+
+        def step(from_host=False):
+            if from_host:
+                x_d.copy_(x_h, non_blocking=True)
+            st.forward(x_d, out=y_d)
+            if from_host:
+                y_h.copy_(y_d, non_blocking=True)
 
     def timed(n, from_host=False):
         total = 0.0
@@ -336,30 +554,10 @@ def main():
     eng.sync()
     e2e_ms = timed(args.steps, from_host=True)
     # live roofline of the tcgen05 kernels over one profiled step
-    eng_h = eng.handle
-    _lib.lib().zjai_ctx_profile(eng_h, 1)
-    flush.zero_()
-    torch.cuda.synchronize()
-    step()
-    ms, fl, nl = ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
-    _lib.lib().zjai_ctx_profile_read(eng_h, ctypes.byref(ms), ctypes.byref(fl), ctypes.byref(nl))
-    _lib.lib().zjai_ctx_profile(eng_h, 0)
+    conv_ms, conv_fl, conv_n = profile_step(eng, step, flush)
     if args.layers and rank == 0:
-        buf = ctypes.create_string_buffer(1 << 20)
-        _lib.lib().zjai_ctx_profile_report(eng_h, buf, len(buf))
-        rows = [ln.split("\t") for ln in buf.value.decode().splitlines()[1:]]
-        rows.sort(key=lambda r: -float(r[2]))
-        sys.stderr.write("per-layer kernel time of one step, luma and chroma serialised "
-                         "(layer, launches, ms, GFLOP, TFLOP/s, GB, GB/s):\n")
-        for r in rows:
-            sys.stderr.write("  %-48s %4s %9s %9s %7s %8s %6s\n" % tuple(r))
-        kinds = {}
-        for r in rows:
-            k = r[0].split("[")[-1].rstrip("]") if r[0].endswith("]") else "conv"
-            kinds[k] = kinds.get(k, 0.0) + float(r[2])
-        sys.stderr.write("per kernel kind (ms): %s\n" % ", ".join(
-            "%s %.3f" % kv for kv in sorted(kinds.items(), key=lambda kv: -kv[1])))
-    stats = torch.tensor([ms.value, fl.value, float(nl.value), float(launches)],
+        layer_report(eng)
+    stats = torch.tensor([conv_ms, conv_fl, float(conv_n), float(launches)],
                          dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.SUM)
@@ -367,38 +565,26 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        v, desc = cpu_sample(cfg, threads)
-        cpu = {"value": v, "unit": "Mpixel/s", "cores": threads, "kind": "port",
-               "sample": desc + ", oracle/ (C restatement of the crate's f32 path)"}
+        cpu = cpu_baseline(cfg)
 
     if rank == 0:
-        mpx = H * W / 1e6
         peak, peak_src = peaks()
         achieved = conv_fl / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
+        traffic = conv_traffic(args.config) if world == 1 else None
         line = {
-            "metric": "synthesis decode Mpixel/s",
-            "value": args.steps * mpx / (total_ms / 1e3),
+            "metric": cfg["metric"],
+            "value": args.steps * out_px / 1e6 / (total_ms / 1e3),
             "unit": "Mpixel/s",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps,
             "higher_is_better": True,
-            "scaling": "strong",
+            "scaling": cfg["scaling"],
             "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic",
-            "config": {
-                "workload": args.config + ": " + cfg["desc"],
-                "picture": "%dx%d 4:2:0, 8-bit YUV out" % (W, H),
-                "tiles": len(tiles),
-                "parallelism": "tiles round-robin over %d GPU(s), NCCL reduce of 8-bit cores"
-                               % world,
-                "weights": "random-init, seed %d (role-scaled normal)" % cfg["seed"],
-                "l2": "flushed between steps (256 MiB write, outside the timed events)",
-                "precision": "f16 operands, f32 accumulation (TMEM)",
-            },
+            "config": config_dict(args, cfg, world),
             "roofline": {
                 "bound": "tensor",
                 "kernel": "conv_tc_kernel + ffn_tc_kernel (tcgen05 implicit-GEMM conv and fused "
@@ -410,23 +596,25 @@ def main():
                 "peak_source": peak_src,
                 "launches_per_step": conv_n,
                 "flops_per_step": conv_fl,
-                # bytes per step (all tcgen05 launches of the step, like `achieved`), from the
-                # committed single-pass ncu capture of this workload
-                "traffic": conv_traffic(args.config),
-                "traffic_unit": "bytes per step (DRAM read + write, ncu)",
+                # DRAM bytes of one step's tcgen05 launches from the committed one-GPU ncu
+                # capture of this workload (profiles/tcgen05_<config>_step_dram.txt), reported
+                # at N = 1 only
+                "traffic": traffic,
+                "traffic_unit": "bytes per step (DRAM read + write, ncu, one GPU)",
             },
             "cpu_baseline": cpu,
             "e2e": {
-                "value": args.steps * mpx / (e2e_ms / 1e3),
+                "value": args.steps * out_px / 1e6 / (e2e_ms / 1e3),
                 "unit": "Mpixel/s",
-                "h2d_bytes_per_step": world * (ly_h.numel() + luv_h.numel()) * 4,
-                "d2h_bytes_per_step": out8.numel(),
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
             },
             "clocks": clk,
             "gpu_launches": int(all_launches),
         }
         print(json.dumps(line), flush=True)
-    dec.close()
+    for c in closers:
+        c()
     eng.close()
     if world > 1:
         dist.barrier()

@@ -59,6 +59,7 @@ DUMP_FN = ctypes.CFUNCTYPE(None, ctypes.c_char_p, _f, _i, _i, _i)
 
 def _declare(L):
     L.zo_set_threads.argtypes = [_i]
+    L.zo_set_fast.argtypes = [_i]
     L.zo_conv2d_out_size.argtypes = [_i] * 7 + [ctypes.POINTER(_i)] * 3
     L.zo_conv2d.argtypes = [_f, _i, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i,
                             ctypes.POINTER(_i), _f]
@@ -104,6 +105,16 @@ def _c32(a):
 
 def set_threads(n):
     lib().zo_set_threads(int(n))
+
+
+def set_fast(on):
+    """Convolutions on the restatement of the crate's nn::fast algorithm (fast.c: same bits,
+    blocked layout and register tiles; the timed CPU baseline) or on the reference loops."""
+    lib().zo_set_fast(1 if on else 0)
+
+
+def get_fast():
+    return bool(lib().zo_get_fast())
 
 
 def conv2d(x, w, b=None, stride=1, pad=(0, 0), groups=1, extra=(0, 0, 0, 0)):

@@ -8,6 +8,7 @@
  */
 #include "oracle.h"
 
+#include <malloc.h>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -17,11 +18,28 @@
 #endif
 
 static int g_threads = 1;
+static int g_fast = 0;  /* 1: convolutions run the nn::fast restatement (fast.c) */
 static zo_dump_fn g_dump = NULL;
 
 void zo_set_threads(int n) { g_threads = n > 0 ? n : 1; }
 int zo_get_threads(void) { return g_threads; }
 void zo_set_dump(zo_dump_fn fn) { g_dump = fn; }
+void zo_set_fast(int on) {
+    g_fast = on != 0;
+#ifdef __GLIBC__
+    /* the per-layer buffers are large: keep freed memory in the heap instead of returning it
+     * to the kernel, so the next layer's buffers do not take fresh page faults */
+    if (g_fast) {
+        mallopt(M_MMAP_THRESHOLD, 1 << 30);
+        mallopt(M_TRIM_THRESHOLD, 1 << 30);
+    }
+#endif
+}
+int zo_get_fast(void) { return g_fast; }
+
+/* Element-parallel loops in the baseline mode (the crate's math runs SIMD and threaded); each
+ * element's arithmetic is the same as on one thread, so the result is the same bits. */
+#define ZO_PAR_FOR _Pragma("omp parallel for schedule(static) if(g_fast) num_threads(g_threads)")
 
 static float clampf(float v, float lo, float hi) {
     /* Rust f32::clamp: NaN passes through. */
@@ -45,6 +63,11 @@ void zo_conv2d_out_size(int h, int w, int kh, int kw, int stride, int pad_h, int
 int zo_conv2d(const float *x, int c, int h, int w, const float *weight, const float *bias,
               int oc, int kh, int kw, int stride, int pad_h, int pad_w, int groups,
               const int extra[4], float *out) {
+    if (g_fast) {  /* the timed CPU baseline: same bits, blocked algorithm */
+        int r = zf_conv2d(x, c, h, w, weight, bias, oc, kh, kw, stride, pad_h, pad_w, groups,
+                          extra, out);
+        if (r != 1) return r;
+    }
     if (groups <= 0 || c % groups || oc % groups || stride <= 0 || kh <= 0 || kw <= 0)
         return -1;
     int et = extra ? extra[0] : 0, el = extra ? extra[1] : 0;
@@ -112,6 +135,10 @@ void zo_conv_transpose2d_out_size(int h, int w, int k, int stride, int pad, int 
 int zo_conv_transpose2d(const float *x, int c, int h, int w, const float *weight,
                         const float *bias, int oc, int k, int stride, int pad, int out_pad,
                         float *out) {
+    if (g_fast) {
+        int r = zf_conv_transpose2d(x, c, h, w, weight, bias, oc, k, stride, pad, out_pad, out);
+        if (r != 1) return r;
+    }
     if (stride <= 0 || k <= 0 || pad >= k || out_pad >= stride || h <= 0 || w <= 0) return -1;
     int oh, ow;
     zo_conv_transpose2d_out_size(h, w, k, stride, pad, out_pad, &oh, &ow);
@@ -176,19 +203,24 @@ int zo_pixel_shuffle(const float *x, int c4, int h, int w, int r, float *out) {
 /* ======================================================================================= */
 
 void zo_relu(float *x, int64_t n) {
+    ZO_PAR_FOR
     for (int64_t i = 0; i < n; i++) x[i] = x[i] > 0.0f ? x[i] : 0.0f;
 }
 void zo_relu6(float *x, int64_t n) {
+    ZO_PAR_FOR
     for (int64_t i = 0; i < n; i++) x[i] = clampf(x[i], 0.0f, 6.0f);
 }
 void zo_add(float *dst, const float *src, int64_t n) {
+    ZO_PAR_FOR
     for (int64_t i = 0; i < n; i++) dst[i] += src[i];
 }
 /* `x *= 1 + m`: two IEEE operations, not an FMA (layers.rs:195-201) */
 void zo_gate(float *x, const float *mask, int64_t n) {
+    ZO_PAR_FOR
     for (int64_t i = 0; i < n; i++) x[i] *= 1.0f + mask[i];
 }
 void zo_mul(float *a, const float *b, int64_t n) {
+    ZO_PAR_FOR
     for (int64_t i = 0; i < n; i++) a[i] *= b[i];
 }
 
@@ -219,11 +251,13 @@ float zo_exp(float x) {
 }
 
 void zo_sigmoid(float *x, int64_t n) {
+    ZO_PAR_FOR
     for (int64_t i = 0; i < n; i++) x[i] = 1.0f / (1.0f + zo_exp(-x[i]));
 }
 
 /* elu(a) * b (math.rs:66-72) */
 void zo_elu_gate(float *a, const float *b, int64_t n) {
+    ZO_PAR_FOR
     for (int64_t i = 0; i < n; i++) {
         float e = zo_exp(a[i]) - 1.0f;
         float elu = a[i] > 0.0f ? a[i] : e;
@@ -233,11 +267,13 @@ void zo_elu_gate(float *a, const float *b, int64_t n) {
 
 /* `x * 128 + 127.5` clamped to [0, 255] (synthesis.rs:188-192) */
 void zo_denormalize(float *x, int64_t n) {
+    ZO_PAR_FOR
     for (int64_t i = 0; i < n; i++) x[i] = clampf(x[i] * 128.0f + 127.5f, 0.0f, 255.0f);
 }
 
 /* `(x - 127.5) / 128` (analysis.rs:36-39) */
 void zo_normalize(const float *x, int64_t n, float *out) {
+    ZO_PAR_FOR
     for (int64_t i = 0; i < n; i++) out[i] = (x[i] - 127.5f) / 128.0f;
 }
 
@@ -253,35 +289,39 @@ int zo_layer_norm_channels(float *x, int c, int h, int w, const float *weight,
                            const float *bias) {
     if (c <= 0) return -1;
     int64_t n = (int64_t)h * w;
-    double *mean = (double *)calloc(n, sizeof(double));
-    double *var = (double *)calloc(n, sizeof(double));
-    float *mean32 = (float *)malloc(sizeof(float) * n);
-    float *denom = (float *)malloc(sizeof(float) * n);
-    for (int ch = 0; ch < c; ch++) {
-        const float *p = x + ch * n;
-        for (int64_t i = 0; i < n; i++) mean[i] += (double)p[i];
-    }
-    for (int64_t i = 0; i < n; i++) mean[i] /= (double)c;
-    for (int ch = 0; ch < c; ch++) {
-        const float *p = x + ch * n;
-        for (int64_t i = 0; i < n; i++) {
-            double d = (double)p[i] - mean[i];
-            var[i] += d * d;
+    /* per pixel: f64 mean and biased variance over the channels in channel order, then
+     * (x - mean) / sqrt(var + 1e-5) * w + b in f32; pixel blocks are independent */
+    const int64_t blk = 256;
+    const int64_t nblk = (n + blk - 1) / blk;
+#pragma omp parallel for schedule(static) if(g_fast) num_threads(g_threads)
+    for (int64_t bi = 0; bi < nblk; bi++) {
+        const int64_t i0 = bi * blk, i1 = i0 + blk < n ? i0 + blk : n;
+        double mean[256], var[256];
+        float mean32[256], denom[256];
+        for (int64_t i = i0; i < i1; i++) mean[i - i0] = 0.0, var[i - i0] = 0.0;
+        for (int ch = 0; ch < c; ch++) {
+            const float *p = x + ch * n;
+            for (int64_t i = i0; i < i1; i++) mean[i - i0] += (double)p[i];
+        }
+        for (int64_t i = i0; i < i1; i++) mean[i - i0] /= (double)c;
+        for (int ch = 0; ch < c; ch++) {
+            const float *p = x + ch * n;
+            for (int64_t i = i0; i < i1; i++) {
+                double d = (double)p[i] - mean[i - i0];
+                var[i - i0] += d * d;
+            }
+        }
+        for (int64_t i = i0; i < i1; i++) {
+            mean32[i - i0] = (float)mean[i - i0];
+            denom[i - i0] = sqrtf((float)(var[i - i0] / (double)c) + 1e-5f);
+        }
+        for (int ch = 0; ch < c; ch++) {
+            float *p = x + ch * n;
+            float wv = weight[ch], bv = bias[ch];
+            for (int64_t i = i0; i < i1; i++)
+                p[i] = (p[i] - mean32[i - i0]) / denom[i - i0] * wv + bv;
         }
     }
-    for (int64_t i = 0; i < n; i++) {
-        mean32[i] = (float)mean[i];
-        denom[i] = sqrtf((float)(var[i] / (double)c) + 1e-5f);
-    }
-    for (int ch = 0; ch < c; ch++) {
-        float *p = x + ch * n;
-        float wv = weight[ch], bv = bias[ch];
-        for (int64_t i = 0; i < n; i++) p[i] = (p[i] - mean32[i]) / denom[i] * wv + bv;
-    }
-    free(mean);
-    free(var);
-    free(mean32);
-    free(denom);
     return 0;
 }
 

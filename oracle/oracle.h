@@ -31,6 +31,18 @@ extern "C" {
 /* ---- threading of the oracle's loops (OpenMP); 1 = serial ---------------------------- */
 void zo_set_threads(int n);
 int zo_get_threads(void);
+/* 1: zo_conv2d / zo_conv_transpose2d run the restatement of the crate's nn::fast algorithm
+ * (fast.c: blocked layout, register tiles, per-row threads), which gives the same bits; the
+ * timed CPU baseline. 0 (default): the nn::reference loops. */
+void zo_set_fast(int on);
+int zo_get_fast(void);
+/* nn::fast restatements (fast.c); return 1 when the geometry is not handled there */
+int zf_conv2d(const float *x, int c, int h, int w, const float *weight, const float *bias,
+              int oc, int kh, int kw, int stride, int pad_h, int pad_w, int groups,
+              const int extra[4], float *out);
+int zf_conv_transpose2d(const float *x, int c, int h, int w, const float *weight,
+                        const float *bias, int oc, int k, int stride, int pad, int out_pad,
+                        float *out);
 
 /* ---- layer functions (planar [c][h][w] f32 tensors, caller-owned buffers) -------------- */
 

@@ -806,17 +806,26 @@ __global__ void __launch_bounds__(256, 2) attn_gram_mma_kernel(
 }
 
 // attn[n][h][i][j] = softmax_j( G_ij / (max(|q_i|, eps) max(|k_j|, eps)) * T[h] )
-// red[n][e] = sum over the nparts partial slots of part[n][k][e], k in order (one thread per
-// element, coalesced): the Gram [dim][c] and squared norms [2 dim] of each picture.
+// red[n][e] = sum over the nparts partial slots of part[n][k][e] (one thread per element,
+// coalesced): the Gram [dim][c] and squared norms [2 dim] of each picture. Eight accumulators
+// (slot k goes to accumulator k % 8) keep eight loads in flight per thread; they are combined
+// in a fixed tree, so the result is the same on every run.
 __global__ void attn_reduce_kernel(const float* __restrict__ part, int nparts, long long stride,
                                    int n_img, float* __restrict__ red) {
   const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (id >= (long long)n_img * stride) return;
   const long long n = id / stride, e = id - n * stride;
   const float* p = part + n * nparts * stride + e;
-  float acc = 0.f;
-  for (int k = 0; k < nparts; ++k) acc += p[k * stride];
-  red[id] = acc;
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  int k = 0;
+  for (; k + 8 <= nparts; k += 8) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] += __ldg(p + (long long)(k + j) * stride);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (k + j < nparts) a[j] += __ldg(p + (long long)(k + j) * stride);
+  red[id] = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
 }
 
 // One attention row (picture n, row ri = h*c + i) from the reduced Gram and norms.
@@ -953,57 +962,60 @@ __global__ void attn_fold_kernel(const float* __restrict__ wo, const float* __re
   blk[rr * kc + (((col >> 3) ^ f) << 3) + (col & 7)] = __float2half_rn(acc * s);
 }
 
-// attn_reduce_kernel + attn_softmax_kernel + attn_fold_kernel in one launch for the common
-// shapes (c = 16 or 32, packed layer without padding rows or columns): block (head hd,
-// picture n) sums the head's Gram block and norms over the partial slots in slot order,
-// takes the c x c softmax (one thread per row) and writes the head's columns of
-// W_o . blockdiag(A) in the packed layout: the same operations in the same order as the three
-// kernels, with two launches fewer per attention.
+// attn_softmax_kernel + attn_fold_kernel in one launch for the common shapes (c = 16 or 32,
+// packed layer without padding rows or columns), after attn_reduce_kernel: block (head hd,
+// picture n) reads the head's reduced Gram block and norms, takes the c x c softmax (one
+// thread per row) and writes the head's columns of W_o . blockdiag(A) in the packed layout
+// from the head's W_o columns staged in shared memory (dim <= 256).
 template <int C>
 __global__ void __launch_bounds__(256) attn_fold_fused_kernel(
-    const float* __restrict__ part, int nparts, long long stride, const float* __restrict__ temp,
+    const float* __restrict__ red, long long stride, const float* __restrict__ temp,
     const float* __restrict__ wo, int dim, float s, __half* __restrict__ wout, int npad,
     int cin_pad, int kc, int bn) {
-  __shared__ float sa[C * C];   // the head's Gram block, then its attention matrix
-  __shared__ float sn[2 * C];   // q norms of its rows, k norms of its columns
+  __shared__ float sa[C * C];      // the head's Gram block, then its attention matrix
+  __shared__ float sn[2 * C];      // q norms of its rows, k norms of its columns
+  __shared__ float sw[256 * C];    // W_o[r][hd * C + i] at sw[r * C + i]
   const int hd = blockIdx.x, n = blockIdx.y;
-  const float* p = part + (long long)n * nparts * stride;
+  const float* p = red + (long long)n * stride;
   for (int e = threadIdx.x; e < C * C + 2 * C; e += blockDim.x) {
     const long long off = e < C * C     ? (long long)(hd * C + e / C) * C + e % C
                           : e < C * C + C ? (long long)dim * C + hd * C + (e - C * C)
                                           : (long long)dim * C + dim + hd * C + (e - C * C - C);
-    float acc = 0.f;
-    for (int k = 0; k < nparts; ++k) acc += p[k * stride + off];
+    const float v = __ldg(p + off);
     if (e < C * C)
-      sa[e] = acc;
+      sa[e] = v;
     else
-      sn[e - C * C] = acc;
+      sn[e - C * C] = v;
   }
+  for (int e = threadIdx.x; e < dim * C; e += blockDim.x)
+    sw[e] = __ldg(wo + (long long)(e / C) * dim + hd * C + e % C);
   __syncthreads();
   if (threadIdx.x < C) {
+    // row i of the softmax in place in sa (logits, then exponentials, then probabilities)
     const int i = threadIdx.x;
+    float* row = sa + i * C;
     const float nq = fmaxf(sqrtf(sn[i]), 1e-12f);
-    float vals[C];
     float mx = -INFINITY;
     for (int j = 0; j < C; ++j) {
       const float nk = fmaxf(sqrtf(sn[C + j]), 1e-12f);
-      const float v = sa[i * C + j] / (nq * nk) * temp[hd];
-      vals[j] = v;
+      const float v = row[j] / (nq * nk) * temp[hd];
+      row[j] = v;
       mx = fmaxf(mx, v);
     }
     float sum = 0.f;
     for (int j = 0; j < C; ++j) {
-      vals[j] = expf(vals[j] - mx);
-      sum += vals[j];
+      const float e = expf(row[j] - mx);
+      row[j] = e;
+      sum += e;
     }
-    for (int j = 0; j < C; ++j) sa[i * C + j] = vals[j] / sum;
+    for (int j = 0; j < C; ++j) row[j] = row[j] / sum;
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < dim * C; idx += blockDim.x) {
     const int r = idx / C, jj = idx % C, j = hd * C + jj;
-    const float* W = wo + (long long)r * dim + hd * C;
     float acc = 0.f;
-    for (int i = 0; i < C; ++i) acc = fmaf(__ldg(W + i), sa[i * C + jj], acc);
+#pragma unroll 8
+    for (int i = 0; i < C; ++i) acc = fmaf(sw[r * C + i], sa[i * C + jj], acc);
     const int cc = j / kc, col = j % kc, nt = r / bn, rr = r % bn;
     const int f = kc == 64 ? (rr & 7) : kc == 32 ? ((rr >> 1) & 3) : ((rr >> 2) & 1);
     __half* blk =
@@ -1242,11 +1254,11 @@ static float* attention_weights(const TView& qkv, int heads, const float* temp, 
 
 static bool fold_fused(int dim, int heads, const ConvLayer& L) {
   const int c = dim / heads;
-  return (c == 16 || c == 32) && L.npad == dim && L.cin_pad == dim;
+  return (c == 16 || c == 32) && dim <= 256 && L.npad == dim && L.cin_pad == dim;
 }
 
 int attention_fold_launches(int dim, int heads, const ConvLayer& L) {
-  return fold_fused(dim, heads, L) ? 2 : 4;
+  return fold_fused(dim, heads, L) ? 3 : 4;
 }
 
 void launch_attention_fold(const TView& qkv, int heads, const float* temp, const float* wo,
@@ -1254,21 +1266,26 @@ void launch_attention_fold(const TView& qkv, int heads, const float* temp, const
                            int sms, cudaStream_t s) {
   const int dim = qkv.c / 3;
   const int c = dim / heads;
+  const int n = qkv.n;
   if (fold_fused(dim, heads, L)) {
-    const GramPlan gp = gram_plan(qkv.n, dim, heads, qkv.h * qkv.w, sms);
+    // Gram partial slots, their ordered sum (one wide launch), then softmax + fold per head
+    const GramPlan gp = gram_plan(n, dim, heads, qkv.h * qkv.w, sms);
     const long long stride = (long long)dim * c + 2 * dim;
     attention_weights(qkv, heads, temp, scratch, sms, s, /*gram_only=*/true);
-    dim3 g(heads, qkv.n);
+    float* red = scratch + (size_t)n * gp.nparts * stride;
+    attn_reduce_kernel<<<blocks_for((long long)n * stride, 256), 256, 0, s>>>(scratch, gp.nparts,
+                                                                             stride, n, red);
+    dim3 g(heads, n);
     if (c == 32)
-      attn_fold_fused_kernel<32><<<g, 256, 0, s>>>(scratch, gp.nparts, stride, temp, wo, dim,
-                                                   wscale, wout, L.npad, L.cin_pad, L.kc, L.bn);
+      attn_fold_fused_kernel<32><<<g, 256, 0, s>>>(red, stride, temp, wo, dim, wscale, wout,
+                                                   L.npad, L.cin_pad, L.kc, L.bn);
     else
-      attn_fold_fused_kernel<16><<<g, 256, 0, s>>>(scratch, gp.nparts, stride, temp, wo, dim,
-                                                   wscale, wout, L.npad, L.cin_pad, L.kc, L.bn);
+      attn_fold_fused_kernel<16><<<g, 256, 0, s>>>(red, stride, temp, wo, dim, wscale, wout,
+                                                   L.npad, L.cin_pad, L.kc, L.bn);
     return;
   }
   const float* attn = attention_weights(qkv, heads, temp, scratch, sms, s);
-  dim3 g(blocks_for((long long)L.npad * L.cin_pad, 256), qkv.n);
+  dim3 g(blocks_for((long long)L.npad * L.cin_pad, 256), n);
   attn_fold_kernel<<<g, 256, 0, s>>>(wo, attn, dim, dim / heads, wscale, wout, L.npad,
                                      L.cin_pad, L.kc, L.bn);
 }
