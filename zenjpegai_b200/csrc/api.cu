@@ -156,6 +156,11 @@ int zjai_ctx_destroy(zjai_ctx* ctx) {
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
   if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
+  for (cudaStream_t gs : ctx->group_streams) {
+    cudaStreamSynchronize(gs);
+    cudaStreamDestroy(gs);
+  }
+  for (cudaEvent_t ge : ctx->group_events) cudaEventDestroy(ge);
   if (ctx->stream2) cudaStreamDestroy(ctx->stream2);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;

@@ -4,9 +4,12 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <array>
 #include <atomic>
 #include <cstdint>
+#include <map>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/zjai.h"
@@ -72,6 +75,13 @@ struct Ctx {
   // about 2 s), zjai_ctx_set_wait_limit
   long long wait_cycles = 0;
   std::atomic<long long> launches{0};
+  // Tiled synthesis runs the shape groups' chains concurrently once their arena needs are
+  // known: per group key (operating point, tile h, w, latent h, w, batch) the bytes its luma
+  // and its chroma chains took from the arenas, recorded by a sequential call; and a pool of
+  // streams (luma, chroma per group) and events for the fork and join.
+  std::map<std::array<int, 6>, std::pair<size_t, size_t>> group_need;
+  std::vector<cudaStream_t> group_streams;
+  std::vector<cudaEvent_t> group_events;
   // driver entry point
   void* encode_fn = nullptr;
   int driver_version = 0;

@@ -962,26 +962,41 @@ __global__ void attn_fold_kernel(const float* __restrict__ wo, const float* __re
   blk[rr * kc + (((col >> 3) ^ f) << 3) + (col & 7)] = __float2half_rn(acc * s);
 }
 
-// attn_softmax_kernel + attn_fold_kernel in one launch for the common shapes (c = 16 or 32,
-// packed layer without padding rows or columns), after attn_reduce_kernel: block (head hd,
-// picture n) reads the head's reduced Gram block and norms, takes the c x c softmax (one
-// thread per row) and writes the head's columns of W_o . blockdiag(A) in the packed layout
-// from the head's W_o columns staged in shared memory (dim <= 256).
+// attn_reduce_kernel + attn_softmax_kernel + attn_fold_kernel in one launch for the common
+// shapes (c = 16 or 32, packed layer without padding rows or columns, power-of-two kc / bn):
+// block (head hd, picture n) of kFoldThreads threads
+//  1. sums the head's Gram block and norms over the partial slots (every thread eight slots
+//     in flight, the same fixed combination as attn_reduce_kernel),
+//  2. takes the c x c softmax with a warp per row (32 / c rows per warp, shuffle reductions of
+//     the row max and sum in a fixed tree),
+//  3. writes the head's columns of W_o . blockdiag(A) in the packed layout from the head's W_o
+//     columns staged in shared memory (dim <= 256).
+constexpr int kFoldThreads = 512;
 template <int C>
-__global__ void __launch_bounds__(256) attn_fold_fused_kernel(
-    const float* __restrict__ red, long long stride, const float* __restrict__ temp,
+__global__ void __launch_bounds__(kFoldThreads) attn_fold_fused_kernel(
+    const float* __restrict__ part, int nparts, long long stride, const float* __restrict__ temp,
     const float* __restrict__ wo, int dim, float s, __half* __restrict__ wout, int npad,
-    int cin_pad, int kc, int bn) {
-  __shared__ float sa[C * C];      // the head's Gram block, then its attention matrix
-  __shared__ float sn[2 * C];      // q norms of its rows, k norms of its columns
-  __shared__ float sw[256 * C];    // W_o[r][hd * C + i] at sw[r * C + i]
+    int cin_pad, int lkc, int lbn) {
+  __shared__ float sa[C * C];    // the head's Gram block, then its attention matrix
+  __shared__ float sn[2 * C];    // q norms of its rows, k norms of its columns
+  __shared__ float sw[256 * C];  // W_o[r][hd * C + i] at sw[r * C + i]
   const int hd = blockIdx.x, n = blockIdx.y;
-  const float* p = red + (long long)n * stride;
+  const float* p = part + (long long)n * nparts * stride;
   for (int e = threadIdx.x; e < C * C + 2 * C; e += blockDim.x) {
     const long long off = e < C * C     ? (long long)(hd * C + e / C) * C + e % C
                           : e < C * C + C ? (long long)dim * C + hd * C + (e - C * C)
                                           : (long long)dim * C + dim + hd * C + (e - C * C - C);
-    const float v = __ldg(p + off);
+    const float* q = p + off;
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int k = 0;
+    for (; k + 8 <= nparts; k += 8) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] += __ldg(q + (long long)(k + j) * stride);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (k + j < nparts) a[j] += __ldg(q + (long long)(k + j) * stride);
+    const float v = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
     if (e < C * C)
       sa[e] = v;
     else
@@ -990,37 +1005,39 @@ __global__ void __launch_bounds__(256) attn_fold_fused_kernel(
   for (int e = threadIdx.x; e < dim * C; e += blockDim.x)
     sw[e] = __ldg(wo + (long long)(e / C) * dim + hd * C + e % C);
   __syncthreads();
-  if (threadIdx.x < C) {
-    // row i of the softmax in place in sa (logits, then exponentials, then probabilities)
-    const int i = threadIdx.x;
-    float* row = sa + i * C;
-    const float nq = fmaxf(sqrtf(sn[i]), 1e-12f);
-    float mx = -INFINITY;
-    for (int j = 0; j < C; ++j) {
-      const float nk = fmaxf(sqrtf(sn[C + j]), 1e-12f);
-      const float v = row[j] / (nq * nk) * temp[hd];
-      row[j] = v;
-      mx = fmaxf(mx, v);
+  {
+    // softmax: lane l of a warp is column l % C of row (warp * 32 + l) / C (+ 32 / C rows per
+    // pass over the warps)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int RPW = 32 / C;  // rows per warp per pass
+    const int j = lane % C;
+    const float tmp = temp[hd];
+    const float nk = fmaxf(sqrtf(sn[C + j]), 1e-12f);
+    for (int i = warp * RPW + lane / C; i < C; i += (kFoldThreads / 32) * RPW) {
+      const float nq = fmaxf(sqrtf(sn[i]), 1e-12f);
+      const float v = sa[i * C + j] / (nq * nk) * tmp;
+      float mx = v;
+#pragma unroll
+      for (int o = C / 2; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float ex = expf(v - mx);
+      float sum = ex;
+#pragma unroll
+      for (int o = C / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      sa[i * C + j] = ex / sum;
     }
-    float sum = 0.f;
-    for (int j = 0; j < C; ++j) {
-      const float e = expf(row[j] - mx);
-      row[j] = e;
-      sum += e;
-    }
-    for (int j = 0; j < C; ++j) row[j] = row[j] / sum;
   }
   __syncthreads();
+  const int kc = 1 << lkc, bnm = (1 << lbn) - 1;
   for (int idx = threadIdx.x; idx < dim * C; idx += blockDim.x) {
     const int r = idx / C, jj = idx % C, j = hd * C + jj;
     float acc = 0.f;
 #pragma unroll 8
     for (int i = 0; i < C; ++i) acc = fmaf(sw[r * C + i], sa[i * C + jj], acc);
-    const int cc = j / kc, col = j % kc, nt = r / bn, rr = r % bn;
+    const int cc = j >> lkc, col = j & (kc - 1), nt = r >> lbn, rr = r & bnm;
     const int f = kc == 64 ? (rr & 7) : kc == 32 ? ((rr >> 1) & 3) : ((rr >> 2) & 1);
-    __half* blk =
-        wout + (long long)n * npad * cin_pad + ((long long)cc * (npad / bn) + nt) * bn * kc;
-    blk[rr * kc + (((col >> 3) ^ f) << 3) + (col & 7)] = __float2half_rn(acc * s);
+    __half* blk = wout + (long long)n * npad * cin_pad +
+                  ((((long long)cc * (npad >> lbn) + nt) << lbn) << lkc);
+    blk[(rr << lkc) + (((col >> 3) ^ f) << 3) + (col & 7)] = __float2half_rn(acc * s);
   }
 }
 
@@ -1189,8 +1206,8 @@ static GramPlan gram_plan(int n, int dim, int heads, int npix, int sms) {
     // two blocks per SM (registers allow two) over the whole batch, one wave, whole chunks
     // per block; 8 / heads warps share a head's pixels (the slices)
     const int chunks = (npix + kGramChunk - 1) / kGramChunk;
-    // (at most 32 blocks per picture: small batches keep few partial slots to sum)
-    const int splits = std::max(1, std::min(std::min(chunks, 32), (2 * sms) / std::max(1, n)));
+    // (at most 16 blocks per picture: small batches keep few partial slots to sum)
+    const int splits = std::max(1, std::min(std::min(chunks, 16), (2 * sms) / std::max(1, n)));
     g.per_block = ((chunks + splits - 1) / splits) * kGramChunk;
     g.blocks = (npix + g.per_block - 1) / g.per_block;
     g.nparts = g.blocks * (8 / heads);
@@ -1252,13 +1269,16 @@ static float* attention_weights(const TView& qkv, int heads, const float* temp, 
   return attn;
 }
 
+static bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
+
 static bool fold_fused(int dim, int heads, const ConvLayer& L) {
   const int c = dim / heads;
-  return (c == 16 || c == 32) && dim <= 256 && L.npad == dim && L.cin_pad == dim;
+  return (c == 16 || c == 32) && dim <= 256 && L.npad == dim && L.cin_pad == dim &&
+         pow2(L.kc) && pow2(L.bn);
 }
 
 int attention_fold_launches(int dim, int heads, const ConvLayer& L) {
-  return fold_fused(dim, heads, L) ? 3 : 4;
+  return fold_fused(dim, heads, L) ? 2 : 4;
 }
 
 void launch_attention_fold(const TView& qkv, int heads, const float* temp, const float* wo,
@@ -1268,20 +1288,20 @@ void launch_attention_fold(const TView& qkv, int heads, const float* temp, const
   const int c = dim / heads;
   const int n = qkv.n;
   if (fold_fused(dim, heads, L)) {
-    // Gram partial slots, their ordered sum (one wide launch), then softmax + fold per head
+    // Gram partial slots, then their ordered sum + softmax + fold per (head, picture)
     const GramPlan gp = gram_plan(n, dim, heads, qkv.h * qkv.w, sms);
     const long long stride = (long long)dim * c + 2 * dim;
     attention_weights(qkv, heads, temp, scratch, sms, s, /*gram_only=*/true);
-    float* red = scratch + (size_t)n * gp.nparts * stride;
-    attn_reduce_kernel<<<blocks_for((long long)n * stride, 256), 256, 0, s>>>(scratch, gp.nparts,
-                                                                             stride, n, red);
+    const int lkc = __builtin_ctz((unsigned)L.kc), lbn = __builtin_ctz((unsigned)L.bn);
     dim3 g(heads, n);
     if (c == 32)
-      attn_fold_fused_kernel<32><<<g, 256, 0, s>>>(red, stride, temp, wo, dim, wscale, wout,
-                                                   L.npad, L.cin_pad, L.kc, L.bn);
+      attn_fold_fused_kernel<32><<<g, kFoldThreads, 0, s>>>(scratch, gp.nparts, stride, temp, wo,
+                                                            dim, wscale, wout, L.npad, L.cin_pad,
+                                                            lkc, lbn);
     else
-      attn_fold_fused_kernel<16><<<g, 256, 0, s>>>(red, stride, temp, wo, dim, wscale, wout,
-                                                   L.npad, L.cin_pad, L.kc, L.bn);
+      attn_fold_fused_kernel<16><<<g, kFoldThreads, 0, s>>>(scratch, gp.nparts, stride, temp, wo,
+                                                            dim, wscale, wout, L.npad, L.cin_pad,
+                                                            lkc, lbn);
     return;
   }
   const float* attn = attention_weights(qkv, heads, temp, scratch, sms, s);

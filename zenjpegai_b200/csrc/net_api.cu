@@ -43,10 +43,12 @@ Runner make_runner(Ctx* ctx, Net* net, Arena* arena, cudaStream_t s, int n,
   return r;
 }
 
-// Sync after a failure so the context and its arena stay usable.
+// Sync after a failure so the context and its arena stay usable (the group streams too: a
+// failure or cancellation can leave chains of a concurrent tiled synthesis enqueued).
 int settle(Ctx* ctx, int st) {
   cudaStreamSynchronize(ctx->stream);
   cudaStreamSynchronize(ctx->stream2);
+  for (cudaStream_t gs : ctx->group_streams) cudaStreamSynchronize(gs);
   return st;
 }
 
@@ -54,9 +56,101 @@ int settle(Ctx* ctx, int st) {
 
 namespace zjai {
 
-// Synthesis of the listed tiles: same-shape tiles run as one batch; luma on ctx->stream with
-// ctx->arena, chroma on ctx->stream2 with ctx->arena2 (reconstruct.rs:314-323 runs the two
-// components side by side). Output planes are device pointers.
+// One shape group of a tiled synthesis: the latent windows of its tiles gathered into one
+// batch, the luma network on stream `sy` with arena `ay`, the chroma network on `sc` with `ac`
+// (after the gather). Output planes are device pointers.
+struct GroupJob {
+  int img_h, img_w, lat_h, lat_w;
+  std::vector<int> idx;
+};
+
+static int run_group(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const float* lat_uv, int lh,
+                     int lw, const std::vector<zjai_tile>& tiles, const GroupJob& g, int out_h,
+                     int out_w, int sv, int sh, float* rec_y, float* rec_u, float* rec_v,
+                     const volatile int* cancel, double* flops, int qbytes, float qmax,
+                     cudaStream_t sy, cudaStream_t sc, Arena* ay, Arena* ac, cudaEvent_t ev) {
+  const int n = (int)g.idx.size();
+  const int cw_ = cdiv(out_w, sh);
+  std::vector<int> origin, win;
+  for (int i : g.idx) {
+    const zjai_tile& t = tiles[i];
+    origin.push_back(t.lat_x);
+    origin.push_back(t.lat_y);
+    win.insert(win.end(), {t.img_y, t.img_x, t.core_y, std::min(t.core_y + t.core_h, out_h),
+                           t.core_x, std::min(t.core_x + t.core_w, out_w)});
+  }
+  // each stream reads descriptor copies from its own arena
+  int *d_origin, *d_origin2, *d_win_y, *d_win_uv;
+  ZJAI_TRY(upload_ints(ctx, ay, origin, sy, &d_origin));
+  ZJAI_TRY(upload_ints(ctx, ay, win, sy, &d_win_y));
+  ZJAI_TRY(upload_ints(ctx, ac, origin, sc, &d_origin2));
+  ZJAI_TRY(upload_ints(ctx, ac, win, sc, &d_win_uv));
+  // latent windows: [n][lat_h][lat_w][256] = luma 160 | chroma 96 (luma stream)
+  TView cat;
+  ZJAI_TRY(alloc_tensor(ctx, n, g.lat_h, g.lat_w, 256, &cat, false, ay, sy));
+  launch_gather_latent(lat_y, 160, lh, lw, d_origin, cat.channels(0, 160), sy);
+  launch_gather_latent(lat_uv, 96, lh, lw, d_origin, cat.channels(160, 96), sy);
+  ctx->launches += 2;
+  ZJAI_TRY(cuda_check(cudaEventRecord(ev, sy), "event"));
+  // luma
+  {
+    Runner r = make_runner(ctx, ny, ay, sy, n, cancel);
+    r.count_flops = flops != nullptr;
+    FinalOut fo;
+    fo.plane0 = rec_y;
+    fo.row = out_w;
+    fo.win = d_win_y;
+    fo.qbytes = qbytes;
+    fo.qmax = qmax;
+    ZJAI_TRY(r.primary(cat.channels(0, 160), g.img_h, g.img_w, fo));
+    if (flops) *flops += r.flops;
+  }
+  // chroma (reads `cat`, gathered on the luma stream)
+  ZJAI_TRY(cuda_check(cudaStreamWaitEvent(sc, ev, 0), "event wait"));
+  {
+    Runner r = make_runner(ctx, nuv, ac, sc, n, cancel);
+    r.count_flops = flops != nullptr;
+    TView x144;
+    ZJAI_TRY(alloc_tensor(ctx, n, g.lat_h, g.lat_w, 144, &x144, false, ac, sc));
+    launch_gather_latent(lat_uv, 96, lh, lw, d_origin2, x144.channels(48, 96), sc);
+    ctx->launches++;
+    FinalOut fo;
+    fo.plane0 = rec_u;
+    fo.plane1 = rec_v;
+    fo.row = cw_;
+    fo.win = d_win_uv;
+    fo.sv = sv;
+    fo.sh = sh;
+    fo.qbytes = qbytes;
+    fo.qmax = qmax;
+    ZJAI_TRY(r.secondary(cat, x144, g.img_h, g.img_w, fo));
+    if (flops) *flops += r.flops;
+  }
+  return ZJAI_OK;
+}
+
+// The pool of group streams / events, created on first use.
+static int group_pool(Ctx* ctx, size_t streams, size_t events) {
+  while (ctx->group_streams.size() < streams) {
+    cudaStream_t s;
+    ZJAI_TRY(cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream"));
+    ctx->group_streams.push_back(s);
+  }
+  while (ctx->group_events.size() < events) {
+    cudaEvent_t e;
+    ZJAI_TRY(cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event"));
+    ctx->group_events.push_back(e);
+  }
+  return ZJAI_OK;
+}
+
+// Synthesis of the listed tiles: same-shape tiles run as one batch, luma and chroma of a batch
+// on two streams (reconstruct.rs:314-323 runs the two components side by side). The shape
+// groups' chains (e.g. interior, bottom-row, right-column and corner tiles) run one after
+// another on the context's two streams the first time a group shape is seen, which records how
+// much of each arena every chain takes; once every group's needs are known and fit, each group
+// runs on its own pair of streams in its own slice of the arenas, so the small groups' chains
+// overlap the large one's. Output planes are device pointers.
 int synthesize_tiles_dev(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const float* lat_uv,
                          int lh, int lw, const std::vector<zjai_tile>& tiles, int out_h, int out_w,
                          int sv, int sh, float* rec_y, float* rec_u, float* rec_v,
@@ -68,83 +162,94 @@ int synthesize_tiles_dev(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const 
   if (!ny || !nuv || ny->kind != ZJAI_SYN_Y || nuv->kind != ZJAI_SYN_UV || ny->op != nuv->op)
     return fail(ZJAI_INVALID_ARGUMENT, "synthesize: needs a SYN_Y and a SYN_UV network of one op");
   if (sv <= 0 || sh <= 0) return fail(ZJAI_INVALID_DATA, "chroma subsampling factor");
-  const int cw_ = cdiv(out_w, sh);
-  // group same-shape tiles
-  std::map<std::tuple<int, int, int, int>, std::vector<int>> groups;
+  // group same-shape tiles (largest group first: it sets the critical path)
+  std::map<std::tuple<int, int, int, int>, std::vector<int>> by_shape;
   for (size_t i = 0; i < tiles.size(); ++i) {
     const zjai_tile& t = tiles[i];
     if (t.lat_x < 0 || t.lat_y < 0 || t.lat_x + t.lat_w > lw || t.lat_y + t.lat_h > lh)
       return fail(ZJAI_INVALID_DATA, "synthesis tile outside the latent");
-    groups[std::make_tuple(t.img_h, t.img_w, t.lat_h, t.lat_w)].push_back((int)i);
+    by_shape[std::make_tuple(t.img_h, t.img_w, t.lat_h, t.lat_w)].push_back((int)i);
   }
-  // while profiling, chroma runs after luma on one stream so per-layer events see no overlap
-  cudaStream_t s1 = ctx->stream, s2 = ctx->profiling ? ctx->stream : ctx->stream2;
-  ZJAI_TRY(cuda_check(cudaEventRecord(ctx->ev_fork, s1), "event"));
-  ZJAI_TRY(cuda_check(cudaStreamWaitEvent(s2, ctx->ev_fork, 0), "event wait"));
-  for (auto& kv : groups) {
-    if (cancel && *cancel) return fail(ZJAI_CANCELLED, "stopped: cancelled by the caller");
-    const int img_h = std::get<0>(kv.first), img_w = std::get<1>(kv.first);
-    const int lat_h = std::get<2>(kv.first), lat_w = std::get<3>(kv.first);
-    const std::vector<int>& idx = kv.second;
-    const int n = (int)idx.size();
-    std::vector<int> origin, win;
-    for (int i : idx) {
-      const zjai_tile& t = tiles[i];
-      origin.push_back(t.lat_x);
-      origin.push_back(t.lat_y);
-      win.insert(win.end(), {t.img_y, t.img_x, t.core_y, std::min(t.core_y + t.core_h, out_h),
-                             t.core_x, std::min(t.core_x + t.core_w, out_w)});
+  std::vector<GroupJob> groups;
+  for (auto& kv : by_shape)
+    groups.push_back({std::get<0>(kv.first), std::get<1>(kv.first), std::get<2>(kv.first),
+                      std::get<3>(kv.first), kv.second});
+  std::stable_sort(groups.begin(), groups.end(), [](const GroupJob& a, const GroupJob& b) {
+    return a.idx.size() * a.img_h * a.img_w > b.idx.size() * b.img_h * b.img_w;
+  });
+  auto key = [&](const GroupJob& g) {
+    return std::array<int, 6>{ny->op, g.img_h, g.img_w, g.lat_h, g.lat_w, (int)g.idx.size()};
+  };
+  // concurrent chains when every group's arena needs are known and fit
+  bool concurrent = !ctx->profiling && groups.size() > 1 && groups.size() <= 4;
+  size_t sum_y = 0, sum_c = 0;
+  for (const GroupJob& g : groups) {
+    auto it = ctx->group_need.find(key(g));
+    if (it == ctx->group_need.end()) {
+      concurrent = false;
+      break;
     }
-    // each stream reads descriptor copies from its own arena
-    int *d_origin, *d_origin2, *d_win_y, *d_win_uv;
-    ZJAI_TRY(upload_ints(ctx, &ctx->arena, origin, s1, &d_origin));
-    ZJAI_TRY(upload_ints(ctx, &ctx->arena, win, s1, &d_win_y));
-    ZJAI_TRY(upload_ints(ctx, &ctx->arena2, origin, s2, &d_origin2));
-    ZJAI_TRY(upload_ints(ctx, &ctx->arena2, win, s2, &d_win_uv));
-    // latent windows: [n][lat_h][lat_w][256] = luma 160 | chroma 96 (stream 1)
-    TView cat;
-    ZJAI_TRY(alloc_tensor(ctx, n, lat_h, lat_w, 256, &cat, false, &ctx->arena, s1));
-    launch_gather_latent(lat_y, 160, lh, lw, d_origin, cat.channels(0, 160), s1);
-    launch_gather_latent(lat_uv, 96, lh, lw, d_origin, cat.channels(160, 96), s1);
-    ctx->launches += 2;
+    // slack for the 256-byte alignment of each slice
+    sum_y += it->second.first + 1024;
+    sum_c += it->second.second + 1024;
+  }
+  if (concurrent && (sum_y > ctx->arena.cap - ctx->arena.top || sum_c > ctx->arena2.cap - ctx->arena2.top))
+    concurrent = false;
+  if (!concurrent) {
+    // while profiling, chroma runs after luma on one stream so per-layer events see no overlap
+    cudaStream_t s1 = ctx->stream, s2 = ctx->profiling ? ctx->stream : ctx->stream2;
     ZJAI_TRY(cuda_check(cudaEventRecord(ctx->ev_fork, s1), "event"));
-    // luma
-    {
-      Runner r = make_runner(ctx, ny, &ctx->arena, s1, n, cancel);
-      r.count_flops = flops != nullptr;
-      FinalOut fo;
-      fo.plane0 = rec_y;
-      fo.row = out_w;
-      fo.win = d_win_y;
-      fo.qbytes = qbytes;
-      fo.qmax = qmax;
-      ZJAI_TRY(r.primary(cat.channels(0, 160), img_h, img_w, fo));
-      if (flops) *flops += r.flops;
-    }
-    // chroma
     ZJAI_TRY(cuda_check(cudaStreamWaitEvent(s2, ctx->ev_fork, 0), "event wait"));
-    {
-      Runner r = make_runner(ctx, nuv, &ctx->arena2, s2, n, cancel);
-      r.count_flops = flops != nullptr;
-      TView x144;
-      ZJAI_TRY(alloc_tensor(ctx, n, lat_h, lat_w, 144, &x144, false, &ctx->arena2, s2));
-      launch_gather_latent(lat_uv, 96, lh, lw, d_origin2, x144.channels(48, 96), s2);
-      ctx->launches++;
-      FinalOut fo;
-      fo.plane0 = rec_u;
-      fo.plane1 = rec_v;
-      fo.row = cw_;
-      fo.win = d_win_uv;
-      fo.sv = sv;
-      fo.sh = sh;
-      fo.qbytes = qbytes;
-      fo.qmax = qmax;
-      ZJAI_TRY(r.secondary(cat, x144, img_h, img_w, fo));
-      if (flops) *flops += r.flops;
+    for (const GroupJob& g : groups) {
+      if (cancel && *cancel) return fail(ZJAI_CANCELLED, "stopped: cancelled by the caller");
+      const size_t m1 = ctx->arena.top, m2 = ctx->arena2.top;
+      ctx->arena.peak = m1;
+      ctx->arena2.peak = m2;
+      ZJAI_TRY(run_group(ctx, ny, nuv, lat_y, lat_uv, lh, lw, tiles, g, out_h, out_w, sv, sh,
+                         rec_y, rec_u, rec_v, cancel, flops, qbytes, qmax, s1, s2, &ctx->arena,
+                         &ctx->arena2, ctx->ev_fork));
+      ctx->group_need[key(g)] = {ctx->arena.peak - m1, ctx->arena2.peak - m2};
+    }
+    ZJAI_TRY(cuda_check(cudaEventRecord(ctx->ev_join, s2), "event"));
+    return cuda_check(cudaStreamWaitEvent(s1, ctx->ev_join, 0), "event wait");
+  }
+  const size_t ng = groups.size();
+  // events: fork, then per group one for its gather and one each for its two chains' ends
+  ZJAI_TRY(group_pool(ctx, 2 * ng, 1 + 3 * ng));
+  cudaEvent_t fork = ctx->group_events[0];
+  ZJAI_TRY(cuda_check(cudaEventRecord(fork, ctx->stream), "event"));
+  std::vector<Arena> ay(ng), ac(ng);
+  for (size_t i = 0; i < ng; ++i) {
+    const auto& need = ctx->group_need[key(groups[i])];
+    auto carve = [](Arena& main, size_t bytes, Arena* sub) {
+      const size_t start = (main.top + 255) & ~size_t(255);
+      sub->base = main.base + start;
+      sub->cap = bytes + 768;
+      sub->top = sub->peak = 0;
+      main.top = start + sub->cap;
+      main.peak = std::max(main.peak, main.top);
+    };
+    carve(ctx->arena, need.first, &ay[i]);
+    carve(ctx->arena2, need.second, &ac[i]);
+  }
+  for (size_t i = 0; i < ng; ++i) {
+    if (cancel && *cancel) return fail(ZJAI_CANCELLED, "stopped: cancelled by the caller");
+    cudaStream_t sy = ctx->group_streams[2 * i], sc = ctx->group_streams[2 * i + 1];
+    ZJAI_TRY(cuda_check(cudaStreamWaitEvent(sy, fork, 0), "event wait"));
+    ZJAI_TRY(cuda_check(cudaStreamWaitEvent(sc, fork, 0), "event wait"));
+    ZJAI_TRY(run_group(ctx, ny, nuv, lat_y, lat_uv, lh, lw, tiles, groups[i], out_h, out_w, sv,
+                       sh, rec_y, rec_u, rec_v, cancel, flops, qbytes, qmax, sy, sc, &ay[i],
+                       &ac[i], ctx->group_events[1 + 3 * i]));
+  }
+  // join every chain back into the context's stream
+  for (size_t i = 0; i < ng; ++i) {
+    for (int k = 0; k < 2; ++k) {
+      cudaEvent_t e = ctx->group_events[2 + 3 * i + k];
+      ZJAI_TRY(cuda_check(cudaEventRecord(e, ctx->group_streams[2 * i + k]), "event"));
+      ZJAI_TRY(cuda_check(cudaStreamWaitEvent(ctx->stream, e, 0), "event wait"));
     }
   }
-  ZJAI_TRY(cuda_check(cudaEventRecord(ctx->ev_join, s2), "event"));
-  return cuda_check(cudaStreamWaitEvent(s1, ctx->ev_join, 0), "event wait");
+  return ZJAI_OK;
 }
 
 }  // namespace zjai
