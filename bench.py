@@ -328,7 +328,9 @@ def config_dict(args, cfg, world):
     return {"workload": args.config + ": " + cfg["desc"],
             "picture": "%dx%d 4:2:0, 8-bit YUV out" % (cfg["W"], cfg["H"]),
             "tiles": cfg.get("ntiles"),
-            "parallelism": "tiles round-robin over %d GPU(s), NCCL reduce of 8-bit cores" % world,
+            "parallelism": "tiles round-robin over %d GPU(s), each rank sent only the latent "
+                           "rows / columns its tiles read" % world,
+            "gather": cfg.get("gather", "none (one GPU)") if world > 1 else "none (one GPU)",
             "weights": "random-init, seed %d (role-scaled normal)" % cfg["seed"],
             "l2": "flushed between steps (256 MiB write, outside the timed events)",
             "precision": "f16 operands, f32 accumulation (TMEM); the CPU arm computes f32"}
@@ -475,24 +477,49 @@ def main():
         ly, luv = ly_h.cuda(), luv_h.cuda()
         tiles = zj.synthesis_tiles(H, W, lh, lw, cfg["tile"], cfg["overlap"])
         mine = sharding.shard_tiles(tiles, rank, world)
+        if world > 1:
+            # each rank receives only the latent rows / columns its tiles read
+            ly_h, luv_h, mine = sharding.compact_latent(mine, ly_h, luv_h)
+            ly_h, luv_h = ly_h.pin_memory(), luv_h.pin_memory()
+            ly, luv = ly_h.cuda(), luv_h.cuda()
         out8 = torch.zeros(H * W + 2 * ch * cw, dtype=torch.uint8, device="cuda")
+        sizes = (H * W, ch * cw, ch * cw)
         # the 8-bit planes of the picture, written by the final layers (fused output stage)
         planes8 = (out8[:H * W].view(H, W), out8[H * W:H * W + ch * cw].view(ch, cw),
                    out8[H * W + ch * cw:].view(ch, cw))
         out8_host = torch.empty_like(out8, device="cpu").pin_memory()
         out_px = H * W
-        h2d = world * (ly_h.numel() + luv_h.numel()) * 4
+        peer = None
+        if world > 1:
+            # final gather: every rank's epilogue writes its cores into rank 0's planes over
+            # NVLink (CUDA IPC); the NCCL sum-reduce of zero-elsewhere planes where it cannot
+            peer = sharding.PeerPlanes(eng, dist, out8 if rank == 0 else None, sizes)
+            if peer.ok:
+                closers.append(peer.close)
+            else:
+                peer = None
+        cfg["gather"] = ("NVLink peer writes of the 8-bit cores into rank 0's planes (CUDA IPC)"
+                         if peer else "NCCL reduce of zero-elsewhere 8-bit planes")
+        h2d_t = torch.tensor([float(ly_h.numel() + luv_h.numel()) * 4], dtype=torch.float64,
+                             device="cuda")
+        if world > 1:
+            dist.all_reduce(h2d_t)
+        h2d = int(h2d_t.item())
         d2h = out8.numel()
 
         def step(from_host=False):
             if from_host:
                 ly.copy_(ly_h, non_blocking=True)
                 luv.copy_(luv_h, non_blocking=True)
-            # every rank starts from a zero picture: the reduce sums the ranks' disjoint
-            # cores, so a plane still holding last step's picture would add it in again
-            out8.zero_()
-            dec.synthesize_tiles(ly, luv, mine, H, W, out=planes8, bit_depth=8)
-            sharding.gather_cores(out8, dist)
+            if peer is not None:
+                dec.synthesize_tiles(ly, luv, mine, H, W, out=peer.planes, bit_depth=8)
+                peer.done()
+            else:
+                if world > 1:
+                    # the reduce sums the ranks' disjoint cores: every rank starts from zero
+                    out8.zero_()
+                dec.synthesize_tiles(ly, luv, mine, H, W, out=planes8, bit_depth=8)
+                sharding.gather_cores(out8, dist)
             if from_host and rank == 0:
                 out8_host.copy_(out8, non_blocking=True)
     else:

@@ -222,6 +222,18 @@ int zjai_synthesize_q(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, const fl
                       void *rec_y, void *rec_u, void *rec_v, int mem,
                       const volatile int *cancel);
 
+/* Multi-GPU final gather without a collective (the crate has none: its tiles are gathered in
+ * one address space, reconstruct.rs:379-464). The process owning the picture exports the
+ * allocation holding its device planes (`ptr` may point inside it): a 64-byte CUDA IPC handle
+ * and the offset of `ptr` in the allocation. Another process on the same box maps it with
+ * zjai_ipc_import and passes the mapped pointer as the output planes of zjai_synthesize_tiles_q
+ * (mem = ZJAI_MEM_DEVICE): the final layers then store that rank's cores straight into the
+ * owner's planes over NVLink. The caller orders the owner's reads after the writers' work
+ * (e.g. a stream-ordered all-reduce after the synthesis); zjai_ipc_close unmaps. */
+int zjai_ipc_export(zjai_ctx *ctx, const void *ptr, void *handle, uint64_t *offset);
+int zjai_ipc_import(zjai_ctx *ctx, const void *handle, uint64_t offset, void **ptr);
+int zjai_ipc_close(zjai_ctx *ctx, void *ptr);
+
 /* ---------------------------------------------------------------------------------------- */
 /* Output stage (src/decoder/output.rs)                                                       */
 /* ---------------------------------------------------------------------------------------- */

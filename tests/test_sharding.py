@@ -71,7 +71,9 @@ def _worker(rank, world, port, q):
         ly, luv, py, puv = _picture()
         tiles = zo.synthesis_tiles(H, W, ly.shape[1], ly.shape[2], TILE, OVERLAP)
         mine = sharding.shard_tiles(tiles, rank, world)
-        buf = _pack8(*_synth_tiles(mine, ly, luv, py, puv))
+        # the rank receives only the latent rows / columns its tiles read
+        cly, cluv, cmine = sharding.compact_latent(mine, ly, luv)
+        buf = _pack8(*_synth_tiles(cmine, cly, cluv, py, puv))
         sharding.gather_cores(buf, dist)
         if rank == 0:
             q.put(buf.numpy().copy())
@@ -88,6 +90,31 @@ def test_shard_partition():
         assert sorted(seen) == sorted(id(t) for t in tiles)
     with pytest.raises(ValueError):
         sharding.shard_tiles(tiles, 2, 2)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_compact_latent_windows(world):
+    """Every tile's latent window read from its rank's compacted latent equals the window of
+    the full latent (4K config-4 tiling), and the compacted latent is no larger than needed."""
+    lh, lw = 135, 240
+    ly = syn.laplace_latent(32, "cl/ly", (160, lh, lw), 1.5)
+    luv = syn.laplace_latent(32, "cl/luv", (96, lh, lw), 1.5)
+    tiles = zo.synthesis_tiles(2160, 3840, lh, lw, 512, 16)
+    for r in range(world):
+        mine = sharding.shard_tiles(tiles, r, world)
+        cly, cluv, cmine = sharding.compact_latent(mine, ly, luv)
+        for t, u in zip(mine, cmine):
+            for k in ("img_x", "img_y", "core_x", "core_y", "core_w", "core_h", "lat_w", "lat_h"):
+                assert t[k] == u[k]
+            for full, comp in ((ly, cly), (luv, cluv)):
+                a = full[:, t["lat_y"]:t["lat_y"] + t["lat_h"], t["lat_x"]:t["lat_x"] + t["lat_w"]]
+                b = comp[:, u["lat_y"]:u["lat_y"] + u["lat_h"], u["lat_x"]:u["lat_x"] + u["lat_w"]]
+                assert np.array_equal(a, b)
+        cols = len({x for t in mine for x in range(t["lat_x"], t["lat_x"] + t["lat_w"])})
+        rows = len({y for t in mine for y in range(t["lat_y"], t["lat_y"] + t["lat_h"])})
+        assert cly.shape == (160, rows, cols)
+        if world == 8:
+            assert cly.shape[2] <= 32  # one tile column: 1/7.5 of the latent
 
 
 def test_two_rank_gather_reproduces_picture():

@@ -85,6 +85,9 @@ def lib():
     L.zjai_synthesis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _vp, _i]
     L.zjai_analysis_primary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
     L.zjai_analysis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
+    L.zjai_ipc_export.argtypes = [_vp, _vp, _vp, ctypes.POINTER(ctypes.c_uint64)]
+    L.zjai_ipc_import.argtypes = [_vp, _vp, ctypes.c_uint64, ctypes.POINTER(_vp)]
+    L.zjai_ipc_close.argtypes = [_vp, _vp]
     L.zjai_stage_create.argtypes = [_vp, _i, _i, _i, ctypes.POINTER(Param), _i,
                                      ctypes.POINTER(_vp)]
     L.zjai_stage_forward.argtypes = [_vp, _vp, _i, _i, _i, _vp, _i]
