@@ -57,8 +57,17 @@ class Tile(ctypes.Structure):
 DUMP_FN = ctypes.CFUNCTYPE(None, ctypes.c_char_p, _f, _i, _i, _i)
 
 
+class ATile(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_int) for k in (
+        "img_x", "img_y", "img_w", "img_h", "lat_x", "lat_y", "lat_w", "lat_h",
+        "core_x", "core_y", "core_w", "core_h", "off_x", "off_y")]
+
+
 def _declare(L):
     L.zo_set_threads.argtypes = [_i]
+    L.zo_preprocess_rgb.argtypes = [ctypes.c_void_p, _i, _i, _f, _f]
+    L.zo_analysis_tiles.argtypes = [_i, _i, _i, _i, _i, ctypes.c_void_p, _i]
+    L.zo_analyze_tiled.argtypes = [ctypes.c_void_p, _i, _i, _f, _i, _i, _f]
     L.zo_set_fast.argtypes = [_i]
     L.zo_conv2d_out_size.argtypes = [_i] * 7 + [ctypes.POINTER(_i)] * 3
     L.zo_conv2d.argtypes = [_f, _i, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i,
@@ -378,3 +387,35 @@ def quantize_rgb(r, g, b, bit_depth=8):
 
 def pad_amount(n, d):
     return lib().zo_pad_amount(n, d)
+
+
+def preprocess_rgb(rgb):
+    """`preprocess_rgb` (colour.rs:535-541): uint8 RGB [h, w, 3] -> (luma [1, h, w],
+    chroma [12, ph / 2, pw / 2]) in [0, 255]."""
+    rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+    h, w, _ = rgb.shape
+    luma = np.empty((1, h, w), np.float32)
+    chroma = np.empty((12, (h + h % 2) // 2, (w + w % 2) // 2), np.float32)
+    lib().zo_preprocess_rgb(rgb.ctypes.data, h, w, _fp(luma), _fp(chroma))
+    return luma, chroma
+
+
+def analysis_tiles(ccs, h, w, lh, lw):
+    """`analysis_tiles` (encoder/tiles.rs:51-156) as a list of dicts."""
+    n = lib().zo_analysis_tiles(ccs, h, w, lh, lw, None, 0)
+    if n <= 0:
+        raise ValueError("malformed analysis tiling")
+    arr = (ATile * n)()
+    lib().zo_analysis_tiles(ccs, h, w, lh, lw, ctypes.cast(arr, ctypes.c_void_p), n)
+    return [{k: getattr(t, k) for k, _ in ATile._fields_} for t in arr]
+
+
+def analyze_tiled(ck, op, ccs, x):
+    """Tiled analysis of component ccs: x [1 or 12, h, w] -> latent [160 or 96, ., .]."""
+    x = _c32(x)
+    _, h, w = x.shape
+    d = 8 if ccs else 16
+    out = np.empty((96 if ccs else 160, -(-h // d), -(-w // d)), np.float32)
+    if lib().zo_analyze_tiled(ctypes.byref(ck.ck), op, ccs, _fp(x), h, w, _fp(out)):
+        raise ValueError("analyze_tiled")
+    return out

@@ -1095,3 +1095,138 @@ void zo_quantize_rgb(const float *r, const float *g, const float *b, int64_t n, 
         out[3 * i + 2] = (uint16_t)clampf(rintf(convert_range(b[i], 255.0f, mx)), 0.0f, mx);
     }
 }
+
+/* ======================================================================================= */
+/* Encoder front end: colour pre-processing (encoder/colour.rs) and analysis tiling         */
+/* (encoder/tiles.rs, encoder/mod.rs)                                                        */
+/* ======================================================================================= */
+
+/* replicate_pad (colour.rs:331-342) to an even size, then unshuffle_into (colour.rs:316-329):
+ * channel k = dy * 2 + dx of out takes sample (2y + dy, 2x + dx) of the padded plane */
+static void unshuffle_padded(const float *plane, int h, int w, float *out) {
+    int ph = h + h % 2, pw = w + w % 2, ch = ph / 2, cw = pw / 2;
+    for (int k = 0; k < 4; k++) {
+        int dy = k / 2, dx = k % 2;
+        float *dst = out + (size_t)k * ch * cw;
+        for (int y = 0; y < ch; y++) {
+            int sy = 2 * y + dy < h ? 2 * y + dy : h - 1;
+            for (int x = 0; x < cw; x++) {
+                int sx = 2 * x + dx < w ? 2 * x + dx : w - 1;
+                dst[(size_t)y * cw + x] = plane[(size_t)sy * w + sx];
+            }
+        }
+    }
+}
+
+void zo_preprocess_rgb(const uint8_t *rgb, int h, int w, float *luma, float *chroma) {
+    /* BT.709 weights and chroma denominators (colour.rs:26-30) */
+    const float KR = 0.2126f, KG = 0.7152f, KB = 0.0722f, KBY = 1.8556f, KRY = 1.5748f;
+    const float mx = 255.0f;
+    size_t n = (size_t)h * w;
+    float *u = (float *)malloc(sizeof(float) * n);
+    float *v = (float *)malloc(sizeof(float) * n);
+    for (size_t i = 0; i < n; i++) {
+        /* to_YUV_ on [0, 1] (colour.rs:418-428), then * 255 (source_planes, :396-400); every
+         * operation rounded on its own (Rust does not contract) */
+        float r = (float)rgb[3 * i] / mx, g = (float)rgb[3 * i + 1] / mx,
+              b = (float)rgb[3 * i + 2] / mx;
+        float y = KR * r + KG * g + KB * b;
+        luma[i] = y * 255.0f;
+        u[i] = ((b - y) / KBY + 0.5f) * 255.0f;
+        v[i] = ((r - y) / KRY + 0.5f) * 255.0f;
+    }
+    int ph = h + h % 2, pw = w + w % 2;
+    size_t cplane = (size_t)(ph / 2) * (pw / 2);
+    unshuffle_padded(luma, h, w, chroma);
+    unshuffle_padded(u, h, w, chroma + 4 * cplane);
+    unshuffle_padded(v, h, w, chroma + 8 * cplane);
+    free(u);
+    free(v);
+}
+
+/* cfg/CTC.json tile_manager_enc per component (encoder/tiles.rs:20-24) */
+static const int ENC_SAMPLES_PER_TILE[2] = {1048576, 262144};
+static const int ENC_TILE_OVERLAP[2] = {64, 32};
+static const int ENC_LATENT_DOWNSCALE[2] = {16, 8};
+
+/* `_get_latent_tile_from_image_tile` for one axis (encoder/tiles.rs:276-284) */
+static int latent_len(int pos, int len, int down, int full, int *out) {
+    if (len % down && cdiv(pos + len, down) < full) return -1;
+    *out = cdiv(len, down);
+    return 0;
+}
+
+int zo_analysis_tiles(int ccs, int h, int w, int lh, int lw, zo_atile *tiles, int max_tiles) {
+    if (ccs < 0 || ccs > 1 || h <= 0 || w <= 0) return -1;
+    const int nsamp = ENC_SAMPLES_PER_TILE[ccs], yd = ENC_LATENT_DOWNSCALE[ccs];
+    if ((int64_t)nsamp >= (int64_t)h * w) {  /* tile_size: no tiling (tiles.rs:53-60) */
+        if (max_tiles > 0 && tiles) {
+            zo_atile t = {0, 0, w, h, 0, 0, lw, lh, 0, 0, lw, lh, 0, 0};
+            tiles[0] = t;
+        }
+        return 1;
+    }
+    const int size = cdiv((int)floor(sqrt((double)nsamp)), yd) * yd;
+    const int overlap = ENC_TILE_OVERLAP[ccs];
+    const int tile_h = size < h ? size : h, tile_w = size < w ? size : w;
+    if (tile_h <= overlap || tile_w <= overlap) return -1;
+    const int o = overlap / 2 / yd;
+    int n = 0;
+    for (int y = 0; y < h - overlap; y += tile_h - overlap)
+        for (int x = 0; x < w - overlap; x += tile_w - overlap) {
+            zo_atile t;
+            t.img_x = x;
+            t.img_y = y;
+            t.img_w = tile_w < w - x ? tile_w : w - x;
+            t.img_h = tile_h < h - y ? tile_h : h - y;
+            t.lat_x = x / yd;
+            t.lat_y = y / yd;
+            if (latent_len(t.img_x, t.img_w, yd, lw, &t.lat_w) ||
+                latent_len(t.img_y, t.img_h, yd, lh, &t.lat_h))
+                return -1;
+            /* `_get_core_of_overlapping_tile`, picture-border branch (tiles.rs:127-139) */
+            int left = x == 0 ? 0 : o, top = y == 0 ? 0 : o;
+            int right = x + t.img_w >= w ? 0 : o, bottom = y + t.img_h >= h ? 0 : o;
+            if (t.lat_w < left + right || t.lat_h < top + bottom) return -1;
+            t.core_x = t.lat_x + left;
+            t.core_y = t.lat_y + top;
+            t.core_w = t.lat_w - left - right;
+            t.core_h = t.lat_h - top - bottom;
+            t.off_x = left;
+            t.off_y = top;
+            if (tiles && n < max_tiles) tiles[n] = t;
+            n++;
+        }
+    return n;
+}
+
+int zo_analyze_tiled(const zo_ckpt *ck, int op, int ccs, const float *x, int h, int w,
+                     float *out) {
+    const int cin = ccs ? 12 : 1, cout = ccs ? 96 : 160, d = ENC_LATENT_DOWNSCALE[ccs];
+    const int lh = cdiv(h, d), lw = cdiv(w, d);
+    int nt = zo_analysis_tiles(ccs, h, w, lh, lw, NULL, 0);
+    if (nt <= 0) return -1;
+    zo_atile *tiles = (zo_atile *)malloc(sizeof(zo_atile) * nt);
+    zo_analysis_tiles(ccs, h, w, lh, lw, tiles, nt);
+    int rc = 0;
+    for (int i = 0; i < nt && !rc; i++) {
+        zo_atile t = tiles[i];
+        float *win = (float *)malloc(sizeof(float) * cin * t.img_h * t.img_w);
+        for (int c = 0; c < cin; c++)
+            for (int y = 0; y < t.img_h; y++)
+                memcpy(win + ((size_t)c * t.img_h + y) * t.img_w,
+                       x + ((size_t)c * h + t.img_y + y) * w + t.img_x, sizeof(float) * t.img_w);
+        float *lat = (float *)malloc(sizeof(float) * cout * t.lat_h * t.lat_w);
+        rc = ccs ? zo_analysis_secondary(ck, op, win, t.img_h, t.img_w, lat)
+                 : zo_analysis_primary(ck, op, win, t.img_h, t.img_w, lat);
+        for (int c = 0; c < cout && !rc; c++)
+            for (int y = 0; y < t.core_h; y++)
+                memcpy(out + ((size_t)c * lh + t.core_y + y) * lw + t.core_x,
+                       lat + ((size_t)c * t.lat_h + t.off_y + y) * t.lat_w + t.off_x,
+                       sizeof(float) * t.core_w);
+        free(win);
+        free(lat);
+    }
+    free(tiles);
+    return rc;
+}

@@ -162,6 +162,33 @@ void zo_quantize_rgb(const float *r, const float *g, const float *b, int64_t n, 
 void zo_normalize(const float *x, int64_t n, float *out);
 int zo_pad_amount(int len, int divider);
 
+/* `preprocess_rgb` (colour.rs:535-541 -> source_planes colour.rs:390-436 and preprocess
+ * colour.rs:462-495, 4:4:4 coded) of an 8-bit interleaved RGB picture [h][w][3]: luma [h][w]
+ * in [0, 255], chroma [12][ph / 2][pw / 2] (ph, pw = h, w rounded up to even): the four
+ * pixel-unshuffle phases of the replicate-padded luma, then of U, then of V. */
+void zo_preprocess_rgb(const uint8_t *rgb, int h, int w, float *luma, float *chroma);
+
+/* One analysis tile (encoder/tiles.rs:33-49 `AnalysisTile`, without the hyper-latent grid):
+ * the plane area the analysis runs on, the latent area it produces, the kept core of that
+ * latent (whole-latent coordinates) and the core's offset inside the tile's own latent. */
+typedef struct {
+    int img_x, img_y, img_w, img_h;
+    int lat_x, lat_y, lat_w, lat_h;
+    int core_x, core_y, core_w, core_h;
+    int off_x, off_y;
+} zo_atile;
+
+/* `analysis_tiles` (encoder/tiles.rs:51-156, no independent regions) of component ccs (0 luma,
+ * 1 chroma) for a plane of h x w samples with latent lh x lw. Returns the tile count (-1:
+ * malformed geometry); writes at most max_tiles. */
+int zo_analysis_tiles(int ccs, int h, int w, int lh, int lw, zo_atile *tiles, int max_tiles);
+
+/* The encoder's tiled analysis transform of component ccs: plane x [1 or 12][h][w] -> latent
+ * [160 or 96][ceil(h / d)][ceil(w / d)] (d = 16 or 8), each tile analysed on its own and its
+ * latent core kept (encoder/mod.rs:1128-1170). */
+int zo_analyze_tiled(const zo_ckpt *ck, int op, int ccs, const float *x, int h, int w,
+                     float *out);
+
 #ifdef __cplusplus
 }
 #endif
