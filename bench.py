@@ -48,6 +48,10 @@ CONFIGS = {
     "sop1080": dict(kind="synth", op="sop", H=1080, W=1920, tile=0, overlap=0, seed=2,
                     lat_seed=100, metric=SYNTH_METRIC, scaling="strong",
                     desc="BASELINE config 3: SOP synthesis, 1920x1080 4:2:0, one tile"),
+    "bop_batch64": dict(kind="batch", op="bop", H=1024, W=1024, npic=64, per_call=8, seed=4,
+                        metric="batched decode + analysis Mpixel/s", scaling="strong",
+                        desc="BASELINE config 5: 64 BOP 1024x1024 4:4:4 pictures, RGB analysis "
+                             "+ synthesis, pictures round-robin over the GPUs, 8 per call"),
     "conv1": dict(kind="stage", shuffle=1, act="leaky", nres=0, metric=STAGE_METRIC,
                   scaling="weak",
                   desc="BASELINE config 1: conv 3x3 128->128 on 128x128, LeakyReLU(0.01)",
@@ -285,6 +289,43 @@ class CpuStage:
         return y.shape[1] * y.shape[2], time.perf_counter() - t0
 
 
+def batch_picture(cfg, i):
+    """Picture i of config 5: its latents (Laplace(2.0), seed 100 + i) and its RGB picture
+    (uniform 8-bit samples, seed 1100 + i)."""
+    import synthetic as syn
+    lh, lw = cfg["H"] // 16, cfg["W"] // 16
+    ly = syn.laplace_latent(100 + i, "ly", (160, lh, lw), 2.0)
+    luv = syn.laplace_latent(100 + i, "luv", (96, lh, lw), 2.0)
+    rgb = np.floor(syn.uniform(1100 + i, "rgb", (cfg["H"], cfg["W"], 3), 0.0, 256.0))
+    return ly, luv, rgb.astype(np.uint8)
+
+
+class CpuBatch:
+    """The CPU baseline of config 5: per picture, preprocess_rgb + both analysis transforms and
+    the 4:4:4 synthesis of its latents, on the nn::fast restatement."""
+
+    def __init__(self, cfg):
+        import oracle as zo
+        import synthetic as syn
+        self.zo, self.cfg = zo, cfg
+        py, puv = syn.synthesis_params(cfg["op"], cfg["seed"])
+        pa, pauv = syn.analysis_params(cfg["op"], cfg["seed"])
+        self.ck = [zo.Checkpoint(p) for p in (py, puv, pa, pauv)]
+
+    def run(self, i, threads):
+        zo, cfg = self.zo, self.cfg
+        zo.set_fast(True)
+        zo.set_threads(threads)
+        op = zo.OPS[cfg["op"]]
+        ly, luv, rgb = batch_picture(cfg, i)
+        t0 = time.perf_counter()
+        luma, chroma = zo.preprocess_rgb(rgb)
+        zo.analyze_tiled(self.ck[2], op, 0, luma)
+        zo.analyze_tiled(self.ck[3], op, 1, chroma)
+        zo.synthesize(self.ck[0], self.ck[1], op, ly, luv, cfg["H"], cfg["W"], sv=1, sh=1)
+        return cfg["H"] * cfg["W"], time.perf_counter() - t0
+
+
 def stage_inputs(cfg):
     import synthetic as syn
     if cfg["name"] == "conv1":
@@ -296,6 +337,15 @@ def cpu_baseline(cfg):
     """Rank 0, N = 1: the nn::fast restatement on all host threads and on one thread, on a
     bounded sample of the workload (a few seconds each)."""
     threads = os.cpu_count() or 1
+    if cfg["kind"] == "batch":
+        c = CpuBatch(cfg)
+        px, dt = c.run(0, threads)
+        px1, dt1 = c.run(1, 1)
+        return {"value": px / dt / 1e6, "unit": "Mpixel/s", "cores": threads, "kind": "port",
+                "value_1core": px1 / dt1 / 1e6,
+                "sample": "picture 0 (RGB analysis + synthesis) on %d threads, picture 1 on one "
+                          "thread; oracle/fast.c, the crate's nn::fast convolution algorithm "
+                          "restated (bit-identical to nn::reference)" % threads}
     if cfg["kind"] == "stage":
         c = CpuStage(cfg)
         c.run(threads)
@@ -320,6 +370,13 @@ def cpu_baseline(cfg):
 
 def config_dict(args, cfg, world):
     """The workload description both arms print (the same dict)."""
+    if cfg["kind"] == "batch":
+        return {"workload": args.config + ": " + cfg["desc"],
+                "pictures": cfg["npic"],
+                "parallelism": "pictures round-robin over %d GPU(s), no collective" % world,
+                "weights": "random-init, seed %d (role-scaled normal)" % cfg["seed"],
+                "l2": "flushed between steps (256 MiB write, outside the timed events)",
+                "precision": "f16 operands, f32 accumulation (TMEM); the CPU arm computes f32"}
     if cfg["kind"] == "stage":
         return {"workload": args.config + ": " + cfg["desc"],
                 "parallelism": "replicas: the same stage on each of %d GPU(s)" % world,
@@ -346,7 +403,11 @@ def run_reference(args, cfg):
         return
     threads = os.cpu_count() or 1
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if cfg["kind"] == "stage":
+    if cfg["kind"] == "batch":
+        c = CpuBatch(cfg)
+        run = lambda s: c.run(s % cfg["npic"], threads)
+        sample = "one picture per step (RGB analysis + synthesis), pictures in turn"
+    elif cfg["kind"] == "stage":
         c = CpuStage(cfg)
         run = lambda s: c.run(threads)
         sample = "the whole stage per step"
@@ -456,7 +517,8 @@ def main():
     from zenjpegai_b200 import sharding
     from zenjpegai_b200.decoder import Decoder
 
-    eng = zj.Engine(local, arena_bytes=(64 << 30) if cfg["kind"] == "synth" else (4 << 30))
+    eng = zj.Engine(local, arena_bytes={"synth": 64 << 30, "batch": 32 << 30}.get(cfg["kind"],
+                                                                                4 << 30))
     # one non-default stream shared by torch (copies, events, NCCL) and the engine
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -522,6 +584,44 @@ def main():
                 sharding.gather_cores(out8, dist)
             if from_host and rank == 0:
                 out8_host.copy_(out8, non_blocking=True)
+    elif cfg["kind"] == "batch":
+        from zenjpegai_b200.decoder import Encoder
+        op = cfg["op"]
+        py, puv = syn.synthesis_params(op, cfg["seed"])
+        pa, pauv = syn.analysis_params(op, cfg["seed"])
+        dec = Decoder(eng, op, py, puv)
+        enc = Encoder(eng, op, pa, pauv)
+        closers += [dec.close, enc.close]
+        mine = [i for i in range(cfg["npic"]) if i % world == rank]
+        pics = [batch_picture(cfg, i) for i in mine]
+        ly_h = torch.from_numpy(np.stack([p[0] for p in pics])).pin_memory()
+        luv_h = torch.from_numpy(np.stack([p[1] for p in pics])).pin_memory()
+        rgb_h = torch.from_numpy(np.stack([p[2] for p in pics])).pin_memory()
+        ly, luv, rgb = ly_h.cuda(), luv_h.cuda(), rgb_h.cuda()
+        n, Hb, Wb = len(mine), cfg["H"], cfg["W"]
+        planes = (torch.empty((n, Hb, Wb), dtype=torch.uint8, device="cuda"),
+                  torch.empty((n, Hb, Wb), dtype=torch.uint8, device="cuda"),
+                  torch.empty((n, Hb, Wb), dtype=torch.uint8, device="cuda"))
+        lat_out = (torch.empty((n, 160, Hb // 16, Wb // 16), device="cuda"),
+                   torch.empty((n, 96, Hb // 16, Wb // 16), device="cuda"))
+        planes_h = tuple(torch.empty(p.shape, dtype=p.dtype).pin_memory() for p in planes)
+        lat_h = tuple(torch.empty(l.shape).pin_memory() for l in lat_out)
+        calls = [(a, min(a + cfg["per_call"], n)) for a in range(0, n, cfg["per_call"])]
+        out_px = cfg["npic"] * Hb * Wb
+        h2d = sum(t.numel() * t.element_size() for t in (ly_h, luv_h, rgb_h)) * world
+        d2h = sum(t.numel() * t.element_size() for t in planes_h + lat_h) * world
+
+        def step(from_host=False):
+            if from_host:
+                for d, hbuf in ((ly, ly_h), (luv, luv_h), (rgb, rgb_h)):
+                    d.copy_(hbuf, non_blocking=True)
+            for a, b in calls:
+                enc.analyze_rgb(rgb[a:b], out=(lat_out[0][a:b], lat_out[1][a:b]))
+                dec.synthesize_batch(ly[a:b], luv[a:b], Hb, Wb, sv=1, sh=1, bit_depth=8,
+                                     out=(planes[0][a:b], planes[1][a:b], planes[2][a:b]))
+            if from_host:
+                for d, hbuf in zip(planes + lat_out, planes_h + lat_h):
+                    hbuf.copy_(d, non_blocking=True)
     else:
         prm, x_np = stage_inputs(cfg)
         st = zj.Stage(eng, prm, shuffle=cfg["shuffle"],

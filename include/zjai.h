@@ -171,6 +171,23 @@ int zjai_stage_create(zjai_ctx *ctx, int shuffle, int act, int res_act, const zj
 /* Runs a stage: x [cin][h][w] -> out [cout][h * shuffle][w * shuffle], planar f32. */
 int zjai_stage_forward(zjai_net *net, const float *x, int c, int h, int w, float *out, int mem);
 
+/* `colour::preprocess_rgb` (src/encoder/colour.rs:535-541, with source_planes :390-436 and
+ * preprocess :462-495 for 4:4:4 coding): an 8-bit interleaved RGB picture [h][w][3] ->
+ * luma [h][w] and chroma [12][ceil(h/2)][ceil(w/2)] (planar f32 in [0, 255]: BT.709 Y, U, V,
+ * the chroma tensor the four pixel-unshuffle phases of the edge-replicated Y, then U, then V),
+ * bit-exact with the crate's f32 arithmetic. */
+int zjai_preprocess_rgb(zjai_ctx *ctx, const uint8_t *rgb, int h, int w, float *luma,
+                        float *chroma, int mem);
+
+/* The encoder's analysis of n same-size 8-bit RGB pictures [n][h][w][3] in one call:
+ * preprocess_rgb, then `AnalysisPrimary::forward` / `AnalysisSecondary::forward`
+ * (analysis.rs:242-311) on all n pictures as one batch, tiled like the crate's encoder above
+ * 1,048,576 luma / 262,144 chroma samples per plane (encoder/tiles.rs:51-156, each tile's
+ * latent core kept; encoder/mod.rs:1128-1170). lat_y [n][160][ceil(h/16)][ceil(w/16)],
+ * lat_uv [n][96][ceil(ceil(h/2)/8)][ceil(ceil(w/2)/8)]. */
+int zjai_analyze_rgb(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, int n,
+                     const uint8_t *rgb, int h, int w, float *lat_y, float *lat_uv, int mem);
+
 /* One synthesis tile (src/tools/tiles.rs:26-32 `SynthesisTile`). */
 typedef struct {
   int img_x, img_y, img_w, img_h;
@@ -233,6 +250,17 @@ int zjai_synthesize_q(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, const fl
 int zjai_ipc_export(zjai_ctx *ctx, const void *ptr, void *handle, uint64_t *offset);
 int zjai_ipc_import(zjai_ctx *ctx, const void *handle, uint64_t offset, void **ptr);
 int zjai_ipc_close(zjai_ctx *ctx, void *ptr);
+
+/* A batch of n independent pictures of one size synthesised in one call (the crate decodes
+ * them one `synthesize_with` call at a time, reconstruct.rs:274-331; here every tile of every
+ * picture runs in the same shape batches): latents y_hat_y [n][160][lh][lw], y_hat_uv
+ * [n][96][lh][lw]; planes rec_y [n][out_h][out_w], rec_u / rec_v [n][ceil(out_h/sv)]
+ * [ceil(out_w/sh)], f32 for bit_depth 0, else the quantized samples of zjai_synthesize_q. */
+int zjai_synthesize_batch(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, int n,
+                          const float *y_hat_y, const float *y_hat_uv, int lh, int lw, int height,
+                          int width, int out_h, int out_w, int tile_size, int overlap, int sv,
+                          int sh, int bit_depth, void *rec_y, void *rec_u, void *rec_v, int mem,
+                          const volatile int *cancel);
 
 /* ---------------------------------------------------------------------------------------- */
 /* Output stage (src/decoder/output.rs)                                                       */

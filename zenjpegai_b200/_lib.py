@@ -85,6 +85,10 @@ def lib():
     L.zjai_synthesis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _vp, _i]
     L.zjai_analysis_primary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
     L.zjai_analysis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
+    L.zjai_synthesize_batch.argtypes = [_vp, _vp, _vp, _i, _vp, _vp] + [_i] * 11 + [_vp, _vp,
+                                                                                  _vp, _i, _vp]
+    L.zjai_preprocess_rgb.argtypes = [_vp, _vp, _i, _i, _vp, _vp, _i]
+    L.zjai_analyze_rgb.argtypes = [_vp, _vp, _vp, _i, _vp, _i, _i, _vp, _vp, _i]
     L.zjai_ipc_export.argtypes = [_vp, _vp, _vp, ctypes.POINTER(ctypes.c_uint64)]
     L.zjai_ipc_import.argtypes = [_vp, _vp, ctypes.c_uint64, ctypes.POINTER(_vp)]
     L.zjai_ipc_close.argtypes = [_vp, _vp]

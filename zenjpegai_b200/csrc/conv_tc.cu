@@ -261,8 +261,10 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
                                            const uint32_t* tab, const float* btab) {
   if (!valid) return;
   int py0 = a.py0, px0 = a.px0, cy0 = a.cy0, cy1 = a.cy1, cx0 = a.cx0, cx1 = a.cx1;
+  long long base = a.img_win ? 0 : img * a.p_img;
   if (a.img_win) {
-    const int* wv = a.img_win + 6 * img;
+    const int* wv = a.img_win + 7 * img;
+    base = wv[6];
     py0 = wv[0];
     px0 = wv[1];
     cy0 = wv[2];
@@ -293,7 +295,7 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
     }
     float x = act_rt(v[j] * a.scale + btab[col0 + j], a.act1);
     if (a.denorm) x = fminf(fmaxf(x * 128.f + 127.5f, 0.f), 255.f);
-    const long long ei = (a.img_win ? 0 : img * a.p_img) + (long long)SY * a.p_row + SX;
+    const long long ei = base + (long long)SY * a.p_row + SX;
     const bool second = ch == 1 && a.pout2;  // plane 1 has its own pointer
     if (a.qbytes) {
       // fused output stage: the sample quantize_plane_par would make of x

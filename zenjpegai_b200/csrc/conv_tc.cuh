@@ -100,7 +100,9 @@ struct ConvArgs {
   long long p_plane, p_row, p_img;
   int py0, px0;        // picture coordinates of output pixel (0, 0)
   int cy0, cy1, cx0, cx1;
-  const int* img_win;  // per-image {py0, px0, cy0, cy1, cx0, cx1} (device), or null
+  // per-image {py0, px0, cy0, cy1, cx0, cx1, base} (device), or null: picture coordinates of the
+  // image's output pixel (0, 0), the kept window, and the sample offset of its picture's planes
+  const int* img_win;
   int sv, sh;
   int lsv, lsh;        // log2 of sv / sh when both are powers of two, else -1
   // fused output stage: qbytes 1 (uint8) or 2 (uint16) writes quantized samples

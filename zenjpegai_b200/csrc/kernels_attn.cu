@@ -1041,8 +1041,8 @@ __global__ void __launch_bounds__(kFoldThreads) attn_fold_fused_kernel(
   }
 }
 
-// planar f32 latent [C][LH][LW] -> NHWC f16 [n][h][w] at channel offset; per-image window
-// origins (x, y) in `origin` (device int pairs).
+// planar f32 latents [pictures][C][LH][LW] -> NHWC f16 [n][h][w] at channel offset; per-image
+// window origin (x, y) and picture index in `origin` (device int triplets).
 __global__ void gather_latent_kernel(const float* __restrict__ src, int C, int LH, int LW,
                                      const int* __restrict__ origin, __half* __restrict__ dst,
                                      int n_img, int h, int w, long long pix, long long row,
@@ -1053,8 +1053,9 @@ __global__ void gather_latent_kernel(const float* __restrict__ src, int C, int L
   const int x = (int)(idx % w);
   long long r = idx / w;
   const int y = (int)(r % h), n = (int)(r / h);
-  const int sx = origin[2 * n] + x, sy = origin[2 * n + 1] + y;
+  const int sx = origin[3 * n] + x, sy = origin[3 * n + 1] + y;
   const long long plane = (long long)LH * LW;
+  src += (long long)origin[3 * n + 2] * C * plane;  // the tile's picture
   const float* s = src + (long long)sy * LW + sx;
   __half* d = dst + n * img + (long long)y * row + (long long)x * pix;
   for (int ch = 0; ch + 1 < C; ch += 2)
@@ -1078,8 +1079,9 @@ __global__ void gather_latent8_kernel(const float* __restrict__ src, int C, int 
   const int g = (int)(r % groups);
   r /= groups;
   const int y = (int)(r % h), n = (int)(r / h);
-  const int sx = origin[2 * n] + x, sy = origin[2 * n + 1] + y;
+  const int sx = origin[3 * n] + x, sy = origin[3 * n + 1] + y;
   const long long plane = (long long)LH * LW;
+  src += (long long)origin[3 * n + 2] * C * plane;  // the tile's picture
   const float* sp = src + (long long)(8 * g) * plane + (long long)sy * LW + sx;
   uint4 u;
   __half2* hv = reinterpret_cast<__half2*>(&u);

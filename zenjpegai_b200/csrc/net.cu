@@ -2,6 +2,7 @@
 // synthesis / analysis topologies of src/model/{synthesis,attention,analysis}.rs on batches of
 // same-shape tiles (NHWC f16 activations in the context arena).
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -931,6 +932,45 @@ int synthesis_tiles(int height, int width, int latent_h, int latent_w, int tile_
       t.off_x = left;
       t.off_y = top;
       out->push_back(t);
+    }
+  return ZJAI_OK;
+}
+
+// Analysis tiling (encoder/tiles.rs:51-156): above ENC_SAMPLES_PER_TILE samples per plane the
+// encoder analyses overlapping tiles of floor(sqrt(n)) samples rounded up to the latent grid and
+// keeps each tile's latent core (half the overlap trimmed from interior sides).
+int analysis_tiles(int ccs, int h, int w, int lh, int lw, std::vector<std::array<int, 14>>* out) {
+  static const int kSamples[2] = {1048576, 262144}, kOverlap[2] = {64, 32}, kDown[2] = {16, 8};
+  out->clear();
+  if (ccs < 0 || ccs > 1 || h <= 0 || w <= 0) return fail(ZJAI_INVALID_ARGUMENT, "analysis tiles");
+  if ((long long)kSamples[ccs] >= (long long)h * w) {
+    out->push_back({0, 0, w, h, 0, 0, lw, lh, 0, 0, lw, lh, 0, 0});
+    return ZJAI_OK;
+  }
+  const int d = kDown[ccs], overlap = kOverlap[ccs];
+  const int size = cdiv((int)std::floor(std::sqrt((double)kSamples[ccs])), d) * d;
+  const int tile_h = std::min(size, h), tile_w = std::min(size, w);
+  if (tile_h <= overlap || tile_w <= overlap)
+    return fail(ZJAI_INVALID_DATA, "analysis tile not larger than overlap");
+  const int o = overlap / 2 / d;
+  auto latent_len = [&](int pos, int len, int full, int* r) {
+    if (len % d && cdiv(pos + len, d) < full)
+      return fail(ZJAI_INVALID_DATA, "unaligned analysis tile inside the plane");
+    *r = cdiv(len, d);
+    return (int)ZJAI_OK;
+  };
+  for (int y = 0; y < h - overlap; y += tile_h - overlap)
+    for (int x = 0; x < w - overlap; x += tile_w - overlap) {
+      const int iw = std::min(tile_w, w - x), ih = std::min(tile_h, h - y);
+      int lw_t, lh_t;
+      ZJAI_TRY(latent_len(x, iw, lw, &lw_t));
+      ZJAI_TRY(latent_len(y, ih, lh, &lh_t));
+      const int left = x == 0 ? 0 : o, top = y == 0 ? 0 : o;
+      const int right = x + iw >= w ? 0 : o, bottom = y + ih >= h ? 0 : o;
+      if (lw_t < left + right || lh_t < top + bottom)
+        return fail(ZJAI_INVALID_DATA, "analysis tile is all overlap");
+      out->push_back({x, y, iw, ih, x / d, y / d, lw_t, lh_t, x / d + left, y / d + top,
+                      lw_t - left - right, lh_t - top - bottom, left, top});
     }
   return ZJAI_OK;
 }

@@ -1,5 +1,6 @@
 // Network objects and the per-call runner that executes a topology on a batch of tiles.
 #pragma once
+#include <array>
 #include <map>
 #include <string>
 #include <vector>
@@ -34,7 +35,8 @@ struct FinalOut {
   float* plane0 = nullptr;
   float* plane1 = nullptr;       // second plane (chroma V); null: plane0 + plane_stride
   long long plane_stride = 0, row = 0, img = 0;
-  const int* win = nullptr;      // per-tile {py0, px0, cy0, cy1, cx0, cx1} (device) or null
+  // per-tile {py0, px0, cy0, cy1, cx0, cx1, plane base} (device) or null
+  const int* win = nullptr;
   int sv = 1, sh = 1;
   int full_h = -1, full_w = -1;  // clip of the network output extent (-1: natural)
   // fused output stage: planes of quantized samples (1 = uint8, 2 = uint16, to qmax)
@@ -107,5 +109,19 @@ void synth_out_size(int kind, int op, int h, int w, int* oh, int* ow);
 
 void launch_replicate_pad(const TView& src, const TView& dst, cudaStream_t s);
 void launch_normalize_pad(const float* src, int c, int h, int w, const TView& dst, cudaStream_t s);
+// normalize_pad of the h x w window at (y0, x0) of planar pictures [n][c][SH][SW]
+void launch_normalize_pad_window(const float* src, int c, int SH, int SW, int y0, int x0, int h,
+                                 int w, const TView& dst, cudaStream_t s);
+// colour.rs preprocess_rgb of n pictures [n][h][w][3] -> luma [n][h][w], chroma
+// [n][12][ph / 2][pw / 2] (planar f32, [0, 255])
+void launch_preprocess_rgb(const uint8_t* rgb, int n, int h, int w, float* luma, float* chroma,
+                           cudaStream_t s);
+void launch_copy_core(const float* tile, int n, int C, int th, int tw, int oy, int ox, int core_h,
+                      int core_w, float* full, int LH, int LW, int cy, int cx, cudaStream_t s);
+
+// `analysis_tiles` (encoder/tiles.rs:51-156, no independent regions) of component ccs for a
+// plane of h x w samples with latent lh x lw: {img x, y, w, h, latent x, y, w, h, core x, y, w,
+// h, core offset x, y} per tile.
+int analysis_tiles(int ccs, int h, int w, int lh, int lw, std::vector<std::array<int, 14>>* out);
 
 }  // namespace zjai

@@ -56,6 +56,14 @@ int settle(Ctx* ctx, int st) {
 
 namespace zjai {
 
+// The pictures of a batched synthesis: per tile its picture (latents [picture][C][lh][lw]),
+// and the samples of one picture's luma / chroma output plane (the planes are
+// [picture][h][w]). Empty: every tile belongs to the one picture.
+struct TilePictures {
+  std::vector<int> pic;
+  long long plane_y = 0, plane_uv = 0;
+};
+
 // One shape group of a tiled synthesis: the latent windows of its tiles gathered into one
 // batch, the luma network on stream `sy` with arena `ay`, the chroma network on `sc` with `ac`
 // (after the gather). Output planes are device pointers.
@@ -65,26 +73,32 @@ struct GroupJob {
 };
 
 static int run_group(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const float* lat_uv, int lh,
-                     int lw, const std::vector<zjai_tile>& tiles, const GroupJob& g, int out_h,
-                     int out_w, int sv, int sh, float* rec_y, float* rec_u, float* rec_v,
-                     const volatile int* cancel, double* flops, int qbytes, float qmax,
-                     cudaStream_t sy, cudaStream_t sc, Arena* ay, Arena* ac, cudaEvent_t ev) {
+                     int lw, const std::vector<zjai_tile>& tiles, const TilePictures& pics,
+                     const GroupJob& g, int out_h, int out_w, int sv, int sh, float* rec_y,
+                     float* rec_u, float* rec_v, const volatile int* cancel, double* flops,
+                     int qbytes, float qmax, cudaStream_t sy, cudaStream_t sc, Arena* ay,
+                     Arena* ac, cudaEvent_t ev) {
   const int n = (int)g.idx.size();
   const int cw_ = cdiv(out_w, sh);
-  std::vector<int> origin, win;
+  std::vector<int> origin, win_y, win_uv;
   for (int i : g.idx) {
     const zjai_tile& t = tiles[i];
-    origin.push_back(t.lat_x);
-    origin.push_back(t.lat_y);
-    win.insert(win.end(), {t.img_y, t.img_x, t.core_y, std::min(t.core_y + t.core_h, out_h),
-                           t.core_x, std::min(t.core_x + t.core_w, out_w)});
+    const int p = pics.pic.empty() ? 0 : pics.pic[i];
+    origin.insert(origin.end(), {t.lat_x, t.lat_y, p});
+    const std::initializer_list<int> w = {t.img_y, t.img_x, t.core_y,
+                                          std::min(t.core_y + t.core_h, out_h), t.core_x,
+                                          std::min(t.core_x + t.core_w, out_w)};
+    win_y.insert(win_y.end(), w);
+    win_y.push_back((int)(p * pics.plane_y));
+    win_uv.insert(win_uv.end(), w);
+    win_uv.push_back((int)(p * pics.plane_uv));
   }
   // each stream reads descriptor copies from its own arena
   int *d_origin, *d_origin2, *d_win_y, *d_win_uv;
   ZJAI_TRY(upload_ints(ctx, ay, origin, sy, &d_origin));
-  ZJAI_TRY(upload_ints(ctx, ay, win, sy, &d_win_y));
+  ZJAI_TRY(upload_ints(ctx, ay, win_y, sy, &d_win_y));
   ZJAI_TRY(upload_ints(ctx, ac, origin, sc, &d_origin2));
-  ZJAI_TRY(upload_ints(ctx, ac, win, sc, &d_win_uv));
+  ZJAI_TRY(upload_ints(ctx, ac, win_uv, sc, &d_win_uv));
   // latent windows: [n][lat_h][lat_w][256] = luma 160 | chroma 96 (luma stream)
   TView cat;
   ZJAI_TRY(alloc_tensor(ctx, n, g.lat_h, g.lat_w, 256, &cat, false, ay, sy));
@@ -154,7 +168,8 @@ static int group_pool(Ctx* ctx, size_t streams, size_t events) {
 int synthesize_tiles_dev(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const float* lat_uv,
                          int lh, int lw, const std::vector<zjai_tile>& tiles, int out_h, int out_w,
                          int sv, int sh, float* rec_y, float* rec_u, float* rec_v,
-                         const volatile int* cancel, double* flops, int bit_depth) {
+                         const volatile int* cancel, double* flops, int bit_depth,
+                         const TilePictures& pics) {
   // bit_depth > 0: the final layers write quantized samples (uint8 for 8 bits, else uint16)
   // into rec_* instead of f32 planes
   const int qbytes = bit_depth <= 0 ? 0 : bit_depth == 8 ? 1 : 2;
@@ -205,7 +220,7 @@ int synthesize_tiles_dev(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const 
       const size_t m1 = ctx->arena.top, m2 = ctx->arena2.top;
       ctx->arena.peak = m1;
       ctx->arena2.peak = m2;
-      ZJAI_TRY(run_group(ctx, ny, nuv, lat_y, lat_uv, lh, lw, tiles, g, out_h, out_w, sv, sh,
+      ZJAI_TRY(run_group(ctx, ny, nuv, lat_y, lat_uv, lh, lw, tiles, pics, g, out_h, out_w, sv, sh,
                          rec_y, rec_u, rec_v, cancel, flops, qbytes, qmax, s1, s2, &ctx->arena,
                          &ctx->arena2, ctx->ev_fork));
       ctx->group_need[key(g)] = {ctx->arena.peak - m1, ctx->arena2.peak - m2};
@@ -237,7 +252,7 @@ int synthesize_tiles_dev(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const 
     cudaStream_t sy = ctx->group_streams[2 * i], sc = ctx->group_streams[2 * i + 1];
     ZJAI_TRY(cuda_check(cudaStreamWaitEvent(sy, fork, 0), "event wait"));
     ZJAI_TRY(cuda_check(cudaStreamWaitEvent(sc, fork, 0), "event wait"));
-    ZJAI_TRY(run_group(ctx, ny, nuv, lat_y, lat_uv, lh, lw, tiles, groups[i], out_h, out_w, sv,
+    ZJAI_TRY(run_group(ctx, ny, nuv, lat_y, lat_uv, lh, lw, tiles, pics, groups[i], out_h, out_w, sv,
                        sh, rec_y, rec_u, rec_v, cancel, flops, qbytes, qmax, sy, sc, &ay[i],
                        &ac[i], ctx->group_events[1 + 3 * i]));
   }
@@ -298,7 +313,7 @@ int zjai_synthesis_primary(zjai_net* net, const float* y_hat, int lh, int lw, in
   const float* dy;
   ZJAI_TRY(stage_in(ctx, y_hat, (size_t)160 * lh * lw, mem, &dy));
   int* d_origin;
-  ZJAI_TRY(upload_ints(ctx, &ctx->arena, {0, 0}, ctx->stream, &d_origin));
+  ZJAI_TRY(upload_ints(ctx, &ctx->arena, {0, 0, 0}, ctx->stream, &d_origin));
   TView y;
   ZJAI_TRY(alloc_tensor(ctx, 1, lh, lw, 160, &y));
   launch_gather_latent(dy, 160, lh, lw, d_origin, y, ctx->stream);
@@ -333,7 +348,7 @@ int zjai_synthesis_secondary(zjai_net* net, const float* y_hat_luma, int llh, in
   ZJAI_TRY(stage_in(ctx, y_hat_luma, (size_t)160 * llh * llw, mem, &dl));
   ZJAI_TRY(stage_in(ctx, y_hat_chroma, (size_t)96 * lh * lw, mem, &dc));
   int* d_origin;
-  ZJAI_TRY(upload_ints(ctx, &ctx->arena, {0, 0}, ctx->stream, &d_origin));
+  ZJAI_TRY(upload_ints(ctx, &ctx->arena, {0, 0, 0}, ctx->stream, &d_origin));
   TView cat, x144;
   ZJAI_TRY(alloc_tensor(ctx, 1, lh, lw, 256, &cat));
   ZJAI_TRY(alloc_tensor(ctx, 1, lh, lw, 144, &x144));
@@ -385,6 +400,105 @@ int zjai_analysis_secondary(zjai_net* net, const float* x, int h, int w, float* 
   return analysis_entry(net, ZJAI_ANA_UV, 12, 96, 8, x, h, w, out, mem);
 }
 
+int zjai_preprocess_rgb(zjai_ctx* ctx, const uint8_t* rgb, int h, int w, float* luma,
+                        float* chroma, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!rgb || !luma || !chroma || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "preprocess_rgb: bad arguments");
+  if (mem != ZJAI_MEM_HOST && mem != ZJAI_MEM_DEVICE)
+    return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  ArenaScope scope(ctx);
+  const size_t nrgb = (size_t)h * w * 3, nl = (size_t)h * w;
+  const size_t nc = (size_t)12 * ((h + 1) / 2) * ((w + 1) / 2);
+  const uint8_t* drgb = rgb;
+  if (mem == ZJAI_MEM_HOST) {
+    uint8_t* d = static_cast<uint8_t*>(ctx->arena.alloc(nrgb));
+    if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (RGB staging)");
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(d, rgb, nrgb, cudaMemcpyHostToDevice, ctx->stream), "H2D"));
+    drgb = d;
+  }
+  float *dl, *dc;
+  ZJAI_TRY(stage_out_alloc(ctx, luma, nl, mem, &dl));
+  ZJAI_TRY(stage_out_alloc(ctx, chroma, nc, mem, &dc));
+  launch_preprocess_rgb(drgb, 1, h, w, dl, dc, ctx->stream);
+  ctx->launches++;
+  ZJAI_TRY(stage_out_finish(ctx, luma, dl, nl, mem));
+  ZJAI_TRY(stage_out_finish(ctx, chroma, dc, nc, mem));
+  return finish_call(ctx, mem);
+}
+
+// Analysis of one component of n same-size pictures: plane [n][c][H][W] (planar f32 in
+// [0, 255]) -> latent [n][cout][LH][LW], tile by tile above the tiling threshold, each tile of
+// all n pictures one batch.
+static int analyze_component(Ctx* ctx, Net* net, int ccs, int n, const float* plane, int c, int H,
+                             int W, float* out) {
+  const int d = ccs ? 8 : 16, cout = ccs ? 96 : 160;
+  const int LH = cdiv(H, d), LW = cdiv(W, d);
+  std::vector<std::array<int, 14>> tiles;
+  ZJAI_TRY(analysis_tiles(ccs, H, W, LH, LW, &tiles));
+  const bool whole = tiles.size() == 1;
+  for (const auto& t : tiles) {
+    ArenaMark mark(&ctx->arena);
+    const int tx = t[0], ty = t[1], tw = t[2], th = t[3], tlw = t[6], tlh = t[7];
+    TView x;
+    ZJAI_TRY(alloc_tensor(ctx, n, 2 * cdiv(th, 2), 2 * cdiv(tw, 2), c, &x, true));
+    launch_normalize_pad_window(plane, c, H, W, ty, tx, th, tw, x, ctx->stream);
+    ctx->launches++;
+    float* tout = out;
+    if (!whole) {
+      tout = static_cast<float*>(ctx->arena.alloc((size_t)n * cout * tlh * tlw * sizeof(float)));
+      if (!tout) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (analysis tile)");
+    }
+    Runner r = make_runner(ctx, net, &ctx->arena, ctx->stream, n, nullptr);
+    ZJAI_TRY(r.analysis(x, th, tw, tout));
+    if (!whole) {
+      launch_copy_core(tout, n, cout, tlh, tlw, t[13], t[12], t[11], t[10], out, LH, LW, t[9],
+                       t[8], ctx->stream);
+      ctx->launches++;
+    }
+  }
+  return ZJAI_OK;
+}
+
+int zjai_analyze_rgb(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, int n, const uint8_t* rgb,
+                     int h, int w, float* lat_y, float* lat_uv, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  Net* ny = reinterpret_cast<Net*>(net_y);
+  Net* nuv = reinterpret_cast<Net*>(net_uv);
+  if (!ny || !nuv || ny->kind != ZJAI_ANA_Y || nuv->kind != ZJAI_ANA_UV || ny->op != nuv->op)
+    return fail(ZJAI_INVALID_ARGUMENT, "analyze_rgb: needs an ANA_Y and an ANA_UV network of one op");
+  if (!rgb || !lat_y || !lat_uv || n <= 0 || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "analyze_rgb: bad arguments");
+  if (mem != ZJAI_MEM_HOST && mem != ZJAI_MEM_DEVICE)
+    return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  ArenaScope scope(ctx);
+  const int ch = (h + 1) / 2, cw = (w + 1) / 2;
+  const size_t nrgb = (size_t)n * h * w * 3;
+  const uint8_t* drgb = rgb;
+  if (mem == ZJAI_MEM_HOST) {
+    uint8_t* d = static_cast<uint8_t*>(ctx->arena.alloc(nrgb));
+    if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (RGB staging)");
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(d, rgb, nrgb, cudaMemcpyHostToDevice, ctx->stream), "H2D"));
+    drgb = d;
+  }
+  float* dl = static_cast<float*>(ctx->arena.alloc((size_t)n * h * w * sizeof(float)));
+  float* dc = static_cast<float*>(ctx->arena.alloc((size_t)n * 12 * ch * cw * sizeof(float)));
+  if (!dl || !dc) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (analysis inputs)");
+  launch_preprocess_rgb(drgb, n, h, w, dl, dc, ctx->stream);
+  ctx->launches++;
+  const size_t ny_out = (size_t)n * 160 * cdiv(h, 16) * cdiv(w, 16);
+  const size_t nuv_out = (size_t)n * 96 * cdiv(ch, 8) * cdiv(cw, 8);
+  float *oy, *ouv;
+  ZJAI_TRY(stage_out_alloc(ctx, lat_y, ny_out, mem, &oy));
+  ZJAI_TRY(stage_out_alloc(ctx, lat_uv, nuv_out, mem, &ouv));
+  int st = analyze_component(ctx, ny, 0, n, dl, 1, h, w, oy);
+  if (st == ZJAI_OK) st = analyze_component(ctx, nuv, 1, n, dc, 12, ch, cw, ouv);
+  if (st != ZJAI_OK) return settle(ctx, st);
+  ZJAI_TRY(stage_out_finish(ctx, lat_y, oy, ny_out, mem));
+  ZJAI_TRY(stage_out_finish(ctx, lat_uv, ouv, nuv_out, mem));
+  return finish_call(ctx, mem);
+}
+
 int zjai_stage_create(zjai_ctx* ctx, int shuffle, int act, int res_act, const zjai_param* params,
                       int nparams, zjai_net** out) {
   if (!out) return fail(ZJAI_INVALID_ARGUMENT, "null output handle");
@@ -431,20 +545,26 @@ int zjai_synthesis_tiles(int height, int width, int latent_h, int latent_w, int 
 }  // extern "C"
 
 // zjai_synthesize_tiles with f32 planes (bit_depth 0) or quantized sample planes (8: uint8,
-// else uint16), written by the final layers' epilogue.
+// else uint16), written by the final layers' epilogue; `npic` pictures of one size (latents
+// [npic][C][lh][lw], planes [npic][h][w]) each cut into the same `tiles`.
 static int synthesize_tiles_entry(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv,
                                   const float* y_hat_y, const float* y_hat_uv, int lh, int lw,
                                   const zjai_tile* tiles, int ntiles, int out_h, int out_w,
                                   int sv, int sh, int bit_depth, void* rec_y, void* rec_u,
-                                  void* rec_v, int mem, const volatile int* cancel) {
+                                  void* rec_v, int mem, const volatile int* cancel,
+                                  int npic = 1) {
   ZJAI_TRY(ctx_enter(ctx));
   if (!y_hat_y || !y_hat_uv || !rec_y || !rec_u || !rec_v || (ntiles > 0 && !tiles) ||
-      lh <= 0 || lw <= 0 || out_h <= 0 || out_w <= 0)
+      lh <= 0 || lw <= 0 || out_h <= 0 || out_w <= 0 || npic <= 0)
     return fail(ZJAI_INVALID_ARGUMENT, "synthesize: bad arguments");
   if (sv <= 0 || sh <= 0) return fail(ZJAI_INVALID_DATA, "chroma subsampling factor");
   if (bit_depth < 0 || bit_depth > 16 || (bit_depth > 0 && bit_depth < 8))
     return fail(ZJAI_INVALID_ARGUMENT, "synthesize: bit depth must be 8..16 (or 0 for f32)");
   const size_t es = bit_depth == 0 ? sizeof(float) : bit_depth == 8 ? 1 : 2;  // sample bytes
+  const int ch = cdiv(out_h, sv), cw = cdiv(out_w, sh);
+  const size_t ny = (size_t)out_h * out_w, nc = (size_t)ch * cw;
+  if ((double)ny * npic > 2147483647.0)
+    return fail(ZJAI_LIMIT_EXCEEDED, "synthesize: more than 2^31 output samples per call");
   ArenaScope scope(ctx);
   const size_t m2 = ctx->arena2.mark();
   struct Rel {
@@ -453,29 +573,36 @@ static int synthesize_tiles_entry(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_
     ~Rel() { a->release(m); }
   } rel{&ctx->arena2, m2};
   const float *dy, *duv;
-  ZJAI_TRY(stage_in(ctx, y_hat_y, (size_t)160 * lh * lw, mem, &dy));
-  ZJAI_TRY(stage_in(ctx, y_hat_uv, (size_t)96 * lh * lw, mem, &duv));
-  const int ch = cdiv(out_h, sv), cw = cdiv(out_w, sh);
-  const size_t ny = (size_t)out_h * out_w, nc = (size_t)ch * cw;
+  ZJAI_TRY(stage_in(ctx, y_hat_y, (size_t)npic * 160 * lh * lw, mem, &dy));
+  ZJAI_TRY(stage_in(ctx, y_hat_uv, (size_t)npic * 96 * lh * lw, mem, &duv));
   char *oy = static_cast<char*>(rec_y), *ou = static_cast<char*>(rec_u),
        *ov = static_cast<char*>(rec_v);
+  const size_t all = (size_t)npic * (ny + 2 * nc) * es;
   if (mem == ZJAI_MEM_HOST) {
-    oy = static_cast<char*>(ctx->arena.alloc((ny + 2 * nc) * es));
+    oy = static_cast<char*>(ctx->arena.alloc(all));
     if (!oy) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (output planes)");
-    ou = oy + ny * es;
-    ov = ou + nc * es;
-    ZJAI_TRY(cuda_check(cudaMemsetAsync(oy, 0, (ny + 2 * nc) * es, ctx->stream), "memset"));
+    ou = oy + npic * ny * es;
+    ov = ou + npic * nc * es;
+    ZJAI_TRY(cuda_check(cudaMemsetAsync(oy, 0, all, ctx->stream), "memset"));
   }
-  std::vector<zjai_tile> tv(tiles, tiles + ntiles);
+  std::vector<zjai_tile> tv;
+  TilePictures pics;
+  for (int p = 0; p < npic; ++p)
+    for (int i = 0; i < ntiles; ++i) {
+      tv.push_back(tiles[i]);
+      if (npic > 1) pics.pic.push_back(p);
+    }
+  pics.plane_y = (long long)ny;
+  pics.plane_uv = (long long)nc;
   int st = synthesize_tiles_dev(ctx, reinterpret_cast<Net*>(net_y), reinterpret_cast<Net*>(net_uv),
                                 dy, duv, lh, lw, tv, out_h, out_w, sv, sh,
                                 reinterpret_cast<float*>(oy), reinterpret_cast<float*>(ou),
-                                reinterpret_cast<float*>(ov), cancel, nullptr, bit_depth);
+                                reinterpret_cast<float*>(ov), cancel, nullptr, bit_depth, pics);
   if (st != ZJAI_OK) return settle(ctx, st);
   if (mem == ZJAI_MEM_HOST) {
-    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_y, oy, ny * es, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
-    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_u, ou, nc * es, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
-    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_v, ov, nc * es, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_y, oy, npic * ny * es, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_u, ou, npic * nc * es, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rec_v, ov, npic * nc * es, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
   }
   return finish_call(ctx, mem);
 }
@@ -510,6 +637,18 @@ int zjai_synthesize(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const floa
   return zjai_synthesize_tiles(ctx, net_y, net_uv, y_hat_y, y_hat_uv, lh, lw, v.data(),
                                (int)v.size(), out_h, out_w, sv, sh, rec_y, rec_u, rec_v, mem,
                                cancel);
+}
+
+int zjai_synthesize_batch(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, int n,
+                          const float* y_hat_y, const float* y_hat_uv, int lh, int lw, int height,
+                          int width, int out_h, int out_w, int tile_size, int overlap, int sv,
+                          int sh, int bit_depth, void* rec_y, void* rec_u, void* rec_v, int mem,
+                          const volatile int* cancel) {
+  std::vector<zjai_tile> v;
+  ZJAI_TRY(synthesis_tiles(height, width, lh, lw, tile_size, overlap, &v));
+  return synthesize_tiles_entry(ctx, net_y, net_uv, y_hat_y, y_hat_uv, lh, lw, v.data(),
+                                (int)v.size(), out_h, out_w, sv, sh, bit_depth, rec_y, rec_u,
+                                rec_v, mem, cancel, n);
 }
 
 int zjai_synthesize_q(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const float* y_hat_y,

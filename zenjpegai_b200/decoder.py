@@ -116,6 +116,33 @@ class Decoder:
                 stop))
         return ry, ru, rv
 
+    def synthesize_batch(self, y_hat_y, y_hat_uv, height, width, tile_size=0, overlap=0, sv=1,
+                         sh=1, bit_depth=8, out=None, cancel=None):
+        """n independent pictures of one size in one call: latents [n, 160, lh, lw] /
+        [n, 96, lh, lw] -> planes ([n, h, w], [n, ch, cw], [n, ch, cw]) of quantized samples
+        (bit_depth 8..16) or f32 (bit_depth 0)."""
+        n, _, lh, lw = y_hat_y.shape
+        ch, cw = _cdiv(height, sv), _cdiv(width, sh)
+        if out is None:
+            if type(y_hat_y).__module__.startswith("torch"):
+                import torch
+                dt = (torch.float32 if bit_depth == 0 else
+                      torch.uint8 if bit_depth == 8 else torch.int16)
+                z = lambda s: torch.zeros(s, dtype=dt, device=y_hat_y.device)
+            else:
+                dt = np.float32 if bit_depth == 0 else np.uint8 if bit_depth == 8 else np.uint16
+                z = lambda s: np.zeros(s, dt)
+            out = (z((n, height, width)), z((n, ch, cw)), z((n, ch, cw)))
+        ry, ru, rv = out
+        py, mem = _arg(y_hat_y)
+        puv, _ = _arg(y_hat_uv)
+        stop = ctypes.byref(cancel) if cancel is not None else None
+        check(_lib.lib().zjai_synthesize_batch(
+            self.engine.handle, self.net_y.handle, self.net_uv.handle, n, py, puv, lh, lw,
+            height, width, height, width, tile_size, overlap, sv, sh, bit_depth, _ptr(ry),
+            _ptr(ru), _ptr(rv), mem, stop))
+        return ry, ru, rv
+
     # ---- output stage (src/decoder/output.rs) -------------------------------------------
     def quantize_plane(self, x, bit_depth=8, out=None):
         """`quantize_plane_par` (output.rs:330-342); uint8 for 8-bit, else uint16."""
@@ -178,3 +205,37 @@ class Encoder:
         check(_lib.lib().zjai_analysis_secondary(self.net_uv.handle, _arg(chroma12)[0], h2, w2,
                                                  _arg(luv)[0], mem))
         return ly, luv
+
+    def analyze_rgb(self, rgb, out=None):
+        """n 8-bit RGB pictures [n, h, w, 3] (numpy uint8 or a torch CUDA uint8 tensor) ->
+        latents ([n, 160, ceil(h/16), ceil(w/16)], [n, 96, ceil(ceil(h/2)/8), ...]):
+        `preprocess_rgb` and both analysis transforms, tiled like the crate's encoder."""
+        n, h, w, _ = rgb.shape
+        h2, w2 = _cdiv(h, 2), _cdiv(w, 2)
+        shapes = ((n, 160, _cdiv(h, 16), _cdiv(w, 16)), (n, 96, _cdiv(h2, 8), _cdiv(w2, 8)))
+        if out is None:
+            if type(rgb).__module__.startswith("torch"):
+                import torch
+                out = tuple(torch.empty(s, device=rgb.device) for s in shapes)
+            else:
+                out = tuple(np.empty(s, np.float32) for s in shapes)
+        ly, luv = out
+        mem = _lib.MEM_DEVICE if type(rgb).__module__.startswith("torch") else _lib.MEM_HOST
+        if mem == _lib.MEM_HOST:
+            rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+        check(_lib.lib().zjai_analyze_rgb(self.engine.handle, self.net_y.handle,
+                                          self.net_uv.handle, n, _ptr(rgb), h, w, _ptr(ly),
+                                          _ptr(luv), mem))
+        return ly, luv
+
+
+def preprocess_rgb(engine, rgb):
+    """`colour::preprocess_rgb` on the GPU: uint8 RGB [h, w, 3] (host) -> (luma [1, h, w],
+    chroma [12, ceil(h/2), ceil(w/2)]), bit-exact with the crate."""
+    rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+    h, w, _ = rgb.shape
+    luma = np.empty((1, h, w), np.float32)
+    chroma = np.empty((12, _cdiv(h, 2), _cdiv(w, 2)), np.float32)
+    check(_lib.lib().zjai_preprocess_rgb(engine.handle, _ptr(rgb), h, w, _ptr(luma),
+                                         _ptr(chroma), _lib.MEM_HOST))
+    return luma, chroma
