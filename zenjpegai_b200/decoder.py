@@ -188,6 +188,10 @@ class Encoder:
         self.net_y = Network(engine, ANA_Y, self.op, params_y)
         self.net_uv = Network(engine, ANA_UV, self.op, params_uv)
 
+    def close(self):
+        self.net_y.close()
+        self.net_uv.close()
+
     def analyze(self, luma, chroma12):
         """luma [1, h, w] and chroma [12, h/2, w/2] in [0, 255] -> latents
         ([160, ceil(h/16), ceil(w/16)], [96, ceil(h2/8), ceil(w2/8)])."""
