@@ -251,6 +251,17 @@ int zjai_ipc_export(zjai_ctx *ctx, const void *ptr, void *handle, uint64_t *offs
 int zjai_ipc_import(zjai_ctx *ctx, const void *handle, uint64_t offset, void **ptr);
 int zjai_ipc_close(zjai_ctx *ctx, void *ptr);
 
+/* Synthesis straight to RGB, the decoder's `decode` output for a 4:2:0 stream
+ * (reconstruct.rs:274-331, then output.rs:124-262 `to_source_format_par` bicubic 4:2:0 ->
+ * 4:4:4, `to_rgb_planes_owned_par` BT.709, `quantize_par` :407-438): the f32 planes stay in
+ * device memory and the output stage reads them there, as the crate's GPU backend does in
+ * `emit_output` (gpu/src/kernels.rs:910); rgb [height][width][3], uint8 for bit_depth 8, uint16
+ * for 10. Bit-exact with zjai_synthesize (sv = sh = 2) followed by zjai_yuv_to_rgb. */
+int zjai_synthesize_rgb(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, const float *y_hat_y,
+                        const float *y_hat_uv, int lh, int lw, int height, int width,
+                        int tile_size, int overlap, int bit_depth, void *rgb, int mem,
+                        const volatile int *cancel);
+
 /* A batch of n independent pictures of one size synthesised in one call (the crate decodes
  * them one `synthesize_with` call at a time, reconstruct.rs:274-331; here every tile of every
  * picture runs in the same shape batches): latents y_hat_y [n][160][lh][lw], y_hat_uv

@@ -367,3 +367,40 @@ def test_arena_limit_and_bad_geometry():
     assert np.isfinite(out[0]).all()
     dec.close()
     small.close()
+
+
+@pytest.mark.parametrize("op,H,W,tile,overlap,bits", [
+    ("hop", 272, 400, 128, 32, 8),
+    ("sop", 136, 203, 0, 0, 8),
+    ("bop", 96, 128, 0, 0, 10),
+])
+def test_synthesize_rgb(eng, op, H, W, tile, overlap, bits):
+    """Synthesis straight to RGB (the f32 planes never leave the device) equals zjai_synthesize
+    followed by zjai_yuv_to_rgb to the bit, and the oracle's RGB (output.rs on its planes)
+    within one step on >= 99.9% of samples."""
+    import ctypes
+    import synthetic as syn
+    import zenjpegai_b200 as zj
+    from zenjpegai_b200 import _lib
+    from zenjpegai_b200.decoder import Decoder
+    py, puv, ny, nuv = nets(eng, op)
+    dec = Decoder.__new__(Decoder)
+    dec.engine, dec.op, dec.net_y, dec.net_uv = eng, zo.OPS[op], ny, nuv
+    lh, lw = -(-H // 16), -(-W // 16)
+    ly = syn.laplace_latent(13, "ly", (160, lh, lw), 1.5)
+    luv = syn.laplace_latent(13, "luv", (96, lh, lw), 1.5)
+    got = dec.synthesize_rgb(ly, luv, H, W, tile_size=tile, overlap=overlap, bit_depth=bits)
+    y, u, v = dec.synthesize(ly, luv, H, W, tile_size=tile, overlap=overlap)
+    dt = np.uint8 if bits == 8 else np.uint16
+    two = np.empty((H, W, 3), dt)
+    p = lambda a: ctypes.c_void_p(a.ctypes.data)
+    zj.check(_lib.lib().zjai_yuv_to_rgb(eng.handle, p(y), p(u), p(v), H, W, u.shape[0],
+                                        u.shape[1], bits, p(two), 0))
+    assert np.array_equal(got, two)
+    wy, wu, wv = zo.synthesize(zo.Checkpoint(py), zo.Checkpoint(puv), zo.OPS[op], ly, luv, H, W,
+                               tile_size=tile, overlap=overlap)
+    r, g, b = zo.to_rgb_planes(wy, zo.resize_bicubic(wu[None], H, W)[0],
+                               zo.resize_bicubic(wv[None], H, W)[0])
+    want = zo.quantize_rgb(r, g, b, bits)
+    d = np.abs(got.astype(np.int32) - want.astype(np.int32))
+    assert float(np.mean(d <= (1 if bits == 8 else 4))) >= 0.999

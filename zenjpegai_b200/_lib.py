@@ -85,6 +85,7 @@ def lib():
     L.zjai_synthesis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _vp, _i]
     L.zjai_analysis_primary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
     L.zjai_analysis_secondary.argtypes = [_vp, _vp, _i, _i, _vp, _i]
+    L.zjai_synthesize_rgb.argtypes = [_vp, _vp, _vp, _vp, _vp] + [_i] * 7 + [_vp, _i, _vp]
     L.zjai_synthesize_batch.argtypes = [_vp, _vp, _vp, _i, _vp, _vp] + [_i] * 11 + [_vp, _vp,
                                                                                   _vp, _i, _vp]
     L.zjai_preprocess_rgb.argtypes = [_vp, _vp, _i, _i, _vp, _vp, _i]

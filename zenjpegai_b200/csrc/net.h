@@ -116,6 +116,10 @@ void launch_normalize_pad_window(const float* src, int c, int SH, int SW, int y0
 // [n][12][ph / 2][pw / 2] (planar f32, [0, 255])
 void launch_preprocess_rgb(const uint8_t* rgb, int n, int h, int w, float* luma, float* chroma,
                            cudaStream_t s);
+// output.cu: bicubic 4:2:0 -> 4:4:4, BT.709 and quantisation of device planes into interleaved
+// RGB (uint8 for 8 bits, else uint16), on stream s
+int output_yuv_to_rgb(Ctx* ctx, const float* y, const float* u, const float* v, int h, int w,
+                      int ch, int cw, int bit_depth, void* rgb, cudaStream_t s);
 void launch_copy_core(const float* tile, int n, int C, int th, int tw, int oy, int ox, int core_h,
                       int core_w, float* full, int LH, int LW, int cy, int cx, cudaStream_t s);
 

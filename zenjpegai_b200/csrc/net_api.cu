@@ -639,6 +639,50 @@ int zjai_synthesize(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const floa
                                cancel);
 }
 
+// Whole-picture synthesis straight to RGB: the f32 planes stay in the arena and the output
+// stage (bicubic 4:2:0 -> 4:4:4, BT.709, rounding) reads them there, so only the RGB samples
+// reach the caller (the reference GPU backend's emit_output, gpu/src/kernels.rs:910).
+int zjai_synthesize_rgb(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const float* y_hat_y,
+                        const float* y_hat_uv, int lh, int lw, int height, int width,
+                        int tile_size, int overlap, int bit_depth, void* rgb, int mem,
+                        const volatile int* cancel) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!y_hat_y || !y_hat_uv || !rgb || lh <= 0 || lw <= 0 || height <= 0 || width <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "synthesize_rgb: bad arguments");
+  if (bit_depth != 8 && bit_depth != 10)
+    return fail(ZJAI_INVALID_ARGUMENT, "synthesize_rgb: bit depth must be 8 or 10");
+  if (mem != ZJAI_MEM_HOST && mem != ZJAI_MEM_DEVICE)
+    return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  std::vector<zjai_tile> tiles;
+  ZJAI_TRY(synthesis_tiles(height, width, lh, lw, tile_size, overlap, &tiles));
+  ArenaScope scope(ctx);
+  const size_t m2 = ctx->arena2.mark();
+  struct Rel {
+    Arena* a;
+    size_t m;
+    ~Rel() { a->release(m); }
+  } rel{&ctx->arena2, m2};
+  const float *dy, *duv;
+  ZJAI_TRY(stage_in(ctx, y_hat_y, (size_t)160 * lh * lw, mem, &dy));
+  ZJAI_TRY(stage_in(ctx, y_hat_uv, (size_t)96 * lh * lw, mem, &duv));
+  const int ch = cdiv(height, 2), cw = cdiv(width, 2);
+  const size_t ny = (size_t)height * width, nc = (size_t)ch * cw;
+  float* planes = static_cast<float*>(ctx->arena.alloc((ny + 2 * nc) * sizeof(float)));
+  const size_t ob = ny * 3 * (bit_depth == 8 ? 1 : 2);
+  void* dout = mem == ZJAI_MEM_HOST ? ctx->arena.alloc(ob + 16) : rgb;
+  if (!planes || !dout) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (RGB planes)");
+  int st = synthesize_tiles_dev(ctx, reinterpret_cast<Net*>(net_y), reinterpret_cast<Net*>(net_uv),
+                                dy, duv, lh, lw, tiles, height, width, 2, 2, planes, planes + ny,
+                                planes + ny + nc, cancel, nullptr, 0, TilePictures());
+  if (st == ZJAI_OK)
+    st = output_yuv_to_rgb(ctx, planes, planes + ny, planes + ny + nc, height, width, ch, cw,
+                           bit_depth, dout, ctx->stream);
+  if (st != ZJAI_OK) return settle(ctx, st);
+  if (mem == ZJAI_MEM_HOST)
+    ZJAI_TRY(cuda_check(cudaMemcpyAsync(rgb, dout, ob, cudaMemcpyDeviceToHost, ctx->stream), "D2H"));
+  return finish_call(ctx, mem);
+}
+
 int zjai_synthesize_batch(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, int n,
                           const float* y_hat_y, const float* y_hat_uv, int lh, int lw, int height,
                           int width, int out_h, int out_w, int tile_size, int overlap, int sv,

@@ -116,6 +116,25 @@ class Decoder:
                 stop))
         return ry, ru, rv
 
+    def synthesize_rgb(self, y_hat_y, y_hat_uv, height, width, tile_size=0, overlap=0,
+                       bit_depth=8, cancel=None):
+        """Whole picture straight to interleaved RGB [h, w, 3] (synthesis, then bicubic
+        4:2:0 -> 4:4:4, BT.709 and rounding on the device; output.rs:124-262, 407-438)."""
+        _, lh, lw = y_hat_y.shape
+        if type(y_hat_y).__module__.startswith("torch"):
+            import torch
+            out = torch.empty((height, width, 3), dtype=torch.uint8 if bit_depth == 8
+                              else torch.int16, device=y_hat_y.device)
+        else:
+            out = np.empty((height, width, 3), np.uint8 if bit_depth == 8 else np.uint16)
+        py, mem = _arg(y_hat_y, (160, lh, lw))
+        puv, _ = _arg(y_hat_uv, (96, lh, lw))
+        stop = ctypes.byref(cancel) if cancel is not None else None
+        check(_lib.lib().zjai_synthesize_rgb(
+            self.engine.handle, self.net_y.handle, self.net_uv.handle, py, puv, lh, lw, height,
+            width, tile_size, overlap, bit_depth, _ptr(out), mem, stop))
+        return out
+
     def synthesize_batch(self, y_hat_y, y_hat_uv, height, width, tile_size=0, overlap=0, sv=1,
                          sh=1, bit_depth=8, out=None, cancel=None):
         """n independent pictures of one size in one call: latents [n, 160, lh, lw] /
