@@ -46,7 +46,7 @@ CONFIGS = {
                   lat_seed=100, metric=SYNTH_METRIC, scaling="strong",
                   desc="BASELINE config 4: HOP synthesis, 3840x2160 4:2:0, 512/16 tiles"),
     "sop1080": dict(kind="synth", op="sop", H=1080, W=1920, tile=0, overlap=0, seed=2,
-                    lat_seed=100, metric=SYNTH_METRIC, scaling="strong",
+                    lat_seed=100, metric=SYNTH_METRIC, scaling="strong", law="he",
                     desc="BASELINE config 3: SOP synthesis, 1920x1080 4:2:0, one tile"),
     "bop_batch64": dict(kind="batch", op="bop", H=1024, W=1024, npic=64, per_call=8, seed=4,
                         metric="batched decode + analysis Mpixel/s", scaling="strong",
@@ -213,6 +213,21 @@ class ClockSampler:
 # oracle's nn::reference loops), timed on the box's host cores
 # ---------------------------------------------------------------------------------------------
 
+def synth_params(cfg):
+    """The synthesis weights of a config: the He-normal law where BASELINE prescribes it
+    (config 3), else the role-scaled random init (synthetic.make_params)."""
+    import synthetic as syn
+    if cfg.get("law") == "he":
+        return syn.synthesis_params_he(cfg["op"], cfg["seed"])
+    return syn.synthesis_params(cfg["op"], cfg["seed"])
+
+
+def weights_desc(cfg):
+    if cfg.get("law") == "he":
+        return "random-init, seed %d, He-normal N(0, 2 / fan_in) (the prescribed law)" % cfg["seed"]
+    return "random-init, seed %d (role-scaled normal)" % cfg["seed"]
+
+
 def _tile_rows(cfg):
     """The workload's tiles (oracle tiling, tools/tiles.rs:39-119) grouped by tile row."""
     import oracle as zo
@@ -235,7 +250,7 @@ class CpuSynth:
         self.zo, self.cfg = zo, cfg
         H, W = cfg["H"], cfg["W"]
         lh, lw = -(-H // 16), -(-W // 16)
-        py, puv = syn.synthesis_params(cfg["op"], cfg["seed"])
+        py, puv = synth_params(cfg)
         self.cky, self.ckuv = zo.Checkpoint(py), zo.Checkpoint(puv)
         self.ly = syn.laplace_latent(cfg["lat_seed"], "ly", (160, lh, lw), 1.5)
         self.luv = syn.laplace_latent(cfg["lat_seed"], "luv", (96, lh, lw), 1.5)
@@ -388,7 +403,7 @@ def config_dict(args, cfg, world):
             "parallelism": "tiles round-robin over %d GPU(s), each rank sent only the latent "
                            "rows / columns its tiles read" % world,
             "gather": cfg.get("gather", "none (one GPU)") if world > 1 else "none (one GPU)",
-            "weights": "random-init, seed %d (role-scaled normal)" % cfg["seed"],
+            "weights": weights_desc(cfg),
             "l2": "flushed between steps (256 MiB write, outside the timed events)",
             "precision": "f16 operands, f32 accumulation (TMEM); the CPU arm computes f32"}
 
@@ -530,7 +545,7 @@ def main():
         op = cfg["op"]
         lh, lw = -(-H // 16), -(-W // 16)
         ch, cw = -(-H // 2), -(-W // 2)
-        py, puv = syn.synthesis_params(op, cfg["seed"])
+        py, puv = synth_params(cfg)
         dec = Decoder(eng, op, py, puv)
         closers.append(dec.close)
         ly_h = torch.from_numpy(syn.laplace_latent(cfg["lat_seed"], "ly", (160, lh, lw), 1.5))

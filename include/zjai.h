@@ -38,7 +38,8 @@ typedef enum {
   ZJAI_OK = 0,
   ZJAI_INVALID_ARGUMENT = 1, /* Error::InvalidArgument */
   ZJAI_UNSUPPORTED = 2,      /* Error::Unsupported */
-  ZJAI_LIMIT_EXCEEDED = 3,   /* Error::LimitExceeded (arena / size limits) */
+  ZJAI_LIMIT_EXCEEDED = 3,   /* Error::LimitExceeded (arena / size limits, or an activation
+                              * beyond the f16 range, reported at the next synchronising call) */
   ZJAI_CANCELLED = 4,        /* Error::Cancelled (the caller's stop flag was set) */
   ZJAI_MODEL = 5,            /* Error::Model (missing / mis-shaped parameter) */
   ZJAI_INVALID_DATA = 6,     /* Error::InvalidData (malformed tile geometry) */
@@ -95,6 +96,12 @@ int zjai_ctx_sync(zjai_ctx *ctx);
  * counterpart in the reference (its CPU path has no device waits): a watchdog bound for
  * callers that prefer to fail fast, and the way the timeout path is exercised in tests. */
 int zjai_ctx_set_wait_limit(zjai_ctx *ctx, int64_t cycles);
+
+/* Diagnostics: with clamp = 0 the f32 planes of zjai_synthesis_primary / _secondary /
+ * zjai_synthesize* are the denormalised x * 128 + 127.5 without the [0, 255] clamp of
+ * `denormalize` (synthesis.rs:188-192), so tests can compare the networks' values where the
+ * clamp would saturate them (quantized outputs clamp regardless). Default 1. */
+int zjai_ctx_set_output_clamp(zjai_ctx *ctx, int clamp);
 
 /* Number of kernels this context has launched since creation (for launch accounting). */
 int64_t zjai_ctx_launch_count(const zjai_ctx *ctx);

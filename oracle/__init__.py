@@ -69,6 +69,7 @@ def _declare(L):
     L.zo_analysis_tiles.argtypes = [_i, _i, _i, _i, _i, ctypes.c_void_p, _i]
     L.zo_analyze_tiled.argtypes = [ctypes.c_void_p, _i, _i, _f, _i, _i, _f]
     L.zo_set_fast.argtypes = [_i]
+    L.zo_set_output_clamp.argtypes = [_i]
     L.zo_conv2d_out_size.argtypes = [_i] * 7 + [ctypes.POINTER(_i)] * 3
     L.zo_conv2d.argtypes = [_f, _i, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i,
                             ctypes.POINTER(_i), _f]
@@ -120,6 +121,11 @@ def set_fast(on):
     """Convolutions on the restatement of the crate's nn::fast algorithm (fast.c: same bits,
     blocked layout and register tiles; the timed CPU baseline) or on the reference loops."""
     lib().zo_set_fast(1 if on else 0)
+
+
+def set_output_clamp(on):
+    """False: the synthesis outputs are x * 128 + 127.5 without the [0, 255] clamp."""
+    lib().zo_set_output_clamp(1 if on else 0)
 
 
 def get_fast():

@@ -265,10 +265,16 @@ void zo_elu_gate(float *a, const float *b, int64_t n) {
     }
 }
 
-/* `x * 128 + 127.5` clamped to [0, 255] (synthesis.rs:188-192) */
+/* `x * 128 + 127.5` clamped to [0, 255] (synthesis.rs:188-192); without the clamp while
+ * zo_set_output_clamp(0) (a diagnostic for comparing values the clamp would saturate) */
+static int g_clamp = 1;
+void zo_set_output_clamp(int on) { g_clamp = on != 0; }
 void zo_denormalize(float *x, int64_t n) {
     ZO_PAR_FOR
-    for (int64_t i = 0; i < n; i++) x[i] = clampf(x[i] * 128.0f + 127.5f, 0.0f, 255.0f);
+    for (int64_t i = 0; i < n; i++) {
+        float v = x[i] * 128.0f + 127.5f;
+        x[i] = g_clamp ? clampf(v, 0.0f, 255.0f) : v;
+    }
 }
 
 /* `(x - 127.5) / 128` (analysis.rs:36-39) */

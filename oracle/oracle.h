@@ -35,6 +35,8 @@ int zo_get_threads(void);
  * (fast.c: blocked layout, register tiles, per-row threads), which gives the same bits; the
  * timed CPU baseline. 0 (default): the nn::reference loops. */
 void zo_set_fast(int on);
+/* 0: `denormalize` without its [0, 255] clamp (diagnostics); 1 (default): as the crate. */
+void zo_set_output_clamp(int on);
 int zo_get_fast(void);
 /* nn::fast restatements (fast.c); return 1 when the geometry is not handled there */
 int zf_conv2d(const float *x, int c, int h, int w, const float *weight, const float *bias,

@@ -90,7 +90,7 @@ def _conv(specs, prefix, cin, cout, kh, kw, groups=1, bias=True, gain=1.0):
 
 def _convt(specs, prefix, cin, cout, k, gain=1.0):
     # stride-2 transposed conv: about k*k/4 taps reach each output
-    specs.append((prefix + ".weight", (cin, cout, k, k), "w", max(1, cin * k * k // 4) / gain ** 2))
+    specs.append((prefix + ".weight", (cin, cout, k, k), "wt", max(1, cin * k * k // 4) / gain ** 2))
     specs.append((prefix + ".bias", (cout,), "b", 0))
 
 
@@ -225,7 +225,7 @@ def make_params(spec, seed, tag=""):
     out = {}
     for name, shape, kind, fan_in in spec:
         key = tag + name
-        if kind == "w":
+        if kind in ("w", "wt"):
             out[name] = normal(seed, key, shape, std=float(np.sqrt(1.0 / fan_in)))
         elif kind == "b":
             out[name] = normal(seed, key, shape, std=0.01)
@@ -238,6 +238,25 @@ def make_params(spec, seed, tag=""):
         else:
             raise ValueError(kind)
     return out
+
+
+def he_normal(spec, seed, tag=""):
+    """The law BASELINE prescribes: every conv / transposed-conv weight N(0, 2 / fan_in) with
+    PyTorch's fan_in (dim 1 x kernel taps: in / groups x kh x kw for a conv [out][in / g][kh][kw],
+    out x k x k for a transposed conv [in][out][k][k]); biases, layer-norm parameters and
+    temperatures as in make_params."""
+    out = make_params(spec, seed, tag)
+    for name, shape, kind, _ in spec:
+        if kind in ("w", "wt"):
+            fan = int(np.prod(shape[1:]))
+            out[name] = normal(seed, tag + name, shape, std=float(np.sqrt(2.0 / fan)))
+    return out
+
+
+def synthesis_params_he(op, seed):
+    """(luma params, chroma params) with the prescribed He-normal weight law."""
+    return (he_normal(synthesis_primary_spec(op), seed, "Y/"),
+            he_normal(synthesis_secondary_spec(op), seed, "UV/"))
 
 
 def synthesis_params(op, seed):

@@ -94,6 +94,10 @@ class Engine:
     def sync(self):
         check(_lib.lib().zjai_ctx_sync(self.handle))
 
+    def set_output_clamp(self, clamp):
+        """False: synthesis planes without the final [0, 255] clamp (diagnostics)."""
+        check(_lib.lib().zjai_ctx_set_output_clamp(self.handle, 1 if clamp else 0))
+
     def set_wait_limit(self, cycles):
         """Limit of the convolution kernel's pipeline waits in SM cycles (0: default)."""
         check(_lib.lib().zjai_ctx_set_wait_limit(self.handle, int(cycles)))

@@ -71,6 +71,7 @@ def lib():
     L.zjai_ctx_destroy.argtypes = [_vp]
     L.zjai_ctx_set_stream.argtypes = [_vp, _vp]
     L.zjai_ctx_sync.argtypes = [_vp]
+    L.zjai_ctx_set_output_clamp.argtypes = [_vp, _i]
     L.zjai_ctx_set_wait_limit.argtypes = [_vp, ctypes.c_int64]
     L.zjai_ctx_launch_count.argtypes = [_vp]
     L.zjai_ctx_launch_count.restype = ctypes.c_int64

@@ -16,16 +16,20 @@ int ctx_enter(zjai_ctx* ctx) {
 }
 
 int ctx_check_status(Ctx* ctx) {
-  int err = 0;
-  ZJAI_TRY(cuda_check(cudaMemcpyAsync(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost,
+  int err[2] = {0, 0};
+  ZJAI_TRY(cuda_check(cudaMemcpyAsync(err, ctx->d_err, sizeof err, cudaMemcpyDeviceToHost,
                                       ctx->stream),
                       "status word read"));
   ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "stream sync"));
-  if (err != 0) {
-    cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream);
+  if (err[0] != 0 || err[1] != 0) {
+    cudaMemsetAsync(ctx->d_err, 0, sizeof err, ctx->stream);
     cudaStreamSynchronize(ctx->stream);
-    return fail(ZJAI_DEVICE_TIMEOUT,
-                "a kernel's bounded wait gave up (device status " + std::to_string(err) + ")");
+    if (err[0] != 0)
+      return fail(ZJAI_DEVICE_TIMEOUT,
+                  "a kernel's bounded wait gave up (device status " + std::to_string(err[0]) + ")");
+    return fail(ZJAI_LIMIT_EXCEEDED,
+                "an activation left the f16 range (|x| > 65504) in a residual or gate epilogue: "
+                "the weights / inputs exceed what the f16 activation storage holds");
   }
   return ZJAI_OK;
 }
@@ -125,8 +129,8 @@ int zjai_ctx_create(int device, size_t arena_bytes, zjai_ctx** out) {
       (st = cuda_check(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming), "event")) ||
       (st = cuda_check(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming), "event")) ||
       (st = cuda_check(cudaMalloc(&c->arena.base, arena_bytes), "arena cudaMalloc")) ||
-      (st = cuda_check(cudaMalloc(&c->d_err, sizeof(int)), "status cudaMalloc")) ||
-      (st = cuda_check(cudaMemset(c->d_err, 0, sizeof(int)), "status memset")) ||
+      (st = cuda_check(cudaMalloc(&c->d_err, 2 * sizeof(int)), "status cudaMalloc")) ||
+      (st = cuda_check(cudaMemset(c->d_err, 0, 2 * sizeof(int)), "status memset")) ||
       (st = cuda_check(cudaDriverGetVersion(&c->driver_version), "driver version"))) {
     zjai_ctx_destroy(c);
     return st;
@@ -176,6 +180,12 @@ int zjai_ctx_set_stream(zjai_ctx* ctx, void* s) {
 int zjai_ctx_sync(zjai_ctx* ctx) {
   ZJAI_TRY(ctx_enter(ctx));
   return ctx_check_status(ctx);
+}
+
+int zjai_ctx_set_output_clamp(zjai_ctx* ctx, int clamp) {
+  if (!ctx) return fail(ZJAI_INVALID_ARGUMENT, "null context");
+  ctx->clamp_output = clamp != 0;
+  return ZJAI_OK;
 }
 
 int zjai_ctx_set_wait_limit(zjai_ctx* ctx, int64_t cycles) {

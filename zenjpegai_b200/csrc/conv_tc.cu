@@ -114,7 +114,7 @@ constexpr int kChunk = 16;  // accumulator columns per TMEM load and epilogue st
 template <int OP>
 __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kChunk], int col0,
                                          int img, int oy, int ox, bool valid, const uint32_t* tab,
-                                         const float* btab) {
+                                         const float* btab, float& rmax) {
   constexpr int G = kChunk / 8;
   int Yg[G], Xg[G], cg[G];
   bool ok[G];
@@ -172,6 +172,10 @@ __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kCh
       }
     }
     act8_fast(x, a.act2);
+    if constexpr (OP != OP_NONE) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) rmax = fmaxf(rmax, fabsf(x[e]));
+    }
     *reinterpret_cast<uint4*>(a.out + img * a.out_img + Yg[g] * a.out_row + Xg[g] * a.out_pix +
                               cg[g]) = pack_h8(x);
     if (a.out2) {
@@ -197,7 +201,8 @@ template <int OP>
 __device__ __forceinline__ void epi_staged(const ConvArgs& a, const float (&v)[kChunk],
                                            int col0, int ch0, long long p1, long long p2,
                                            long long p2o, bool valid, const float* btab,
-                                           uint4* dst, const uint4* rs1, const uint4* rs2) {
+                                           uint4* dst, const uint4* rs1, const uint4* rs2,
+                                           float& rmax) {
   constexpr int G = kChunk / 8;
   uint4 r1[G], r2[G];
   if constexpr (OP != OP_NONE) {
@@ -246,6 +251,14 @@ __device__ __forceinline__ void epi_staged(const ConvArgs& a, const float (&v)[k
       }
     }
     act8_fast(x, a.act2);
+    // residual / gate outputs grow along the network: track the largest stored magnitude of
+    // the pixels this thread owns (lanes outside the view stage values nobody stores)
+    if constexpr (OP != OP_NONE) {
+      if (valid && c < a.cph) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) rmax = fmaxf(rmax, fabsf(x[e]));
+      }
+    }
     dst[g] = pack_h8(x);
     if (a.out2 && valid && c < a.cph) {
 #pragma unroll
@@ -294,7 +307,10 @@ __device__ __forceinline__ void epi_planar(const ConvArgs& a, const float (&v)[k
       SX = PX / a.sh;
     }
     float x = act_rt(v[j] * a.scale + btab[col0 + j], a.act1);
-    if (a.denorm) x = fminf(fmaxf(x * 128.f + 127.5f, 0.f), 255.f);
+    if (a.denorm) {
+      x = x * 128.f + 127.5f;
+      if (a.denorm == 1) x = fminf(fmaxf(x, 0.f), 255.f);  // 2: unclamped (diagnostics)
+    }
     const long long ei = base + (long long)SY * a.p_row + SX;
     const bool second = ch == 1 && a.pout2;  // plane 1 has its own pointer
     if (a.qbytes) {
@@ -737,6 +753,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       c = it - sub * nchunks;
       return it < items;
     };
+    float rmax = 0.f;  // largest |stored value| of a residual / gate epilogue (range check)
     if (pre && (int)blockIdx.x < a.num_tiles) {
       int s0, c0;
       if (first_item(s0, c0)) res_issue(decode_tile(a, blockIdx.x), s0, c0);
@@ -807,7 +824,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             __syncwarp();
             uint8_t* sl = wslots + slot * kEpiSlotBytes;
             epi_staged<OP>(a, v, col0, col0, p1, p2, p2o, valid, btab,
-                           reinterpret_cast<uint4*>(sl + lane * 32), rs1, rs2);
+                           reinterpret_cast<uint4*>(sl + lane * 32), rs1, rs2, rmax);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -831,7 +848,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
               __syncwarp();
               uint8_t* sl = wslots + slot * kEpiSlotBytes;
               epi_staged<OP>(a, v, col0, ch0, q1, q2, q2o, valid, btab,
-                             reinterpret_cast<uint4*>(sl + lane * 32), rs1, rs2);
+                             reinterpret_cast<uint4*>(sl + lane * 32), rs1, rs2, rmax);
               fence_proxy_async_smem();
               __syncwarp();
               if (lane == 0) {
@@ -844,7 +861,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           } else if constexpr (MODE == kModePlanar) {
             epi_planar(a, v, col0, tc.img, oy, ox, valid, tab, btab);
           } else {
-            epi_nhwc<OP>(a, v, col0, tc.img, oy, ox, valid, tab, btab);
+            epi_nhwc<OP>(a, v, col0, tc.img, oy, ox, valid, tab, btab, rmax);
           }
         }
       };
@@ -871,6 +888,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         acc = 0;
         acc_phase ^= 1u;
       }
+    }
+    // an activation beyond the f16 range (it would be stored as inf): flag it for the host
+    if constexpr (OP != OP_NONE) {
+      if (!(rmax <= 65504.f)) atomicOr(a.err + 1, 1);
     }
     // residual boxes still in flight (a wait gave up) land before shared memory goes away
     for (; ruse < rissue; ++ruse) mbar_wait_drain(rb0 + 8u * (ruse & 1u), (ruse >> 1) & 1u, a.err);

@@ -94,7 +94,7 @@ struct ConvArgs {
   const CUtensorMap* tmR;
   int nres;
   // planar f32 output
-  int planar, denorm;
+  int planar, denorm;  // denorm 1: x * 128 + 127.5 clamped to [0, 255]; 2: not clamped
   float* pout;
   float* pout2;        // plane 1 (when not at pout + p_plane)
   long long p_plane, p_row, p_img;
@@ -110,7 +110,7 @@ struct ConvArgs {
   // integer planes and the strides count samples
   int qbytes;
   float qmax;
-  int* err;
+  int* err;            // [0] wait status, [1] set when a residual / gate output left the f16 range
   // limit of the kernel's pipeline waits in SM cycles (0: the default of about 2 s); a wait
   // that runs out records DEV_TIMEOUT_* in *err and the CTA drains its copies and MMAs and ends
   long long wait_cycles;

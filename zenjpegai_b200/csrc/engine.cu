@@ -551,7 +551,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     }
   } else {
     a.planar = 1;
-    a.denorm = o.denorm;
+    a.denorm = o.denorm ? (o.clamp ? 1 : 2) : 0;
     a.pout = o.pout;
     a.pout2 = o.pout2;
     a.img_win = o.img_win;

@@ -70,7 +70,12 @@ struct Ctx {
   Arena arena;   // work of `stream`
   Arena arena2;  // work of `stream2` (chroma synthesis runs beside luma)
   Arena* cur_arena = nullptr;  // arena of the network runner currently launching (or null)
-  int* d_err = nullptr;  // kernel status word
+  // kernel status words: [0] the code of a bounded wait that gave up, [1] set when a residual /
+  // gate epilogue produced an activation beyond the f16 range
+  int* d_err = nullptr;
+  // final synthesis layers clamp the denormalised planes to [0, 255] (false: the raw
+  // x * 128 + 127.5, zjai_ctx_set_output_clamp)
+  bool clamp_output = true;
   // limit of the convolution kernel's pipeline waits in SM cycles (0: the kernel's default of
   // about 2 s), zjai_ctx_set_wait_limit
   long long wait_cycles = 0;
@@ -183,6 +188,7 @@ struct ConvOut {
   const TView* out2 = nullptr;  // relu6 copy
   // planar f32 output
   bool planar = false, denorm = false;
+  bool clamp = true;  // denormalised planar output clamped to [0, 255]
   float* pout = nullptr;
   float* pout2 = nullptr;
   const int* img_win = nullptr;  // per-image output windows (device), see ConvArgs

@@ -575,6 +575,7 @@ int Runner::final_planar(const std::string& name, const TView& x, const FinalOut
   ConvOut o;
   o.planar = true;
   o.denorm = true;
+  o.clamp = ctx->clamp_output;
   o.pout = fo.plane0;
   o.pout2 = fo.plane1;
   o.p_plane = fo.plane_stride;
