@@ -53,8 +53,10 @@ enum { ZJAI_MEM_HOST = 0, ZJAI_MEM_DEVICE = 1 };
 enum { ZJAI_SOP = 0, ZJAI_BOP = 1, ZJAI_HOP = 2 };
 
 /* Network kinds: synthesis primary / secondary (src/model/synthesis.rs), analysis primary /
- * secondary (src/model/analysis.rs). */
-enum { ZJAI_SYN_Y = 0, ZJAI_SYN_UV = 1, ZJAI_ANA_Y = 2, ZJAI_ANA_UV = 3 };
+ * secondary (src/model/analysis.rs), and the latent-domain float networks of one component's
+ * common modules (src/model/common.rs:34-131): the hyper-decoder (hyper_decoder.rs) and, when
+ * the checkpoint holds it, the context model (mcm.rs). */
+enum { ZJAI_SYN_Y = 0, ZJAI_SYN_UV = 1, ZJAI_ANA_Y = 2, ZJAI_ANA_UV = 3, ZJAI_LATENT = 5 };
 
 /* Epilogue activations of the layer entry points. ZJAI_ACT_LEAKY is LeakyReLU(0.01), which
  * the reference does not have (only relu / relu6, src/nn/fast/layers.rs:174-186); it exists
@@ -194,6 +196,30 @@ int zjai_preprocess_rgb(zjai_ctx *ctx, const uint8_t *rgb, int h, int w, float *
  * lat_uv [n][96][ceil(ceil(h/2)/8)][ceil(ceil(w/2)/8)]. */
 int zjai_analyze_rgb(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, int n,
                      const uint8_t *rgb, int h, int w, float *lat_y, float *lat_uv, int mem);
+
+/* Latent-domain float networks of one component, from a ZJAI_LATENT network (zjai_net_create
+ * with the common checkpoint's "hyper_decoder.*" and optional "context.MCM.*" parameters; the
+ * operating point is not used). C is the checkpoint's channel count (160 luma, 96 chroma). */
+
+/* `HyperDecoder::forward_f32` (src/model/hyper_decoder.rs:94-113; `forward` :47-90 on i8 values
+ * gives the same output): z_hat [C][hz][wz] -> psi [4C][out_h][out_w], the 2x upsampled map
+ * cropped to (out_h, out_w) (at most 2 hz x 2 wz). */
+int zjai_hyper_decode(zjai_net *net, const float *z_hat, int hz, int wz, int out_h, int out_w,
+                      float *psi, int mem);
+
+/* The latent y_hat [C][h][w] from the dequantised residual [C][h][w] and psi
+ * [4C][ceil(h/2)][ceil(w/2)] (src/decoder/reconstruct.rs:200-212): `ContextModel::decompress`
+ * (src/model/mcm.rs:161-257, four stages over the 2x2 grid) when the network holds a context
+ * model, else `upshuffle_psi` (mcm.rs:742-760) plus the residual. */
+int zjai_context_decompress(zjai_net *net, const float *residual, int h, int w, const float *psi,
+                            float *y_hat, int mem);
+
+/* One region of `reconstruct_latent` (src/decoder/reconstruct.rs:107-230, a picture without
+ * independent regions): psi = hyper-decoder(z_hat) at ceil(h/2) x ceil(w/2), then y_hat as
+ * zjai_context_decompress, psi kept on the device between the two. psi (output) may be null. */
+int zjai_reconstruct_latent(zjai_net *net, const float *z_hat, int hz, int wz,
+                            const float *residual, int h, int w, float *psi, float *y_hat,
+                            int mem);
 
 /* One synthesis tile (src/tools/tiles.rs:26-32 `SynthesisTile`). */
 typedef struct {

@@ -93,6 +93,8 @@ def _declare(L):
                                          _i, _i, _f]
     L.zo_analysis_primary.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f]
     L.zo_analysis_secondary.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f]
+    L.zo_hyper_decode.argtypes = [ctypes.POINTER(Ckpt), _f, _i, _i, _i, _i, _i, _f]
+    L.zo_context_decompress.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f, _f]
     L.zo_synthesis_tiles.argtypes = [_i] * 6 + [ctypes.POINTER(Tile), _i]
     L.zo_synthesize.argtypes = [ctypes.POINTER(Ckpt), ctypes.POINTER(Ckpt), _i, _f, _f] + \
         [_i] * 10 + [_f, _f, _f]
@@ -331,6 +333,32 @@ def analysis_secondary(ck, op, x):
     if lib().zo_analysis_secondary(ctypes.byref(ck.ck), op, _fp(x), h, w, _fp(out)):
         raise ValueError("analysis_secondary")
     return out
+
+
+def hyper_decode(ck, z, out_h, out_w):
+    """HyperDecoder::forward_f32 (hyper_decoder.rs:94-113): z [c, hz, wz] -> psi
+    [4c, out_h, out_w]."""
+    z = _c32(z)
+    c, hz, wz = z.shape
+    psi = np.empty((4 * c, out_h, out_w), np.float32)
+    if lib().zo_hyper_decode(ctypes.byref(ck.ck), _fp(z), c, hz, wz, out_h, out_w, _fp(psi)):
+        raise ValueError("hyper_decode: crop larger than the upsampled map")
+    return psi
+
+
+def context_decompress(ck, residual, psi):
+    """The latent y_hat from the dequantised residual [c, h, w] and psi [4c, ceil(h/2),
+    ceil(w/2)] (reconstruct.rs:200-212): the context model (mcm.rs:161-257) when `ck` has one,
+    else upshuffle_psi + residual."""
+    residual, psi = _c32(residual), _c32(psi)
+    c, h, w = residual.shape
+    if psi.shape != (4 * c, -(-h // 2), -(-w // 2)):
+        raise ValueError("context_decompress: residual / psi shape mismatch")
+    y = np.empty_like(residual)
+    if lib().zo_context_decompress(ctypes.byref(ck.ck), c, _fp(residual), h, w, _fp(psi),
+                                   _fp(y)):
+        raise ValueError("context_decompress: channel count must be a multiple of 32")
+    return y
 
 
 def synthesis_tiles(height, width, lh, lw, tile_size, overlap):

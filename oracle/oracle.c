@@ -877,6 +877,134 @@ int zo_analysis_secondary(const zo_ckpt *ck, int op, const float *xin, int h, in
 }
 
 /* ======================================================================================= */
+/* Latent-domain networks: the hyper-decoder z_hat -> psi (hyper_decoder.rs) and the        */
+/* multi-stage context model psi, residual -> y_hat (mcm.rs)                               */
+/* ======================================================================================= */
+
+/* HyperDecoder::forward_f32 (hyper_decoder.rs:94-113, layers :24-42): conv1x1 C -> C (no bias),
+ * convT 4x4 s2 p1 C -> C (bias), crop to (out_h, out_w), ReLU6, conv3x3 C -> C (bias), ReLU6,
+ * conv3x3 C -> 4C (bias). z [c][hz][wz] -> psi [4c][out_h][out_w]. Returns -1 when the crop
+ * is larger than the upsampled map. */
+int zo_hyper_decode(const zo_ckpt *ck, const float *z, int c, int hz, int wz, int out_h,
+                    int out_w, float *psi) {
+    if (c <= 0 || hz <= 0 || wz <= 0 || out_h <= 0 || out_w <= 0 || out_h > 2 * hz ||
+        out_w > 2 * wz)
+        return -1;
+    T x = {c, hz, wz, (float *)z};
+    T t = conv1x1(ck, "hyper_decoder.conv1", &x, c, 0);
+    t_move(&t, convt(ck, "hyper_decoder.conv2", &t, c, 4, 2, 1, 0));
+    if (t.h != out_h || t.w != out_w) t_move(&t, crop(&t, out_h, out_w));
+    zo_relu6(t.d, t_len(&t));
+    t_move(&t, conv3x3(ck, "hyper_decoder.conv3", &t, c, 1, 1));
+    zo_relu6(t.d, t_len(&t));
+    t_move(&t, conv3x3(ck, "hyper_decoder.conv4", &t, 4 * c, 1, 1));
+    dump("hyper.psi", &t);
+    memcpy(psi, t.d, sizeof(float) * t_len(&t));
+    t_free(&t);
+    return 0;
+}
+
+/* (row, column) of each context-model stage in a 2 x 2 cell (mcm.rs:25 STAGE_POSITIONS) */
+static const int MCM_PY[4] = {0, 1, 0, 1}, MCM_PX[4] = {0, 1, 1, 0};
+
+static T cat2(const T *a, const T *b) {
+    if (a->h != b->h || a->w != b->w) ZO_FAIL("cat: extent mismatch");
+    T o = t_new(a->c + b->c, a->h, a->w);
+    memcpy(o.d, a->d, sizeof(float) * t_len(a));
+    memcpy(o.d + t_len(a), b->d, sizeof(float) * t_len(b));
+    return o;
+}
+
+/* FusionPredNet::forward (mcm.rs:59-65): three bias-free 1x1 convs, ReLU between them. */
+static T fusion_pred(const zo_ckpt *ck, const char *prefix, const T *x, int c) {
+    char n1[160], n2[160], n3[160];
+    snprintf(n1, sizeof n1, "%s.conv1", prefix);
+    snprintf(n2, sizeof n2, "%s.conv2", prefix);
+    snprintf(n3, sizeof n3, "%s.conv3", prefix);
+    T t = conv1x1(ck, n1, x, c, 0);
+    zo_relu(t.d, t_len(&t));
+    t_move(&t, conv1x1(ck, n2, &t, c, 0));
+    zo_relu(t.d, t_len(&t));
+    t_move(&t, conv1x1(ck, n3, &t, c, 0));
+    return t;
+}
+
+/* The latent from psi and the dequantised residual (reconstruct.rs:200-212): with a context
+ * model in the checkpoint (present iff "context.MCM.0.fusion_pred_net.conv1.weight" is,
+ * common.rs:111-115), ContextModel::decompress (mcm.rs:161-257); without one,
+ * upshuffle_psi (mcm.rs:742-760, stage of (y % 2, x % 2) from STAGE_LUT) plus the residual.
+ * residual, y [c][h][w]; psi [4c][ceil(h/2)][ceil(w/2)]. Returns -1 on a shape the crate
+ * rejects (a context model needs c a multiple of 32, mcm.rs:123-127). */
+int zo_context_decompress(const zo_ckpt *ck, int c, const float *residual, int h, int w,
+                          const float *psi, float *y) {
+    if (c <= 0 || h <= 0 || w <= 0) return -1;
+    const int hh = cdiv(h, 2), hw = cdiv(w, 2);
+    const size_t qplane = (size_t)hh * hw, plane = (size_t)h * w;
+    if (!find(ck, "context.MCM.0.fusion_pred_net.conv1.weight")) {
+        static const int LUT[4] = {0, 2, 3, 1};
+        for (int ch = 0; ch < c; ch++)
+            for (int yy = 0; yy < h; yy++)
+                for (int xx = 0; xx < w; xx++) {
+                    const int s = LUT[(yy % 2) * 2 + xx % 2];
+                    const float m = psi[((size_t)s * c + ch) * qplane + (size_t)(yy / 2) * hw +
+                                        xx / 2];
+                    const size_t i = ch * plane + (size_t)yy * w + xx;
+                    y[i] = m + residual[i];
+                }
+        return 0;
+    }
+    if (c % 32) return -1;
+    memset(y, 0, sizeof(float) * c * plane);
+    T ctx = {0, hh, hw, NULL};
+    for (int s = 0; s < 4; s++) {
+        T psi_s = t_new(c, hh, hw);
+        memcpy(psi_s.d, psi + (size_t)s * c * qplane, sizeof(float) * c * qplane);
+        char pre[96], name[128];
+        snprintf(pre, sizeof pre, "context.MCM.%d", s);
+        T mean;
+        if (s == 0) {
+            snprintf(name, sizeof name, "%s.fusion_pred_net", pre);
+            mean = fusion_pred(ck, name, &psi_s, c);
+        } else {
+            snprintf(name, sizeof name, "%s.conv.0", pre);
+            T t = conv1x1(ck, name, &ctx, c, 0);
+            snprintf(name, sizeof name, "%s.conv.1", pre);
+            t_move(&t, conv3x3(ck, name, &t, c, c / 32, 1));
+            T joined = cat2(&t, &psi_s);
+            t_free(&t);
+            snprintf(name, sizeof name, "%s.fusion_pred_net", pre);
+            mean = fusion_pred(ck, name, &joined, c);
+            t_free(&joined);
+        }
+        t_free(&psi_s);
+        /* stage = mean + residual at (2y + py, 2x + px); padded positions keep the mean */
+        const int py = MCM_PY[s], px = MCM_PX[s];
+        for (int ch = 0; ch < c; ch++)
+            for (int yy = 0; yy < hh; yy++) {
+                const int sy = 2 * yy + py;
+                if (sy >= h) continue;
+                for (int xx = 0; xx < hw; xx++) {
+                    const int sx = 2 * xx + px;
+                    if (sx >= w) continue;
+                    float *m = mean.d + ch * qplane + (size_t)yy * hw + xx;
+                    const size_t i = ch * plane + (size_t)sy * w + sx;
+                    *m = *m + residual[i];
+                    y[i] = *m;
+                }
+            }
+        if (s == 0)
+            ctx = mean;
+        else {
+            T nc = cat2(&ctx, &mean);
+            t_free(&mean);
+            t_move(&ctx, nc);
+        }
+    }
+    t_free(&ctx);
+    return 0;
+}
+
+/* ======================================================================================= */
 /* Tiling (tiles.rs:39-119, 220-229) and whole-picture synthesis (reconstruct.rs:274-464)   */
 /* ======================================================================================= */
 

@@ -185,6 +185,15 @@ typedef struct {
  * malformed geometry); writes at most max_tiles. */
 int zo_analysis_tiles(int ccs, int h, int w, int lh, int lw, zo_atile *tiles, int max_tiles);
 
+/* HyperDecoder::forward_f32 (hyper_decoder.rs:94-113): z [c][hz][wz] -> psi
+ * [4c][out_h][out_w]. -1 when (out_h, out_w) exceeds the upsampled map. */
+int zo_hyper_decode(const zo_ckpt *ck, const float *z, int c, int hz, int wz, int out_h,
+                    int out_w, float *psi);
+/* reconstruct.rs:200-212: ContextModel::decompress (mcm.rs:161-257) when the checkpoint holds
+ * a context model, else upshuffle_psi (mcm.rs:742-760) + residual. residual, y [c][h][w],
+ * psi [4c][ceil(h/2)][ceil(w/2)]. */
+int zo_context_decompress(const zo_ckpt *ck, int c, const float *residual, int h, int w,
+                          const float *psi, float *y);
 /* The encoder's tiled analysis transform of component ccs: plane x [1 or 12][h][w] -> latent
  * [160 or 96][ceil(h / d)][ceil(w / d)] (d = 16 or 8), each tile analysed on its own and its
  * latent core kept (encoder/mod.rs:1128-1170). */

@@ -219,6 +219,27 @@ def analysis_spec(op, secondary):
     return s
 
 
+def latent_spec(chs, context):
+    """`HyperDecoder::load` (hyper_decoder.rs:24-42) and, with `context`, `ContextModel::load`
+    (mcm.rs:119-156) for `chs` latent channels."""
+    s = []
+    _conv(s, "hyper_decoder.conv1", chs, chs, 1, 1, bias=False)
+    _convt(s, "hyper_decoder.conv2", chs, chs, 4, gain=HE)
+    _conv(s, "hyper_decoder.conv3", chs, chs, 3, 3, gain=HE)
+    _conv(s, "hyper_decoder.conv4", chs, 4 * chs, 3, 3)
+    if context:
+        for st in range(4):
+            p = "context.MCM.%d" % st
+            if st:
+                _conv(s, p + ".conv.0", st * chs, chs, 1, 1, bias=False)
+                _conv(s, p + ".conv.1", chs, chs, 3, 3, groups=chs // 32)
+            f = p + ".fusion_pred_net"
+            _conv(s, f + ".conv1", 2 * chs if st else chs, chs, 1, 1, bias=False, gain=HE)
+            _conv(s, f + ".conv2", chs, chs, 1, 1, bias=False, gain=HE)
+            _conv(s, f + ".conv3", chs, chs, 1, 1, bias=False)
+    return s
+
+
 def make_params(spec, seed, tag=""):
     """Normal weights (std sqrt(1 / effective fan_in), see the gains above), N(0, 0.01^2)
     biases, LN weight 1 + N(0, 0.1^2) and bias N(0, 0.05^2), temperature U(0.5, 2)."""
@@ -268,6 +289,11 @@ def synthesis_params(op, seed):
 def analysis_params(op, seed):
     return (make_params(analysis_spec(op, False), seed, "AY/"),
             make_params(analysis_spec(op, True), seed, "AUV/"))
+
+
+def latent_params(seed, chs=160, context=True):
+    """A component's latent networks (hyper-decoder, optional context model)."""
+    return make_params(latent_spec(chs, context), seed, "L%d/" % chs)
 
 
 def conv_layer_params(seed=0):

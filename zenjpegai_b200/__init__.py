@@ -12,6 +12,9 @@ Python host side over the C ABI of `include/zjai.h` (library `libzjai.so`, built
   `forward(...)`.
 * `synthesize` / `synthesis_tiles` — src/decoder/reconstruct.rs:274-464 and
   src/tools/tiles.rs:39-119.
+* `LatentModel` — the float networks of src/model/common.rs `CommonModel`: the hyper-decoder
+  (hyper_decoder.rs) and the optional context model (mcm.rs), with reconstruct.rs:107-230's
+  one-region latent reconstruction.
 
 Arrays are numpy float32 (host memory) or torch CUDA float32 tensors (device memory of the
 engine's GPU). Errors raise `ZjaiError` whose `.status` mirrors the crate's `Error` variant.
@@ -24,10 +27,11 @@ import numpy as np
 
 from . import _lib
 from ._lib import (ACT_LEAKY, ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SIGMOID, ANA_UV, ANA_Y, BOP,
-                   HOP, SOP, SYN_UV, SYN_Y, ZjaiError, check)
+                   HOP, LATENT, SOP, SYN_UV, SYN_Y, ZjaiError, check)
 
 __all__ = ["Engine", "ZjaiError", "SOP", "BOP", "HOP", "SYN_Y", "SYN_UV", "ANA_Y", "ANA_UV",
            "ACT_NONE", "ACT_RELU", "ACT_LEAKY", "ACT_SIGMOID", "ACT_RELU6", "Network", "Stage",
+           "LatentModel", "LATENT",
            "synthesis_tiles", "synth_out_size", "version"]
 
 _lib.lib()  # load now: importing the package without its CUDA library is an error
@@ -279,3 +283,57 @@ class Stage(Network):
             raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
         check(_lib.lib().zjai_stage_forward(self.handle, px, c, h, w, po, mem))
         return out
+
+
+class LatentModel(Network):
+    """The latent-domain float networks of one component (`CommonModel`, common.rs:34-131):
+    `HyperDecoder` and, when `params` hold "context.MCM.*", the `ContextModel`. C is the
+    checkpoint's channel count (160 luma, 96 chroma)."""
+
+    def __init__(self, engine, params):
+        super().__init__(engine, LATENT, 0, params)
+        self.chs = int(params["hyper_decoder.conv1.weight"].shape[0])
+        self.has_context = "context.MCM.0.fusion_pred_net.conv1.weight" in params
+
+    def hyper_decode(self, z_hat, out_h, out_w, out=None):
+        """`HyperDecoder::forward_f32` (hyper_decoder.rs:94-113): z_hat [C, hz, wz] -> psi
+        [4C, out_h, out_w]."""
+        c, hz, wz = z_hat.shape
+        shape = (4 * self.chs, out_h, out_w)
+        if out is None:
+            out = _like(z_hat, shape)
+        pz, mem = _arg(z_hat, (self.chs, hz, wz))
+        po, m2 = _arg(out, shape)
+        if mem != m2:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        check(_lib.lib().zjai_hyper_decode(self.handle, pz, hz, wz, out_h, out_w, po, mem))
+        return out
+
+    def decompress(self, residual, psi, out=None):
+        """y_hat [C, h, w] from the residual [C, h, w] and psi [4C, ceil(h/2), ceil(w/2)]
+        (reconstruct.rs:200-212: the context model, or upshuffle_psi + residual)."""
+        c, h, w = residual.shape
+        if out is None:
+            out = _like(residual, (c, h, w))
+        pr, mem = _arg(residual, (self.chs, h, w))
+        pp, m2 = _arg(psi, (4 * self.chs, -(-h // 2), -(-w // 2)))
+        po, m3 = _arg(out, (self.chs, h, w))
+        if len({mem, m2, m3}) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        check(_lib.lib().zjai_context_decompress(self.handle, pr, h, w, pp, po, mem))
+        return out
+
+    def reconstruct(self, z_hat, residual, with_psi=False):
+        """One region of `reconstruct_latent` (reconstruct.rs:107-230): (y_hat, psi or None)."""
+        c, hz, wz = z_hat.shape
+        _, h, w = residual.shape
+        y = _like(residual, (self.chs, h, w))
+        psi = _like(residual, (4 * self.chs, -(-h // 2), -(-w // 2))) if with_psi else None
+        pz, mem = _arg(z_hat, (self.chs, hz, wz))
+        pr, m2 = _arg(residual, (self.chs, h, w))
+        py, m3 = _arg(y)
+        pp = _arg(psi)[0] if with_psi else None
+        if len({mem, m2, m3}) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        check(_lib.lib().zjai_reconstruct_latent(self.handle, pz, hz, wz, pr, h, w, pp, py, mem))
+        return y, psi

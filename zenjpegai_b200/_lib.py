@@ -19,6 +19,7 @@ STATUS_NAMES = ["OK", "INVALID_ARGUMENT", "UNSUPPORTED", "LIMIT_EXCEEDED", "CANC
 MEM_HOST, MEM_DEVICE = 0, 1
 SOP, BOP, HOP = 0, 1, 2
 SYN_Y, SYN_UV, ANA_Y, ANA_UV = 0, 1, 2, 3
+LATENT = 5
 ACT_NONE, ACT_RELU, ACT_LEAKY, ACT_SIGMOID, ACT_RELU6 = range(5)
 
 
@@ -97,6 +98,9 @@ def lib():
     L.zjai_stage_create.argtypes = [_vp, _i, _i, _i, ctypes.POINTER(Param), _i,
                                      ctypes.POINTER(_vp)]
     L.zjai_stage_forward.argtypes = [_vp, _vp, _i, _i, _i, _vp, _i]
+    L.zjai_hyper_decode.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _i]
+    L.zjai_context_decompress.argtypes = [_vp, _vp, _i, _i, _vp, _vp, _i]
+    L.zjai_reconstruct_latent.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _vp, _i]
     L.zjai_synthesis_tiles.argtypes = [_i] * 6 + [ctypes.POINTER(Tile), _i, ctypes.POINTER(_i)]
     L.zjai_synthesize.argtypes = [_vp, _vp, _vp, _vp, _vp] + [_i] * 10 + [_vp, _vp, _vp, _i, _vp]
     L.zjai_synthesize_q.argtypes = [_vp, _vp, _vp, _vp, _vp] + [_i] * 11 + [_vp, _vp, _vp, _i,

@@ -156,6 +156,91 @@ __global__ void copy_core_kernel(const float* __restrict__ tile, int n_img, int 
   full[(r * LH + cy + y) * LW + cx + x] = tile[(r * th + oy + y) * tw + ox + x];
 }
 
+// Context model (mcm.rs:161-257) layout kernels. The half-resolution maps of one picture are
+// hh x hw pixels; tiles of 32 pixels x 32 channels go through shared memory so that the planar
+// f32 side is read / written along rows and the NHWC f16 side along channels.
+constexpr int kLatTile = 32;
+
+// psi planar f32 [4C][hh][hw] -> the joined buffer J (NHWC f16, 8C channels a pixel): channel k
+// of quarter s = k / C lands at channel k + (s + 1) C, i.e. beside the slot [2sC, 2sC + C) the
+// stage's context branch writes, so that J channels [2sC, 2sC + 2C) are cat(t_s, psi_s).
+// Grid (ceil(hh*hw / 32), 4C / 32); C a multiple of 32.
+__global__ void psi_to_joined_kernel(const float* __restrict__ psi, int C, int npix,
+                                     __half* __restrict__ J, int hw, long long pix, long long row) {
+  __shared__ float t[kLatTile][kLatTile + 1];
+  const int p0 = blockIdx.x * kLatTile, k0 = blockIdx.y * kLatTile;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 256 threads: 8 rows of 32
+  for (int r = ty; r < kLatTile; r += 8) {
+    const int p = p0 + tx;
+    t[r][tx] = p < npix ? __ldg(psi + (long long)(k0 + r) * npix + p) : 0.f;
+  }
+  __syncthreads();
+  const int kd = k0 + (k0 / C + 1) * C;  // the 32-channel block never straddles a quarter
+  for (int i = threadIdx.x; i < kLatTile * 16; i += 256) {
+    const int pp = i >> 4, pair = i & 15, p = p0 + pp;
+    if (p >= npix) continue;
+    const int y = p / hw, x = p - y * hw;
+    *reinterpret_cast<__half2*>(J + y * row + x * pix + kd + 2 * pair) =
+        __floats2half2_rn(t[2 * pair][pp], t[2 * pair + 1][pp]);
+  }
+}
+
+// One context-model stage's output (mcm.rs:208-247): stage = mean + residual at latent
+// position (2y + py, 2x + px) (a position past an odd edge keeps the mean: the reference's
+// zero padding), y_hat at that position = stage, and, when ctx is given, the stage as NHWC
+// f16 into the context buffer (channels [0, C) of the view). mean planar f32 [C][hh][hw],
+// residual / y_hat planar f32 [C][h][w]. Grid (ceil(hh*hw / 32), C / 32).
+__global__ void mcm_stage_kernel(const float* __restrict__ mean, const float* __restrict__ res,
+                                 int h, int w, int hh, int hw, int py, int px,
+                                 float* __restrict__ y, __half* __restrict__ ctx, long long pix,
+                                 long long row) {
+  __shared__ float t[kLatTile][kLatTile + 1];
+  const int npix = hh * hw;
+  const int p0 = blockIdx.x * kLatTile, k0 = blockIdx.y * kLatTile;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const long long plane = (long long)h * w;
+  for (int r = ty; r < kLatTile; r += 8) {
+    const int p = p0 + tx;
+    if (p >= npix) continue;
+    const int yy = p / hw, xx = p - yy * hw;
+    const int sy = 2 * yy + py, sx = 2 * xx + px;
+    float v = __ldg(mean + (long long)(k0 + r) * npix + p);
+    if (sy < h && sx < w) {
+      const long long i = (long long)(k0 + r) * plane + (long long)sy * w + sx;
+      v = v + __ldg(res + i);
+      y[i] = v;
+    }
+    t[r][tx] = v;
+  }
+  if (!ctx) return;
+  __syncthreads();
+  for (int i = threadIdx.x; i < kLatTile * 16; i += 256) {
+    const int pp = i >> 4, pair = i & 15, p = p0 + pp;
+    if (p >= npix) continue;
+    const int yy = p / hw, xx = p - yy * hw;
+    *reinterpret_cast<__half2*>(ctx + yy * row + xx * pix + k0 + 2 * pair) =
+        __floats2half2_rn(t[2 * pair][pp], t[2 * pair + 1][pp]);
+  }
+}
+
+// Without a context model (reconstruct.rs:200-212): y = upshuffle_psi(psi) + residual, where
+// sample (Y, X) of channel c takes psi channel STAGE_LUT[(Y % 2) * 2 + X % 2] * C + c at
+// (Y / 2, X / 2) (mcm.rs:733-760). One thread per latent sample.
+__global__ void upshuffle_add_kernel(const float* __restrict__ psi, const float* __restrict__ res,
+                                     int C, int h, int w, float* __restrict__ y) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long plane = (long long)h * w;
+  if (idx >= C * plane) return;
+  const int c = (int)(idx / plane);
+  const int r = (int)(idx - (long long)c * plane);
+  const int Y = r / w, X = r - Y * w;
+  const int hh = (h + 1) / 2, hw = (w + 1) / 2;
+  const int q = (Y & 1) * 2 + (X & 1);
+  const int s = q == 0 ? 0 : q == 1 ? 2 : q == 2 ? 3 : 1;  // STAGE_LUT
+  const float m = __ldg(psi + ((long long)(s * C + c) * hh + (Y >> 1)) * hw + (X >> 1));
+  y[idx] = m + __ldg(res + idx);
+}
+
 }  // namespace
 
 void launch_replicate_pad(const TView& src, const TView& dst, cudaStream_t s) {
@@ -216,6 +301,28 @@ void launch_relu6(const TView& src, const TView& dst, cudaStream_t s) {
   relu6_kernel<<<blocks_for(total, 256), 256, 0, s>>>(src.p, dst.p, src.n, src.h, src.w, c8,
                                                       src.pix, src.row, src.img, dst.pix, dst.row,
                                                       dst.img);
+}
+
+void launch_psi_to_joined(const float* psi, int C, int hh, int hw, const TView& J, cudaStream_t s) {
+  const int npix = hh * hw;
+  dim3 grid((npix + kLatTile - 1) / kLatTile, 4 * C / kLatTile);
+  psi_to_joined_kernel<<<grid, 256, 0, s>>>(psi, C, npix, J.p, hw, J.pix, J.row);
+}
+
+void launch_mcm_stage(const float* mean, const float* res, int C, int h, int w, int py, int px,
+                      float* y, const TView* ctx, cudaStream_t s) {
+  const int hh = (h + 1) / 2, hw = (w + 1) / 2;
+  dim3 grid((hh * hw + kLatTile - 1) / kLatTile, C / kLatTile);
+  mcm_stage_kernel<<<grid, 256, 0, s>>>(mean, res, h, w, hh, hw, py, px, y,
+                                        ctx ? ctx->p : nullptr, ctx ? ctx->pix : 0,
+                                        ctx ? ctx->row : 0);
+}
+
+void launch_upshuffle_add(const float* psi, const float* res, int C, int h, int w, float* y,
+                          cudaStream_t s) {
+  const long long total = (long long)C * h * w;
+  if (total == 0) return;
+  upshuffle_add_kernel<<<blocks_for(total, 256), 256, 0, s>>>(psi, res, C, h, w, y);
 }
 
 }  // namespace zjai

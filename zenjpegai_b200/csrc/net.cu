@@ -225,6 +225,37 @@ static int load_net(Net* n, Loader& L) {
       ZJAI_TRY(L.conv("conv4", c, 160, 3, 3, 2, 1, 1, true));
       return L.conv("conv5", 160, 160, 1, 1, 1, 0, 1, false);
     }
+    case ZJAI_LATENT: {
+      // HyperDecoder::load (hyper_decoder.rs:24-42); ContextModel::load (mcm.rs:119-156) when
+      // the checkpoint holds "context.MCM.0.fusion_pred_net.conv1.weight" (common.rs:111-115).
+      // The channel count is the checkpoint's (160 luma, 96 chroma in the crate).
+      auto it = L.byname.find("hyper_decoder.conv1.weight");
+      if (it == L.byname.end() || it->second->ndim != 4)
+        return fail(ZJAI_MODEL, "hyper_decoder.conv1.weight: missing or not 4-D");
+      const int c = (int)it->second->shape[0];
+      if (c <= 0 || c % 16)
+        return fail(ZJAI_UNSUPPORTED, "latent networks: channel count must be a multiple of 16");
+      n->lat_c = c;
+      ZJAI_TRY(L.conv("hyper_decoder.conv1", c, c, 1, 1, 1, 0, 1, false));
+      ZJAI_TRY(L.convt("hyper_decoder.conv2", c, c, 4, 1, 0));
+      ZJAI_TRY(L.conv("hyper_decoder.conv3", c, c, 3, 3, 1, 1, 1, true));
+      ZJAI_TRY(L.conv("hyper_decoder.conv4", c, 4 * c, 3, 3, 1, 1, 1, true));
+      if (!L.has("context.MCM.0.fusion_pred_net.conv1.weight")) return ZJAI_OK;
+      if (c % 32) return fail(ZJAI_MODEL, "context model: channel count must be a multiple of 32");
+      for (int st = 0; st < 4; ++st) {
+        const std::string p = "context.MCM." + std::to_string(st);
+        if (st > 0) {
+          ZJAI_TRY(L.conv(p + ".conv.0", st * c, c, 1, 1, 1, 0, 1, false));
+          ZJAI_TRY(L.conv(p + ".conv.1", c, c, 3, 3, 1, 1, c / 32, true));
+        }
+        const std::string f = p + ".fusion_pred_net";  // FusionPredNet::load (mcm.rs:36-57)
+        ZJAI_TRY(L.conv(f + ".conv1", st ? 2 * c : c, c, 1, 1, 1, 0, 1, false));
+        ZJAI_TRY(L.conv(f + ".conv2", c, c, 1, 1, 1, 0, 1, false));
+        ZJAI_TRY(L.conv(f + ".conv3", c, c, 1, 1, 1, 0, 1, false));
+      }
+      n->lat_ctx = true;
+      return ZJAI_OK;
+    }
     default:
       return fail(ZJAI_INVALID_ARGUMENT, "unknown network kind");
   }
@@ -232,7 +263,9 @@ static int load_net(Net* n, Loader& L) {
 
 int load_network(Ctx* ctx, int kind, int op, const zjai_param* params, int nparams, Net** out) {
   *out = nullptr;
-  if (op < ZJAI_SOP || op > ZJAI_HOP) return fail(ZJAI_INVALID_ARGUMENT, "unknown operating point");
+  // the latent networks are the same for every operating point
+  if (kind != ZJAI_LATENT && (op < ZJAI_SOP || op > ZJAI_HOP))
+    return fail(ZJAI_INVALID_ARGUMENT, "unknown operating point");
   if (nparams < 0 || (nparams > 0 && !params)) return fail(ZJAI_INVALID_ARGUMENT, "params");
   Net* n = new Net();
   n->ctx = ctx;
@@ -322,6 +355,8 @@ const ConvLayer* Runner::layer(const std::string& name) {
 // Profile tag prefix: network kind and batch size ("Y28:" = luma, 28 tiles).
 std::string Runner::kind_tag() const {
   static const char* k[] = {"Y", "UV", "AY", "AUV"};
+  if (net->kind == ZJAI_LATENT) return "L" + std::to_string(net->lat_c) + ":";
+  if (net->kind == kStageKind) return "S" + std::to_string(n) + ":";
   return std::string(k[net->kind & 3]) + std::to_string(n) + ":";
 }
 
@@ -883,6 +918,111 @@ int Runner::stage(const TView& x, float* out) {
   launch_nhwc_to_planar(y, out, stream);
   ctx->launches++;
   return cuda_check(cudaGetLastError(), "nhwc_to_planar");
+}
+
+// HyperDecoder::forward_f32 (hyper_decoder.rs:94-113): conv1 1x1 -> convT 4x4 s2, its output
+// cropped to (out_h, out_w) with ReLU6 in the epilogue -> conv3 3x3 + ReLU6 -> conv4 3x3 into
+// planar f32 psi.
+int Runner::hyper(const TView& z, int out_h, int out_w, float* psi) {
+  const int c = net->lat_c;
+  int nh, nw;
+  ZJAI_TRY(out_extent("hyper_decoder.conv2", z.h, z.w, &nh, &nw));
+  if (out_h <= 0 || out_w <= 0 || out_h > nh || out_w > nw)
+    return fail(ZJAI_INVALID_ARGUMENT, "hyper-decoder: crop larger than the upsampled map");
+  TView x1, x2, x3;
+  ZJAI_TRY(alloc(z.h, z.w, c, &x1));
+  {
+    ConvOut o;
+    o.out = x1;
+    ZJAI_TRY(conv("hyper_decoder.conv1", z, o));
+  }
+  ZJAI_TRY(alloc(out_h, out_w, c, &x2));
+  {
+    ConvOut o;
+    o.out = x2;
+    o.act1 = ACT_RELU6;
+    ZJAI_TRY(conv("hyper_decoder.conv2", x1, o));
+  }
+  ZJAI_TRY(stop_check());
+  ZJAI_TRY(alloc(out_h, out_w, c, &x3));
+  {
+    ConvOut o;
+    o.out = x3;
+    o.act1 = ACT_RELU6;
+    ZJAI_TRY(conv("hyper_decoder.conv3", x2, o));
+  }
+  ZJAI_TRY(stop_check());
+  ConvOut o;
+  o.planar = true;
+  o.pout = psi;
+  o.p_plane = (long long)out_h * out_w;
+  o.p_row = out_w;
+  o.p_img = 4LL * c * out_h * out_w;
+  return conv("hyper_decoder.conv4", x3, o);
+}
+
+// The latent from psi and the residual (reconstruct.rs:200-212). With the context model,
+// ContextModel::decompress (mcm.rs:161-257) on NHWC f16 maps at half resolution:
+//   J   [hh][hw][8C]: stage s's fusion input cat(t_s, psi_s) at channels [2sC, 2sC + 2C)
+//                     (psi_s copied in once, t_s written by the stage's grouped conv);
+//   ctx [hh][hw][3C]: the reconstructed stages 0..2 (the spatial context), stage s at sC;
+// stage s: conv.0 1x1 (sC -> C) on ctx[0, sC) -> conv.1 3x3 grouped into J -> FusionPredNet
+// (1x1, ReLU, 1x1, ReLU, 1x1) with the mean as planar f32 -> mcm_stage (mean + residual into
+// y_hat and ctx).
+int Runner::latent(const float* psi, const float* res, int h, int w, float* y) {
+  const int c = net->lat_c;
+  if (!net->lat_ctx) {
+    mem_kernel("upshuffle", "add", (double)c * h * w * 12.0, 1,
+               [&] { launch_upshuffle_add(psi, res, c, h, w, y, stream); });
+    return cuda_check(cudaGetLastError(), "upshuffle_psi");
+  }
+  const int hh = cdiv(h, 2), hw = cdiv(w, 2);
+  const double q = (double)c * hh * hw;
+  TView J, cx, t0, f1, f2;
+  ZJAI_TRY(alloc(hh, hw, 8 * c, &J));
+  ZJAI_TRY(alloc(hh, hw, 3 * c, &cx));
+  ZJAI_TRY(alloc(hh, hw, c, &t0));
+  ZJAI_TRY(alloc(hh, hw, c, &f1));
+  ZJAI_TRY(alloc(hh, hw, c, &f2));
+  float* mean = static_cast<float*>(arena->alloc((size_t)c * hh * hw * sizeof(float)));
+  if (!mean) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (context model)");
+  mem_kernel("psi", "joined", q * 4 * 6.0, 1,
+             [&] { launch_psi_to_joined(psi, c, hh, hw, J, stream); });
+  static const int PY[4] = {0, 1, 0, 1}, PX[4] = {0, 1, 1, 0};  // mcm.rs:25
+  for (int st = 0; st < 4; ++st) {
+    ZJAI_TRY(stop_check());
+    const std::string p = "context.MCM." + std::to_string(st);
+    TView fin = J.channels(c, c);
+    if (st > 0) {
+      ConvOut o0;
+      o0.out = t0;
+      ZJAI_TRY(conv(p + ".conv.0", cx.channels(0, st * c), o0));
+      ConvOut o1;
+      o1.out = J.channels(2 * st * c, c);
+      ZJAI_TRY(conv(p + ".conv.1", t0, o1));
+      fin = J.channels(2 * st * c, 2 * c);
+    }
+    ConvOut a1;
+    a1.out = f1;
+    a1.act1 = ACT_RELU;
+    ZJAI_TRY(conv(p + ".fusion_pred_net.conv1", fin, a1));
+    ConvOut a2;
+    a2.out = f2;
+    a2.act1 = ACT_RELU;
+    ZJAI_TRY(conv(p + ".fusion_pred_net.conv2", f1, a2));
+    ConvOut a3;
+    a3.planar = true;
+    a3.pout = mean;
+    a3.p_plane = (long long)hh * hw;
+    a3.p_row = hw;
+    a3.p_img = (long long)c * hh * hw;
+    ZJAI_TRY(conv(p + ".fusion_pred_net.conv3", f2, a3));
+    const TView cs = cx.channels(st * c, c);
+    mem_kernel("stage" + std::to_string(st), "mcm", q * (st < 3 ? 14.0 : 12.0), 1, [&] {
+      launch_mcm_stage(mean, res, c, h, w, PY[st], PX[st], y, st < 3 ? &cs : nullptr, stream);
+    });
+  }
+  return cuda_check(cudaGetLastError(), "context model");
 }
 
 // ---------------------------------------------------------------------------------------------

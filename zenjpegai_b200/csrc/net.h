@@ -24,6 +24,10 @@ struct Net {
   // conv stage (zjai_stage_create): activation of the first conv, its pixel shuffle, the
   // activation inside the residual blocks, their number, input and output channels
   int st_act = 0, st_shuffle = 1, st_res_act = 0, st_nres = 0, st_cin = 0, st_cout = 0;
+  // latent networks (ZJAI_LATENT): latent channel count, and whether the checkpoint holds the
+  // context model
+  int lat_c = 0;
+  bool lat_ctx = false;
   ~Net();
 };
 
@@ -91,6 +95,11 @@ struct Runner {
   int analysis(const TView& x, int h, int w, float* out);
   // conv stage: x (NHWC, st_cin channels) -> planar f32 out [st_cout][h * r][w * r]
   int stage(const TView& x, float* out);
+  // hyper-decoder: z (NHWC, lat_c channels) -> psi planar f32 [4 lat_c][out_h][out_w]
+  int hyper(const TView& z, int out_h, int out_w, float* psi);
+  // latent from psi planar f32 [4C][ceil(h/2)][ceil(w/2)] and the residual planar f32
+  // [C][h][w] -> y planar f32 [C][h][w] (context model, or upshuffle_psi + residual)
+  int latent(const float* psi, const float* res, int h, int w, float* y);
 };
 
 struct ArenaMark {
@@ -120,6 +129,14 @@ void launch_preprocess_rgb(const uint8_t* rgb, int n, int h, int w, float* luma,
 // RGB (uint8 for 8 bits, else uint16), on stream s
 int output_yuv_to_rgb(Ctx* ctx, const float* y, const float* u, const float* v, int h, int w,
                       int ch, int cw, int bit_depth, void* rgb, cudaStream_t s);
+// context-model layout kernels (kernels_misc.cu): psi quarters into the joined buffer J
+// (channel k of quarter s at k + (s + 1) C), one stage's residual add / y_hat scatter / context
+// write, and upshuffle_psi + residual
+void launch_psi_to_joined(const float* psi, int C, int hh, int hw, const TView& J, cudaStream_t s);
+void launch_mcm_stage(const float* mean, const float* res, int C, int h, int w, int py, int px,
+                      float* y, const TView* ctx, cudaStream_t s);
+void launch_upshuffle_add(const float* psi, const float* res, int C, int h, int w, float* y,
+                          cudaStream_t s);
 void launch_copy_core(const float* tile, int n, int C, int th, int tw, int oy, int ox, int core_h,
                       int core_w, float* full, int LH, int LW, int cy, int cx, cudaStream_t s);
 

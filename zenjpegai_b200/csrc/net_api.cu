@@ -276,7 +276,8 @@ int zjai_net_create(zjai_ctx* ctx, int kind, int op, const zjai_param* params, i
   if (!out) return fail(ZJAI_INVALID_ARGUMENT, "null output handle");
   *out = nullptr;
   ZJAI_TRY(ctx_enter(ctx));
-  if (kind < ZJAI_SYN_Y || kind > ZJAI_ANA_UV) return fail(ZJAI_INVALID_ARGUMENT, "unknown network kind");
+  if ((kind < ZJAI_SYN_Y || kind > ZJAI_ANA_UV) && kind != ZJAI_LATENT)
+    return fail(ZJAI_INVALID_ARGUMENT, "unknown network kind");
   Net* n = nullptr;
   ZJAI_TRY(load_network(ctx, kind, op, params, nparams, &n));
   // the C handle is the same object
@@ -530,6 +531,95 @@ int zjai_stage_forward(zjai_net* net, const float* x, int c, int h, int w, float
   int st = r.stage(t, dout);
   if (st != ZJAI_OK) return settle(ctx, st);
   ZJAI_TRY(stage_out_finish(ctx, out, dout, nout, mem));
+  return finish_call(ctx, mem);
+}
+
+// ---- latent-domain networks -----------------------------------------------------------------
+
+static int latent_net(zjai_net* net, Net** out) {
+  ZJAI_TRY(net_enter(net));
+  Net* n = reinterpret_cast<Net*>(net);
+  if (n->kind != ZJAI_LATENT) return fail(ZJAI_INVALID_ARGUMENT, "not a latent network");
+  *out = n;
+  return ZJAI_OK;
+}
+
+int zjai_hyper_decode(zjai_net* net, const float* z_hat, int hz, int wz, int out_h, int out_w,
+                      float* psi, int mem) {
+  Net* n;
+  ZJAI_TRY(latent_net(net, &n));
+  Ctx* ctx = n->ctx;
+  if (!z_hat || !psi || hz <= 0 || wz <= 0 || out_h <= 0 || out_w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "hyper_decode: bad arguments");
+  const int c = n->lat_c;
+  ArenaScope scope(ctx);
+  const float* dz;
+  ZJAI_TRY(stage_in(ctx, z_hat, (size_t)c * hz * wz, mem, &dz));
+  TView t;
+  ZJAI_TRY(planar_to_tensor(ctx, dz, c, hz, wz, &t));
+  const size_t npsi = (size_t)4 * c * out_h * out_w;
+  float* dpsi;
+  ZJAI_TRY(stage_out_alloc(ctx, psi, npsi, mem, &dpsi));
+  Runner r = make_runner(ctx, n, &ctx->arena, ctx->stream, 1, nullptr);
+  const int st = r.hyper(t, out_h, out_w, dpsi);
+  if (st != ZJAI_OK) return settle(ctx, st);
+  ZJAI_TRY(stage_out_finish(ctx, psi, dpsi, npsi, mem));
+  return finish_call(ctx, mem);
+}
+
+int zjai_context_decompress(zjai_net* net, const float* residual, int h, int w, const float* psi,
+                            float* y_hat, int mem) {
+  Net* n;
+  ZJAI_TRY(latent_net(net, &n));
+  Ctx* ctx = n->ctx;
+  if (!residual || !psi || !y_hat || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "context_decompress: bad arguments");
+  const int c = n->lat_c;
+  ArenaScope scope(ctx);
+  const size_t ny = (size_t)c * h * w, npsi = (size_t)4 * c * cdiv(h, 2) * cdiv(w, 2);
+  const float *dres, *dpsi;
+  ZJAI_TRY(stage_in(ctx, residual, ny, mem, &dres));
+  ZJAI_TRY(stage_in(ctx, psi, npsi, mem, &dpsi));
+  float* dy;
+  ZJAI_TRY(stage_out_alloc(ctx, y_hat, ny, mem, &dy));
+  Runner r = make_runner(ctx, n, &ctx->arena, ctx->stream, 1, nullptr);
+  const int st = r.latent(dpsi, dres, h, w, dy);
+  if (st != ZJAI_OK) return settle(ctx, st);
+  ZJAI_TRY(stage_out_finish(ctx, y_hat, dy, ny, mem));
+  return finish_call(ctx, mem);
+}
+
+int zjai_reconstruct_latent(zjai_net* net, const float* z_hat, int hz, int wz,
+                            const float* residual, int h, int w, float* psi, float* y_hat,
+                            int mem) {
+  Net* n;
+  ZJAI_TRY(latent_net(net, &n));
+  Ctx* ctx = n->ctx;
+  if (!z_hat || !residual || !y_hat || hz <= 0 || wz <= 0 || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "reconstruct_latent: bad arguments");
+  const int c = n->lat_c, hh = cdiv(h, 2), hw = cdiv(w, 2);
+  ArenaScope scope(ctx);
+  const size_t ny = (size_t)c * h * w, npsi = (size_t)4 * c * hh * hw;
+  const float *dz, *dres;
+  ZJAI_TRY(stage_in(ctx, z_hat, (size_t)c * hz * wz, mem, &dz));
+  ZJAI_TRY(stage_in(ctx, residual, ny, mem, &dres));
+  TView t;
+  ZJAI_TRY(planar_to_tensor(ctx, dz, c, hz, wz, &t));
+  float* dpsi = nullptr;
+  if (psi) {
+    ZJAI_TRY(stage_out_alloc(ctx, psi, npsi, mem, &dpsi));
+  } else {
+    dpsi = static_cast<float*>(ctx->arena.alloc(npsi * sizeof(float)));
+    if (!dpsi) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (psi)");
+  }
+  float* dy;
+  ZJAI_TRY(stage_out_alloc(ctx, y_hat, ny, mem, &dy));
+  Runner r = make_runner(ctx, n, &ctx->arena, ctx->stream, 1, nullptr);
+  int st = r.hyper(t, hh, hw, dpsi);
+  if (st == ZJAI_OK) st = r.latent(dpsi, dres, h, w, dy);
+  if (st != ZJAI_OK) return settle(ctx, st);
+  if (psi) ZJAI_TRY(stage_out_finish(ctx, psi, dpsi, npsi, mem));
+  ZJAI_TRY(stage_out_finish(ctx, y_hat, dy, ny, mem));
   return finish_call(ctx, mem);
 }
 
