@@ -99,6 +99,15 @@ int zjai_ctx_sync(zjai_ctx *ctx);
  * callers that prefer to fail fast, and the way the timeout path is exercised in tests. */
 int zjai_ctx_set_wait_limit(zjai_ctx *ctx, int64_t cycles);
 
+/* Capture a named intermediate map of the networks this context runs (a debugging and
+ * per-stage parity facility; the reference has no counterpart, its Python oracle dumps the
+ * same names): every later network run that reaches the point `name` writes the map there
+ * as planar f32 [n][c][h][w] into `dst` (device memory of the context's GPU, `capacity`
+ * floats; a larger map fails the call with ZJAI_LIMIT_EXCEEDED). Points: "ana.act1",
+ * "ana.act2", "ana.act3" (the analysis trunk's ResAu outputs, analysis.rs:157-206). A tiled
+ * call writes each tile in turn (the last one stays). dst = NULL removes the capture. */
+int zjai_ctx_set_probe(zjai_ctx *ctx, const char *name, float *dst, int64_t capacity);
+
 /* Diagnostics: with clamp = 0 the f32 planes of zjai_synthesis_primary / _secondary /
  * zjai_synthesize* are the denormalised x * 128 + 127.5 without the [0, 255] clamp of
  * `denormalize` (synthesis.rs:188-192), so tests can compare the networks' values where the

@@ -93,6 +93,7 @@ def _declare(L):
                                          _i, _i, _f]
     L.zo_analysis_primary.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f]
     L.zo_analysis_secondary.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f]
+    L.zo_analysis_stage.argtypes = [ctypes.POINTER(Ckpt), _i, _i, _i, _f, _i, _i, _i, _f]
     L.zo_hyper_decode.argtypes = [ctypes.POINTER(Ckpt), _f, _i, _i, _i, _i, _i, _f]
     L.zo_context_decompress.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f, _f]
     L.zo_synthesis_tiles.argtypes = [_i] * 6 + [ctypes.POINTER(Tile), _i]
@@ -323,6 +324,19 @@ def analysis_primary(ck, op, x):
     out = np.empty((160, -(-h // 16), -(-w // 16)), np.float32)
     if lib().zo_analysis_primary(ctypes.byref(ck.ck), op, _fp(x), h, w, _fp(out)):
         raise ValueError("analysis_primary")
+    return out
+
+
+def analysis_stage(ck, op, secondary, stage, x, h, w):
+    """Analysis stage `stage` (1..4) of an h x w picture on its input x (the picture for stage
+    1, else the previous stage's 128-channel map): act1, act2, act3 or the latent."""
+    x = _c32(x)
+    d = {1: 2, 2: 4, 3: 8}.get(stage, 16 if not secondary else 8)
+    cout = 128 if stage < 4 else (96 if secondary else 160)
+    out = np.empty((cout, -(-h // d), -(-w // d)), np.float32)
+    if lib().zo_analysis_stage(ctypes.byref(ck.ck), op, int(bool(secondary)), stage, _fp(x),
+                               x.shape[0], h, w, _fp(out)):
+        raise ValueError("analysis_stage")
     return out
 
 

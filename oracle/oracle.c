@@ -850,6 +850,53 @@ static T trunk(const zo_ckpt *ck, int op, const T *xin, int tam_ds) {
     return x;
 }
 
+/* One stage of the analysis transform of an h x w picture, from that stage's input (the
+ * per-stage parity check: the engine's stage output is compared with this stage run on the
+ * engine's own input). Stage 1: picture [1 or 12][h][w] in [0, 255] -> act1 (normalize, pad,
+ * conv1 s2, ResAu act1); stage 2: act1 -> act2 (pad, HOP TAM, conv2 s2, ResAu act2); stage 3:
+ * act2 -> act3 (pad, HOP CAB, conv3 s2, ResAu act3); stage 4: act3 -> the latent (primary:
+ * pad, conv4 s2, conv5 1x1; secondary: conv5 1x1). Trunk::forward (analysis.rs:157-206),
+ * AnalysisPrimary/Secondary::forward (:242-311). Returns -1 for a stage outside 1..4, a
+ * malformed input extent or SOP. */
+int zo_analysis_stage(const zo_ckpt *ck, int op, int secondary, int stage, const float *x, int c,
+                      int h, int w, float *out) {
+    if (op == ZO_SOP || stage < 1 || stage > 4) return -1;
+    static const int div_in[5] = {0, 1, 2, 4, 8};
+    const int d = div_in[stage];
+    if (c != (stage == 1 ? (secondary ? 12 : 1) : 128)) return -1;
+    T in = {c, cdiv(h, d), cdiv(w, d), (float *)x};
+    const int C = 128;
+    T t;
+    if (stage == 1) {
+        T n = t_new(in.c, in.h, in.w);
+        zo_normalize(in.d, t_len(&in), n.d);
+        t = pad_for(&n, h, w, 1);
+        t_free(&n);
+        t_move(&t, conv_layer(ck, "conv1", &t, C, 3, 3, 2, 1, 1, 1, NULL));
+        resau(ck, "act1", &t);
+    } else if (stage == 2) {
+        t = pad_for(&in, h, w, 2);
+        if (op == ZO_HOP) tam(ck, "TAM", &t, !secondary);
+        t_move(&t, conv_layer(ck, "conv2", &t, C, 3, 3, 2, 1, 1, 1, NULL));
+        resau(ck, "act2", &t);
+    } else if (stage == 3) {
+        t = pad_for(&in, h, w, 4);
+        if (op == ZO_HOP) t_move(&t, cab(ck, "cab", &t));
+        t_move(&t, conv_layer(ck, "conv3", &t, C, 3, 3, 2, 1, 1, 1, NULL));
+        resau(ck, "act3", &t);
+    } else if (secondary) {
+        t = t_clone(&in);
+        t_move(&t, conv1x1(ck, "conv5", &t, 96, 0));
+    } else {
+        t = pad_for(&in, h, w, 8);
+        t_move(&t, conv_layer(ck, "conv4", &t, 160, 3, 3, 2, 1, 1, 1, NULL));
+        t_move(&t, conv1x1(ck, "conv5", &t, 160, 0));
+    }
+    memcpy(out, t.d, sizeof(float) * t_len(&t));
+    t_free(&t);
+    return 0;
+}
+
 int zo_analysis_primary(const zo_ckpt *ck, int op, const float *xin, int h, int w,
                         float *out) {
     if (op == ZO_SOP) return -1;

@@ -126,6 +126,11 @@ int zo_synthesis_secondary(const zo_ckpt *ck, int op, const float *y_hat_luma, i
 /* `AnalysisPrimary::forward` (analysis.rs:242-269): [1][h][w] in [0,255] ->
  * [160][ceil(h/16)][ceil(w/16)]. */
 int zo_analysis_primary(const zo_ckpt *ck, int op, const float *x, int h, int w, float *out);
+/* One analysis stage (1..4) of an h x w picture from its input: picture -> act1 -> act2 ->
+ * act3 -> latent (Trunk::forward, analysis.rs:157-206, and the heads :242-311); the stage's
+ * input is [1 or 12][h][w] for stage 1, else [128][ceil(h / d)][ceil(w / d)], d = 2, 4, 8. */
+int zo_analysis_stage(const zo_ckpt *ck, int op, int secondary, int stage, const float *x, int c,
+                      int h, int w, float *out);
 
 /* `AnalysisSecondary::forward` (analysis.rs:292-311): [12][h][w] -> [96][ceil(h/8)][ceil(w/8)]. */
 int zo_analysis_secondary(const zo_ckpt *ck, int op, const float *x, int h, int w, float *out);

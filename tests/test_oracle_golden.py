@@ -139,3 +139,19 @@ def test_tiles_cfg4_grid():
     for x in t:
         cover[x["core_y"]:x["core_y"] + x["core_h"], x["core_x"]:x["core_x"] + x["core_w"]] += 1
     assert (cover == 1).all()
+
+
+@pytest.mark.parametrize("op,secondary", [("bop", False), ("bop", True), ("hop", False)])
+def test_analysis_stages_compose(op, secondary):
+    """The four analysis stages chained give the whole transform bit for bit (the per-stage
+    GPU check runs them one at a time)."""
+    import synthetic as syn
+    pa, puv = syn.analysis_params(op, 4)
+    ck = zo.Checkpoint(puv if secondary else pa)
+    h, w = (20, 28) if secondary else (40, 56)
+    x = np.floor(syn.uniform(1, "x", (12 if secondary else 1, h, w), 0, 256)).astype(np.float32)
+    t = x
+    for stage in range(1, 5):
+        t = zo.analysis_stage(ck, zo.OPS[op], secondary, stage, t, h, w)
+    whole = (zo.analysis_secondary if secondary else zo.analysis_primary)(ck, zo.OPS[op], x)
+    assert np.array_equal(t, whole)

@@ -106,6 +106,17 @@ class Engine:
         """Limit of the convolution kernel's pipeline waits in SM cycles (0: default)."""
         check(_lib.lib().zjai_ctx_set_wait_limit(self.handle, int(cycles)))
 
+    def set_probe(self, name, buf):
+        """Capture the intermediate map `name` ("ana.act1" ..) of later network runs into `buf`
+        (a float32 CUDA tensor, planar [n, c, h, w] or larger); buf None removes it."""
+        if buf is None:
+            check(_lib.lib().zjai_ctx_set_probe(self.handle, name.encode(), None, 0))
+            return
+        p, mem = _arg(buf)
+        if mem != _lib.MEM_DEVICE:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "a probe buffer must be a CUDA tensor")
+        check(_lib.lib().zjai_ctx_set_probe(self.handle, name.encode(), p, buf.numel()))
+
     @property
     def launch_count(self):
         return int(_lib.lib().zjai_ctx_launch_count(self.handle))

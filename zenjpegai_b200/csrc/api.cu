@@ -188,6 +188,24 @@ int zjai_ctx_set_output_clamp(zjai_ctx* ctx, int clamp) {
   return ZJAI_OK;
 }
 
+int zjai_ctx_set_probe(zjai_ctx* ctx, const char* name, float* dst, int64_t capacity) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!name) return fail(ZJAI_INVALID_ARGUMENT, "probe: null name");
+  if (!dst) {
+    ctx->probes.erase(name);
+    return ZJAI_OK;
+  }
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, dst) != cudaSuccess || at.type != cudaMemoryTypeDevice ||
+      at.device != ctx->device) {
+    cudaGetLastError();
+    return fail(ZJAI_INVALID_ARGUMENT, "probe: the buffer must be device memory of the context's GPU");
+  }
+  if (capacity <= 0) return fail(ZJAI_INVALID_ARGUMENT, "probe: capacity must be positive");
+  ctx->probes[name] = {dst, (long long)capacity};
+  return ZJAI_OK;
+}
+
 int zjai_ctx_set_wait_limit(zjai_ctx* ctx, int64_t cycles) {
   if (!ctx) return fail(ZJAI_INVALID_ARGUMENT, "null context");
   if (cycles < 0) return fail(ZJAI_INVALID_ARGUMENT, "wait limit must be >= 0 (0: default)");

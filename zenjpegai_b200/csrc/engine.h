@@ -76,6 +76,9 @@ struct Ctx {
   // final synthesis layers clamp the denormalised planes to [0, 255] (false: the raw
   // x * 128 + 127.5, zjai_ctx_set_output_clamp)
   bool clamp_output = true;
+  // captures of named intermediate maps (zjai_ctx_set_probe): name -> (device buffer of planar
+  // f32 [n][c][h][w], its capacity in floats)
+  std::map<std::string, std::pair<float*, long long>> probes;
   // limit of the convolution kernel's pipeline waits in SM cycles (0: the kernel's default of
   // about 2 s), zjai_ctx_set_wait_limit
   long long wait_cycles = 0;

@@ -402,6 +402,18 @@ int Runner::stop_check() {
   return ZJAI_OK;
 }
 
+int Runner::probe(const char* name, const TView& t) {
+  if (ctx->probes.empty()) return ZJAI_OK;
+  auto it = ctx->probes.find(name);
+  if (it == ctx->probes.end()) return ZJAI_OK;
+  if ((long long)t.n * t.c * t.h * t.w > it->second.second)
+    return fail(ZJAI_LIMIT_EXCEEDED, std::string("probe ") + name + ": buffer too small");
+  float* dst = it->second.first;
+  mem_kernel(std::string("probe.") + name, "copy", (double)t.n * t.c * t.h * t.w * 6.0, 1,
+             [&] { launch_nhwc_to_planar(t, dst, stream); });
+  return cuda_check(cudaGetLastError(), "probe");
+}
+
 // ResAu::forward (synthesis.rs:61-74): y = x * (1 + conv1x1(gconv3x3(relu6 x))), cropped to
 // (ch, cw) afterwards (the reference's crop follows the block). `a` = relu6(x).
 int Runner::resau(const std::string& p, const TView& x, const TView& a, int ch, int cw,
@@ -813,6 +825,7 @@ int Runner::analysis(const TView& x, int h, int w, float* out) {
   }
   TView y1;
   ZJAI_TRY(resau("act1", x1, a1, h1, w1, &y1));
+  ZJAI_TRY(probe("ana.act1", y1));
   ZJAI_TRY(stop_check());
   TView p1 = y1.crop(padded(2), paddedw(2));
   launch_replicate_pad(y1, p1, stream);
@@ -836,6 +849,7 @@ int Runner::analysis(const TView& x, int h, int w, float* out) {
   }
   TView y2;
   ZJAI_TRY(resau("act2", x2, a2, h2, w2, &y2));
+  ZJAI_TRY(probe("ana.act2", y2));
   ZJAI_TRY(stop_check());
   TView p2 = y2.crop(padded(4), paddedw(4));
   launch_replicate_pad(y2, p2, stream);
@@ -860,6 +874,7 @@ int Runner::analysis(const TView& x, int h, int w, float* out) {
   }
   TView y3;
   ZJAI_TRY(resau("act3", x3, a3, h3, w3, &y3));
+  ZJAI_TRY(probe("ana.act3", y3));
   ZJAI_TRY(stop_check());
   ConvOut of;
   of.planar = true;

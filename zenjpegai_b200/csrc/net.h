@@ -80,6 +80,8 @@ struct Runner {
   }
   int out_extent(const std::string& name, int h, int w, int* oh, int* ow);
   int stop_check();
+  // copy `t` as planar f32 [n][c][h][w] into the capture registered under `name`, if any
+  int probe(const char* name, const TView& t);
 
   int resau(const std::string& p, const TView& x, const TView& a, int ch, int cw, TView* y);
   int rb(const std::string& p, const TView& x, const TView& y, const TView* relu6_out = nullptr,
