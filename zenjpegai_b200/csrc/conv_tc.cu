@@ -68,9 +68,10 @@ __device__ __forceinline__ uint4 pack_h8(const float (&v)[8]) {
   return u;
 }
 
-// Activation of an 8-vector (one uniform branch per group, not per element).
-__device__ __forceinline__ void act8(float (&x)[8], int a);
-// The common activations (none, ReLU) without a switch; the rest through act8.
+// The activations of the NHWC epilogues. The sigmoid (with its exponential and division) is
+// compiled in only where SIG is set (the CAB epilogue, the one NHWC layer that uses it): its
+// code in the other instantiations' chunk loop made every chunk slower, sigmoid or not.
+template <bool SIG>
 __device__ __forceinline__ void act8_fast(float (&x)[8], int a) {
   if (a == ACT_NONE) return;
   if (a == ACT_RELU) {
@@ -78,29 +79,19 @@ __device__ __forceinline__ void act8_fast(float (&x)[8], int a) {
     for (int e = 0; e < 8; ++e) x[e] = x[e] > 0.f ? x[e] : 0.f;
     return;
   }
-  act8(x, a);
-}
-
-__device__ __forceinline__ void act8(float (&x)[8], int a) {
-  switch (a) {
-    case ACT_RELU:
-#pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = act<ACT_RELU>(x[e]);
-      break;
-    case ACT_LEAKY:
-#pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = act<ACT_LEAKY>(x[e]);
-      break;
-    case ACT_SIGMOID:
+  if constexpr (SIG) {
+    if (a == ACT_SIGMOID) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) x[e] = act<ACT_SIGMOID>(x[e]);
-      break;
-    case ACT_RELU6:
+      return;
+    }
+  }
+  if (a == ACT_RELU6) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = act<ACT_RELU6>(x[e]);
-      break;
-    default:
-      break;
+    for (int e = 0; e < 8; ++e) x[e] = act<ACT_RELU6>(x[e]);
+  } else if (a == ACT_LEAKY) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = act<ACT_LEAKY>(x[e]);
   }
 }
 
@@ -154,7 +145,7 @@ __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kCh
     x[5] = v[8 * g + 5] * a.scale + b1.y;
     x[6] = v[8 * g + 6] * a.scale + b1.z;
     x[7] = v[8 * g + 7] * a.scale + b1.w;
-    act8_fast(x, a.act1);
+    act8_fast<OP == OP_CAB>(x, a.act1);
     if constexpr (OP != OP_NONE) {
       float q1[8];
       unpack_h8(r1[g], q1);
@@ -171,7 +162,7 @@ __device__ __forceinline__ void epi_nhwc(const ConvArgs& a, const float (&v)[kCh
         for (int e = 0; e < 8; ++e) x[e] = q2[e] + q1[e] * x[e];
       }
     }
-    act8_fast(x, a.act2);
+    act8_fast<false>(x, a.act2);
     if constexpr (OP != OP_NONE) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) rmax = fmaxf(rmax, fabsf(x[e]));
@@ -222,35 +213,43 @@ __device__ __forceinline__ void epi_staged(const ConvArgs& a, const float (&v)[k
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     const int c = ch0 + 8 * g;
+    // packed f32 pairs (FFMA2 / FADD2 / FMUL2): per lane the same IEEE operations as the
+    // scalar expressions in the comments, in half the instructions
     float x[8];
     const float4 b0 = *reinterpret_cast<const float4*>(btab + col0 + 8 * g);
     const float4 b1 = *reinterpret_cast<const float4*>(btab + col0 + 8 * g + 4);
-    x[0] = v[8 * g + 0] * a.scale + b0.x;
-    x[1] = v[8 * g + 1] * a.scale + b0.y;
-    x[2] = v[8 * g + 2] * a.scale + b0.z;
-    x[3] = v[8 * g + 3] * a.scale + b0.w;
-    x[4] = v[8 * g + 4] * a.scale + b1.x;
-    x[5] = v[8 * g + 5] * a.scale + b1.y;
-    x[6] = v[8 * g + 6] * a.scale + b1.z;
-    x[7] = v[8 * g + 7] * a.scale + b1.w;
-    act8_fast(x, a.act1);
-    if constexpr (OP != OP_NONE) {
-      float q1[8];
-      unpack_h8(r1[g], q1);
-      if constexpr (OP == OP_ADD) {
+    {
+      // x = v * scale + b (one fused multiply-add)
+      const float2 s2 = make_float2(a.scale, a.scale);
+      const float2 bb[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
+                            make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = x[e] + q1[e];
-      } else if constexpr (OP == OP_GATE) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = q1[e] * (1.f + x[e]);
-      } else {
-        float q2[8];
-        unpack_h8(r2[g], q2);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = q2[e] + q1[e] * x[e];
+      for (int i = 0; i < 4; ++i) {
+        const float2 r = __ffma2_rn(make_float2(v[8 * g + 2 * i], v[8 * g + 2 * i + 1]), s2, bb[i]);
+        x[2 * i] = r.x;
+        x[2 * i + 1] = r.y;
       }
     }
-    act8_fast(x, a.act2);
+    act8_fast<OP == OP_CAB>(x, a.act1);
+    if constexpr (OP != OP_NONE) {
+      const __half2* h1 = reinterpret_cast<const __half2*>(&r1[g]);
+      const __half2* h2 = reinterpret_cast<const __half2*>(&r2[g]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 q1 = __half22float2(h1[i]), xi = make_float2(x[2 * i], x[2 * i + 1]);
+        float2 r;
+        if constexpr (OP == OP_ADD) {
+          r = __fadd2_rn(xi, q1);  // x + q1
+        } else if constexpr (OP == OP_GATE) {
+          r = __fmul2_rn(q1, __fadd2_rn(make_float2(1.f, 1.f), xi));  // q1 * (1 + x)
+        } else {
+          r = __ffma2_rn(q1, xi, __half22float2(h2[i]));  // q2 + q1 * x, fused
+        }
+        x[2 * i] = r.x;
+        x[2 * i + 1] = r.y;
+      }
+    }
+    act8_fast<false>(x, a.act2);
     // residual / gate outputs grow along the network: track the largest stored magnitude of
     // the pixels this thread owns (lanes outside the view stage values nobody stores)
     if constexpr (OP != OP_NONE) {
@@ -259,11 +258,16 @@ __device__ __forceinline__ void epi_staged(const ConvArgs& a, const float (&v)[k
         for (int e = 0; e < 8; ++e) rmax = fmaxf(rmax, fabsf(x[e]));
       }
     }
-    dst[g] = pack_h8(x);
+    const uint4 packed = pack_h8(x);
+    dst[g] = packed;
     if (a.out2 && valid && c < a.cph) {
+      // relu6 of the stored f16 values (clamping commutes with the monotonic rounding)
+      uint4 q = packed;
+      __half2* h = reinterpret_cast<__half2*>(&q);
+      const __half2 z = __float2half2_rn(0.f), six = __float2half2_rn(6.f);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] = fminf(fmaxf(x[k], 0.f), 6.f);
-      *reinterpret_cast<uint4*>(a.out2 + p2o + c) = pack_h8(x);
+      for (int i = 0; i < 4; ++i) h[i] = __hmin2(__hmax2(h[i], z), six);
+      *reinterpret_cast<uint4*>(a.out2 + p2o + c) = q;
     }
   }
 }
@@ -438,6 +442,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const TileCoord tc = decode_tile(a, t);
         const int nt = tc.n0 / a.bn;
         const __half* wbase = a.wblk + (size_t)tc.img * a.wblk_img + (size_t)nt * brows * a.kc;
+        const uint32_t live = a.tmask_on ? a.tmask[nt] : 0xFFFFFFFFu;
         for (int cc = 0; cc < a.cchunks; ++cc) {
           if (!mbar_wait_idle(heb + 8u * hs, hphase ^ 1u, abort_flag, a.err, DEV_TIMEOUT_EMPTY, 64, wl))
             goto halo_done;
@@ -450,6 +455,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             hphase ^= 1u;
           }
           for (int tap = 0; tap < a.taps; ++tap) {
+            if (!((live >> tap) & 1u)) continue;
             if (!mbar_wait_idle(eb_base + 8u * stage, phase ^ 1u, abort_flag, a.err,
                                 DEV_TIMEOUT_EMPTY, 64, wl))
               goto halo_done;
@@ -579,6 +585,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           break;
         tc_fence_after();
         const uint32_t d0 = tmem_base + (uint32_t)(acc * a.msub * a.bn) + d_off;
+        const int nt = t % a.n_tiles;
+        const uint32_t live = a.tmask_on ? a.tmask[nt] : 0xFFFFFFFFu;
         bool ok = true;
         for (int cc = 0; cc < a.cchunks && ok; ++cc) {
           if (!mbar_wait(hfb + 8u * hs, hphase, abort_flag, a.err, DEV_TIMEOUT_FULL, wl)) {
@@ -586,27 +594,32 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             break;
           }
           // grouped: this chunk's (pseudo-)group owns accumulator columns cc * grp_n ..
-          // (grp_n wide) and its first tap starts them; dense: the tile's first UMMA starts all
+          // (grp_n wide) and its first live tap starts them; dense: the tile's first UMMA
+          // starts all
           const uint32_t d = d0 + (a.grp_pc ? (uint32_t)(cc * a.grp_n) : 0u);
-          const bool fresh = a.grp_pc || cc == 0;
+          bool fresh = a.grp_pc || cc == 0;
           uint64_t da = dH0 + (uint64_t)hs * dslot;
           int kx = 0;
           for (int tap = 0; tap < a.taps; ++tap) {
-            if (!mbar_wait(fb_base + 8u * stage, phase, abort_flag, a.err, DEV_TIMEOUT_FULL, wl)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            umma_f16(d, da, db, idesc, (fresh && tap == 0) ? 0u : 1u);
-            umma_f16(d, da + 2, db + 2, idesc, 1u);
-            umma_f16(d, da + 4, db + 4, idesc, 1u);
-            umma_f16(d, da + 6, db + 6, idesc, 1u);
-            umma_commit(eb_base + 8u * stage);
-            db += dstage;
-            if (++stage == S) {
-              stage = 0;
-              phase ^= 1u;
-              db = dB0;
+            if ((live >> tap) & 1u) {
+              if (!mbar_wait(fb_base + 8u * stage, phase, abort_flag, a.err, DEV_TIMEOUT_FULL,
+                             wl)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              umma_f16(d, da, db, idesc, fresh ? 0u : 1u);
+              umma_f16(d, da + 2, db + 2, idesc, 1u);
+              umma_f16(d, da + 4, db + 4, idesc, 1u);
+              umma_f16(d, da + 6, db + 6, idesc, 1u);
+              umma_commit(eb_base + 8u * stage);
+              fresh = false;
+              db += dstage;
+              if (++stage == S) {
+                stage = 0;
+                phase ^= 1u;
+                db = dB0;
+              }
             }
             da += 8;
             if (++kx == a.kw) {

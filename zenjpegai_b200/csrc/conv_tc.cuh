@@ -23,6 +23,8 @@ namespace zjai {
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_LEAKY = 2, ACT_SIGMOID = 3, ACT_RELU6 = 4 };
 enum EpiOp : int { OP_NONE = 0, OP_ADD = 1, OP_GATE = 2, OP_CAB = 3 };
 
+constexpr int kMaxTapMasks = 8;
+
 struct ConvArgs {
   // tile grid
   int tiles_x, tiles_y, n_img, n_tiles, num_tiles;
@@ -67,6 +69,13 @@ struct ConvArgs {
   // kMaxHaloSlots: layers with little MMA work per halo keep more halos in flight).
   int halo, hw, hh, hslots;
   uint32_t halo_bytes;
+  // Live taps of a halo-mode layer per N tile (bit tap of tmask[nt]; taps <= 32, n_tiles <=
+  // kMaxTapMasks), or tmask_on == 0 when every tap of every tile is live: a stride-2 transposed
+  // conv packed with whole phases per N tile uses only some taps of its window per phase, and
+  // the dead taps' weight blocks are neither loaded nor multiplied (the halo window still
+  // steps over them).
+  int tmask_on;
+  uint32_t tmask[8];
   // epilogue
   const float* bias;   // [n_tiles * bn] in packed column order, or null
   float scale;         // weight unscale (power of two)

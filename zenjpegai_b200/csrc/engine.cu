@@ -347,6 +347,11 @@ int pack_convT(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, 
   L->R = 2 * r2;
   L->cph = cout / (r2 * r2);
   L->ncols = 4 * cout;
+  // Each phase reads only some taps of the window (1, 2, 2 and 4 of the 2 x 2 window for
+  // k = 3): an N tile whose phases leave taps unused skips them (ConvArgs::tmask). Narrower
+  // tiles of single phases were measured slower in the network (the halo is re-read per N tile
+  // and the MMA is not what bounds these layers), so the tiles stay as wide as choose_n makes
+  // them.
   choose_n(L->ncols, &L->bn, &L->n_tiles);
   L->npad = L->bn * L->n_tiles;
   const int taps = win * win;
@@ -373,6 +378,24 @@ int pack_convT(Ctx* ctx, ConvLayer* L, const float* w, const float* b, int cin, 
   }
   // live (tap, column) pairs summed over all columns = MACs per input pixel / cin
   L->flops_per_px = 2LL * live * cin;
+  if (taps <= 32 && L->n_tiles > 1 && L->n_tiles <= kMaxTapMasks) {
+    bool any_dead = false;
+    for (int nt = 0; nt < L->n_tiles; ++nt) {
+      uint32_t m = 0;
+      for (int tap = 0; tap < taps; ++tap) {
+        bool on = false;
+        for (int n = nt * L->bn; n < (nt + 1) * L->bn && !on; ++n) {
+          const float* row = wf.data() + ((size_t)tap * L->npad + n) * L->cin_pad;
+          for (int ci = 0; ci < cin && !on; ++ci) on = row[ci] != 0.f;
+        }
+        if (on) m |= 1u << tap;
+      }
+      if (!m) m = 1u;  // a tile's first UMMA initialises its accumulator
+      any_dead |= m != (taps == 32 ? 0xFFFFFFFFu : (1u << taps) - 1u);
+      L->tmask[nt] = m;
+    }
+    L->tmask_on = any_dead ? 1 : 0;
+  }
   return upload_layer(ctx, L, wf, bf, false);
 }
 
@@ -438,6 +461,9 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   ow = std::min(ow, (want_w + L.R - 1) / L.R);
   if (!o.planar && (L.cph % 8 != 0))
     return fail(ZJAI_UNSUPPORTED, "conv: NHWC output needs a multiple of 8 channels");
+  // the NHWC epilogues carry the sigmoid only in the CAB op (its one use on the networks)
+  if (!o.planar && ((o.act1 == ACT_SIGMOID && o.op != OP_CAB) || o.act2 == ACT_SIGMOID))
+    return fail(ZJAI_UNSUPPORTED, "conv: NHWC output takes the sigmoid only with the CAB op");
 
   ConvArgs a;
   memset(&a, 0, sizeof a);
@@ -621,6 +647,8 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   a.wblk_img = L.w_img;
   a.klist = L.klist;
   a.koff = L.koff;
+  a.tmask_on = L.tmask_on;
+  for (int i = 0; i < kMaxTapMasks; ++i) a.tmask[i] = L.tmask[i];
   cudaError_t lerr = cudaSuccess;
   char detail[256] = "";
   // an error left by an earlier asynchronous launch must not be reported as this one's

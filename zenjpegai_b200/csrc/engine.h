@@ -164,6 +164,9 @@ struct ConvLayer {
   // grouped packing (ConvArgs::grp_n / grp_pc): output columns per group and groups per
   // 64-channel chunk, 0 for a dense layer
   int grp_n = 0, grp_pc = 0;
+  // live taps per N tile of a halo-mode transposed conv (ConvArgs::tmask), tmask_on = 0: all
+  int tmask_on = 0;
+  uint32_t tmask[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   float* bias = nullptr;
   long long flops_per_px = 0;  // algorithmic MACs*2 per conv-output pixel (live taps only)
   // conv output extent (GEMM M space) and shuffled output extent for an input of h x w
