@@ -72,16 +72,17 @@ def peaks():
         return 1590.0, "fallback (1.59 PFLOP/s)"
 
 
-def conv_traffic(config):
+def conv_traffic(config, algorithmic_bytes):
     """DRAM bytes (read + write) of one step's tcgen05 kernel launches (conv_tc_kernel and
-    ffn_tc_kernel), from the committed ncu capture summary
-    profiles/tcgen05_<config>_step_dram.txt (`dram_bytes_per_step: N`), or None."""
+    ffn_tc_kernel): the step's algorithmic bytes times the DRAM-to-algorithmic ratio measured
+    by ncu on a small case of the same workload, from the committed capture summary
+    profiles/tcgen05_<config>_step_dram.txt (`traffic_per_algorithmic_byte: r`), or None."""
     path = os.path.join(ROOT, "profiles", "tcgen05_%s_step_dram.txt" % config)
     try:
         with open(path) as f:
             for ln in f:
-                if ln.startswith("dram_bytes_per_step:"):
-                    return float(ln.split(":", 1)[1])
+                if ln.startswith("traffic_per_algorithmic_byte:"):
+                    return float(ln.split(":", 1)[1]) * algorithmic_bytes
     except OSError:
         pass
     return None
@@ -462,8 +463,8 @@ def run_reference(args, cfg):
 # ---------------------------------------------------------------------------------------------
 
 def profile_step(eng, step, flush):
-    """Algorithmic FLOPs, summed CUDA-event ms and launches of the tcgen05 kernels over one
-    profiled step."""
+    """Summed CUDA-event ms, algorithmic FLOPs, algorithmic bytes and launches of the tcgen05
+    kernels over one profiled step."""
     import ctypes
     import torch
     from zenjpegai_b200 import _lib
@@ -472,10 +473,11 @@ def profile_step(eng, step, flush):
     flush.zero_()
     torch.cuda.synchronize()
     step()
-    ms, fl, nl = ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
-    L.zjai_ctx_profile_read(eng.handle, ctypes.byref(ms), ctypes.byref(fl), ctypes.byref(nl))
+    ms, fl, by, nl = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
+    L.zjai_ctx_profile_read_bytes(eng.handle, ctypes.byref(ms), ctypes.byref(fl),
+                                  ctypes.byref(by), ctypes.byref(nl))
     L.zjai_ctx_profile(eng.handle, 0)
-    return ms.value, fl.value, nl.value
+    return ms.value, fl.value, by.value, nl.value
 
 
 def layer_report(eng):
@@ -507,8 +509,18 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", action="store_true",
                     help="print the per-layer conv time of one profiled step to stderr")
+    ap.add_argument("--picture", default=None, metavar="WxH",
+                    help="a synthesis config on a smaller picture of the same tiling (the small "
+                         "case of the profiles' DRAM captures); the line then carries no traffic")
+    ap.add_argument("--arena-gb", type=int, default=0,
+                    help="device arena of the engine in GiB (default: the config's)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config], name=args.config)
+    if args.picture:
+        if cfg["kind"] != "synth":
+            ap.error("--picture applies to the synthesis configs")
+        pw, ph = (int(v) for v in args.picture.lower().split("x"))
+        cfg.update(W=pw, H=ph, desc=cfg["desc"] + " (picture %dx%d)" % (pw, ph))
     if cfg["kind"] == "synth":
         H, W = cfg["H"], cfg["W"]
         cfg["ntiles"] = sum(len(r) for r in _tile_rows(cfg)) if cfg["tile"] else 1
@@ -532,8 +544,9 @@ def main():
     from zenjpegai_b200 import sharding
     from zenjpegai_b200.decoder import Decoder
 
-    eng = zj.Engine(local, arena_bytes={"synth": 64 << 30, "batch": 32 << 30}.get(cfg["kind"],
-                                                                                4 << 30))
+    arena = args.arena_gb << 30 if args.arena_gb else \
+        {"synth": 64 << 30, "batch": 32 << 30}.get(cfg["kind"], 4 << 30)
+    eng = zj.Engine(local, arena_bytes=arena)
     # one non-default stream shared by torch (copies, events, NCCL) and the engine
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -696,14 +709,14 @@ def main():
     eng.sync()
     e2e_ms = timed(args.steps, from_host=True)
     # live roofline of the tcgen05 kernels over one profiled step
-    conv_ms, conv_fl, conv_n = profile_step(eng, step, flush)
+    conv_ms, conv_fl, conv_by, conv_n = profile_step(eng, step, flush)
     if args.layers and rank == 0:
         layer_report(eng)
-    stats = torch.tensor([conv_ms, conv_fl, float(conv_n), float(launches)],
+    stats = torch.tensor([conv_ms, conv_fl, conv_by, float(conv_n), float(launches)],
                          dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.SUM)
-    conv_ms, conv_fl, conv_n, all_launches = (float(x) for x in stats.tolist())
+    conv_ms, conv_fl, conv_by, conv_n, all_launches = (float(x) for x in stats.tolist())
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -712,7 +725,8 @@ def main():
     if rank == 0:
         peak, peak_src = peaks()
         achieved = conv_fl / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
-        traffic = conv_traffic(args.config) if world == 1 else None
+        traffic = (conv_traffic(args.config, conv_by)
+                   if world == 1 and not args.picture else None)
         line = {
             "metric": cfg["metric"],
             "value": args.steps * out_px / 1e6 / (total_ms / 1e3),
@@ -738,11 +752,15 @@ def main():
                 "peak_source": peak_src,
                 "launches_per_step": conv_n,
                 "flops_per_step": conv_fl,
-                # DRAM bytes of one step's tcgen05 launches from the committed one-GPU ncu
-                # capture of this workload (profiles/tcgen05_<config>_step_dram.txt), reported
-                # at N = 1 only
+                # each launch's input, live weights, output and residual operands once: the
+                # figure `traffic` is to be compared with
+                "algorithmic_bytes_per_step": conv_by,
+                # DRAM bytes of one step's tcgen05 launches: the algorithmic bytes times the
+                # DRAM / algorithmic ratio ncu measured on a small case of this workload
+                # (profiles/tcgen05_<config>_step_dram.txt), reported at N = 1 only
                 "traffic": traffic,
-                "traffic_unit": "bytes per step (DRAM read + write, ncu, one GPU)",
+                "traffic_unit": "bytes per step (DRAM read + write, ncu on a small case, "
+                                "scaled by algorithmic bytes; a lower bound)",
             },
             "cpu_baseline": cpu,
             "e2e": {

@@ -129,6 +129,10 @@ int zjai_ctx_profile(zjai_ctx *ctx, int enable);
 int zjai_ctx_profile_report(zjai_ctx *ctx, char *buf, size_t len);
 int zjai_ctx_profile_read(zjai_ctx *ctx, double *conv_ms, double *conv_flops,
                           int64_t *conv_launches);
+/* zjai_ctx_profile_read that also returns the convolution launches' algorithmic bytes (each
+ * launch's input, live weights, output, residual operands and relu6 copy counted once). */
+int zjai_ctx_profile_read_bytes(zjai_ctx *ctx, double *conv_ms, double *conv_flops,
+                                double *conv_bytes, int64_t *conv_launches);
 
 /* ---------------------------------------------------------------------------------------- */
 /* Networks (model load + GPU-resident packed weights)                                        */

@@ -223,10 +223,15 @@ int zjai_ctx_profile(zjai_ctx* ctx, int enable) {
 
 int zjai_ctx_profile_read(zjai_ctx* ctx, double* conv_ms, double* conv_flops,
                           int64_t* conv_launches) {
+  return zjai_ctx_profile_read_bytes(ctx, conv_ms, conv_flops, nullptr, conv_launches);
+}
+
+int zjai_ctx_profile_read_bytes(zjai_ctx* ctx, double* conv_ms, double* conv_flops,
+                                double* conv_bytes, int64_t* conv_launches) {
   ZJAI_TRY(ctx_enter(ctx));
   ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "stream sync"));
   ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream2), "stream sync"));
-  double ms = 0.0, fl = 0.0;
+  double ms = 0.0, fl = 0.0, by = 0.0;
   int64_t nconv = 0;
   for (auto& r : ctx->conv_records) {
     float t = 0.f;
@@ -234,6 +239,7 @@ int zjai_ctx_profile_read(zjai_ctx* ctx, double* conv_ms, double* conv_flops,
     if (r.conv) {
       ms += t;
       fl += r.flops;
+      by += r.bytes;
       ++nconv;
     }
     auto it = std::find_if(ctx->tag_totals.begin(), ctx->tag_totals.end(),
@@ -253,6 +259,7 @@ int zjai_ctx_profile_read(zjai_ctx* ctx, double* conv_ms, double* conv_flops,
   ctx->conv_records.clear();
   if (conv_ms) *conv_ms = ms;
   if (conv_flops) *conv_flops = fl;
+  if (conv_bytes) *conv_bytes = by;
   return ZJAI_OK;
 }
 

@@ -651,6 +651,15 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
   for (int i = 0; i < kMaxTapMasks; ++i) a.tmask[i] = L.tmask[i];
   cudaError_t lerr = cudaSuccess;
   char detail[256] = "";
+  // Algorithmic bytes of the launch (the profile's memory figure for it): the input once, the
+  // live weights once (f16: 2 bytes a MAC of one pixel = flops_per_px), the output once, and
+  // the residual operands and the relu6 copy once each.
+  const double out_elems = (double)in.n * want_h * want_w * L.cph;
+  const double out_elt = o.planar ? (o.qbytes ? (double)o.qbytes : 4.0) : 2.0;
+  const int extra_ops = o.planar ? 0 : (o.op == OP_CAB ? 2 : o.op != OP_NONE ? 1 : 0) +
+                                          (o.out2 ? 1 : 0);
+  const double bytes = 2.0 * in.n * in.h * in.w * L.cin + (double)L.flops_per_px +
+                       out_elems * out_elt + 2.0 * out_elems * extra_ops;
   // an error left by an earlier asynchronous launch must not be reported as this one's
   ZJAI_TRY(cuda_check(cudaGetLastError(), "before conv launch"));
   if (!a.s2) {
@@ -663,7 +672,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     a.num_tiles = a.tiles_x * a.tiles_y * a.n_img * a.n_tiles;
     const double fl = (double)L.flops_per_px * oh * ow * in.n;
     ctx->launches++;
-    timed_launch(ctx, true, fl, 0.0, [&] {
+    timed_launch(ctx, true, fl, bytes, [&] {
       lerr = launch_conv(tmA, tmO, a, std::min(a.num_tiles, ctx->sms), ctx->stream, detail,
                          (int)sizeof detail);
     });
@@ -685,7 +694,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     a.num_tiles = a.tiles_x * a.tiles_y * a.n_img * a.n_tiles;
     const double fl = (double)L.flops_per_px * oh * ow * in.n;
     ctx->launches++;
-    timed_launch(ctx, true, fl, 0.0, [&] {
+    timed_launch(ctx, true, fl, bytes, [&] {
       lerr = launch_conv(maps[0], tmO, a, std::min(a.num_tiles, ctx->sms), ctx->stream, detail,
                          (int)sizeof detail);
     });

@@ -636,9 +636,12 @@ int run_ffn(Ctx* ctx, const FfnLayer& L, const TView& ln, const TView& x) {
   ZJAI_TRY(cuda_check(cudaGetLastError(), "before FFN launch"));
   const double px = (double)x.n * x.h * x.w;
   const double fl = 2.0 * px * (2.0 * L.hidden * L.dim + (double)L.hidden * L.dim);
+  // algorithmic bytes: ln read, x read and written, the three weight sets once
+  const double bytes = 2.0 * px * 3.0 * L.dim +
+                       2.0 * (3.0 * L.hidden * L.dim) + 4.0 * 2.0 * L.hidden * 9.0;
   cudaError_t e = cudaSuccess;
   ctx->launches++;
-  timed_launch(ctx, true, fl, 0.0, [&] {
+  timed_launch(ctx, true, fl, bytes, [&] {
     e = launch_ffn(tm, a, std::min(a.num_tiles, ctx->sms), ctx->stream);
   });
   return cuda_check(e, "FFN launch");
