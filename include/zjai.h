@@ -234,6 +234,45 @@ int zjai_reconstruct_latent(zjai_net *net, const float *z_hat, int hz, int wz,
                             const float *residual, int h, int w, float *psi, float *y_hat,
                             int mem);
 
+/* ---------------------------------------------------------------------------------------- */
+/* Weight files (host only): the crate's checkpoint readers                                  */
+/* ---------------------------------------------------------------------------------------- */
+
+/* A parsed checkpoint: `Checkpoint::parse` (src/weights/mod.rs:131-183) of a PyTorch `.pth`
+ * file (an uncompressed ZIP with a pickled state dict; a data-only pickle interpreter, no code
+ * runs) or a packed `ZJM1` file (src/weights/packed.rs:8-21). The bytes are copied. Tensors:
+ * those at the top level of the state dict, then the tensors of nested dicts under dotted
+ * names (three levels at most, like the crate); integer entries; numeric lists of nested
+ * dicts. Dtype codes are ZJM1's: 0 f64, 1 f32, 2 f16, 3 i64, 4 i32, 5 i16, 6 i8, 7 u8,
+ * 8 bool. Malformed files fail with ZJAI_MODEL. */
+typedef struct zjai_ckpt zjai_ckpt;
+int zjai_ckpt_open(const void *data, size_t len, zjai_ckpt **out);
+int zjai_ckpt_close(zjai_ckpt *ck);
+int zjai_ckpt_count(const zjai_ckpt *ck, int *ntensors, int *nints, int *nlists);
+/* Tensor i: name (valid until close), dtype code, rank, dims (up to 8). */
+int zjai_ckpt_tensor(const zjai_ckpt *ck, int i, const char **name, int *dtype, int *ndim,
+                     int64_t *shape);
+int zjai_ckpt_find(const zjai_ckpt *ck, const char *name, int *index);
+/* Tensor i as contiguous row-major little-endian bytes (a strided view is gathered). */
+int zjai_ckpt_read(const zjai_ckpt *ck, int i, void *dst, size_t capacity);
+int zjai_ckpt_int(const zjai_ckpt *ck, int i, const char **name, int64_t *value);
+int zjai_ckpt_list(const zjai_ckpt *ck, int i, const char **name, const double **values, int *n);
+/* The f32 and f16 tensors of rank <= 4 as f32 parameters (f16 upcast exactly, like
+ * `Checkpoint::f32`), ready for zjai_net_create / zjai_stage_create; the array and its data
+ * stay valid until close. */
+int zjai_ckpt_params(zjai_ckpt *ck, const zjai_param **params, int *n);
+
+/* A `ZJB1` bundle (or `ZJB2`, its f16-weight variant; f16 = 1): files addressed by their path
+ * relative to the reference's models/ directory, plus the notice that travels with the weights
+ * (src/weights/packed.rs:23-43, `PackedBundle`). File data points into the bundle's copy. */
+typedef struct zjai_bundle zjai_bundle;
+int zjai_bundle_open(const void *data, size_t len, zjai_bundle **out);
+int zjai_bundle_close(zjai_bundle *b);
+int zjai_bundle_info(const zjai_bundle *b, int *nfiles, int *f16, const char **notice,
+                     size_t *notice_len);
+int zjai_bundle_file(const zjai_bundle *b, int i, const char **path, const void **data,
+                     size_t *len);
+
 /* One synthesis tile (src/tools/tiles.rs:26-32 `SynthesisTile`). */
 typedef struct {
   int img_x, img_y, img_w, img_h;

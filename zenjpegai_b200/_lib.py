@@ -103,6 +103,24 @@ def lib():
     L.zjai_stage_create.argtypes = [_vp, _i, _i, _i, ctypes.POINTER(Param), _i,
                                      ctypes.POINTER(_vp)]
     L.zjai_stage_forward.argtypes = [_vp, _vp, _i, _i, _i, _vp, _i]
+    L.zjai_ckpt_open.argtypes = [_vp, ctypes.c_size_t, ctypes.POINTER(_vp)]
+    L.zjai_ckpt_close.argtypes = [_vp]
+    L.zjai_ckpt_count.argtypes = [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]
+    L.zjai_ckpt_tensor.argtypes = [_vp, _i, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_i),
+                                   ctypes.POINTER(_i), ctypes.POINTER(ctypes.c_int64)]
+    L.zjai_ckpt_find.argtypes = [_vp, ctypes.c_char_p, ctypes.POINTER(_i)]
+    L.zjai_ckpt_read.argtypes = [_vp, _i, _vp, ctypes.c_size_t]
+    L.zjai_ckpt_int.argtypes = [_vp, _i, ctypes.POINTER(ctypes.c_char_p),
+                                ctypes.POINTER(ctypes.c_int64)]
+    L.zjai_ckpt_list.argtypes = [_vp, _i, ctypes.POINTER(ctypes.c_char_p),
+                                 ctypes.POINTER(ctypes.POINTER(ctypes.c_double)), ctypes.POINTER(_i)]
+    L.zjai_ckpt_params.argtypes = [_vp, ctypes.POINTER(ctypes.POINTER(Param)), ctypes.POINTER(_i)]
+    L.zjai_bundle_open.argtypes = [_vp, ctypes.c_size_t, ctypes.POINTER(_vp)]
+    L.zjai_bundle_close.argtypes = [_vp]
+    L.zjai_bundle_info.argtypes = [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i),
+                                   ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t)]
+    L.zjai_bundle_file.argtypes = [_vp, _i, ctypes.POINTER(ctypes.c_char_p),
+                                   ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t)]
     L.zjai_hyper_decode.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _i]
     L.zjai_context_decompress.argtypes = [_vp, _vp, _i, _i, _vp, _vp, _i]
     L.zjai_reconstruct_latent.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _vp, _i]
