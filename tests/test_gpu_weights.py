@@ -70,3 +70,21 @@ def test_latent_model_from_f16_packed(eng):
         assert rel < 2e-3
     finally:
         m.close()
+
+
+def test_load_synthesis_from_model_dir(eng, tmp_path):
+    """load_synthesis through a ModelDir laid out like the reference's models/ directory."""
+    import zenjpegai_b200 as zj
+    from zenjpegai_b200 import weights as W
+    py, _ = syn.synthesis_params("sop", 2)
+    rel = W.synthesis_path(1, 0, zj.SOP)
+    (tmp_path / rel).parent.mkdir(parents=True)
+    torch.save({k: torch.from_numpy(v) for k, v in py.items()}, tmp_path / rel)
+    lat = syn.laplace_latent(8, "ly", (160, 3, 5), 2.0)
+    a = W.load_synthesis(eng, W.ModelDir(str(tmp_path)), 1, zj.SOP, 0)
+    b = zj.Network(eng, zj.SYN_Y, zj.SOP, py)
+    try:
+        assert np.array_equal(net_forward(a, lat), net_forward(b, lat))
+    finally:
+        a.close()
+        b.close()

@@ -202,3 +202,24 @@ def test_malformed_inputs_fail_cleanly(tmp_path):
             W.Checkpoint(bad)
     with pytest.raises(_lib.ZjaiError):
         W.Bundle(b"ZJB1\x01\0\0\0\x05\0\0\0\xff\xff\xff\xff")
+
+
+def test_model_paths_and_sources(tmp_path):
+    """Paths follow src/model/mod.rs:94-140; a ModelDir and a Bundle serve the same bytes."""
+    assert W.common_path(1, 0) == "VM_common_int/Y_0.012.pth"
+    assert W.synthesis_path(3, 1, 2) == "VM_hop/decoder_UV_0.5.pth"
+    assert W.synthesis_path(0, 0, 0) == "VM_sop/decoder_Y_0.002.pth"
+    assert W.analysis_path(2, 0, 0) == "VM_bop/encoder_Y_0.075.pth"  # SOP encodes with BOP
+    with pytest.raises(_lib.ZjaiError):
+        W.common_path(4, 0)
+    rel = W.synthesis_path(1, 0, 1)
+    (tmp_path / "VM_bop").mkdir()
+    data = write_zjm({"first_stage.0.0.conv1.weight": np.ones((2, 2, 1, 1), np.float32)})
+    (tmp_path / rel).write_bytes(data)
+    bd = W.Bundle(write_bundle([(rel, data)], "n"))
+    for src in (W.ModelDir(str(tmp_path)), bd):
+        assert src.read(rel) == data
+        assert np.array_equal(W._params(src, rel)["first_stage.0.0.conv1.weight"],
+                              np.ones((2, 2, 1, 1), np.float32))
+    with pytest.raises(_lib.ZjaiError):
+        W.ModelDir(str(tmp_path)).read("VM_bop/missing.pth")

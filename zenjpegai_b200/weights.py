@@ -147,3 +147,72 @@ class Bundle:
             self.close()
         except Exception:
             pass
+
+
+# ---- model sources (src/model/mod.rs:19-240) --------------------------------------------
+
+MODEL_BETAS = ("0.002", "0.012", "0.075", "0.5")  # beta of each model_id
+COMPONENT_NAMES = ("Y", "UV")
+_OP_DIRS = {0: "VM_sop", 1: "VM_bop", 2: "VM_hop"}  # SOP, BOP, HOP
+
+
+def _beta(model_id):
+    if not 0 <= model_id < len(MODEL_BETAS):
+        raise _lib.ZjaiError(_lib.INVALID_DATA, "model_id out of range")
+    return MODEL_BETAS[model_id]
+
+
+def common_path(model_id, ccs):
+    """The common (entropy-stage and latent networks) checkpoint of component ccs."""
+    return "VM_common_int/%s_%s.pth" % (COMPONENT_NAMES[ccs], _beta(model_id))
+
+
+def synthesis_path(model_id, ccs, op):
+    return "%s/decoder_%s_%s.pth" % (_OP_DIRS[op], COMPONENT_NAMES[ccs], _beta(model_id))
+
+
+def analysis_path(model_id, ccs, op):
+    """SOP streams are encoded with the BOP analysis transform."""
+    return "%s/encoder_%s_%s.pth" % (_OP_DIRS[max(op, 1)], COMPONENT_NAMES[ccs], _beta(model_id))
+
+
+class ModelDir:
+    """Checkpoints in a directory laid out like the reference's models/ directory."""
+
+    def __init__(self, root):
+        self.root = root
+
+    def read(self, rel):
+        import os
+        path = os.path.join(self.root, rel)
+        if not os.path.isfile(path):
+            raise _lib.ZjaiError(_lib.MODEL, "model file `%s` not found" % rel)
+        with open(path, "rb") as f:
+            return f.read()
+
+
+def _params(src, rel):
+    ck = Checkpoint(src.read(rel))
+    try:
+        return ck.params()
+    finally:
+        ck.close()
+
+
+def load_synthesis(engine, src, model_id, op, ccs):
+    """SynthesisPrimary (ccs 0) / SynthesisSecondary (ccs 1) of model `model_id` at operating
+    point `op`, from a ModelDir or a Bundle."""
+    from . import Network, SYN_UV, SYN_Y
+    return Network(engine, SYN_UV if ccs else SYN_Y, op, _params(src, synthesis_path(model_id, ccs, op)))
+
+
+def load_analysis(engine, src, model_id, op, ccs):
+    from . import ANA_UV, ANA_Y, Network
+    return Network(engine, ANA_UV if ccs else ANA_Y, max(op, 1),
+                   _params(src, analysis_path(model_id, ccs, op)))
+
+
+def load_latent(engine, src, model_id, ccs):
+    """The hyper-decoder and (luma) context model of the common checkpoint."""
+    from . import LatentModel
+    return LatentModel(engine, _params(src, common_path(model_id, ccs)))
