@@ -273,6 +273,14 @@ int zjai_bundle_info(const zjai_bundle *b, int *nfiles, int *f16, const char **n
 int zjai_bundle_file(const zjai_bundle *b, int i, const char **path, const void **data,
                      size_t *len);
 
+/* LEF, the luma edge filter (src/filters/lef.rs:100-171, the last post-filter of
+ * filters::apply): luma [h][w] in [0, 255] -> out [h][w], sharpened where channel `channel` of
+ * the luma sigma-index map scale_log [c][sh][sw] (int32, nearest-upsampled to the picture)
+ * crosses the thresholds of model `model_id`; bit-exact with the crate's f32 arithmetic.
+ * out may equal luma. */
+int zjai_lef(zjai_ctx *ctx, const float *luma, int h, int w, const int32_t *scale_log, int c,
+             int sh, int sw, int channel, int model_id, int bit_depth, float *out, int mem);
+
 /* One synthesis tile (src/tools/tiles.rs:26-32 `SynthesisTile`). */
 typedef struct {
   int img_x, img_y, img_w, img_h;

@@ -94,6 +94,8 @@ def _declare(L):
     L.zo_analysis_primary.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f]
     L.zo_analysis_secondary.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f]
     L.zo_analysis_stage.argtypes = [ctypes.POINTER(Ckpt), _i, _i, _i, _f, _i, _i, _i, _f]
+    L.zo_lef.argtypes = [_f, _i, _i, ctypes.POINTER(ctypes.c_int32), _i, _i, _i, _i, _i, _i, _f]
+    L.zo_nearest_index.argtypes = [_i, _i, _i]
     L.zo_hyper_decode.argtypes = [ctypes.POINTER(Ckpt), _f, _i, _i, _i, _i, _i, _f]
     L.zo_context_decompress.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f, _f]
     L.zo_synthesis_tiles.argtypes = [_i] * 6 + [ctypes.POINTER(Tile), _i]
@@ -347,6 +349,22 @@ def analysis_secondary(ck, op, x):
     if lib().zo_analysis_secondary(ctypes.byref(ck.ck), op, _fp(x), h, w, _fp(out)):
         raise ValueError("analysis_secondary")
     return out
+
+
+def lef(luma, scale_log, channel, model_id, bit_depth=8):
+    """LEF sharpening (src/filters/lef.rs:100-171) of luma [h, w] (or [1, h, w])."""
+    y = _c32(luma).reshape(luma.shape[-2:])
+    s = np.ascontiguousarray(scale_log, dtype=np.int32)
+    c, sh, sw = s.shape
+    out = np.empty_like(y)
+    if lib().zo_lef(_fp(y), y.shape[0], y.shape[1], s.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                    c, sh, sw, channel, model_id, bit_depth, _fp(out)):
+        raise ValueError("LEF: model_id / channel / bit depth / extent out of range")
+    return out
+
+
+def nearest_index(i, src, dst):
+    return lib().zo_nearest_index(i, src, dst)
 
 
 def hyper_decode(ck, z, out_h, out_w):

@@ -1411,3 +1411,67 @@ int zo_analyze_tiled(const zo_ckpt *ck, int op, int ccs, const float *x, int h, 
     free(tiles);
     return rc;
 }
+
+/* ======================================================================================= */
+/* LEF luma edge filter (src/filters/lef.rs:67-171)                                         */
+/* ======================================================================================= */
+
+static const int LEF_THR[4][3] = {{600, 1200, 2000}, {800, 1400, 2400}, {1000, 1600, 2800},
+                                  {1200, 2000, 3200}};
+static const float LEF_MAG[4][3] = {{1.10f, 1.13f, 1.16f}, {1.07f, 1.09f, 1.11f},
+                                    {1.03f, 1.04f, 1.05f}, {1.01f, 1.02f, 1.03f}};
+
+/* torch nearest interpolation source index: min(floor(dst * (src / dst)), src - 1), f32 */
+int zo_nearest_index(int i, int src, int dst) {
+    const float scale = (float)src / (float)dst;
+    const int v = (int)floorf((float)i * scale);
+    return v < src - 1 ? v : src - 1;
+}
+
+static float clamp01(float v) { return v < 0.f ? 0.f : v > 1.f ? 1.f : v; }
+
+/* LEF `sharpen`: luma [h][w] in [0, 255] filtered into out (out != luma); scale_log [c][sh][sw]
+ * int32. Returns -1 for the inputs the crate rejects. */
+int zo_lef(const float *luma, int h, int w, const int32_t *scale_log, int c, int sh, int sw,
+           int channel, int model_id, int bit_depth, float *out) {
+    if (model_id < 0 || model_id > 3 || channel < 0 || channel >= c) return -1;
+    if (h <= 0 || w <= 0 || sh <= 0 || sw <= 0 || bit_depth < 1 || bit_depth > 16) return -1;
+    const float range = 255.f, outer = 5.f / 64.f, centre = 24.f / 64.f;
+    const int32_t *region = scale_log + (size_t)channel * sh * sw;
+    float *x = (float *)malloc(sizeof(float) * (size_t)h * w);
+    for (size_t i = 0; i < (size_t)h * w; i++) x[i] = luma[i] / range;
+    for (int y = 0; y < h; y++) {
+        const float *cur = x + (size_t)y * w;
+        float *o = out + (size_t)y * w;
+        if (y == 0 || y + 1 == h || w < 3) {
+            for (int i = 0; i < w; i++) o[i] = clamp01(cur[i]) * range;
+            continue;
+        }
+        const float *up = cur - w, *down = cur + w;
+        const int32_t *rrow = region + (size_t)zo_nearest_index(y, sh, h) * sw;
+        o[0] = clamp01(cur[0]) * range;
+        o[w - 1] = clamp01(cur[w - 1]) * range;
+        for (int i = 1; i < w - 1; i++) {
+            const int s = rrow[zo_nearest_index(i, sw, w)];
+            const int *t = LEF_THR[model_id];
+            const float g = s >= t[2] ? LEF_MAG[model_id][2] : s >= t[1] ? LEF_MAG[model_id][1]
+                            : s >= t[0] ? LEF_MAG[model_id][0] : 1.f;
+            float acc = 0.f;
+            acc = fmaf(up[i - 1], outer, acc);
+            acc = fmaf(up[i], outer, acc);
+            acc = fmaf(up[i + 1], outer, acc);
+            acc = fmaf(cur[i - 1], outer, acc);
+            acc = fmaf(cur[i], centre, acc);
+            acc = fmaf(cur[i + 1], outer, acc);
+            acc = fmaf(down[i - 1], outer, acc);
+            acc = fmaf(down[i], outer, acc);
+            acc = fmaf(down[i + 1], outer, acc);
+            const float blur = clamp01(acc);
+            const float diff = (cur[i] - blur) * g;
+            o[i] = clamp01(blur + diff) * range;
+        }
+    }
+    free(x);
+    return 0;
+}
+

@@ -205,6 +205,13 @@ int zo_context_decompress(const zo_ckpt *ck, int c, const float *residual, int h
 int zo_analyze_tiled(const zo_ckpt *ck, int op, int ccs, const float *x, int h, int w,
                      float *out);
 
+/* LEF (src/filters/lef.rs:100-171): luma [h][w] -> out, steered by channel `channel` of the
+ * luma sigma-index map scale_log [c][sh][sw]; -1 on the inputs the crate rejects. */
+int zo_lef(const float *luma, int h, int w, const int32_t *scale_log, int c, int sh, int sw,
+           int channel, int model_id, int bit_depth, float *out);
+/* torch nearest-neighbour source index (lef.rs:67-74) */
+int zo_nearest_index(int i, int src, int dst);
+
 #ifdef __cplusplus
 }
 #endif

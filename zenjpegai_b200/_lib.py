@@ -121,6 +121,7 @@ def lib():
                                    ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t)]
     L.zjai_bundle_file.argtypes = [_vp, _i, ctypes.POINTER(ctypes.c_char_p),
                                    ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t)]
+    L.zjai_lef.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _i]
     L.zjai_hyper_decode.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _i]
     L.zjai_context_decompress.argtypes = [_vp, _vp, _i, _i, _vp, _vp, _i]
     L.zjai_reconstruct_latent.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _vp, _i]
