@@ -155,3 +155,18 @@ def test_analysis_stages_compose(op, secondary):
         t = zo.analysis_stage(ck, zo.OPS[op], secondary, stage, t, h, w)
     whole = (zo.analysis_secondary if secondary else zo.analysis_primary)(ck, zo.OPS[op], x)
     assert np.array_equal(t, whole)
+
+
+def test_lef_reference_unit_cases():
+    """src/filters/lef.rs tests: torch's nearest indices for 56 -> 888 rows and 3 -> 3, a flat
+    picture kept, a border sample above the range clamped, out-of-range indices rejected."""
+    assert [zo.nearest_index(i, 56, 888) for i in (0, 15, 16, 887)] == [0, 0, 1, 55]
+    assert [zo.nearest_index(i, 3, 3) for i in range(3)] == [0, 1, 2]
+    y = np.full((4, 4), 128.0, np.float32)
+    y[0, 0] = 300.0
+    s = np.array([[[5000]]], np.int32)
+    out = zo.lef(y, s, 0, 0)
+    assert out[0, 0] == 255.0 and abs(out[3, 3] - 128.0) < 1e-4
+    for bad in ((1, 0), (0, 4)):
+        with pytest.raises(ValueError):
+            zo.lef(y, s, *bad)
