@@ -55,8 +55,10 @@ enum { ZJAI_SOP = 0, ZJAI_BOP = 1, ZJAI_HOP = 2 };
 /* Network kinds: synthesis primary / secondary (src/model/synthesis.rs), analysis primary /
  * secondary (src/model/analysis.rs), and the latent-domain float networks of one component's
  * common modules (src/model/common.rs:34-131): the hyper-decoder (hyper_decoder.rs) and, when
- * the checkpoint holds it, the context model (mcm.rs). */
-enum { ZJAI_SYN_Y = 0, ZJAI_SYN_UV = 1, ZJAI_ANA_Y = 2, ZJAI_ANA_UV = 3, ZJAI_LATENT = 5 };
+ * the checkpoint holds it, the context model (mcm.rs); one network of the eICCI post-filter bank
+ * (src/model/icci.rs `IcciNet`). */
+enum { ZJAI_SYN_Y = 0, ZJAI_SYN_UV = 1, ZJAI_ANA_Y = 2, ZJAI_ANA_UV = 3, ZJAI_LATENT = 5,
+       ZJAI_ICCI = 6 };
 
 /* Epilogue activations of the layer entry points. ZJAI_ACT_LEAKY is LeakyReLU(0.01), which
  * the reference does not have (only relu / relu6, src/nn/fast/layers.rs:174-186); it exists
@@ -280,6 +282,18 @@ int zjai_bundle_file(const zjai_bundle *b, int i, const char **path, const void 
  * out may equal luma. */
 int zjai_lef(zjai_ctx *ctx, const float *luma, int h, int w, const int32_t *scale_log, int c,
              int sh, int sw, int channel, int model_id, int bit_depth, float *out, int mem);
+
+/* The eICCI post-filter (src/filters/icci.rs:175-325) of a 4:4:4 picture, in place on its planes
+ * y, u, v [h][w] in [0, 255]: normalised, then per filter tile (tile_size / overlap as signalled;
+ * tile_size 0: one tile; tiles in raster order, each reading the cores its predecessors wrote,
+ * like the crate) two Haar levels per plane, the luma network `net_y` and / or the chroma network
+ * `net_uv` (ZJAI_ICCI networks of the bank the header selects; NULL: that part not filtered;
+ * use_u / use_v: the chroma planes corrected), inverse transform, core written back; finally
+ * clamped and scaled back. 4:2:0 / 4:2:2 sources are up-sampled to 4:4:4 by the caller (the
+ * crate's `to_444_`); eICCI is not signalled for 4:2:0. */
+int zjai_icci_filter(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, int use_u, int use_v,
+                     float *y, float *u, float *v, int h, int w, int tile_size, int overlap,
+                     int mem);
 
 /* One synthesis tile (src/tools/tiles.rs:26-32 `SynthesisTile`). */
 typedef struct {

@@ -96,6 +96,9 @@ def _declare(L):
     L.zo_analysis_stage.argtypes = [ctypes.POINTER(Ckpt), _i, _i, _i, _f, _i, _i, _i, _f]
     L.zo_lef.argtypes = [_f, _i, _i, ctypes.POINTER(ctypes.c_int32), _i, _i, _i, _i, _i, _i, _f]
     L.zo_nearest_index.argtypes = [_i, _i, _i]
+    L.zo_icci_filter.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _i, _i, _f, _f, _f, _i, _i, _i, _i]
+    L.zo_dwt2_block.argtypes = [_f, _f]
+    L.zo_idwt2_block.argtypes = [_f, _f]
     L.zo_hyper_decode.argtypes = [ctypes.POINTER(Ckpt), _f, _i, _i, _i, _i, _i, _f]
     L.zo_context_decompress.argtypes = [ctypes.POINTER(Ckpt), _i, _f, _i, _i, _f, _f]
     L.zo_synthesis_tiles.argtypes = [_i] * 6 + [ctypes.POINTER(Tile), _i]
@@ -365,6 +368,30 @@ def lef(luma, scale_log, channel, model_id, bit_depth=8):
 
 def nearest_index(i, src, dst):
     return lib().zo_nearest_index(i, src, dst)
+
+
+def icci_filter(ck_y, ck_uv, use_u, use_v, y, u, v, tile=0, overlap=0):
+    """eICCI (src/filters/icci.rs) of a 4:4:4 picture: filtered copies of y, u, v [h, w]."""
+    y, u, v = (np.array(_c32(p), copy=True) for p in (y, u, v))
+    h, w = y.shape
+    r = lib().zo_icci_filter(ctypes.byref(ck_y.ck) if ck_y is not None else None,
+                             ctypes.byref(ck_uv.ck) if ck_uv is not None else None,
+                             int(use_u), int(use_v), _fp(y), _fp(u), _fp(v), h, w, tile, overlap)
+    if r:
+        raise ValueError("eICCI: malformed tiling")
+    return y, u, v
+
+
+def dwt2_block(p):
+    out = np.empty(16, np.float32)
+    lib().zo_dwt2_block(_fp(_c32(p).reshape(16)), _fp(out))
+    return out
+
+
+def idwt2_block(s):
+    out = np.empty(16, np.float32)
+    lib().zo_idwt2_block(_fp(_c32(s).reshape(16)), _fp(out))
+    return out.reshape(4, 4)
 
 
 def hyper_decode(ck, z, out_h, out_w):

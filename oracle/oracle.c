@@ -1475,3 +1475,269 @@ int zo_lef(const float *luma, int h, int w, const int32_t *scale_log, int c, int
     return 0;
 }
 
+
+/* ======================================================================================= */
+/* eICCI post-filter (src/model/icci.rs, src/filters/icci.rs), 4:4:4 pictures               */
+/* ======================================================================================= */
+
+#define ICCI_NF 48
+#define ICCI_BANDS 16
+
+static double ck_scalar(const zo_ckpt *ck, const char *name) {
+    const zo_param *p = find(ck, name);
+    if (!p || p->ndim > 1 || (p->ndim == 1 && p->shape[0] != 1)) ZO_FAIL(name);
+    return (double)p->data[0];
+}
+
+/* folded_conv (icci.rs:99-125): conv `prefix` then the per-channel affine map (a, shift):
+ * w' = w * a, b' = b * a + shift in f64, rounded once; the conv runs in f32 */
+typedef struct {
+    int cin, cout, kh, kw;
+    float *w, *b;
+} FConv;
+
+static FConv fold(const zo_ckpt *ck, const char *prefix, int cin, int cout, int kh, int kw,
+                  const double *a, const double *shift) {
+    FConv f = {cin, cout, kh, kw, NULL, NULL};
+    const float *w = need(ck, prefix, "weight", cout, cin, kh, kw);
+    const float *b = need(ck, prefix, "bias", cout, -1, -1, -1);
+    const int per = cin * kh * kw;
+    f.w = (float *)malloc(sizeof(float) * cout * per);
+    f.b = (float *)malloc(sizeof(float) * cout);
+    for (int o = 0; o < cout; o++) {
+        for (int i = 0; i < per; i++) f.w[o * per + i] = (float)((double)w[o * per + i] * a[o]);
+        f.b[o] = (float)((double)b[o] * a[o] + shift[o]);
+    }
+    return f;
+}
+
+/* batch_norm (icci.rs:64-87): (a s, (beta - mean a) s), a = gamma / sqrt(var + 1e-5) */
+static void bn_affine(const zo_ckpt *ck, const char *prefix, double s, double *a, double *sh) {
+    const float *g = need(ck, prefix, "weight", ICCI_NF, -1, -1, -1);
+    const float *be = need(ck, prefix, "bias", ICCI_NF, -1, -1, -1);
+    const float *m = need(ck, prefix, "running_mean", ICCI_NF, -1, -1, -1);
+    const float *v = need(ck, prefix, "running_var", ICCI_NF, -1, -1, -1);
+    for (int c = 0; c < ICCI_NF; c++) {
+        const double k = (double)g[c] / sqrt((double)v[c] + 1e-5);
+        a[c] = k * s;
+        sh[c] = ((double)be[c] - (double)m[c] * k) * s;
+    }
+}
+
+static T fconv(const FConv *f, const T *x) {
+    T o = t_new(f->cout, x->h, x->w);
+    if (zo_conv2d(x->d, x->c, x->h, x->w, f->w, f->b, f->cout, f->kh, f->kw, 1, f->kh / 2,
+                  f->kw / 2, 1, NULL, o.d))
+        ZO_FAIL("icci conv");
+    return o;
+}
+
+static void ffree(FConv *f) {
+    free(f->w);
+    free(f->b);
+}
+
+/* Trunk::forward (icci.rs:168-178): relu(first(x)), then f += conv2(relu(conv1(f))) */
+static T icci_trunk(const zo_ckpt *ck, const T *x, const char *first, const char *bn,
+                    const char *hidden, int blocks) {
+    double a[ICCI_NF], sh[ICCI_NF];
+    char n1[128], n2[128];
+    bn_affine(ck, bn, 1.0, a, sh);
+    FConv f0 = fold(ck, first, 3 * ICCI_BANDS, ICCI_NF, 3, 3, a, sh);
+    T f = fconv(&f0, x);
+    ffree(&f0);
+    zo_relu(f.d, t_len(&f));
+    for (int i = 0; i < blocks; i++) {
+        snprintf(n1, sizeof n1, "%s.%d.scale", hidden, i);
+        const double s = ck_scalar(ck, n1);
+        double a2[ICCI_NF], sh2[ICCI_NF];
+        snprintf(n1, sizeof n1, "%s.%d.BN1", hidden, i);
+        bn_affine(ck, n1, 1.0, a, sh);
+        snprintf(n2, sizeof n2, "%s.%d.BN2", hidden, i);
+        bn_affine(ck, n2, s, a2, sh2);
+        snprintf(n1, sizeof n1, "%s.%d.conv1", hidden, i);
+        snprintf(n2, sizeof n2, "%s.%d.conv2", hidden, i);
+        FConv c1 = fold(ck, n1, ICCI_NF, ICCI_NF, 1, 3, a, sh);
+        FConv c2 = fold(ck, n2, ICCI_NF, ICCI_NF, 3, 1, a2, sh2);
+        T o = fconv(&c1, &f);
+        zo_relu(o.d, t_len(&o));
+        T r = fconv(&c2, &o);
+        zo_add(f.d, r.d, t_len(&f));
+        t_free(&o);
+        t_free(&r);
+        ffree(&c1);
+        ffree(&c2);
+    }
+    return f;
+}
+
+/* the last conv of a plane: 48 -> 16 sub-band corrections times the plane's scale */
+static T icci_last(const zo_ckpt *ck, const T *f, const char *conv, const char *scale) {
+    double a[ICCI_BANDS], sh[ICCI_BANDS];
+    const double s = ck_scalar(ck, scale);
+    for (int i = 0; i < ICCI_BANDS; i++) {
+        a[i] = s;
+        sh[i] = 0.0;
+    }
+    FConv c = fold(ck, conv, ICCI_NF, ICCI_BANDS, 3, 3, a, sh);
+    T o = fconv(&c, f);
+    ffree(&c);
+    return o;
+}
+
+static void haar4(float x1, float x2, float x3, float x4, float o[4]) {
+    o[0] = x1 + x2 + x3 + x4;
+    o[1] = -x1 - x2 + x3 + x4;
+    o[2] = -x1 + x2 - x3 + x4;
+    o[3] = x1 - x2 - x3 + x4;
+}
+static void ihaar4(float x1, float x2, float x3, float x4, float o[4]) {
+    o[0] = x1 - x2 - x3 + x4;
+    o[1] = x1 - x2 + x3 - x4;
+    o[2] = x1 + x2 - x3 - x4;
+    o[3] = x1 + x2 + x3 + x4;
+}
+
+/* dwt2_block (icci.rs:326-360): two Haar levels of a 4 x 4 block p[row][col] */
+void zo_dwt2_block(const float p[16], float out[16]) {
+    float l1[2][2][4];
+    for (int by = 0; by < 2; by++)
+        for (int bx = 0; bx < 2; bx++) {
+            const int r = 2 * by, c = 2 * bx;
+            haar4(p[r * 4 + c] / 2.f, p[(r + 1) * 4 + c] / 2.f, p[r * 4 + c + 1] / 2.f,
+                  p[(r + 1) * 4 + c + 1] / 2.f, l1[by][bx]);
+        }
+    for (int k = 0; k < 4; k++)
+        haar4(l1[0][0][k] / 2.f, l1[1][0][k] / 2.f, l1[0][1][k] / 2.f, l1[1][1][k] / 2.f,
+              out + 4 * k);
+}
+
+/* idwt2_block (icci.rs:363-402) */
+void zo_idwt2_block(const float s[16], float out[16]) {
+    float q[4][2][2];
+    for (int i = 0; i < 4; i++) {
+        float r[4];
+        ihaar4(s[4 * i] / 2.f, s[4 * i + 1] / 2.f, s[4 * i + 2] / 2.f, s[4 * i + 3] / 2.f, r);
+        q[i][0][0] = r[0];
+        q[i][0][1] = r[2];
+        q[i][1][0] = r[1];
+        q[i][1][1] = r[3];
+    }
+    for (int dy = 0; dy < 2; dy++)
+        for (int dx = 0; dx < 2; dx++) {
+            float r[4];
+            ihaar4(q[0][dy][dx] / 2.f, q[1][dy][dx] / 2.f, q[2][dy][dx] / 2.f,
+                   q[3][dy][dx] / 2.f, r);
+            out[(2 * dy) * 4 + 2 * dx] = r[0];
+            out[(2 * dy + 1) * 4 + 2 * dx] = r[1];
+            out[(2 * dy) * 4 + 2 * dx + 1] = r[2];
+            out[(2 * dy + 1) * 4 + 2 * dx + 1] = r[3];
+        }
+}
+
+/* axis of the filter tiling (filters/icci.rs:68-96): starts / lengths; -1 when malformed */
+#define ICCI_MIN_TILE 176
+static int icci_axis(int len, int tile, int overlap, int *pos, int *sz, int max) {
+    tile = tile < len ? tile : len;
+    if (tile <= overlap || len <= overlap) return -1;
+    int n = 0;
+    for (int p = 0; p < len - overlap; p += tile - overlap) {
+        if (n >= max) return -1;
+        pos[n] = p;
+        sz[n] = tile < len - p ? tile : len - p;
+        n++;
+    }
+    if (sz[n - 1] < ICCI_MIN_TILE) {
+        if (n < 2 || sz[n - 2] <= ICCI_MIN_TILE + overlap) return -1;
+        sz[n - 2] -= ICCI_MIN_TILE;
+        pos[n - 1] -= ICCI_MIN_TILE;
+        sz[n - 1] += ICCI_MIN_TILE;
+    }
+    return n;
+}
+
+/* The eICCI filter (filters/icci.rs:175-325) of a 4:4:4 picture in place: planes y, u, v
+ * [h][w] in [0, 255]; ck_y filters luma, ck_uv the chroma planes selected by use_u / use_v
+ * (NULL: not filtered); tile_size 0: one tile. Tiles in raster order, each reading the cores
+ * its predecessors wrote. Returns -1 for a malformed tiling. */
+int zo_icci_filter(const zo_ckpt *ck_y, const zo_ckpt *ck_uv, int use_u, int use_v, float *y,
+                   float *u, float *v, int h, int w, int tile_size, int overlap) {
+    enum { MAXT = 256 };
+    int ry[MAXT], rh[MAXT], cx[MAXT], cw[MAXT], nr = 1, nc = 1;
+    if (h <= 0 || w <= 0) return -1;
+    if (tile_size > 0) {
+        nr = icci_axis(h, tile_size, overlap, ry, rh, MAXT);
+        nc = icci_axis(w, tile_size, overlap, cx, cw, MAXT);
+        if (nr < 0 || nc < 0) return -1;
+    } else {
+        ry[0] = cx[0] = 0;
+        rh[0] = h;
+        cw[0] = w;
+        overlap = 0;
+    }
+    const int half = overlap / 2;
+    float *planes[3] = {y, u, v};
+    const size_t n = (size_t)h * w;
+    for (int p = 0; p < 3; p++)
+        for (size_t i = 0; i < n; i++) planes[p][i] = planes[p][i] / 255.f;
+    for (int ti = 0; ti < nr; ti++)
+        for (int tj = 0; tj < nc; tj++) {
+            const int x0 = cx[tj], y0 = ry[ti], tw = cw[tj], th = rh[ti];
+            const int left = x0 == 0 ? 0 : half, top = y0 == 0 ? 0 : half;
+            const int right = x0 + tw >= w ? 0 : half, bottom = y0 + th >= h ? 0 : half;
+            if (tw <= left + right || th <= top + bottom) return -1;
+            if (!ck_y && !ck_uv) continue;
+            const int bh = cdiv(th, 4), bw = cdiv(tw, 4);
+            T in = t_new(3 * ICCI_BANDS, bh, bw);
+            for (int p = 0; p < 3; p++)
+                for (int by = 0; by < bh; by++)
+                    for (int bx = 0; bx < bw; bx++) {
+                        float blk[16], o[16];
+                        for (int r = 0; r < 4; r++)
+                            for (int c = 0; c < 4; c++) {
+                                const int sy = y0 + (4 * by + r < th - 1 ? 4 * by + r : th - 1);
+                                const int sx = x0 + (4 * bx + c < tw - 1 ? 4 * bx + c : tw - 1);
+                                blk[r * 4 + c] = planes[p][(size_t)sy * w + sx];
+                            }
+                        zo_dwt2_block(blk, o);
+                        for (int k = 0; k < 16; k++)
+                            in.d[((size_t)(p * 16 + k) * bh + by) * bw + bx] = o[k];
+                    }
+            T corr[3] = {{0, 0, 0, NULL}, {0, 0, 0, NULL}, {0, 0, 0, NULL}};
+            if (ck_y) {
+                T f = icci_trunk(ck_y, &in, "conv_first_Y", "BNY", "hidden_layer_Y", 2);
+                corr[0] = icci_last(ck_y, &f, "conv_last_Y", "scaleY");
+                t_free(&f);
+            }
+            if (ck_uv && (use_u || use_v)) {
+                T f = icci_trunk(ck_uv, &in, "conv_firstUV", "BNUV", "hidden_layer_UV", 4);
+                if (use_u) corr[1] = icci_last(ck_uv, &f, "conv_last_u", "scaleU");
+                if (use_v) corr[2] = icci_last(ck_uv, &f, "conv_last_v", "scaleV");
+                t_free(&f);
+            }
+            for (int p = 0; p < 3; p++) {
+                if (!corr[p].d) continue;
+                for (int by = 0; by < bh; by++)
+                    for (int bx = 0; bx < bw; bx++) {
+                        float s[16], o[16];
+                        for (int k = 0; k < 16; k++) {
+                            const size_t i = ((size_t)k * bh + by) * bw + bx;
+                            s[k] = corr[p].d[i] + in.d[((size_t)(p * 16 + k) * bh + by) * bw + bx];
+                        }
+                        zo_idwt2_block(s, o);
+                        for (int r = 0; r < 4; r++)
+                            for (int c = 0; c < 4; c++) {
+                                const int fy = 4 * by + r, fx = 4 * bx + c;  /* padded tile */
+                                if (fy < top || fy >= th - bottom || fx < left || fx >= tw - right)
+                                    continue;
+                                planes[p][(size_t)(y0 + fy) * w + x0 + fx] = o[r * 4 + c];
+                            }
+                    }
+                t_free(&corr[p]);
+            }
+            t_free(&in);
+        }
+    for (int p = 0; p < 3; p++)
+        for (size_t i = 0; i < n; i++) planes[p][i] = clamp01(planes[p][i]) * 255.f;
+    return 0;
+}

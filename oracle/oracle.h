@@ -212,6 +212,14 @@ int zo_lef(const float *luma, int h, int w, const int32_t *scale_log, int c, int
 /* torch nearest-neighbour source index (lef.rs:67-74) */
 int zo_nearest_index(int i, int src, int dst);
 
+/* eICCI (src/filters/icci.rs:175-325, network src/model/icci.rs) of a 4:4:4 picture in place:
+ * planes y, u, v [h][w] in [0, 255]; ck_y / ck_uv the networks for luma / chroma (NULL: plane
+ * not filtered), use_u / use_v the chroma planes filtered; tile_size 0: one tile. */
+int zo_icci_filter(const zo_ckpt *ck_y, const zo_ckpt *ck_uv, int use_u, int use_v, float *y,
+                   float *u, float *v, int h, int w, int tile_size, int overlap);
+void zo_dwt2_block(const float p[16], float out[16]);
+void zo_idwt2_block(const float s[16], float out[16]);
+
 #ifdef __cplusplus
 }
 #endif

@@ -291,6 +291,45 @@ def analysis_params(op, seed):
             make_params(analysis_spec(op, True), seed, "AUV/"))
 
 
+def icci_params(seed):
+    """One eICCI network (`IcciNet::load`, src/model/icci.rs:181-212): both trunks (48
+    features; luma 2 residual blocks, chroma 4), batch norms with running statistics, the
+    learned residual scales and the three last convs."""
+    out = {}
+    nf, bands = 48, 16
+
+    def conv(name, cout, cin, kh, kw, gain=1.0):
+        fan = cin * kh * kw
+        out[name + ".weight"] = normal(seed, "IC/" + name, (cout, cin, kh, kw),
+                                       std=float(np.sqrt(gain / fan)))
+        out[name + ".bias"] = normal(seed, "IC/" + name + ".b", (cout,), std=0.01)
+
+    def bn(name):
+        out[name + ".weight"] = normal(seed, "IC/" + name + ".g", (nf,), std=0.1, mean=1.0)
+        out[name + ".bias"] = normal(seed, "IC/" + name + ".be", (nf,), std=0.05)
+        out[name + ".running_mean"] = normal(seed, "IC/" + name + ".m", (nf,), std=0.05)
+        out[name + ".running_var"] = uniform(seed, "IC/" + name + ".v", (nf,), 0.5, 1.5)
+
+    def scalar(name, lo, hi):
+        out[name] = uniform(seed, "IC/" + name, (1,), lo, hi)
+
+    for first, bnn, hidden, blocks in (("conv_first_Y", "BNY", "hidden_layer_Y", 2),
+                                       ("conv_firstUV", "BNUV", "hidden_layer_UV", 4)):
+        conv(first, nf, 3 * bands, 3, 3, 2.0)
+        bn(bnn)
+        for i in range(blocks):
+            p = "%s.%d" % (hidden, i)
+            conv(p + ".conv1", nf, nf, 1, 3, 2.0)
+            conv(p + ".conv2", nf, nf, 3, 1, 1.0)
+            bn(p + ".BN1")
+            bn(p + ".BN2")
+            scalar(p + ".scale", 0.1, 0.5)
+    for last, sc in (("conv_last_Y", "scaleY"), ("conv_last_u", "scaleU"), ("conv_last_v", "scaleV")):
+        conv(last, bands, nf, 3, 3, 1.0)
+        scalar(sc, 0.01, 0.05)
+    return out
+
+
 def latent_params(seed, chs=160, context=True):
     """A component's latent networks (hyper-decoder, optional context model)."""
     return make_params(latent_spec(chs, context), seed, "L%d/" % chs)

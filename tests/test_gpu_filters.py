@@ -62,3 +62,77 @@ def test_lef_device_and_in_place_4k(eng):
     lef(eng, yt, st, 0, 2, out=yt)  # in place
     eng.sync()
     assert np.array_equal(yt.cpu().numpy(), want)
+
+
+# ---- eICCI -----------------------------------------------------------------------------------
+
+def _picture(seed, h, w):
+    rng = np.random.default_rng(seed)
+    base = rng.uniform(20.0, 235.0, (3, h // 8 + 2, w // 8 + 2)).astype(np.float32)
+    big = np.repeat(np.repeat(base, 8, axis=1), 8, axis=2)[:, :h, :w]
+    return [np.ascontiguousarray(big[i] + rng.normal(0, 6, (h, w)).astype(np.float32))
+            for i in range(3)]
+
+
+def _check(got, want, src):
+    """The corrections (filtered minus input) within 5e-3 relative L2 of the oracle's; planes
+    the filter leaves alone bit-exact."""
+    for g, w_, s in zip(got, want, src):
+        dw = w_.astype(np.float64) - np.clip(s, 0, 255)
+        if np.abs(dw).max() < 1e-3:
+            assert np.array_equal(g, w_)
+        else:
+            dg = g.astype(np.float64) - np.clip(s, 0, 255)
+            assert np.linalg.norm(dg - dw) / np.linalg.norm(dw) < 5e-3
+            assert np.abs(g - w_).max() < 0.05
+
+
+@pytest.mark.parametrize("h,w,tile,overlap,sel", [
+    (37, 50, 0, 0, (True, True, True, True)),
+    (96, 128, 0, 0, (True, False, False, False)),
+    (64, 80, 0, 0, (False, True, False, True)),
+    (400, 600, 256, 32, (True, True, True, True)),
+])
+def test_icci_against_oracle(eng, h, w, tile, overlap, sel):
+    import synthetic as syn
+    from zenjpegai_b200 import filters
+    use_y, use_uv, use_u, use_v = sel
+    py, puv = syn.icci_params(5), syn.icci_params(6)
+    ny = filters.icci_network(eng, py) if use_y else None
+    nuv = filters.icci_network(eng, puv) if use_uv else None
+    try:
+        src = _picture(h + w, h, w)
+        got = [p.copy() for p in src]
+        filters.icci(eng, ny, nuv, *got, use_u=use_u, use_v=use_v, tile=tile, overlap=overlap)
+        want = zo.icci_filter(zo.Checkpoint(py) if use_y else None,
+                              zo.Checkpoint(puv) if use_uv else None, use_u, use_v, *src,
+                              tile=tile, overlap=overlap)
+        _check(got, want, src)
+    finally:
+        for n in (ny, nuv):
+            if n:
+                n.close()
+
+
+def test_icci_device_tensors_and_errors(eng):
+    import torch
+    import synthetic as syn
+    import zenjpegai_b200 as zj
+    from zenjpegai_b200 import filters
+    p = syn.icci_params(7)
+    net = filters.icci_network(eng, p)
+    try:
+        src = _picture(3, 72, 88)
+        host = [s.copy() for s in src]
+        filters.icci(eng, net, net, *host)
+        dev = [torch.from_numpy(s).cuda() for s in src]
+        filters.icci(eng, net, net, *dev)
+        eng.sync()
+        for a, b in zip(dev, host):
+            assert np.array_equal(a.cpu().numpy(), b)
+        with pytest.raises(zj.ZjaiError):  # a last tile below the minimum with no room to grow
+            filters.icci(eng, net, net, *[s.copy() for s in src], tile=64, overlap=8)
+    finally:
+        net.close()
+    with pytest.raises(zj.ZjaiError):
+        filters.icci_network(eng, {k: v for k, v in p.items() if not k.startswith("BNY")})

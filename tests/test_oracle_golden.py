@@ -170,3 +170,22 @@ def test_lef_reference_unit_cases():
     for bad in ((1, 0), (0, 4)):
         with pytest.raises(ValueError):
             zo.lef(y, s, *bad)
+
+
+def test_icci_transforms_and_tiling():
+    """The two-level Haar transform pair inverts to f32 rounding, and the oracle's filter
+    tiling follows src/filters/icci.rs:68-96 (a short last tile takes 176 samples from its
+    neighbour; impossible layouts are rejected)."""
+    rng = np.random.default_rng(2)
+    for _ in range(20):
+        b = rng.uniform(0, 1, 16).astype(np.float32)
+        assert np.abs(zo.idwt2_block(zo.dwt2_block(b)).reshape(16) - b).max() < 1e-6
+    flat = np.full(16, 0.5, np.float32)
+    bands = zo.dwt2_block(flat)
+    assert bands[0] == 2.0 * 0.5 * 2.0 and np.all(bands[1:] == 0)  # DC only, scaled by 2 per level
+    import synthetic as syn
+    ck = zo.Checkpoint(syn.icci_params(1))
+    y = u = v = np.full((200, 500), 100.0, np.float32)
+    with pytest.raises(ValueError):
+        zo.icci_filter(ck, ck, 1, 1, y, u, v, tile=64, overlap=8)
+    zo.icci_filter(ck, None, 0, 0, y, u, v, tile=256, overlap=32)

@@ -27,11 +27,11 @@ import numpy as np
 
 from . import _lib
 from ._lib import (ACT_LEAKY, ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SIGMOID, ANA_UV, ANA_Y, BOP,
-                   HOP, LATENT, SOP, SYN_UV, SYN_Y, ZjaiError, check)
+                   HOP, ICCI, LATENT, SOP, SYN_UV, SYN_Y, ZjaiError, check)
 
 __all__ = ["Engine", "ZjaiError", "SOP", "BOP", "HOP", "SYN_Y", "SYN_UV", "ANA_Y", "ANA_UV",
            "ACT_NONE", "ACT_RELU", "ACT_LEAKY", "ACT_SIGMOID", "ACT_RELU6", "Network", "Stage",
-           "LatentModel", "LATENT",
+           "LatentModel", "LATENT", "ICCI",
            "synthesis_tiles", "synth_out_size", "version"]
 
 _lib.lib()  # load now: importing the package without its CUDA library is an error

@@ -20,6 +20,7 @@ MEM_HOST, MEM_DEVICE = 0, 1
 SOP, BOP, HOP = 0, 1, 2
 SYN_Y, SYN_UV, ANA_Y, ANA_UV = 0, 1, 2, 3
 LATENT = 5
+ICCI = 6
 ACT_NONE, ACT_RELU, ACT_LEAKY, ACT_SIGMOID, ACT_RELU6 = range(5)
 
 
@@ -121,6 +122,7 @@ def lib():
                                    ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t)]
     L.zjai_bundle_file.argtypes = [_vp, _i, ctypes.POINTER(ctypes.c_char_p),
                                    ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t)]
+    L.zjai_icci_filter.argtypes = [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i]
     L.zjai_lef.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _i]
     L.zjai_hyper_decode.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _i]
     L.zjai_context_decompress.argtypes = [_vp, _vp, _i, _i, _vp, _vp, _i]

@@ -162,6 +162,86 @@ struct Loader {
   }
 };
 
+// eICCI (src/model/icci.rs:64-212): conv `prefix` followed by a per-output-channel affine map
+// (an inference-mode batch norm and / or a learned scale), folded into the weights and bias in
+// f64 and rounded once, like the crate's `folded_conv`; packed under `store`.
+static int icci_fold(Loader& L, const std::string& prefix, const std::string& store, int cin,
+                     int cout, int kh, int kw, const std::vector<double>& a,
+                     const std::vector<double>& shift) {
+  const float *w, *b;
+  ZJAI_TRY(L.get(prefix + ".weight", {cout, cin, kh, kw}, &w));
+  ZJAI_TRY(L.get(prefix + ".bias", {cout}, &b));
+  const size_t per = (size_t)cin * kh * kw;
+  std::vector<float> wf((size_t)cout * per), bf(cout);
+  for (int o = 0; o < cout; ++o) {
+    for (size_t i = 0; i < per; ++i) wf[o * per + i] = (float)((double)w[o * per + i] * a[o]);
+    bf[o] = (float)((double)b[o] * a[o] + shift[o]);
+  }
+  ConvLayer C;
+  ZJAI_TRY(pack_conv(L.net->ctx, &C, wf.data(), bf.data(), cin, cout, kh, kw, 1, kh / 2, kw / 2,
+                     1, nullptr, 1));
+  L.net->convs[store] = C;
+  return ZJAI_OK;
+}
+
+// a scalar parameter ([] or [1])
+static int icci_scalar(Loader& L, const std::string& name, double* out) {
+  auto it = L.byname.find(name);
+  if (it == L.byname.end()) return fail(ZJAI_MODEL, name + ": missing");
+  const zjai_param* p = it->second;
+  if (p->ndim > 1 || (p->ndim == 1 && p->shape[0] != 1) || !p->data)
+    return fail(ZJAI_MODEL, name + ": not a scalar");
+  *out = (double)p->data[0];
+  return ZJAI_OK;
+}
+
+// batch_norm (icci.rs:64-87): (a s, (beta - mean a) s) with a = gamma / sqrt(var + 1e-5)
+static int icci_bn(Loader& L, const std::string& prefix, int ch, double s, std::vector<double>* a,
+                   std::vector<double>* shift) {
+  const float *g, *be, *m, *v;
+  ZJAI_TRY(L.get(prefix + ".weight", {ch}, &g));
+  ZJAI_TRY(L.get(prefix + ".bias", {ch}, &be));
+  ZJAI_TRY(L.get(prefix + ".running_mean", {ch}, &m));
+  ZJAI_TRY(L.get(prefix + ".running_var", {ch}, &v));
+  a->resize(ch);
+  shift->resize(ch);
+  for (int c = 0; c < ch; ++c) {
+    const double k = (double)g[c] / std::sqrt((double)v[c] + 1e-5);
+    (*a)[c] = k * s;
+    (*shift)[c] = ((double)be[c] - (double)m[c] * k) * s;
+  }
+  return ZJAI_OK;
+}
+
+// Trunk::load (icci.rs:137-166): packed as "<tag>.first", "<tag>.<i>.c1", "<tag>.<i>.c2"
+static int icci_trunk(Loader& L, const std::string& first, const std::string& bn,
+                      const std::string& hidden, int blocks, const std::string& tag) {
+  const int nf = kIcciFeatures;
+  if (L.has(hidden + "." + std::to_string(blocks) + ".scale"))
+    return fail(ZJAI_MODEL, hidden + ": more than " + std::to_string(blocks) + " residual blocks");
+  std::vector<double> a, sh, a2, sh2;
+  ZJAI_TRY(icci_bn(L, bn, nf, 1.0, &a, &sh));
+  ZJAI_TRY(icci_fold(L, first, tag + ".first", 3 * kIcciBands, nf, 3, 3, a, sh));
+  for (int i = 0; i < blocks; ++i) {
+    const std::string p = hidden + "." + std::to_string(i), q = tag + "." + std::to_string(i);
+    double s;
+    ZJAI_TRY(icci_scalar(L, p + ".scale", &s));
+    ZJAI_TRY(icci_bn(L, p + ".BN1", nf, 1.0, &a, &sh));
+    ZJAI_TRY(icci_bn(L, p + ".BN2", nf, s, &a2, &sh2));
+    ZJAI_TRY(icci_fold(L, p + ".conv1", q + ".c1", nf, nf, 1, 3, a, sh));
+    ZJAI_TRY(icci_fold(L, p + ".conv2", q + ".c2", nf, nf, 3, 1, a2, sh2));
+  }
+  return ZJAI_OK;
+}
+
+static int icci_last(Loader& L, const std::string& conv, const std::string& scale,
+                     const std::string& store) {
+  double s;
+  ZJAI_TRY(icci_scalar(L, scale, &s));
+  return icci_fold(L, conv, store, kIcciFeatures, kIcciBands, 3, 3,
+                   std::vector<double>(kIcciBands, s), std::vector<double>(kIcciBands, 0.0));
+}
+
 static int load_net(Net* n, Loader& L) {
   const int op = n->op;
   switch (n->kind) {
@@ -225,6 +305,13 @@ static int load_net(Net* n, Loader& L) {
       ZJAI_TRY(L.conv("conv4", c, 160, 3, 3, 2, 1, 1, true));
       return L.conv("conv5", 160, 160, 1, 1, 1, 0, 1, false);
     }
+    case ZJAI_ICCI:  // IcciNet::load (icci.rs:181-212)
+      ZJAI_TRY(icci_trunk(L, "conv_first_Y", "BNY", "hidden_layer_Y", kIcciLumaBlocks, "icci.y"));
+      ZJAI_TRY(icci_last(L, "conv_last_Y", "scaleY", "icci.last_y"));
+      ZJAI_TRY(icci_trunk(L, "conv_firstUV", "BNUV", "hidden_layer_UV", kIcciChromaBlocks,
+                          "icci.uv"));
+      ZJAI_TRY(icci_last(L, "conv_last_u", "scaleU", "icci.last_u"));
+      return icci_last(L, "conv_last_v", "scaleV", "icci.last_v");
     case ZJAI_LATENT: {
       // HyperDecoder::load (hyper_decoder.rs:24-42); ContextModel::load (mcm.rs:119-156) when
       // the checkpoint holds "context.MCM.0.fusion_pred_net.conv1.weight" (common.rs:111-115).
@@ -263,8 +350,8 @@ static int load_net(Net* n, Loader& L) {
 
 int load_network(Ctx* ctx, int kind, int op, const zjai_param* params, int nparams, Net** out) {
   *out = nullptr;
-  // the latent networks are the same for every operating point
-  if (kind != ZJAI_LATENT && (op < ZJAI_SOP || op > ZJAI_HOP))
+  // the latent and eICCI networks are the same for every operating point
+  if (kind != ZJAI_LATENT && kind != ZJAI_ICCI && (op < ZJAI_SOP || op > ZJAI_HOP))
     return fail(ZJAI_INVALID_ARGUMENT, "unknown operating point");
   if (nparams < 0 || (nparams > 0 && !params)) return fail(ZJAI_INVALID_ARGUMENT, "params");
   Net* n = new Net();
@@ -356,6 +443,7 @@ const ConvLayer* Runner::layer(const std::string& name) {
 std::string Runner::kind_tag() const {
   static const char* k[] = {"Y", "UV", "AY", "AUV"};
   if (net->kind == ZJAI_LATENT) return "L" + std::to_string(net->lat_c) + ":";
+  if (net->kind == ZJAI_ICCI) return "I:";
   if (net->kind == kStageKind) return "S" + std::to_string(n) + ":";
   return std::string(k[net->kind & 3]) + std::to_string(n) + ":";
 }
@@ -933,6 +1021,49 @@ int Runner::stage(const TView& x, float* out) {
   launch_nhwc_to_planar(y, out, stream);
   ctx->launches++;
   return cuda_check(cudaGetLastError(), "nhwc_to_planar");
+}
+
+// IcciNet::luma_correction / chroma_corrections (icci.rs:214-241) on the 48 sub-bands x
+// (NHWC f16, quarter resolution): trunk(x) = blocks(relu(first(x))), block(f) = f + c2(relu(c1(f)))
+// (batch norms and scales folded), then the last convs into planar f32 corrections [16][h][w]
+// (null: not wanted). chroma selects the chroma trunk (corrections u, v) instead of luma (y).
+int Runner::icci(const TView& x, bool chroma, float* c0, float* c1) {
+  const std::string t = chroma ? "icci.uv" : "icci.y";
+  const int blocks = chroma ? kIcciChromaBlocks : kIcciLumaBlocks;
+  TView f, o;
+  ZJAI_TRY(alloc(x.h, x.w, kIcciFeatures, &f));
+  ZJAI_TRY(alloc(x.h, x.w, kIcciFeatures, &o));
+  {
+    ConvOut a;
+    a.out = f;
+    a.act1 = ACT_RELU;
+    ZJAI_TRY(conv(t + ".first", x, a));
+  }
+  for (int i = 0; i < blocks; ++i) {
+    const std::string q = t + "." + std::to_string(i);
+    ConvOut a;
+    a.out = o;
+    a.act1 = ACT_RELU;
+    ZJAI_TRY(conv(q + ".c1", f, a));
+    ConvOut b;
+    b.out = f;
+    b.op = OP_ADD;
+    b.r1 = &f;
+    ZJAI_TRY(conv(q + ".c2", o, b));
+  }
+  const char* last[2] = {chroma ? "icci.last_u" : "icci.last_y", "icci.last_v"};
+  float* dst[2] = {c0, c1};
+  for (int k = 0; k < 2; ++k) {
+    if (!dst[k]) continue;
+    ConvOut a;
+    a.planar = true;
+    a.pout = dst[k];
+    a.p_plane = (long long)x.h * x.w;
+    a.p_row = x.w;
+    a.p_img = (long long)kIcciBands * x.h * x.w;
+    ZJAI_TRY(conv(last[k], f, a));
+  }
+  return ZJAI_OK;
 }
 
 // HyperDecoder::forward_f32 (hyper_decoder.rs:94-113): conv1 1x1 -> convT 4x4 s2, its output

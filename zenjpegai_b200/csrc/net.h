@@ -31,6 +31,9 @@ struct Net {
   ~Net();
 };
 
+// eICCI network shape (src/model/icci.rs:33-40)
+constexpr int kIcciFeatures = 48, kIcciBands = 16, kIcciLumaBlocks = 2, kIcciChromaBlocks = 4;
+
 // Net::kind of a conv stage (not one of the crate's network kinds)
 constexpr int kStageKind = 4;
 
@@ -97,6 +100,9 @@ struct Runner {
   int analysis(const TView& x, int h, int w, float* out);
   // conv stage: x (NHWC, st_cin channels) -> planar f32 out [st_cout][h * r][w * r]
   int stage(const TView& x, float* out);
+  // eICCI trunk + last convs on the 48 sub-bands: planar f32 corrections [16][h][w] of the
+  // luma (c0) or of u (c0) and v (c1) when `chroma`; a null pointer skips that output
+  int icci(const TView& x, bool chroma, float* c0, float* c1);
   // hyper-decoder: z (NHWC, lat_c channels) -> psi planar f32 [4 lat_c][out_h][out_w]
   int hyper(const TView& z, int out_h, int out_w, float* psi);
   // latent from psi planar f32 [4C][ceil(h/2)][ceil(w/2)] and the residual planar f32

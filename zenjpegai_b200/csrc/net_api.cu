@@ -276,7 +276,7 @@ int zjai_net_create(zjai_ctx* ctx, int kind, int op, const zjai_param* params, i
   if (!out) return fail(ZJAI_INVALID_ARGUMENT, "null output handle");
   *out = nullptr;
   ZJAI_TRY(ctx_enter(ctx));
-  if ((kind < ZJAI_SYN_Y || kind > ZJAI_ANA_UV) && kind != ZJAI_LATENT)
+  if ((kind < ZJAI_SYN_Y || kind > ZJAI_ANA_UV) && kind != ZJAI_LATENT && kind != ZJAI_ICCI)
     return fail(ZJAI_INVALID_ARGUMENT, "unknown network kind");
   Net* n = nullptr;
   ZJAI_TRY(load_network(ctx, kind, op, params, nparams, &n));
