@@ -407,6 +407,9 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
               for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
+                  // input row i is tap ky of output row i - ky: rows outside the band's six
+                  // take nothing (a compile-time condition once the rows are unrolled)
+                  if (i - ky < 0 || i - ky > 5) continue;
                   float2(&s)[2][2] = acc[(J - ky + 3) % 3];
                   if (jx < 3) {
                     const float4 w4 = wr[ky * 3 + jx];
