@@ -101,6 +101,14 @@ int zjai_ctx_sync(zjai_ctx *ctx);
  * callers that prefer to fail fast, and the way the timeout path is exercised in tests. */
 int zjai_ctx_set_wait_limit(zjai_ctx *ctx, int64_t cycles);
 
+/* CUDA graphs for repeated device calls of the tiled synthesis (zjai_synthesize_tiles,
+ * zjai_synthesize_tiles_q; ZJAI_MEM_DEVICE, no cancel flag): with graphs enabled, the first call
+ * with a given set of arguments (networks, pointers, sizes, tile list) runs as usual, the second
+ * is captured into a graph and every later one replays it with one launch. The arguments'
+ * pointers must then stay valid and keep their meaning (same buffers); destroying a network of
+ * the context drops the graphs. Off by default; disabling drops the graphs. */
+int zjai_ctx_set_graphs(zjai_ctx *ctx, int enable);
+
 /* Capture a named intermediate map of the networks this context runs (a debugging and
  * per-stage parity facility; the reference has no counterpart, its Python oracle dumps the
  * same names): every later network run that reaches the point `name` writes the map there

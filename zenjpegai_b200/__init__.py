@@ -106,6 +106,11 @@ class Engine:
         """Limit of the convolution kernel's pipeline waits in SM cycles (0: default)."""
         check(_lib.lib().zjai_ctx_set_wait_limit(self.handle, int(cycles)))
 
+    def set_graphs(self, enable):
+        """Replay repeated device calls of the tiled synthesis as CUDA graphs (captured on the
+        second call with the same arguments)."""
+        check(_lib.lib().zjai_ctx_set_graphs(self.handle, 1 if enable else 0))
+
     def set_probe(self, name, buf):
         """Capture the intermediate map `name` ("ana.act1" ..) of later network runs into `buf`
         (a float32 CUDA tensor, planar [n, c, h, w] or larger); buf None removes it."""

@@ -78,6 +78,7 @@ def lib():
     L.zjai_ctx_launch_count.argtypes = [_vp]
     L.zjai_ctx_launch_count.restype = ctypes.c_int64
     L.zjai_ctx_profile.argtypes = [_vp, _i]
+    L.zjai_ctx_set_graphs.argtypes = [_vp, _i]
     L.zjai_ctx_set_probe.argtypes = [_vp, ctypes.c_char_p, _vp, ctypes.c_int64]
     L.zjai_ctx_profile_read_bytes.argtypes = [_vp, ctypes.POINTER(ctypes.c_double),
                                               ctypes.POINTER(ctypes.c_double),

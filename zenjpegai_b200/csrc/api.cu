@@ -156,6 +156,7 @@ int zjai_ctx_destroy(zjai_ctx* ctx) {
   if (!ctx) return ZJAI_OK;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  ctx->clear_graphs();
   if (ctx->arena.base) cudaFree(ctx->arena.base);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
@@ -203,6 +204,14 @@ int zjai_ctx_set_probe(zjai_ctx* ctx, const char* name, float* dst, int64_t capa
   }
   if (capacity <= 0) return fail(ZJAI_INVALID_ARGUMENT, "probe: capacity must be positive");
   ctx->probes[name] = {dst, (long long)capacity};
+  return ZJAI_OK;
+}
+
+int zjai_ctx_set_graphs(zjai_ctx* ctx, int enable) {
+  ZJAI_TRY(ctx_enter(ctx));
+  ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "stream sync"));
+  ctx->graphs = enable != 0;
+  if (!ctx->graphs) ctx->clear_graphs();
   return ZJAI_OK;
 }
 

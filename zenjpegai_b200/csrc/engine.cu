@@ -40,6 +40,25 @@ cudaEvent_t Ctx::take_event() {
   return e;
 }
 
+void Ctx::clear_graphs() {
+  for (auto& kv : graph_cache) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    for (void* p : kv.second.pins) cudaFreeHost(p);
+  }
+  graph_cache.clear();
+}
+
+int h2d_async(Ctx* ctx, void* dst, const void* src, size_t bytes, cudaStream_t s) {
+  if (ctx->capture_pins) {
+    void* pin = nullptr;
+    ZJAI_TRY(cuda_check(cudaHostAlloc(&pin, bytes, cudaHostAllocDefault), "cudaHostAlloc"));
+    std::memcpy(pin, src, bytes);
+    ctx->capture_pins->push_back(pin);
+    src = pin;
+  }
+  return cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s), "H2D");
+}
+
 // ---- arena --------------------------------------------------------------------------------
 void* Arena::alloc(size_t bytes) {
   size_t start = (top + 255) & ~size_t(255);
@@ -613,9 +632,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     Arena* ar = ctx->cur_arena ? ctx->cur_arena : &ctx->arena;
     void* dm = ar->alloc(sizeof(CUtensorMap) * pm.size());
     if (!dm) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (tensor maps)");
-    ZJAI_TRY(cuda_check(cudaMemcpyAsync(dm, pm.data(), sizeof(CUtensorMap) * pm.size(),
-                                        cudaMemcpyHostToDevice, ctx->stream),
-                        "tensor map upload"));
+    ZJAI_TRY(h2d_async(ctx, dm, pm.data(), sizeof(CUtensorMap) * pm.size(), ctx->stream));
     a.tmO_img = static_cast<const CUtensorMap*>(dm);
   }
   if (a.nres) {
@@ -638,9 +655,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     Arena* ar = ctx->cur_arena ? ctx->cur_arena : &ctx->arena;
     void* dm = ar->alloc(sizeof(CUtensorMap) * rm.size());
     if (!dm) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (tensor maps)");
-    ZJAI_TRY(cuda_check(cudaMemcpyAsync(dm, rm.data(), sizeof(CUtensorMap) * rm.size(),
-                                        cudaMemcpyHostToDevice, ctx->stream),
-                        "tensor map upload"));
+    ZJAI_TRY(h2d_async(ctx, dm, rm.data(), sizeof(CUtensorMap) * rm.size(), ctx->stream));
     a.tmR = static_cast<const CUtensorMap*>(dm);
   }
   a.wblk = L.w;
@@ -686,9 +701,7 @@ int run_conv(Ctx* ctx, const ConvLayer& L, const TView& in, const ConvOut& o) {
     Arena* ar = ctx->cur_arena ? ctx->cur_arena : &ctx->arena;
     void* dmaps = ar->alloc(sizeof(CUtensorMap) * maps.size());
     if (!dmaps) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (tensor maps)");
-    ZJAI_TRY(cuda_check(cudaMemcpyAsync(dmaps, maps.data(), sizeof(CUtensorMap) * maps.size(),
-                                        cudaMemcpyHostToDevice, ctx->stream),
-                        "tensor map upload"));
+    ZJAI_TRY(h2d_async(ctx, dmaps, maps.data(), sizeof(CUtensorMap) * maps.size(), ctx->stream));
     a.tmA_img = static_cast<const CUtensorMap*>(dmaps);
     a.n_img = in.n;
     a.num_tiles = a.tiles_x * a.tiles_y * a.n_img * a.n_tiles;

@@ -62,6 +62,15 @@ struct TView {
   }
 };
 
+// A captured call (zjai_ctx_set_graphs): the instantiated graph, the pinned host copies its
+// uploads read at every replay, and the kernel launches it holds.
+struct GraphEntry {
+  cudaGraphExec_t exec = nullptr;
+  std::vector<void*> pins;
+  long long launches = 0;
+  int calls = 0;  // eager calls seen with this key (negative: capture failed, stay eager)
+};
+
 struct Ctx {
   int device = 0;
   int sms = 148;
@@ -76,6 +85,13 @@ struct Ctx {
   // final synthesis layers clamp the denormalised planes to [0, 255] (false: the raw
   // x * 128 + 127.5, zjai_ctx_set_output_clamp)
   bool clamp_output = true;
+  // CUDA graphs of repeated tiled-synthesis calls (zjai_ctx_set_graphs): per call signature the
+  // entry; while a call is being captured, the pinned host copies of its uploads are collected
+  // in capture_pins
+  bool graphs = false;
+  std::map<std::string, GraphEntry> graph_cache;
+  std::vector<void*>* capture_pins = nullptr;
+  void clear_graphs();
   // captures of named intermediate maps (zjai_ctx_set_probe): name -> (device buffer of planar
   // f32 [n][c][h][w], its capacity in floats)
   std::map<std::string, std::pair<float*, long long>> probes;
@@ -133,6 +149,10 @@ void timed_launch(Ctx* ctx, bool conv, double flops, double bytes, F&& f) {
 // Allocate an NHWC f16 tensor in the arena; channels padded to `cpad` (multiple of 8), and
 // rows / cols rounded up to even so any stride-2 consumer can read it. Zero-filled when
 // `zero` (async on ctx stream).
+// Host -> device copy on stream s; during a graph capture the source is first copied into
+// pinned memory kept with the graph (replays read it), otherwise copied as given.
+int h2d_async(Ctx* ctx, void* dst, const void* src, size_t bytes, cudaStream_t s);
+
 int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero = false,
                  Arena* arena = nullptr, cudaStream_t stream = nullptr);
 

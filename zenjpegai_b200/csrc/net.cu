@@ -2,6 +2,7 @@
 // synthesis / analysis topologies of src/model/{synthesis,attention,analysis}.rs on batches of
 // same-shape tiles (NHWC f16 activations in the context arena).
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -348,6 +349,11 @@ static int load_net(Net* n, Loader& L) {
   }
 }
 
+uint64_t next_net_uid() {
+  static std::atomic<uint64_t> next{1};
+  return next++;
+}
+
 int load_network(Ctx* ctx, int kind, int op, const zjai_param* params, int nparams, Net** out) {
   *out = nullptr;
   // the latent and eICCI networks are the same for every operating point
@@ -358,6 +364,7 @@ int load_network(Ctx* ctx, int kind, int op, const zjai_param* params, int npara
   n->ctx = ctx;
   n->kind = kind;
   n->op = op;
+  n->uid = next_net_uid();
   Loader L;
   L.net = n;
   for (int i = 0; i < nparams; ++i) {
@@ -390,6 +397,7 @@ int load_stage(Ctx* ctx, int shuffle, int act, int res_act, const zjai_param* pa
   std::unique_ptr<Net> n(new Net());
   n->ctx = ctx;
   n->kind = kStageKind;
+  n->uid = next_net_uid();
   Loader L;
   L.net = n.get();
   for (int i = 0; i < nparams; ++i) {

@@ -13,6 +13,9 @@ namespace zjai {
 struct Net {
   Ctx* ctx = nullptr;
   int kind = 0, op = 0;
+  // unique per loaded network for the life of the process (graph cache keys: a network created
+  // at the address of a destroyed one is a different network)
+  uint64_t uid = 0;
   std::map<std::string, ConvLayer> convs;
   std::map<std::string, float*> vecs;  // LN weight/bias, temperature, depthwise weights [c][9]
   // f16 scale of the per-picture weights W_o . blockdiag(A) of each transformer block's folded

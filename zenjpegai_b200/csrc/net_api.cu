@@ -25,8 +25,7 @@ int net_enter(zjai_net* net) {
 int upload_ints(Ctx* ctx, Arena* arena, const std::vector<int>& v, cudaStream_t s, int** out) {
   int* d = static_cast<int*>(arena->alloc(v.size() * sizeof(int) + 16));
   if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (descriptors)");
-  ZJAI_TRY(cuda_check(cudaMemcpyAsync(d, v.data(), v.size() * sizeof(int), cudaMemcpyHostToDevice, s),
-                      "descriptor H2D"));
+  ZJAI_TRY(h2d_async(ctx, d, v.data(), v.size() * sizeof(int), s));
   *out = d;
   return ZJAI_OK;
 }
@@ -289,6 +288,7 @@ int zjai_net_destroy(zjai_net* net) {
   if (!net) return ZJAI_OK;
   cudaSetDevice(net->ctx->device);
   cudaDeviceSynchronize();
+  net->ctx->clear_graphs();  // graphs may hold this network's weights
   delete reinterpret_cast<Net*>(net);
   return ZJAI_OK;
 }
@@ -655,6 +655,68 @@ static int synthesize_tiles_entry(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_
   const size_t ny = (size_t)out_h * out_w, nc = (size_t)ch * cw;
   if ((double)ny * npic > 2147483647.0)
     return fail(ZJAI_LIMIT_EXCEEDED, "synthesize: more than 2^31 output samples per call");
+  // CUDA graph of a repeated device call (zjai_ctx_set_graphs): the first call with these
+  // arguments runs eagerly, the second is captured and every later one replays the graph
+  GraphEntry* ge = nullptr;
+  if (ctx->graphs && mem == ZJAI_MEM_DEVICE && !cancel && !ctx->profiling && ctx->probes.empty()) {
+    std::string key;
+    auto put = [&](const void* p, size_t n) { key.append(static_cast<const char*>(p), n); };
+    const uint64_t ids[2] = {net_y ? net_y->uid : 0, net_uv ? net_uv->uid : 0};
+    const void* ptrs[5] = {y_hat_y, y_hat_uv, rec_y, rec_u, rec_v};
+    const long long vals[10] = {lh, lw, ntiles, out_h, out_w, sv, sh, bit_depth, npic,
+                                ctx->wait_cycles};
+    put(ids, sizeof ids);
+    put(ptrs, sizeof ptrs);
+    put(vals, sizeof vals);
+    const bool clamp = ctx->clamp_output;
+    put(&clamp, sizeof clamp);
+    put(tiles, sizeof(zjai_tile) * (size_t)ntiles);
+    ge = &ctx->graph_cache[key];
+    if (ge->exec) {
+      ZJAI_TRY(cuda_check(cudaGraphLaunch(ge->exec, ctx->stream), "graph launch"));
+      ctx->launches += ge->launches;
+      return finish_call(ctx, mem);
+    }
+    if (ge->calls++ < 1) ge = nullptr;  // first call: eager
+  }
+  if (ge) {
+    // capture this call; a call that fails to capture runs eagerly (and is never captured again)
+    std::vector<void*> pins;
+    const long long l0 = ctx->launches;
+    ZJAI_TRY(cuda_check(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeRelaxed),
+                        "begin capture"));
+    ctx->capture_pins = &pins;
+    ctx->graphs = false;
+    const int st = synthesize_tiles_entry(ctx, net_y, net_uv, y_hat_y, y_hat_uv, lh, lw, tiles,
+                                          ntiles, out_h, out_w, sv, sh, bit_depth, rec_y, rec_u,
+                                          rec_v, mem, cancel, npic);
+    ctx->graphs = true;
+    ctx->capture_pins = nullptr;
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(ctx->stream, &g);
+    cudaGraphExec_t exec = nullptr;
+    if (st == ZJAI_OK && ce == cudaSuccess && g &&
+        cudaGraphInstantiate(&exec, g, 0) == cudaSuccess) {
+      cudaGraphDestroy(g);
+      ge->exec = exec;
+      ge->pins.swap(pins);
+      ge->launches = ctx->launches - l0;
+      ctx->launches = l0 + ge->launches;
+      ZJAI_TRY(cuda_check(cudaGraphLaunch(exec, ctx->stream), "graph launch"));
+      return finish_call(ctx, mem);
+    }
+    if (g) cudaGraphDestroy(g);
+    for (void* p : pins) cudaFreeHost(p);
+    cudaGetLastError();
+    ge->calls = -(1 << 30);
+    ctx->launches = l0;
+    ctx->graphs = false;
+    const int st2 = synthesize_tiles_entry(ctx, net_y, net_uv, y_hat_y, y_hat_uv, lh, lw, tiles,
+                                           ntiles, out_h, out_w, sv, sh, bit_depth, rec_y, rec_u,
+                                           rec_v, mem, cancel, npic);
+    ctx->graphs = true;
+    return st2;
+  }
   ArenaScope scope(ctx);
   const size_t m2 = ctx->arena2.mark();
   struct Rel {
