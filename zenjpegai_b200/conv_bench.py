@@ -32,6 +32,8 @@ LAYERS = [
     ("hop_resau_g4_128@H2x28", 28, 256, 256, 128, 128, 3, 1, 4, 0, 0),
     ("hop_ffn_in_1x1_128_1024@H4x28", 28, 128, 128, 128, 1024, 1, 1, 1, 0, 0),
     ("hop_ffn_out_1x1_512_128@H4x28", 28, 128, 128, 512, 128, 1, 1, 1, 0, 1),
+    ("hop_prep_conv1_1x1_128_384@H4x28", 28, 128, 128, 128, 384, 1, 1, 1, 0, 0),
+    ("hop_conv3_t_1x1_128_512@H4x28", 28, 128, 128, 128, 512, 1, 1, 1, 0, 0),
     ("hop_us_convT3_128@H4x28", 28, 128, 128, 128, 128, 3, 1, 1, 1, 0),
     ("hop_subscale_s2_128@H4x1", 1, 128, 128, 128, 128, 3, 2, 1, 0, 0),
     # residual 2: the network's final layer (planar f32 output, denormalised)
