@@ -146,13 +146,13 @@ void timed_launch(Ctx* ctx, bool conv, double flops, double bytes, F&& f) {
   ctx->conv_records.push_back(r);
 }
 
-// Allocate an NHWC f16 tensor in the arena; channels padded to `cpad` (multiple of 8), and
-// rows / cols rounded up to even so any stride-2 consumer can read it. Zero-filled when
-// `zero` (async on ctx stream).
 // Host -> device copy on stream s; during a graph capture the source is first copied into
 // pinned memory kept with the graph (replays read it), otherwise copied as given.
 int h2d_async(Ctx* ctx, void* dst, const void* src, size_t bytes, cudaStream_t s);
 
+// Allocate an NHWC f16 tensor in the arena; channels padded to `cpad` (multiple of 8), and
+// rows / cols rounded up to even so any stride-2 consumer can read it. Zero-filled when
+// `zero` (async on ctx stream).
 int alloc_tensor(Ctx* ctx, int n, int h, int w, int c, TView* out, bool zero = false,
                  Arena* arena = nullptr, cudaStream_t stream = nullptr);
 
