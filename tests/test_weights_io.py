@@ -223,3 +223,17 @@ def test_model_paths_and_sources(tmp_path):
                               np.ones((2, 2, 1, 1), np.float32))
     with pytest.raises(_lib.ZjaiError):
         W.ModelDir(str(tmp_path)).read("VM_bop/missing.pth")
+
+
+def test_extents_that_wrap_are_rejected():
+    # a ZJM1 table entry whose element count times the element size wraps to 0 in 128 bits
+    # (f32, shape 2^62 x 2^62 x 16, length 0) must fail cleanly, not pass the extent check
+    name = b"w"
+    head = b"ZJM1" + struct.pack("<III", 1, 1, 0)
+    head += struct.pack("<H", len(name)) + name + struct.pack("<BB", 1, 3)
+    head += b"".join(struct.pack("<Q", d) for d in (1 << 62, 1 << 62, 16))
+    head += struct.pack("<QQ", 64, 0)
+    data = head + b"\0" * (64 - len(head) % 64)
+    with pytest.raises(_lib.ZjaiError) as e:
+        W.Checkpoint(data)
+    assert e.value.status == _lib.LIMIT_EXCEEDED

@@ -53,6 +53,10 @@ bool dtype_of_storage(const std::string& cls, int* d) {
 
 constexpr uint32_t kMaxEntries = 1u << 20;  // table sizes accepted (hostile-input bound)
 constexpr int kMaxRank = 8;
+// Largest dimension, stride, storage offset and element count accepted: with rank <= 8 every
+// product and index sum below stays far inside 128 bits, so no bound check can be defeated by
+// wrap-around.
+constexpr uint64_t kMaxExtent = (uint64_t)1 << 40;
 
 // Bounds-checked little-endian cursor over [p, p + n).
 struct Cursor {
@@ -591,7 +595,14 @@ int parse_zjm(Ckpt* ck) {
     if (!r.ok) return fail(ZJAI_MODEL, "packed model: truncated table");
     const uint64_t es = (uint64_t)dtype_size(t.dtype);
     unsigned __int128 numel = es;
-    for (uint64_t d : t.shape) numel *= d;
+    bool big = false;
+    for (uint64_t d : t.shape) {
+      big = big || d > kMaxExtent;
+      numel *= d;
+      big = big || numel > (unsigned __int128)kMaxExtent;
+      if (big) break;
+    }
+    if (big) return fail(ZJAI_LIMIT_EXCEEDED, "packed model: tensor `" + name + "` too large");
     if (numel != len || off % 64 || off > ck->file.size() || len > ck->file.size() - off)
       return fail(ZJAI_MODEL, "packed model: tensor `" + name + "` has an invalid extent");
     t.stride.assign(rank, 1);
@@ -628,14 +639,18 @@ int tensor_bytes(const Ckpt* ck, const std::string& name, const TRef& t, std::ve
   if (t.shape.size() != t.stride.size())
     return fail(ZJAI_MODEL, "tensor `" + name + "`: shape/stride rank mismatch");
   const size_t es = (size_t)dtype_size(t.dtype), elems = st_len / es;
+  if (t.shape.size() > (size_t)kMaxRank || t.offset > kMaxExtent)
+    return fail(ZJAI_LIMIT_EXCEEDED, "tensor `" + name + "`: rank or offset too large");
   unsigned __int128 numel = 1, last = t.offset;  // highest element index the view touches
   bool empty = false;
   for (size_t a = 0; a < t.shape.size(); ++a) {
+    if (t.shape[a] > kMaxExtent || t.stride[a] > kMaxExtent)
+      return fail(ZJAI_LIMIT_EXCEEDED, "tensor `" + name + "`: extent or stride too large");
     numel *= t.shape[a];
+    if (numel * es > kMaxExtent) return fail(ZJAI_LIMIT_EXCEEDED, "tensor too large");
     if (t.shape[a] == 0) empty = true;
     else last += (unsigned __int128)(t.shape[a] - 1) * t.stride[a];
   }
-  if (numel * es > ((unsigned __int128)1 << 40)) return fail(ZJAI_LIMIT_EXCEEDED, "tensor too large");
   out->assign((size_t)(numel * es), 0);
   if (empty) return ZJAI_OK;
   if (last >= elems) return fail(ZJAI_MODEL, "tensor `" + name + "` exceeds its storage");
