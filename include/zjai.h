@@ -12,7 +12,10 @@
  *    (src/tensor.rs:10-120). `mem` says whether the pointers are host (ZJAI_MEM_HOST) or
  *    device (ZJAI_MEM_DEVICE) memory of the context's GPU. Host calls are synchronous: they
  *    return after the output has been written. Device calls are ordered on the context's
- *    stream and return after the work has been enqueued (zjai_ctx_sync waits).
+ *    stream and return after the work has been enqueued (zjai_ctx_sync waits). Buffers passed
+ *    as ZJAI_MEM_DEVICE are checked first (device memory of the context's GPU, managed
+ *    memory or mapped pinned host memory); anything else returns ZJAI_INVALID_ARGUMENT before
+ *    any kernel runs.
  *  - The caller owns inputs and outputs; the library owns weights and scratch.
  *  - One call in flight per context at a time; separate contexts are independent and may be
  *    used from separate host threads.

@@ -42,8 +42,25 @@ int finish_call(Ctx* ctx, int mem) {
 }
 
 // Device copy of a caller tensor (host or device) as f32; returns a device pointer.
+int check_device_buffer(Ctx* ctx, const void* p, const char* what) {
+  if (!p) return fail(ZJAI_INVALID_ARGUMENT, std::string(what) + ": null buffer");
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(ZJAI_INVALID_ARGUMENT, std::string(what) + ": not a CUDA-visible buffer");
+  }
+  const bool ok = (at.type == cudaMemoryTypeDevice && at.device == ctx->device) ||
+                  at.type == cudaMemoryTypeManaged ||
+                  (at.type == cudaMemoryTypeHost && at.devicePointer != nullptr);
+  if (!ok)
+    return fail(ZJAI_INVALID_ARGUMENT,
+                std::string(what) + ": ZJAI_MEM_DEVICE needs memory the context's GPU can address");
+  return ZJAI_OK;
+}
+
 int stage_in(Ctx* ctx, const float* p, size_t n, int mem, const float** out) {
   if (mem == ZJAI_MEM_DEVICE) {
+    if (n) ZJAI_TRY(check_device_buffer(ctx, p, "input"));
     *out = p;
     return ZJAI_OK;
   }
@@ -58,6 +75,7 @@ int stage_in(Ctx* ctx, const float* p, size_t n, int mem, const float** out) {
 
 int stage_out_alloc(Ctx* ctx, float* p, size_t n, int mem, float** dev) {
   if (mem == ZJAI_MEM_DEVICE) {
+    if (n) ZJAI_TRY(check_device_buffer(ctx, p, "output"));
     *dev = p;
     return ZJAI_OK;
   }

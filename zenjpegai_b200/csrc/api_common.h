@@ -12,6 +12,10 @@ const char* last_error_cstr();
 int ctx_enter(zjai_ctx* ctx);
 int ctx_check_status(Ctx* ctx);
 int finish_call(Ctx* ctx, int mem);
+// ZJAI_INVALID_ARGUMENT unless p is memory the context's GPU can address (its device memory,
+// managed memory or mapped pinned host memory): caller buffers passed as ZJAI_MEM_DEVICE are
+// checked before any kernel touches them.
+int check_device_buffer(Ctx* ctx, const void* p, const char* what);
 int stage_in(Ctx* ctx, const float* p, size_t n, int mem, const float** out);
 int stage_out_alloc(Ctx* ctx, float* p, size_t n, int mem, float** dev);
 int stage_out_finish(Ctx* ctx, float* host, const float* dev, size_t n, int mem);

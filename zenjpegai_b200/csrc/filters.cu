@@ -223,6 +223,10 @@ int zjai_lef(zjai_ctx* ctx, const float* luma, int h, int w, const int32_t* scal
   const float* din;
   ZJAI_TRY(stage_in(ctx, luma, n, mem, &din));
   const int32_t* dreg = scale_log + (size_t)channel * nr;
+  if (mem == ZJAI_MEM_DEVICE) {
+    ZJAI_TRY(check_device_buffer(ctx, scale_log, "LEF scale map"));
+    ZJAI_TRY(check_device_buffer(ctx, out, "LEF output"));
+  }
   if (mem == ZJAI_MEM_HOST) {
     int32_t* d = static_cast<int32_t*>(ctx->arena.alloc(nr * sizeof(int32_t)));
     if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (LEF scale map)");
@@ -273,6 +277,8 @@ int zjai_icci_filter(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, int use_u
     overlap = 0;
   }
   const int half = overlap / 2;
+  if (mem == ZJAI_MEM_DEVICE)
+    for (float* pl : {y, u, v}) ZJAI_TRY(check_device_buffer(ctx, pl, "eICCI plane"));
   ArenaScope scope(ctx);
   const long long n = (long long)h * w;
   float* d[3] = {y, u, v};

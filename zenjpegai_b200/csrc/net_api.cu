@@ -412,6 +412,7 @@ int zjai_preprocess_rgb(zjai_ctx* ctx, const uint8_t* rgb, int h, int w, float* 
   const size_t nrgb = (size_t)h * w * 3, nl = (size_t)h * w;
   const size_t nc = (size_t)12 * ((h + 1) / 2) * ((w + 1) / 2);
   const uint8_t* drgb = rgb;
+  if (mem == ZJAI_MEM_DEVICE) ZJAI_TRY(check_device_buffer(ctx, rgb, "RGB input"));
   if (mem == ZJAI_MEM_HOST) {
     uint8_t* d = static_cast<uint8_t*>(ctx->arena.alloc(nrgb));
     if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (RGB staging)");
@@ -476,6 +477,7 @@ int zjai_analyze_rgb(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, int n, co
   const int ch = (h + 1) / 2, cw = (w + 1) / 2;
   const size_t nrgb = (size_t)n * h * w * 3;
   const uint8_t* drgb = rgb;
+  if (mem == ZJAI_MEM_DEVICE) ZJAI_TRY(check_device_buffer(ctx, rgb, "RGB input"));
   if (mem == ZJAI_MEM_HOST) {
     uint8_t* d = static_cast<uint8_t*>(ctx->arena.alloc(nrgb));
     if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (RGB staging)");
@@ -730,6 +732,8 @@ static int synthesize_tiles_entry(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_
   char *oy = static_cast<char*>(rec_y), *ou = static_cast<char*>(rec_u),
        *ov = static_cast<char*>(rec_v);
   const size_t all = (size_t)npic * (ny + 2 * nc) * es;
+  if (mem == ZJAI_MEM_DEVICE)
+    for (const void* pl : {rec_y, rec_u, rec_v}) ZJAI_TRY(check_device_buffer(ctx, pl, "output plane"));
   if (mem == ZJAI_MEM_HOST) {
     oy = static_cast<char*>(ctx->arena.alloc(all));
     if (!oy) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (output planes)");
@@ -821,6 +825,7 @@ int zjai_synthesize_rgb(zjai_ctx* ctx, zjai_net* net_y, zjai_net* net_uv, const 
   const size_t ny = (size_t)height * width, nc = (size_t)ch * cw;
   float* planes = static_cast<float*>(ctx->arena.alloc((ny + 2 * nc) * sizeof(float)));
   const size_t ob = ny * 3 * (bit_depth == 8 ? 1 : 2);
+  if (mem == ZJAI_MEM_DEVICE) ZJAI_TRY(check_device_buffer(ctx, rgb, "RGB output"));
   void* dout = mem == ZJAI_MEM_HOST ? ctx->arena.alloc(ob + 16) : rgb;
   if (!planes || !dout) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (RGB planes)");
   int st = synthesize_tiles_dev(ctx, reinterpret_cast<Net*>(net_y), reinterpret_cast<Net*>(net_uv),

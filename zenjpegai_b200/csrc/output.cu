@@ -159,6 +159,7 @@ int zjai_quantize_plane(zjai_ctx* ctx, const float* x, int64_t n, int bit_depth,
   ZJAI_TRY(stage_in(ctx, x, (size_t)n, mem, &dx));
   const size_t ob = (size_t)n * (bit_depth == 8 ? 1 : 2);
   void* dout = out;
+  if (mem == ZJAI_MEM_DEVICE && n) ZJAI_TRY(check_device_buffer(ctx, out, "quantize output"));
   if (mem == ZJAI_MEM_HOST) {
     dout = ctx->arena.alloc(ob + 16);
     if (!dout) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (quantize)");
@@ -180,6 +181,7 @@ int zjai_yuv_to_rgb(zjai_ctx* ctx, const float* y, const float* u, const float* 
   ZJAI_TRY(stage_in(ctx, v, (size_t)ch * cw, mem, &dv));
   const size_t ob = (size_t)h * w * 3 * (bit_depth == 8 ? 1 : 2);
   void* dout = rgb;
+  if (mem == ZJAI_MEM_DEVICE) ZJAI_TRY(check_device_buffer(ctx, rgb, "RGB output"));
   if (mem == ZJAI_MEM_HOST) {
     dout = ctx->arena.alloc(ob + 16);
     if (!dout) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (rgb)");
