@@ -104,6 +104,44 @@ __global__ void normalize_pad_kernel(const float* __restrict__ src, int c, int S
     d[ch] = __float2half_rn((__ldg(s + (long long)ch * plane) - 127.5f) / 128.0f);
 }
 
+// The luma analysis's first layer (3x3, stride 2, pad 1, one input channel) as a 1x1 conv:
+// per output pixel (oy, ox) of the h1 x w1 output, its nine input taps (ky, kx) as channels
+// 3 ky + kx (channels 9..15 zero). A tap reads input (2 oy - 1 + ky, 2 ox - 1 + kx) of the
+// normalize_pad picture (the h x w window at (y0, x0) of the planar source, normalised to
+// (s - 127.5) / 128 in f16, its rows / columns past the window replicating the last one), and 0
+// above or left of it (the conv's zero padding; the padded picture has 2 h1 x 2 w1 samples,
+// so no tap falls below or right of it). The f16 values equal normalize_pad's.
+__global__ void normalize_im2col_kernel(const float* __restrict__ src, int SH, int SW, int y0,
+                                        int x0, int h, int w, __half* __restrict__ dst, int n_img,
+                                        int h1, int w1, long long pix, long long row,
+                                        long long img) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)n_img * h1 * w1) return;
+  const int ox = (int)(idx % w1);
+  const long long r = idx / w1;
+  const int oy = (int)(r % h1), n = (int)(r / h1);
+  const float* s = src + (long long)n * SH * SW;
+  __half v[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = __float2half_rn(0.f);
+#pragma unroll
+  for (int ky = 0; ky < 3; ++ky) {
+    const int y = 2 * oy - 1 + ky;
+    if (y < 0) continue;
+    const int sy = y0 + (y < h ? y : h - 1);
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx) {
+      const int x = 2 * ox - 1 + kx;
+      if (x < 0) continue;
+      const int sx = x0 + (x < w ? x : w - 1);
+      v[3 * ky + kx] = __float2half_rn((__ldg(s + (long long)sy * SW + sx) - 127.5f) / 128.0f);
+    }
+  }
+  uint4* d = reinterpret_cast<uint4*>(dst + n * img + oy * row + ox * pix);
+  d[0] = *reinterpret_cast<const uint4*>(&v[0]);
+  d[1] = *reinterpret_cast<const uint4*>(&v[8]);
+}
+
 // `preprocess_rgb` (colour.rs:535-541 -> source_planes colour.rs:390-436, preprocess
 // colour.rs:462-495 for 4:4:4 coding) of 8-bit RGB pictures [n][h][w][3]: one thread per
 // (picture, chroma sample): the 2 x 2 luma samples it covers (rows / columns past the picture
@@ -261,6 +299,14 @@ void launch_normalize_pad_window(const float* src, int c, int SH, int SW, int y0
   normalize_pad_kernel<<<blocks_for(total, 256), 256, 0, s>>>(src, c, SH, SW, y0, x0, h, w,
                                                                dst.p, dst.n, dst.h, dst.w,
                                                                dst.pix, dst.row, dst.img);
+}
+
+void launch_normalize_im2col(const float* src, int SH, int SW, int y0, int x0, int h, int w,
+                             const TView& dst, cudaStream_t s) {
+  const long long total = (long long)dst.n * dst.h * dst.w;
+  if (total == 0) return;
+  normalize_im2col_kernel<<<blocks_for(total, 256), 256, 0, s>>>(
+      src, SH, SW, y0, x0, h, w, dst.p, dst.n, dst.h, dst.w, dst.pix, dst.row, dst.img);
 }
 
 void launch_preprocess_rgb(const uint8_t* rgb, int n, int h, int w, float* luma, float* chroma,

@@ -74,6 +74,19 @@ struct Loader {
     net->convs[prefix] = L;
     return ZJAI_OK;
   }
+  // The luma analysis's first layer (weight [cout][1][3][3], bias) as a 1x1 conv over its nine
+  // taps (launch_normalize_im2col): weight [cout][9][1][1], row co holding w[co][0][ky][kx] at
+  // 3 ky + kx. Packed with the same power-of-two scale rule over the same values, so its f16
+  // weights and its bias are the 3x3 layer's.
+  int conv_im2col(const std::string& prefix, int cout) {
+    const float *w, *b;
+    ZJAI_TRY(get(prefix + ".weight", {cout, 1, 3, 3}, &w));
+    ZJAI_TRY(get(prefix + ".bias", {cout}, &b));
+    ConvLayer L;
+    ZJAI_TRY(pack_conv(net->ctx, &L, w, b, 9, cout, 1, 1, 1, 0, 0, 1, nullptr, 1));
+    net->convs[prefix + "#im2col"] = L;
+    return ZJAI_OK;
+  }
   int vec(const std::string& name, std::vector<int64_t> shape) {
     const float* p;
     ZJAI_TRY(get(name, shape, &p));
@@ -295,6 +308,7 @@ static int load_net(Net* n, Loader& L) {
       const bool sec = n->kind == ZJAI_ANA_UV, hop = op == ZJAI_HOP;
       const int c = 128;
       ZJAI_TRY(L.conv("conv1", sec ? 12 : 1, c, 3, 3, 2, 1, 1, true));
+      if (!sec) ZJAI_TRY(L.conv_im2col("conv1", c));
       ZJAI_TRY(L.resau("act1", c));
       if (hop) ZJAI_TRY(L.tam("TAM", c, !sec));
       ZJAI_TRY(L.conv("conv2", c, c, 3, 3, 2, 1, 1, true));
@@ -917,7 +931,9 @@ int Runner::analysis(const TView& x, int h, int w, float* out) {
     ConvOut o;
     o.out = x1;
     o.out2 = &a1;
-    ZJAI_TRY(conv("conv1", x, o));
+    // x with 9 channels: the input already laid out as conv1's taps per output pixel
+    // (launch_normalize_im2col), for the 1x1 form of conv1
+    ZJAI_TRY(conv(x.c == 9 ? "conv1#im2col" : "conv1", x, o));
   }
   TView y1;
   ZJAI_TRY(resau("act1", x1, a1, h1, w1, &y1));

@@ -132,6 +132,11 @@ void launch_normalize_pad(const float* src, int c, int h, int w, const TView& ds
 // normalize_pad of the h x w window at (y0, x0) of planar pictures [n][c][SH][SW]
 void launch_normalize_pad_window(const float* src, int c, int SH, int SW, int y0, int x0, int h,
                                  int w, const TView& dst, cudaStream_t s);
+// The luma analysis input as the nine taps of its first layer per output pixel: dst
+// [n][cdiv(h, 2)][cdiv(w, 2)][9 (16 in memory)] from the h x w window at (y0, x0) of one-channel
+// planar pictures [n][SH][SW] (normalize_pad's values; see the kernel)
+void launch_normalize_im2col(const float* src, int SH, int SW, int y0, int x0, int h, int w,
+                             const TView& dst, cudaStream_t s);
 // colour.rs preprocess_rgb of n pictures [n][h][w][3] -> luma [n][h][w], chroma
 // [n][12][ph / 2][pw / 2] (planar f32, [0, 255])
 void launch_preprocess_rgb(const uint8_t* rgb, int n, int h, int w, float* luma, float* chroma,

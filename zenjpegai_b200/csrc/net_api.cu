@@ -381,8 +381,14 @@ static int analysis_entry(zjai_net* net, int kind, int cin, int cout, int down, 
   const float* dx;
   ZJAI_TRY(stage_in(ctx, x, (size_t)cin * h * w, mem, &dx));
   TView t;
-  ZJAI_TRY(alloc_tensor(ctx, 1, 2 * cdiv(h, 2), 2 * cdiv(w, 2), cin, &t, true));
-  launch_normalize_pad(dx, cin, h, w, t, ctx->stream);
+  if (cin == 1 && n->convs.count("conv1#im2col")) {
+    // luma: the first layer's taps per output pixel, for its 1x1 form
+    ZJAI_TRY(alloc_tensor(ctx, 1, cdiv(h, 2), cdiv(w, 2), 9, &t));
+    launch_normalize_im2col(dx, h, w, 0, 0, h, w, t, ctx->stream);
+  } else {
+    ZJAI_TRY(alloc_tensor(ctx, 1, 2 * cdiv(h, 2), 2 * cdiv(w, 2), cin, &t, true));
+    launch_normalize_pad(dx, cin, h, w, t, ctx->stream);
+  }
   const size_t nout = (size_t)cout * cdiv(h, down) * cdiv(w, down);
   float* dout;
   ZJAI_TRY(stage_out_alloc(ctx, out, nout, mem, &dout));
@@ -443,8 +449,14 @@ static int analyze_component(Ctx* ctx, Net* net, int ccs, int n, const float* pl
     ArenaMark mark(&ctx->arena);
     const int tx = t[0], ty = t[1], tw = t[2], th = t[3], tlw = t[6], tlh = t[7];
     TView x;
-    ZJAI_TRY(alloc_tensor(ctx, n, 2 * cdiv(th, 2), 2 * cdiv(tw, 2), c, &x, true));
-    launch_normalize_pad_window(plane, c, H, W, ty, tx, th, tw, x, ctx->stream);
+    if (c == 1 && net->convs.count("conv1#im2col")) {
+      // luma: the first layer's taps per output pixel, for its 1x1 form
+      ZJAI_TRY(alloc_tensor(ctx, n, cdiv(th, 2), cdiv(tw, 2), 9, &x));
+      launch_normalize_im2col(plane, H, W, ty, tx, th, tw, x, ctx->stream);
+    } else {
+      ZJAI_TRY(alloc_tensor(ctx, n, 2 * cdiv(th, 2), 2 * cdiv(tw, 2), c, &x, true));
+      launch_normalize_pad_window(plane, c, H, W, ty, tx, th, tw, x, ctx->stream);
+    }
     ctx->launches++;
     float* tout = out;
     if (!whole) {
