@@ -306,6 +306,24 @@ def test_analysis(eng, op):
     assert rel_l2(gotc, wantc) < 5e-3
 
 
+@pytest.mark.parametrize("op,h,w", [("bop", 75, 131), ("hop", 57, 93)])
+def test_analysis_primary_odd_size(eng, op, h, w):
+    # odd picture sizes: the luma input's first-layer taps past the last row / column replicate
+    # it (normalize_pad's padding), those above / left of the picture are the conv's zeros
+    import ctypes
+    import zenjpegai_b200 as zj
+    from zenjpegai_b200 import _lib
+    import synthetic as syn
+    pa, _ = syn.analysis_params(op, 4)
+    x = np.floor(syn.uniform(11, "odd", (1, h, w), 0.0, 256.0)).astype(np.float32)
+    na = zj.Network(eng, zj.ANA_Y, zo.OPS[op], pa)
+    got = np.empty((160, -(-h // 16), -(-w // 16)), np.float32)
+    p = lambda a: ctypes.c_void_p(a.ctypes.data)
+    zj.check(_lib.lib().zjai_analysis_primary(na.handle, p(x), h, w, p(got), 0))
+    want = zo.analysis_primary(zo.Checkpoint(pa), zo.OPS[op], x)
+    assert rel_l2(got, want) < 5e-3
+
+
 def test_model_errors(eng):
     """Missing / mis-shaped parameters fail like the crate's loaders (Error::Model)."""
     import zenjpegai_b200 as zj
