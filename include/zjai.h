@@ -306,6 +306,60 @@ int zjai_icci_filter(zjai_ctx *ctx, zjai_net *net_y, zjai_net *net_uv, int use_u
                      float *y, float *u, float *v, int h, int w, int tile_size, int overlap,
                      int mem);
 
+/* One coded EFE linear filter set (src/header.rs:623-639 `EfeLinearSet`): per chroma plane p
+ * (0 = U, 1 = V) the split candidate cand[p] (0..7, -1: plane not filtered), the filter side
+ * filter_len[p] (1..4) and the weight codes of the split's regions in order (1, 2, 2, 3, 3, 4, 6
+ * and 6 regions for candidates 0..7): chroma_codes[p] holds regions x P x fL x fL codes (P = 1
+ * for a picture coded at the source's chroma resolution, else the 4 sub-sampling phases),
+ * luma_codes[p] regions x fL x fL. min_symbol is added to every code. Host memory. */
+typedef struct {
+  int cand[2];
+  int filter_len[2];
+  int min_symbol;
+  const uint32_t *chroma_codes[2];
+  const uint32_t *luma_codes[2];
+} zjai_efe_linear_set;
+
+/* EFE linear (src/filters/efe_linear.rs:403-460, `filter_plane` :308-359): the luma-aided
+ * linear filter of the chroma planes with one coded set, bit-exact with the crate's f32
+ * arithmetic. y [h][w], u / v [ch][cw] in [0, 255] of a source subsampled s_ver x s_hor
+ * (1 or 2) and coded c_ver x c_hor; mean_u / mean_v the B1 codes (1/100 units). Writes the
+ * filtered planes to out_u / out_v (which may equal u / v). The crate runs it once per coded
+ * set: the first set (`upsample_set`) gives the alternative picture of the EFE non-linear
+ * filter's on/off switch, the second the filtered picture. Formats the reference does not
+ * decode return ZJAI_UNSUPPORTED, like a plane left unfiltered in a picture coded at the
+ * source's chroma resolution; mis-sized planes ZJAI_INVALID_ARGUMENT; sets out of range
+ * ZJAI_INVALID_DATA. */
+int zjai_efe_linear(zjai_ctx *ctx, const float *y, int h, int w, const float *u, const float *v,
+                    int ch, int cw, int s_ver, int s_hor, int c_ver, int c_hor, int mean_u,
+                    int mean_v, const zjai_efe_linear_set *set, float *out_u, float *out_v,
+                    int mem);
+
+/* EFE non-linear parameters (src/header.rs:655-682): the per-tile luma network
+ * (tile_width x tile_height chroma samples, ntiles entries of luma_min / luma_max in 1/100
+ * units, 8 weight codes per tile in codes[p], ncodes[p] of them; codes[p] NULL: plane p not
+ * filtered) and the on/off switch (mask[p]: mask_h x mask_w values in 0..2 for blocks of
+ * mask_bs samples, NULL: no mask). Host memory. */
+typedef struct {
+  int min_symbol;
+  int tile_width, tile_height, ntiles;
+  const uint16_t *luma_min, *luma_max;
+  const uint32_t *codes[2];
+  int ncodes[2];
+  int mask_bs, mask_h, mask_w;
+  const uint8_t *mask[2];
+} zjai_efe_nonlinear_params;
+
+/* EFE non-linear (src/filters/efe_nonlinear.rs:190-237), in place on u / v [ch][cw] (ch =
+ * ceil(h / s_ver), cw = ceil(w / s_hor)): the tile network on the planes whose codes are given,
+ * then, when the U mask is given (the reference looks at it alone), the on/off switch of each
+ * masked plane towards alt_u / alt_v (the EFE linear filter's alternative picture, required
+ * then). Bit-exact with the crate's f32 arithmetic; status codes as zjai_efe_linear. */
+int zjai_efe_nonlinear(zjai_ctx *ctx, const float *y, int h, int w, float *u, float *v, int ch,
+                       int cw, int s_ver, int s_hor, int c_ver, int c_hor,
+                       const zjai_efe_nonlinear_params *prm, const float *alt_u,
+                       const float *alt_v, int mem);
+
 /* One synthesis tile (src/tools/tiles.rs:26-32 `SynthesisTile`). */
 typedef struct {
   int img_x, img_y, img_w, img_h;

@@ -110,6 +110,11 @@ def _declare(L):
     L.zo_quantize_rgb.argtypes = [_f, _f, _f, _i64, _i, ctypes.POINTER(ctypes.c_uint16)]
     L.zo_normalize.argtypes = [_f, _i64, _f]
     L.zo_pad_amount.argtypes = [_i, _i]
+    L.zo_efe_split_edge.argtypes = [ctypes.c_double, _i]
+    L.zo_efe_linear.argtypes = [_f, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i, _i,
+                                ctypes.POINTER(EfeLinearSet), _f, _f]
+    L.zo_efe_nonlinear.argtypes = [_f, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i,
+                                   ctypes.POINTER(EfeNonlinearParams), _f, _f]
 
 
 def _fp(a):
@@ -364,6 +369,113 @@ def lef(luma, scale_log, channel, model_id, bit_depth=8):
                     c, sh, sw, channel, model_id, bit_depth, _fp(out)):
         raise ValueError("LEF: model_id / channel / bit depth / extent out of range")
     return out
+
+
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+
+
+class EfeLinearSet(ctypes.Structure):
+    _fields_ = [("cand", _i * 2), ("filter_len", _i * 2), ("min_symbol", _i),
+                ("chroma_codes", _u32p * 2), ("luma_codes", _u32p * 2)]
+
+
+class EfeNonlinearParams(ctypes.Structure):
+    _fields_ = [("min_symbol", _i), ("tile_width", _i), ("tile_height", _i), ("ntiles", _i),
+                ("luma_min", _u16p), ("luma_max", _u16p), ("codes", _u32p * 2),
+                ("ncodes", _i * 2), ("mask_bs", _i), ("mask_h", _i), ("mask_w", _i),
+                ("mask", _u8p * 2)]
+
+
+class EfeError(ValueError):
+    """A filter call the crate rejects; `status` is its zjai_status number (1 invalid
+    argument, 2 unsupported, 6 invalid data)."""
+
+    def __init__(self, status):
+        super().__init__(f"EFE: status {status}")
+        self.status = status
+
+
+def _arr(a, dtype, ptype, keep):
+    if a is None:
+        return None
+    a = np.ascontiguousarray(a, dtype=dtype).ravel()
+    keep.append(a)
+    return a.ctypes.data_as(ptype)
+
+
+def _efe_linear_set(st, keep):
+    """ctypes set from {"cand": [c_u, c_v] (-1 / None: plane not filtered), "filter_len",
+    "min_symbol", "chroma": [codes_u, codes_v], "luma": [codes_u, codes_v]}."""
+    s = EfeLinearSet()
+    for p in range(2):
+        c = st["cand"][p]
+        s.cand[p] = -1 if c is None else int(c)
+        s.filter_len[p] = int(st["filter_len"][p])
+        s.chroma_codes[p] = _arr(st["chroma"][p], np.uint32, _u32p, keep)
+        s.luma_codes[p] = _arr(st["luma"][p], np.uint32, _u32p, keep)
+    s.min_symbol = int(st.get("min_symbol", 0))
+    return s
+
+
+def efe_split_edge(fraction, s):
+    return lib().zo_efe_split_edge(float(fraction), int(s))
+
+
+def efe_linear(y, u, v, fmt, mean, st):
+    """EFE linear (src/filters/efe_linear.rs:403-460) with one coded set `st`; fmt = (s_ver,
+    s_hor, c_ver, c_hor); mean = the two B1 codes. Returns the filtered (u, v)."""
+    y, u, v = _c32(y), _c32(u), _c32(v)
+    keep = []
+    s = _efe_linear_set(st, keep)
+    ou, ov = np.empty_like(u), np.empty_like(v)
+    r = lib().zo_efe_linear(_fp(y), y.shape[0], y.shape[1], _fp(u), _fp(v), u.shape[0],
+                            u.shape[1], *fmt, int(mean[0]), int(mean[1]), ctypes.byref(s),
+                            _fp(ou), _fp(ov))
+    if r:
+        raise EfeError(r)
+    return ou, ov
+
+
+def _efe_nonlinear_params(prm, keep):
+    """ctypes parameters from {"min_symbol", "tile_width", "tile_height", "luma_min",
+    "luma_max", "codes": [u, v] (None: off), "mask_bs", "masks": [u, v] ([my, mx] arrays or
+    None)}."""
+    q = EfeNonlinearParams()
+    q.min_symbol = int(prm.get("min_symbol", 0))
+    q.tile_width = int(prm.get("tile_width", 0))
+    q.tile_height = int(prm.get("tile_height", 0))
+    lmin, lmax = prm.get("luma_min"), prm.get("luma_max")
+    q.ntiles = 0 if lmin is None else min(len(lmin), len(lmax))
+    q.luma_min = _arr(lmin, np.uint16, _u16p, keep)
+    q.luma_max = _arr(lmax, np.uint16, _u16p, keep)
+    codes = prm.get("codes", [None, None])
+    masks = prm.get("masks", [None, None])
+    geo = next((np.asarray(m).shape for m in masks if m is not None), (0, 0))
+    q.mask_bs = int(prm.get("mask_bs", 0))
+    q.mask_h, q.mask_w = int(geo[0]), int(geo[1])
+    for p in range(2):
+        q.codes[p] = _arr(codes[p], np.uint32, _u32p, keep)
+        q.ncodes[p] = 0 if codes[p] is None else int(np.asarray(codes[p]).size)
+        q.mask[p] = _arr(masks[p], np.uint8, _u8p, keep)
+    return q
+
+
+def efe_nonlinear(y, u, v, fmt, prm, alt=None):
+    """EFE non-linear (src/filters/efe_nonlinear.rs:190-237): returns the filtered (u, v);
+    alt = the EFE linear filter's alternative (u, v) or None."""
+    y = _c32(y)
+    u, v = _c32(u).copy(), _c32(v).copy()
+    keep = []
+    q = _efe_nonlinear_params(prm, keep)
+    au, av = (None, None) if alt is None else (_c32(alt[0]), _c32(alt[1]))
+    r = lib().zo_efe_nonlinear(_fp(y), y.shape[0], y.shape[1], _fp(u), _fp(v), u.shape[0],
+                               u.shape[1], *fmt, ctypes.byref(q),
+                               None if au is None else _fp(au), None if av is None else _fp(av))
+    if r:
+        raise EfeError(r)
+    return u, v
 
 
 def nearest_index(i, src, dst):

@@ -1741,3 +1741,316 @@ int zo_icci_filter(const zo_ckpt *ck_y, const zo_ckpt *ck_uv, int use_u, int use
         for (size_t i = 0; i < n; i++) planes[p][i] = clamp01(planes[p][i]) * 255.f;
     return 0;
 }
+
+
+/* ======================================================================================= */
+/* EFE post-filters (src/filters/efe_linear.rs, src/filters/efe_nonlinear.rs)              */
+/* ======================================================================================= */
+
+/* The candidate splits of a phase plane (efe_linear.rs:34-73, `EFElinear.cands`): regions as
+ * fractions [row_start, row_end, col_start, col_end]; EFE_NSPLITS = header.rs:619. Constants of
+ * the format, kept as the reference lists them. */
+static const int EFE_NSPLITS[8] = {1, 2, 2, 3, 3, 4, 6, 6};
+static const double EFE_SPLITS[8][6][4] = {
+    {{0, 1, 0, 1}},
+    {{0, .5, 0, 1}, {.5, 1, 0, 1}},
+    {{0, 1, 0, .5}, {0, 1, .5, 1}},
+    {{0, 1, 0, .33}, {0, 1, .33, .66}, {0, 1, .66, 1}},
+    {{0, .33, 0, 1}, {.33, .66, 0, 1}, {.66, 1, 0, 1}},
+    {{0, .5, 0, .5}, {0, .5, .5, 1}, {.5, 1, 0, .5}, {.5, 1, .5, 1}},
+    {{0, .33, 0, .5}, {0, .33, .5, 1}, {.33, .66, 0, .5}, {.33, .66, .5, 1}, {.66, 1, 0, .5},
+     {.66, 1, .5, 1}},
+    {{0, .5, 0, .33}, {.5, 1, 0, .33}, {0, .5, .33, .66}, {.5, 1, .33, .66}, {0, .5, .66, 1},
+     {.5, 1, .66, 1}},
+};
+/* DCT-IF 4-tap interpolation kernels of the sub-sampling phases 0..3 (efe_linear.rs:77-110),
+ * unsignalled constants of the format: horizontal, vertical and diagonal half-sample taps. */
+static const float EFE_DCT_IF[4][16] = {
+    {0},
+    {0, 0, 0, 0, -0.0625f, -0.4375f, 0.5625f, -0.0625f, 0, 0, 0, 0, 0, 0, 0, 0},
+    {0, -0.0625f, 0, 0, 0, -0.4375f, 0, 0, 0, 0.5625f, 0, 0, 0, -0.0625f, 0, 0},
+    {0.00390625f, -0.03515625f, -0.03515625f, 0.00390625f,
+     -0.03515625f, -0.68359375f, 0.31640625f, -0.03515625f,
+     -0.03515625f, 0.31640625f, 0.31640625f, -0.03515625f,
+     0.00390625f, -0.03515625f, -0.03515625f, 0.00390625f},
+};
+
+/* `deinteger` (efe_linear.rs:113-115): (code - 32767) / 2^11 in f32 */
+static float efe_deinteger(long long code) { return (float)(code - 32767) / 2048.0f; }
+
+/* round(f * (s + 31) / 32) * 32, Python's round (half to even, rint) on doubles
+ * (efe_linear.rs:128-131) */
+int zo_efe_split_edge(double fraction, int s) {
+    return (int)rint(fraction * (double)(s + 31) / 32.0) * 32;
+}
+
+typedef struct {
+    int r0, r1, c0, c1, k, before;
+    float chroma[4][16], luma[16];
+} efe_region;
+
+/* `regions` (efe_linear.rs:134-219): the non-empty regions of plane p with their kernels
+ * (identity and, below the source's chroma resolution, DCT-IF taps included). */
+static int efe_regions(const zo_efe_linear_set *set, int p, int coded_444, int s0, int s1,
+                       efe_region *out, int *nout) {
+    const int weighted = set->cand[p] >= 0;
+    const int cand = weighted ? set->cand[p] : 0, fl = weighted ? set->filter_len[p] : 0;
+    if (set->cand[p] < -1 || cand >= 8 || fl > 4 || fl < 0 || (weighted && fl == 0)) return 6;
+    if (weighted && (!set->chroma_codes[p] || !set->luma_codes[p])) return 6;
+    *nout = 0;
+    for (int num = 0; num < EFE_NSPLITS[cand]; num++) {
+        const double *sp = EFE_SPLITS[cand][num];
+        const int r0 = zo_efe_split_edge(sp[0], s0), c0 = zo_efe_split_edge(sp[2], s1);
+        int r1 = zo_efe_split_edge(sp[1], s0), c1 = zo_efe_split_edge(sp[3], s1);
+        if (r1 > s0) r1 = s0;
+        if (c1 > s1) c1 = s1;
+        if (r0 >= r1 || c0 >= c1) continue;
+        efe_region *r = &out[(*nout)++];
+        memset(r, 0, sizeof *r);
+        r->r0 = r0; r->r1 = r1; r->c0 = c0; r->c1 = c1;
+        int off;
+        if (coded_444) {
+            r->k = fl;
+            r->before = fl > 0 ? (fl - 1) / 2 : 0;
+            off = 0;
+        } else {
+            r->k = 4;
+            r->before = 1;
+            off = 1 - ((fl > 1 ? fl : 1) - 1) / 2;
+        }
+        const int k = r->k, centre = coded_444 ? (fl - 1) / 2 : 1;
+        if (weighted) {
+            const int phases = coded_444 ? 1 : 4;
+            const uint32_t *cw = set->chroma_codes[p] + (size_t)num * phases * fl * fl;
+            const uint32_t *lw = set->luma_codes[p] + (size_t)num * fl * fl;
+            for (int ky = 0; ky < fl; ky++)
+                for (int kx = 0; kx < fl; kx++) {
+                    const int dst = (off + ky) * k + off + kx;
+                    r->luma[dst] = efe_deinteger((long long)lw[ky * fl + kx] + set->min_symbol);
+                    for (int i = 0; i < 4; i++) {
+                        const int ph = coded_444 ? 0 : i;
+                        r->chroma[i][dst] = efe_deinteger(
+                            (long long)cw[(ph * fl + ky) * fl + kx] + set->min_symbol);
+                    }
+                }
+        }
+        for (int i = 0; i < 4; i++) {
+            if (!coded_444)
+                for (int t = 0; t < k * k; t++) r->chroma[i][t] += EFE_DCT_IF[i][t];
+            r->chroma[i][centre * k + centre] += 1.0f;
+        }
+    }
+    return 0;
+}
+
+/* `phase_plane` (efe_linear.rs:238-275): phase (py, px) of src [h][w] sampled every (fv, fh)
+ * samples as an s0 x s1 plane with a replicated border of 1 before and 2 after, `offset`
+ * subtracted; stride s1 + 3. */
+static float *efe_phase_plane(const float *src, int h, int w, int fv, int fh, int py, int px,
+                              int s0, int s1, float offset) {
+    const int stride = s1 + 3, rows = s0 + 3;
+    float *d = (float *)calloc((size_t)rows * stride, sizeof(float));
+    int direct = 0;
+    if (w > px) {
+        direct = (w - px + fh - 1) / fh;
+        if (direct > s1) direct = s1;
+    }
+    for (int r = 0; r < rows; r++) {
+        int sy = r > 0 ? r - 1 : 0;
+        if (sy > s0 - 1) sy = s0 - 1;
+        int row_i = sy * fv + py;
+        if (row_i > h - 1) row_i = h - 1;
+        const float *row = src + (size_t)row_i * w;
+        float *dst = d + (size_t)r * stride;
+        const int start = px < w - 1 ? px : w - 1;
+        for (int i = 0; i < direct; i++) dst[1 + i] = row[start + i * fh] - offset;
+        const float last = row[w - 1] - offset;
+        const float edge = direct > 0 ? dst[direct] : last;
+        const float fill = direct < s1 ? last : edge;
+        for (int i = 1 + direct; i < stride; i++) dst[i] = fill;
+        dst[0] = dst[1];
+    }
+    return d;
+}
+
+/* `filter_plane` (efe_linear.rs:308-359) for plane p; out [ch][cw] */
+static int efe_filter_plane(int coded_444, const zo_efe_linear_set *set, int p, float mean,
+                            int fv, int fh, int s0, int s1, float *const luma[4],
+                            float *const chroma[4], int ch, int cw, float *out) {
+    if (set->cand[p] < 0 && coded_444) return 2;
+    efe_region reg[6];
+    int nreg = 0;
+    const int st = efe_regions(set, p, coded_444, s0, s1, reg, &nreg);
+    if (st) return st;
+    const int stride = s1 + 3;
+    memset(out, 0, sizeof(float) * (size_t)ch * cw);
+    float *acc = (float *)malloc(sizeof(float) * (size_t)(s1 + 1));
+    float *lum = (float *)malloc(sizeof(float) * (size_t)(s1 + 1));
+    for (int oy = 0; oy < ch; oy++) {
+        const int py = oy % fv, yy = oy / fv;
+        float *row = out + (size_t)oy * cw;
+        for (int ri = 0; ri < nreg; ri++) {
+            const efe_region *r = &reg[ri];
+            if (!(r->r0 <= yy && yy < r->r1)) continue;
+            const int n = r->c1 - r->c0;
+            for (int px = 0; px < fh; px++) {
+                const int group = py * 2 + px;
+                const float *c = chroma[group], *l = luma[group];
+                if (!c || !l) continue;
+                for (int i = 0; i < n; i++) acc[i] = lum[i] = 0.f;
+                for (int ky = 0; ky < r->k; ky++) {
+                    const size_t line = (size_t)(yy + 1 + ky - r->before) * stride;
+                    for (int kx = 0; kx < r->k; kx++) {
+                        const size_t x0 = line + r->c0 + 1 + kx - r->before;
+                        const float wc = r->chroma[group][ky * r->k + kx];
+                        const float wl = r->luma[ky * r->k + kx];
+                        if (wc != 0.f)
+                            for (int i = 0; i < n; i++) acc[i] += wc * c[x0 + i];
+                        if (wl != 0.f)
+                            for (int i = 0; i < n; i++) lum[i] += wl * l[x0 + i];
+                    }
+                }
+                for (int i = 0; i < n; i++) {
+                    const int x = (r->c0 + i) * fh + px;
+                    if (x >= cw) break;
+                    row[x] = (acc[i] + mean) + lum[i];
+                }
+            }
+        }
+    }
+    free(acc);
+    free(lum);
+    return 0;
+}
+
+/* `supported_format` (efe_linear.rs:364-379) */
+static int efe_supported(int s_ver, int s_hor, int c_ver, int c_hor) {
+    if (s_ver == 1 && s_hor == 1)
+        return (c_ver == 1 && c_hor == 1) || (c_ver == 1 && c_hor == 2) ||
+               (c_ver == 2 && c_hor == 2);
+    if (s_ver == 1 && s_hor == 2) return c_ver == 1 && c_hor == 2;
+    if (s_ver == 2 && s_hor == 2) return c_ver == 2 && c_hor == 2;
+    return 0;
+}
+
+int zo_efe_linear(const float *y, int h, int w, const float *u, const float *v, int ch, int cw,
+                  int s_ver, int s_hor, int c_ver, int c_hor, int mean_u, int mean_v,
+                  const zo_efe_linear_set *set, float *out_u, float *out_v) {
+    if (!efe_supported(s_ver, s_hor, c_ver, c_hor)) return 2;
+    if (h <= 0 || w <= 0) return 1;
+    const int fv = 3 - s_ver, fh = 3 - s_hor, s0 = (h + 1) / 2, s1 = (w + 1) / 2;
+    if ((ch + fv - 1) / fv != s0 || (cw + fh - 1) / fh != s1) return 1;
+    /* float(code) / 100 in doubles, narrowed to f32 (efe_linear.rs:427-429) */
+    const float mean[2] = {(float)((double)mean_u / 100.0), (float)((double)mean_v / 100.0)};
+    float *luma[4] = {0}, *chroma[2][4] = {{0}};
+    for (int py = 0; py < fv; py++)
+        for (int px = 0; px < fh; px++) {
+            luma[py * 2 + px] = efe_phase_plane(y, h, w, 2, 2, py, px, s0, s1, 0.f);
+            chroma[0][py * 2 + px] = efe_phase_plane(u, ch, cw, fv, fh, py, px, s0, s1, mean[0]);
+            chroma[1][py * 2 + px] = efe_phase_plane(v, ch, cw, fv, fh, py, px, s0, s1, mean[1]);
+        }
+    const int coded_444 = c_ver == s_ver && c_hor == s_hor;
+    int st = efe_filter_plane(coded_444, set, 0, mean[0], fv, fh, s0, s1, luma, chroma[0], ch,
+                              cw, out_u);
+    if (!st)
+        st = efe_filter_plane(coded_444, set, 1, mean[1], fv, fh, s0, s1, luma, chroma[1], ch,
+                              cw, out_v);
+    for (int i = 0; i < 4; i++) {
+        free(luma[i]);
+        free(chroma[0][i]);
+        free(chroma[1][i]);
+    }
+    return st;
+}
+
+#define EFE_BINS 8
+
+/* `tile_edge` (efe_nonlinear.rs:50-53): round(float(a) / n * n) in doubles */
+static int efe_tile_edge(long long a, long long n) {
+    return (int)rint(((double)a / (double)n) * (double)n);
+}
+
+/* `filter_plane` (efe_nonlinear.rs:57-141), with the per-tile parameters of `tiles` */
+static int efe_nl_plane(const zo_efe_nonlinear_params *t, int p, const float *y, int lw, int sv,
+                        int sh, float *plane, int hh, int ww) {
+    const int th = t->tile_height, tw = t->tile_width;
+    if (th <= 0 || tw <= 0) return 6;
+    const int ni = (hh + th - 1) / th, nj = (ww + tw - 1) / tw, count = ni * nj;
+    if (t->ntiles < count || t->ncodes[p] < count * EFE_BINS || !t->luma_min || !t->luma_max)
+        return 6;
+    for (int i = 0; i < ni; i++)
+        for (int j = 0; j < nj; j++) {
+            const int idx = i * nj + j;
+            const uint32_t *cd = t->codes[p] + (size_t)idx * EFE_BINS;
+            float wv[EFE_BINS];
+            for (int k = 0; k < EFE_BINS; k++)
+                wv[k] = efe_deinteger((long long)cd[k] + t->min_symbol);
+            const double minimum = (double)t->luma_min[idx] / 100.0;
+            const double gap = ((double)t->luma_max[idx] / 100.0 - minimum) / EFE_BINS;
+            float ceil_k[EFE_BINS];
+            for (int k = 0; k < EFE_BINS; k++)
+                ceil_k[k] = -(1.0f * (float)minimum + (float)k * (float)gap);
+            const float w0 = wv[0], b0 = wv[0] * ceil_k[0];
+            const int r0 = efe_tile_edge((long long)i * th, hh);
+            const int r1 = efe_tile_edge((long long)((i + 1) * th < hh ? (i + 1) * th : hh), hh);
+            const int c0 = efe_tile_edge((long long)j * tw, ww);
+            int c1 = efe_tile_edge((long long)((j + 1) * tw < ww ? (j + 1) * tw : ww), ww);
+            if (c1 > ww) c1 = ww;
+            for (int r = r0; r < r1; r++) {
+                const float *yrow = y + (size_t)r * sv * lw;
+                float *row = plane + (size_t)r * ww;
+                for (int x = c0; x < c1; x++) {
+                    const float l = yrow[(size_t)x * sh];
+                    float acc = fmaxf(w0 * l + row[x] + b0, 0.f);
+                    for (int k = 0; k < EFE_BINS - 1; k++)
+                        acc += wv[k + 1] * fmaxf(l + ceil_k[k + 1], 0.f);
+                    row[x] = acc;
+                }
+            }
+        }
+    return 0;
+}
+
+/* `switch_plane` (efe_nonlinear.rs:145-187) */
+static int efe_switch(int bs, int my, int mx, const uint8_t *mask, const float *alt,
+                      float *plane, int h, int w) {
+    if (bs <= 0 || my != (h + bs - 1) / bs || mx != (w + bs - 1) / bs) return 6;
+    for (int y = 0; y < h; y++) {
+        const uint8_t *mrow = mask + (size_t)(y / bs) * mx;
+        for (int x = 0; x < w; x++) {
+            const uint8_t m = mrow[x / bs];
+            const size_t i = (size_t)y * w + x;
+            if (m == 0) continue;
+            plane[i] = m == 2 ? alt[i] : (alt[i] + plane[i]) / 2.0f;
+        }
+    }
+    return 0;
+}
+
+int zo_efe_nonlinear(const float *y, int h, int w, float *u, float *v, int ch, int cw,
+                     int s_ver, int s_hor, int c_ver, int c_hor,
+                     const zo_efe_nonlinear_params *prm, const float *alt_u, const float *alt_v) {
+    if (!efe_supported(s_ver, s_hor, c_ver, c_hor)) return 2;
+    if (h < 0 || w < 0) return 1;
+    const int hh = (h + s_ver - 1) / s_ver, ww = (w + s_hor - 1) / s_hor;
+    if (ch != hh || cw != ww) return 1;
+    float *planes[2] = {u, v};
+    for (int p = 0; p < 2; p++)
+        if (prm->codes[p] && hh > 0 && ww > 0) {
+            const int st = efe_nl_plane(prm, p, y, w, s_ver, s_hor, planes[p], hh, ww);
+            if (st) return st;
+        }
+    /* `has_first_mask` (efe_nonlinear.rs:31-33): the U mask decides; the alternative picture
+     * (both planes) must then be there */
+    if (prm->mask[0] && (prm->mask_h > 0 || prm->mask_w > 0)) {
+        if (!alt_u || !alt_v) return 6;
+        const float *alt[2] = {alt_u, alt_v};
+        for (int p = 0; p < 2; p++) {
+            if (!prm->mask[p]) continue;
+            const int st = efe_switch(prm->mask_bs, prm->mask_h, prm->mask_w, prm->mask[p],
+                                      alt[p], planes[p], hh, ww);
+            if (st) return st;
+        }
+    }
+    return 0;
+}

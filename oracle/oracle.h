@@ -220,6 +220,43 @@ int zo_icci_filter(const zo_ckpt *ck_y, const zo_ckpt *ck_uv, int use_u, int use
 void zo_dwt2_block(const float p[16], float out[16]);
 void zo_idwt2_block(const float s[16], float out[16]);
 
+/* EFE linear (src/filters/efe_linear.rs:120-460). One coded filter set (header.rs:623-639):
+ * per chroma plane p the split candidate cand[p] (0..7, -1: not filtered), the filter side
+ * filter_len[p], and the weight codes of the split's regions in order, chroma_codes[p]
+ * regions x P x fL x fL (P = 1 for pictures coded at the source's chroma resolution, else 4)
+ * and luma_codes[p] regions x fL x fL; min_symbol is added to every code. */
+typedef struct {
+    int cand[2], filter_len[2], min_symbol;
+    const uint32_t *chroma_codes[2], *luma_codes[2];
+} zo_efe_linear_set;
+/* `split_edge` (efe_linear.rs:128-131) */
+int zo_efe_split_edge(double fraction, int s);
+/* `apply` (efe_linear.rs:403-460) with one set: y [h][w], u / v [ch][cw] in [0, 255] of a
+ * source subsampled s_ver x s_hor and coded c_ver x c_hor; mean_* the B1 codes (1/100 units).
+ * Writes the filtered chroma planes. Returns the crate's error as a zjai_status number
+ * (0 ok, 1 invalid argument, 2 unsupported, 6 invalid data). */
+int zo_efe_linear(const float *y, int h, int w, const float *u, const float *v, int ch, int cw,
+                  int s_ver, int s_hor, int c_ver, int c_hor, int mean_u, int mean_v,
+                  const zo_efe_linear_set *set, float *out_u, float *out_v);
+
+/* EFE non-linear (src/filters/efe_nonlinear.rs:177-237) in place on u / v [ch][cw]: the
+ * per-tile luma network where codes[p] is given (8 codes per tile, ncodes[p] of them), then the
+ * on/off switch towards alt_u / alt_v where mask[0] is given (mask_h x mask_w values per plane,
+ * blocks of mask_bs samples); source / coded formats as zo_efe_linear. Return codes as
+ * zo_efe_linear. */
+typedef struct {
+    int min_symbol;
+    int tile_width, tile_height, ntiles;
+    const uint16_t *luma_min, *luma_max;
+    const uint32_t *codes[2];
+    int ncodes[2];
+    int mask_bs, mask_h, mask_w;
+    const uint8_t *mask[2];
+} zo_efe_nonlinear_params;
+int zo_efe_nonlinear(const float *y, int h, int w, float *u, float *v, int ch, int cw,
+                     int s_ver, int s_hor, int c_ver, int c_hor,
+                     const zo_efe_nonlinear_params *prm, const float *alt_u, const float *alt_v);
+
 #ifdef __cplusplus
 }
 #endif

@@ -49,6 +49,23 @@ class Tile(ctypes.Structure):
         "core_x", "core_y", "core_w", "core_h", "off_x", "off_y")]
 
 
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+
+
+class EfeLinearSet(ctypes.Structure):
+    _fields_ = [("cand", _i * 2), ("filter_len", _i * 2), ("min_symbol", _i),
+                ("chroma_codes", _u32p * 2), ("luma_codes", _u32p * 2)]
+
+
+class EfeNonlinearParams(ctypes.Structure):
+    _fields_ = [("min_symbol", _i), ("tile_width", _i), ("tile_height", _i), ("ntiles", _i),
+                ("luma_min", _u16p), ("luma_max", _u16p), ("codes", _u32p * 2),
+                ("ncodes", _i * 2), ("mask_bs", _i), ("mask_h", _i), ("mask_w", _i),
+                ("mask", _u8p * 2)]
+
+
 _lib = None
 
 
@@ -125,6 +142,10 @@ def lib():
                                    ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t)]
     L.zjai_icci_filter.argtypes = [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i]
     L.zjai_lef.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _i]
+    L.zjai_efe_linear.argtypes = [_vp, _vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i,
+                                  ctypes.POINTER(EfeLinearSet), _vp, _vp, _i]
+    L.zjai_efe_nonlinear.argtypes = [_vp, _vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i,
+                                     ctypes.POINTER(EfeNonlinearParams), _vp, _vp, _i]
     L.zjai_hyper_decode.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _i]
     L.zjai_context_decompress.argtypes = [_vp, _vp, _i, _i, _vp, _vp, _i]
     L.zjai_reconstruct_latent.argtypes = [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _vp, _i]
