@@ -4,9 +4,9 @@
 //
 // The host resolves the coded parameters (regions and kernels of the linear filter, per-tile
 // network weights of the non-linear one) exactly as the crate does; each kernel then computes
-// one output sample per thread. The crate materialises replicate-padded phase planes
-// (`phase_plane`); here a thread reads the sample a padded-plane position stands for straight
-// from the full-resolution plane (`phase_col`), so nothing but the outputs is written.
+// output samples. The crate materialises replicate-padded phase planes (`phase_plane`); here
+// the kernels read the samples a padded-plane position stands for straight from the
+// full-resolution planes (`phase_col`), so nothing but the outputs is written.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -140,51 +140,83 @@ __device__ __forceinline__ int phase_col(int sx, int px, int fh, int w, int dire
   return direct < s1 ? w - 1 : px + (direct - 1) * fh;
 }
 
-// One output chroma sample per thread, both planes (blockIdx.z): `filter_plane`
-// (efe_linear.rs:308-359) — over the region holding the sample's phase-plane position, the
-// chroma and luma taps in (ky, kx) order, zero taps skipped, each a separate multiply and add,
-// then (acc + mean) + luma. Samples in no region stay 0.
-__global__ void efe_linear_kernel(const float* __restrict__ y, int h, int w,
-                                  const float* __restrict__ u, const float* __restrict__ v,
-                                  int ch, int cw, int fv, int fh, int s0, int s1,
-                                  const EfeLinearTables* __restrict__ tab,
-                                  float* __restrict__ out_u, float* __restrict__ out_v) {
-  const int ox = blockIdx.x * blockDim.x + threadIdx.x;
-  const int p = blockIdx.z;
-  if (ox >= cw) return;
+// `filter_plane` (efe_linear.rs:308-359). A block takes a 32 x 32 tile of one phase plane
+// (blockIdx.z = plane * groups + sub-sampling phase group): split edges are multiples of 32, so
+// the tile lies in one region (or in none: its samples stay 0). The block stages the padded
+// windows of the chroma phase (mean subtracted) and of the luma phase that its taps reach in
+// shared memory, each sample read once from the full-resolution plane with the padded phase
+// plane's clamping done as index arithmetic; a thread then sums its outputs' chroma and luma
+// taps in (ky, kx) order, zero taps skipped, each a separate multiply and add, and stores
+// (acc + mean) + luma.
+constexpr int kEfeTile = 32, kEfeWin = kEfeTile + 3;
+__global__ void __launch_bounds__(256) efe_linear_kernel(
+    const float* __restrict__ y, int h, int w, const float* __restrict__ u,
+    const float* __restrict__ v, int ch, int cw, int fv, int fh, int s0, int s1,
+    const EfeLinearTables* __restrict__ tab, float* __restrict__ out_u,
+    float* __restrict__ out_v) {
+  __shared__ float cwin[kEfeWin][kEfeWin], lwin[kEfeWin][kEfeWin];
+  __shared__ float wc[16], wl[16];
+  const int ngroups = fv * fh;
+  const int p = blockIdx.z / ngroups, gi = blockIdx.z - p * ngroups;
+  const int py = gi / fh, px = gi - py * fh, group = py * 2 + px;
+  const int xx0 = blockIdx.x * kEfeTile, yy0 = blockIdx.y * kEfeTile;
+  const int tid = threadIdx.y * 32 + threadIdx.x;
   const float* src = p ? v : u;
   float* out = p ? out_v : out_u;
-  for (int oy = blockIdx.y; oy < ch; oy += gridDim.y) {
-    const int py = oy % fv, yy = oy / fv, px = ox % fh, xx = ox / fh;
-    const EfeRegion* reg = nullptr;
-    for (int i = 0; i < tab->nreg[p]; ++i) {
-      const EfeRegion* r = &tab->reg[p][i];
-      if (r->r0 <= yy && yy < r->r1 && r->c0 <= xx && xx < r->c1) reg = r;
+  const EfeRegion* reg = nullptr;
+  for (int i = 0; i < tab->nreg[p]; ++i) {
+    const EfeRegion* r = &tab->reg[p][i];
+    if (r->r0 <= yy0 && yy0 < r->r1 && r->c0 <= xx0 && xx0 < r->c1) reg = r;
+  }
+  const int k = reg ? reg->k : 0, before = reg ? reg->before : 0;
+  const float mean = tab->mean[p];
+  if (reg) {
+    if (tid < 16) {
+      wc[tid] = tid < k * k ? reg->chroma[group][tid] : 0.f;
+      wl[tid] = tid < k * k ? reg->luma[tid] : 0.f;
     }
+    // samples of the phase available without clamping (`direct` of phase_plane)
+    const int dc = cw > px ? min((cw - px + fh - 1) / fh, s1) : 0;
+    const int dl = w > px ? min((w - px + 1) / 2, s1) : 0;
+    const int wn = kEfeTile + k - 1;
+    // the window's columns (phase column xx0 + j - before clamped at 0, the right side by
+    // phase_col) are the same for every row: a thread keeps its one or two
+    const int j0 = threadIdx.x, j1 = threadIdx.x + 32;
+    const int cx0 = phase_col(max(xx0 - before + j0, 0), px, fh, cw, dc, s1);
+    const int lx0 = phase_col(max(xx0 - before + j0, 0), px, 2, w, dl, s1);
+    const int cx1 = phase_col(max(xx0 - before + j1, 0), px, fh, cw, dc, s1);
+    const int lx1 = phase_col(max(xx0 - before + j1, 0), px, 2, w, dl, s1);
+    for (int i = threadIdx.y; i < wn; i += 8) {
+      // padded row yy0 + i + 1 - before: phase row yy0 + i - before clamped to the plane
+      const int sy = min(max(yy0 - before + i, 0), s0 - 1);
+      const float* crow = src + (long long)min(sy * fv + py, ch - 1) * cw;
+      const float* lrow = y + (long long)min(sy * 2 + py, h - 1) * w;
+      cwin[i][j0] = __fsub_rn(__ldg(crow + cx0), mean);
+      lwin[i][j0] = __ldg(lrow + lx0);
+      if (j1 < wn) {
+        cwin[i][j1] = __fsub_rn(__ldg(crow + cx1), mean);
+        lwin[i][j1] = __ldg(lrow + lx1);
+      }
+    }
+  }
+  __syncthreads();
+  const int tx = threadIdx.x, ox = (xx0 + tx) * fh + px;
+#pragma unroll
+  for (int q = 0; q < kEfeTile / 8; ++q) {
+    const int ty = threadIdx.y + 8 * q, oy = (yy0 + ty) * fv + py;
+    if (oy >= ch || ox >= cw) continue;
     float res = 0.f;
     if (reg) {
-      const int group = py * 2 + px, k = reg->k, before = reg->before;
-      const float mean = tab->mean[p];
-      // samples of the phase available without clamping (`direct` of phase_plane)
-      const int dc = cw > px ? min((cw - px + fh - 1) / fh, s1) : 0;
-      const int dl = w > px ? min((w - px + 1) / 2, s1) : 0;
       float acc = 0.f, lum = 0.f;
-      for (int ky = 0; ky < k; ++ky) {
-        // padded row yy + 1 + ky - before, i.e. phase row yy + ky - before clamped to the plane
-        const int sy = min(max(yy + ky - before, 0), s0 - 1);
-        const float* crow = src + (long long)min(sy * fv + py, ch - 1) * cw;
-        const float* lrow = y + (long long)min(sy * 2 + py, h - 1) * w;
-        for (int kx = 0; kx < k; ++kx) {
-          const int sx = max(xx + kx - before, 0);
-          const float wc = reg->chroma[group][ky * k + kx], wl = reg->luma[ky * k + kx];
-          if (wc != 0.f) {
-            const float c = __fsub_rn(__ldg(crow + phase_col(sx, px, fh, cw, dc, s1)), mean);
-            acc = __fadd_rn(acc, __fmul_rn(wc, c));
-          }
-          if (wl != 0.f) {
-            const float l = __ldg(lrow + phase_col(sx, px, 2, w, dl, s1));
-            lum = __fadd_rn(lum, __fmul_rn(wl, l));
-          }
+#pragma unroll
+      for (int ky = 0; ky < 4; ++ky) {
+        if (ky >= k) break;
+#pragma unroll
+        for (int kx = 0; kx < 4; ++kx) {
+          if (kx >= k) break;
+          const float a = wc[ky * k + kx], b = wl[ky * k + kx];
+          if (a != 0.f) acc = __fadd_rn(acc, __fmul_rn(a, cwin[ty + ky][tx + kx]));
+          if (b != 0.f) lum = __fadd_rn(lum, __fmul_rn(b, lwin[ty + ky][tx + kx]));
         }
       }
       res = __fadd_rn(__fadd_rn(acc, mean), lum);
@@ -309,12 +341,12 @@ int zjai_efe_linear(zjai_ctx* ctx, const float* y, int h, int w, const float* u,
   float *dou, *dov;
   ZJAI_TRY(stage_out_alloc(ctx, out_u, nc, mem, &dou));
   ZJAI_TRY(stage_out_alloc(ctx, out_v, nc, mem, &dov));
-  dim3 grid((cw + 127) / 128, std::min(ch, 65535), 2);
+  dim3 grid((s1 + kEfeTile - 1) / kEfeTile, (s0 + kEfeTile - 1) / kEfeTile, 2 * fv * fh);
   ctx->launches++;
   if (ctx->profiling) ctx->tag = "EFE linear";
   timed_launch(ctx, false, 0.0, 4.0 * n + 16.0 * nc, [&] {
-    efe_linear_kernel<<<grid, 128, 0, ctx->stream>>>(dy, h, w, du, dv, ch, cw, fv, fh, s0, s1,
-                                                     dtab, dou, dov);
+    efe_linear_kernel<<<grid, dim3(32, 8), 0, ctx->stream>>>(dy, h, w, du, dv, ch, cw, fv, fh,
+                                                             s0, s1, dtab, dou, dov);
   });
   ZJAI_TRY(cuda_check(cudaGetLastError(), "EFE linear launch"));
   ZJAI_TRY(stage_out_finish(ctx, out_u, dou, nc, mem));
