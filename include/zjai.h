@@ -476,6 +476,23 @@ int zjai_conv_transpose2d(zjai_ctx *ctx, const float *x, int c, int h, int w,
                           const float *weight, const float *bias, int oc, int k, int pad,
                           int out_pad, float *out, int mem);
 
+/* The RDLR VJPs of those two layers: input gradients, which the encoder's latent refinement
+ * chains through the synthesis network. `ConvLayer::backward` (layers.rs:72-90, over
+ * `conv2d_backward`, reference.rs:241-292): dout [oc][oh][ow], the output extent of the layer
+ * above on an input [c][h][w] with the zero border `extra` (or NULL) -> din [c][h][w]; strides 1
+ * and 2 (stride 2: dense square kernels without extra border). `ConvTransposeLayer::backward`
+ * (layers.rs:156-160, `conv_transpose2d_backward`, reference.rs:294-336) of a stride-2
+ * transposed conv with weight [c][oc][k][k] on an input [c][h][w]. Both run as convolutions
+ * on the tensor cores (f16 operands, d_out scaled by a power of two first, f32 accumulation):
+ * within about 1e-3 relative L2 of the crate's f32 loops, not bit-exact. */
+int zjai_conv2d_backward(zjai_ctx *ctx, const float *dout, int oc, int oh, int ow,
+                         const float *weight, int c, int kh, int kw, int stride, int pad_h,
+                         int pad_w, int groups, const int *extra, int h, int w, float *din,
+                         int mem);
+int zjai_conv_transpose2d_backward(zjai_ctx *ctx, const float *dout, int oc, int oh, int ow,
+                                   const float *weight, int c, int k, int pad, int h, int w,
+                                   float *din, int mem);
+
 /* `math::layer_norm_channels` (math.rs:423-448), out of place. */
 int zjai_layer_norm(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,
                     const float *bias, float *out, int mem);

@@ -110,6 +110,9 @@ def _declare(L):
     L.zo_quantize_rgb.argtypes = [_f, _f, _f, _i64, _i, ctypes.POINTER(ctypes.c_uint16)]
     L.zo_normalize.argtypes = [_f, _i64, _f]
     L.zo_pad_amount.argtypes = [_i, _i]
+    L.zo_conv2d_backward.argtypes = [_f, _i, _i, _i, _f, _i, _i, _i, _i, _i, _i, _i,
+                                     ctypes.POINTER(_i), _i, _i, _f]
+    L.zo_conv_transpose2d_backward.argtypes = [_f, _i, _i, _i, _f, _i, _i, _i, _i, _i, _i, _f]
     L.zo_efe_split_edge.argtypes = [ctypes.c_double, _i]
     L.zo_efe_linear.argtypes = [_f, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i, _i,
                                 ctypes.POINTER(EfeLinearSet), _f, _f]
@@ -176,6 +179,34 @@ def conv_transpose2d(x, w, b=None, stride=2, pad=1, out_pad=0):
                                   out_pad, _fp(out))
     if r:
         raise ValueError("oracle conv_transpose2d: bad geometry")
+    return out
+
+
+def conv2d_backward(dout, w, h, wd, stride=1, pad=(0, 0), groups=1, extra=None):
+    """Input gradient of `conv2d` (reference.rs:241-292, layers.rs:72-90): dout [oc, oh, ow],
+    w [oc, c/groups, kh, kw] -> [c, h, wd] (h, wd: the layer input without its extra border)."""
+    dout, w = _c32(dout), _c32(w)
+    oc, oh, ow = dout.shape
+    _, icg, kh, kw = w.shape
+    c = icg * groups
+    out = np.empty((c, h, wd), np.float32)
+    ex = (_i * 4)(*extra) if extra is not None else None
+    if lib().zo_conv2d_backward(_fp(dout), oc, oh, ow, _fp(w), c, kh, kw, stride, pad[0],
+                                pad[1], groups, ex, h, wd, _fp(out)):
+        raise ValueError("oracle conv2d_backward: bad geometry")
+    return out
+
+
+def conv_transpose2d_backward(dout, w, h, wd, stride=2, pad=1):
+    """Input gradient of `conv_transpose2d` (reference.rs:294-336): dout [oc, oh, ow],
+    w [c, oc, k, k] -> [c, h, wd]."""
+    dout, w = _c32(dout), _c32(w)
+    oc, oh, ow = dout.shape
+    c, _, k, _ = w.shape
+    out = np.empty((c, h, wd), np.float32)
+    if lib().zo_conv_transpose2d_backward(_fp(dout), oc, oh, ow, _fp(w), c, k, stride, pad, h,
+                                          wd, _fp(out)):
+        raise ValueError("oracle conv_transpose2d_backward: bad geometry")
     return out
 
 

@@ -2054,3 +2054,91 @@ int zo_efe_nonlinear(const float *y, int h, int w, float *u, float *v, int ch, i
     }
     return 0;
 }
+
+
+/* ======================================================================================= */
+/* RDLR layer VJPs: input gradients of the conv layers (src/nn/reference.rs:238-336,        */
+/* src/nn/fast/layers.rs:72-90, 156-160)                                                    */
+/* ======================================================================================= */
+
+/* `conv2d_backward` (reference.rs:241-292) through `ConvLayer::backward` (layers.rs:72-90):
+ * the gradient on the padded input (h + top + bottom) x (w + left + right), each d_out sample's
+ * products `g_o * w` added in the crate's loop order (output channel, its group's input
+ * channels, output row, column, ky, kx; zero d_out samples skipped), then the extra border
+ * dropped. The input channels are independent, so they run in parallel. */
+int zo_conv2d_backward(const float *dout, int oc, int oh, int ow, const float *weight, int c,
+                       int kh, int kw, int stride, int pad_h, int pad_w, int groups,
+                       const int extra[4], int h, int w, float *din) {
+    if (oc <= 0 || c <= 0 || groups <= 0 || c % groups || oc % groups || h <= 0 || w <= 0 ||
+        stride <= 0)
+        return -1;
+    const int pt = extra ? extra[0] : 0, pl = extra ? extra[1] : 0;
+    const int pb = extra ? extra[2] : 0, pr = extra ? extra[3] : 0;
+    const int H = h + pt + pb, W = w + pl + pr;
+    const int icg = c / groups, ocg = oc / groups;
+    float *full = (float *)calloc((size_t)c * H * W, sizeof(float));
+    if (!full) return -1;
+#pragma omp parallel for schedule(dynamic) num_threads(g_threads)
+    for (int c_in = 0; c_in < c; c_in++) {
+        const int g = c_in / icg, ci = c_in % icg;
+        float *dst = full + (size_t)c_in * H * W;
+        for (int co = g * ocg; co < (g + 1) * ocg; co++) {
+            const float *wb = weight + ((size_t)co * icg + ci) * kh * kw;
+            const float *d = dout + (size_t)co * oh * ow;
+            for (int oy = 0; oy < oh; oy++)
+                for (int ox = 0; ox < ow; ox++) {
+                    const float g_o = d[(size_t)oy * ow + ox];
+                    if (g_o == 0.0f) continue;
+                    for (int ky = 0; ky < kh; ky++) {
+                        const int y = oy * stride + ky;
+                        if (y < pad_h || y - pad_h >= H) continue;
+                        const int iy = y - pad_h;
+                        for (int kx = 0; kx < kw; kx++) {
+                            const int x = ox * stride + kx;
+                            if (x < pad_w || x - pad_w >= W) continue;
+                            dst[(size_t)iy * W + x - pad_w] += g_o * wb[ky * kw + kx];
+                        }
+                    }
+                }
+        }
+    }
+    for (int ch = 0; ch < c; ch++)
+        for (int y = 0; y < h; y++)
+            memcpy(din + ((size_t)ch * h + y) * w, full + ((size_t)ch * H + y + pt) * W + pl,
+                   sizeof(float) * w);
+    free(full);
+    return 0;
+}
+
+/* `conv_transpose2d_backward` (reference.rs:294-336): per input channel, per output channel of
+ * the transposed conv, per input position the taps' products summed in (ky, kx) order, then
+ * added to the gradient (weight [c][oc][k][k]). */
+int zo_conv_transpose2d_backward(const float *dout, int oc, int oh, int ow, const float *weight,
+                                 int c, int k, int stride, int pad, int h, int w, float *din) {
+    if (oc <= 0 || c <= 0 || k <= 0 || stride <= 0 || h <= 0 || w <= 0) return -1;
+#pragma omp parallel for schedule(dynamic) num_threads(g_threads)
+    for (int ic = 0; ic < c; ic++) {
+        float *dst = din + (size_t)ic * h * w;
+        memset(dst, 0, sizeof(float) * (size_t)h * w);
+        const float *wb = weight + (size_t)ic * oc * k * k;
+        for (int o = 0; o < oc; o++) {
+            const float *d = dout + (size_t)o * oh * ow;
+            for (int y = 0; y < h; y++)
+                for (int x = 0; x < w; x++) {
+                    float acc = 0.0f;
+                    for (int ky = 0; ky < k; ky++) {
+                        const int oy = y * stride + ky;
+                        if (oy < pad || oy - pad >= oh) continue;
+                        for (int kx = 0; kx < k; kx++) {
+                            const int ox = x * stride + kx;
+                            if (ox < pad || ox - pad >= ow) continue;
+                            acc += d[(size_t)(oy - pad) * ow + ox - pad] *
+                                   wb[(size_t)o * k * k + ky * k + kx];
+                        }
+                    }
+                    dst[(size_t)y * w + x] += acc;
+                }
+        }
+    }
+    return 0;
+}

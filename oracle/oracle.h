@@ -257,6 +257,18 @@ int zo_efe_nonlinear(const float *y, int h, int w, float *u, float *v, int ch, i
                      int s_ver, int s_hor, int c_ver, int c_hor,
                      const zo_efe_nonlinear_params *prm, const float *alt_u, const float *alt_v);
 
+/* RDLR layer VJPs, the input gradients of the conv layers. `conv2d_backward`
+ * (reference.rs:241-292) through `ConvLayer::backward` (layers.rs:72-90): d_out [oc][oh][ow]
+ * of a conv with weight [oc][c/groups][kh][kw] and zero border extra ([top, left, bottom,
+ * right] or NULL) on an input [c][h][w] -> din [c][h][w]. */
+int zo_conv2d_backward(const float *dout, int oc, int oh, int ow, const float *weight, int c,
+                       int kh, int kw, int stride, int pad_h, int pad_w, int groups,
+                       const int extra[4], int h, int w, float *din);
+/* `conv_transpose2d_backward` (reference.rs:294-336): d_out [oc][oh][ow] of a transposed conv
+ * with weight [c][oc][k][k] on an input [c][h][w] -> din [c][h][w]. */
+int zo_conv_transpose2d_backward(const float *dout, int oc, int oh, int ow, const float *weight,
+                                 int c, int k, int stride, int pad, int h, int w, float *din);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,96 @@
+"""RDLR layer VJPs on the GPU through the C ABI (`zjai_conv2d_backward`,
+`zjai_conv_transpose2d_backward`): the input gradients of the synthesis network's conv layer
+shapes (3x3 residual-block convs, the grouped ResAU conv, 1x1 projections, depthwise 3x3, the
+stride-2 CAB subscale conv, a zero-bordered conv, the upsampling transposed convs) against the
+oracle's restatement of the crate's f32 loops. The GPU path runs them as convolutions with f16
+operands (d_out scaled by a power of two first) and f32 accumulation: relative L2 within 2e-3,
+also for gradients of 1e-7 magnitude, which unscaled f16 could not hold."""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+import oracle as zo
+
+TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def eng():
+    import zenjpegai_b200 as zj
+    e = zj.Engine(0, arena_bytes=1 << 30)
+    yield e
+    e.close()
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm((a - b).ravel()) / max(np.linalg.norm(b.ravel()), 1e-30))
+
+
+def he(rng, shape, fan_in):
+    return (rng.standard_normal(shape) * np.sqrt(2.0 / fan_in)).astype(np.float32)
+
+
+@pytest.mark.parametrize("c,oc,k,stride,pad,groups,extra,h,w", [
+    (128, 128, 3, 1, 1, 1, None, 40, 36),      # residual block conv
+    (128, 128, 3, 1, 1, 4, None, 33, 30),      # ResAU grouped conv
+    (128, 384, 1, 1, 0, 1, None, 32, 32),      # prep / qkv projection
+    (384, 128, 1, 1, 0, 1, None, 24, 40),      # output projection
+    (64, 64, 3, 1, 1, 64, None, 31, 29),       # depthwise
+    (128, 128, 3, 2, 1, 1, None, 33, 29),      # CAB subscale, odd extent
+    (160, 64, 3, 2, 1, 1, None, 32, 48),       # stride 2, even extent
+    (64, 96, 3, 1, 1, 1, (0, 1, 1, 0), 30, 26),  # zero-bordered conv
+    (96, 16, 3, 1, 1, 1, None, 27, 35),
+])
+@pytest.mark.parametrize("mag", [1.0, 1e-7])
+def test_conv2d_backward(eng, c, oc, k, stride, pad, groups, extra, h, w, mag):
+    rng = np.random.default_rng(c + oc + k * 10 + stride * 100 + h)
+    wt = he(rng, (oc, c // groups, k, k), c // groups * k * k)
+    H, W = h + (extra[0] + extra[2] if extra else 0), w + (extra[1] + extra[3] if extra else 0)
+    oh, ow = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+    d = (rng.standard_normal((oc, oh, ow)) * mag).astype(np.float32)
+    want = zo.conv2d_backward(d, wt, h, w, stride, (pad, pad), groups, extra)
+    got = eng.conv2d_backward(d, wt, h, w, stride, (pad, pad), groups, extra)
+    assert got.shape == want.shape
+    assert rel_l2(got, want) < TOL
+
+
+@pytest.mark.parametrize("c,oc,k,pad,out_pad,h,w", [
+    (160, 64, 4, 1, 0, 17, 15),    # BOP / SOP upsampling convT 4x4
+    (128, 128, 3, 1, 1, 16, 18),   # HOP upsampling convT 3x3
+    (64, 64, 4, 1, 0, 32, 24),
+    (128, 4, 3, 1, 1, 20, 21),     # final layer shape (few outputs)
+])
+@pytest.mark.parametrize("mag", [1.0, 1e-7])
+def test_conv_transpose2d_backward(eng, c, oc, k, pad, out_pad, h, w, mag):
+    rng = np.random.default_rng(c + oc + k + h)
+    wt = he(rng, (c, oc, k, k), c * k * k)
+    oh, ow = (h - 1) * 2 - 2 * pad + k + out_pad, (w - 1) * 2 - 2 * pad + k + out_pad
+    d = (rng.standard_normal((oc, oh, ow)) * mag).astype(np.float32)
+    want = zo.conv_transpose2d_backward(d, wt, h, w, 2, pad)
+    got = eng.conv_transpose2d_backward(d, wt, h, w, pad)
+    assert rel_l2(got, want) < TOL
+
+
+def test_device_tensors_and_errors(eng):
+    import torch
+    import zenjpegai_b200 as zj
+    rng = np.random.default_rng(3)
+    wt = he(rng, (64, 32, 3, 3), 32 * 9)
+    d = rng.standard_normal((64, 20, 22)).astype(np.float32)
+    want = zo.conv2d_backward(d, wt, 20, 22, 1, (1, 1), 1)
+    got = eng.conv2d_backward(torch.from_numpy(d).cuda(), torch.from_numpy(wt).cuda(), 20, 22,
+                              1, (1, 1), 1)
+    torch.cuda.synchronize()
+    assert rel_l2(got.cpu().numpy(), want) < TOL
+    # a d_out that is not the layer's output extent
+    with pytest.raises(zj.ZjaiError) as e:
+        eng.conv2d_backward(d, wt, 21, 22, 1, (1, 1), 1)
+    assert e.value.status == zj._lib.INVALID_ARGUMENT
+    with pytest.raises(zj.ZjaiError) as e:
+        eng.conv2d_backward(d[:, :10, :11], wt, 20, 22, 2, (1, 1), 1, extra=(1, 0, 0, 0))
+    assert e.value.status in (zj._lib.INVALID_ARGUMENT, zj._lib.UNSUPPORTED)
+    # an all-zero gradient gives zeros
+    z = eng.conv2d_backward(np.zeros_like(d), wt, 20, 22, 1, (1, 1), 1)
+    assert not z.any()

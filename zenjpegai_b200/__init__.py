@@ -162,6 +162,41 @@ class Engine:
                                                out_pad, po, mem))
         return out
 
+    def conv2d_backward(self, dout, weight, h, w, stride=1, pad=(0, 0), groups=1, extra=None,
+                        out=None):
+        """Input gradient of `conv2d` (`ConvLayer::backward`, the RDLR VJP): dout [oc, oh, ow]
+        of the layer on an input [c, h, w] -> [c, h, w]."""
+        oc, oh, ow = dout.shape
+        _, icg, kh, kw = weight.shape
+        c = icg * groups
+        if out is None:
+            out = _like(dout, (c, h, w))
+        pd, mem = _arg(dout)
+        pw, m2 = _arg(weight)
+        po, m3 = _arg(out, (c, h, w))
+        if len({mem, m2, m3}) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        exa = (ctypes.c_int * 4)(*extra) if extra else None
+        check(_lib.lib().zjai_conv2d_backward(self.handle, pd, oc, oh, ow, pw, c, kh, kw, stride,
+                                              pad[0], pad[1], groups, exa, h, w, po, mem))
+        return out
+
+    def conv_transpose2d_backward(self, dout, weight, h, w, pad=1, out=None):
+        """Input gradient of the stride-2 `conv_transpose2d` (`ConvTransposeLayer::backward`):
+        dout [oc, oh, ow], weight [c, oc, k, k] -> [c, h, w]."""
+        oc, oh, ow = dout.shape
+        c, _, k, _ = weight.shape
+        if out is None:
+            out = _like(dout, (c, h, w))
+        pd, mem = _arg(dout)
+        pw, m2 = _arg(weight)
+        po, m3 = _arg(out, (c, h, w))
+        if len({mem, m2, m3}) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        check(_lib.lib().zjai_conv_transpose2d_backward(self.handle, pd, oc, oh, ow, pw, c, k, pad,
+                                                        h, w, po, mem))
+        return out
+
     def layer_norm(self, x, weight, bias, out=None):
         c, h, w = x.shape
         out = _like(x, x.shape) if out is None else out

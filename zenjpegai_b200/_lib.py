@@ -162,6 +162,10 @@ def lib():
     L.zjai_conv2d.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i,
                               ctypes.POINTER(_i), _i, _vp, _i]
     L.zjai_conv_transpose2d.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _i, _i, _vp, _i]
+    L.zjai_conv2d_backward.argtypes = [_vp, _vp, _i, _i, _i, _vp, _i, _i, _i, _i, _i, _i, _i,
+                                       _vp, _i, _i, _vp, _i]
+    L.zjai_conv_transpose2d_backward.argtypes = [_vp, _vp, _i, _i, _i, _vp, _i, _i, _i, _i, _i,
+                                                 _vp, _i]
     L.zjai_layer_norm.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]
     L.zjai_channel_attention.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i]
     L.zjai_depthwise3x3.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i]
