@@ -145,8 +145,8 @@ __device__ __forceinline__ int phase_col(int sx, int px, int fh, int w, int dire
 // the tile lies in one region (or in none: its samples stay 0). The block stages the padded
 // windows of the chroma phase (mean subtracted) and of the luma phase that its taps reach in
 // shared memory, each sample read once from the full-resolution plane with the padded phase
-// plane's clamping done as index arithmetic; a thread then sums its outputs' chroma and luma
-// taps in (ky, kx) order, zero taps skipped, each a separate multiply and add, and stores
+// plane's clamping done as index arithmetic; a thread then sums its four outputs' chroma and
+// luma taps in (ky, kx) order, zero taps skipped, each a separate multiply and add, and stores
 // (acc + mean) + luma.
 constexpr int kEfeTile = 32, kEfeWin = kEfeTile + 3;
 __global__ void __launch_bounds__(256) efe_linear_kernel(
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(256) efe_linear_kernel(
     const EfeLinearTables* __restrict__ tab, float* __restrict__ out_u,
     float* __restrict__ out_v) {
   __shared__ float cwin[kEfeWin][kEfeWin], lwin[kEfeWin][kEfeWin];
-  __shared__ float wc[16], wl[16];
+  __shared__ float wc[16], wl[16];  // taps at [ky * 4 + kx], zero outside the k x k kernel
   const int ngroups = fv * fh;
   const int p = blockIdx.z / ngroups, gi = blockIdx.z - p * ngroups;
   const int py = gi / fh, px = gi - py * fh, group = py * 2 + px;
@@ -172,8 +172,10 @@ __global__ void __launch_bounds__(256) efe_linear_kernel(
   const float mean = tab->mean[p];
   if (reg) {
     if (tid < 16) {
-      wc[tid] = tid < k * k ? reg->chroma[group][tid] : 0.f;
-      wl[tid] = tid < k * k ? reg->luma[tid] : 0.f;
+      const int ky = tid >> 2, kx = tid & 3;
+      const bool in = ky < k && kx < k;
+      wc[tid] = in ? reg->chroma[group][ky * k + kx] : 0.f;
+      wl[tid] = in ? reg->luma[ky * k + kx] : 0.f;
     }
     // samples of the phase available without clamping (`direct` of phase_plane)
     const int dc = cw > px ? min((cw - px + fh - 1) / fh, s1) : 0;
@@ -200,28 +202,41 @@ __global__ void __launch_bounds__(256) efe_linear_kernel(
     }
   }
   __syncthreads();
-  const int tx = threadIdx.x, ox = (xx0 + tx) * fh + px;
+  // a thread's four outputs are the vertically adjacent rows r0 .. r0 + 3 of its column: each
+  // window sample it loads serves every output whose taps reach it, in the outputs' (ky, kx)
+  // order (window row rr = q + ky, so rr ascending is ky ascending for output q)
+  const int tx = threadIdx.x, ox = (xx0 + tx) * fh + px, r0 = threadIdx.y * 4;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f}, lum[4] = {0.f, 0.f, 0.f, 0.f};
+  if (reg) {
+    float wcr[16], wlr[16];
 #pragma unroll
-  for (int q = 0; q < kEfeTile / 8; ++q) {
-    const int ty = threadIdx.y + 8 * q, oy = (yy0 + ty) * fv + py;
-    if (oy >= ch || ox >= cw) continue;
-    float res = 0.f;
-    if (reg) {
-      float acc = 0.f, lum = 0.f;
+    for (int i = 0; i < 16; ++i) {
+      wcr[i] = wc[i];
+      wlr[i] = wl[i];
+    }
 #pragma unroll
-      for (int ky = 0; ky < 4; ++ky) {
-        if (ky >= k) break;
+    for (int rr = 0; rr < 7; ++rr) {
+      if (rr >= k + 3) break;
 #pragma unroll
-        for (int kx = 0; kx < 4; ++kx) {
-          if (kx >= k) break;
-          const float a = wc[ky * k + kx], b = wl[ky * k + kx];
-          if (a != 0.f) acc = __fadd_rn(acc, __fmul_rn(a, cwin[ty + ky][tx + kx]));
-          if (b != 0.f) lum = __fadd_rn(lum, __fmul_rn(b, lwin[ty + ky][tx + kx]));
+      for (int kx = 0; kx < 4; ++kx) {
+        if (kx >= k) break;
+        const float cv = cwin[r0 + rr][tx + kx], lv = lwin[r0 + rr][tx + kx];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int ky = rr - q;
+          if (ky < 0 || ky > 3 || ky >= k) continue;
+          const float a = wcr[ky * 4 + kx], b = wlr[ky * 4 + kx];
+          if (a != 0.f) acc[q] = __fadd_rn(acc[q], __fmul_rn(a, cv));
+          if (b != 0.f) lum[q] = __fadd_rn(lum[q], __fmul_rn(b, lv));
         }
       }
-      res = __fadd_rn(__fadd_rn(acc, mean), lum);
     }
-    out[(long long)oy * cw + ox] = res;
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int oy = (yy0 + r0 + q) * fv + py;
+    if (oy >= ch || ox >= cw) continue;
+    out[(long long)oy * cw + ox] = reg ? __fadd_rn(__fadd_rn(acc[q], mean), lum[q]) : 0.f;
   }
 }
 
