@@ -492,6 +492,13 @@ int zjai_conv2d_backward(zjai_ctx *ctx, const float *dout, int oc, int oh, int o
 int zjai_conv_transpose2d_backward(zjai_ctx *ctx, const float *dout, int oc, int oh, int ow,
                                    const float *weight, int c, int k, int pad, int h, int w,
                                    float *din, int mem);
+/* `ResidualBlock::backward` (src/model/attention.rs:58-75), the first network-level VJP of the
+ * RDLR HOP chain: d_out [c][h][w] of `conv3x3 -> ReLU -> conv3x3 + x` and its tape conv1_out
+ * [c][h][w] (conv1's output before the ReLU) -> din = d_out + conv1^T(relu'(conv1_out) .
+ * conv2^T d_out); w1 / w2 the convs' weights [c][c][3][3]. Tolerance as zjai_conv2d_backward. */
+int zjai_residual_block_backward(zjai_ctx *ctx, const float *dout, const float *conv1_out,
+                                 int c, int h, int w, const float *w1, const float *w2,
+                                 float *din, int mem);
 
 /* `math::layer_norm_channels` (math.rs:423-448), out of place. */
 int zjai_layer_norm(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,

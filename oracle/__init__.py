@@ -113,6 +113,7 @@ def _declare(L):
     L.zo_conv2d_backward.argtypes = [_f, _i, _i, _i, _f, _i, _i, _i, _i, _i, _i, _i,
                                      ctypes.POINTER(_i), _i, _i, _f]
     L.zo_conv_transpose2d_backward.argtypes = [_f, _i, _i, _i, _f, _i, _i, _i, _i, _i, _i, _f]
+    L.zo_residual_block_backward.argtypes = [_f, _f, _i, _i, _i, _f, _f, _f]
     L.zo_efe_split_edge.argtypes = [ctypes.c_double, _i]
     L.zo_efe_linear.argtypes = [_f, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i, _i,
                                 ctypes.POINTER(EfeLinearSet), _f, _f]
@@ -207,6 +208,17 @@ def conv_transpose2d_backward(dout, w, h, wd, stride=2, pad=1):
     if lib().zo_conv_transpose2d_backward(_fp(dout), oc, oh, ow, _fp(w), c, k, stride, pad, h,
                                           wd, _fp(out)):
         raise ValueError("oracle conv_transpose2d_backward: bad geometry")
+    return out
+
+
+def residual_block_backward(dout, conv1_out, w1, w2):
+    """`ResidualBlock::backward` (attention.rs:58-75): dout, conv1_out [c, h, w], conv weights
+    [c, c, 3, 3] -> d_x [c, h, w]."""
+    dout, t, w1, w2 = _c32(dout), _c32(conv1_out), _c32(w1), _c32(w2)
+    c, h, w = dout.shape
+    out = np.empty_like(dout)
+    if lib().zo_residual_block_backward(_fp(dout), _fp(t), c, h, w, _fp(w1), _fp(w2), _fp(out)):
+        raise ValueError("oracle residual_block_backward: bad geometry")
     return out
 
 

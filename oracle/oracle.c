@@ -2142,3 +2142,22 @@ int zo_conv_transpose2d_backward(const float *dout, int oc, int oh, int ow, cons
     }
     return 0;
 }
+
+/* `ResidualBlock::backward` (attention.rs:58-75): d = conv2^T d_out; d = 0 where the tape
+ * conv1_out <= 0; din = conv1^T d + d_out (3x3 convs, padding 1, c -> c). */
+int zo_residual_block_backward(const float *dout, const float *conv1_out, int c, int h, int w,
+                               const float *w1, const float *w2, float *din) {
+    const size_t n = (size_t)c * h * w;
+    float *d = (float *)malloc(sizeof(float) * n);
+    if (!d) return -1;
+    int r = zo_conv2d_backward(dout, c, h, w, w2, c, 3, 3, 1, 1, 1, 1, NULL, h, w, d);
+    if (!r) {
+        for (size_t i = 0; i < n; i++)
+            if (conv1_out[i] <= 0.0f) d[i] = 0.0f;
+        r = zo_conv2d_backward(d, c, h, w, w1, c, 3, 3, 1, 1, 1, 1, NULL, h, w, din);
+    }
+    if (!r)
+        for (size_t i = 0; i < n; i++) din[i] += dout[i];
+    free(d);
+    return r;
+}

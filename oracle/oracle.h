@@ -268,6 +268,10 @@ int zo_conv2d_backward(const float *dout, int oc, int oh, int ow, const float *w
  * with weight [c][oc][k][k] on an input [c][h][w] -> din [c][h][w]. */
 int zo_conv_transpose2d_backward(const float *dout, int oc, int oh, int ow, const float *weight,
                                  int c, int k, int stride, int pad, int h, int w, float *din);
+/* `ResidualBlock::backward` (attention.rs:58-75): d_out and the tape conv1_out [c][h][w], conv
+ * weights [c][c][3][3] -> din [c][h][w]. */
+int zo_residual_block_backward(const float *dout, const float *conv1_out, int c, int h, int w,
+                               const float *w1, const float *w2, float *din);
 
 #ifdef __cplusplus
 }

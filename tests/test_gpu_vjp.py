@@ -94,3 +94,17 @@ def test_device_tensors_and_errors(eng):
     # an all-zero gradient gives zeros
     z = eng.conv2d_backward(np.zeros_like(d), wt, 20, 22, 1, (1, 1), 1)
     assert not z.any()
+
+
+@pytest.mark.parametrize("c,h,w", [(128, 40, 36), (64, 33, 47), (160, 24, 24)])
+@pytest.mark.parametrize("mag", [1.0, 1e-7])
+def test_residual_block_backward(eng, c, h, w, mag):
+    rng = np.random.default_rng(c + h + w)
+    x = rng.standard_normal((c, h, w)).astype(np.float32)
+    w1, w2 = he(rng, (c, c, 3, 3), c * 9), he(rng, (c, c, 3, 3), c * 9)
+    b1 = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    tape = zo.conv2d(x, w1, b1, 1, (1, 1))
+    d = (rng.standard_normal((c, h, w)) * mag).astype(np.float32)
+    want = zo.residual_block_backward(d, tape, w1, w2)
+    got = eng.residual_block_backward(d, tape, w1, w2)
+    assert rel_l2(got, want) < TOL

@@ -63,3 +63,44 @@ def test_conv2d_backward_of_a_one_hot_gradient_is_the_flipped_kernel():
     want = np.zeros((3, 6, 7), np.float32)
     want[:, 1:4, 2:5] = wt[1]
     assert np.array_equal(dx, want)
+
+
+def conv3x3_f64(x, w, b):
+    """3x3 conv, padding 1, in float64 (the finite differences' forward)."""
+    c, h, wd = x.shape
+    xp = np.pad(x.astype(np.float64), ((0, 0), (1, 1), (1, 1)))
+    out = np.zeros((w.shape[0], h, wd)) + np.asarray(b, np.float64)[:, None, None]
+    for ky in range(3):
+        for kx in range(3):
+            out += np.einsum("oc,chw->ohw", w[:, :, ky, kx].astype(np.float64),
+                             xp[:, ky:ky + h, kx:kx + wd])
+    return out
+
+
+def test_residual_block_backward_matches_finite_differences():
+    # ResidualBlock::backward (attention.rs:58-75) against the block's forward
+    # conv2(relu(conv1(x) + b1)) + b2 + x: <d_out, F(x + e v) - F(x - e v)> / 2e = <d_x, v>
+    # (the step small enough that no pre-activation crosses the ReLU's kink)
+    rng = np.random.default_rng(11)
+    c, h, w = 8, 12, 10
+    x = rng.standard_normal((c, h, w)).astype(np.float32)
+    w1 = (rng.standard_normal((c, c, 3, 3)) * 0.2).astype(np.float32)
+    w2 = (rng.standard_normal((c, c, 3, 3)) * 0.2).astype(np.float32)
+    b1 = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    b2 = (rng.standard_normal(c) * 0.1).astype(np.float32)
+
+    def forward(xx):
+        t = conv3x3_f64(xx, w1, b1)
+        return conv3x3_f64(np.maximum(t, 0), w2, b2) + xx, t
+
+    y, tape = forward(x)
+    d = rng.standard_normal(y.shape).astype(np.float32)
+    dx = zo.residual_block_backward(d, tape.astype(np.float32), w1, w2)
+    v = rng.standard_normal(x.shape).astype(np.float32)
+    eps = 1e-3
+    lhs = float((d * (forward(x + eps * v)[0] - forward(x - eps * v)[0])).sum()) / (2 * eps)
+    rhs = float((dx.astype(np.float64) * v).sum())
+    assert rel(lhs, rhs) < 1e-3, (lhs, rhs)
+    # the skip alone: with zero conv weights the gradient is d_out
+    z = np.zeros_like(w1)
+    assert np.array_equal(zo.residual_block_backward(d, tape.astype(np.float32), z, z), d)

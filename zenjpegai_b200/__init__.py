@@ -197,6 +197,23 @@ class Engine:
                                                         h, w, po, mem))
         return out
 
+    def residual_block_backward(self, dout, conv1_out, w1, w2, out=None):
+        """`ResidualBlock::backward` (the RDLR VJP of conv3x3 -> ReLU -> conv3x3 + x): dout and
+        the tape conv1_out [c, h, w], conv weights [c, c, 3, 3] -> d_x [c, h, w]."""
+        c, h, w = dout.shape
+        if out is None:
+            out = _like(dout, (c, h, w))
+        pd, mem = _arg(dout)
+        pt, m1 = _arg(conv1_out, (c, h, w))
+        p1, m2 = _arg(w1, (c, c, 3, 3))
+        p2, m3 = _arg(w2, (c, c, 3, 3))
+        po, m4 = _arg(out, (c, h, w))
+        if len({mem, m1, m2, m3, m4}) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        check(_lib.lib().zjai_residual_block_backward(self.handle, pd, pt, c, h, w, p1, p2, po,
+                                                      mem))
+        return out
+
     def layer_norm(self, x, weight, bias, out=None):
         c, h, w = x.shape
         out = _like(x, x.shape) if out is None else out

@@ -166,6 +166,7 @@ def lib():
                                        _vp, _i, _i, _vp, _i]
     L.zjai_conv_transpose2d_backward.argtypes = [_vp, _vp, _i, _i, _i, _vp, _i, _i, _i, _i, _i,
                                                  _vp, _i]
+    L.zjai_residual_block_backward.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]
     L.zjai_layer_norm.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]
     L.zjai_channel_attention.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i]
     L.zjai_depthwise3x3.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i]

@@ -10,6 +10,8 @@
 //   [oc][c][k][k] is a transposed-conv weight with c outputs), cut to the input extent.
 // * conv_transpose2d: the stride-2 conv with the same weights (a transposed-conv weight
 //   [c][oc][k][k] is a conv weight with c outputs).
+// * ResidualBlock (attention.rs:58-75): conv2's VJP, masked by relu' of the block's tape
+//   (conv1's output), conv1's VJP, plus the skip's d_out.
 //
 // The tensor cores take f16 operands: d_out is scaled by a power of two that brings its largest
 // magnitude into [2^13, 2^14) before the f16 conversion (RDLR gradients are small: unscaled
@@ -43,6 +45,24 @@ __global__ void scale_kernel(const float* __restrict__ x, size_t n, float s,
     y[i] = x[i] * s;
 }
 
+// relu' of the tape: g = 0 where the pre-activation p <= 0 (attention.rs:64-69)
+__global__ void relu_mask_kernel(float* __restrict__ g, const float* __restrict__ p, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    if (p[i] <= 0.f) g[i] = 0.f;
+}
+
+__global__ void add_kernel(float* __restrict__ a, const float* __restrict__ b, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    a[i] += b[i];
+}
+
+// grid of the grid-stride elementwise kernels
+int launch_elementwise_blocks(Ctx* ctx, size_t n) {
+  return (int)std::max<size_t>(1, std::min<size_t>((n + 255) / 256, (size_t)ctx->sms * 8));
+}
+
 // Power of two that brings amax into [2^(top - 1), 2^top) (1 for zero or non-finite amax).
 float grad_scale(float amax, int top) {
   if (!(amax > 0.f) || !std::isfinite(amax)) return 1.f;
@@ -59,7 +79,7 @@ int stage_grad(Ctx* ctx, const float* d, int c, int h, int w, int top, TView* t,
   float* scaled = static_cast<float*>(ctx->arena.alloc(n * sizeof(float)));
   if (!dmax || !scaled) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (VJP d_out)");
   ZJAI_TRY(cuda_check(cudaMemsetAsync(dmax, 0, sizeof(unsigned), ctx->stream), "memset"));
-  const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sms * 8);
+  const int blocks = launch_elementwise_blocks(ctx, n);
   amax_kernel<<<blocks, 256, 0, ctx->stream>>>(d, n, dmax);
   ctx->launches++;
   unsigned bits = 0;
@@ -93,6 +113,32 @@ int run_into(Ctx* ctx, ConvLayer& L, float s, const TView& t, float* din, int h,
   o.cx0 = 0;
   o.cx1 = w;
   return run_conv(ctx, L, t, o);
+}
+
+// the input gradient of a stride-1 conv (weight [oc][c/groups][kh][kw], host) from the device
+// planar gradient dd [oc][oh][ow] into the device planar din [c][h][w] of an input with zero
+// border (pt, pl) in front: the flipped, channel-swapped kernel with padding k - 1 - pad
+int conv_vjp_s1(Ctx* ctx, const float* dd, int oc, int oh, int ow, const float* hw, int c, int kh,
+                int kw, int pad_h, int pad_w, int groups, int h, int w, int pt, int pl,
+                float* din) {
+  const int icg = c / groups, ocg = oc / groups;
+  // W'[g icg + ci][co][ky][kx] = w[g ocg + co][ci][kh - 1 - ky][kw - 1 - kx]
+  std::vector<float> wt((size_t)c * ocg * kh * kw);
+  for (int g = 0; g < groups; ++g)
+    for (int co = 0; co < ocg; ++co)
+      for (int ci = 0; ci < icg; ++ci)
+        for (int ky = 0; ky < kh; ++ky)
+          for (int kx = 0; kx < kw; ++kx)
+            wt[((((size_t)g * icg + ci) * ocg + co) * kh + ky) * kw + kx] =
+                hw[((((size_t)g * ocg + co) * icg + ci) * kh + kh - 1 - ky) * kw + kw - 1 - kx];
+  ConvLayer L;
+  ZJAI_TRY(pack_conv(ctx, &L, wt.data(), nullptr, oc, c, kh, kw, 1, kh - 1 - pad_h,
+                     kw - 1 - pad_w, groups, nullptr, 1));
+  LayerGuard guard(&L);
+  TView t;
+  float s;
+  ZJAI_TRY(stage_grad(ctx, dd, oc, oh, ow, 14, &t, &s));
+  return run_into(ctx, L, s, t, din, h, w, pt, pl);
 }
 
 }  // namespace
@@ -132,7 +178,7 @@ int zjai_conv2d_backward(zjai_ctx* ctx, const float* dout, int oc, int oh, int o
   if (stride == 2 && pad_h >= kh)
     return fail(ZJAI_UNSUPPORTED, "conv2d_backward: padding wider than the kernel");
   ArenaScope scope(ctx);
-  const int icg = c / groups, ocg = oc / groups;
+  const int icg = c / groups;
   std::vector<float> wbuf;
   const float* hw;
   ZJAI_TRY(fetch_host(weight, (size_t)oc * icg * kh * kw, mem, &wbuf, &hw));
@@ -160,35 +206,24 @@ int zjai_conv2d_backward(zjai_ctx* ctx, const float* dout, int oc, int oh, int o
     float* tmp = static_cast<float*>(ctx->arena.alloc(nin * sizeof(float)));
     if (!tmp) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (VJP output)");
     launch_nhwc_to_planar(o, tmp, ctx->stream);
-    const int blocks = (int)std::min<size_t>((nin + 255) / 256, (size_t)ctx->sms * 8);
-    scale_kernel<<<blocks, 256, 0, ctx->stream>>>(tmp, nin, 1.f / s, ddin);
+    scale_kernel<<<launch_elementwise_blocks(ctx, nin), 256, 0, ctx->stream>>>(tmp, nin, 1.f / s,
+                                                                             ddin);
     ctx->launches += 3;
     // `flip` is a host vector: its copy must have been read before it goes
     ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "VJP depthwise"));
+  } else if (stride == 1) {
+    ZJAI_TRY(conv_vjp_s1(ctx, dd, oc, oh, ow, hw, c, kh, kw, pad_h, pad_w, groups, h, w, pt, pl,
+                         ddin));
   } else {
+    // out_pad 1: the transposed conv covers the input extent (one row / column beyond it where
+    // the forward's output size rounded down, dropped by the crop)
     ConvLayer L;
-    if (stride == 1) {
-      // W'[g icg + ci][co][ky][kx] = w[g ocg + co][ci][kh - 1 - ky][kw - 1 - kx]
-      std::vector<float> wt((size_t)c * ocg * kh * kw);
-      for (int g = 0; g < groups; ++g)
-        for (int co = 0; co < ocg; ++co)
-          for (int ci = 0; ci < icg; ++ci)
-            for (int ky = 0; ky < kh; ++ky)
-              for (int kx = 0; kx < kw; ++kx)
-                wt[((((size_t)g * icg + ci) * ocg + co) * kh + ky) * kw + kx] =
-                    hw[((((size_t)g * ocg + co) * icg + ci) * kh + kh - 1 - ky) * kw + kw - 1 - kx];
-      ZJAI_TRY(pack_conv(ctx, &L, wt.data(), nullptr, oc, c, kh, kw, 1, kh - 1 - pad_h,
-                         kw - 1 - pad_w, groups, nullptr, 1));
-    } else {
-      // out_pad 1: the transposed conv covers the input extent (one row / column beyond it
-      // where the forward's output size rounded down, dropped by the crop)
-      ZJAI_TRY(pack_convT(ctx, &L, hw, nullptr, oc, c, kh, pad_h, 1, 1));
-    }
+    ZJAI_TRY(pack_convT(ctx, &L, hw, nullptr, oc, c, kh, pad_h, 1, 1));
     LayerGuard guard(&L);
     TView t;
     float s;
     ZJAI_TRY(stage_grad(ctx, dd, oc, oh, ow, 14, &t, &s));
-    ZJAI_TRY(run_into(ctx, L, s, t, ddin, h, w, pt, pl));
+    ZJAI_TRY(run_into(ctx, L, s, t, ddin, h, w, 0, 0));
   }
   ZJAI_TRY(stage_out_finish(ctx, din, ddin, nin, mem));
   return ctx_check_status(ctx);
@@ -225,6 +260,39 @@ int zjai_conv_transpose2d_backward(zjai_ctx* ctx, const float* dout, int oc, int
   ZJAI_TRY(stage_grad(ctx, dd, oc, oh, ow, 14, &t, &s));
   ZJAI_TRY(run_into(ctx, L, s, t, ddin, h, w, 0, 0));
   ZJAI_TRY(stage_out_finish(ctx, din, ddin, nin, mem));
+  return ctx_check_status(ctx);
+}
+
+int zjai_residual_block_backward(zjai_ctx* ctx, const float* dout, const float* conv1_out,
+                                 int c, int h, int w, const float* w1, const float* w2,
+                                 float* din, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!dout || !conv1_out || !w1 || !w2 || !din || c <= 0 || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "residual_block_backward: bad arguments");
+  if (mem != ZJAI_MEM_HOST && mem != ZJAI_MEM_DEVICE)
+    return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  ArenaScope scope(ctx);
+  const size_t n = (size_t)c * h * w, nw = (size_t)c * c * 9;
+  std::vector<float> b1, b2;
+  const float *h1, *h2;
+  ZJAI_TRY(fetch_host(w1, nw, mem, &b1, &h1));
+  ZJAI_TRY(fetch_host(w2, nw, mem, &b2, &h2));
+  const float *dd, *dp;
+  ZJAI_TRY(stage_in(ctx, dout, n, mem, &dd));
+  ZJAI_TRY(stage_in(ctx, conv1_out, n, mem, &dp));
+  float* ddin;
+  ZJAI_TRY(stage_out_alloc(ctx, din, n, mem, &ddin));
+  float* d = static_cast<float*>(ctx->arena.alloc(n * sizeof(float)));
+  if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (residual block VJP)");
+  const int blocks = launch_elementwise_blocks(ctx, n);
+  // conv2^T d_out, masked by relu'(conv1_out); conv1^T of that, plus the skip's d_out
+  ZJAI_TRY(conv_vjp_s1(ctx, dd, c, h, w, h2, c, 3, 3, 1, 1, 1, h, w, 0, 0, d));
+  relu_mask_kernel<<<blocks, 256, 0, ctx->stream>>>(d, dp, n);
+  ZJAI_TRY(conv_vjp_s1(ctx, d, c, h, w, h1, c, 3, 3, 1, 1, 1, h, w, 0, 0, ddin));
+  add_kernel<<<blocks, 256, 0, ctx->stream>>>(ddin, dd, n);
+  ctx->launches += 2;
+  ZJAI_TRY(cuda_check(cudaGetLastError(), "residual block VJP"));
+  ZJAI_TRY(stage_out_finish(ctx, din, ddin, n, mem));
   return ctx_check_status(ctx);
 }
 
