@@ -500,6 +500,29 @@ int zjai_residual_block_backward(zjai_ctx *ctx, const float *dout, const float *
                                  int c, int h, int w, const float *w1, const float *w2,
                                  float *din, int mem);
 
+/* `Cab::backward` (src/model/attention.rs:182-223) of the CAB block x + trunk(x) .
+ * sigmoid(mask(x)) on c channels at h x w (even): the tape of `Cab::forward_tape` — trunk_pre
+ * (the trunk's output before the product), sig (the sigmoid of the mask), rb_c1 (the trunk
+ * residual blocks' conv1 outputs) [c][h][w], and mask_c1 (the mask residual blocks' conv1
+ * outputs) [c][h/2][w/2] — and the layers' weights ([c][c][3][3] each: the residual blocks'
+ * conv1 and conv2, the stride-2 subscale conv, the upscale transposed conv [c][c][3][3]). All
+ * arrays in the memory `mem` names. Tolerance as zjai_conv2d_backward. */
+typedef struct {
+  const float *trunk_pre, *sig;
+  const float *rb_c1[2];
+  const float *mask_c1[2];
+} zjai_cab_tape;
+typedef struct {
+  const float *trunk[2][2];  /* residual_trunk.{0,1}.{conv1,conv2} */
+  const float *subscale;
+  const float *mask2[2];     /* residual_mask2.0.{conv1,conv2} */
+  const float *mask3[2];     /* residual_mask3.0.{conv1,conv2} */
+  const float *upscale;
+} zjai_cab_weights;
+int zjai_cab_backward(zjai_ctx *ctx, const float *dout, int c, int h, int w,
+                      const zjai_cab_tape *tape, const zjai_cab_weights *wts, float *din,
+                      int mem);
+
 /* `math::layer_norm_channels` (math.rs:423-448), out of place. */
 int zjai_layer_norm(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,
                     const float *bias, float *out, int mem);

@@ -114,6 +114,7 @@ def _declare(L):
                                      ctypes.POINTER(_i), _i, _i, _f]
     L.zo_conv_transpose2d_backward.argtypes = [_f, _i, _i, _i, _f, _i, _i, _i, _i, _i, _i, _f]
     L.zo_residual_block_backward.argtypes = [_f, _f, _i, _i, _i, _f, _f, _f]
+    L.zo_cab_backward.argtypes = [_f, _i, _i, _i, _f * 4, _f * 2, _f * 10, _f]
     L.zo_efe_split_edge.argtypes = [ctypes.c_double, _i]
     L.zo_efe_linear.argtypes = [_f, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i, _i,
                                 ctypes.POINTER(EfeLinearSet), _f, _f]
@@ -219,6 +220,27 @@ def residual_block_backward(dout, conv1_out, w1, w2):
     out = np.empty_like(dout)
     if lib().zo_residual_block_backward(_fp(dout), _fp(t), c, h, w, _fp(w1), _fp(w2), _fp(out)):
         raise ValueError("oracle residual_block_backward: bad geometry")
+    return out
+
+
+CAB_WEIGHTS = ("trunk0.conv1", "trunk0.conv2", "trunk1.conv1", "trunk1.conv2", "subscale",
+               "mask2.conv1", "mask2.conv2", "mask3.conv1", "mask3.conv2", "upscale")
+
+
+def cab_backward(dout, tape, weights):
+    """`Cab::backward` (attention.rs:182-223): dout [c, h, w]; tape {"trunk_pre", "sig",
+    "rb_c1": [2], "mask_c1": [2]}; weights {name in CAB_WEIGHTS: [c, c, 3, 3]} -> d_x."""
+    dout = _c32(dout)
+    c, h, w = dout.shape
+    ts = [_c32(tape["trunk_pre"]), _c32(tape["sig"]), _c32(tape["rb_c1"][0]),
+          _c32(tape["rb_c1"][1])]
+    ms = [_c32(m) for m in tape["mask_c1"]]
+    ws = [_c32(weights[k]) for k in CAB_WEIGHTS]
+    out = np.empty_like(dout)
+    if lib().zo_cab_backward(_fp(dout), c, h, w, (_f * 4)(*[_fp(a) for a in ts]),
+                             (_f * 2)(*[_fp(a) for a in ms]), (_f * 10)(*[_fp(a) for a in ws]),
+                             _fp(out)):
+        raise ValueError("oracle cab_backward: bad geometry")
     return out
 
 

@@ -2161,3 +2161,38 @@ int zo_residual_block_backward(const float *dout, const float *conv1_out, int c,
     free(d);
     return r;
 }
+
+/* `Cab::backward` (attention.rs:182-223): tape t = {trunk_pre, sig, rb_c1[0], rb_c1[1]}
+ * [c][h][w] and mask_c1[2] [c][h/2][w/2]; weights wt = {trunk0 conv1, conv2, trunk1 conv1,
+ * conv2, subscale, mask2 conv1, conv2, mask3 conv1, conv2, upscale}, each [c][c][3][3]. */
+int zo_cab_backward(const float *dout, int c, int h, int w, const float *const t[4],
+                    const float *const mask_c1[2], const float *const wt[10], float *din) {
+    if (c <= 0 || h <= 0 || w <= 0 || h % 2 || w % 2) return -1;
+    const int mh = h / 2, mw = w / 2;
+    const size_t n = (size_t)c * h * w, nm = (size_t)c * mh * mw;
+    float *dtr = (float *)malloc(sizeof(float) * n), *dsg = (float *)malloc(sizeof(float) * n);
+    float *t1 = (float *)malloc(sizeof(float) * n);
+    float *m1 = (float *)malloc(sizeof(float) * nm), *m2 = (float *)malloc(sizeof(float) * nm);
+    int r = (!dtr || !dsg || !t1 || !m1 || !m2) ? -1 : 0;
+    if (!r) {
+        for (size_t i = 0; i < n; i++) {
+            const float s = t[1][i];
+            dtr[i] = dout[i] * s;
+            float ds = dout[i] * t[0][i];
+            ds *= s * (1.0f - s);
+            dsg[i] = ds;
+        }
+        r = zo_residual_block_backward(dtr, t[3], c, h, w, wt[2], wt[3], t1);
+        if (!r) r = zo_residual_block_backward(t1, t[2], c, h, w, wt[0], wt[1], din);
+        if (!r) r = zo_conv_transpose2d_backward(dsg, c, h, w, wt[9], c, 3, 2, 1, mh, mw, m1);
+        if (!r) r = zo_residual_block_backward(m1, mask_c1[1], c, mh, mw, wt[7], wt[8], m2);
+        if (!r) r = zo_residual_block_backward(m2, mask_c1[0], c, mh, mw, wt[5], wt[6], m1);
+        if (!r) r = zo_conv2d_backward(m1, c, mh, mw, wt[4], c, 3, 3, 2, 1, 1, 1, NULL, h, w, t1);
+        if (!r) {
+            for (size_t i = 0; i < n; i++) din[i] += t1[i];
+            for (size_t i = 0; i < n; i++) din[i] += dout[i];
+        }
+    }
+    free(dtr); free(dsg); free(t1); free(m1); free(m2);
+    return r;
+}

@@ -272,6 +272,12 @@ int zo_conv_transpose2d_backward(const float *dout, int oc, int oh, int ow, cons
  * weights [c][c][3][3] -> din [c][h][w]. */
 int zo_residual_block_backward(const float *dout, const float *conv1_out, int c, int h, int w,
                                const float *w1, const float *w2, float *din);
+/* `Cab::backward` (attention.rs:182-223): tape t = {trunk_pre, sig, trunk RB0 conv1 output,
+ * trunk RB1 conv1 output} [c][h][w], mask_c1 = the mask RBs' conv1 outputs [c][h/2][w/2];
+ * weights wt = trunk0 conv1, conv2, trunk1 conv1, conv2, subscale, mask2 conv1, conv2, mask3
+ * conv1, conv2, upscale (each [c][c][3][3]). */
+int zo_cab_backward(const float *dout, int c, int h, int w, const float *const t[4],
+                    const float *const mask_c1[2], const float *const wt[10], float *din);
 
 #ifdef __cplusplus
 }

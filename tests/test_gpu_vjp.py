@@ -108,3 +108,21 @@ def test_residual_block_backward(eng, c, h, w, mag):
     want = zo.residual_block_backward(d, tape, w1, w2)
     got = eng.residual_block_backward(d, tape, w1, w2)
     assert rel_l2(got, want) < TOL
+
+
+@pytest.mark.parametrize("c,h,w", [(128, 32, 40), (64, 26, 18)])
+@pytest.mark.parametrize("mag", [1.0, 1e-7])
+def test_cab_backward(eng, c, h, w, mag):
+    # a chain of eight conv VJPs per call: 3e-3 relative L2
+    from test_vjp_oracle import cab_case, cab_forward_f64
+    rng = np.random.default_rng(c + h + w)
+    x, wts, bias = cab_case(rng, c, h, w)
+    _, tape = cab_forward_f64(x, wts, bias)
+    tape = {"trunk_pre": tape["trunk_pre"].astype(np.float32),
+            "sig": tape["sig"].astype(np.float32),
+            "rb_c1": [a.astype(np.float32) for a in tape["rb_c1"]],
+            "mask_c1": [a.astype(np.float32) for a in tape["mask_c1"]]}
+    d = (rng.standard_normal((c, h, w)) * mag).astype(np.float32)
+    want = zo.cab_backward(d, tape, wts)
+    got = eng.cab_backward(d, tape, wts)
+    assert rel_l2(got, want) < 3e-3

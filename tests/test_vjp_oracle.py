@@ -104,3 +104,67 @@ def test_residual_block_backward_matches_finite_differences():
     # the skip alone: with zero conv weights the gradient is d_out
     z = np.zeros_like(w1)
     assert np.array_equal(zo.residual_block_backward(d, tape.astype(np.float32), z, z), d)
+
+
+CAB_NAMES = ("trunk0.conv1", "trunk0.conv2", "trunk1.conv1", "trunk1.conv2", "subscale",
+             "mask2.conv1", "mask2.conv2", "mask3.conv1", "mask3.conv2", "upscale")
+
+
+def convT3_s2_f64(x, w, b):
+    """`conv3x3_t` (attention.rs:77-80): transposed conv, kernel 3, stride 2, padding 1, output
+    padding 1, weight [c][oc][3][3], in float64: input (iy, ix) feeds output
+    (2 iy - 1 + ky, 2 ix - 1 + kx)."""
+    c, h, wd = x.shape
+    oc = w.shape[1]
+    out = np.zeros((oc, 2 * h, 2 * wd)) + np.asarray(b, np.float64)[:, None, None]
+    for ky in range(3):
+        for kx in range(3):
+            contrib = np.einsum("co,chw->ohw", w[:, :, ky, kx].astype(np.float64),
+                                x.astype(np.float64))
+            ys, xs = 2 * np.arange(h) - 1 + ky, 2 * np.arange(wd) - 1 + kx
+            vy, vx = (ys >= 0) & (ys < 2 * h), (xs >= 0) & (xs < 2 * wd)
+            out[:, ys[vy][:, None], xs[vx][None, :]] += contrib[:, vy][:, :, vx]
+    return out
+
+
+def cab_forward_f64(x, wts, bias):
+    """`Cab::forward_tape` (attention.rs:146-180) in float64: output and tape."""
+    def rb(xx, a, b):
+        t = conv3x3_f64(xx, wts[a], bias[a])
+        return conv3x3_f64(np.maximum(t, 0), wts[b], bias[b]) + xx, t
+    t0, rb0 = rb(x, "trunk0.conv1", "trunk0.conv2")
+    trunk, rb1 = rb(t0, "trunk1.conv1", "trunk1.conv2")
+    m = conv3x3_f64(x, wts["subscale"], bias["subscale"])[:, ::2, ::2]  # stride 2, padding 1
+    m, mc0 = rb(m, "mask2.conv1", "mask2.conv2")
+    m, mc1 = rb(m, "mask3.conv1", "mask3.conv2")
+    sig = 1.0 / (1.0 + np.exp(-convT3_s2_f64(m, wts["upscale"], bias["upscale"])))
+    tape = {"trunk_pre": trunk, "sig": sig, "rb_c1": [rb0, rb1], "mask_c1": [mc0, mc1]}
+    return trunk * sig + x, tape
+
+
+def cab_case(rng, c, h, w):
+    wts = {k: (rng.standard_normal((c, c, 3, 3)) * (0.6 / np.sqrt(9 * c))).astype(np.float32)
+           for k in CAB_NAMES}
+    bias = {k: (rng.standard_normal(c) * 0.05).astype(np.float32) for k in CAB_NAMES}
+    x = rng.standard_normal((c, h, w)).astype(np.float32)
+    return x, wts, bias
+
+
+def test_cab_backward_matches_finite_differences():
+    # Cab::backward (attention.rs:182-223) against finite differences of the CAB's forward
+    rng = np.random.default_rng(21)
+    x, wts, bias = cab_case(rng, 8, 12, 14)
+    y, tape = cab_forward_f64(x, wts, bias)
+    d = rng.standard_normal(y.shape).astype(np.float32)
+    tape32 = {"trunk_pre": tape["trunk_pre"].astype(np.float32),
+              "sig": tape["sig"].astype(np.float32),
+              "rb_c1": [a.astype(np.float32) for a in tape["rb_c1"]],
+              "mask_c1": [a.astype(np.float32) for a in tape["mask_c1"]]}
+    dx = zo.cab_backward(d, tape32, wts)
+    v = rng.standard_normal(x.shape).astype(np.float32)
+    eps = 1e-3
+    fp = cab_forward_f64(x + eps * v, wts, bias)[0]
+    fm = cab_forward_f64(x - eps * v, wts, bias)[0]
+    lhs = float((d * (fp - fm)).sum()) / (2 * eps)
+    rhs = float((dx.astype(np.float64) * v).sum())
+    assert rel(lhs, rhs) < 1e-3, (lhs, rhs)

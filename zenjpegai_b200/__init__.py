@@ -214,6 +214,48 @@ class Engine:
                                                       mem))
         return out
 
+    CAB_WEIGHTS = ("trunk0.conv1", "trunk0.conv2", "trunk1.conv1", "trunk1.conv2", "subscale",
+                   "mask2.conv1", "mask2.conv2", "mask3.conv1", "mask3.conv2", "upscale")
+
+    def cab_backward(self, dout, tape, weights, out=None):
+        """`Cab::backward` (the RDLR VJP of x + trunk(x) . sigmoid(mask(x))): dout [c, h, w];
+        tape {"trunk_pre", "sig", "rb_c1": [2 arrays], "mask_c1": [2 arrays at h/2 x w/2]};
+        weights {name in CAB_WEIGHTS: [c, c, 3, 3]} -> d_x [c, h, w]."""
+        c, h, w = dout.shape
+        if out is None:
+            out = _like(dout, (c, h, w))
+        pd, mem = _arg(dout)
+        po, m = _arg(out, (c, h, w))
+        mems = {mem, m}
+        t = _lib.CabTape()
+        for name in ("trunk_pre", "sig"):
+            p, m = _arg(tape[name], (c, h, w))
+            setattr(t, name, p)
+            mems.add(m)
+        for i in range(2):
+            p, m = _arg(tape["rb_c1"][i], (c, h, w))
+            t.rb_c1[i] = p
+            mems.add(m)
+            p, m = _arg(tape["mask_c1"][i], (c, h // 2, w // 2))
+            t.mask_c1[i] = p
+            mems.add(m)
+        wts = _lib.CabWeights()
+        ptr = {}
+        for k in self.CAB_WEIGHTS:
+            ptr[k], m = _arg(weights[k], (c, c, 3, 3))
+            mems.add(m)
+        for i in range(2):
+            for j in range(2):
+                wts.trunk[i][j] = ptr["trunk%d.conv%d" % (i, j + 1)]
+            wts.mask2[i] = ptr["mask2.conv%d" % (i + 1)]
+            wts.mask3[i] = ptr["mask3.conv%d" % (i + 1)]
+        wts.subscale, wts.upscale = ptr["subscale"], ptr["upscale"]
+        if len(mems) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        check(_lib.lib().zjai_cab_backward(self.handle, pd, c, h, w, ctypes.byref(t),
+                                           ctypes.byref(wts), po, mem))
+        return out
+
     def layer_norm(self, x, weight, bias, out=None):
         c, h, w = x.shape
         out = _like(x, x.shape) if out is None else out

@@ -66,6 +66,15 @@ class EfeNonlinearParams(ctypes.Structure):
                 ("mask", _u8p * 2)]
 
 
+class CabTape(ctypes.Structure):
+    _fields_ = [("trunk_pre", _vp), ("sig", _vp), ("rb_c1", _vp * 2), ("mask_c1", _vp * 2)]
+
+
+class CabWeights(ctypes.Structure):
+    _fields_ = [("trunk", (_vp * 2) * 2), ("subscale", _vp), ("mask2", _vp * 2),
+                ("mask3", _vp * 2), ("upscale", _vp)]
+
+
 _lib = None
 
 
@@ -167,6 +176,8 @@ def lib():
     L.zjai_conv_transpose2d_backward.argtypes = [_vp, _vp, _i, _i, _i, _vp, _i, _i, _i, _i, _i,
                                                  _vp, _i]
     L.zjai_residual_block_backward.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]
+    L.zjai_cab_backward.argtypes = [_vp, _vp, _i, _i, _i, ctypes.POINTER(CabTape),
+                                    ctypes.POINTER(CabWeights), _vp, _i]
     L.zjai_layer_norm.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]
     L.zjai_channel_attention.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i]
     L.zjai_depthwise3x3.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i]

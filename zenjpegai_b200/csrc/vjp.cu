@@ -12,6 +12,9 @@
 //   [c][oc][k][k] is a conv weight with c outputs).
 // * ResidualBlock (attention.rs:58-75): conv2's VJP, masked by relu' of the block's tape
 //   (conv1's output), conv1's VJP, plus the skip's d_out.
+// * CAB (attention.rs:182-223): d_out split into the trunk's (times sigma) and the mask's
+//   (times trunk and sigma'), the trunk's two residual blocks, the mask chain back to full
+//   resolution (upscale, two residual blocks, subscale), and the skip.
 //
 // The tensor cores take f16 operands: d_out is scaled by a power of two that brings its largest
 // magnitude into [2^13, 2^14) before the f16 conversion (RDLR gradients are small: unscaled
@@ -141,6 +144,66 @@ int conv_vjp_s1(Ctx* ctx, const float* dd, int oc, int oh, int ow, const float* 
   return run_into(ctx, L, s, t, din, h, w, pt, pl);
 }
 
+// the input gradient of a stride-2 3x3-style conv (weight [oc][c][k][k], host, padding pad)
+// from dd [oc][oh][ow] into din [c][h][w]: the stride-2 transposed conv over the same weights
+// with output padding 1, cut to the input extent
+int conv_vjp_s2(Ctx* ctx, const float* dd, int oc, int oh, int ow, const float* hw, int c, int k,
+                int pad, int h, int w, float* din) {
+  ConvLayer L;
+  ZJAI_TRY(pack_convT(ctx, &L, hw, nullptr, oc, c, k, pad, 1, 1));
+  LayerGuard guard(&L);
+  TView t;
+  float s;
+  ZJAI_TRY(stage_grad(ctx, dd, oc, oh, ow, 14, &t, &s));
+  return run_into(ctx, L, s, t, din, h, w, 0, 0);
+}
+
+// the input gradient of a stride-2 transposed conv (weight [c][oc][k][k], host) from dd
+// [oc][oh][ow] into din [c][h][w]: the stride-2 conv over the same weights
+int convT_vjp(Ctx* ctx, const float* dd, int oc, int oh, int ow, const float* hw, int c, int k,
+              int pad, int h, int w, float* din) {
+  ConvLayer L;
+  ZJAI_TRY(pack_conv(ctx, &L, hw, nullptr, oc, c, k, k, 2, pad, pad, 1, nullptr, 1));
+  LayerGuard guard(&L);
+  TView t;
+  float s;
+  ZJAI_TRY(stage_grad(ctx, dd, oc, oh, ow, 14, &t, &s));
+  return run_into(ctx, L, s, t, din, h, w, 0, 0);
+}
+
+// ResidualBlock::backward (attention.rs:58-75) on device planar arrays: din = dd +
+// conv1^T(relu'(tape) . conv2^T dd); host weights [c][c][3][3]
+int rb_vjp(Ctx* ctx, const float* dd, const float* tape, const float* h1, const float* h2, int c,
+           int h, int w, float* din) {
+  const size_t n = (size_t)c * h * w;
+  const size_t mark = ctx->arena.mark();
+  float* d = static_cast<float*>(ctx->arena.alloc(n * sizeof(float)));
+  if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (residual block VJP)");
+  const int blocks = launch_elementwise_blocks(ctx, n);
+  ZJAI_TRY(conv_vjp_s1(ctx, dd, c, h, w, h2, c, 3, 3, 1, 1, 1, h, w, 0, 0, d));
+  relu_mask_kernel<<<blocks, 256, 0, ctx->stream>>>(d, tape, n);
+  ZJAI_TRY(conv_vjp_s1(ctx, d, c, h, w, h1, c, 3, 3, 1, 1, 1, h, w, 0, 0, din));
+  add_kernel<<<blocks, 256, 0, ctx->stream>>>(din, dd, n);
+  ctx->launches += 2;
+  ZJAI_TRY(cuda_check(cudaGetLastError(), "residual block VJP"));
+  // every use of d is queued on the stream, which orders its next user after them
+  ctx->arena.release(mark);
+  return ZJAI_OK;
+}
+
+// Cab::backward's split of d_out (attention.rs:185-203, 209-211): d_trunk = o . sig and
+// d_sig = (o . trunk) . (sig . (1 - sig)), each product rounded on its own
+__global__ void cab_split_kernel(const float* __restrict__ o, const float* __restrict__ sig,
+                                 const float* __restrict__ trunk, size_t n,
+                                 float* __restrict__ d_trunk, float* __restrict__ d_sig) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const float s = sig[i];
+    d_trunk[i] = __fmul_rn(o[i], s);
+    d_sig[i] = __fmul_rn(__fmul_rn(o[i], trunk[i]), __fmul_rn(s, __fsub_rn(1.f, s)));
+  }
+}
+
 }  // namespace
 }  // namespace zjai
 
@@ -215,15 +278,7 @@ int zjai_conv2d_backward(zjai_ctx* ctx, const float* dout, int oc, int oh, int o
     ZJAI_TRY(conv_vjp_s1(ctx, dd, oc, oh, ow, hw, c, kh, kw, pad_h, pad_w, groups, h, w, pt, pl,
                          ddin));
   } else {
-    // out_pad 1: the transposed conv covers the input extent (one row / column beyond it where
-    // the forward's output size rounded down, dropped by the crop)
-    ConvLayer L;
-    ZJAI_TRY(pack_convT(ctx, &L, hw, nullptr, oc, c, kh, pad_h, 1, 1));
-    LayerGuard guard(&L);
-    TView t;
-    float s;
-    ZJAI_TRY(stage_grad(ctx, dd, oc, oh, ow, 14, &t, &s));
-    ZJAI_TRY(run_into(ctx, L, s, t, ddin, h, w, 0, 0));
+    ZJAI_TRY(conv_vjp_s2(ctx, dd, oc, oh, ow, hw, c, kh, pad_h, h, w, ddin));
   }
   ZJAI_TRY(stage_out_finish(ctx, din, ddin, nin, mem));
   return ctx_check_status(ctx);
@@ -251,14 +306,8 @@ int zjai_conv_transpose2d_backward(zjai_ctx* ctx, const float* dout, int oc, int
   float* ddin;
   const size_t nin = (size_t)c * h * w;
   ZJAI_TRY(stage_out_alloc(ctx, din, nin, mem, &ddin));
-  ConvLayer L;
   // weight [c][oc][k][k] read as a conv weight with c outputs and oc inputs
-  ZJAI_TRY(pack_conv(ctx, &L, hw, nullptr, oc, c, k, k, 2, pad, pad, 1, nullptr, 1));
-  LayerGuard guard(&L);
-  TView t;
-  float s;
-  ZJAI_TRY(stage_grad(ctx, dd, oc, oh, ow, 14, &t, &s));
-  ZJAI_TRY(run_into(ctx, L, s, t, ddin, h, w, 0, 0));
+  ZJAI_TRY(convT_vjp(ctx, dd, oc, oh, ow, hw, c, k, pad, h, w, ddin));
   ZJAI_TRY(stage_out_finish(ctx, din, ddin, nin, mem));
   return ctx_check_status(ctx);
 }
@@ -282,16 +331,65 @@ int zjai_residual_block_backward(zjai_ctx* ctx, const float* dout, const float* 
   ZJAI_TRY(stage_in(ctx, conv1_out, n, mem, &dp));
   float* ddin;
   ZJAI_TRY(stage_out_alloc(ctx, din, n, mem, &ddin));
-  float* d = static_cast<float*>(ctx->arena.alloc(n * sizeof(float)));
-  if (!d) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (residual block VJP)");
+  ZJAI_TRY(rb_vjp(ctx, dd, dp, h1, h2, c, h, w, ddin));
+  ZJAI_TRY(stage_out_finish(ctx, din, ddin, n, mem));
+  return ctx_check_status(ctx);
+}
+
+int zjai_cab_backward(zjai_ctx* ctx, const float* dout, int c, int h, int w,
+                      const zjai_cab_tape* tape, const zjai_cab_weights* wts, float* din,
+                      int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!dout || !tape || !wts || !din || c <= 0 || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "cab_backward: bad arguments");
+  if (mem != ZJAI_MEM_HOST && mem != ZJAI_MEM_DEVICE)
+    return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  // the mask branch runs at the subscale conv's output extent, which the upscale doubles back
+  const int mh = (h - 1) / 2 + 1, mw = (w - 1) / 2 + 1;
+  if (2 * mh != h || 2 * mw != w)
+    return fail(ZJAI_INVALID_ARGUMENT, "CAB: odd feature map size");
+  const float* tp[6] = {tape->trunk_pre, tape->sig, tape->rb_c1[0], tape->rb_c1[1],
+                        tape->mask_c1[0], tape->mask_c1[1]};
+  const float* wp[10] = {wts->trunk[0][0], wts->trunk[0][1], wts->trunk[1][0], wts->trunk[1][1],
+                         wts->subscale,    wts->mask2[0],    wts->mask2[1],    wts->mask3[0],
+                         wts->mask3[1],    wts->upscale};
+  for (const float* p : tp)
+    if (!p) return fail(ZJAI_INVALID_ARGUMENT, "cab_backward: missing tape array");
+  for (const float* p : wp)
+    if (!p) return fail(ZJAI_INVALID_ARGUMENT, "cab_backward: missing weight");
+  ArenaScope scope(ctx);
+  const size_t n = (size_t)c * h * w, nm = (size_t)c * mh * mw, nw = (size_t)c * c * 9;
+  std::vector<float> wb[10];
+  const float* hw[10];
+  for (int i = 0; i < 10; ++i) ZJAI_TRY(fetch_host(wp[i], nw, mem, &wb[i], &hw[i]));
+  const float *dd, *dt[6];
+  ZJAI_TRY(stage_in(ctx, dout, n, mem, &dd));
+  for (int i = 0; i < 6; ++i) ZJAI_TRY(stage_in(ctx, tp[i], i < 4 ? n : nm, mem, &dt[i]));
+  float* ddin;
+  ZJAI_TRY(stage_out_alloc(ctx, din, n, mem, &ddin));
+  float* d_trunk = static_cast<float*>(ctx->arena.alloc(n * sizeof(float)));
+  float* d_sig = static_cast<float*>(ctx->arena.alloc(n * sizeof(float)));
+  float* t1 = static_cast<float*>(ctx->arena.alloc(n * sizeof(float)));
+  float* m1 = static_cast<float*>(ctx->arena.alloc(nm * sizeof(float)));
+  float* m2 = static_cast<float*>(ctx->arena.alloc(nm * sizeof(float)));
+  if (!d_trunk || !d_sig || !t1 || !m1 || !m2)
+    return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (CAB VJP)");
   const int blocks = launch_elementwise_blocks(ctx, n);
-  // conv2^T d_out, masked by relu'(conv1_out); conv1^T of that, plus the skip's d_out
-  ZJAI_TRY(conv_vjp_s1(ctx, dd, c, h, w, h2, c, 3, 3, 1, 1, 1, h, w, 0, 0, d));
-  relu_mask_kernel<<<blocks, 256, 0, ctx->stream>>>(d, dp, n);
-  ZJAI_TRY(conv_vjp_s1(ctx, d, c, h, w, h1, c, 3, 3, 1, 1, 1, h, w, 0, 0, ddin));
+  cab_split_kernel<<<blocks, 256, 0, ctx->stream>>>(dd, dt[1], dt[0], n, d_trunk, d_sig);
+  ctx->launches++;
+  // trunk branch: residual blocks 1 then 0
+  ZJAI_TRY(rb_vjp(ctx, d_trunk, dt[3], hw[2], hw[3], c, h, w, t1));
+  ZJAI_TRY(rb_vjp(ctx, t1, dt[2], hw[0], hw[1], c, h, w, ddin));
+  // mask branch: upscale (transposed conv 3x3, padding 1), mask3, mask2, subscale (3x3 stride 2)
+  ZJAI_TRY(convT_vjp(ctx, d_sig, c, h, w, hw[9], c, 3, 1, mh, mw, m1));
+  ZJAI_TRY(rb_vjp(ctx, m1, dt[5], hw[7], hw[8], c, mh, mw, m2));
+  ZJAI_TRY(rb_vjp(ctx, m2, dt[4], hw[5], hw[6], c, mh, mw, m1));
+  ZJAI_TRY(conv_vjp_s2(ctx, m1, c, mh, mw, hw[4], c, 3, 1, h, w, t1));
+  // d_x = trunk branch + mask branch + d_out (the skip), in that order
+  add_kernel<<<blocks, 256, 0, ctx->stream>>>(ddin, t1, n);
   add_kernel<<<blocks, 256, 0, ctx->stream>>>(ddin, dd, n);
   ctx->launches += 2;
-  ZJAI_TRY(cuda_check(cudaGetLastError(), "residual block VJP"));
+  ZJAI_TRY(cuda_check(cudaGetLastError(), "CAB VJP"));
   ZJAI_TRY(stage_out_finish(ctx, din, ddin, n, mem));
   return ctx_check_status(ctx);
 }
