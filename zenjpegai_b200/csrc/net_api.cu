@@ -144,15 +144,16 @@ static int run_group(Ctx* ctx, Net* ny, Net* nuv, const float* lat_y, const floa
 
 // The pool of group streams / events, created on first use.
 static int group_pool(Ctx* ctx, size_t streams, size_t events) {
-  // Stream 0 carries the luma chain of the largest shape group (groups run largest first), the
-  // step's critical path: at the greatest priority its blocks are scheduled ahead of the other
-  // chains', which fill the SMs it leaves (4K HOP step 8.30 -> 8.22 ms; raising every luma
-  // chain instead was not steadily better). Graph replays keep it (node priorities).
+  // Streams 0 and 1 carry the luma and chroma chains of the largest shape group (groups run
+  // largest first), the step's critical path: at the greatest priority their blocks are
+  // scheduled ahead of the other chains', which fill the SMs they leave (4K HOP step 8.30 ->
+  // 8.12 ms; raising every luma chain instead was not steadily better). Graph replays keep the
+  // priorities (node priorities).
   while (ctx->group_streams.size() < streams) {
     int least = 0, greatest = 0;
     ZJAI_TRY(cuda_check(cudaDeviceGetStreamPriorityRange(&least, &greatest), "priority range"));
     cudaStream_t s;
-    const int prio = ctx->group_streams.empty() ? greatest : least;
+    const int prio = ctx->group_streams.size() < 2 ? greatest : least;
     ZJAI_TRY(cuda_check(cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, prio), "stream"));
     ctx->group_streams.push_back(s);
   }
