@@ -523,6 +523,16 @@ int zjai_cab_backward(zjai_ctx *ctx, const float *dout, int c, int h, int w,
                       const zjai_cab_tape *tape, const zjai_cab_weights *wts, float *din,
                       int mem);
 
+/* The transformer block's per-pixel VJPs. `elu_gate_backward` (src/nn/fast/math.rs:838-858)
+ * of y = elu(a) . b over n elements: d_a = elu'(a) . b . d, d_b = elu(a) . d (the GPU's expf in
+ * place of the crate's exp: within a few ulp). `layer_norm_channels_backward` (math.rs:860-913):
+ * d, x [c][h][w] (x the forward's input), weight [c] -> dx, the statistics recomputed with f64
+ * sums as the crate does. */
+int zjai_elu_gate_backward(zjai_ctx *ctx, const float *d, const float *a, const float *b,
+                           int64_t n, float *d_a, float *d_b, int mem);
+int zjai_layer_norm_backward(zjai_ctx *ctx, const float *d, const float *x, int c, int h, int w,
+                             const float *weight, float *dx, int mem);
+
 /* `math::layer_norm_channels` (math.rs:423-448), out of place. */
 int zjai_layer_norm(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,
                     const float *bias, float *out, int mem);

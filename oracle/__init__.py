@@ -115,6 +115,8 @@ def _declare(L):
     L.zo_conv_transpose2d_backward.argtypes = [_f, _i, _i, _i, _f, _i, _i, _i, _i, _i, _i, _f]
     L.zo_residual_block_backward.argtypes = [_f, _f, _i, _i, _i, _f, _f, _f]
     L.zo_cab_backward.argtypes = [_f, _i, _i, _i, _f * 4, _f * 2, _f * 10, _f]
+    L.zo_elu_gate_backward.argtypes = [_f, _f, _f, _i64, _f, _f]
+    L.zo_layer_norm_backward.argtypes = [_f, _f, _i, _i, _i, _f, _f]
     L.zo_efe_split_edge.argtypes = [ctypes.c_double, _i]
     L.zo_efe_linear.argtypes = [_f, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i, _i,
                                 ctypes.POINTER(EfeLinearSet), _f, _f]
@@ -241,6 +243,24 @@ def cab_backward(dout, tape, weights):
                              (_f * 2)(*[_fp(a) for a in ms]), (_f * 10)(*[_fp(a) for a in ws]),
                              _fp(out)):
         raise ValueError("oracle cab_backward: bad geometry")
+    return out
+
+
+def elu_gate_backward(d, a, b):
+    """`elu_gate_backward` (math.rs:838-858): (d_a, d_b) of y = elu(a) . b."""
+    d, a, b = _c32(d), _c32(a), _c32(b)
+    da, db = np.empty_like(d), np.empty_like(d)
+    lib().zo_elu_gate_backward(_fp(d), _fp(a), _fp(b), d.size, _fp(da), _fp(db))
+    return da, db
+
+
+def layer_norm_backward(d, x, weight):
+    """`layer_norm_channels_backward` (math.rs:860-913): d, x [c, h, w], weight [c] -> d_x."""
+    d, x = _c32(d), _c32(x)
+    c, h, w = x.shape
+    out = np.empty_like(x)
+    if lib().zo_layer_norm_backward(_fp(d), _fp(x), c, h, w, _fp(_c32(weight)), _fp(out)):
+        raise ValueError("oracle layer_norm_backward: bad shape")
     return out
 
 

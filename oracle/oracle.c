@@ -2196,3 +2196,53 @@ int zo_cab_backward(const float *dout, int c, int h, int w, const float *const t
     free(dtr); free(dsg); free(t1); free(m1); free(m2);
     return r;
 }
+
+/* `elu_gate_backward` (math.rs:838-858) of y = elu(a) . b: d_a = elu'(a) . b . d (elu' = 1 above
+ * 0, exp(a) else) and d_b = elu(a) . d, with the crate's exp. */
+void zo_elu_gate_backward(const float *d, const float *a, const float *b, int64_t n, float *d_a,
+                          float *d_b) {
+    for (int64_t i = 0; i < n; i++) {
+        const float av = a[i];
+        const float e = av > 0.0f ? 0.0f : zo_exp(av);
+        const float elu = av > 0.0f ? av : e - 1.0f;
+        const float delu = av > 0.0f ? 1.0f : e;
+        d_a[i] = delu * b[i] * d[i];
+        d_b[i] = elu * d[i];
+    }
+}
+
+/* `layer_norm_channels_backward` (math.rs:860-913): per position, mean and variance over the
+ * channels in f64 (channel order), the f32 deviation and normalised x as the forward makes them,
+ * then d_x[c] = (dy[c] - s1 / c - xn[c] . s2 / c) / sigma with dy = d . w and the f64 sums
+ * s1 = sum dy, s2 = sum dy . xn. */
+int zo_layer_norm_backward(const float *d, const float *x, int c, int h, int w,
+                           const float *weight, float *dx) {
+    if (c <= 0 || h <= 0 || w <= 0) return -1;
+    const int64_t n = (int64_t)h * w;
+#pragma omp parallel for schedule(static) num_threads(g_threads)
+    for (int64_t i = 0; i < n; i++) {
+        double mean = 0.0, var = 0.0;
+        for (int ch = 0; ch < c; ch++) mean += (double)x[ch * n + i];
+        mean /= c;
+        for (int ch = 0; ch < c; ch++) {
+            const double dv = (double)x[ch * n + i] - mean;
+            var += dv * dv;
+        }
+        const float sig = sqrtf((float)(var / c) + 1e-5f);
+        const float m = (float)mean;
+        double s1 = 0.0, s2 = 0.0;
+        for (int ch = 0; ch < c; ch++) {
+            const float xn = (x[ch * n + i] - m) / sig;
+            const float dy = d[ch * n + i] * weight[ch];
+            s1 += (double)dy;
+            s2 += (double)dy * (double)xn;
+        }
+        const float m1 = (float)s1 / (float)c, m2 = (float)s2 / (float)c;
+        for (int ch = 0; ch < c; ch++) {
+            const float xn = (x[ch * n + i] - m) / sig;
+            const float dy = d[ch * n + i] * weight[ch];
+            dx[ch * n + i] = (dy - m1 - xn * m2) / sig;
+        }
+    }
+    return 0;
+}

@@ -278,6 +278,11 @@ int zo_residual_block_backward(const float *dout, const float *conv1_out, int c,
  * conv1, conv2, upscale (each [c][c][3][3]). */
 int zo_cab_backward(const float *dout, int c, int h, int w, const float *const t[4],
                     const float *const mask_c1[2], const float *const wt[10], float *din);
+/* `elu_gate_backward` (math.rs:838-858) and `layer_norm_channels_backward` (math.rs:860-913). */
+void zo_elu_gate_backward(const float *d, const float *a, const float *b, int64_t n, float *d_a,
+                          float *d_b);
+int zo_layer_norm_backward(const float *d, const float *x, int c, int h, int w,
+                           const float *weight, float *dx);
 
 #ifdef __cplusplus
 }

@@ -126,3 +126,28 @@ def test_cab_backward(eng, c, h, w, mag):
     want = zo.cab_backward(d, tape, wts)
     got = eng.cab_backward(d, tape, wts)
     assert rel_l2(got, want) < 3e-3
+
+
+def test_elu_gate_and_layer_norm_backward(eng):
+    import torch
+    rng = np.random.default_rng(9)
+    a = (rng.standard_normal((64, 33, 29)) * 3).astype(np.float32)
+    b = rng.standard_normal(a.shape).astype(np.float32)
+    d = rng.standard_normal(a.shape).astype(np.float32)
+    wa, wb = zo.elu_gate_backward(d, a, b)
+    ga, gb = eng.elu_gate_backward(d, a, b)
+    # the GPU's expf against the crate's exp: a few ulp
+    assert np.allclose(ga, wa, rtol=1e-5, atol=1e-6) and np.allclose(gb, wb, rtol=1e-5, atol=1e-6)
+    for c in (64, 128, 160):
+        x = (rng.standard_normal((c, 37, 41)) * 2 + 0.3).astype(np.float32)
+        wt = rng.standard_normal(c).astype(np.float32)
+        dd = rng.standard_normal(x.shape).astype(np.float32)
+        want = zo.layer_norm_backward(dd, x, wt)
+        got = eng.layer_norm_backward(dd, x, wt)
+        # the same f64 sums in channel order and the same f32 operations: equal up to the last
+        # ulp of the division order
+        assert np.allclose(got, want, rtol=1e-5, atol=1e-6)
+        tg = eng.layer_norm_backward(torch.from_numpy(dd).cuda(), torch.from_numpy(x).cuda(),
+                                     torch.from_numpy(wt).cuda())
+        torch.cuda.synchronize()
+        assert np.array_equal(tg.cpu().numpy(), got)

@@ -168,3 +168,41 @@ def test_cab_backward_matches_finite_differences():
     lhs = float((d * (fp - fm)).sum()) / (2 * eps)
     rhs = float((dx.astype(np.float64) * v).sum())
     assert rel(lhs, rhs) < 1e-3, (lhs, rhs)
+
+
+def test_elu_gate_backward_is_the_derivative():
+    # elu_gate_backward (math.rs:838-858) against the analytic derivative of elu(a) . b
+    rng = np.random.default_rng(5)
+    a = (rng.standard_normal(4096) * 3).astype(np.float32)
+    b = rng.standard_normal(4096).astype(np.float32)
+    d = rng.standard_normal(4096).astype(np.float32)
+    da, db = zo.elu_gate_backward(d, a, b)
+    a64, b64, d64 = a.astype(np.float64), b.astype(np.float64), d.astype(np.float64)
+    want_a = np.where(a64 > 0, 1.0, np.exp(a64)) * b64 * d64
+    want_b = np.where(a64 > 0, a64, np.expm1(a64)) * d64
+    assert np.abs(da - want_a).max() < 1e-5 * (1 + np.abs(want_a).max())
+    assert np.abs(db - want_b).max() < 1e-5 * (1 + np.abs(want_b).max())
+
+
+def test_layer_norm_backward_matches_finite_differences():
+    # layer_norm_channels_backward (math.rs:860-913) against finite differences of the channel
+    # layer norm (math.rs:423-448) in float64
+    rng = np.random.default_rng(6)
+    c, h, w = 24, 7, 9
+    x = (rng.standard_normal((c, h, w)) * 2 + 0.5).astype(np.float32)
+    wt = rng.standard_normal(c).astype(np.float32)
+    bs = rng.standard_normal(c).astype(np.float32)
+
+    def ln(xx):
+        m = xx.mean(0, keepdims=True)
+        v = ((xx - m) ** 2).mean(0, keepdims=True)
+        return (xx - m) / np.sqrt(v + 1e-5) * wt[:, None, None] + bs[:, None, None]
+
+    d = rng.standard_normal((c, h, w)).astype(np.float32)
+    dx = zo.layer_norm_backward(d, x, wt)
+    v = rng.standard_normal(x.shape)
+    eps = 1e-4
+    x64 = x.astype(np.float64)
+    lhs = float((d * (ln(x64 + eps * v) - ln(x64 - eps * v))).sum()) / (2 * eps)
+    rhs = float((dx.astype(np.float64) * v).sum())
+    assert rel(lhs, rhs) < 1e-4, (lhs, rhs)

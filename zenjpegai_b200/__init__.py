@@ -214,6 +214,32 @@ class Engine:
                                                       mem))
         return out
 
+    def elu_gate_backward(self, d, a, b):
+        """`elu_gate_backward` (math.rs:838-858): (d_a, d_b) of y = elu(a) . b."""
+        pd, mem = _arg(d)
+        pa, m1 = _arg(a, tuple(d.shape))
+        pb, m2 = _arg(b, tuple(d.shape))
+        oa, ob = _like(d, tuple(d.shape)), _like(d, tuple(d.shape))
+        if len({mem, m1, m2}) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        n = int(np.prod(d.shape))
+        check(_lib.lib().zjai_elu_gate_backward(self.handle, pd, pa, pb, n, _arg(oa)[0],
+                                                _arg(ob)[0], mem))
+        return oa, ob
+
+    def layer_norm_backward(self, d, x, weight, out=None):
+        """`layer_norm_channels_backward` (math.rs:860-913): d, x [c, h, w], weight [c]."""
+        c, h, w = x.shape
+        out = _like(x, (c, h, w)) if out is None else out
+        pd, mem = _arg(d, (c, h, w))
+        px, m1 = _arg(x)
+        pw, m2 = _arg(weight, (c,))
+        po, m3 = _arg(out, (c, h, w))
+        if len({mem, m1, m2, m3}) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        check(_lib.lib().zjai_layer_norm_backward(self.handle, pd, px, c, h, w, pw, po, mem))
+        return out
+
     CAB_WEIGHTS = ("trunk0.conv1", "trunk0.conv2", "trunk1.conv1", "trunk1.conv2", "subscale",
                    "mask2.conv1", "mask2.conv2", "mask3.conv1", "mask3.conv2", "upscale")
 

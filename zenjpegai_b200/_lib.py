@@ -178,6 +178,8 @@ def lib():
     L.zjai_residual_block_backward.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]
     L.zjai_cab_backward.argtypes = [_vp, _vp, _i, _i, _i, ctypes.POINTER(CabTape),
                                     ctypes.POINTER(CabWeights), _vp, _i]
+    L.zjai_elu_gate_backward.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_int64, _vp, _vp, _i]
+    L.zjai_layer_norm_backward.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i]
     L.zjai_layer_norm.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]
     L.zjai_channel_attention.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i]
     L.zjai_depthwise3x3.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i]

@@ -12,6 +12,8 @@
 //   [c][oc][k][k] is a conv weight with c outputs).
 // * ResidualBlock (attention.rs:58-75): conv2's VJP, masked by relu' of the block's tape
 //   (conv1's output), conv1's VJP, plus the skip's d_out.
+// * the transformer block's per-pixel pieces: the ELU gate (math.rs:838-858) and the channel
+//   layer norm (math.rs:860-913), elementwise / per-position kernels.
 // * CAB (attention.rs:182-223): d_out split into the trunk's (times sigma) and the mask's
 //   (times trunk and sigma'), the trunk's two residual blocks, the mask chain back to full
 //   resolution (upscale, two residual blocks, subscale), and the skip.
@@ -204,6 +206,56 @@ __global__ void cab_split_kernel(const float* __restrict__ o, const float* __res
   }
 }
 
+// elu_gate_backward (math.rs:838-858), one element per thread: d_a = (elu'(a) . b) . d,
+// d_b = elu(a) . d
+__global__ void elu_gate_bwd_kernel(const float* __restrict__ d, const float* __restrict__ a,
+                                    const float* __restrict__ b, size_t n,
+                                    float* __restrict__ d_a, float* __restrict__ d_b) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const float av = a[i];
+    const float e = av > 0.f ? 0.f : expf(av);
+    const float elu = av > 0.f ? av : __fsub_rn(e, 1.f);
+    const float delu = av > 0.f ? 1.f : e;
+    d_a[i] = __fmul_rn(__fmul_rn(delu, b[i]), d[i]);
+    d_b[i] = __fmul_rn(elu, d[i]);
+  }
+}
+
+// layer_norm_channels_backward (math.rs:860-913), one position per thread over planar
+// [c][n]: the forward's mean and variance in f64 (channel order), its f32 deviation and
+// normalised x, then d_x[c] = (dy[c] - s1 / c - xn[c] . s2 / c) / sigma with dy = d . w and the
+// f64 sums s1, s2; adjacent threads read adjacent positions of each channel plane
+__global__ void ln_bwd_kernel(const float* __restrict__ d, const float* __restrict__ x, int c,
+                              long long n, const float* __restrict__ wt,
+                              float* __restrict__ dx) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    double mean = 0.0, var = 0.0;
+    for (int ch = 0; ch < c; ++ch) mean += (double)__ldg(x + ch * n + i);
+    mean /= c;
+    for (int ch = 0; ch < c; ++ch) {
+      const double dv = (double)__ldg(x + ch * n + i) - mean;
+      var += dv * dv;
+    }
+    const float sig = __fsqrt_rn(__fadd_rn((float)(var / c), 1e-5f));
+    const float m = (float)mean;
+    double s1 = 0.0, s2 = 0.0;
+    for (int ch = 0; ch < c; ++ch) {
+      const float xn = __fdiv_rn(__fsub_rn(__ldg(x + ch * n + i), m), sig);
+      const float dy = __fmul_rn(__ldg(d + ch * n + i), __ldg(wt + ch));
+      s1 += (double)dy;
+      s2 += (double)dy * (double)xn;
+    }
+    const float m1 = __fdiv_rn((float)s1, (float)c), m2 = __fdiv_rn((float)s2, (float)c);
+    for (int ch = 0; ch < c; ++ch) {
+      const float xn = __fdiv_rn(__fsub_rn(__ldg(x + ch * n + i), m), sig);
+      const float dy = __fmul_rn(__ldg(d + ch * n + i), __ldg(wt + ch));
+      dx[ch * n + i] = __fdiv_rn(__fsub_rn(__fsub_rn(dy, m1), __fmul_rn(xn, m2)), sig);
+    }
+  }
+}
+
 }  // namespace
 }  // namespace zjai
 
@@ -392,6 +444,54 @@ int zjai_cab_backward(zjai_ctx* ctx, const float* dout, int c, int h, int w,
   ZJAI_TRY(cuda_check(cudaGetLastError(), "CAB VJP"));
   ZJAI_TRY(stage_out_finish(ctx, din, ddin, n, mem));
   return ctx_check_status(ctx);
+}
+
+int zjai_elu_gate_backward(zjai_ctx* ctx, const float* d, const float* a, const float* b,
+                           int64_t n, float* d_a, float* d_b, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!d || !a || !b || !d_a || !d_b || n <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "elu_gate_backward: bad arguments");
+  if (mem != ZJAI_MEM_HOST && mem != ZJAI_MEM_DEVICE)
+    return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  ArenaScope scope(ctx);
+  const float *dd, *da, *db;
+  ZJAI_TRY(stage_in(ctx, d, (size_t)n, mem, &dd));
+  ZJAI_TRY(stage_in(ctx, a, (size_t)n, mem, &da));
+  ZJAI_TRY(stage_in(ctx, b, (size_t)n, mem, &db));
+  float *oa, *ob;
+  ZJAI_TRY(stage_out_alloc(ctx, d_a, (size_t)n, mem, &oa));
+  ZJAI_TRY(stage_out_alloc(ctx, d_b, (size_t)n, mem, &ob));
+  elu_gate_bwd_kernel<<<launch_elementwise_blocks(ctx, (size_t)n), 256, 0, ctx->stream>>>(
+      dd, da, db, (size_t)n, oa, ob);
+  ctx->launches++;
+  ZJAI_TRY(cuda_check(cudaGetLastError(), "elu gate VJP"));
+  ZJAI_TRY(stage_out_finish(ctx, d_a, oa, (size_t)n, mem));
+  ZJAI_TRY(stage_out_finish(ctx, d_b, ob, (size_t)n, mem));
+  return finish_call(ctx, mem);
+}
+
+int zjai_layer_norm_backward(zjai_ctx* ctx, const float* d, const float* x, int c, int h, int w,
+                             const float* weight, float* dx, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!d || !x || !weight || !dx || c <= 0 || h <= 0 || w <= 0)
+    return fail(ZJAI_INVALID_ARGUMENT, "layer norm backward: shape");
+  if (mem != ZJAI_MEM_HOST && mem != ZJAI_MEM_DEVICE)
+    return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  ArenaScope scope(ctx);
+  const long long n = (long long)h * w;
+  const size_t nt = (size_t)c * n;
+  const float *dd, *dxin, *dw;
+  ZJAI_TRY(stage_in(ctx, d, nt, mem, &dd));
+  ZJAI_TRY(stage_in(ctx, x, nt, mem, &dxin));
+  ZJAI_TRY(stage_in(ctx, weight, (size_t)c, mem, &dw));
+  float* out;
+  ZJAI_TRY(stage_out_alloc(ctx, dx, nt, mem, &out));
+  ln_bwd_kernel<<<launch_elementwise_blocks(ctx, (size_t)n), 256, 0, ctx->stream>>>(
+      dd, dxin, c, n, dw, out);
+  ctx->launches++;
+  ZJAI_TRY(cuda_check(cudaGetLastError(), "layer norm VJP"));
+  ZJAI_TRY(stage_out_finish(ctx, dx, out, nt, mem));
+  return finish_call(ctx, mem);
 }
 
 }  // extern "C"
