@@ -1,6 +1,7 @@
-// RDLR layer VJPs: the input gradients of the conv layers (src/nn/reference.rs:238-336 through
-// src/nn/fast/layers.rs:72-90, 156-160), which the encoder's latent refinement chains through
-// the synthesis network. Each is itself a convolution, run on the tcgen05 conv kernel:
+// RDLR VJPs: the input gradients of the synthesis network's layers and blocks
+// (src/nn/reference.rs:238-336 through src/nn/fast/layers.rs:72-90, 156-160; math.rs:838-913;
+// attention.rs:58-75, 182-223), which the encoder's latent refinement chains through the
+// network. The conv VJPs are themselves convolutions, run on the tcgen05 conv kernel:
 //
 // * conv2d, stride 1: the full convolution of d_out with the kernel flipped by 180 degrees and
 //   its channel axes swapped (padding kh - 1 - pad), per group; the extra zero border of the
