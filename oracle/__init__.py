@@ -117,6 +117,8 @@ def _declare(L):
     L.zo_cab_backward.argtypes = [_f, _i, _i, _i, _f * 4, _f * 2, _f * 10, _f]
     L.zo_elu_gate_backward.argtypes = [_f, _f, _f, _i64, _f, _f]
     L.zo_layer_norm_backward.argtypes = [_f, _f, _i, _i, _i, _f, _f]
+    L.zo_channel_attention_weights.argtypes = [_f, _i, _i, _i, _i, _f, _f]
+    L.zo_channel_attention_backward.argtypes = [_f, _i, _i, _i, _i, _f, _f, _f, _f]
     L.zo_efe_split_edge.argtypes = [ctypes.c_double, _i]
     L.zo_efe_linear.argtypes = [_f, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i, _i,
                                 ctypes.POINTER(EfeLinearSet), _f, _f]
@@ -261,6 +263,21 @@ def layer_norm_backward(d, x, weight):
     out = np.empty_like(x)
     if lib().zo_layer_norm_backward(_fp(d), _fp(x), c, h, w, _fp(_c32(weight)), _fp(out)):
         raise ValueError("oracle layer_norm_backward: bad shape")
+    return out
+
+
+def channel_attention_backward(qkv, heads, temperature, dout):
+    """`channel_attention_backward` (math.rs:668-836) with the forward's softmax weights as the
+    tape: qkv [3 dim, h, w], dout [dim, h, w] -> dqkv [3 dim, h, w]."""
+    qkv, dout, t = _c32(qkv), _c32(dout), _c32(temperature)
+    c3, h, w = qkv.shape
+    dim = c3 // 3
+    attn = np.empty((dim, dim // heads), np.float32)
+    out = np.empty_like(qkv)
+    if lib().zo_channel_attention_weights(_fp(qkv), c3, h, w, heads, _fp(t), _fp(attn)) or \
+            lib().zo_channel_attention_backward(_fp(qkv), c3, h, w, heads, _fp(t), _fp(attn),
+                                                _fp(dout), _fp(out)):
+        raise ValueError("oracle channel_attention_backward: channel / head counts")
     return out
 
 

@@ -2246,3 +2246,111 @@ int zo_layer_norm_backward(const float *d, const float *x, int c, int h, int w,
     }
     return 0;
 }
+
+/* The softmax weights attn [dim][c] of `channel_attention` (math.rs:506-603), the tape
+ * `channel_attention_backward` reads; computed as zo_channel_attention computes them. */
+int zo_channel_attention_weights(const float *qkv, int c3, int h, int w, int heads,
+                                 const float *temperature, float *attn) {
+    if (heads <= 0 || c3 % (3 * heads)) return -1;
+    const int dim = c3 / 3, c = dim / heads;
+    const int64_t n = (int64_t)h * w;
+    float *qk = (float *)malloc(sizeof(float) * 2 * dim * n);
+    if (!qk) return -1;
+    memcpy(qk, qkv, sizeof(float) * 2 * dim * n);
+    for (int r = 0; r < 2 * dim; r++) {
+        float *row = qk + (int64_t)r * n;
+        const float norm = (float)sqrt(zo_dot8(row, row, n));
+        const float d = norm > 1e-12f ? norm : 1e-12f;
+        for (int64_t i = 0; i < n; i++) row[i] /= d;
+    }
+    const float *q = qk, *k = qk + (int64_t)dim * n;
+    for (int ri = 0; ri < dim; ri++) {
+        const int head = ri / c;
+        float *row = attn + (int64_t)ri * c;
+        float mx = -INFINITY;
+        for (int j = 0; j < c; j++) {
+            row[j] = (float)zo_dot8(q + (int64_t)ri * n, k + (int64_t)(head * c + j) * n, n) *
+                     temperature[head];
+            mx = row[j] > mx ? row[j] : mx;
+        }
+        for (int j = 0; j < c; j++) row[j] = zo_exp(row[j] - mx);
+        double sum = 0.0;
+        for (int j = 0; j < c; j++) sum += (double)row[j];
+        const float s32 = (float)sum;
+        for (int j = 0; j < c; j++) row[j] /= s32;
+    }
+    free(qk);
+    return 0;
+}
+
+/* `channel_attention_backward` (math.rs:668-836, the exact path): d_out [dim][h][w] ->
+ * dqkv [3 dim][h][w]. q, k re-normalised with their clamped L2 norms kept; d_attn = d_out . v^T
+ * (dot8) and the row softmax VJP with an f64 row sum; dq = T . da . k, dk = T . da^T . q in f64
+ * accumulators followed by the L2-norm backward ((s - <x, s> x) / |x|); dv = attn^T . d_out in
+ * f64. */
+int zo_channel_attention_backward(const float *qkv, int c3, int h, int w, int heads,
+                                  const float *temperature, const float *attn,
+                                  const float *dout, float *dqkv) {
+    if (heads <= 0 || c3 % (3 * heads)) return -1;
+    const int dim = c3 / 3, c = dim / heads;
+    const int64_t n = (int64_t)h * w;
+    float *qk = (float *)malloc(sizeof(float) * 2 * dim * n);
+    float *norms = (float *)malloc(sizeof(float) * 2 * dim);
+    float *da = (float *)malloc(sizeof(float) * dim * c);
+    if (!qk || !norms || !da) {
+        free(qk); free(norms); free(da);
+        return -1;
+    }
+    memcpy(qk, qkv, sizeof(float) * 2 * dim * n);
+    for (int r = 0; r < 2 * dim; r++) {
+        float *row = qk + (int64_t)r * n;
+        const float nv = (float)sqrt(zo_dot8(row, row, n));
+        norms[r] = nv > 1e-12f ? nv : 1e-12f;
+        for (int64_t i = 0; i < n; i++) row[i] /= norms[r];
+    }
+    const float *q = qk, *k = qk + (int64_t)dim * n, *v = qkv + (int64_t)2 * dim * n;
+    for (int ri = 0; ri < dim; ri++) {
+        const int head = ri / c;
+        const float *a_row = attn + (int64_t)ri * c;
+        float *row = da + (int64_t)ri * c;
+        double sdot = 0.0;
+        for (int j = 0; j < c; j++) {
+            row[j] = (float)zo_dot8(dout + (int64_t)ri * n, v + (int64_t)(head * c + j) * n, n);
+            sdot += (double)a_row[j] * (double)row[j];
+        }
+        for (int j = 0; j < c; j++) row[j] = a_row[j] * (row[j] - (float)sdot);
+    }
+#pragma omp parallel for schedule(dynamic) num_threads(g_threads)
+    for (int ri = 0; ri < 3 * dim; ri++) {
+        double *acc = (double *)calloc(n, sizeof(double));
+        float *o = dqkv + (int64_t)ri * n;
+        if (ri < 2 * dim) {
+            const int is_k = ri >= dim;
+            const int head = (ri - (is_k ? dim : 0)) / c, j = (ri - (is_k ? dim : 0)) % c;
+            const float *x = is_k ? k + (int64_t)(head * c + j) * n : q + (int64_t)ri * n;
+            for (int i = 0; i < c; i++) {
+                /* dq: row ri of da against k_i; dk: column j of da against q_i */
+                const float wv = is_k ? temperature[head] * da[(int64_t)(head * c + i) * c + j]
+                                      : temperature[head] * da[(int64_t)ri * c + i];
+                const float *src = is_k ? q + (int64_t)(head * c + i) * n
+                                        : k + (int64_t)(head * c + i) * n;
+                for (int64_t l = 0; l < n; l++) acc[l] += (double)wv * (double)src[l];
+            }
+            double proj = 0.0;
+            for (int64_t l = 0; l < n; l++) proj += (double)x[l] * acc[l];
+            const double inv = 1.0 / (double)norms[ri];
+            for (int64_t l = 0; l < n; l++) o[l] = (float)((acc[l] - proj * (double)x[l]) * inv);
+        } else {
+            const int head = (ri - 2 * dim) / c, j = (ri - 2 * dim) % c;
+            for (int i = 0; i < c; i++) {
+                const double a = (double)attn[(int64_t)(head * c + i) * c + j];
+                const float *d = dout + (int64_t)(head * c + i) * n;
+                for (int64_t l = 0; l < n; l++) acc[l] += a * (double)d[l];
+            }
+            for (int64_t l = 0; l < n; l++) o[l] = (float)acc[l];
+        }
+        free(acc);
+    }
+    free(qk); free(norms); free(da);
+    return 0;
+}

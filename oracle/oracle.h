@@ -283,6 +283,13 @@ void zo_elu_gate_backward(const float *d, const float *a, const float *b, int64_
                           float *d_b);
 int zo_layer_norm_backward(const float *d, const float *x, int c, int h, int w,
                            const float *weight, float *dx);
+/* The softmax weights attn [dim][c] of `channel_attention` (the backward's tape) and
+ * `channel_attention_backward` (math.rs:668-836): d_out [dim][h][w] -> dqkv [3 dim][h][w]. */
+int zo_channel_attention_weights(const float *qkv, int c3, int h, int w, int heads,
+                                 const float *temperature, float *attn);
+int zo_channel_attention_backward(const float *qkv, int c3, int h, int w, int heads,
+                                  const float *temperature, const float *attn,
+                                  const float *dout, float *dqkv);
 
 #ifdef __cplusplus
 }

@@ -206,3 +206,42 @@ def test_layer_norm_backward_matches_finite_differences():
     lhs = float((d * (ln(x64 + eps * v) - ln(x64 - eps * v))).sum()) / (2 * eps)
     rhs = float((dx.astype(np.float64) * v).sum())
     assert rel(lhs, rhs) < 1e-4, (lhs, rhs)
+
+
+def attention_f64(qkv, heads, temp):
+    """`channel_attention` (math.rs:506-603) in float64: q, k rows L2-normalised over the
+    pixels (norm clamped at 1e-12), per head softmax(T . q k^T) applied to v."""
+    c3, h, w = qkv.shape
+    dim, n = c3 // 3, h * w
+    c = dim // heads
+    x = qkv.reshape(c3, n).astype(np.float64)
+    q, k, v = x[:dim], x[dim:2 * dim], x[2 * dim:]
+    q = q / np.maximum(np.linalg.norm(q, axis=1, keepdims=True), 1e-12)
+    k = k / np.maximum(np.linalg.norm(k, axis=1, keepdims=True), 1e-12)
+    out = np.empty((dim, n))
+    for hd in range(heads):
+        s = slice(hd * c, (hd + 1) * c)
+        a = temp[hd] * (q[s] @ k[s].T)
+        a = np.exp(a - a.max(1, keepdims=True))
+        a /= a.sum(1, keepdims=True)
+        out[s] = a @ v[s]
+    return out.reshape(dim, h, w)
+
+
+@pytest.mark.parametrize("dim,heads,h,w", [(32, 4, 6, 7), (64, 2, 5, 9)])
+def test_channel_attention_backward_matches_finite_differences(dim, heads, h, w):
+    # channel_attention_backward (math.rs:668-836) against finite differences of the attention
+    rng = np.random.default_rng(dim + heads)
+    qkv = rng.standard_normal((3 * dim, h, w)).astype(np.float32)
+    temp = (rng.uniform(0.5, 2.0, heads)).astype(np.float32)
+    d = rng.standard_normal((dim, h, w)).astype(np.float32)
+    dq = zo.channel_attention_backward(qkv, heads, temp, d)
+    v = rng.standard_normal(qkv.shape)
+    eps = 1e-4
+    q64 = qkv.astype(np.float64)
+    lhs = float((d * (attention_f64(q64 + eps * v, heads, temp) -
+                      attention_f64(q64 - eps * v, heads, temp))).sum()) / (2 * eps)
+    rhs = float((dq.astype(np.float64) * v).sum())
+    assert rel(lhs, rhs) < 1e-4, (lhs, rhs)
+    # and the oracle's attention forward is the float64 one
+    assert np.abs(zo.channel_attention(qkv, heads, temp) - attention_f64(q64, heads, temp)).max() < 1e-5
