@@ -532,6 +532,14 @@ int zjai_elu_gate_backward(zjai_ctx *ctx, const float *d, const float *a, const 
                            int64_t n, float *d_a, float *d_b, int mem);
 int zjai_layer_norm_backward(zjai_ctx *ctx, const float *d, const float *x, int c, int h, int w,
                              const float *weight, float *dx, int mem);
+/* `channel_attention_backward` (src/nn/fast/math.rs:668-836): qkv [3 dim][h][w] (the forward's
+ * input), temperature [heads], attn [dim][dim / heads] (the forward's softmax weights, its
+ * tape), d_out [dim][h][w] -> dqkv [3 dim][h][w]: the softmax VJP of d_out . v^T, dq, dk through
+ * the L2-norm backward, dv = attn^T . d_out; f64 sums, within about 1e-5 relative L2 of the
+ * crate's dot8 sums. */
+int zjai_channel_attention_backward(zjai_ctx *ctx, const float *qkv, int c3, int h, int w,
+                                    int heads, const float *temperature, const float *attn,
+                                    const float *dout, float *dqkv, int mem);
 
 /* `math::layer_norm_channels` (math.rs:423-448), out of place. */
 int zjai_layer_norm(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,

@@ -266,6 +266,16 @@ def layer_norm_backward(d, x, weight):
     return out
 
 
+def channel_attention_weights(qkv, heads, temperature):
+    """The forward's softmax weights [dim, dim / heads] (the attention VJP's tape)."""
+    qkv, t = _c32(qkv), _c32(temperature)
+    c3, h, w = qkv.shape
+    attn = np.empty((c3 // 3, c3 // 3 // heads), np.float32)
+    if lib().zo_channel_attention_weights(_fp(qkv), c3, h, w, heads, _fp(t), _fp(attn)):
+        raise ValueError("oracle channel_attention_weights: channel / head counts")
+    return attn
+
+
 def channel_attention_backward(qkv, heads, temperature, dout):
     """`channel_attention_backward` (math.rs:668-836) with the forward's softmax weights as the
     tape: qkv [3 dim, h, w], dout [dim, h, w] -> dqkv [3 dim, h, w]."""

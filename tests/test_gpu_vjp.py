@@ -151,3 +151,17 @@ def test_elu_gate_and_layer_norm_backward(eng):
                                      torch.from_numpy(wt).cuda())
         torch.cuda.synchronize()
         assert np.array_equal(tg.cpu().numpy(), got)
+
+
+@pytest.mark.parametrize("dim,heads,h,w", [(128, 4, 37, 41), (64, 4, 64, 64), (256, 4, 20, 23)])
+def test_channel_attention_backward(eng, dim, heads, h, w):
+    rng = np.random.default_rng(dim + h)
+    qkv = rng.standard_normal((3 * dim, h, w)).astype(np.float32)
+    temp = rng.uniform(0.5, 2.0, heads).astype(np.float32)
+    d = rng.standard_normal((dim, h, w)).astype(np.float32)
+    attn = zo.channel_attention_weights(qkv, heads, temp)
+    want = zo.channel_attention_backward(qkv, heads, temp, d)
+    got = eng.channel_attention_backward(qkv, heads, temp, attn, d)
+    # f64 sums on both sides in different orders: 1e-4 relative L2 per third (dq, dk, dv)
+    for s in (slice(0, dim), slice(dim, 2 * dim), slice(2 * dim, 3 * dim)):
+        assert rel_l2(got[s], want[s]) < 1e-4

@@ -240,6 +240,22 @@ class Engine:
         check(_lib.lib().zjai_layer_norm_backward(self.handle, pd, px, c, h, w, pw, po, mem))
         return out
 
+    def channel_attention_backward(self, qkv, heads, temperature, attn, dout, out=None):
+        """`channel_attention_backward` (math.rs:668-836): qkv [3 dim, h, w], the forward's
+        softmax weights attn [dim, dim / heads], dout [dim, h, w] -> dqkv [3 dim, h, w]."""
+        c3, h, w = qkv.shape
+        out = _like(qkv, (c3, h, w)) if out is None else out
+        pq, mem = _arg(qkv)
+        pt, m1 = _arg(temperature, (heads,))
+        pa, m2 = _arg(attn, (c3 // 3, c3 // 3 // heads))
+        pd, m3 = _arg(dout, (c3 // 3, h, w))
+        po, m4 = _arg(out, (c3, h, w))
+        if len({mem, m1, m2, m3, m4}) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        check(_lib.lib().zjai_channel_attention_backward(self.handle, pq, c3, h, w, heads, pt, pa,
+                                                         pd, po, mem))
+        return out
+
     CAB_WEIGHTS = ("trunk0.conv1", "trunk0.conv2", "trunk1.conv1", "trunk1.conv2", "subscale",
                    "mask2.conv1", "mask2.conv2", "mask3.conv1", "mask3.conv2", "upscale")
 

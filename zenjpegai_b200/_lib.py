@@ -180,6 +180,8 @@ def lib():
                                     ctypes.POINTER(CabWeights), _vp, _i]
     L.zjai_elu_gate_backward.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_int64, _vp, _vp, _i]
     L.zjai_layer_norm_backward.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i]
+    L.zjai_channel_attention_backward.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp,
+                                                  _i]
     L.zjai_layer_norm.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]
     L.zjai_channel_attention.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i]
     L.zjai_depthwise3x3.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i]

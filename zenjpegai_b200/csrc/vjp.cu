@@ -13,8 +13,9 @@
 //   [c][oc][k][k] is a conv weight with c outputs).
 // * ResidualBlock (attention.rs:58-75): conv2's VJP, masked by relu' of the block's tape
 //   (conv1's output), conv1's VJP, plus the skip's d_out.
-// * the transformer block's per-pixel pieces: the ELU gate (math.rs:838-858) and the channel
-//   layer norm (math.rs:860-913), elementwise / per-position kernels.
+// * the transformer block's other pieces: the ELU gate (math.rs:838-858), the channel layer
+//   norm (math.rs:860-913) and the channel attention (math.rs:668-836), as elementwise,
+//   per-position and row-reduction kernels.
 // * CAB (attention.rs:182-223): d_out split into the trunk's (times sigma) and the mask's
 //   (times trunk and sigma'), the trunk's two residual blocks, the mask chain back to full
 //   resolution (upscale, two residual blocks, subscale), and the skip.
@@ -257,6 +258,102 @@ __global__ void ln_bwd_kernel(const float* __restrict__ d, const float* __restri
   }
 }
 
+// ---- channel_attention_backward (math.rs:668-836) ----------------------------------------
+// One block per pair: the dot product over the pixels of rows a[ra] and b[rb] (f64 partial
+// sums, a shared-memory tree): out[o] = sum_l a[ra][l] b[rb][l], rows n floats apart.
+__global__ void __launch_bounds__(256) row_dot_kernel(const float* __restrict__ a,
+                                                      const float* __restrict__ b,
+                                                      const int* __restrict__ pairs, long long n,
+                                                      double* __restrict__ out) {
+  __shared__ double part[256];
+  const int ra = pairs[2 * blockIdx.x], rb = pairs[2 * blockIdx.x + 1];
+  const float* x = a + (long long)ra * n;
+  const float* y = b + (long long)rb * n;
+  double s = 0.0;
+  for (long long l = threadIdx.x; l < n; l += blockDim.x) s += (double)x[l] * (double)y[l];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if ((int)threadIdx.x < o) part[threadIdx.x] += part[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[blockIdx.x] = part[0];
+}
+
+// q and k rows divided by their clamped L2 norms (norm2: the rows' squared norms)
+__global__ void normalise_rows_kernel(const float* __restrict__ qkv, const double* __restrict__ norm2,
+                                      int rows, long long n, float* __restrict__ qk,
+                                      float* __restrict__ norms) {
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < rows * n;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(e / n);
+    const float nv = fmaxf((float)sqrt(norm2[r]), 1e-12f);
+    qk[e] = __fdiv_rn(qkv[e], nv);
+    if (e % n == 0) norms[r] = nv;
+  }
+}
+
+// the row softmax VJP in place on da [dim][c] (= d_out . v^T): da = a . (da - sum_j a_j da_j),
+// the row sum in f64
+__global__ void softmax_vjp_kernel(const double* __restrict__ dots, const float* __restrict__ attn,
+                                   int dim, int c, float* __restrict__ da) {
+  const int ri = blockIdx.x * blockDim.x + threadIdx.x;
+  if (ri >= dim) return;
+  double sdot = 0.0;
+  for (int j = 0; j < c; ++j) {
+    const float v = (float)dots[(long long)ri * c + j];
+    da[(long long)ri * c + j] = v;
+    sdot += (double)attn[(long long)ri * c + j] * (double)v;
+  }
+  for (int j = 0; j < c; ++j) {
+    const long long e = (long long)ri * c + j;
+    da[e] = __fmul_rn(attn[e], __fsub_rn(da[e], (float)sdot));
+  }
+}
+
+// acc rows of dq (T . da . k), dk (T . da^T . q) and dv (attn^T . d_out, final), one pixel of one
+// row per thread, the c terms in order
+__global__ void attn_grad_acc_kernel(const float* __restrict__ qk, const float* __restrict__ dout,
+                                     const float* __restrict__ da, const float* __restrict__ attn,
+                                     const float* __restrict__ temp, int dim, int c, long long n,
+                                     float* __restrict__ out) {
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < 3LL * dim * n;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int ri = (int)(e / n);
+    const long long l = e - (long long)ri * n;
+    double acc = 0.0;
+    if (ri < dim) {
+      const int head = ri / c;
+      const float* k = qk + (long long)dim * n;
+      for (int i = 0; i < c; ++i)
+        acc += (double)__fmul_rn(temp[head], da[(long long)ri * c + i]) *
+               (double)k[(long long)(head * c + i) * n + l];
+    } else if (ri < 2 * dim) {
+      const int head = (ri - dim) / c, j = (ri - dim) % c;
+      for (int i = 0; i < c; ++i)
+        acc += (double)__fmul_rn(temp[head], da[(long long)(head * c + i) * c + j]) *
+               (double)qk[(long long)(head * c + i) * n + l];
+    } else {
+      const int head = (ri - 2 * dim) / c, j = (ri - 2 * dim) % c;
+      for (int i = 0; i < c; ++i)
+        acc += (double)attn[(long long)(head * c + i) * c + j] *
+               (double)dout[(long long)(head * c + i) * n + l];
+    }
+    out[e] = (float)acc;
+  }
+}
+
+// the L2-norm backward of the q / k rows: out = (acc - <x, acc> x) / |x|
+__global__ void l2_backward_kernel(const float* __restrict__ qk, const double* __restrict__ proj,
+                                   const float* __restrict__ norms, int rows, long long n,
+                                   float* __restrict__ out) {
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < rows * n;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(e / n);
+    out[e] = (float)(((double)out[e] - proj[r] * (double)qk[e]) / (double)norms[r]);
+  }
+}
+
 }  // namespace
 }  // namespace zjai
 
@@ -492,6 +589,71 @@ int zjai_layer_norm_backward(zjai_ctx* ctx, const float* d, const float* x, int 
   ctx->launches++;
   ZJAI_TRY(cuda_check(cudaGetLastError(), "layer norm VJP"));
   ZJAI_TRY(stage_out_finish(ctx, dx, out, nt, mem));
+  return finish_call(ctx, mem);
+}
+
+int zjai_channel_attention_backward(zjai_ctx* ctx, const float* qkv, int c3, int h, int w,
+                                    int heads, const float* temperature, const float* attn,
+                                    const float* dout, float* dqkv, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!qkv || !temperature || !attn || !dout || !dqkv || h <= 0 || w <= 0 || heads <= 0 ||
+      c3 <= 0 || c3 % (3 * heads))
+    return fail(ZJAI_INVALID_ARGUMENT, "attention: channel / head counts");
+  if (mem != ZJAI_MEM_HOST && mem != ZJAI_MEM_DEVICE)
+    return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  ArenaScope scope(ctx);
+  const int dim = c3 / 3, c = dim / heads;
+  const long long n = (long long)h * w;
+  const float *dq, *dt, *da_in, *dd;
+  ZJAI_TRY(stage_in(ctx, qkv, (size_t)c3 * n, mem, &dq));
+  ZJAI_TRY(stage_in(ctx, temperature, (size_t)heads, mem, &dt));
+  ZJAI_TRY(stage_in(ctx, attn, (size_t)dim * c, mem, &da_in));
+  ZJAI_TRY(stage_in(ctx, dout, (size_t)dim * n, mem, &dd));
+  float* out;
+  ZJAI_TRY(stage_out_alloc(ctx, dqkv, (size_t)c3 * n, mem, &out));
+  // the row pairs of the three dot-product passes: q, k norms (2 dim), d_out . v (dim c), and
+  // the projections <x, acc> of the dq / dk rows (2 dim)
+  const int np_norm = 2 * dim, np_dot = dim * c;
+  std::vector<int> pairs(2 * (size_t)(np_norm + np_dot + np_norm));
+  for (int r = 0; r < np_norm; ++r) pairs[2 * r] = pairs[2 * r + 1] = r;
+  for (int ri = 0; ri < dim; ++ri)
+    for (int j = 0; j < c; ++j) {
+      const size_t p = (size_t)np_norm + (size_t)ri * c + j;
+      pairs[2 * p] = ri;
+      pairs[2 * p + 1] = (ri / c) * c + j;
+    }
+  for (int r = 0; r < np_norm; ++r) {
+    const size_t p = (size_t)np_norm + np_dot + r;
+    pairs[2 * p] = pairs[2 * p + 1] = r;
+  }
+  int* dpairs = static_cast<int*>(ctx->arena.alloc(pairs.size() * sizeof(int)));
+  double* dots = static_cast<double*>(ctx->arena.alloc((size_t)(2 * np_norm + np_dot) * sizeof(double)));
+  float* qk = static_cast<float*>(ctx->arena.alloc((size_t)2 * dim * n * sizeof(float)));
+  float* norms = static_cast<float*>(ctx->arena.alloc((size_t)2 * dim * sizeof(float)));
+  float* dam = static_cast<float*>(ctx->arena.alloc((size_t)dim * c * sizeof(float)));
+  if (!dpairs || !dots || !qk || !norms || !dam)
+    return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (attention VJP)");
+  ZJAI_TRY(cuda_check(cudaMemcpyAsync(dpairs, pairs.data(), pairs.size() * sizeof(int),
+                                      cudaMemcpyHostToDevice, ctx->stream),
+                      "attention VJP pairs"));
+  const int eb = (int)std::min<long long>((3LL * dim * n + 255) / 256, (long long)ctx->sms * 8);
+  row_dot_kernel<<<np_norm, 256, 0, ctx->stream>>>(dq, dq, dpairs, n, dots);
+  normalise_rows_kernel<<<eb, 256, 0, ctx->stream>>>(dq, dots, 2 * dim, n, qk, norms);
+  row_dot_kernel<<<np_dot, 256, 0, ctx->stream>>>(dd, dq + 2LL * dim * n, dpairs + 2 * np_norm, n,
+                                                  dots + np_norm);
+  softmax_vjp_kernel<<<(dim + 127) / 128, 128, 0, ctx->stream>>>(dots + np_norm, da_in, dim, c,
+                                                                 dam);
+  attn_grad_acc_kernel<<<eb, 256, 0, ctx->stream>>>(qk, dd, dam, da_in, dt, dim, c, n, out);
+  // <x, acc> of each dq / dk row: x = the normalised q / k row, acc = that row of out
+  row_dot_kernel<<<np_norm, 256, 0, ctx->stream>>>(qk, out, dpairs + 2 * (np_norm + np_dot), n,
+                                                   dots + np_norm + np_dot);
+  l2_backward_kernel<<<eb, 256, 0, ctx->stream>>>(qk, dots + np_norm + np_dot, norms, 2 * dim, n,
+                                                  out);
+  ctx->launches += 7;
+  ZJAI_TRY(cuda_check(cudaGetLastError(), "attention VJP"));
+  // `pairs` is a host vector: its copy must have been read before it goes
+  ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "attention VJP"));
+  ZJAI_TRY(stage_out_finish(ctx, dqkv, out, (size_t)c3 * n, mem));
   return finish_call(ctx, mem);
 }
 
