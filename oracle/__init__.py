@@ -119,6 +119,7 @@ def _declare(L):
     L.zo_layer_norm_backward.argtypes = [_f, _f, _i, _i, _i, _f, _f]
     L.zo_channel_attention_weights.argtypes = [_f, _i, _i, _i, _i, _f, _f]
     L.zo_channel_attention_backward.argtypes = [_f, _i, _i, _i, _i, _f, _f, _f, _f]
+    L.zo_transformer_block_backward.argtypes = [_f, _i, _i, _i, _i, _i, _f * 5, _f * 9, _f]
     L.zo_efe_split_edge.argtypes = [ctypes.c_double, _i]
     L.zo_efe_linear.argtypes = [_f, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i, _i,
                                 ctypes.POINTER(EfeLinearSet), _f, _f]
@@ -288,6 +289,26 @@ def channel_attention_backward(qkv, heads, temperature, dout):
             lib().zo_channel_attention_backward(_fp(qkv), c3, h, w, heads, _fp(t), _fp(attn),
                                                 _fp(dout), _fp(out)):
         raise ValueError("oracle channel_attention_backward: channel / head counts")
+    return out
+
+
+TB_TAPE = ("x_in", "qkv", "attn", "x_mid", "gate")
+TB_WEIGHTS = ("prep_norm", "prep_conv1", "prep_conv2", "temperature", "attn_out", "ffn_norm",
+              "ffn_in", "ffn_dw", "ffn_out")
+
+
+def transformer_block_backward(dout, heads, hidden, tape, weights):
+    """`TransformerBlock::backward` (attention.rs:435-480): dout [dim, h, w]; tape and weights
+    dicts keyed by TB_TAPE / TB_WEIGHTS -> d_x [dim, h, w]."""
+    dout = _c32(dout)
+    dim, h, w = dout.shape
+    ts = [_c32(tape[k]) for k in TB_TAPE]
+    ws = [_c32(weights[k]) for k in TB_WEIGHTS]
+    out = np.empty_like(dout)
+    if lib().zo_transformer_block_backward(_fp(dout), dim, hidden, heads, h, w,
+                                           (_f * 5)(*[_fp(a) for a in ts]),
+                                           (_f * 9)(*[_fp(a) for a in ws]), _fp(out)):
+        raise ValueError("oracle transformer_block_backward: shapes")
     return out
 
 

@@ -2354,3 +2354,50 @@ int zo_channel_attention_backward(const float *qkv, int c3, int h, int w, int he
     free(qk); free(norms); free(da);
     return 0;
 }
+
+/* `TransformerBlock::backward` (attention.rs:435-480) from its tape: the feed-forward branch
+ * (project_out, ELU gate, depthwise, project_in, layer norm of x_mid) added to d_out gives
+ * d_xmid; the attention branch (project_out, channel attention, depthwise, project_in, layer
+ * norm of x_in) of d_xmid added to it gives d_x. Shapes: x_in, x_mid [dim][n], qkv [3 dim][n],
+ * attn [dim][dim / heads], gate [2 hidden][n]; weights w[] = prep_norm.weight [dim], prep_conv1
+ * [3 dim][dim], prep_conv2 [3 dim][1][3][3], temperature [heads], attn_out [dim][dim],
+ * ffn_norm.weight [dim], ffn_in [2 hidden][dim], ffn_dw [2 hidden][1][3][3], ffn_out
+ * [dim][hidden]. */
+int zo_transformer_block_backward(const float *dout, int dim, int hidden, int heads, int h, int w,
+                                  const float *const tape[5], const float *const wt[9],
+                                  float *din) {
+    const float *x_in = tape[0], *qkv = tape[1], *attn = tape[2], *x_mid = tape[3],
+                *gate = tape[4];
+    const int64_t n = (int64_t)h * w;
+    float *df = (float *)malloc(sizeof(float) * hidden * n);
+    float *dd = (float *)malloc(sizeof(float) * 2 * hidden * n);
+    float *dd2 = (float *)malloc(sizeof(float) * 2 * hidden * n);
+    float *dm = (float *)malloc(sizeof(float) * dim * n);
+    float *d3 = (float *)malloc(sizeof(float) * 3 * dim * n);
+    float *d3b = (float *)malloc(sizeof(float) * 3 * dim * n);
+    float *da = (float *)malloc(sizeof(float) * dim * n);
+    int r = (!df || !dd || !dd2 || !dm || !d3 || !d3b || !da) ? -1 : 0;
+    /* feed-forward branch */
+    if (!r) r = zo_conv2d_backward(dout, dim, h, w, wt[8], hidden, 1, 1, 1, 0, 0, 1, NULL, h, w, df);
+    if (!r) {
+        zo_elu_gate_backward(df, gate, gate + (int64_t)hidden * n, (int64_t)hidden * n, dd,
+                             dd + (int64_t)hidden * n);
+        r = zo_conv2d_backward(dd, 2 * hidden, h, w, wt[7], 2 * hidden, 3, 3, 1, 1, 1,
+                               2 * hidden, NULL, h, w, dd2);
+    }
+    if (!r) r = zo_conv2d_backward(dd2, 2 * hidden, h, w, wt[6], dim, 1, 1, 1, 0, 0, 1, NULL, h, w, dm);
+    if (!r) r = zo_layer_norm_backward(dm, x_mid, dim, h, w, wt[5], da);
+    if (!r)
+        for (int64_t i = 0; i < (int64_t)dim * n; i++) din[i] = dout[i] + da[i];  /* d_xmid */
+    /* attention branch on d_xmid */
+    if (!r) r = zo_conv2d_backward(din, dim, h, w, wt[4], dim, 1, 1, 1, 0, 0, 1, NULL, h, w, dm);
+    if (!r) r = zo_channel_attention_backward(qkv, 3 * dim, h, w, heads, wt[3], attn, dm, d3);
+    if (!r) r = zo_conv2d_backward(d3, 3 * dim, h, w, wt[2], 3 * dim, 3, 3, 1, 1, 1, 3 * dim,
+                                   NULL, h, w, d3b);
+    if (!r) r = zo_conv2d_backward(d3b, 3 * dim, h, w, wt[1], dim, 1, 1, 1, 0, 0, 1, NULL, h, w, dm);
+    if (!r) r = zo_layer_norm_backward(dm, x_in, dim, h, w, wt[0], da);
+    if (!r)
+        for (int64_t i = 0; i < (int64_t)dim * n; i++) din[i] += da[i];
+    free(df); free(dd); free(dd2); free(dm); free(d3); free(d3b); free(da);
+    return r;
+}

@@ -290,6 +290,12 @@ int zo_channel_attention_weights(const float *qkv, int c3, int h, int w, int hea
 int zo_channel_attention_backward(const float *qkv, int c3, int h, int w, int heads,
                                   const float *temperature, const float *attn,
                                   const float *dout, float *dqkv);
+/* `TransformerBlock::backward` (attention.rs:435-480): tape = {x_in, qkv, attn, x_mid, gate},
+ * wt = {prep_norm.weight, prep_conv1, prep_conv2, temperature, attn_out, ffn_norm.weight,
+ * ffn_in, ffn_dw, ffn_out}; d_out [dim][h][w] -> din [dim][h][w]. */
+int zo_transformer_block_backward(const float *dout, int dim, int hidden, int heads, int h, int w,
+                                  const float *const tape[5], const float *const wt[9],
+                                  float *din);
 
 #ifdef __cplusplus
 }

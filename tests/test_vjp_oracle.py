@@ -245,3 +245,69 @@ def test_channel_attention_backward_matches_finite_differences(dim, heads, h, w)
     assert rel(lhs, rhs) < 1e-4, (lhs, rhs)
     # and the oracle's attention forward is the float64 one
     assert np.abs(zo.channel_attention(qkv, heads, temp) - attention_f64(q64, heads, temp)).max() < 1e-5
+
+
+def tb_forward_f64(x, wts, heads, hidden):
+    """`TransformerBlock::forward_tape` (attention.rs:373-430) in float64: the block's output and
+    its tape (x_in, qkv, x_mid, gate); layer norms over the channels (eps 1e-5), 1x1 and depthwise
+    3x3 convs without bias."""
+    def ln(t, wgt, b):
+        m = t.mean(0, keepdims=True)
+        v = ((t - m) ** 2).mean(0, keepdims=True)
+        return (t - m) / np.sqrt(v + 1e-5) * wgt[:, None, None] + b[:, None, None]
+
+    def pw(t, wgt):
+        return np.einsum("oc,chw->ohw", wgt[:, :, 0, 0].astype(np.float64), t)
+
+    def dw(t, wgt):
+        c, h, w = t.shape
+        tp = np.pad(t, ((0, 0), (1, 1), (1, 1)))
+        out = np.zeros_like(t)
+        for ky in range(3):
+            for kx in range(3):
+                out += wgt[:, 0, ky, kx][:, None, None].astype(np.float64) * tp[:, ky:ky + h, kx:kx + w]
+        return out
+
+    x = x.astype(np.float64)
+    qkv = dw(pw(ln(x, wts["prep_norm"], wts["prep_norm_b"]), wts["prep_conv1"]), wts["prep_conv2"])
+    a = attention_f64(qkv, heads, wts["temperature"])
+    x_mid = x + pw(a, wts["attn_out"])
+    gate = dw(pw(ln(x_mid, wts["ffn_norm"], wts["ffn_norm_b"]), wts["ffn_in"]), wts["ffn_dw"])
+    x1, x2 = gate[:hidden], gate[hidden:]
+    out = x_mid + pw(np.where(x1 > 0, x1, np.expm1(x1)) * x2, wts["ffn_out"])
+    return out, {"x_in": x, "qkv": qkv, "x_mid": x_mid, "gate": gate}
+
+
+def tb_case(rng, dim, hidden, heads):
+    def w(*shape, fan):
+        return (rng.standard_normal(shape) * (0.8 / np.sqrt(fan))).astype(np.float32)
+    return {"prep_norm": (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32),
+            "prep_norm_b": (0.1 * rng.standard_normal(dim)).astype(np.float32),
+            "prep_conv1": w(3 * dim, dim, 1, 1, fan=dim), "prep_conv2": w(3 * dim, 1, 3, 3, fan=9),
+            "temperature": rng.uniform(0.5, 2.0, heads).astype(np.float32),
+            "attn_out": w(dim, dim, 1, 1, fan=dim),
+            "ffn_norm": (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32),
+            "ffn_norm_b": (0.1 * rng.standard_normal(dim)).astype(np.float32),
+            "ffn_in": w(2 * hidden, dim, 1, 1, fan=dim), "ffn_dw": w(2 * hidden, 1, 3, 3, fan=9),
+            "ffn_out": w(dim, hidden, 1, 1, fan=hidden)}
+
+
+def test_transformer_block_backward_matches_finite_differences():
+    # TransformerBlock::backward (attention.rs:435-480) against finite differences of the block
+    rng = np.random.default_rng(31)
+    dim, hidden, heads, h, w = 16, 24, 4, 6, 7
+    wts = tb_case(rng, dim, hidden, heads)
+    x = rng.standard_normal((dim, h, w)).astype(np.float32)
+    y, tape = tb_forward_f64(x, wts, heads, hidden)
+    qkv32 = tape["qkv"].astype(np.float32)
+    tape32 = {"x_in": x, "qkv": qkv32,
+              "attn": zo.channel_attention_weights(qkv32, heads, wts["temperature"]),
+              "x_mid": tape["x_mid"].astype(np.float32), "gate": tape["gate"].astype(np.float32)}
+    d = rng.standard_normal(y.shape).astype(np.float32)
+    dx = zo.transformer_block_backward(d, heads, hidden, tape32, wts)
+    v = rng.standard_normal(x.shape)
+    eps = 1e-4
+    lhs = float((d * (tb_forward_f64(x + eps * v, wts, heads, hidden)[0] -
+                      tb_forward_f64(x - eps * v, wts, heads, hidden)[0])).sum()) / (2 * eps)
+    rhs = float((dx.astype(np.float64) * v).sum())
+    assert rel(lhs, rhs) < 1e-3, (lhs, rhs)
