@@ -541,6 +541,24 @@ int zjai_channel_attention_backward(zjai_ctx *ctx, const float *qkv, int c3, int
                                     int heads, const float *temperature, const float *attn,
                                     const float *dout, float *dqkv, int mem);
 
+/* `TransformerBlock::backward` (src/model/attention.rs:435-480) from the tape of
+ * `forward_tape`: x_in, x_mid [dim][h][w] (the block's input and its input after the attention
+ * half), qkv [3 dim][h][w], attn [dim][dim / heads], gate [2 hidden][h][w] (the depthwise conv's
+ * output, the ELU gate's two halves); weights: the two layer norms' weights [dim], prep_conv1
+ * [3 dim][dim], prep_conv2 [3 dim][1][3][3], temperature [heads], attn_out [dim][dim], ffn_in
+ * [2 hidden][dim], ffn_dw [2 hidden][1][3][3], ffn_out [dim][hidden]; 3 dim and 2 hidden
+ * multiples of 8. d_out [dim][h][w] -> din. Tolerance as zjai_conv2d_backward. */
+typedef struct {
+  const float *x_in, *qkv, *attn, *x_mid, *gate;
+} zjai_tb_tape;
+typedef struct {
+  const float *prep_norm, *prep_conv1, *prep_conv2, *temperature, *attn_out;
+  const float *ffn_norm, *ffn_in, *ffn_dw, *ffn_out;
+} zjai_tb_weights;
+int zjai_transformer_block_backward(zjai_ctx *ctx, const float *dout, int dim, int hidden,
+                                    int heads, int h, int w, const zjai_tb_tape *tape,
+                                    const zjai_tb_weights *wts, float *din, int mem);
+
 /* `math::layer_norm_channels` (math.rs:423-448), out of place. */
 int zjai_layer_norm(zjai_ctx *ctx, const float *x, int c, int h, int w, const float *weight,
                     const float *bias, float *out, int mem);

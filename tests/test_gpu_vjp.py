@@ -165,3 +165,21 @@ def test_channel_attention_backward(eng, dim, heads, h, w):
     # f64 sums on both sides in different orders: 1e-4 relative L2 per third (dq, dk, dv)
     for s in (slice(0, dim), slice(dim, 2 * dim), slice(2 * dim, 3 * dim)):
         assert rel_l2(got[s], want[s]) < 1e-4
+
+
+@pytest.mark.parametrize("dim,hidden,heads,h,w", [(64, 128, 4, 24, 20), (128, 256, 4, 16, 18)])
+def test_transformer_block_backward(eng, dim, hidden, heads, h, w):
+    # a chain of five conv VJPs, two depthwise ones, the attention and two layer norms
+    from test_vjp_oracle import tb_case, tb_forward_f64
+    rng = np.random.default_rng(dim + hidden)
+    wts = tb_case(rng, dim, hidden, heads)
+    x = rng.standard_normal((dim, h, w)).astype(np.float32)
+    _, tape = tb_forward_f64(x, wts, heads, hidden)
+    qkv = tape["qkv"].astype(np.float32)
+    tape32 = {"x_in": x, "qkv": qkv,
+              "attn": zo.channel_attention_weights(qkv, heads, wts["temperature"]),
+              "x_mid": tape["x_mid"].astype(np.float32), "gate": tape["gate"].astype(np.float32)}
+    d = rng.standard_normal((dim, h, w)).astype(np.float32)
+    want = zo.transformer_block_backward(d, heads, hidden, tape32, wts)
+    got = eng.transformer_block_backward(d, heads, hidden, tape32, wts)
+    assert rel_l2(got, want) < 3e-3

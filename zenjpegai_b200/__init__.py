@@ -256,6 +256,31 @@ class Engine:
                                                          pd, po, mem))
         return out
 
+    def transformer_block_backward(self, dout, heads, hidden, tape, weights, out=None):
+        """`TransformerBlock::backward` (attention.rs:435-480): dout [dim, h, w]; tape {"x_in",
+        "qkv", "attn", "x_mid", "gate"}; weights {"prep_norm", "prep_conv1", "prep_conv2",
+        "temperature", "attn_out", "ffn_norm", "ffn_in", "ffn_dw", "ffn_out"} -> d_x."""
+        dim, h, w = dout.shape
+        out = _like(dout, (dim, h, w)) if out is None else out
+        pd, mem = _arg(dout)
+        po, m = _arg(out, (dim, h, w))
+        mems = {mem, m}
+        t, wt = _lib.TbTape(), _lib.TbWeights()
+        for k, _ in _lib.TbTape._fields_:
+            p, m = _arg(tape[k])
+            setattr(t, k, p)
+            mems.add(m)
+        for k, _ in _lib.TbWeights._fields_:
+            p, m = _arg(weights[k])
+            setattr(wt, k, p)
+            mems.add(m)
+        if len(mems) != 1:
+            raise ZjaiError(_lib.INVALID_ARGUMENT, "mixed host and device arguments")
+        check(_lib.lib().zjai_transformer_block_backward(self.handle, pd, dim, hidden, heads, h,
+                                                         w, ctypes.byref(t), ctypes.byref(wt),
+                                                         po, mem))
+        return out
+
     CAB_WEIGHTS = ("trunk0.conv1", "trunk0.conv2", "trunk1.conv1", "trunk1.conv2", "subscale",
                    "mask2.conv1", "mask2.conv2", "mask3.conv1", "mask3.conv2", "upscale")
 

@@ -75,6 +75,15 @@ class CabWeights(ctypes.Structure):
                 ("mask3", _vp * 2), ("upscale", _vp)]
 
 
+class TbTape(ctypes.Structure):
+    _fields_ = [(k, _vp) for k in ("x_in", "qkv", "attn", "x_mid", "gate")]
+
+
+class TbWeights(ctypes.Structure):
+    _fields_ = [(k, _vp) for k in ("prep_norm", "prep_conv1", "prep_conv2", "temperature",
+                                   "attn_out", "ffn_norm", "ffn_in", "ffn_dw", "ffn_out")]
+
+
 _lib = None
 
 
@@ -182,6 +191,9 @@ def lib():
     L.zjai_layer_norm_backward.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _i]
     L.zjai_channel_attention_backward.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp,
                                                   _i]
+    L.zjai_transformer_block_backward.argtypes = [_vp, _vp, _i, _i, _i, _i, _i,
+                                                  ctypes.POINTER(TbTape),
+                                                  ctypes.POINTER(TbWeights), _vp, _i]
     L.zjai_layer_norm.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i]
     L.zjai_channel_attention.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i]
     L.zjai_depthwise3x3.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _i]

@@ -15,7 +15,8 @@
 //   (conv1's output), conv1's VJP, plus the skip's d_out.
 // * the transformer block's other pieces: the ELU gate (math.rs:838-858), the channel layer
 //   norm (math.rs:860-913) and the channel attention (math.rs:668-836), as elementwise,
-//   per-position and row-reduction kernels.
+//   per-position and row-reduction kernels; and the block itself (attention.rs:435-480): the
+//   feed-forward branch added to d_out, the attention branch of that added to it.
 // * CAB (attention.rs:182-223): d_out split into the trunk's (times sigma) and the mask's
 //   (times trunk and sigma'), the trunk's two residual blocks, the mask chain back to full
 //   resolution (upscale, two residual blocks, subscale), and the skip.
@@ -354,6 +355,89 @@ __global__ void l2_backward_kernel(const float* __restrict__ qk, const double* _
   }
 }
 
+// the input gradient of a depthwise 3x3 conv (padding 1, weight [c][1][3][3], host) from the
+// device planar dd [c][h][w] into din: the depthwise kernel with the flipped taps; its f16
+// outputs get the scale [2^7, 2^8), undone by scale_kernel (c a multiple of 8)
+int dw_vjp(Ctx* ctx, const float* dd, int c, int h, int w, const float* hw, float* din) {
+  const size_t nin = (size_t)c * h * w;
+  const size_t mark = ctx->arena.mark();
+  std::vector<float> flip((size_t)c * 9);
+  for (int ch = 0; ch < c; ++ch)
+    for (int t = 0; t < 9; ++t) flip[(size_t)ch * 9 + t] = hw[(size_t)ch * 9 + 8 - t];
+  float* dwt = static_cast<float*>(ctx->arena.alloc(flip.size() * sizeof(float)));
+  float* tmp = static_cast<float*>(ctx->arena.alloc(nin * sizeof(float)));
+  if (!dwt || !tmp) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (depthwise VJP)");
+  ZJAI_TRY(cuda_check(cudaMemcpyAsync(dwt, flip.data(), flip.size() * sizeof(float),
+                                      cudaMemcpyHostToDevice, ctx->stream),
+                      "VJP weights H2D"));
+  TView t, o;
+  float s;
+  ZJAI_TRY(stage_grad(ctx, dd, c, h, w, 8, &t, &s));
+  ZJAI_TRY(alloc_tensor(ctx, 1, h, w, c, &o));
+  ZJAI_TRY(launch_dw3x3(ctx, t, o, dwt, false, ctx->stream));
+  launch_nhwc_to_planar(o, tmp, ctx->stream);
+  scale_kernel<<<launch_elementwise_blocks(ctx, nin), 256, 0, ctx->stream>>>(tmp, nin, 1.f / s,
+                                                                           din);
+  ctx->launches += 3;
+  // `flip` is a host vector: its copy must have been read before it goes
+  ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "VJP depthwise"));
+  ctx->arena.release(mark);
+  return ZJAI_OK;
+}
+
+// channel_attention_backward (math.rs:668-836) on device arrays: qkv [3 dim][n], temp [heads],
+// attn [dim][c], dout [dim][n] -> out [3 dim][n]
+int attn_vjp(Ctx* ctx, const float* dq, int c3, long long n, int heads, const float* dt,
+             const float* da_in, const float* dd, float* out) {
+  const int dim = c3 / 3, c = dim / heads;
+  const size_t mark = ctx->arena.mark();
+  // the row pairs of the three dot-product passes: q, k norms (2 dim), d_out . v (dim c), and
+  // the projections <x, acc> of the dq / dk rows (2 dim)
+  const int np_norm = 2 * dim, np_dot = dim * c;
+  std::vector<int> pairs(2 * (size_t)(np_norm + np_dot + np_norm));
+  for (int r = 0; r < np_norm; ++r) pairs[2 * r] = pairs[2 * r + 1] = r;
+  for (int ri = 0; ri < dim; ++ri)
+    for (int j = 0; j < c; ++j) {
+      const size_t p = (size_t)np_norm + (size_t)ri * c + j;
+      pairs[2 * p] = ri;
+      pairs[2 * p + 1] = (ri / c) * c + j;
+    }
+  for (int r = 0; r < np_norm; ++r) {
+    const size_t p = (size_t)np_norm + np_dot + r;
+    pairs[2 * p] = pairs[2 * p + 1] = r;
+  }
+  int* dpairs = static_cast<int*>(ctx->arena.alloc(pairs.size() * sizeof(int)));
+  double* dots =
+      static_cast<double*>(ctx->arena.alloc((size_t)(2 * np_norm + np_dot) * sizeof(double)));
+  float* qk = static_cast<float*>(ctx->arena.alloc((size_t)2 * dim * n * sizeof(float)));
+  float* norms = static_cast<float*>(ctx->arena.alloc((size_t)2 * dim * sizeof(float)));
+  float* dam = static_cast<float*>(ctx->arena.alloc((size_t)dim * c * sizeof(float)));
+  if (!dpairs || !dots || !qk || !norms || !dam)
+    return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (attention VJP)");
+  ZJAI_TRY(cuda_check(cudaMemcpyAsync(dpairs, pairs.data(), pairs.size() * sizeof(int),
+                                      cudaMemcpyHostToDevice, ctx->stream),
+                      "attention VJP pairs"));
+  const int eb = (int)std::min<long long>((3LL * dim * n + 255) / 256, (long long)ctx->sms * 8);
+  row_dot_kernel<<<np_norm, 256, 0, ctx->stream>>>(dq, dq, dpairs, n, dots);
+  normalise_rows_kernel<<<eb, 256, 0, ctx->stream>>>(dq, dots, 2 * dim, n, qk, norms);
+  row_dot_kernel<<<np_dot, 256, 0, ctx->stream>>>(dd, dq + 2LL * dim * n, dpairs + 2 * np_norm, n,
+                                                  dots + np_norm);
+  softmax_vjp_kernel<<<(dim + 127) / 128, 128, 0, ctx->stream>>>(dots + np_norm, da_in, dim, c,
+                                                                 dam);
+  attn_grad_acc_kernel<<<eb, 256, 0, ctx->stream>>>(qk, dd, dam, da_in, dt, dim, c, n, out);
+  // <x, acc> of each dq / dk row: x = the normalised q / k row, acc = that row of out
+  row_dot_kernel<<<np_norm, 256, 0, ctx->stream>>>(qk, out, dpairs + 2 * (np_norm + np_dot), n,
+                                                   dots + np_norm + np_dot);
+  l2_backward_kernel<<<eb, 256, 0, ctx->stream>>>(qk, dots + np_norm + np_dot, norms, 2 * dim, n,
+                                                  out);
+  ctx->launches += 7;
+  ZJAI_TRY(cuda_check(cudaGetLastError(), "attention VJP"));
+  // `pairs` is a host vector: its copy must have been read before it goes
+  ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "attention VJP"));
+  ctx->arena.release(mark);
+  return ZJAI_OK;
+}
+
 }  // namespace
 }  // namespace zjai
 
@@ -401,29 +485,7 @@ int zjai_conv2d_backward(zjai_ctx* ctx, const float* dout, int oc, int oh, int o
   const size_t nin = (size_t)c * h * w;
   ZJAI_TRY(stage_out_alloc(ctx, din, nin, mem, &ddin));
   if (depthwise) {
-    // flipped taps [c][9]; the depthwise kernel stores f16, so the scale leaves room for the
-    // sum of nine products
-    std::vector<float> flip((size_t)c * 9);
-    for (int ch = 0; ch < c; ++ch)
-      for (int t = 0; t < 9; ++t) flip[(size_t)ch * 9 + t] = hw[(size_t)ch * 9 + 8 - t];
-    float* dwt = static_cast<float*>(ctx->arena.alloc(flip.size() * sizeof(float)));
-    if (!dwt) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (VJP weights)");
-    ZJAI_TRY(cuda_check(cudaMemcpyAsync(dwt, flip.data(), flip.size() * sizeof(float),
-                                        cudaMemcpyHostToDevice, ctx->stream),
-                        "VJP weights H2D"));
-    TView t, o;
-    float s;
-    ZJAI_TRY(stage_grad(ctx, dd, oc, oh, ow, 8, &t, &s));
-    ZJAI_TRY(alloc_tensor(ctx, 1, h, w, c, &o));
-    ZJAI_TRY(launch_dw3x3(ctx, t, o, dwt, false, ctx->stream));
-    float* tmp = static_cast<float*>(ctx->arena.alloc(nin * sizeof(float)));
-    if (!tmp) return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (VJP output)");
-    launch_nhwc_to_planar(o, tmp, ctx->stream);
-    scale_kernel<<<launch_elementwise_blocks(ctx, nin), 256, 0, ctx->stream>>>(tmp, nin, 1.f / s,
-                                                                             ddin);
-    ctx->launches += 3;
-    // `flip` is a host vector: its copy must have been read before it goes
-    ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "VJP depthwise"));
+    ZJAI_TRY(dw_vjp(ctx, dd, c, h, w, hw, ddin));
   } else if (stride == 1) {
     ZJAI_TRY(conv_vjp_s1(ctx, dd, oc, oh, ow, hw, c, kh, kw, pad_h, pad_w, groups, h, w, pt, pl,
                          ddin));
@@ -611,50 +673,86 @@ int zjai_channel_attention_backward(zjai_ctx* ctx, const float* qkv, int c3, int
   ZJAI_TRY(stage_in(ctx, dout, (size_t)dim * n, mem, &dd));
   float* out;
   ZJAI_TRY(stage_out_alloc(ctx, dqkv, (size_t)c3 * n, mem, &out));
-  // the row pairs of the three dot-product passes: q, k norms (2 dim), d_out . v (dim c), and
-  // the projections <x, acc> of the dq / dk rows (2 dim)
-  const int np_norm = 2 * dim, np_dot = dim * c;
-  std::vector<int> pairs(2 * (size_t)(np_norm + np_dot + np_norm));
-  for (int r = 0; r < np_norm; ++r) pairs[2 * r] = pairs[2 * r + 1] = r;
-  for (int ri = 0; ri < dim; ++ri)
-    for (int j = 0; j < c; ++j) {
-      const size_t p = (size_t)np_norm + (size_t)ri * c + j;
-      pairs[2 * p] = ri;
-      pairs[2 * p + 1] = (ri / c) * c + j;
-    }
-  for (int r = 0; r < np_norm; ++r) {
-    const size_t p = (size_t)np_norm + np_dot + r;
-    pairs[2 * p] = pairs[2 * p + 1] = r;
-  }
-  int* dpairs = static_cast<int*>(ctx->arena.alloc(pairs.size() * sizeof(int)));
-  double* dots = static_cast<double*>(ctx->arena.alloc((size_t)(2 * np_norm + np_dot) * sizeof(double)));
-  float* qk = static_cast<float*>(ctx->arena.alloc((size_t)2 * dim * n * sizeof(float)));
-  float* norms = static_cast<float*>(ctx->arena.alloc((size_t)2 * dim * sizeof(float)));
-  float* dam = static_cast<float*>(ctx->arena.alloc((size_t)dim * c * sizeof(float)));
-  if (!dpairs || !dots || !qk || !norms || !dam)
-    return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (attention VJP)");
-  ZJAI_TRY(cuda_check(cudaMemcpyAsync(dpairs, pairs.data(), pairs.size() * sizeof(int),
-                                      cudaMemcpyHostToDevice, ctx->stream),
-                      "attention VJP pairs"));
-  const int eb = (int)std::min<long long>((3LL * dim * n + 255) / 256, (long long)ctx->sms * 8);
-  row_dot_kernel<<<np_norm, 256, 0, ctx->stream>>>(dq, dq, dpairs, n, dots);
-  normalise_rows_kernel<<<eb, 256, 0, ctx->stream>>>(dq, dots, 2 * dim, n, qk, norms);
-  row_dot_kernel<<<np_dot, 256, 0, ctx->stream>>>(dd, dq + 2LL * dim * n, dpairs + 2 * np_norm, n,
-                                                  dots + np_norm);
-  softmax_vjp_kernel<<<(dim + 127) / 128, 128, 0, ctx->stream>>>(dots + np_norm, da_in, dim, c,
-                                                                 dam);
-  attn_grad_acc_kernel<<<eb, 256, 0, ctx->stream>>>(qk, dd, dam, da_in, dt, dim, c, n, out);
-  // <x, acc> of each dq / dk row: x = the normalised q / k row, acc = that row of out
-  row_dot_kernel<<<np_norm, 256, 0, ctx->stream>>>(qk, out, dpairs + 2 * (np_norm + np_dot), n,
-                                                   dots + np_norm + np_dot);
-  l2_backward_kernel<<<eb, 256, 0, ctx->stream>>>(qk, dots + np_norm + np_dot, norms, 2 * dim, n,
-                                                  out);
-  ctx->launches += 7;
-  ZJAI_TRY(cuda_check(cudaGetLastError(), "attention VJP"));
-  // `pairs` is a host vector: its copy must have been read before it goes
-  ZJAI_TRY(cuda_check(cudaStreamSynchronize(ctx->stream), "attention VJP"));
+  ZJAI_TRY(attn_vjp(ctx, dq, c3, n, heads, dt, da_in, dd, out));
   ZJAI_TRY(stage_out_finish(ctx, dqkv, out, (size_t)c3 * n, mem));
   return finish_call(ctx, mem);
+}
+
+int zjai_transformer_block_backward(zjai_ctx* ctx, const float* dout, int dim, int hidden,
+                                    int heads, int h, int w, const zjai_tb_tape* tape,
+                                    const zjai_tb_weights* wts, float* din, int mem) {
+  ZJAI_TRY(ctx_enter(ctx));
+  if (!dout || !tape || !wts || !din || dim <= 0 || hidden <= 0 || heads <= 0 || h <= 0 ||
+      w <= 0 || dim % heads || (3 * dim) % 8 || (2 * hidden) % 8)
+    return fail(ZJAI_INVALID_ARGUMENT, "transformer_block_backward: shapes");
+  if (mem != ZJAI_MEM_HOST && mem != ZJAI_MEM_DEVICE)
+    return fail(ZJAI_INVALID_ARGUMENT, "mem must be HOST or DEVICE");
+  const float* tp[5] = {tape->x_in, tape->qkv, tape->attn, tape->x_mid, tape->gate};
+  const float* wp[9] = {wts->prep_norm,  wts->prep_conv1, wts->prep_conv2,
+                        wts->temperature, wts->attn_out,  wts->ffn_norm,
+                        wts->ffn_in,     wts->ffn_dw,     wts->ffn_out};
+  for (const float* p : tp)
+    if (!p) return fail(ZJAI_INVALID_ARGUMENT, "transformer_block_backward: missing tape array");
+  for (const float* p : wp)
+    if (!p) return fail(ZJAI_INVALID_ARGUMENT, "transformer_block_backward: missing weight");
+  ArenaScope scope(ctx);
+  const long long n = (long long)h * w;
+  const int c = dim / heads;
+  const size_t tn[5] = {(size_t)dim * n, (size_t)3 * dim * n, (size_t)dim * c, (size_t)dim * n,
+                        (size_t)2 * hidden * n};
+  // conv weights on the host (packing), the rest staged on the device
+  std::vector<float> wb[9];
+  const float* hw[9] = {};
+  const size_t wn[9] = {(size_t)dim, (size_t)3 * dim * dim, (size_t)3 * dim * 9, (size_t)heads,
+                        (size_t)dim * dim, (size_t)dim, (size_t)2 * hidden * dim,
+                        (size_t)2 * hidden * 9, (size_t)dim * hidden};
+  for (int i : {1, 2, 4, 6, 7, 8}) ZJAI_TRY(fetch_host(wp[i], wn[i], mem, &wb[i], &hw[i]));
+  const float *dd, *dt[5], *dprep_norm, *dtemp, *dffn_norm;
+  ZJAI_TRY(stage_in(ctx, dout, (size_t)dim * n, mem, &dd));
+  for (int i = 0; i < 5; ++i) ZJAI_TRY(stage_in(ctx, tp[i], tn[i], mem, &dt[i]));
+  ZJAI_TRY(stage_in(ctx, wp[0], wn[0], mem, &dprep_norm));
+  ZJAI_TRY(stage_in(ctx, wp[3], wn[3], mem, &dtemp));
+  ZJAI_TRY(stage_in(ctx, wp[5], wn[5], mem, &dffn_norm));
+  float* ddin;
+  ZJAI_TRY(stage_out_alloc(ctx, din, (size_t)dim * n, mem, &ddin));
+  float* df = static_cast<float*>(ctx->arena.alloc((size_t)hidden * n * sizeof(float)));
+  float* g1 = static_cast<float*>(ctx->arena.alloc((size_t)2 * hidden * n * sizeof(float)));
+  float* g2 = static_cast<float*>(ctx->arena.alloc((size_t)2 * hidden * n * sizeof(float)));
+  float* dm = static_cast<float*>(ctx->arena.alloc((size_t)dim * n * sizeof(float)));
+  float* dln = static_cast<float*>(ctx->arena.alloc((size_t)dim * n * sizeof(float)));
+  float* q1 = static_cast<float*>(ctx->arena.alloc((size_t)3 * dim * n * sizeof(float)));
+  float* q2 = static_cast<float*>(ctx->arena.alloc((size_t)3 * dim * n * sizeof(float)));
+  if (!df || !g1 || !g2 || !dm || !dln || !q1 || !q2)
+    return fail(ZJAI_LIMIT_EXCEEDED, "device arena exhausted (transformer block VJP)");
+  const size_t nd = (size_t)dim * n, nh = (size_t)hidden * n;
+  // feed-forward branch: project_out, the ELU gate, the depthwise conv, project_in, its norm
+  ZJAI_TRY(conv_vjp_s1(ctx, dd, dim, h, w, hw[8], hidden, 1, 1, 0, 0, 1, h, w, 0, 0, df));
+  elu_gate_bwd_kernel<<<launch_elementwise_blocks(ctx, nh), 256, 0, ctx->stream>>>(
+      df, dt[4], dt[4] + nh, nh, g1, g1 + nh);
+  ctx->launches++;
+  ZJAI_TRY(dw_vjp(ctx, g1, 2 * hidden, h, w, hw[7], g2));
+  ZJAI_TRY(conv_vjp_s1(ctx, g2, 2 * hidden, h, w, hw[6], dim, 1, 1, 0, 0, 1, h, w, 0, 0, dm));
+  ln_bwd_kernel<<<launch_elementwise_blocks(ctx, (size_t)n), 256, 0, ctx->stream>>>(
+      dm, dt[3], dim, n, dffn_norm, dln);
+  // d_xmid = d_out + that branch
+  ZJAI_TRY(cuda_check(cudaMemcpyAsync(ddin, dd, nd * sizeof(float), cudaMemcpyDeviceToDevice,
+                                      ctx->stream),
+                      "d_xmid"));
+  add_kernel<<<launch_elementwise_blocks(ctx, nd), 256, 0, ctx->stream>>>(ddin, dln, nd);
+  ctx->launches += 2;
+  // attention branch on d_xmid: project_out, the attention, the depthwise conv, project_in,
+  // its norm; added to d_xmid
+  ZJAI_TRY(conv_vjp_s1(ctx, ddin, dim, h, w, hw[4], dim, 1, 1, 0, 0, 1, h, w, 0, 0, dm));
+  ZJAI_TRY(attn_vjp(ctx, dt[1], 3 * dim, n, heads, dtemp, dt[2], dm, q1));
+  ZJAI_TRY(dw_vjp(ctx, q1, 3 * dim, h, w, hw[2], q2));
+  ZJAI_TRY(conv_vjp_s1(ctx, q2, 3 * dim, h, w, hw[1], dim, 1, 1, 0, 0, 1, h, w, 0, 0, dm));
+  ln_bwd_kernel<<<launch_elementwise_blocks(ctx, (size_t)n), 256, 0, ctx->stream>>>(
+      dm, dt[0], dim, n, dprep_norm, dln);
+  add_kernel<<<launch_elementwise_blocks(ctx, nd), 256, 0, ctx->stream>>>(ddin, dln, nd);
+  ctx->launches += 2;
+  ZJAI_TRY(cuda_check(cudaGetLastError(), "transformer block VJP"));
+  ZJAI_TRY(stage_out_finish(ctx, din, ddin, (size_t)dim * n, mem));
+  return ctx_check_status(ctx);
 }
 
 }  // extern "C"
