@@ -120,6 +120,8 @@ def _declare(L):
     L.zo_channel_attention_weights.argtypes = [_f, _i, _i, _i, _i, _f, _f]
     L.zo_channel_attention_backward.argtypes = [_f, _i, _i, _i, _i, _f, _f, _f, _f]
     L.zo_transformer_block_backward.argtypes = [_f, _i, _i, _i, _i, _i, _f * 5, _f * 9, _f]
+    L.zo_tam_backward.argtypes = [_f, _i, _i, _i, _i, _i, _i, _f * 5, _f * 5, _f * 9, _f * 9, _f,
+                                  _f, _f]
     L.zo_efe_split_edge.argtypes = [ctypes.c_double, _i]
     L.zo_efe_linear.argtypes = [_f, _i, _i, _f, _f, _i, _i, _i, _i, _i, _i, _i, _i,
                                 ctypes.POINTER(EfeLinearSet), _f, _f]
@@ -309,6 +311,29 @@ def transformer_block_backward(dout, heads, hidden, tape, weights):
                                            (_f * 5)(*[_fp(a) for a in ts]),
                                            (_f * 9)(*[_fp(a) for a in ws]), _fp(out)):
         raise ValueError("oracle transformer_block_backward: shapes")
+    return out
+
+
+def tam_backward(dout, heads, hidden, h, w, tapes, weights, ds_w=None, us_w=None):
+    """`Tam::backward` (attention.rs:578-600): dout at the TAM's output, tapes / weights of its
+    two blocks (dicts as transformer_block_backward takes), ds_w / us_w the resampling convs
+    (None: no resampling) -> d_x [dim, h, w]."""
+    dout = _c32(dout)
+    dim = dout.shape[0]
+    keep = []
+
+    def arr(a):
+        a = _c32(a)
+        keep.append(a)
+        return _fp(a)
+    tp = [(_f * 5)(*[arr(t[k]) for k in TB_TAPE]) for t in tapes]
+    wp = [(_f * 9)(*[arr(wd[k]) for k in TB_WEIGHTS]) for wd in weights]
+    rs = ds_w is not None
+    out = np.empty((dim, h, w), np.float32)
+    if lib().zo_tam_backward(_fp(dout), dim, hidden, heads, h, w, int(rs), tp[0], tp[1], wp[0],
+                             wp[1], arr(ds_w) if rs else None, arr(us_w) if rs else None,
+                             _fp(out)):
+        raise ValueError("oracle tam_backward: shapes")
     return out
 
 

@@ -2401,3 +2401,38 @@ int zo_transformer_block_backward(const float *dout, int dim, int hidden, int he
     free(df); free(dd); free(dd2); free(dm); free(d3); free(d3b); free(da);
     return r;
 }
+
+/* `Tam::backward` (attention.rs:578-600): d_out through us_conv's VJP when resampled, block 1,
+ * block 0, then ds_conv's VJP. h x w: the TAM's input extent; with resample the blocks run at
+ * (h + 1) / 2 x (w + 1) / 2 (ds_conv: 3x3 stride 2 padding 1; us_conv: 3x3 transposed, stride 2,
+ * padding 1, output padding 1, weight [dim][dim][3][3]). tape0 / tape1, wt0 / wt1: the blocks'
+ * tapes and weights as zo_transformer_block_backward takes them. */
+int zo_tam_backward(const float *dout, int dim, int hidden, int heads, int h, int w, int resample,
+                    const float *const tape0[5], const float *const tape1[5],
+                    const float *const wt0[9], const float *const wt1[9], const float *ds_w,
+                    const float *us_w, float *din) {
+    const int bh = resample ? (h + 1) / 2 : h, bw = resample ? (w + 1) / 2 : w;
+    const size_t nb = (size_t)dim * bh * bw;
+    float *a = (float *)malloc(sizeof(float) * nb), *b = (float *)malloc(sizeof(float) * nb);
+    int r = (!a || !b) ? -1 : 0;
+    if (!r) {
+        if (resample)
+            r = zo_conv_transpose2d_backward(dout, dim, 2 * bh, 2 * bw, us_w, dim, 3, 2, 1, bh,
+                                             bw, a);
+        else
+            memcpy(a, dout, sizeof(float) * nb);
+    }
+    if (!r) r = zo_transformer_block_backward(a, dim, hidden, heads, bh, bw, tape1, wt1, b);
+    if (!r) {
+        if (resample) {
+            r = zo_transformer_block_backward(b, dim, hidden, heads, bh, bw, tape0, wt0, a);
+            if (!r) r = zo_conv2d_backward(a, dim, bh, bw, ds_w, dim, 3, 3, 2, 1, 1, 1, NULL, h,
+                                           w, din);
+        } else {
+            r = zo_transformer_block_backward(b, dim, hidden, heads, bh, bw, tape0, wt0, din);
+        }
+    }
+    free(a);
+    free(b);
+    return r;
+}

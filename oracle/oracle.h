@@ -296,6 +296,12 @@ int zo_channel_attention_backward(const float *qkv, int c3, int h, int w, int he
 int zo_transformer_block_backward(const float *dout, int dim, int hidden, int heads, int h, int w,
                                   const float *const tape[5], const float *const wt[9],
                                   float *din);
+/* `Tam::backward` (attention.rs:578-600): the two blocks' VJPs, between the VJPs of the
+ * stride-2 ds_conv and the transposed us_conv when resample is set; h x w the TAM's input. */
+int zo_tam_backward(const float *dout, int dim, int hidden, int heads, int h, int w, int resample,
+                    const float *const tape0[5], const float *const tape1[5],
+                    const float *const wt0[9], const float *const wt1[9], const float *ds_w,
+                    const float *us_w, float *din);
 
 #ifdef __cplusplus
 }

@@ -311,3 +311,43 @@ def test_transformer_block_backward_matches_finite_differences():
                       tb_forward_f64(x - eps * v, wts, heads, hidden)[0])).sum()) / (2 * eps)
     rhs = float((dx.astype(np.float64) * v).sum())
     assert rel(lhs, rhs) < 1e-3, (lhs, rhs)
+
+
+def tape32(tape, wts, heads):
+    qkv = tape["qkv"].astype(np.float32)
+    return {"x_in": tape["x_in"].astype(np.float32), "qkv": qkv,
+            "attn": zo.channel_attention_weights(qkv, heads, wts["temperature"]),
+            "x_mid": tape["x_mid"].astype(np.float32), "gate": tape["gate"].astype(np.float32)}
+
+
+@pytest.mark.parametrize("resample", [True, False])
+def test_tam_backward_matches_finite_differences(resample):
+    # Tam::backward (attention.rs:578-600): us_conv's VJP, the two blocks', ds_conv's
+    rng = np.random.default_rng(41 + resample)
+    dim, hidden, heads, h, w = 16, 24, 4, 12, 10
+    blocks = [tb_case(rng, dim, hidden, heads) for _ in range(2)]
+    ds_w = (rng.standard_normal((dim, dim, 3, 3)) * (0.8 / np.sqrt(9 * dim))).astype(np.float32)
+    us_w = (rng.standard_normal((dim, dim, 3, 3)) * (0.8 / np.sqrt(9 * dim))).astype(np.float32)
+    zero = np.zeros(dim, np.float32)
+
+    def forward(x):
+        if resample:
+            x = conv3x3_f64(x, ds_w, zero)[:, ::2, ::2]
+        x, t0 = tb_forward_f64(x, blocks[0], heads, hidden)
+        x, t1 = tb_forward_f64(x, blocks[1], heads, hidden)
+        if resample:
+            x = convT3_s2_f64(x, us_w, zero)
+        return x, (t0, t1)
+
+    x = rng.standard_normal((dim, h, w)).astype(np.float32)
+    y, (t0, t1) = forward(x.astype(np.float64))
+    d = rng.standard_normal(y.shape).astype(np.float32)
+    dx = zo.tam_backward(d, heads, hidden, h, w, [tape32(t0, blocks[0], heads),
+                                                  tape32(t1, blocks[1], heads)], blocks,
+                         ds_w if resample else None, us_w if resample else None)
+    v = rng.standard_normal(x.shape)
+    eps = 1e-4
+    x64 = x.astype(np.float64)
+    lhs = float((d * (forward(x64 + eps * v)[0] - forward(x64 - eps * v)[0])).sum()) / (2 * eps)
+    rhs = float((dx.astype(np.float64) * v).sum())
+    assert rel(lhs, rhs) < 1e-3, (lhs, rhs)
